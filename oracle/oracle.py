@@ -1,0 +1,517 @@
+"""CPU restatement of the reference Oracle: the specification the engine is checked against.
+
+TEST INFRASTRUCTURE ONLY.  Nothing in the product (xgraph_b200/) imports this module;
+only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline arm use it, and only
+as the checker or as the timed CPU baseline.
+
+Parity is pinned: tests/test_oracle_golden.py replays the golden walks in tests/golden/
+(made by tests/golden/make_golden.py from the reference's own Oracle,
+src/xgraph/oracle.py) through this oracle and requires every allowed set, public
+state projection and closed span to be equal.
+
+Scope: the span language of src/xgraph/oracle.py with the policies the engine serves:
+ordinary entity/fact spans, escapes, repeats, derivation, paths (union and committed),
+bound_escapes, unquoted_starts, start_rank "degree"/"sitelinks", KG versions,
+end_after_answer and opened states.  The reference's observation, menu, audit, STOP,
+expression and relation-support policies are not restated; asking for them raises.
+
+Like the reference it reads a KG index's arrays as plain data (edge tuples, token
+tuples) and recomputes everything per token from them.  One restructuring, for speed
+only: `allowed` computes the token-independent part of a span step (the complete
+candidates and which delimiters may start) once per state instead of once per token;
+each token then takes the same branch logic as `advance`.
+"""
+
+from __future__ import annotations
+
+from bisect import bisect_left, bisect_right
+from collections.abc import Iterable, Mapping
+from dataclasses import dataclass, replace
+from enum import Enum
+
+MAX_FACTS = 64  # src/xgraph/oracle.py:172
+MAX_REACHED = 64  # src/xgraph/oracle.py:175
+MAX_PATH_RELATIONS = 8  # src/xgraph/oracle.py:177
+
+
+class Phase(Enum):
+    FREE = "free text"
+    SPAN = "span"
+    ESCAPED = "escaped"
+
+
+class Segment(Enum):
+    SUBJECT = "subject"
+    RELATION = "relation"
+    OBJECT = "object"
+
+
+class TokenNotAllowed(ValueError):
+    pass
+
+
+class IndexMismatch(ValueError):
+    pass
+
+
+@dataclass(frozen=True)
+class ClosedSpan:
+    """src/xgraph/oracle.py:202-240."""
+
+    labels: tuple[tuple[int, ...], ...]
+    entity_ids: tuple[str, ...]
+    triples: tuple[tuple[str, str, str], ...]
+    resolved: bool
+    operator: str = ""
+    operands: tuple[str, ...] = ()
+    path: bool = False
+
+
+UNRESOLVED = ClosedSpan((), (), (), resolved=False)
+
+
+@dataclass(frozen=True)
+class OracleState:
+    """The in-scope fields of src/xgraph/oracle.py:249-341."""
+
+    phase: Phase
+    tail: bytes = b""
+    segment: Segment = Segment.SUBJECT
+    subjects: frozenset[str] = frozenset()
+    relations: frozenset[str] = frozenset()
+    written: tuple[tuple[int, ...], ...] = ()
+    typed: tuple[int, ...] | None = ()
+    closing: bytes | None = None
+    closing_label: tuple[int, ...] = ()
+    separating: bytes | None = None
+    separating_label: tuple[int, ...] = ()
+    escaping: bytes | None = None
+    last_span: ClosedSpan | None = None
+    facts: tuple[tuple[tuple[int, ...], ...], ...] = ()
+    reached: frozenset[int] | None = None
+    ranks: tuple[tuple[str, int], ...] = ()
+    version: str | None = None
+    answer_complete: bool = False
+
+
+class _Graph:
+    """One KG version as plain edges (src/xgraph/oracle.py:344-364)."""
+
+    def __init__(self, edges: set[tuple[str, str, int]]) -> None:
+        self.edges = frozenset(edges)
+        self.outgoing: dict[str, list[tuple[str, str, int]]] = {}
+        for edge in edges:
+            self.outgoing.setdefault(edge[0], []).append(edge)
+        self.degree = {s: len(v) for s, v in self.outgoing.items()}
+        self.has_triples = frozenset(self.degree)
+
+    def from_subjects(self, subjects):
+        for s in subjects:
+            yield from self.outgoing.get(s, ())
+
+
+@dataclass
+class _SpanContext:
+    """Token-independent facts of one span state (which delimiter branches may start)."""
+
+    complete: list[tuple[str, int]]
+    closes: bool
+    separates: bool
+    escapes: bool
+
+
+_UNSUPPORTED = {
+    "expressions": False, "stop": None, "relations": "frontier", "observe": 0,
+    "observe_width": 0, "observe_defer": 0, "menu_close_next": False, "observe_select": False,
+    "observe_answer": False, "observe_required": False, "observe_no_loop": False,
+    "audit": False, "menu": 0, "observe_terminal": 0,
+}
+
+
+class Oracle:
+    """src/xgraph/oracle.py:367-1923, restricted to the policies listed in the module doc."""
+
+    def __init__(
+        self,
+        index,
+        tokenizer,
+        syntax,
+        *,
+        escapes: bool = True,
+        repeats: bool = True,
+        derivation: bool = False,
+        paths: bool = False,
+        bound_escapes: bool = True,
+        committed_paths: bool = False,
+        versions: Mapping[str, Iterable[tuple[str, str, str | None]]] | None = None,
+        start_rank: str = "degree",
+        unquoted_starts: bool = False,
+        end_after_answer: bool = False,
+        eos_token_ids: Iterable[int] = (),
+        **others,
+    ) -> None:
+        # Constructor checks in the reference's order (src/xgraph/oracle.py:439-455).
+        if index.tokenizer_fingerprint != tokenizer.fingerprint:
+            raise IndexMismatch("the KG index was built for another tokenizer")
+        if index.span_syntax != syntax:
+            raise IndexMismatch("the KG index was built for another span syntax")
+        if not (escapes or repeats):
+            raise ValueError("repeats can only be switched off with escapes, the way out")
+        if committed_paths and not paths:
+            raise ValueError("committed_paths needs path mode (paths=True)")
+        if end_after_answer and not paths:
+            raise ValueError("end_after_answer needs path mode (paths=True)")
+        for name, value in others.items():
+            if name not in _UNSUPPORTED:
+                raise TypeError(f"unexpected keyword argument {name!r}")
+            if value != _UNSUPPORTED[name]:
+                raise ValueError(f"the {name} policy is not restated by this oracle")
+        self._eos = tokenizer.check_eos_token_ids(eos_token_ids) if end_after_answer else frozenset()
+        self._end_after_answer = end_after_answer
+        if start_rank not in ("degree", "sitelinks"):
+            raise ValueError(f"start_rank must be one of ('degree', 'sitelinks'), got {start_rank!r}")
+        labels, relations = index.labels, index.relations
+        self._sitelinks: dict[str, int] = {}
+        if start_rank == "sitelinks":
+            if index.sitelinks is None:
+                raise ValueError("the sitelink rank needs a KG index with sitelink counts")
+            self._sitelinks = {e: int(n) for e, n in zip(labels.owner_ids, index.sitelinks, strict=True)}
+        self._entity_rows = [(labels.row_tokens(r), labels.owner_id(r)) for r in range(labels.num_rows)]
+        self._relation_rows = [
+            (relations.row_tokens(r), relations.owner_id(r)) for r in range(relations.num_rows)
+        ]
+        self._first_row: dict[str, int] = {}
+        self._rows_of: dict[str, list[int]] = {}
+        for row, (_, owner) in enumerate(self._entity_rows):
+            self._first_row.setdefault(owner, row)
+            self._rows_of.setdefault(owner, []).append(row)
+        # Plain base edges (src/xgraph/oracle.py:581-587).
+        edges: set[tuple[str, str, int]] = set()
+        for entity, subject in enumerate(labels.owner_ids):
+            a, b = int(index.adjacency_offsets[entity]), int(index.adjacency_offsets[entity + 1])
+            for e in range(a, b):
+                edges.add((subject, relations.owner_ids[int(index.edge_relations[e])],
+                           int(index.edge_objects[e])))
+        self._graphs: dict[str | None, _Graph] = {None: _Graph(edges)}
+        # A version replaces every edge of an edited pair (src/xgraph/oracle.py:588-624).
+        writable = {owner for _, owner in self._relation_rows}
+        for name, edits in (versions or {}).items():
+            if not isinstance(name, str) or not name:
+                raise ValueError(f"a KG version needs a non-empty name, got {name!r}")
+            edits = list(edits)
+            pairs = {(s, r) for s, r, _ in edits}
+            kept = {(s, r, o) for s, r, o in edges if (s, r) not in pairs}
+            added = {
+                (s, r, row)
+                for s, r, o in edits
+                if s in self._rows_of and r in writable
+                for row in self._rows_of.get(o, ())
+            }
+            self._graphs[name] = _Graph(kept | added)
+        self._derivation = derivation or paths
+        self._paths = paths
+        self._bound_escapes = bound_escapes
+        self._committed = committed_paths
+        self._escapes = escapes
+        self._repeats = repeats
+        self._bytes = [tokenizer.token_bytes(t) for t in range(tokenizer.vocab_size)]
+        self._special = tokenizer.special_ids
+        self._opener = syntax.opener.encode("utf-8")
+        self._closer = syntax.closer.encode("utf-8")
+        self._separator = syntax.separator.encode("utf-8")
+        self._escape = syntax.escape.encode("utf-8")
+        self._entity_ids = labels.owner_ids
+        self._quoted_rows = frozenset(
+            row
+            for row, (tokens, _) in enumerate(self._entity_rows)
+            if unquoted_starts and syntax.quoted(b"".join(self._bytes[t] for t in tokens))
+        )
+
+    # -- states (src/xgraph/oracle.py:660-724) ------------------------------------
+
+    def initial_state(self, version: str | None = None) -> OracleState:
+        return OracleState(Phase.FREE, version=self._version(version))
+
+    def anchored_state(self, entities: list[str], version: str | None = None) -> OracleState:
+        rows = self._rows_for(entities)
+        if not rows:
+            raise ValueError(f"anchor has no writable label rows: {entities!r}")
+        return OracleState(Phase.FREE, reached=frozenset(rows[:MAX_REACHED]), version=self._version(version))
+
+    def opened_state(self, state: OracleState) -> OracleState:
+        if state.answer_complete:
+            raise ValueError("the answer is complete; only EOS may follow")
+        if state.phase is not Phase.FREE:
+            raise ValueError(f"a span opens from free text, not from {state.phase.value}")
+        return OracleState(Phase.SPAN, last_span=state.last_span, facts=state.facts,
+                           reached=state.reached, version=state.version)
+
+    def _version(self, version: str | None) -> str | None:
+        if version not in self._graphs:
+            names = sorted(n for n in self._graphs if n is not None)
+            raise ValueError(f"the oracle has no KG version {version!r}; it has {names}")
+        return version
+
+    def _graph(self, state: OracleState) -> _Graph:
+        return self._graphs[state.version]
+
+    def _rows_for(self, entities) -> list[int]:
+        return sorted(r for e in set(entities) for r in self._rows_of.get(e, ()))
+
+    # -- stepping (src/xgraph/oracle.py:736-828) ----------------------------------
+
+    def allowed(self, state: OracleState) -> frozenset[int]:
+        ctx = self._context(state) if state.phase is Phase.SPAN and not state.answer_complete else None
+        return frozenset(t for t in range(len(self._bytes)) if self._step(state, t, ctx) is not None)
+
+    def advance(self, state: OracleState, token: int) -> OracleState:
+        following = self._step(state, token, None)
+        if following is None:
+            raise TokenNotAllowed(f"token {token} is not allowed in {state.phase.value}")
+        return following
+
+    def _step(self, state: OracleState, token: int, ctx: _SpanContext | None) -> OracleState | None:
+        if not 0 <= token < len(self._bytes):
+            return None
+        if state.answer_complete:
+            return state if token in self._eos else None
+        data = self._bytes[token]
+        if state.phase is Phase.FREE and token in self._special:
+            return replace(state, tail=b"")
+        if data is None:
+            return None
+        if state.phase is Phase.FREE:
+            return self._free_step(state, data)
+        if state.phase is Phase.SPAN:
+            return self._span_step(state, token, data, ctx or self._context(state))
+        return self._escaped_step(state, data)
+
+    def _free_step(self, state: OracleState, data: bytes) -> OracleState | None:
+        text = state.tail + data
+        at = text.find(self._opener)
+        if at < 0:
+            keep = len(self._opener) - 1
+            return replace(state, tail=text[len(text) - keep:] if keep > 0 else b"")
+        if at + len(self._opener) != len(text):
+            return None
+        return self.opened_state(state)
+
+    def _escaped_step(self, state: OracleState, data: bytes) -> OracleState | None:
+        text = state.tail + data
+        at = text.find(self._closer)
+        if at < 0:
+            keep = len(self._closer) - 1
+            return replace(state, tail=text[len(text) - keep:] if keep > 0 else b"")
+        if at + len(self._closer) != len(text):
+            return None
+        return OracleState(Phase.FREE, last_span=UNRESOLVED, facts=state.facts,
+                           reached=state.reached, version=state.version)
+
+    # -- candidates (src/xgraph/oracle.py:830-894) --------------------------------
+
+    def _unbound(self, state: OracleState) -> bool:
+        return state.segment is Segment.SUBJECT and (not self._derivation or state.reached is None)
+
+    def _candidates(self, state: OracleState, prefix, *, exact: bool = False):
+        """(tokens, item, row) of the segment's candidate rows that start with (or, exact,
+        equal) prefix, in row order."""
+        if prefix is None:
+            return []
+        if self._unbound(state):
+            n = len(prefix)
+            key = (lambda item: item[0]) if exact else (lambda item: item[0][:n])
+            lo = bisect_left(self._entity_rows, prefix, key=key)
+            hi = bisect_right(self._entity_rows, prefix, key=key)
+            return [(*self._entity_rows[r], r) for r in range(lo, hi) if r not in self._quoted_rows]
+        n = len(prefix)
+        return [
+            c for c in self._segment_candidates(state)
+            if (c[0] == prefix if exact else c[0][:n] == prefix)
+        ]
+
+    def _segment_candidates(self, state: OracleState):
+        if state.segment is Segment.SUBJECT:
+            return [(*self._entity_rows[r], r) for r in sorted(state.reached)]
+        graph = self._graph(state)
+        if state.segment is Segment.RELATION:
+            have = {r for _, r, _ in graph.from_subjects(state.subjects)}
+            return [(tokens, r, row) for row, (tokens, r) in enumerate(self._relation_rows) if r in have]
+        objects = {
+            o for s, r, o in graph.from_subjects(state.subjects)
+            if s in state.subjects and r in state.relations
+        }
+        return [(*self._entity_rows[r], r) for r in sorted(objects)]
+
+    # -- span step (src/xgraph/oracle.py:896-1263, in-scope branches) -------------
+
+    def _context(self, state: OracleState) -> _SpanContext:
+        complete: list[tuple[str, int]] = []
+        if state.typed is not None:
+            complete = [(item, row) for _, item, row in self._candidates(state, state.typed, exact=True)]
+        closes = bool(complete) and (state.segment is not Segment.RELATION or self._paths)
+        if closes and state.segment is Segment.OBJECT and not self._repeats:
+            closes = (*state.written, state.typed) not in state.facts
+        graph = self._graph(state)
+        separates = False
+        if state.segment is Segment.SUBJECT:
+            separates = not self._answers_path(state) and any(e in graph.has_triples for e, _ in complete)
+        elif state.segment is Segment.RELATION and complete:
+            separates = not self._paths or (
+                len(state.written) - 1 < MAX_PATH_RELATIONS - 1
+                and any(e in graph.has_triples for e in self._frontier(state, state.typed))
+            )
+        escapes = self._escapes and state.typed is not None and self._may_escape(state)
+        return _SpanContext(complete, closes, separates, escapes)
+
+    @staticmethod
+    def _branch(typed, label, data, delimiter, may_start, current):
+        """src/xgraph/oracle.py:1637-1653."""
+        if typed is not None:
+            typed += data
+        elif may_start:
+            typed, label = data, current or ()
+        if typed is None or not delimiter.startswith(typed):
+            return None, ()
+        return typed, label
+
+    def _span_step(self, state: OracleState, token: int, data: bytes, ctx: _SpanContext):
+        label = None
+        if state.typed is not None and self._candidates(state, (*state.typed, token)):
+            label = (*state.typed, token)
+        closing, closing_label = self._branch(
+            state.closing, state.closing_label, data, self._closer, ctx.closes, state.typed)
+        separating, separating_label = self._branch(
+            state.separating, state.separating_label, data, self._separator, ctx.separates, state.typed)
+        escaping, _ = self._branch(state.escaping, (), data, self._escape, ctx.escapes, state.typed)
+
+        if closing == self._closer and state.segment is Segment.RELATION:  # a path ends
+            frontier = self._frontier(state, closing_label)
+            if self._committed:
+                best = min(frontier.values())
+                frontier = {e: rank for e, rank in frontier.items() if rank == best}
+            rows = self._rows_for(frontier)
+            return OracleState(
+                Phase.FREE,
+                last_span=ClosedSpan((*state.written, closing_label), tuple(sorted(frontier)), (), True),
+                facts=state.facts,
+                reached=frozenset(rows[:MAX_REACHED]),
+                version=state.version,
+            )
+        if closing == self._closer:
+            facts, reached = state.facts, state.reached
+            if state.segment is Segment.OBJECT:
+                if len(facts) < MAX_FACTS:
+                    facts = (*facts, (*state.written, closing_label))
+                if self._derivation:
+                    reached = self._reached(state, closing_label)
+            return OracleState(
+                Phase.FREE,
+                last_span=self._resolve(state, closing_label),
+                answer_complete=self._end_after_answer and self._answers_path(state),
+                facts=facts,
+                reached=reached,
+                version=state.version,
+            )
+        if separating == self._separator:
+            return self._next_segment(state, separating_label)
+        if escaping == self._escape:
+            return OracleState(Phase.ESCAPED, last_span=state.last_span, facts=state.facts,
+                               reached=state.reached, version=state.version)
+        if label is None and closing is None and separating is None and escaping is None:
+            return None
+        return replace(
+            state,
+            typed=label,
+            closing=closing,
+            closing_label=closing_label,
+            separating=separating,
+            separating_label=separating_label,
+            escaping=escaping,
+        )
+
+    # -- resolution and frontiers (src/xgraph/oracle.py:1655-1922) ---------------
+
+    def _resolve(self, state: OracleState, label) -> ClosedSpan:
+        rows = [(item, row) for _, item, row in self._candidates(state, label, exact=True)]
+        if state.segment is Segment.SUBJECT and self._derivation and state.reached is not None:
+            return ClosedSpan((label,), (self._best_connected(state, rows)[0],), (), True)
+        if state.segment is Segment.SUBJECT:
+            return ClosedSpan((label,), tuple(sorted(e for e, _ in rows)), (), True)
+        objects = {row: entity for entity, row in rows}
+        triples = {
+            (s, r, objects[o]) for s, r, o in self._graph(state).edges
+            if s in state.subjects and r in state.relations and o in objects
+        }
+        return ClosedSpan((*state.written, label), (), tuple(sorted(triples)), True)
+
+    def _may_escape(self, state: OracleState) -> bool:
+        bound = state.segment is Segment.SUBJECT and self._derivation and bool(state.reached)
+        return self._bound_escapes or not bound
+
+    def _best_connected(self, state: OracleState, rows) -> list[str]:
+        degree, sitelinks = self._graph(state).degree, self._sitelinks
+        ordered = sorted(rows, key=lambda p: (-sitelinks.get(p[0], 0), -degree.get(p[0], 0), p[1]))
+        return list(dict.fromkeys(e for e, _ in ordered))
+
+    def _kept(self, ranks: dict[str, int]) -> dict[str, int]:
+        if self._committed:
+            order = sorted(ranks, key=lambda e: (ranks[e], self._first_row[e]))
+        else:
+            order = sorted(ranks, key=self._first_row.get)
+        return {e: ranks[e] for e in order[:MAX_REACHED]}
+
+    def _frontier(self, state: OracleState, label) -> dict[str, int]:
+        relations = {r for tokens, r in self._relation_rows if tokens == label}
+        start = dict(state.ranks)
+        ranks: dict[str, int] = {}
+        for s, r, o in self._graph(state).from_subjects(state.subjects):
+            if s in state.subjects and r in relations:
+                entity = self._entity_rows[o][1]
+                ranks[entity] = min(ranks.get(entity, start[s]), start[s])
+        return self._kept(ranks)
+
+    def _answers_path(self, state: OracleState) -> bool:
+        last = state.last_span
+        return self._paths and last is not None and (len(last.labels) > 1 or last.path)
+
+    def _reached(self, state: OracleState, label) -> frozenset[int]:
+        rows = {row for _, _, row in self._candidates(state, label, exact=True)}
+        entities = {
+            self._entity_rows[o][1] for s, r, o in self._graph(state).edges
+            if s in state.subjects and r in state.relations and o in rows
+        }
+        reached = [row for row, (_, e) in enumerate(self._entity_rows) if e in entities]
+        return frozenset(reached[:MAX_REACHED])
+
+    def _next_segment(self, state: OracleState, label) -> OracleState:
+        candidates = [(item, row) for _, item, row in self._candidates(state, label, exact=True)]
+        items = [item for item, _ in candidates]
+        written = (*state.written, label)
+        graph = self._graph(state)
+        if state.segment is Segment.SUBJECT:
+            subjects = frozenset(e for e in items if e in graph.has_triples)
+            ranks: dict[str, int] = {}
+            if self._paths:
+                starts = self._best_connected(state, [(e, r) for e, r in candidates if e in subjects])
+                ranks = self._kept({e: rank for rank, e in enumerate(starts)})
+                subjects = frozenset(ranks)
+            if not self._paths and self._derivation and subjects:
+                best = self._best_connected(state, [(e, r) for e, r in candidates if e in subjects])
+                subjects = frozenset(best[:1])
+            return OracleState(
+                Phase.SPAN, segment=Segment.RELATION, subjects=subjects, written=written,
+                last_span=state.last_span, facts=state.facts, reached=state.reached,
+                version=state.version, ranks=tuple(sorted(ranks.items())),
+            )
+        if self._paths:
+            frontier = self._frontier(state, label)
+            return OracleState(
+                Phase.SPAN, segment=Segment.RELATION, subjects=frozenset(frontier), written=written,
+                last_span=state.last_span, facts=state.facts, reached=state.reached,
+                version=state.version, ranks=tuple(sorted(frontier.items())),
+            )
+        return OracleState(
+            Phase.SPAN, segment=Segment.OBJECT, subjects=state.subjects, relations=frozenset(items),
+            written=written, last_span=state.last_span, facts=state.facts, reached=state.reached,
+            version=state.version,
+        )

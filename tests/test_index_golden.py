@@ -1,0 +1,52 @@
+"""The index builder and version tables against the reference's compiled arrays."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from tests.conftest import case_index, case_versions, golden_index, golden_walks, golden_worlds, world
+
+
+@pytest.mark.parametrize("name", sorted(golden_worlds()))
+def test_index_arrays_equal_reference(name):
+    from xgraph_b200.index import build_kg_index
+    from xgraph_b200.syntax import SpanSyntax
+
+    kg, served, sitelinks = world(name)
+    index = build_kg_index(kg, served, SpanSyntax(), sitelinks=sitelinks)
+    ref = golden_index()
+    for part in ("labels", "relations"):
+        rows = getattr(index, part)
+        for field in ("tokens", "offsets", "owners"):
+            np.testing.assert_array_equal(getattr(rows, field), ref[f"{name}/{part}.{field}"], f"{part}.{field}")
+    for field in ("adjacency_offsets", "edge_relations", "edge_objects", "sitelinks"):
+        np.testing.assert_array_equal(getattr(index, field), ref[f"{name}/{field}"], field)
+    assert index.unwritable_triples == int(ref[f"{name}/unwritable"][0])
+    excluded = [f"{e.owner_id}\t{e.label}\t{e.reason}" for e in index.labels.excluded]
+    assert excluded == list(ref[f"{name}/excluded"])
+
+
+@pytest.mark.parametrize("name", [c["name"] for c in golden_walks() if c["versions"]])
+def test_version_tables_equal_reference(name):
+    from xgraph_b200.kgversions import build_kg_versions
+
+    case = next(c for c in golden_walks() if c["name"] == name)
+    versions = build_kg_versions(case_index(case), case_versions(case))
+    ref = golden_index()
+    for mine, theirs in (
+        ("offsets", "version_offsets"), ("subjects", "version_subjects"),
+        ("adjacency", "version_adjacency"), ("edge_relations", "version_edge_relations"),
+        ("edge_objects", "version_edge_objects"),
+    ):
+        np.testing.assert_array_equal(getattr(versions, mine), ref[f"{name}/{theirs}"], mine)
+
+
+def test_prefix_range_matches_linear_scan():
+    index = case_index({"world": "toy", "options": {}})
+    labels = index.labels
+    rows = [labels.row_tokens(r) for r in range(labels.num_rows)]
+    prefixes = {row[:k] for row in rows for k in range(len(row) + 1)}
+    for prefix in prefixes:
+        hits = [r for r, row in enumerate(rows) if row[: len(prefix)] == prefix]
+        assert labels.prefix_range(prefix) == (hits[0], hits[-1] + 1)

@@ -1,0 +1,447 @@
+"""KG index: tokenized label rows, relation rows and CSR adjacency.
+
+The tables and their order are the reference's (src/xgraph/index.py:51-101, 181-233,
+236-300, 403-516), because the engine's row ranges and the oracle's states name rows
+by position:
+
+- one label row per distinct (item, label) pair, holding the tokens of
+  ``label_prefix + label``; blank labels, labels holding span syntax, and labels whose
+  encoding does not round-trip to their exact bytes (exact-v1) are excluded;
+- rows sorted as token tuples, a row that ends sorting before the rows that continue
+  it, ties broken by item position; so a typed token prefix selects one contiguous row
+  range, and inside it every token column is sorted;
+- adjacency: for every writable triple, one edge per label row of the object, deduped,
+  sorted by (subject, relation, object row), in CSR by subject position.
+
+The build here is vectorised with numpy (lexsort on padded token columns, one int64
+key per edge) so that million-entity graphs build in seconds; `build_kg_index_arrays`
+takes numeric triples directly for graphs too large for Python tuples.
+"""
+
+from __future__ import annotations
+
+import bisect
+import hashlib
+import json
+from collections.abc import Mapping, Sequence
+from dataclasses import dataclass, field
+from pathlib import Path
+
+import numpy as np
+
+from .kg import Entity, KGFormatError, KnowledgeGraph, Relation, validate
+from .syntax import SpanSyntax
+from .tokenizer import ServedTokenizer
+
+END = -1
+"""Column value past a row's last token; sorts before every token id."""
+
+
+class UnknownId(LookupError):
+    """A query names an entity or relation the KG index does not hold."""
+
+
+class IndexMismatch(ValueError):
+    """The KG index, tokenizer, or KG-version base identity differs."""
+
+
+@dataclass(frozen=True)
+class ExcludedLabel:
+    owner_id: str
+    label: str
+    reason: str
+
+
+@dataclass(frozen=True)
+class LabelIndex:
+    """Sorted label rows: row r is ``tokens[offsets[r]:offsets[r+1]]``, naming
+    ``owner_ids[owners[r]]``."""
+
+    tokens: np.ndarray  # int32
+    offsets: np.ndarray  # int64 [rows + 1]
+    owners: np.ndarray  # int32 [rows]
+    owner_ids: tuple[str, ...]
+    tokenizer_fingerprint: str
+    excluded: tuple[ExcludedLabel, ...]
+
+    @property
+    def num_rows(self) -> int:
+        return len(self.owners)
+
+    def row_tokens(self, row: int) -> tuple[int, ...]:
+        a, b = int(self.offsets[row]), int(self.offsets[row + 1])
+        return tuple(int(t) for t in self.tokens[a:b])
+
+    def owner_id(self, row: int) -> str:
+        return self.owner_ids[int(self.owners[row])]
+
+    def token_at(self, row: int, depth: int) -> int:
+        a, b = int(self.offsets[row]), int(self.offsets[row + 1])
+        return int(self.tokens[a + depth]) if a + depth < b else END
+
+    def prefix_range(self, prefix: Sequence[int]) -> tuple[int, int]:
+        """Rows [lo, hi) whose tokens start with ``prefix`` (narrowed one column at a time)."""
+        lo, hi = 0, self.num_rows
+        for depth, token in enumerate(prefix):
+            rows = range(lo, hi)
+
+            def column(row: int, depth: int = depth) -> int:
+                return self.token_at(row, depth)
+
+            first = bisect.bisect_left(rows, token, key=column)
+            last = bisect.bisect_right(rows, token, key=column)
+            lo, hi = lo + first, lo + last
+        return lo, hi
+
+
+def _exact_v1_error(label: str, tokens: list[int], tokenizer, syntax: SpanSyntax) -> str | None:
+    """exact-v1 label admission (src/xgraph/index.py:167-178): no special tokens, a
+    nonempty encoding, known bytes for every token, and bytes equal to prefix + label."""
+    if tokenizer.special_ids.intersection(tokens):
+        return "label contains a special token"
+    if not tokens:
+        return "empty label encoding"
+    pieces = [tokenizer.token_bytes(t) for t in tokens]
+    if any(p is None for p in pieces):
+        return "label contains a token with unknown bytes"
+    if b"".join(pieces) != (syntax.label_prefix + label).encode("utf-8"):
+        return "label bytes do not round-trip"
+    return None
+
+
+def _sorted_rows(rows: list[tuple[list[int], int]]) -> list[int]:
+    """Permutation sorting (tokens, item) pairs as Python tuples would sort."""
+    n = len(rows)
+    if n == 0:
+        return []
+    lengths = np.fromiter((len(t) for t, _ in rows), dtype=np.int64, count=n)
+    width = int(lengths.max())
+    if width > 64:  # long labels: the plain tuple sort
+        return sorted(range(n), key=lambda i: (tuple(rows[i][0]), rows[i][1]))
+    padded = np.full((n, width), END, dtype=np.int64)
+    flat = np.fromiter((t for toks, _ in rows for t in toks), dtype=np.int64, count=int(lengths.sum()))
+    row_of = np.repeat(np.arange(n), lengths)
+    col_of = np.arange(len(flat)) - np.repeat(np.cumsum(lengths) - lengths, lengths)
+    padded[row_of, col_of] = flat
+    items = np.fromiter((i for _, i in rows), dtype=np.int64, count=n)
+    keys = [items] + [padded[:, c] for c in range(width - 1, -1, -1)]
+    return np.lexsort(keys).tolist()
+
+
+def label_rows(
+    items: Sequence[Entity | Relation] | Sequence[tuple[str, Sequence[str]]],
+    tokenizer: ServedTokenizer,
+    syntax: SpanSyntax,
+) -> LabelIndex:
+    """The label index over these items' labels (src/xgraph/index.py:181-233)."""
+    pairs: list[tuple[str, int]] = []
+    excluded: list[ExcludedLabel] = []
+    ids: list[str] = []
+    for position, item in enumerate(items):
+        item_id, labels = (item.id, item.labels) if hasattr(item, "id") else item
+        ids.append(item_id)
+        seen: set[str] = set()
+        for label in labels:
+            if label in seen:
+                continue
+            seen.add(label)
+            if not label.strip():
+                excluded.append(ExcludedLabel(item_id, label, "blank label"))
+            elif syntax.excludes(label):
+                excluded.append(ExcludedLabel(item_id, label, "label contains span syntax"))
+            else:
+                pairs.append((label, position))
+    encoded = tokenizer.encode_batch([syntax.label_prefix + label for label, _ in pairs])
+    rows: list[tuple[list[int], int]] = []
+    for (label, position), tokens in zip(pairs, encoded, strict=True):
+        reason = _exact_v1_error(label, tokens, tokenizer, syntax)
+        if reason:
+            excluded.append(ExcludedLabel(ids[position], label, reason))
+        else:
+            rows.append((tokens, position))
+    order = _sorted_rows(rows)
+    lengths = np.array([len(rows[i][0]) for i in order], dtype=np.int64)
+    offsets = np.zeros(len(order) + 1, dtype=np.int64)
+    np.cumsum(lengths, out=offsets[1:])
+    tokens = np.fromiter(
+        (t for i in order for t in rows[i][0]), dtype=np.int32, count=int(offsets[-1])
+    )
+    owners = np.array([rows[i][1] for i in order], dtype=np.int32)
+    return LabelIndex(
+        tokens=tokens,
+        offsets=offsets,
+        owners=owners,
+        owner_ids=tuple(ids),
+        tokenizer_fingerprint=tokenizer.fingerprint,
+        excluded=tuple(excluded),
+    )
+
+
+def entity_row_lists(labels: LabelIndex) -> tuple[np.ndarray, np.ndarray]:
+    """Each owner's rows in row order, as CSR: (offsets [owners + 1] int64, rows int32)."""
+    owners = np.asarray(labels.owners, dtype=np.int64)
+    count = len(labels.owner_ids)
+    order = np.argsort(owners, kind="stable").astype(np.int32)
+    offsets = np.zeros(count + 1, dtype=np.int64)
+    np.cumsum(np.bincount(owners, minlength=count), out=offsets[1:])
+    return offsets, order
+
+
+@dataclass(frozen=True)
+class KGIndex:
+    """A source KG compiled for one served tokenizer and span syntax."""
+
+    labels: LabelIndex
+    relations: LabelIndex
+    adjacency_offsets: np.ndarray  # int64 [entities + 1]
+    edge_relations: np.ndarray  # int32 [edges]
+    edge_objects: np.ndarray  # int32 [edges], object label rows
+    unwritable_triples: int
+    span_syntax: SpanSyntax = field(default_factory=SpanSyntax)
+    sitelinks: np.ndarray | None = None
+    date_entities: np.ndarray | None = None
+    date_keys: np.ndarray | None = None
+    verdicts: dict[str, str] | None = None
+    expressions: bool = True
+    base_fingerprint: str = ""
+
+    @property
+    def tokenizer_fingerprint(self) -> str:
+        return self.labels.tokenizer_fingerprint
+
+    def edges_at(self, entity: int) -> tuple[np.ndarray, np.ndarray]:
+        a, b = int(self.adjacency_offsets[entity]), int(self.adjacency_offsets[entity + 1])
+        return self.edge_relations[a:b], self.edge_objects[a:b]
+
+    def _position(self, table: str, item: str, kind: str) -> int:
+        cache = self.__dict__.get(table)
+        if cache is None:
+            owner_ids = self.labels.owner_ids if table == "_entity_at" else self.relations.owner_ids
+            cache = {name: n for n, name in enumerate(owner_ids)}
+            object.__setattr__(self, table, cache)
+        if item not in cache:
+            raise UnknownId(f"the KG index holds no {kind} {item!r}")
+        return cache[item]
+
+    def relations_of(self, subject: str) -> list[str]:
+        relations, _ = self.edges_at(self._position("_entity_at", subject, "entity"))
+        return [self.relations.owner_ids[r] for r in np.unique(relations)]
+
+    def object_rows(self, subject: str, relation: str, lo: int = 0, hi: int | None = None) -> list[int]:
+        relations, objects = self.edges_at(self._position("_entity_at", subject, "entity"))
+        r = self._position("_relation_at", relation, "relation")
+        a, b = np.searchsorted(relations, r, "left"), np.searchsorted(relations, r, "right")
+        objects = objects[a:b]
+        hi = self.labels.num_rows if hi is None else hi
+        x, y = np.searchsorted(objects, lo, "left"), np.searchsorted(objects, hi, "left")
+        return [int(o) for o in objects[x:y]]
+
+
+def _fingerprint(index_parts: dict) -> str:
+    digest = hashlib.sha256()
+    for name in sorted(index_parts):
+        value = index_parts[name]
+        digest.update(name.encode())
+        if isinstance(value, np.ndarray):
+            digest.update(str((value.dtype.str, value.shape)).encode())
+            digest.update(np.ascontiguousarray(value).tobytes())
+        else:
+            digest.update(json.dumps(value, sort_keys=True, default=str).encode())
+    return digest.hexdigest()
+
+
+def sitelink_array(counts, entities: int) -> np.ndarray:
+    array = np.asarray(counts, dtype=np.int64).reshape(-1)
+    if len(array) != entities:
+        raise ValueError(
+            f"a KG index needs one sitelink count per entity ({entities}), got {len(array)}"
+        )
+    if len(array) and int(array.min()) < 0:
+        raise ValueError(f"sitelink counts cannot be negative, got {int(array.min())}")
+    if len(array) and int(array.max()) > np.iinfo(np.int32).max:
+        raise ValueError(f"a sitelink count of {int(array.max())} does not fit in int32")
+    return array.astype(np.int32)
+
+
+def _adjacency(
+    labels: LabelIndex, writable_relations: np.ndarray, subjects: np.ndarray,
+    relations: np.ndarray, objects: np.ndarray, entities: int,
+) -> tuple[np.ndarray, np.ndarray, np.ndarray, int]:
+    """CSR edges from position triples: one edge per object label row, deduped and sorted."""
+    row_offsets, row_list = entity_row_lists(labels)
+    row_counts = np.diff(row_offsets)
+    ok = (row_counts[subjects] > 0) & (row_counts[objects] > 0) & writable_relations[relations]
+    unwritable = int(len(subjects) - int(ok.sum()))
+    s, r, o = subjects[ok].astype(np.int64), relations[ok].astype(np.int64), objects[ok]
+    repeat = row_counts[o]
+    starts = np.repeat(row_offsets[o], repeat)
+    within = np.arange(int(repeat.sum()), dtype=np.int64) - np.repeat(np.cumsum(repeat) - repeat, repeat)
+    rows = row_list[starts + within].astype(np.int64)
+    s, r = np.repeat(s, repeat), np.repeat(r, repeat)
+    n_rel = max(1, len(writable_relations))
+    n_rows = max(1, labels.num_rows)
+    if entities * n_rel * n_rows < (1 << 62):
+        keys = np.unique((s * n_rel + r) * n_rows + rows)
+        rows_out = keys % n_rows
+        rel_out = (keys // n_rows) % n_rel
+        subj_out = keys // (n_rows * n_rel)
+    else:  # pragma: no cover - astronomically large indexes
+        stacked = np.unique(np.stack([s, r, rows], axis=1), axis=0)
+        subj_out, rel_out, rows_out = stacked[:, 0], stacked[:, 1], stacked[:, 2]
+    offsets = np.zeros(entities + 1, dtype=np.int64)
+    np.cumsum(np.bincount(subj_out, minlength=entities), out=offsets[1:])
+    return offsets, rel_out.astype(np.int32), rows_out.astype(np.int32), unwritable
+
+
+def build_kg_index_arrays(
+    entities: Sequence[tuple[str, Sequence[str]]],
+    relations: Sequence[tuple[str, Sequence[str]]],
+    triples: np.ndarray,
+    tokenizer: ServedTokenizer,
+    syntax: SpanSyntax,
+    sitelinks: np.ndarray | Sequence[int] | None = None,
+) -> KGIndex:
+    """The KG index of entities and relations given as (id, labels) and triples given as
+    an int (n, 3) array of (subject position, relation position, object position)."""
+    triples = np.asarray(triples, dtype=np.int64).reshape(-1, 3)
+    if len(triples) and (
+        triples.min() < 0
+        or triples[:, 0].max() >= len(entities)
+        or triples[:, 2].max() >= len(entities)
+        or triples[:, 1].max() >= len(relations)
+    ):
+        raise KGFormatError("triples name entity or relation positions outside the KG")
+    labels = label_rows(entities, tokenizer, syntax)
+    relation_index = label_rows(relations, tokenizer, syntax)
+    writable = np.zeros(len(relations), dtype=bool)
+    writable[np.asarray(relation_index.owners, dtype=np.int64)] = True
+    offsets, edge_rel, edge_obj, unwritable = _adjacency(
+        labels, writable, triples[:, 0], triples[:, 1], triples[:, 2], len(entities)
+    )
+    counts = None if sitelinks is None else sitelink_array(sitelinks, len(entities))
+    parts = {
+        "labels.tokens": labels.tokens, "labels.offsets": labels.offsets,
+        "labels.owners": labels.owners, "labels.ids": list(labels.owner_ids),
+        "relations.tokens": relation_index.tokens, "relations.offsets": relation_index.offsets,
+        "relations.owners": relation_index.owners, "relations.ids": list(relation_index.owner_ids),
+        "adjacency_offsets": offsets, "edge_relations": edge_rel, "edge_objects": edge_obj,
+        "tokenizer": tokenizer.fingerprint, "syntax": repr(syntax),
+        "sitelinks": counts if counts is not None else "none",
+    }
+    return KGIndex(
+        labels=labels,
+        relations=relation_index,
+        adjacency_offsets=offsets,
+        edge_relations=edge_rel,
+        edge_objects=edge_obj,
+        unwritable_triples=unwritable,
+        span_syntax=syntax,
+        sitelinks=counts,
+        base_fingerprint=_fingerprint(parts),
+    )
+
+
+def build_kg_index(
+    kg: KnowledgeGraph,
+    tokenizer: ServedTokenizer,
+    syntax: SpanSyntax,
+    sitelinks: Mapping[str, int] | None = None,
+    dates=None,
+    verdicts: bool = False,
+    *,
+    initial_case_aliases: bool = False,
+) -> KGIndex:
+    """The KG index of an in-memory KG (src/xgraph/index.py:403-516).
+
+    Date tables, verdict entities and initial-case aliases feed the reference's
+    expression and alias policies, which this engine does not implement; asking
+    for them raises ValueError rather than building a different index.
+    """
+    if dates is not None or verdicts or initial_case_aliases:
+        raise ValueError(
+            "dates, verdicts and initial_case_aliases belong to policies this engine "
+            "does not implement"
+        )
+    validate(kg)
+    entity_at = {e.id: n for n, e in enumerate(kg.entities)}
+    relation_at = {r.id: n for n, r in enumerate(kg.relations)}
+    triples = np.array(
+        [(entity_at[s], relation_at[r], entity_at[o]) for s, r, o in kg.triples], dtype=np.int64
+    ).reshape(-1, 3)
+    counts = None
+    if sitelinks is not None:
+        counts = [sitelinks.get(e.id, 0) for e in kg.entities]
+    return build_kg_index_arrays(
+        [(e.id, e.labels) for e in kg.entities],
+        [(r.id, r.labels) for r in kg.relations],
+        triples,
+        tokenizer,
+        syntax,
+        sitelinks=counts,
+    )
+
+
+START_RANKS = ("degree", "sitelinks")
+
+
+def check_start_rank(start_rank: str, index) -> str:
+    if start_rank not in START_RANKS:
+        raise ValueError(f"start_rank must be one of {START_RANKS}, got {start_rank!r}")
+    if start_rank == "sitelinks":
+        if index.sitelinks is None:
+            raise ValueError("the sitelink rank needs a KG index with sitelink counts")
+        sitelink_array(index.sitelinks, len(index.labels.owner_ids))
+    return start_rank
+
+
+def save_kg_index(index: KGIndex, directory: str | Path) -> None:
+    """Write the index as one .npz of arrays plus a JSON header of ids and identity."""
+    directory = Path(directory)
+    directory.mkdir(parents=True, exist_ok=True)
+    arrays = {
+        "labels_tokens": index.labels.tokens, "labels_offsets": index.labels.offsets,
+        "labels_owners": index.labels.owners, "relations_tokens": index.relations.tokens,
+        "relations_offsets": index.relations.offsets, "relations_owners": index.relations.owners,
+        "adjacency_offsets": index.adjacency_offsets, "edge_relations": index.edge_relations,
+        "edge_objects": index.edge_objects,
+    }
+    if index.sitelinks is not None:
+        arrays["sitelinks"] = index.sitelinks
+    np.savez(directory / "kg-index.npz", **arrays)
+    header = {
+        "format": "xgraph-b200-index-1",
+        "tokenizer_fingerprint": index.tokenizer_fingerprint,
+        "span_syntax": {k: getattr(index.span_syntax, k) for k in index.span_syntax.__dataclass_fields__},
+        "unwritable_triples": index.unwritable_triples,
+        "labels": {"owner_ids": list(index.labels.owner_ids),
+                   "excluded": [[e.owner_id, e.label, e.reason] for e in index.labels.excluded]},
+        "relations": {"owner_ids": list(index.relations.owner_ids),
+                      "excluded": [[e.owner_id, e.label, e.reason] for e in index.relations.excluded]},
+        "base_fingerprint": index.base_fingerprint,
+    }
+    (directory / "kg-index.json").write_text(json.dumps(header) + "\n", encoding="utf-8")
+
+
+def load_kg_index(directory: str | Path) -> KGIndex:
+    directory = Path(directory)
+    header = json.loads((directory / "kg-index.json").read_text(encoding="utf-8"))
+    if header.get("format") != "xgraph-b200-index-1":
+        raise ValueError(f"{directory} holds no index of this library's format")
+    data = np.load(directory / "kg-index.npz")
+    syntax = SpanSyntax(**header["span_syntax"])
+
+    def part(name: str) -> LabelIndex:
+        return LabelIndex(
+            tokens=data[f"{name}_tokens"], offsets=data[f"{name}_offsets"],
+            owners=data[f"{name}_owners"], owner_ids=tuple(header[name]["owner_ids"]),
+            tokenizer_fingerprint=header["tokenizer_fingerprint"],
+            excluded=tuple(ExcludedLabel(*e) for e in header[name]["excluded"]),
+        )
+
+    return KGIndex(
+        labels=part("labels"), relations=part("relations"),
+        adjacency_offsets=data["adjacency_offsets"], edge_relations=data["edge_relations"],
+        edge_objects=data["edge_objects"], unwritable_triples=header["unwritable_triples"],
+        span_syntax=syntax, sitelinks=data["sitelinks"] if "sitelinks" in data else None,
+        base_fingerprint=header["base_fingerprint"],
+    )
