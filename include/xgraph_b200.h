@@ -1,0 +1,173 @@
+/* xgraph-b200: C ABI of the B200-native KG constraint engine.
+ *
+ * This is the boundary the reference's Python engine binds through nanobind
+ * (csrc/engine.cu:3191-3256, class Engine); here every method is a plain extern "C"
+ * function over raw pointers, sizes and a cudaStream_t passed as void*, so any FFI
+ * (ctypes, cffi, cgo, JNI) can bind it.  No torch or DLPack type crosses it.
+ *
+ * Conventions
+ *   - Every function returns XG_OK (0) or an error code; xg_last_error() gives the
+ *     message of the calling thread's last error.  XG_EINVAL maps to the reference's
+ *     std::invalid_argument (Python ValueError), XG_ECUDA to std::runtime_error after
+ *     a CUDA failure (the sticky error is cleared, as csrc/engine.cu:210-215 does).
+ *   - Device pointers are CUDA device addresses on the engine's device; "host"
+ *     arguments are ordinary host memory.  All work is enqueued on `stream`
+ *     (NULL = legacy default stream) unless the function says it waits.
+ *   - Token masks are uint32 words, bit i of word w = token 32*w + i (little-endian),
+ *     as src/xgraph/engine.py:86-94 packs them.
+ */
+#ifndef XGRAPH_B200_H
+#define XGRAPH_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define XG_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define XG_API __attribute__((visibility("default")))
+#else
+#define XG_API
+#endif
+
+enum xg_status {
+  XG_OK = 0,
+  XG_EINVAL = 1,  /* invalid argument (reference: std::invalid_argument -> ValueError) */
+  XG_ECUDA = 2,   /* a CUDA call failed (reference: std::runtime_error) */
+  XG_ENOMEM = 3,  /* a device allocation failed */
+};
+
+enum xg_dtype { XG_F32 = 0, XG_BF16 = 1, XG_F16 = 2 };
+
+/* Per-slot constraint state: 64 int32 words.  The first 31 fields carry the names and
+ * meaning of the reference's public state projection (csrc/engine.cu:3200-3211 STATE_FIELDS,
+ * read by tests/test_engine.py:1666-1730): phase (0 free, 1 span, 2 escaped, 3 error),
+ * pos (opener/closer bytes matched outside a span), segment (0 subject, 1 relation,
+ * 2 object), depth, [lo, hi) the typed label's row range (-1 when the label branch is
+ * dead), the closer/separator branches' bytes matched and the label rows they started
+ * after, the escape branch's bytes matched, the candidate subject and relation rows,
+ * subj_key (first row of the subject label), hops (relations of the open path, this one
+ * included), four expression fields (always 0: expressions are not served), the
+ * end-after-answer flag and the last closed span (kind 0 none, 1 unresolved, 2 entity,
+ * 3 fact, 4 path; its rows).  ex_hi and flags are this engine's own: the end of the
+ * typed label's exact rows and which delimiter branches may start next. */
+typedef struct XgState {
+  int32_t phase, pos, segment, depth, lo, hi;
+  int32_t close_pos, close_lo, close_hi;
+  int32_t sep_pos, sep_lo, sep_hi;
+  int32_t esc_pos;
+  int32_t subj_lo, subj_hi, rel_lo, rel_hi, subj_key, hops;
+  int32_t op_pos, op_kind, op, operand;
+  int32_t answer_complete;
+  int32_t last_kind, last_lo, last_hi, last_subj_lo, last_subj_hi, last_rel_lo, last_rel_hi;
+  int32_t ex_hi, flags;
+  int32_t reserved[31];
+} XgState;
+
+#define XG_STATE_INTS 64
+
+/* Where each table lives in the packed index blob: byte offsets (16-byte aligned; -1 for
+ * an absent optional table) and the sizes the kernels need.  Built by the host-side
+ * table packer (xgraph_b200/tables.py, the counterpart of src/xgraph/engine.py:311-556
+ * native_tables). */
+typedef struct XgLayout {
+  int64_t blob_bytes;
+  int32_t vocab, words, words_padded;
+  int32_t entity_rows, relation_rows, entities, relations, relation_words;
+  int32_t opener_len, closer_len, separator_len, escape_len;
+  int32_t versions, wide_count;
+  int32_t pad0;
+  int64_t ent_tok, ent_off, ent_owner, rel_tok, rel_off, rel_owner;
+  int64_t ent_first_row, ent_rows_off, ent_rows;
+  int64_t adj_off, edge_rel, edge_obj;
+  int64_t sitelinks, kept_prefix;
+  int64_t root_mask, wide_keys, wide_masks;
+  int64_t free_next, free_mask, esc_next, esc_mask, eos_mask;
+  int64_t closer_off, closer_tok, closer_next;
+  int64_t separator_off, separator_tok, separator_next;
+  int64_t escape_off, escape_tok, escape_next;
+  int64_t ver_off, ver_subj, ver_adj, ver_edge_rel, ver_edge_obj;
+} XgLayout;
+
+/* Span-language policies, as the reference Engine's constructor flags
+ * (src/xgraph/engine.py:582-623).  Expressions, STOP, observation, menu, audit,
+ * release and escape-bias policies are not part of this engine. */
+typedef struct XgOptions {
+  int32_t escapes, repeats, derivation, paths, bound_escapes, committed_paths;
+  int32_t sitelinks_rank, end_after_answer;
+} XgOptions;
+
+typedef struct XgInfo {
+  int32_t max_sequences, vocab, words, words_padded, memory_ints, device;
+} XgInfo;
+
+typedef struct XgEngine XgEngine;
+
+/* Message of this thread's last failed call ("" if none). */
+XG_API const char* xg_last_error(void);
+XG_API int32_t xg_abi_version(void);
+
+/* Engine(tables, vocab, words, max_sequences, ...) (csrc/engine.cu:2600-2797): copy the
+ * packed index blob (host memory) to the current device and allocate max_sequences slots,
+ * all inactive in the initial state. */
+XG_API int xg_create(const void* blob_host, const XgLayout* layout, const XgOptions* options,
+              int32_t max_sequences, XgEngine** out);
+/* As xg_create from a blob already on the current device (for example one received by an
+ * NCCL broadcast); the engine copies it and does not keep the caller's pointer. */
+XG_API int xg_create_from_device(const void* blob_device, const XgLayout* layout,
+                          const XgOptions* options, int32_t max_sequences, XgEngine** out);
+XG_API int xg_destroy(XgEngine* engine);
+XG_API int xg_info(const XgEngine* engine, XgInfo* out);
+
+/* Engine::reset (csrc/engine.cu:2799-2814): every slot inactive, initial state. */
+XG_API int xg_reset(XgEngine* engine, void* stream);
+/* Engine::begin (csrc/engine.cu:2818-2826): slots (device int32[count]) back to the
+ * initial state, base KG, cursor unset; active = on. */
+XG_API int xg_begin(XgEngine* engine, const int32_t* slots, int32_t count, int32_t on, void* stream);
+/* Engine::set_reached (csrc/engine.cu:2840-2860): anchor rows (host int32, sorted; the
+ * first 64 are kept). */
+XG_API int xg_set_reached(XgEngine* engine, int32_t slot, const int32_t* rows, int32_t count, void* stream);
+/* Engine::set_version (csrc/engine.cu:2864-2876): 0 = base KG, 1..versions. */
+XG_API int xg_set_version(XgEngine* engine, int32_t slot, int32_t version, void* stream);
+/* Engine::open_span (csrc/engine.cu:2955-2962): the slot starts inside a span. */
+XG_API int xg_open_span(XgEngine* engine, int32_t slot, void* stream);
+/* Engine::advance (csrc/engine.cu:3041-3054): advance slots 0..count-1 by tokens[i];
+ * tokens_on_host != 0 means host memory (copied first). */
+XG_API int xg_advance(XgEngine* engine, const int32_t* tokens, int32_t count, int32_t tokens_on_host,
+               void* stream);
+/* Engine::sync (csrc/engine.cu:2966-2985): each listed active slot advances over
+ * history[slot * history_stride + cursor .. total_len[slot]) (cursor = prompt_len[slot]
+ * the first time); history, prompt_len and total_len are device (or pinned host)
+ * memory with one row / entry per slot (history_rows and lengths_count >= max_sequences). */
+XG_API int xg_sync(XgEngine* engine, const int32_t* slots, int32_t count, const int32_t* history,
+            int64_t history_stride, int64_t history_rows, const int32_t* prompt_len,
+            const int32_t* total_len, int64_t lengths_count, void* stream);
+/* Engine::fill_mask (csrc/engine.cu:3056-3062): materialize the masks of slots
+ * 0..sequences-1 into the mask buffer. */
+XG_API int xg_fill_mask(XgEngine* engine, int32_t sequences, void* stream);
+/* Engine::mask: the device mask buffer, max_sequences rows of words_padded uint32. */
+XG_API int xg_mask_device(XgEngine* engine, uint32_t** out);
+/* Engine::mask_host / states_host (csrc/engine.cu:3076-3084): wait for the device, then
+ * copy sequences x words mask words / sequences x XG_STATE_INTS state words. */
+XG_API int xg_mask_host(XgEngine* engine, int32_t sequences, uint32_t* out);
+XG_API int xg_states_host(XgEngine* engine, int32_t sequences, int32_t* out);
+/* Diagnostic: wait, then copy the slots' memory (facts, reached rows, frontier, version). */
+XG_API int xg_memory_host(XgEngine* engine, int32_t sequences, int32_t* out);
+/* Engine::apply_mask (csrc/engine.cu:2990-3037): in place, logits[r, c] = -inf for every
+ * column c its slot's mask disallows and every c >= vocab; rows of inactive slots and of
+ * slots in the error phase are left untouched.  logits: device, dtype XG_F32/XG_BF16/XG_F16,
+ * rows x cols with row_stride elements between rows.  row_slots: device int32[rows].
+ * local_pos/input_ids: device int32[rows] for speculative draft rows, or both NULL. */
+XG_API int xg_apply_mask(XgEngine* engine, void* logits, int32_t dtype, int32_t rows, int32_t cols,
+                  int64_t row_stride, const int32_t* row_slots, const int32_t* local_pos,
+                  const int32_t* input_ids, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* XGRAPH_B200_H */

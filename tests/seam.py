@@ -1,0 +1,98 @@
+"""The host test seam: the engine's per-row logic (xgraph_b200/csrc/core.cuh) built with
+g++ as a sequential library (seam.cpp), driven through ctypes.  Test infrastructure: it
+checks the kernels' logic against the oracle on the CPU; the product never loads it."""
+
+from __future__ import annotations
+
+import ctypes
+import subprocess
+from functools import cache
+from pathlib import Path
+
+import numpy as np
+
+from xgraph_b200.engine import STATE_FIELDS, STATE_INTS
+from xgraph_b200.tables import XgLayout, XgOptions, pack_tables
+
+ROOT = Path(__file__).resolve().parents[1]
+SOURCE = ROOT / "xgraph_b200" / "csrc" / "seam.cpp"
+BUILT = ROOT / "tests" / "_seam" / "libxgseam.so"
+
+
+@cache
+def library():
+    BUILT.parent.mkdir(exist_ok=True)
+    sources = [SOURCE, SOURCE.with_name("core.cuh"), ROOT / "include" / "xgraph_b200.h"]
+    if not BUILT.exists() or BUILT.stat().st_mtime < max(p.stat().st_mtime for p in sources):
+        subprocess.run(["g++", "-std=c++17", "-O2", "-g", "-fPIC", "-shared", "-o", str(BUILT), str(SOURCE)], check=True)
+    lib = ctypes.CDLL(str(BUILT))
+    p, i32 = ctypes.c_void_p, ctypes.c_int32
+    lib.xgs_create.argtypes = [p, ctypes.POINTER(XgLayout), ctypes.POINTER(XgOptions), i32]
+    lib.xgs_create.restype = p
+    for name, args in {
+        "xgs_destroy": [p], "xgs_begin": [p, i32, i32], "xgs_set_version": [p, i32, i32],
+        "xgs_set_reached": [p, i32, p, i32], "xgs_open_span": [p, i32], "xgs_advance": [p, p, i32],
+        "xgs_masks": [p, i32, p], "xgs_states": [p, i32, p], "xgs_memory": [p, i32, p],
+    }.items():
+        getattr(lib, name).argtypes = args
+        getattr(lib, name).restype = None
+    lib.xgs_memory_ints.argtypes = [p]
+    lib.xgs_memory_ints.restype = i32
+    return lib
+
+
+class SeamEngine:
+    """Engine-shaped driver of the seam (slots 0..n-1)."""
+
+    def __init__(self, index, tokenizer, syntax, slots, *, versions=None, escapes=True, repeats=True,
+                 derivation=False, paths=False, bound_escapes=True, committed_paths=False,
+                 start_rank="degree", unquoted_starts=False, end_after_answer=False, eos_token_ids=()):
+        self.lib = library()
+        self.index, self.versions = index, versions
+        self.tables = pack_tables(index, tokenizer, syntax, escapes=escapes, versions=versions,
+                                  unquoted_starts=unquoted_starts,
+                                  eos_token_ids=sorted(eos_token_ids) if end_after_answer else ())
+        self.options = XgOptions(escapes=int(escapes), repeats=int(repeats), derivation=int(derivation or paths),
+                                 paths=int(paths), bound_escapes=int(bound_escapes),
+                                 committed_paths=int(committed_paths),
+                                 sitelinks_rank=int(start_rank == "sitelinks"),
+                                 end_after_answer=int(end_after_answer))
+        self.slots = slots
+        self.handle = self.lib.xgs_create(self.tables.blob.ctypes.data_as(ctypes.c_void_p),
+                                          ctypes.byref(self.tables.layout), ctypes.byref(self.options), slots)
+
+    def __del__(self):
+        if getattr(self, "handle", None):
+            self.lib.xgs_destroy(self.handle)
+
+    def begin(self, slot):
+        self.lib.xgs_begin(self.handle, slot, 1)
+
+    def set_version(self, slot, name):
+        self.lib.xgs_set_version(self.handle, slot, 0 if name is None else self.versions.number(name))
+
+    def anchor(self, slot, entities):
+        labels = self.index.labels
+        rows = sorted(r for r in range(labels.num_rows) if labels.owner_id(r) in set(entities))
+        arr = np.ascontiguousarray(rows[:64], dtype=np.int32)
+        self.lib.xgs_set_reached(self.handle, slot, arr.ctypes.data_as(ctypes.c_void_p), len(arr))
+
+    def open_span(self, slot):
+        self.lib.xgs_open_span(self.handle, slot)
+
+    def advance(self, tokens):
+        arr = np.ascontiguousarray(tokens, dtype=np.int32)
+        self.lib.xgs_advance(self.handle, arr.ctypes.data_as(ctypes.c_void_p), len(arr))
+
+    def masks(self):
+        out = np.zeros((self.slots, self.tables.words), dtype=np.uint32)
+        self.lib.xgs_masks(self.handle, self.slots, out.ctypes.data_as(ctypes.c_void_p))
+        return out
+
+    def states(self):
+        raw = np.zeros((self.slots, STATE_INTS), dtype=np.int32)
+        self.lib.xgs_states(self.handle, self.slots, raw.ctypes.data_as(ctypes.c_void_p))
+        return {name: raw[:, i].copy() for i, name in enumerate(STATE_FIELDS)}
+
+    def view(self, version):
+        return self.index if version is None else self.versions.view(self.index, version)

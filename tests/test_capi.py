@@ -1,0 +1,52 @@
+"""The C ABI library: it loads, exports every function include/xgraph_b200.h declares, and
+its host-side argument checks raise the reference's error types (no GPU work)."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def declared() -> list[str]:
+    text = (ROOT / "include" / "xgraph_b200.h").read_text()
+    return sorted(set(re.findall(r"^XG_API\s+(?:int|const char\*|int32_t)\s+(xg_\w+)\(", text, flags=re.M)))
+
+
+def test_header_declares_the_engine_lifecycle():
+    names = declared()
+    for name in ("xg_create", "xg_begin", "xg_sync", "xg_advance", "xg_apply_mask", "xg_states_host"):
+        assert name in names
+
+
+def test_library_exports_every_declared_function():
+    from xgraph_b200.build import build
+
+    path = build()
+    lib = ctypes.CDLL(str(path))
+    for name in declared():
+        assert hasattr(lib, name), name
+    lib.xg_abi_version.restype = ctypes.c_int32
+    assert lib.xg_abi_version() == 1
+
+
+def test_null_engine_calls_fail_with_einval():
+    from xgraph_b200.build import build
+
+    lib = ctypes.CDLL(str(build()))
+    lib.xg_reset.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
+    lib.xg_last_error.restype = ctypes.c_char_p
+    assert lib.xg_reset(None, None) == 1
+    assert b"null" in lib.xg_last_error()
+
+
+def test_engine_constructor_fails_loudly_without_the_library(monkeypatch, tmp_path):
+    import xgraph_b200.engine as engine
+
+    monkeypatch.setattr(engine, "_lib", None)
+    with pytest.raises(engine.EngineUnavailable):
+        engine.load_library(tmp_path / "missing.so")

@@ -1,0 +1,186 @@
+"""The CUDA engine (through its C ABI) against the golden walks and the apply contract.
+
+Mirrors the reference's GPU agreement seam (tests/test_engine.py:1733-2002, 2147-2251):
+at every step of every golden walk the device mask must equal the reference Oracle's
+allowed set and the device state must agree with the reference state's projection;
+apply_mask must write -inf exactly over disallowed columns (and columns past the
+vocabulary), leave allowed columns bit-identical, and leave inactive and error rows alone.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from tests.agreement import assert_agrees, engine_state, expected_state
+from tests.conftest import case_index, case_options, case_versions, golden_masks, golden_walks, unpack, world
+
+pytestmark = pytest.mark.gpu
+CASES = [case["name"] for case in golden_walks()]
+
+
+def engine_for(case, slots=None):
+    from xgraph_b200.engine import Engine
+    from xgraph_b200.kgversions import build_kg_versions
+    from xgraph_b200.syntax import SpanSyntax
+
+    _, served, _ = world(case["world"])
+    index = case_index(case)
+    edits = case_versions(case)
+    versions = build_kg_versions(index, edits) if edits else None
+    options = case_options(case)
+    engine = Engine(index, served, SpanSyntax(), slots or len(case["sequences"]), versions=versions, **options)
+    return engine, index, served
+
+
+def start(engine, sequences):
+    import torch
+
+    engine.reset()
+    engine.begin(torch.arange(len(sequences), dtype=torch.int32, device="cuda"))
+    for k, seq in enumerate(sequences):
+        engine.set_version(k, seq["version"])
+        if seq["anchor"]:
+            engine.anchor(k, seq["anchor"])
+        if seq["opened"]:
+            engine.open_span(k)
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_engine_agrees_with_reference_walks(name):
+    from xgraph_b200.syntax import SpanSyntax
+
+    case = next(c for c in golden_walks() if c["name"] == name)
+    engine, index, served = engine_for(case)
+    sequences = case["sequences"]
+    start(engine, sequences)
+    steps = len(sequences[0]["tokens"])
+    paths = case["options"].get("paths", False)
+    syntax = SpanSyntax()
+    for step in range(steps + 1):
+        engine.fill_mask()
+        masks = engine.mask_host().view(np.uint32)
+        states = engine.states_host()
+        for k, seq in enumerate(sequences):
+            record = seq["states"][step] if step < steps else seq["final"]
+            where = (name, k, step)
+            assert_agrees(expected_state(record, index, syntax),
+                          engine_state(states, k, engine.view(seq["version"])), paths, where)
+            if step < steps:
+                expected = unpack(golden_masks()[f"{name}/{k}"][step], served.vocab_size)
+                assert unpack(masks[k], served.vocab_size) == expected, where
+        if step < steps:
+            engine.advance(np.array([seq["tokens"][step] for seq in sequences], dtype=np.int32))
+    assert engine.errors() == 0
+
+
+@pytest.mark.parametrize("name", ["toy_ordinary", "bpe_committed", "crowd_committed"])
+def test_sync_over_history_equals_advance(name):
+    """sync reads each slot's history in place from prompt_len, then from its cursor."""
+    import torch
+
+    case = next(c for c in golden_walks() if c["name"] == name)
+    sequences = case["sequences"]
+    n = len(sequences)
+    a, _, _ = engine_for(case)
+    b, _, _ = engine_for(case)
+    start(a, sequences)
+    start(b, sequences)
+    prompt = 5
+    width = prompt + len(sequences[0]["tokens"])
+    history = torch.zeros((n, width), dtype=torch.int32, device="cuda")
+    for k, seq in enumerate(sequences):
+        history[k, prompt:] = torch.tensor(seq["tokens"], dtype=torch.int32)
+        history[k, :prompt] = 7  # the prompt is never advanced over
+    prompt_len = torch.full((n,), prompt, dtype=torch.int32, device="cuda")
+    slots = torch.arange(n, dtype=torch.int32, device="cuda")
+    done = 0
+    for chunk in (1, 3, 17, 1000):
+        total = torch.clamp(prompt_len + done + chunk, max=width)
+        b.sync(slots, history, prompt_len, total)
+        for step in range(done, min(done + chunk, width - prompt)):
+            a.advance(np.array([seq["tokens"][step] for seq in sequences], dtype=np.int32))
+        done = min(done + chunk, width - prompt)
+        a.fill_mask()
+        b.fill_mask()
+        np.testing.assert_array_equal(a.mask_host(), b.mask_host())
+        sa, sb = a.states_host(), b.states_host()
+        for field in sa:
+            np.testing.assert_array_equal(sa[field], sb[field], field)
+
+
+@pytest.mark.parametrize("dtype", ["float32", "bfloat16", "float16"])
+@pytest.mark.parametrize("pad", [0, 3, 40])
+def test_apply_mask_writes_exactly_the_disallowed_columns(dtype, pad):
+    import torch
+
+    case = next(c for c in golden_walks() if c["name"] == "bpe_ordinary")
+    sequences = case["sequences"]
+    engine, _, served = engine_for(case, slots=len(sequences) + 2)
+    start(engine, sequences)
+    vocab = served.vocab_size
+    rng = np.random.default_rng(5)
+    for step in range(40):
+        engine.advance(np.array([seq["tokens"][step] for seq in sequences], dtype=np.int32))
+    engine.fill_mask()
+    masks = engine.mask_host().view(np.uint32)
+    # rows: every sequence, one inactive slot, and a repeated row
+    row_slots = list(range(len(sequences))) + [len(sequences) + 1, 0]
+    cols = vocab + pad
+    stride = cols + 5  # rows start off 16-byte boundaries
+    torch_dtype = getattr(torch, dtype)
+    base = torch.tensor(rng.normal(size=(len(row_slots), stride)), dtype=torch_dtype, device="cuda")
+    full = base.clone()
+    logits = full[:, :cols]
+    engine.apply_mask(logits, torch.tensor(row_slots, dtype=torch.int32, device="cuda"))
+    got = logits.float().cpu().numpy()
+    before = base[:, :cols].float().cpu().numpy()
+    for r, slot in enumerate(row_slots):
+        if slot >= len(sequences):
+            np.testing.assert_array_equal(got[r], before[r])
+            continue
+        allowed = np.zeros(cols, dtype=bool)
+        allowed[sorted(unpack(masks[slot], vocab))] = True
+        assert np.all(np.isneginf(got[r][~allowed])), (r, slot)
+        np.testing.assert_array_equal(got[r][allowed], before[r][allowed])
+    # the elements between rows (stride padding) are untouched
+    np.testing.assert_array_equal(full[:, cols:].float().cpu().numpy(), base[:, cols:].float().cpu().numpy())
+
+
+def test_error_rows_are_left_untouched_and_counted():
+    import torch
+
+    case = next(c for c in golden_walks() if c["name"] == "toy_ordinary")
+    engine, _, served = engine_for(case, slots=2)
+    engine.reset()
+    slots = torch.arange(2, dtype=torch.int32, device="cuda")
+    engine.begin(slots)
+    opener = served.encode(" ⟦")
+    for t in opener:
+        engine.advance(np.array([t, t], dtype=np.int32))
+    special = sorted(served.special_ids)[0]
+    engine.advance(np.array([special], dtype=np.int32))  # a special token inside a span
+    assert engine.errors(2) == 1
+    logits = torch.zeros((2, served.vocab_size), device="cuda")
+    engine.apply_mask(logits, slots)
+    assert torch.all(logits[0] == 0)  # error row untouched
+    assert torch.isneginf(logits[1]).any()
+
+
+def test_out_of_range_arguments_raise_value_error():
+    import torch
+
+    case = next(c for c in golden_walks() if c["name"] == "toy_committed")
+    engine, _, _ = engine_for(case, slots=2)
+    with pytest.raises(ValueError):
+        engine.set_version(5, None)
+    with pytest.raises(ValueError):
+        engine.open_span(-1)
+    with pytest.raises(ValueError):
+        engine.anchor(0, ["no-such-entity"])
+    with pytest.raises(ValueError):
+        engine.set_version(0, "no-such-version")
+    with pytest.raises(ValueError):
+        engine.advance(np.zeros(3, dtype=np.int32))
+    with pytest.raises(ValueError):
+        engine.begin(torch.arange(3, dtype=torch.int32, device="cuda"))

@@ -1,0 +1,1094 @@
+// Per-row constraint logic of the KG span engine: advance one token, build one mask.
+//
+// The semantics are those of the reference Oracle (src/xgraph/oracle.py:736-1922, the
+// span language with ordinary, derivation and path modes, escapes, repeats, KG versions,
+// anchors, unquoted starts, sitelink ranks and end-after-answer).  The data layout is
+// this engine's own (tables.py packs it; layout.h declares it).
+//
+// One WARP owns one request row.  The scalar state machine runs redundantly in all 32
+// lanes (uniform control flow, broadcast loads, lane 0 stores); loops over rows, edges
+// and candidates are spread over the lanes with ballots.  The same source also compiles
+// as plain C++ (XG_GPU == 0) where every "warp" loop runs sequentially: that build is a
+// test seam only (tests check it against the oracle on the CPU), never a fallback.
+#pragma once
+
+#include <stdint.h>
+
+#include "layout.h"
+
+#if defined(__CUDACC__)
+#define XG_HD __device__ __forceinline__
+#define XG_GPU 1
+#else
+#include <algorithm>
+#define XG_HD inline
+#define XG_GPU 0
+#endif
+
+namespace xg {
+
+constexpr int32_t kMaxSet = 64;       // MAX_FACTS == MAX_REACHED (src/xgraph/oracle.py:172-175)
+constexpr int32_t kMaxHops = 8;       // MAX_PATH_RELATIONS (src/xgraph/oracle.py:177)
+constexpr int32_t kTopCap = 256;      // per-warp candidate buffer of the top-64 selections
+constexpr int32_t kScratchInts = 2 * kMaxSet + 2 + 2 * kMaxSet + kMaxSet;
+constexpr int8_t kReject = -1;
+constexpr int8_t kComplete = -2;
+
+enum Phase : int32_t { kFree = 0, kSpan = 1, kEscaped = 2, kError = 3 };
+enum Segment : int32_t { kSubject = 0, kRelation = 1, kObject = 2 };
+enum Closed : int32_t { kNone = 0, kUnresolved = 1, kEntitySpan = 2, kFactSpan = 3, kPathSpan = 4 };
+enum Flag : int32_t { kMayClose = 1, kMaySep = 2, kMayEsc = 4 };
+
+// Slot memory (int32 words per slot): counts, then the fixed lists, then the bitmap of
+// the relations the current subjects / frontier have.
+enum MemoryField : int32_t {
+  kMemFacts = 0,      // fact spans recorded (<= 64), for repeats=False
+  kMemReached = 1,    // reached rows (<= 64); 0 = no binding yet
+  kMemFrontier = 2,   // path frontier entities (<= 64)
+  kMemVersion = 3,    // KG version the slot reads (0 = base)
+  kMemFactRows = 8,                           // 64 x (subject key, relation key, object key)
+  kMemReachedRows = kMemFactRows + 3 * kMaxSet,  // 64 sorted label rows
+  kMemFrontierEnt = kMemReachedRows + kMaxSet,   // 64 entities
+  kMemFrontierRank = kMemFrontierEnt + kMaxSet,  // their start ranks
+  kMemHave = kMemFrontierRank + kMaxSet,         // relation bitmap
+};
+
+struct Key {
+  uint64_t a;
+  uint32_t b;
+  uint32_t pad;
+};
+XG_HD bool key_less(const Key& x, const Key& y) { return x.a < y.a || (x.a == y.a && x.b < y.b); }
+XG_HD bool key_eq(const Key& x, const Key& y) { return x.a == y.a && x.b == y.b; }
+XG_HD Key max_key() { return Key{~0ull, ~0u, 0u}; }
+XG_HD bool is_max(const Key& k) { return k.a == ~0ull && k.b == ~0u; }
+
+struct Rows {
+  const int32_t* tok;
+  const int32_t* off;
+  const int32_t* owner;
+  int32_t count;
+};
+
+struct Delim {
+  const int32_t* off;
+  const int32_t* tok;
+  const int32_t* next;
+  int32_t len;
+};
+
+// Device (or host-seam) view of the packed tables plus the per-slot buffers.
+struct Tables {
+  Rows ent, rel;
+  const int32_t* ent_first_row;
+  const int32_t* ent_rows_off;
+  const int32_t* ent_rows;
+  const int32_t* adj_off;
+  const int32_t* edge_rel;
+  const int32_t* edge_obj;
+  const int32_t* sitelinks;    // null unless the sitelink rank is on
+  const int32_t* kept_prefix;  // null unless some rows are not unbound candidates
+  const uint32_t* root_mask;
+  const int64_t* wide_keys;
+  const uint32_t* wide_masks;
+  int32_t wide_count;
+  const int8_t* free_next;
+  const uint32_t* free_mask;
+  const int8_t* esc_next;
+  const uint32_t* esc_mask;
+  const uint32_t* eos_mask;
+  Delim closer, separator, escape;
+  const int32_t* ver_off;
+  const int32_t* ver_subj;
+  const int32_t* ver_adj;
+  const int32_t* ver_edge_rel;
+  const int32_t* ver_edge_obj;
+  int32_t versions;
+  int32_t vocab, words, words_padded, entities, relations, relation_words;
+  int32_t escapes, repeats, derivation, paths, bound_escapes, committed, end_after_answer;
+  // per-slot engine buffers
+  XgState* states;
+  int32_t* memory;
+  int32_t memory_ints;
+  uint32_t* masks;           // [slots, words_padded]
+  const uint32_t** src;      // where each slot's current mask lives (null: error)
+  int32_t* cursors;
+  int32_t* active;
+};
+
+// ---------------------------------------------------------------------------------------
+// Warp primitives.  On the host seam each becomes the obvious sequential loop.
+
+struct Warp {
+  int32_t lane;
+  XG_HD bool leader() const { return lane == 0; }
+};
+
+XG_HD void warp_sync() {
+#if XG_GPU
+  __syncwarp();
+#endif
+}
+
+// Whether f(i) holds for some i in [begin, end); begin/end must be warp-uniform.
+template <class F>
+XG_HD bool warp_any(const Warp& w, int32_t begin, int32_t end, F f) {
+#if XG_GPU
+  for (int32_t base = begin; base < end; base += 32) {
+    const int32_t i = base + w.lane;
+    const bool hit = i < end && f(i);
+    if (__any_sync(0xffffffffu, hit)) return true;
+  }
+  return false;
+#else
+  (void)w;
+  for (int32_t i = begin; i < end; ++i)
+    if (f(i)) return true;
+  return false;
+#endif
+}
+
+// f(i) for every i in [begin, end), spread over the lanes (f must not need other lanes).
+template <class F>
+XG_HD void warp_for(const Warp& w, int32_t begin, int32_t end, F f) {
+#if XG_GPU
+  for (int32_t i = begin + w.lane; i < end; i += 32) f(i);
+  __syncwarp();
+#else
+  (void)w;
+  for (int32_t i = begin; i < end; ++i) f(i);
+#endif
+}
+
+// The least key(i) over i in [begin, end) (max_key() when empty).
+template <class F>
+XG_HD Key warp_min(const Warp& w, int32_t begin, int32_t end, F key) {
+  Key best = max_key();
+#if XG_GPU
+  for (int32_t i = begin + w.lane; i < end; i += 32) {
+    const Key k = key(i);
+    if (key_less(k, best)) best = k;
+  }
+  for (int32_t d = 16; d > 0; d >>= 1) {
+    Key o;
+    o.a = __shfl_xor_sync(0xffffffffu, best.a, d);
+    o.b = __shfl_xor_sync(0xffffffffu, best.b, d);
+    o.pad = 0;
+    if (key_less(o, best)) best = o;
+  }
+#else
+  (void)w;
+  for (int32_t i = begin; i < end; ++i) {
+    const Key k = key(i);
+    if (key_less(k, best)) best = k;
+  }
+#endif
+  return best;
+}
+
+XG_HD void set_bit(uint32_t* words, int32_t token) {
+#if XG_GPU
+  atomicOr(&words[token >> 5], 1u << (token & 31));
+#else
+  words[token >> 5] |= 1u << (token & 31);
+#endif
+}
+
+// ---------------------------------------------------------------------------------------
+// Top-64 selection over a stream of keys, in a per-warp buffer of kTopCap keys.
+// DISTINCT keeps the 64 least distinct keys.  ENTITY keys hold (rank << 32 | first row of
+// the entity) and keep, per entity, its least rank, then the 64 least (rank, first row).
+
+enum TopMode : int32_t { kDistinct = 0, kEntity = 1 };
+
+struct TopSet {
+  Key* buf;
+  int32_t n;
+};
+
+XG_HD void top_sort(const Warp& w, Key* buf, int32_t n) {
+#if XG_GPU
+  for (int32_t i = n + w.lane; i < kTopCap; i += 32) buf[i] = max_key();
+  __syncwarp();
+  for (int32_t k = 2; k <= kTopCap; k <<= 1) {
+    for (int32_t j = k >> 1; j > 0; j >>= 1) {
+      for (int32_t i = w.lane; i < kTopCap; i += 32) {
+        const int32_t l = i ^ j;
+        if (l > i) {
+          const Key x = buf[i], y = buf[l];
+          const bool up = (i & k) == 0;
+          if (up ? key_less(y, x) : key_less(x, y)) {
+            buf[i] = y;
+            buf[l] = x;
+          }
+        }
+      }
+      __syncwarp();
+    }
+  }
+#else
+  (void)w;
+  std::sort(buf, buf + n, key_less);
+  for (int32_t i = n; i < kTopCap; ++i) buf[i] = max_key();
+#endif
+}
+
+// Sorted buffer -> its first `limit` entries that are distinct (by full key, or by the
+// high 32 bits of a when by_high); returns how many were kept.
+XG_HD int32_t top_unique(const Warp& w, Key* buf, int32_t limit, bool by_high) {
+#if XG_GPU
+  int32_t out = 0;
+  Key carry = max_key();
+  for (int32_t base = 0; base < kTopCap && out < limit; base += 32) {
+    const Key k = buf[base + w.lane];
+    Key prev;
+    prev.a = __shfl_up_sync(0xffffffffu, k.a, 1);
+    prev.b = __shfl_up_sync(0xffffffffu, k.b, 1);
+    prev.pad = 0;
+    const Key last = Key{__shfl_sync(0xffffffffu, k.a, 31), __shfl_sync(0xffffffffu, k.b, 31), 0u};
+    if (w.lane == 0) prev = carry;
+    const bool first = (base == 0 && w.lane == 0);
+    const bool same = by_high ? (!first && (prev.a >> 32) == (k.a >> 32)) : (!first && key_eq(prev, k));
+    const bool keep = !is_max(k) && !same;
+    const uint32_t m = __ballot_sync(0xffffffffu, keep);
+    __syncwarp();
+    const int32_t pos = out + __popc(m & ((1u << w.lane) - 1u));
+    if (keep && pos < limit) buf[pos] = k;
+    out += __popc(m);
+    carry = last;
+    __syncwarp();
+  }
+  return out < limit ? out : limit;
+#else
+  (void)w;
+  int32_t out = 0;
+  for (int32_t i = 0; i < kTopCap && out < limit; ++i) {
+    const Key k = buf[i];
+    if (is_max(k)) break;
+    if (out > 0) {
+      const Key& prev = buf[out - 1];
+      if (by_high ? (prev.a >> 32) == (k.a >> 32) : key_eq(prev, k)) continue;
+    }
+    buf[out++] = k;
+  }
+  return out;
+#endif
+}
+
+XG_HD void top_compact(const Warp& w, TopSet& ts, int32_t mode) {
+  if (mode == kEntity) {
+    // (rank, row) -> (row, rank): the least rank of each entity comes first.
+    warp_for(w, 0, ts.n, [&](int32_t i) {
+      const uint64_t a = ts.buf[i].a;
+      ts.buf[i].a = (a << 32) | (a >> 32);
+    });
+    top_sort(w, ts.buf, ts.n);
+    int32_t n = top_unique(w, ts.buf, kTopCap, true);
+    warp_for(w, 0, n, [&](int32_t i) {
+      const uint64_t a = ts.buf[i].a;
+      ts.buf[i].a = (a << 32) | (a >> 32);
+    });
+    top_sort(w, ts.buf, n);
+    ts.n = n < kMaxSet ? n : kMaxSet;
+  } else {
+    top_sort(w, ts.buf, ts.n);
+    ts.n = top_unique(w, ts.buf, kMaxSet, false);
+  }
+  warp_sync();
+}
+
+// Offer one key per lane (valid lanes only); all lanes call it together.
+XG_HD void top_push(const Warp& w, TopSet& ts, bool valid, const Key& k, int32_t mode) {
+#if XG_GPU
+  const uint32_t m = __ballot_sync(0xffffffffu, valid);
+  if (m == 0) return;
+  if (ts.n + 32 > kTopCap) top_compact(w, ts, mode);
+  const int32_t pos = ts.n + __popc(m & ((1u << w.lane) - 1u));
+  if (valid) ts.buf[pos] = k;
+  ts.n += __popc(m);
+  __syncwarp();
+#else
+  if (!valid) return;
+  if (ts.n + 1 > kTopCap) top_compact(w, ts, mode);
+  ts.buf[ts.n++] = k;
+#endif
+}
+
+// ---------------------------------------------------------------------------------------
+// Index reads.
+
+XG_HD int32_t row_len(const Rows& r, int32_t row) { return r.off[row + 1] - r.off[row]; }
+
+// Token of a row at a depth, or -1 past its end (so a row that ends sorts first).
+XG_HD int32_t column(const Rows& r, int32_t row, int32_t depth) {
+  const int32_t a = r.off[row];
+  return depth < r.off[row + 1] - a ? r.tok[a + depth] : -1;
+}
+
+// First row in [lo, hi) whose column at depth is >= token (upper: > token).
+XG_HD int32_t bound_row(const Rows& r, int32_t lo, int32_t hi, int32_t depth, int32_t token, bool upper) {
+  while (lo < hi) {
+    const int32_t mid = lo + ((hi - lo) >> 1);
+    const int32_t c = column(r, mid, depth);
+    if (upper ? c <= token : c < token)
+      lo = mid + 1;
+    else
+      hi = mid;
+  }
+  return lo;
+}
+
+template <class T>
+XG_HD int32_t lower_index(const T* a, int32_t lo, int32_t hi, T value) {
+  while (lo < hi) {
+    const int32_t mid = lo + ((hi - lo) >> 1);
+    if (a[mid] < value)
+      lo = mid + 1;
+    else
+      hi = mid;
+  }
+  return lo;
+}
+
+template <class T>
+XG_HD int32_t upper_index(const T* a, int32_t lo, int32_t hi, T value) {
+  while (lo < hi) {
+    const int32_t mid = lo + ((hi - lo) >> 1);
+    if (a[mid] <= value)
+      lo = mid + 1;
+    else
+      hi = mid;
+  }
+  return lo;
+}
+
+struct Edges {
+  const int32_t* rel;
+  const int32_t* obj;
+  int32_t n;
+};
+
+// An entity's adjacency in a KG version: the version's own list for an edited subject,
+// else the base CSR slice (src/xgraph/kgversions.py:14-21, the layout both share).
+XG_HD Edges edges_of(const Tables& t, int32_t version, int32_t e) {
+  if (version > 0) {
+    const int32_t a = t.ver_off[version - 1], b = t.ver_off[version];
+    const int32_t at = lower_index(t.ver_subj, a, b, e);
+    if (at < b && t.ver_subj[at] == e) {
+      const int32_t s = t.ver_adj[at], f = t.ver_adj[at + 1];
+      return Edges{t.ver_edge_rel + s, t.ver_edge_obj + s, f - s};
+    }
+  }
+  const int32_t s = t.adj_off[e], f = t.adj_off[e + 1];
+  return Edges{t.edge_rel + s, t.edge_obj + s, f - s};
+}
+
+// The objects of one relation within an adjacency list: [first, last) indexes.
+XG_HD void relation_slice(const Edges& g, int32_t relation, int32_t& first, int32_t& last) {
+  first = lower_index(g.rel, 0, g.n, relation);
+  last = upper_index(g.rel, first, g.n, relation);
+}
+
+XG_HD int32_t degree(const Tables& t, int32_t version, int32_t e) { return edges_of(t, version, e).n; }
+
+// Best-connected order key (src/xgraph/oracle.py:1736-1747): most sitelinks (with the
+// sitelink rank), then most adjacency entries in the slot's version, then first row.
+XG_HD Key connected_key(const Tables& t, int32_t version, int32_t row) {
+  const int32_t e = t.ent.owner[row];
+  const uint32_t links = t.sitelinks ? static_cast<uint32_t>(t.sitelinks[e]) : 0u;
+  const uint32_t deg = static_cast<uint32_t>(degree(t, version, e));
+  return Key{(static_cast<uint64_t>(~links) << 32) | static_cast<uint64_t>(~deg), static_cast<uint32_t>(row), 0u};
+}
+
+// ---------------------------------------------------------------------------------------
+// One slot's context.
+
+struct Ctx {
+  const Tables& t;
+  Warp w;
+  int32_t slot;
+  int32_t* mem;     // slot memory
+  Key* top;         // per-warp buffer of kTopCap keys
+  int32_t* scratch; // per-warp: kScratchInts ints (slice starts, slice pointers, entity rows)
+};
+
+XG_HD int32_t version_of(const Ctx& c) { return c.mem[kMemVersion]; }
+XG_HD int32_t reached_count(const Ctx& c) { return c.mem[kMemReached]; }
+
+XG_HD void mem_store(const Ctx& c, int32_t at, int32_t value) {
+  if (c.w.leader()) c.mem[at] = value;
+}
+
+XG_HD bool has_relation(const Ctx& c, int32_t relation) {
+  return (static_cast<uint32_t>(c.mem[kMemHave + (relation >> 5)]) >> (relation & 31)) & 1u;
+}
+
+XG_HD bool unbound(const Tables& t, const Ctx& c, const XgState& s) {
+  return s.segment == kSubject && (!t.derivation || reached_count(c) == 0);
+}
+
+XG_HD bool kept_row(const Tables& t, int32_t row) {
+  return !t.kept_prefix || t.kept_prefix[row + 1] > t.kept_prefix[row];
+}
+
+// The last closed span was a path: the next span is its answer.
+XG_HD bool answers_path(const Tables& t, const XgState& s) { return t.paths && s.last_kind == kPathSpan; }
+
+// Whether some candidate row of the state's segment lies in [lo, hi)
+// (src/xgraph/oracle.py:830-894: _candidates / _segment_candidates).
+XG_HD bool has_candidate(const Ctx& c, const XgState& s, int32_t lo, int32_t hi) {
+  const Tables& t = c.t;
+  if (lo >= hi) return false;
+  if (s.segment == kSubject) {
+    if (unbound(t, c, s)) return !t.kept_prefix || t.kept_prefix[hi] > t.kept_prefix[lo];
+    const int32_t* reached = c.mem + kMemReachedRows;
+    return warp_any(c.w, 0, reached_count(c), [&](int32_t i) { return reached[i] >= lo && reached[i] < hi; });
+  }
+  if (s.segment == kRelation) {
+    return warp_any(c.w, lo, hi, [&](int32_t row) { return has_relation(c, t.rel.owner[row]); });
+  }
+  // object: some object row of a (subject, relation) pair in [lo, hi)
+  const int32_t subjects = s.subj_hi - s.subj_lo, relations = s.rel_hi - s.rel_lo;
+  const int32_t version = version_of(c);
+  return warp_any(c.w, 0, subjects * relations, [&](int32_t p) {
+    const int32_t e = t.ent.owner[s.subj_lo + p / relations];
+    const int32_t r = t.rel.owner[s.rel_lo + p % relations];
+    const Edges g = edges_of(t, version, e);
+    int32_t a, b;
+    relation_slice(g, r, a, b);
+    const int32_t x = lower_index(g.obj, a, b, lo);
+    return x < b && g.obj[x] < hi;
+  });
+}
+
+// Calls item(valid, owner_index, value) for every element of `count` int32 slices,
+// spread over the lanes; slice(k, ptr, len) describes slice k (k < 64).
+template <class S, class I>
+XG_HD void for_each_slice_item(const Ctx& c, int32_t count, S slice, I item) {
+#if XG_GPU
+  int32_t* starts = c.scratch;                       // [65]
+  const int32_t** ptrs = reinterpret_cast<const int32_t**>(c.scratch + 2 * kMaxSet + 2);  // [64]
+  for (int32_t base = 0; base < count; base += 64) {
+    const int32_t k0 = base + c.w.lane, k1 = base + 32 + c.w.lane;
+    const int32_t* p0 = nullptr;
+    const int32_t* p1 = nullptr;
+    int32_t n0 = 0, n1 = 0;
+    if (k0 < count) slice(k0, p0, n0);
+    if (k1 < count) slice(k1, p1, n1);
+    // inclusive scan of n0 over lanes, then of n1 continuing after the first half
+    int32_t x0 = n0, x1 = n1;
+    for (int32_t d = 1; d < 32; d <<= 1) {
+      const int32_t y0 = __shfl_up_sync(0xffffffffu, x0, d);
+      const int32_t y1 = __shfl_up_sync(0xffffffffu, x1, d);
+      if (c.w.lane >= d) {
+        x0 += y0;
+        x1 += y1;
+      }
+    }
+    const int32_t half = __shfl_sync(0xffffffffu, x0, 31);
+    const int32_t total = half + __shfl_sync(0xffffffffu, x1, 31);
+    starts[c.w.lane] = x0 - n0;
+    starts[32 + c.w.lane] = half + x1 - n1;
+    ptrs[c.w.lane] = p0;
+    ptrs[32 + c.w.lane] = p1;
+    if (c.w.lane == 0) starts[64] = total;
+    __syncwarp();
+    for (int32_t g0 = 0; g0 < total; g0 += 32) {
+      const int32_t g = g0 + c.w.lane;
+      const bool valid = g < total;
+      int32_t k = 0, value = 0;
+      if (valid) {
+        k = upper_index(starts, 0, 64, g) - 1;
+        value = ptrs[k][g - starts[k]];
+      }
+      item(valid, base + k, value);
+    }
+    __syncwarp();
+  }
+#else
+  for (int32_t k = 0; k < count; ++k) {
+    const int32_t* p = nullptr;
+    int32_t n = 0;
+    slice(k, p, n);
+    for (int32_t i = 0; i < n; ++i) item(true, k, p[i]);
+  }
+#endif
+}
+
+// Writes the bitmap of relations that these entities have (reads entity(k) for k < n).
+template <class E>
+XG_HD void set_have(const Ctx& c, int32_t n, E entity) {
+  const Tables& t = c.t;
+  int32_t* have = c.mem + kMemHave;
+  warp_for(c.w, 0, t.relation_words, [&](int32_t i) { have[i] = 0; });
+  const int32_t version = version_of(c);
+  warp_for(c.w, 0, n, [&](int32_t k) {
+    const int32_t e = entity(k);
+    if (e < 0) return;
+    const Edges g = edges_of(t, version, e);
+    int32_t i = 0;
+    while (i < g.n) {  // one bit per run of equal relations
+      const int32_t r = g.rel[i];
+      set_bit(reinterpret_cast<uint32_t*>(have), r);
+      i = upper_index(g.rel, i, g.n, r);
+    }
+  });
+}
+
+// Next path frontier (src/xgraph/oracle.py:1771-1786): objects of the current frontier
+// under every relation of the exact relation-label rows [rlo, rhi), each with the least
+// start rank it is reached from, kept to 64 by (rank, first row) or, with union paths,
+// by first row.  Leaves the result sorted in c.top[0, n) as ENTITY keys; returns n.
+XG_HD int32_t next_frontier(const Ctx& c, int32_t rlo, int32_t rhi) {
+  const Tables& t = c.t;
+  const int32_t version = version_of(c);
+  const int32_t* ents = c.mem + kMemFrontierEnt;
+  const int32_t* ranks = c.mem + kMemFrontierRank;
+  const int32_t count = c.mem[kMemFrontier];
+  TopSet ts{c.top, 0};
+  for (int32_t rr = rlo; rr < rhi; ++rr) {
+    const int32_t relation = t.rel.owner[rr];
+    for_each_slice_item(
+        c, count,
+        [&](int32_t k, const int32_t*& p, int32_t& n) {
+          const Edges g = edges_of(t, version, ents[k]);
+          int32_t a, b;
+          relation_slice(g, relation, a, b);
+          p = g.obj + a;
+          n = b - a;
+        },
+        [&](bool valid, int32_t k, int32_t object) {
+          Key key{0, 0, 0};
+          if (valid) {
+            const uint32_t first = static_cast<uint32_t>(t.ent_first_row[t.ent.owner[object]]);
+            const uint64_t rank = t.committed ? static_cast<uint32_t>(ranks[k]) : 0u;
+            key.a = (rank << 32) | first;
+          }
+          top_push(c.w, ts, valid, key, kEntity);
+        });
+  }
+  top_compact(c.w, ts, kEntity);
+  return ts.n;
+}
+
+// The rows of the entities whose first rows are given by keys c.top[0, n) (low 32 bits of
+// a), sorted, first 64 (src/xgraph/oracle.py:697-703 _rows_for, capped as reached).
+// Writes them to the slot's reached list.
+XG_HD void reach_rows_of_top(const Ctx& c, int32_t n) {
+  const Tables& t = c.t;
+  int32_t* firsts = c.scratch + 2 * kMaxSet + 2 + 2 * kMaxSet;  // after starts/ptrs
+  warp_for(c.w, 0, n, [&](int32_t i) { firsts[i] = static_cast<int32_t>(c.top[i].a & 0xffffffffu); });
+  TopSet ts{c.top, 0};
+  for_each_slice_item(
+      c, n,
+      [&](int32_t k, const int32_t*& p, int32_t& len) {
+        const int32_t e = t.ent.owner[firsts[k]];
+        p = t.ent_rows + t.ent_rows_off[e];
+        len = t.ent_rows_off[e + 1] - t.ent_rows_off[e];
+      },
+      [&](bool valid, int32_t, int32_t row) {
+        top_push(c.w, ts, valid, Key{static_cast<uint64_t>(static_cast<uint32_t>(row)), 0u, 0u}, kDistinct);
+      });
+  top_compact(c.w, ts, kDistinct);
+  int32_t* reached = c.mem + kMemReachedRows;
+  warp_for(c.w, 0, ts.n, [&](int32_t i) { reached[i] = static_cast<int32_t>(ts.buf[i].a); });
+  mem_store(c, kMemReached, ts.n);
+  warp_sync();
+}
+
+// Write the frontier held as ENTITY keys in c.top[0, n) into slot memory.
+XG_HD void store_frontier(const Ctx& c, int32_t n) {
+  const Tables& t = c.t;
+  int32_t* ents = c.mem + kMemFrontierEnt;
+  int32_t* ranks = c.mem + kMemFrontierRank;
+  warp_for(c.w, 0, n, [&](int32_t i) {
+    const uint64_t a = c.top[i].a;
+    ents[i] = t.ent.owner[static_cast<int32_t>(a & 0xffffffffu)];
+    ranks[i] = static_cast<int32_t>(a >> 32);
+  });
+  mem_store(c, kMemFrontier, n);
+  warp_sync();
+}
+
+// Candidate rows of the exact label rows [lo, hi) in the subject segment.
+XG_HD bool subject_candidate(const Ctx& c, bool bound, int32_t row) {
+  if (!bound) return kept_row(c.t, row);
+  const int32_t* reached = c.mem + kMemReachedRows;
+  const int32_t n = reached_count(c);
+  const int32_t at = lower_index(reached, 0, n, row);
+  return at < n && reached[at] == row;
+}
+
+// Whether the flags' "separator after a relation" holds in path mode: some entity of the
+// capped next frontier has triples.
+XG_HD bool frontier_goes_on(const Ctx& c, int32_t rlo, int32_t rhi) {
+  const int32_t n = next_frontier(c, rlo, rhi);
+  const int32_t version = version_of(c);
+  const Tables& t = c.t;
+  return warp_any(c.w, 0, n, [&](int32_t i) {
+    return degree(t, version, t.ent.owner[static_cast<int32_t>(c.top[i].a & 0xffffffffu)]) > 0;
+  });
+}
+
+// Which delimiter branches may start after the state's typed label
+// (src/xgraph/oracle.py:1039-1113: closes, separates, and the escape condition).
+XG_HD void set_flags(const Ctx& c, XgState& s) {
+  const Tables& t = c.t;
+  s.flags = 0;
+  if (s.lo < 0) {
+    s.ex_hi = -1;
+    return;
+  }
+  const Rows& rows = s.segment == kRelation ? t.rel : t.ent;
+  s.ex_hi = s.depth == 0 ? s.lo : bound_row(rows, s.lo, s.hi, s.depth, 0, false);
+  const bool bound = s.segment == kSubject && !unbound(t, c, s);
+  if (has_candidate(c, s, s.lo, s.ex_hi)) {
+    bool closes = s.segment != kRelation || t.paths;
+    if (closes && s.segment == kObject && !t.repeats) {
+      const int32_t* facts = c.mem + kMemFactRows;
+      const int32_t subj = s.subj_key, rel = s.rel_lo, obj = s.lo;
+      closes = !warp_any(c.w, 0, c.mem[kMemFacts], [&](int32_t i) {
+        return facts[3 * i] == subj && facts[3 * i + 1] == rel && facts[3 * i + 2] == obj;
+      });
+    }
+    if (closes) s.flags |= kMayClose;
+    bool separates = false;
+    if (s.segment == kSubject) {
+      const int32_t version = version_of(c);
+      separates = !answers_path(t, s) && warp_any(c.w, s.lo, s.ex_hi, [&](int32_t row) {
+                    return subject_candidate(c, bound, row) && degree(t, version, t.ent.owner[row]) > 0;
+                  });
+    } else if (s.segment == kRelation) {
+      separates = !t.paths || (s.hops < kMaxHops && frontier_goes_on(c, s.lo, s.ex_hi));
+    }
+    if (separates) s.flags |= kMaySep;
+  }
+  // escape (src/xgraph/oracle.py:1874-1883): a bound subject escapes only with bound_escapes
+  if (t.escapes && (t.bound_escapes || !bound)) s.flags |= kMayEsc;
+}
+
+XG_HD void clear_span(XgState& s) {
+  s.segment = kSubject;
+  s.depth = 0;
+  s.lo = s.hi = 0;
+  s.close_pos = s.close_lo = s.close_hi = 0;
+  s.sep_pos = s.sep_lo = s.sep_hi = 0;
+  s.esc_pos = 0;
+  s.subj_lo = s.subj_hi = s.rel_lo = s.rel_hi = s.subj_key = s.hops = 0;
+  s.ex_hi = 0;
+  s.flags = 0;
+}
+
+// The state right after the span opener (src/xgraph/oracle.py:706-724).
+XG_HD void open_span(const Ctx& c, XgState& s) {
+  clear_span(s);
+  s.phase = kSpan;
+  s.pos = 0;
+  s.hi = c.t.ent.count;
+  set_flags(c, s);
+}
+
+XG_HD void end_span(XgState& s, int32_t phase) {
+  clear_span(s);
+  s.phase = phase;
+  s.pos = 0;
+}
+
+// The separator completed after the label rows [llo, lhi) (src/xgraph/oracle.py:1805-1922).
+XG_HD void next_segment(const Ctx& c, XgState& s, int32_t llo, int32_t lhi) {
+  const Tables& t = c.t;
+  const int32_t version = version_of(c);
+  if (s.segment == kSubject) {
+    const bool bound = !unbound(t, c, s);
+    if (t.paths) {
+      // starts: every candidate with triples in best-connected order, kept to 64
+      TopSet ts{c.top, 0};
+      for (int32_t base = llo; base < lhi; base += 32) {
+#if XG_GPU
+        const int32_t row = base + c.w.lane;
+        const bool valid = row < lhi && subject_candidate(c, bound, row) && degree(t, version, t.ent.owner[row]) > 0;
+        Key k{0, 0, 0};
+        if (valid) {
+          if (t.committed)
+            k = connected_key(t, version, row);
+          else
+            k = Key{static_cast<uint64_t>(static_cast<uint32_t>(t.ent_first_row[t.ent.owner[row]])), 0u, 0u};
+        }
+        top_push(c.w, ts, valid, k, kDistinct);
+#else
+        for (int32_t row = base; row < lhi && row < base + 32; ++row) {
+          const bool valid = subject_candidate(c, bound, row) && degree(t, version, t.ent.owner[row]) > 0;
+          if (!valid) continue;
+          const Key k = t.committed ? connected_key(t, version, row)
+                                    : Key{static_cast<uint64_t>(static_cast<uint32_t>(t.ent_first_row[t.ent.owner[row]])), 0u, 0u};
+          top_push(c.w, ts, true, k, kDistinct);
+        }
+#endif
+      }
+      top_compact(c.w, ts, kDistinct);
+      int32_t* ents = c.mem + kMemFrontierEnt;
+      int32_t* ranks = c.mem + kMemFrontierRank;
+      const int32_t n = ts.n;
+      warp_for(c.w, 0, n, [&](int32_t i) {
+        if (t.committed) {
+          ents[i] = t.ent.owner[static_cast<int32_t>(c.top[i].b)];
+          ranks[i] = i;
+        } else {
+          ents[i] = t.ent.owner[static_cast<int32_t>(c.top[i].a & 0xffffffffu)];
+          ranks[i] = 0;
+        }
+      });
+      mem_store(c, kMemFrontier, n);
+      warp_sync();
+      set_have(c, n, [&](int32_t k) { return ents[k]; });
+      s.subj_lo = llo;
+      s.subj_hi = lhi;
+    } else if (t.derivation) {
+      // one subject: the best-connected candidate with triples
+      const Key best = warp_min(c.w, llo, lhi, [&](int32_t row) {
+        if (!subject_candidate(c, bound, row) || degree(t, version, t.ent.owner[row]) == 0) return max_key();
+        return connected_key(t, version, row);
+      });
+      const int32_t row = static_cast<int32_t>(best.b);
+      s.subj_lo = row;
+      s.subj_hi = row + 1;
+      set_have(c, 1, [&](int32_t) { return t.ent.owner[row]; });
+    } else {
+      s.subj_lo = llo;
+      s.subj_hi = lhi;
+      set_have(c, lhi - llo, [&](int32_t k) { return t.ent.owner[llo + k]; });
+    }
+    s.subj_key = llo;
+    s.segment = kRelation;
+    s.hops = 1;
+  } else if (t.paths) {
+    const int32_t n = next_frontier(c, llo, lhi);
+    store_frontier(c, n);
+    const int32_t* ents = c.mem + kMemFrontierEnt;
+    set_have(c, n, [&](int32_t k) { return ents[k]; });
+    s.hops += 1;
+  } else {
+    s.rel_lo = llo;
+    s.rel_hi = lhi;
+    s.segment = kObject;
+  }
+  warp_sync();
+  s.depth = 0;
+  s.lo = 0;
+  s.hi = s.segment == kRelation ? t.rel.count : t.ent.count;
+  s.close_pos = s.close_lo = s.close_hi = 0;
+  s.sep_pos = s.sep_lo = s.sep_hi = 0;
+  s.esc_pos = 0;
+  set_flags(c, s);
+}
+
+// The closer completed after the label rows [llo, lhi) (src/xgraph/oracle.py:1115-1214).
+XG_HD void close_span(const Ctx& c, XgState& s, int32_t llo, int32_t lhi) {
+  const Tables& t = c.t;
+  const int32_t version = version_of(c);
+  if (s.segment == kRelation) {  // a path ends
+    int32_t n = next_frontier(c, llo, lhi);
+    if (t.committed && n > 0) {  // keep the least rank present (a prefix of the sorted keys)
+      const uint64_t best = c.top[0].a >> 32;
+      int32_t m = 0;
+      while (m < n && (c.top[m].a >> 32) == best) ++m;
+      n = m;
+    }
+    reach_rows_of_top(c, n);
+    s.last_kind = kPathSpan;
+    s.last_lo = s.last_hi = s.last_subj_lo = s.last_subj_hi = s.last_rel_lo = s.last_rel_hi = 0;
+  } else if (s.segment == kSubject) {
+    const bool bound = !unbound(t, c, s);
+    s.answer_complete = t.end_after_answer && answers_path(t, s) ? 1 : 0;
+    if (bound) {  // one entity: the best-connected candidate
+      const Key best = warp_min(c.w, llo, lhi, [&](int32_t row) {
+        return subject_candidate(c, true, row) ? connected_key(t, version, row) : max_key();
+      });
+      const int32_t row = static_cast<int32_t>(best.b);
+      s.last_lo = row;
+      s.last_hi = row + 1;
+      s.last_subj_lo = row;
+    } else {
+      s.last_lo = llo;
+      s.last_hi = lhi;
+      s.last_subj_lo = -1;
+    }
+    s.last_kind = kEntitySpan;
+    s.last_subj_hi = s.last_rel_lo = s.last_rel_hi = 0;
+  } else {  // a fact span
+    const int32_t facts = c.mem[kMemFacts];
+    if (facts < kMaxSet && c.w.leader()) {
+      c.mem[kMemFactRows + 3 * facts] = s.subj_key;
+      c.mem[kMemFactRows + 3 * facts + 1] = s.rel_lo;
+      c.mem[kMemFactRows + 3 * facts + 2] = llo;
+      c.mem[kMemFacts] = facts + 1;
+    }
+    warp_sync();
+    if (t.derivation) {  // reached: every row of the objects with the label (_reached)
+      const int32_t relations = s.rel_hi - s.rel_lo;
+      TopSet ts{c.top, 0};
+      // entities reached, as first rows, kept distinct (at most 64 needed for 64 rows)
+      for (int32_t p = 0; p < (s.subj_hi - s.subj_lo) * relations; ++p) {
+        const int32_t e = t.ent.owner[s.subj_lo + p / relations];
+        const int32_t r = t.rel.owner[s.rel_lo + p % relations];
+        const Edges g = edges_of(t, version, e);
+        int32_t a, b;
+        relation_slice(g, r, a, b);
+        const int32_t x = lower_index(g.obj, a, b, llo);
+        const int32_t y = lower_index(g.obj, x, b, lhi);
+        for (int32_t base = x; base < y; base += 32) {
+#if XG_GPU
+          const int32_t i = base + c.w.lane;
+          const bool valid = i < y;
+          Key k{0, 0, 0};
+          if (valid) k.a = static_cast<uint32_t>(t.ent_first_row[t.ent.owner[g.obj[i]]]);
+          top_push(c.w, ts, valid, k, kDistinct);
+#else
+          for (int32_t i = base; i < y && i < base + 32; ++i)
+            top_push(c.w, ts, true, Key{static_cast<uint32_t>(t.ent_first_row[t.ent.owner[g.obj[i]]]), 0u, 0u}, kDistinct);
+#endif
+        }
+      }
+      top_compact(c.w, ts, kDistinct);
+      reach_rows_of_top(c, ts.n);
+    }
+    s.last_kind = kFactSpan;
+    s.last_lo = llo;
+    s.last_hi = lhi;
+    s.last_subj_lo = s.subj_lo;
+    s.last_subj_hi = s.subj_hi;
+    s.last_rel_lo = s.rel_lo;
+    s.last_rel_hi = s.rel_hi;
+  }
+  end_span(s, kFree);
+}
+
+XG_HD int32_t delim_step(const Delim& d, int32_t pos, int32_t token) {
+  const int32_t a = d.off[pos], b = d.off[pos + 1];
+  const int32_t at = lower_index(d.tok, a, b, token);
+  return at < b && d.tok[at] == token ? d.next[at] : -1;
+}
+
+// One token inside a span (src/xgraph/oracle.py:896-1263, in-scope branches).
+XG_HD void advance_span(const Ctx& c, XgState& s, int32_t token) {
+  const Tables& t = c.t;
+  int32_t close = -1, sep = -1, esc = -1;
+  int32_t close_lo = s.close_lo, close_hi = s.close_hi, sep_lo = s.sep_lo, sep_hi = s.sep_hi;
+  if (s.close_pos > 0) {
+    close = delim_step(t.closer, s.close_pos, token);
+  } else if (s.flags & kMayClose) {
+    close = delim_step(t.closer, 0, token);
+    close_lo = s.lo;
+    close_hi = s.ex_hi;
+  }
+  if (s.sep_pos > 0) {
+    sep = delim_step(t.separator, s.sep_pos, token);
+  } else if (s.flags & kMaySep) {
+    sep = delim_step(t.separator, 0, token);
+    sep_lo = s.lo;
+    sep_hi = s.ex_hi;
+  }
+  if (s.esc_pos > 0) {
+    esc = delim_step(t.escape, s.esc_pos, token);
+  } else if (s.flags & kMayEsc) {
+    esc = delim_step(t.escape, 0, token);
+  }
+  int32_t lo = -1, hi = -1;
+  if (s.lo >= 0) {
+    const Rows& rows = s.segment == kRelation ? t.rel : t.ent;
+    lo = bound_row(rows, s.lo, s.hi, s.depth, token, false);
+    hi = bound_row(rows, lo, s.hi, s.depth, token, true);
+    if (!has_candidate(c, s, lo, hi)) lo = hi = -1;
+  }
+  if (close == t.closer.len) {
+    close_span(c, s, close_lo, close_hi);
+    return;
+  }
+  if (sep == t.separator.len) {
+    next_segment(c, s, sep_lo, sep_hi);
+    return;
+  }
+  if (esc == t.escape.len) {
+    end_span(s, kEscaped);
+    return;
+  }
+  if (lo < 0 && close < 0 && sep < 0 && esc < 0) {
+    s.phase = kError;
+    return;
+  }
+  s.close_pos = close > 0 ? close : 0;
+  s.close_lo = close > 0 ? close_lo : 0;
+  s.close_hi = close > 0 ? close_hi : 0;
+  s.sep_pos = sep > 0 ? sep : 0;
+  s.sep_lo = sep > 0 ? sep_lo : 0;
+  s.sep_hi = sep > 0 ? sep_hi : 0;
+  s.esc_pos = esc > 0 ? esc : 0;
+  if (lo >= 0) {
+    s.lo = lo;
+    s.hi = hi;
+    s.depth += 1;
+  } else {
+    s.lo = s.hi = -1;
+  }
+  set_flags(c, s);
+}
+
+XG_HD bool eos_allowed(const Tables& t, int32_t token) {
+  return (t.eos_mask[token >> 5] >> (token & 31)) & 1u;
+}
+
+// One token of any phase (src/xgraph/oracle.py:759-828).
+XG_HD void advance_state(const Ctx& c, XgState& s, int32_t token) {
+  const Tables& t = c.t;
+  if (s.phase == kError) return;
+  if (token < 0 || token >= t.vocab) {
+    s.phase = kError;
+    return;
+  }
+  if (s.answer_complete) {
+    if (!eos_allowed(t, token)) s.phase = kError;
+    return;
+  }
+  if (s.phase == kFree) {
+    const int8_t code = t.free_next[static_cast<int64_t>(s.pos) * t.vocab + token];
+    if (code == kReject)
+      s.phase = kError;
+    else if (code == kComplete)
+      open_span(c, s);
+    else
+      s.pos = code;
+  } else if (s.phase == kEscaped) {
+    const int8_t code = t.esc_next[static_cast<int64_t>(s.pos) * t.vocab + token];
+    if (code == kReject) {
+      s.phase = kError;
+    } else if (code == kComplete) {
+      end_span(s, kFree);
+      s.last_kind = kUnresolved;
+      s.last_lo = s.last_hi = s.last_subj_lo = s.last_subj_hi = s.last_rel_lo = s.last_rel_hi = 0;
+    } else {
+      s.pos = code;
+    }
+  } else {
+    advance_span(c, s, token);
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// Mask of the slot's current state.
+
+XG_HD const uint32_t* wide_mask(const Tables& t, int32_t lo, int32_t depth) {
+  if (t.wide_count == 0) return nullptr;
+  const int64_t key = static_cast<int64_t>(lo) * 16 + depth;
+  const int32_t at = lower_index(t.wide_keys, 0, t.wide_count, key);
+  if (at < t.wide_count && t.wide_keys[at] == key) return t.wide_masks + static_cast<int64_t>(at) * t.words_padded;
+  return nullptr;
+}
+
+XG_HD void add_delimiter(const Warp& w, const Delim& d, int32_t pos, uint32_t* out) {
+  warp_for(w, d.off[pos], d.off[pos + 1], [&](int32_t i) { set_bit(out, d.tok[i]); });
+}
+
+// Label tokens that keep a live label branch alive: the column at `depth` of every
+// candidate row in [lo, hi) that continues past it.
+XG_HD void add_label_tokens(const Ctx& c, const XgState& s, uint32_t* out) {
+  const Tables& t = c.t;
+  const int32_t d = s.depth, lo = s.lo, hi = s.hi;
+  if (s.segment == kSubject) {
+    if (unbound(t, c, s)) {
+      warp_for(c.w, lo, hi, [&](int32_t row) {
+        if (kept_row(t, row)) {
+          const int32_t tok = column(t.ent, row, d);
+          if (tok >= 0) set_bit(out, tok);
+        }
+      });
+    } else {
+      const int32_t* reached = c.mem + kMemReachedRows;
+      warp_for(c.w, 0, reached_count(c), [&](int32_t i) {
+        const int32_t row = reached[i];
+        if (row >= lo && row < hi) {
+          const int32_t tok = column(t.ent, row, d);
+          if (tok >= 0) set_bit(out, tok);
+        }
+      });
+    }
+  } else if (s.segment == kRelation) {
+    warp_for(c.w, lo, hi, [&](int32_t row) {
+      const int32_t tok = column(t.rel, row, d);
+      if (tok >= 0 && has_relation(c, t.rel.owner[row])) set_bit(out, tok);
+    });
+  } else {
+    const int32_t relations = s.rel_hi - s.rel_lo;
+    const int32_t version = version_of(c);
+    for (int32_t p = 0; p < (s.subj_hi - s.subj_lo) * relations; ++p) {
+      const int32_t e = t.ent.owner[s.subj_lo + p / relations];
+      const int32_t r = t.rel.owner[s.rel_lo + p % relations];
+      const Edges g = edges_of(t, version, e);
+      int32_t a, b;
+      relation_slice(g, r, a, b);
+      const int32_t x = lower_index(g.obj, a, b, lo);
+      const int32_t y = lower_index(g.obj, x, b, hi);
+      warp_for(c.w, x, y, [&](int32_t i) {
+        const int32_t tok = column(t.ent, g.obj[i], d);
+        if (tok >= 0) set_bit(out, tok);
+      });
+    }
+  }
+}
+
+// Point src[slot] at the slot's mask: a precomputed table row outside spans, the slot's
+// own buffer (built here) inside one, none in the error phase.
+XG_HD void build_mask(const Ctx& c, const XgState& s) {
+  const Tables& t = c.t;
+  const int64_t stride = t.words_padded;
+  if (s.phase == kError) {
+    if (c.w.leader()) t.src[c.slot] = nullptr;
+    return;
+  }
+  if (s.phase == kFree) {
+    if (c.w.leader()) t.src[c.slot] = s.answer_complete ? t.eos_mask : t.free_mask + s.pos * stride;
+    return;
+  }
+  if (s.phase == kEscaped) {
+    if (c.w.leader()) t.src[c.slot] = t.esc_mask + s.pos * stride;
+    return;
+  }
+  uint32_t* out = t.masks + c.slot * stride;
+  const uint32_t* base = nullptr;
+  bool scan = s.lo >= 0;
+  if (scan && unbound(t, c, s)) {
+    if (s.depth == 0 && s.lo == 0 && s.hi == t.ent.count) {
+      base = t.root_mask;
+      scan = false;
+    } else if ((base = wide_mask(t, s.lo, s.depth)) != nullptr) {
+      scan = false;
+    }
+  }
+#if XG_GPU
+  {
+    const uint4* from = reinterpret_cast<const uint4*>(base);
+    uint4* to = reinterpret_cast<uint4*>(out);
+    const int32_t quads = t.words_padded >> 2;
+    for (int32_t i = c.w.lane; i < quads; i += 32) to[i] = base ? from[i] : make_uint4(0u, 0u, 0u, 0u);
+    __syncwarp();
+  }
+#else
+  for (int32_t i = 0; i < t.words_padded; ++i) out[i] = base ? base[i] : 0u;
+#endif
+  if (scan) add_label_tokens(c, s, out);
+  if (s.close_pos > 0)
+    add_delimiter(c.w, t.closer, s.close_pos, out);
+  else if (s.flags & kMayClose)
+    add_delimiter(c.w, t.closer, 0, out);
+  if (s.sep_pos > 0)
+    add_delimiter(c.w, t.separator, s.sep_pos, out);
+  else if (s.flags & kMaySep)
+    add_delimiter(c.w, t.separator, 0, out);
+  if (s.esc_pos > 0)
+    add_delimiter(c.w, t.escape, s.esc_pos, out);
+  else if (s.flags & kMayEsc)
+    add_delimiter(c.w, t.escape, 0, out);
+  warp_sync();
+  if (c.w.leader()) t.src[c.slot] = out;
+}
+
+}  // namespace xg

@@ -1,0 +1,630 @@
+// sm_100a kernels and the C ABI of the KG constraint engine.
+//
+// Per decoding step the serving path runs two kernels:
+//   step_kernel   one warp per request row: consume the row's new tokens (advance or
+//                 sync over the token history in place) and rebuild the row's
+//                 allowed-token bitmask for its new state (core.cuh);
+//   apply_kernel  a flat grid over (logits row, 8192-column chunk): read 8 mask bits per
+//                 thread and write -inf over every disallowed column with 16-byte stores,
+//                 leaving allowed columns untouched (HBM-write bound).
+// The reference runs the same step as sync_kernel + row_mask_kernel + apply_kernel
+// (csrc/engine.cu:2057-2074, 2372-2451, 2562-2587); here the mask is built where the
+// state changes, so apply_mask is a single bandwidth kernel.
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "core.cuh"
+
+namespace xg {
+
+constexpr int32_t kWarpsPerBlock = 4;
+constexpr int32_t kApplyThreads = 256;
+constexpr int32_t kApplyIters = 4;
+constexpr int32_t kGroupsPerChunk = kApplyThreads * kApplyIters;  // 8 columns per group
+
+struct __align__(16) WarpShared {
+  Key top[kTopCap];
+  int32_t scratch[kScratchInts + 2];
+};
+
+__device__ __forceinline__ Ctx make_ctx(const Tables& t, int32_t slot, WarpShared& sh) {
+  return Ctx{t, Warp{static_cast<int32_t>(threadIdx.x & 31)}, slot,
+             t.memory + static_cast<int64_t>(slot) * t.memory_ints, sh.top, sh.scratch};
+}
+
+__device__ __forceinline__ void store_state(const Tables& t, int32_t slot, const XgState& s) {
+  if ((threadIdx.x & 31) == 0) t.states[slot] = s;
+  __syncwarp();
+}
+
+struct StepArgs {
+  const int32_t* slots;      // sync: slot per entry; advance: null (entry i is slot i)
+  const int32_t* tokens;     // advance: one token per entry
+  const int32_t* history;    // sync: [slots, stride]
+  int64_t stride;
+  const int32_t* prompt_len;
+  const int32_t* total_len;
+  int32_t count;
+};
+
+// Advance (tokens) or sync (history) one slot per warp, then rebuild its mask.
+__global__ void __launch_bounds__(kWarpsPerBlock * 32)
+    step_kernel(const __grid_constant__ Tables t, const StepArgs a) {
+  __shared__ WarpShared shared[kWarpsPerBlock];
+  const int32_t warp = threadIdx.x >> 5;
+  const int32_t i = blockIdx.x * kWarpsPerBlock + warp;
+  if (i >= a.count) return;  // warp-uniform
+  const int32_t slot = a.slots ? a.slots[i] : i;
+  Ctx c = make_ctx(t, slot, shared[warp]);
+  XgState s = t.states[slot];
+  if (a.history) {
+    if (!t.active[slot]) return;
+    int32_t cursor = t.cursors[slot] < 0 ? a.prompt_len[slot] : t.cursors[slot];
+    const int32_t end = a.total_len[slot];
+    if (cursor >= end) {
+      if ((threadIdx.x & 31) == 0) t.cursors[slot] = cursor;
+      return;
+    }
+    const int32_t* tokens = a.history + a.stride * slot;
+    for (; cursor < end; ++cursor) advance_state(c, s, tokens[cursor]);
+    if ((threadIdx.x & 31) == 0) t.cursors[slot] = cursor;
+  } else {
+    advance_state(c, s, a.tokens[i]);
+  }
+  store_state(t, slot, s);
+  build_mask(c, s);
+}
+
+// Lifecycle of one slot, one warp: 0 open a span, 1 select a version, 2 anchor rows.
+struct SlotArgs {
+  int32_t slot, op, value, count;
+  int32_t rows[kMaxSet];
+};
+
+__global__ void __launch_bounds__(32) slot_kernel(const __grid_constant__ Tables t, const SlotArgs a) {
+  __shared__ WarpShared shared[1];
+  Ctx c = make_ctx(t, a.slot, shared[0]);
+  XgState s = t.states[a.slot];
+  if (a.op == 0) {
+    if (s.phase != kError) {
+      s.answer_complete = 0;
+      open_span(c, s);
+    }
+  } else if (a.op == 1) {
+    if (c.w.leader()) c.mem[kMemVersion] = a.value;
+    __syncwarp();
+    if (s.phase == kSpan) set_flags(c, s);  // a KG read changed under the open span
+  } else {
+    if (threadIdx.x < a.count) c.mem[kMemReachedRows + threadIdx.x] = a.rows[threadIdx.x];
+    if (threadIdx.x + 32 < a.count) c.mem[kMemReachedRows + threadIdx.x + 32] = a.rows[threadIdx.x + 32];
+    if (c.w.leader()) c.mem[kMemReached] = a.count;
+    __syncwarp();
+    if (s.phase == kSpan) set_flags(c, s);
+  }
+  store_state(t, a.slot, s);
+  build_mask(c, s);
+}
+
+// begin/end: listed slots back to the initial state (free text, base KG, no binding).
+__global__ void begin_kernel(const __grid_constant__ Tables t, const int32_t* slots, int32_t count,
+                             int32_t on, int32_t max_slots) {
+  const int32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= count) return;
+  const int32_t slot = slots ? slots[i] : i;
+  if (slot < 0 || slot >= max_slots) return;
+  XgState* s = t.states + slot;
+  int32_t* words = reinterpret_cast<int32_t*>(s);
+  for (int32_t k = 0; k < XG_STATE_INTS; ++k) words[k] = 0;
+  int32_t* mem = t.memory + static_cast<int64_t>(slot) * t.memory_ints;
+  mem[kMemFacts] = mem[kMemReached] = mem[kMemFrontier] = mem[kMemVersion] = 0;
+  t.cursors[slot] = -1;
+  t.active[slot] = on;
+  t.src[slot] = t.free_mask;
+}
+
+// fill_mask: materialize each slot's current mask into its own buffer row.
+__global__ void fill_kernel(const __grid_constant__ Tables t) {
+  const int32_t slot = blockIdx.x;
+  uint32_t* own = t.masks + static_cast<int64_t>(slot) * t.words_padded;
+  const uint32_t* from = t.src[slot];
+  if (from == own) return;
+  for (int32_t i = threadIdx.x; i < t.words_padded; i += blockDim.x) own[i] = from ? from[i] : 0u;
+}
+
+template <typename T>
+struct NegInf;
+template <>
+struct NegInf<float> {
+  static constexpr uint32_t bits = 0xff800000u;
+};
+template <>
+struct NegInf<uint16_t> {  // bf16 and fp16 share the store path; the pattern is passed in
+  static constexpr uint32_t bits = 0u;
+};
+
+// Allowed bits of the 8 columns starting at column c (c >= 0): a 64-bit window of words.
+__device__ __forceinline__ uint32_t allowed8(const uint32_t* m, int32_t words, int64_t c) {
+  const int64_t w = c >> 5;
+  const int32_t sh = static_cast<int32_t>(c & 31);
+  uint64_t x = w < words ? m[w] : 0u;
+  if (sh > 24 && w + 1 < words) x |= static_cast<uint64_t>(m[w + 1]) << 32;
+  return static_cast<uint32_t>(x >> sh) & 0xffu;
+}
+
+// -inf into every disallowed column of every row of an active, non-error slot.
+// ELT: element bytes (2 or 4); neg: the element's -inf bit pattern.
+template <int ELT>
+__global__ void __launch_bounds__(kApplyThreads)
+    apply_kernel(const __grid_constant__ Tables t, char* logits, int32_t cols, int64_t stride,
+                 const int32_t* row_slots, int32_t chunks, int32_t max_slots, uint32_t neg) {
+  const int32_t row = blockIdx.x / chunks;
+  const int32_t chunk = blockIdx.x - row * chunks;
+  const int32_t slot = row_slots[row];
+  if (slot < 0 || slot >= max_slots || !t.active[slot]) return;
+  const uint32_t* m = t.src[slot];
+  if (m == nullptr) return;
+  char* out = logits + static_cast<int64_t>(row) * stride * ELT;
+  const int32_t lead = static_cast<int32_t>(((16u - (reinterpret_cast<uintptr_t>(out) & 15u)) & 15u) / ELT);
+  const int32_t words = t.words;
+  const int64_t first = static_cast<int64_t>(chunk) * kGroupsPerChunk + threadIdx.x;
+#pragma unroll
+  for (int32_t it = 0; it < kApplyIters; ++it) {
+    const int64_t c = lead + 8 * (first + it * kApplyThreads);
+    if (c >= cols) break;
+    uint32_t blocked = ~allowed8(m, words, c) & 0xffu;
+    const int64_t left = cols - c;
+    if (left < 8) blocked &= (1u << left) - 1u;
+    if (blocked == 0u) continue;
+    char* at = out + c * ELT;
+    if (blocked == 0xffu) {
+      if (ELT == 2) {
+        const uint32_t v = neg | (neg << 16);
+        *reinterpret_cast<uint4*>(at) = make_uint4(v, v, v, v);
+      } else {
+        *reinterpret_cast<uint4*>(at) = make_uint4(neg, neg, neg, neg);
+        *reinterpret_cast<uint4*>(at + 16) = make_uint4(neg, neg, neg, neg);
+      }
+    } else {
+      for (int32_t k = 0; k < 8; ++k) {
+        if ((blocked >> k) & 1u) {
+          if (ELT == 2)
+            *reinterpret_cast<uint16_t*>(at + 2 * k) = static_cast<uint16_t>(neg);
+          else
+            *reinterpret_cast<uint32_t*>(at + 4 * k) = neg;
+        }
+      }
+    }
+  }
+  if (chunk == 0 && static_cast<int32_t>(threadIdx.x) < lead && static_cast<int32_t>(threadIdx.x) < cols) {
+    const int32_t col = threadIdx.x;  // the columns before the first 16-byte boundary
+    const bool allowed = col < t.vocab && ((m[col >> 5] >> (col & 31)) & 1u);
+    if (!allowed) {
+      if (ELT == 2)
+        *reinterpret_cast<uint16_t*>(out + 2 * col) = static_cast<uint16_t>(neg);
+      else
+        *reinterpret_cast<uint32_t*>(out + 4 * col) = neg;
+    }
+  }
+}
+
+}  // namespace xg
+
+// ===========================================================================================
+// C ABI
+
+using namespace xg;
+
+struct XgEngine {
+  int device = 0;
+  XgLayout layout{};
+  XgOptions options{};
+  int32_t max_sequences = 0;
+  char* blob = nullptr;
+  XgState* states = nullptr;
+  int32_t* memory = nullptr;
+  uint32_t* masks = nullptr;
+  const uint32_t** src = nullptr;
+  int32_t* cursors = nullptr;
+  int32_t* active = nullptr;
+  int32_t* tokens = nullptr;
+  Tables t{};
+};
+
+namespace {
+
+thread_local std::string g_error;
+
+int fail(int code, const std::string& message) {
+  g_error = message;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  cudaGetLastError();  // clear a non-sticky error so the next call starts clean
+  return fail(XG_ECUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+#define XG_CUDA(call, what)                      \
+  do {                                           \
+    const cudaError_t e_ = (call);               \
+    if (e_ != cudaSuccess) return cuda_fail(e_, what); \
+  } while (0)
+
+cudaStream_t as_stream(void* stream) { return reinterpret_cast<cudaStream_t>(stream); }
+
+template <class T>
+const T* at(const char* blob, int64_t offset) {
+  return offset < 0 ? nullptr : reinterpret_cast<const T*>(blob + offset);
+}
+
+int check_layout(const XgLayout& l) {
+  if (l.vocab <= 0 || l.words != (l.vocab + 31) / 32 || l.words_padded < l.words || l.words_padded % 4)
+    return fail(XG_EINVAL, "layout: vocabulary and mask words disagree");
+  if (l.entity_rows < 0 || l.relation_rows < 0 || l.entities < 0 || l.relations < 0 || l.versions < 0 ||
+      l.wide_count < 0 || l.relation_words != (l.relations + 31) / 32)
+    return fail(XG_EINVAL, "layout: negative or inconsistent table sizes");
+  if (l.opener_len <= 0 || l.closer_len <= 0 || l.separator_len <= 0 || l.escape_len <= 0 ||
+      l.opener_len > 127 || l.closer_len > 127)
+    return fail(XG_EINVAL, "layout: delimiter lengths out of range");
+  const int64_t required[] = {l.ent_tok, l.ent_off, l.ent_owner, l.rel_tok, l.rel_off, l.rel_owner,
+                              l.ent_first_row, l.ent_rows_off, l.ent_rows, l.adj_off, l.edge_rel,
+                              l.edge_obj, l.root_mask, l.free_next, l.free_mask, l.esc_next,
+                              l.esc_mask, l.eos_mask, l.closer_off, l.closer_tok, l.closer_next,
+                              l.separator_off, l.separator_tok, l.separator_next, l.escape_off,
+                              l.escape_tok, l.escape_next, l.ver_off, l.ver_subj, l.ver_adj,
+                              l.ver_edge_rel, l.ver_edge_obj};
+  for (int64_t off : required)
+    if (off < 0 || off > l.blob_bytes || off % 16) return fail(XG_EINVAL, "layout: table offset outside the blob");
+  const int64_t optional[] = {l.sitelinks, l.kept_prefix, l.wide_keys, l.wide_masks};
+  for (int64_t off : optional)
+    if (off != -1 && (off < 0 || off > l.blob_bytes || off % 16))
+      return fail(XG_EINVAL, "layout: optional table offset outside the blob");
+  if (l.wide_count > 0 && (l.wide_keys < 0 || l.wide_masks < 0)) return fail(XG_EINVAL, "layout: wide masks missing");
+  return XG_OK;
+}
+
+void bind_tables(XgEngine* e) {
+  const XgLayout& l = e->layout;
+  const char* b = e->blob;
+  Tables& t = e->t;
+  t.ent = Rows{at<int32_t>(b, l.ent_tok), at<int32_t>(b, l.ent_off), at<int32_t>(b, l.ent_owner), l.entity_rows};
+  t.rel = Rows{at<int32_t>(b, l.rel_tok), at<int32_t>(b, l.rel_off), at<int32_t>(b, l.rel_owner), l.relation_rows};
+  t.ent_first_row = at<int32_t>(b, l.ent_first_row);
+  t.ent_rows_off = at<int32_t>(b, l.ent_rows_off);
+  t.ent_rows = at<int32_t>(b, l.ent_rows);
+  t.adj_off = at<int32_t>(b, l.adj_off);
+  t.edge_rel = at<int32_t>(b, l.edge_rel);
+  t.edge_obj = at<int32_t>(b, l.edge_obj);
+  t.sitelinks = e->options.sitelinks_rank ? at<int32_t>(b, l.sitelinks) : nullptr;
+  t.kept_prefix = at<int32_t>(b, l.kept_prefix);
+  t.root_mask = at<uint32_t>(b, l.root_mask);
+  t.wide_keys = at<int64_t>(b, l.wide_keys);
+  t.wide_masks = at<uint32_t>(b, l.wide_masks);
+  t.wide_count = l.wide_count;
+  t.free_next = at<int8_t>(b, l.free_next);
+  t.free_mask = at<uint32_t>(b, l.free_mask);
+  t.esc_next = at<int8_t>(b, l.esc_next);
+  t.esc_mask = at<uint32_t>(b, l.esc_mask);
+  t.eos_mask = at<uint32_t>(b, l.eos_mask);
+  t.closer = Delim{at<int32_t>(b, l.closer_off), at<int32_t>(b, l.closer_tok), at<int32_t>(b, l.closer_next), l.closer_len};
+  t.separator = Delim{at<int32_t>(b, l.separator_off), at<int32_t>(b, l.separator_tok),
+                      at<int32_t>(b, l.separator_next), l.separator_len};
+  t.escape = Delim{at<int32_t>(b, l.escape_off), at<int32_t>(b, l.escape_tok), at<int32_t>(b, l.escape_next), l.escape_len};
+  t.ver_off = at<int32_t>(b, l.ver_off);
+  t.ver_subj = at<int32_t>(b, l.ver_subj);
+  t.ver_adj = at<int32_t>(b, l.ver_adj);
+  t.ver_edge_rel = at<int32_t>(b, l.ver_edge_rel);
+  t.ver_edge_obj = at<int32_t>(b, l.ver_edge_obj);
+  t.versions = l.versions;
+  t.vocab = l.vocab;
+  t.words = l.words;
+  t.words_padded = l.words_padded;
+  t.entities = l.entities;
+  t.relations = l.relations;
+  t.relation_words = l.relation_words;
+  const XgOptions& o = e->options;
+  t.escapes = o.escapes;
+  t.repeats = o.repeats;
+  t.derivation = o.derivation || o.paths;
+  t.paths = o.paths;
+  t.bound_escapes = o.bound_escapes;
+  t.committed = o.committed_paths;
+  t.end_after_answer = o.end_after_answer;
+  t.states = e->states;
+  t.memory = e->memory;
+  t.memory_ints = kMemHave + ((l.relation_words + 3) & ~3);
+  t.masks = e->masks;
+  t.src = e->src;
+  t.cursors = e->cursors;
+  t.active = e->active;
+}
+
+void release(XgEngine* e) {
+  cudaFree(e->blob);
+  cudaFree(e->states);
+  cudaFree(e->memory);
+  cudaFree(e->masks);
+  cudaFree(const_cast<uint32_t**>(e->src));
+  cudaFree(e->cursors);
+  cudaFree(e->active);
+  cudaFree(e->tokens);
+  delete e;
+}
+
+int create(const void* blob, bool on_device, const XgLayout* layout, const XgOptions* options,
+           int32_t max_sequences, XgEngine** out) {
+  if (!blob || !layout || !options || !out) return fail(XG_EINVAL, "null argument");
+  *out = nullptr;
+  if (max_sequences < 1) return fail(XG_EINVAL, "max_sequences must be at least 1, got " + std::to_string(max_sequences));
+  if (int rc = check_layout(*layout)) return rc;
+  if (options->sitelinks_rank && layout->sitelinks < 0)
+    return fail(XG_EINVAL, "the sitelink rank needs a KG index with sitelink counts");
+  XgEngine* e = new XgEngine();
+  e->layout = *layout;
+  e->options = *options;
+  e->max_sequences = max_sequences;
+  cudaGetDevice(&e->device);
+  const int64_t slots = max_sequences;
+  const int32_t memory_ints = kMemHave + ((layout->relation_words + 3) & ~3);
+  cudaError_t err = cudaSuccess;
+  auto alloc = [&](void** p, size_t bytes) {
+    if (err == cudaSuccess) err = cudaMalloc(p, bytes > 0 ? bytes : 16);
+  };
+  alloc(reinterpret_cast<void**>(&e->blob), static_cast<size_t>(layout->blob_bytes));
+  alloc(reinterpret_cast<void**>(&e->states), slots * sizeof(XgState));
+  alloc(reinterpret_cast<void**>(&e->memory), slots * memory_ints * sizeof(int32_t));
+  alloc(reinterpret_cast<void**>(&e->masks), slots * layout->words_padded * sizeof(uint32_t));
+  alloc(reinterpret_cast<void**>(&e->src), slots * sizeof(uint32_t*));
+  alloc(reinterpret_cast<void**>(&e->cursors), slots * sizeof(int32_t));
+  alloc(reinterpret_cast<void**>(&e->active), slots * sizeof(int32_t));
+  alloc(reinterpret_cast<void**>(&e->tokens), slots * sizeof(int32_t));
+  if (err != cudaSuccess) {
+    release(e);
+    cudaGetLastError();
+    return fail(XG_ENOMEM, std::string("device allocation failed: ") + cudaGetErrorString(err));
+  }
+  err = cudaMemcpy(e->blob, blob, static_cast<size_t>(layout->blob_bytes),
+                   on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice);
+  if (err == cudaSuccess) err = cudaMemset(e->memory, 0, slots * memory_ints * sizeof(int32_t));
+  if (err == cudaSuccess) err = cudaMemset(e->masks, 0, slots * layout->words_padded * sizeof(uint32_t));
+  if (err != cudaSuccess) {
+    release(e);
+    return cuda_fail(err, "engine upload");
+  }
+  bind_tables(e);
+  begin_kernel<<<static_cast<unsigned>((slots + 127) / 128), 128>>>(e->t, nullptr, max_sequences, 0, max_sequences);
+  err = cudaGetLastError();
+  if (err == cudaSuccess) err = cudaDeviceSynchronize();
+  if (err != cudaSuccess) {
+    release(e);
+    return cuda_fail(err, "engine initialization");
+  }
+  *out = e;
+  return XG_OK;
+}
+
+int check_slot(const XgEngine* e, int32_t slot) {
+  if (slot < 0 || slot >= e->max_sequences)
+    return fail(XG_EINVAL, "slot must be between 0 and max_sequences - 1, got " + std::to_string(slot));
+  return XG_OK;
+}
+
+int slot_op(XgEngine* e, const SlotArgs& a, void* stream) {
+  slot_kernel<<<1, 32, 0, as_stream(stream)>>>(e->t, a);
+  XG_CUDA(cudaGetLastError(), "slot kernel");
+  return XG_OK;
+}
+
+int launch_step(XgEngine* e, const StepArgs& a, void* stream) {
+  if (a.count == 0) return XG_OK;
+  step_kernel<<<static_cast<unsigned>((a.count + kWarpsPerBlock - 1) / kWarpsPerBlock), kWarpsPerBlock * 32, 0,
+                as_stream(stream)>>>(e->t, a);
+  XG_CUDA(cudaGetLastError(), "step kernel");
+  return XG_OK;
+}
+
+int copy_host(void* out, const void* device, size_t bytes) {
+  XG_CUDA(cudaDeviceSynchronize(), "engine step");
+  if (bytes) XG_CUDA(cudaMemcpy(out, device, bytes, cudaMemcpyDeviceToHost), "copy to host");
+  return XG_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* xg_last_error(void) { return g_error.c_str(); }
+
+int32_t xg_abi_version(void) { return XG_ABI_VERSION; }
+
+int xg_create(const void* blob_host, const XgLayout* layout, const XgOptions* options, int32_t max_sequences,
+              XgEngine** out) {
+  return create(blob_host, false, layout, options, max_sequences, out);
+}
+
+int xg_create_from_device(const void* blob_device, const XgLayout* layout, const XgOptions* options,
+                          int32_t max_sequences, XgEngine** out) {
+  return create(blob_device, true, layout, options, max_sequences, out);
+}
+
+int xg_destroy(XgEngine* engine) {
+  if (!engine) return XG_OK;
+  cudaDeviceSynchronize();
+  release(engine);
+  return XG_OK;
+}
+
+int xg_info(const XgEngine* e, XgInfo* out) {
+  if (!e || !out) return fail(XG_EINVAL, "null argument");
+  *out = XgInfo{e->max_sequences, e->layout.vocab, e->layout.words, e->layout.words_padded, e->t.memory_ints, e->device};
+  return XG_OK;
+}
+
+int xg_reset(XgEngine* e, void* stream) {
+  if (!e) return fail(XG_EINVAL, "null engine");
+  begin_kernel<<<static_cast<unsigned>((e->max_sequences + 127) / 128), 128, 0, as_stream(stream)>>>(
+      e->t, nullptr, e->max_sequences, 0, e->max_sequences);
+  XG_CUDA(cudaGetLastError(), "reset kernel");
+  return XG_OK;
+}
+
+int xg_begin(XgEngine* e, const int32_t* slots, int32_t count, int32_t on, void* stream) {
+  if (!e) return fail(XG_EINVAL, "null engine");
+  if (count < 0 || count > e->max_sequences) return fail(XG_EINVAL, "more slots than max_sequences");
+  if (count == 0) return XG_OK;
+  if (!slots) return fail(XG_EINVAL, "null slots");
+  begin_kernel<<<static_cast<unsigned>((count + 127) / 128), 128, 0, as_stream(stream)>>>(e->t, slots, count, on ? 1 : 0,
+                                                                                          e->max_sequences);
+  XG_CUDA(cudaGetLastError(), "begin kernel");
+  return XG_OK;
+}
+
+int xg_set_reached(XgEngine* e, int32_t slot, const int32_t* rows, int32_t count, void* stream) {
+  if (!e) return fail(XG_EINVAL, "null engine");
+  if (int rc = check_slot(e, slot)) return rc;
+  if (count <= 0 || !rows) return fail(XG_EINVAL, "anchor has no writable label rows");
+  SlotArgs a{};
+  a.slot = slot;
+  a.op = 2;
+  a.count = count < kMaxSet ? count : kMaxSet;
+  for (int32_t i = 0; i < a.count; ++i) {
+    if (rows[i] < 0 || rows[i] >= e->layout.entity_rows || (i > 0 && rows[i] <= rows[i - 1]))
+      return fail(XG_EINVAL, "anchor rows must be sorted, distinct label rows of the index");
+    a.rows[i] = rows[i];
+  }
+  return slot_op(e, a, stream);
+}
+
+int xg_set_version(XgEngine* e, int32_t slot, int32_t version, void* stream) {
+  if (!e) return fail(XG_EINVAL, "null engine");
+  if (int rc = check_slot(e, slot)) return rc;
+  if (version < 0 || version > e->layout.versions)
+    return fail(XG_EINVAL, "KG version must be between 0 and " + std::to_string(e->layout.versions) + ", got " +
+                               std::to_string(version));
+  SlotArgs a{};
+  a.slot = slot;
+  a.op = 1;
+  a.value = version;
+  return slot_op(e, a, stream);
+}
+
+int xg_open_span(XgEngine* e, int32_t slot, void* stream) {
+  if (!e) return fail(XG_EINVAL, "null engine");
+  if (int rc = check_slot(e, slot)) return rc;
+  SlotArgs a{};
+  a.slot = slot;
+  a.op = 0;
+  return slot_op(e, a, stream);
+}
+
+int xg_advance(XgEngine* e, const int32_t* tokens, int32_t count, int32_t tokens_on_host, void* stream) {
+  if (!e) return fail(XG_EINVAL, "null engine");
+  if (count < 0 || count > e->max_sequences)
+    return fail(XG_EINVAL, "sequences must be between 0 and max_sequences (" + std::to_string(e->max_sequences) +
+                               "), got " + std::to_string(count));
+  if (count == 0) return XG_OK;
+  if (!tokens) return fail(XG_EINVAL, "null tokens");
+  const int32_t* device_tokens = tokens;
+  if (tokens_on_host) {
+    XG_CUDA(cudaMemcpyAsync(e->tokens, tokens, count * sizeof(int32_t), cudaMemcpyHostToDevice, as_stream(stream)),
+            "token upload");
+    device_tokens = e->tokens;
+  }
+  StepArgs a{};
+  a.tokens = device_tokens;
+  a.count = count;
+  return launch_step(e, a, stream);
+}
+
+int xg_sync(XgEngine* e, const int32_t* slots, int32_t count, const int32_t* history, int64_t history_stride,
+            int64_t history_rows, const int32_t* prompt_len, const int32_t* total_len, int64_t lengths_count,
+            void* stream) {
+  if (!e) return fail(XG_EINVAL, "null engine");
+  if (count < 0 || count > e->max_sequences) return fail(XG_EINVAL, "more slots than max_sequences");
+  if (lengths_count < e->max_sequences) return fail(XG_EINVAL, "prompt_len and total_len need one entry per slot");
+  if (history_rows < e->max_sequences || history_stride < 0)
+    return fail(XG_EINVAL, "history needs one contiguous row per slot");
+  if (count == 0) return XG_OK;
+  if (!slots || !history || !prompt_len || !total_len) return fail(XG_EINVAL, "null argument");
+  StepArgs a{};
+  a.slots = slots;
+  a.history = history;
+  a.stride = history_stride;
+  a.prompt_len = prompt_len;
+  a.total_len = total_len;
+  a.count = count;
+  return launch_step(e, a, stream);
+}
+
+int xg_fill_mask(XgEngine* e, int32_t sequences, void* stream) {
+  if (!e) return fail(XG_EINVAL, "null engine");
+  if (sequences < 0 || sequences > e->max_sequences)
+    return fail(XG_EINVAL, "sequences must be between 0 and max_sequences (" + std::to_string(e->max_sequences) +
+                               "), got " + std::to_string(sequences));
+  if (sequences == 0) return XG_OK;
+  fill_kernel<<<sequences, 256, 0, as_stream(stream)>>>(e->t);
+  XG_CUDA(cudaGetLastError(), "fill kernel");
+  return XG_OK;
+}
+
+int xg_mask_device(XgEngine* e, uint32_t** out) {
+  if (!e || !out) return fail(XG_EINVAL, "null argument");
+  *out = e->masks;
+  return XG_OK;
+}
+
+int xg_mask_host(XgEngine* e, int32_t sequences, uint32_t* out) {
+  if (!e || (!out && sequences)) return fail(XG_EINVAL, "null argument");
+  if (sequences < 0 || sequences > e->max_sequences) return fail(XG_EINVAL, "sequences out of range");
+  XG_CUDA(cudaDeviceSynchronize(), "engine step");
+  if (sequences == 0) return XG_OK;
+  XG_CUDA(cudaMemcpy2D(out, e->layout.words * sizeof(uint32_t), e->masks, e->layout.words_padded * sizeof(uint32_t),
+                       e->layout.words * sizeof(uint32_t), sequences, cudaMemcpyDeviceToHost),
+          "copy to host");
+  return XG_OK;
+}
+
+int xg_states_host(XgEngine* e, int32_t sequences, int32_t* out) {
+  if (!e || (!out && sequences)) return fail(XG_EINVAL, "null argument");
+  if (sequences < 0 || sequences > e->max_sequences) return fail(XG_EINVAL, "sequences out of range");
+  return copy_host(out, e->states, static_cast<size_t>(sequences) * sizeof(XgState));
+}
+
+int xg_memory_host(XgEngine* e, int32_t sequences, int32_t* out) {
+  if (!e || (!out && sequences)) return fail(XG_EINVAL, "null argument");
+  if (sequences < 0 || sequences > e->max_sequences) return fail(XG_EINVAL, "sequences out of range");
+  return copy_host(out, e->memory, static_cast<size_t>(sequences) * e->t.memory_ints * sizeof(int32_t));
+}
+
+int xg_apply_mask(XgEngine* e, void* logits, int32_t dtype, int32_t rows, int32_t cols, int64_t row_stride,
+                  const int32_t* row_slots, const int32_t* local_pos, const int32_t* input_ids, void* stream) {
+  if (!e) return fail(XG_EINVAL, "null engine");
+  if ((local_pos == nullptr) != (input_ids == nullptr)) return fail(XG_EINVAL, "local_pos and input_ids go together");
+  if (local_pos) return fail(XG_EINVAL, "speculative draft rows are not supported by this engine version");
+  if (rows < 0 || cols < 0 || row_stride < cols) return fail(XG_EINVAL, "logits need one contiguous row per entry of row_slots");
+  if (dtype != XG_F32 && dtype != XG_BF16 && dtype != XG_F16) return fail(XG_EINVAL, "logits must be float32, bfloat16 or float16");
+  if (rows == 0 || cols == 0) return XG_OK;
+  if (!logits || !row_slots) return fail(XG_EINVAL, "null argument");
+  const int elt = dtype == XG_F32 ? 4 : 2;
+  if (reinterpret_cast<uintptr_t>(logits) % elt) return fail(XG_EINVAL, "logits are not aligned to their element size");
+  const int64_t groups = (static_cast<int64_t>(cols) + 7) / 8 + 1;
+  const int32_t chunks = static_cast<int32_t>((groups + kGroupsPerChunk - 1) / kGroupsPerChunk);
+  const int64_t blocks = static_cast<int64_t>(rows) * chunks;
+  if (blocks > 0x7fffffff) return fail(XG_EINVAL, "too many logits rows");
+  cudaStream_t s = as_stream(stream);
+  if (dtype == XG_F32) {
+    apply_kernel<4><<<static_cast<unsigned>(blocks), kApplyThreads, 0, s>>>(
+        e->t, static_cast<char*>(logits), cols, row_stride, row_slots, chunks, e->max_sequences, 0xff800000u);
+  } else {
+    apply_kernel<2><<<static_cast<unsigned>(blocks), kApplyThreads, 0, s>>>(
+        e->t, static_cast<char*>(logits), cols, row_stride, row_slots, chunks, e->max_sequences,
+        dtype == XG_BF16 ? 0xff80u : 0xfc00u);
+  }
+  XG_CUDA(cudaGetLastError(), "apply kernel");
+  return XG_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,181 @@
+// Host test seam: the engine's per-row logic (core.cuh) compiled as sequential C++.
+//
+// TEST ONLY.  tests/seam.py builds this file with g++ and replays oracle walks through it
+// on the CPU, so logic errors in core.cuh show up without a GPU.  The product library
+// (libxgraph_b200.so, engine.cu) never loads or links it, and it exports xgs_* names that
+// nothing in xgraph_b200/ calls.
+#include <cstring>
+#include <vector>
+
+#include "core.cuh"
+
+using namespace xg;
+
+struct SeamEngine {
+  std::vector<char> blob;
+  XgLayout layout{};
+  int32_t slots = 0;
+  std::vector<XgState> states;
+  std::vector<int32_t> memory;
+  std::vector<uint32_t> masks;
+  std::vector<const uint32_t*> src;
+  std::vector<int32_t> cursors, active;
+  std::vector<Key> top;
+  std::vector<int32_t> scratch;
+  Tables t{};
+};
+
+template <class T>
+static const T* at(const char* blob, int64_t offset) {
+  return offset < 0 ? nullptr : reinterpret_cast<const T*>(blob + offset);
+}
+
+static Ctx ctx(SeamEngine* e, int32_t slot) {
+  return Ctx{e->t, Warp{0}, slot, e->memory.data() + static_cast<int64_t>(slot) * e->t.memory_ints, e->top.data(),
+             e->scratch.data()};
+}
+
+static void begin_slot(SeamEngine* e, int32_t slot, int32_t on) {
+  std::memset(&e->states[slot], 0, sizeof(XgState));
+  int32_t* mem = e->memory.data() + static_cast<int64_t>(slot) * e->t.memory_ints;
+  mem[kMemFacts] = mem[kMemReached] = mem[kMemFrontier] = mem[kMemVersion] = 0;
+  e->cursors[slot] = -1;
+  e->active[slot] = on;
+  e->src[slot] = e->t.free_mask;
+}
+
+extern "C" {
+
+SeamEngine* xgs_create(const void* blob, const XgLayout* l, const XgOptions* o, int32_t slots) {
+  SeamEngine* e = new SeamEngine();
+  e->blob.assign(static_cast<const char*>(blob), static_cast<const char*>(blob) + l->blob_bytes);
+  e->layout = *l;
+  e->slots = slots;
+  const char* b = e->blob.data();
+  Tables& t = e->t;
+  t.ent = Rows{at<int32_t>(b, l->ent_tok), at<int32_t>(b, l->ent_off), at<int32_t>(b, l->ent_owner), l->entity_rows};
+  t.rel = Rows{at<int32_t>(b, l->rel_tok), at<int32_t>(b, l->rel_off), at<int32_t>(b, l->rel_owner), l->relation_rows};
+  t.ent_first_row = at<int32_t>(b, l->ent_first_row);
+  t.ent_rows_off = at<int32_t>(b, l->ent_rows_off);
+  t.ent_rows = at<int32_t>(b, l->ent_rows);
+  t.adj_off = at<int32_t>(b, l->adj_off);
+  t.edge_rel = at<int32_t>(b, l->edge_rel);
+  t.edge_obj = at<int32_t>(b, l->edge_obj);
+  t.sitelinks = o->sitelinks_rank ? at<int32_t>(b, l->sitelinks) : nullptr;
+  t.kept_prefix = at<int32_t>(b, l->kept_prefix);
+  t.root_mask = at<uint32_t>(b, l->root_mask);
+  t.wide_keys = at<int64_t>(b, l->wide_keys);
+  t.wide_masks = at<uint32_t>(b, l->wide_masks);
+  t.wide_count = l->wide_count;
+  t.free_next = at<int8_t>(b, l->free_next);
+  t.free_mask = at<uint32_t>(b, l->free_mask);
+  t.esc_next = at<int8_t>(b, l->esc_next);
+  t.esc_mask = at<uint32_t>(b, l->esc_mask);
+  t.eos_mask = at<uint32_t>(b, l->eos_mask);
+  t.closer = Delim{at<int32_t>(b, l->closer_off), at<int32_t>(b, l->closer_tok), at<int32_t>(b, l->closer_next), l->closer_len};
+  t.separator = Delim{at<int32_t>(b, l->separator_off), at<int32_t>(b, l->separator_tok), at<int32_t>(b, l->separator_next),
+                      l->separator_len};
+  t.escape = Delim{at<int32_t>(b, l->escape_off), at<int32_t>(b, l->escape_tok), at<int32_t>(b, l->escape_next), l->escape_len};
+  t.ver_off = at<int32_t>(b, l->ver_off);
+  t.ver_subj = at<int32_t>(b, l->ver_subj);
+  t.ver_adj = at<int32_t>(b, l->ver_adj);
+  t.ver_edge_rel = at<int32_t>(b, l->ver_edge_rel);
+  t.ver_edge_obj = at<int32_t>(b, l->ver_edge_obj);
+  t.versions = l->versions;
+  t.vocab = l->vocab;
+  t.words = l->words;
+  t.words_padded = l->words_padded;
+  t.entities = l->entities;
+  t.relations = l->relations;
+  t.relation_words = l->relation_words;
+  t.escapes = o->escapes;
+  t.repeats = o->repeats;
+  t.derivation = o->derivation || o->paths;
+  t.paths = o->paths;
+  t.bound_escapes = o->bound_escapes;
+  t.committed = o->committed_paths;
+  t.end_after_answer = o->end_after_answer;
+  t.memory_ints = kMemHave + ((l->relation_words + 3) & ~3);
+  e->states.assign(slots, XgState{});
+  e->memory.assign(static_cast<size_t>(slots) * t.memory_ints, 0);
+  e->masks.assign(static_cast<size_t>(slots) * l->words_padded, 0u);
+  e->src.assign(slots, nullptr);
+  e->cursors.assign(slots, -1);
+  e->active.assign(slots, 0);
+  e->top.assign(kTopCap, Key{});
+  e->scratch.assign(kScratchInts + 2, 0);
+  t.states = e->states.data();
+  t.memory = e->memory.data();
+  t.masks = e->masks.data();
+  t.src = e->src.data();
+  t.cursors = e->cursors.data();
+  t.active = e->active.data();
+  for (int32_t s = 0; s < slots; ++s) begin_slot(e, s, 0);
+  return e;
+}
+
+void xgs_destroy(SeamEngine* e) { delete e; }
+
+void xgs_begin(SeamEngine* e, int32_t slot, int32_t on) { begin_slot(e, slot, on); }
+
+void xgs_set_version(SeamEngine* e, int32_t slot, int32_t version) {
+  Ctx c = ctx(e, slot);
+  c.mem[kMemVersion] = version;
+  XgState s = e->states[slot];
+  if (s.phase == kSpan) set_flags(c, s);
+  e->states[slot] = s;
+  build_mask(c, s);
+}
+
+void xgs_set_reached(SeamEngine* e, int32_t slot, const int32_t* rows, int32_t count) {
+  Ctx c = ctx(e, slot);
+  if (count > kMaxSet) count = kMaxSet;
+  for (int32_t i = 0; i < count; ++i) c.mem[kMemReachedRows + i] = rows[i];
+  c.mem[kMemReached] = count;
+  XgState s = e->states[slot];
+  if (s.phase == kSpan) set_flags(c, s);
+  e->states[slot] = s;
+  build_mask(c, s);
+}
+
+void xgs_open_span(SeamEngine* e, int32_t slot) {
+  Ctx c = ctx(e, slot);
+  XgState s = e->states[slot];
+  if (s.phase != kError) {
+    s.answer_complete = 0;
+    open_span(c, s);
+  }
+  e->states[slot] = s;
+  build_mask(c, s);
+}
+
+void xgs_advance(SeamEngine* e, const int32_t* tokens, int32_t count) {
+  for (int32_t slot = 0; slot < count; ++slot) {
+    Ctx c = ctx(e, slot);
+    XgState s = e->states[slot];
+    advance_state(c, s, tokens[slot]);
+    e->states[slot] = s;
+    build_mask(c, s);
+  }
+}
+
+// Masks of slots 0..n-1 as [n, words] (zeros for the error phase).
+void xgs_masks(SeamEngine* e, int32_t n, uint32_t* out) {
+  const int32_t words = e->layout.words;
+  for (int32_t slot = 0; slot < n; ++slot) {
+    const uint32_t* from = e->src[slot];
+    for (int32_t w = 0; w < words; ++w) out[static_cast<int64_t>(slot) * words + w] = from ? from[w] : 0u;
+  }
+}
+
+void xgs_states(SeamEngine* e, int32_t n, int32_t* out) {
+  std::memcpy(out, e->states.data(), static_cast<size_t>(n) * sizeof(XgState));
+}
+
+void xgs_memory(SeamEngine* e, int32_t n, int32_t* out) {
+  std::memcpy(out, e->memory.data(), static_cast<size_t>(n) * e->t.memory_ints * sizeof(int32_t));
+}
+
+int32_t xgs_memory_ints(SeamEngine* e) { return e->t.memory_ints; }
+
+}  // extern "C"

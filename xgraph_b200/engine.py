@@ -1,0 +1,442 @@
+"""The GPU engine: per-slot constraint states, advanced and masked on the device.
+
+Same API and error behaviour as the reference's `xgraph.engine.Engine`
+(src/xgraph/engine.py:559-1069) for the policies it serves: `reset`, `begin`, `end`,
+`anchor`, `set_version`, `open_span`, `advance`, `sync`, `fill_mask`, `mask`,
+`mask_host`, `apply_mask`, `states_host`, `errors`, `view`, `max_sequences`; every
+method takes `stream` (a raw cudaStream_t as int, 0 = default stream).  Underneath, each
+call is one C-ABI function of libxgraph_b200.so (include/xgraph_b200.h) — hand-written
+sm_100a kernels.  There is no fallback: without the built library the constructor
+raises EngineUnavailable.
+
+Tensor arguments are torch tensors (device memory, or pinned host memory where the
+reference accepts it); host token arrays may also be numpy.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from collections.abc import Iterable
+from dataclasses import dataclass
+from pathlib import Path
+
+import numpy as np
+
+from .index import IndexMismatch, check_start_rank
+from .tables import XgLayout, XgOptions, mask_words, pack_mask, pack_tables  # noqa: F401
+
+PHASES = ("free text", "span", "escaped", "error")
+PHASE_ERROR = PHASES.index("error")
+SEGMENTS = ("subject", "relation", "object")
+CLOSED = ("none", "unresolved", "entity span", "fact span", "path span", "comparison", "relation plan")
+MAX_FACTS = 64
+MAX_REACHED = 64
+MAX_DELIMITER_BYTES = 127
+STATE_FIELDS = (
+    "phase", "pos", "segment", "depth", "lo", "hi", "close_pos", "close_lo", "close_hi",
+    "sep_pos", "sep_lo", "sep_hi", "esc_pos", "subj_lo", "subj_hi", "rel_lo", "rel_hi",
+    "subj_key", "hops", "op_pos", "op_kind", "op", "operand", "answer_complete",
+    "last_kind", "last_lo", "last_hi", "last_subj_lo", "last_subj_hi", "last_rel_lo",
+    "last_rel_hi", "ex_hi", "flags",
+)
+"""Names of the leading int32 words of a slot state (XgState in include/xgraph_b200.h)."""
+STATE_INTS = 64
+LIBRARY = Path(__file__).resolve().parent / "libxgraph_b200.so"
+
+XG_OK, XG_EINVAL, XG_ECUDA, XG_ENOMEM = 0, 1, 2, 3
+DTYPES = {"float32": 0, "bfloat16": 1, "float16": 2}
+
+# Reference constructor options this engine does not serve, with their neutral values.
+_NOT_SERVED = {
+    "release_mass": 0.0, "release_top": False, "escape_bias": 0.0, "expressions": False,
+    "stop": None, "relations": "frontier", "observe": 0, "observe_width": 0,
+    "observe_defer": 0, "menu_close_next": False, "observe_select": False,
+    "observe_answer": False, "observe_required": False, "observe_no_loop": False,
+    "audit": False, "audit_entities": 20, "audit_relations": 8, "menu": 0,
+    "relation_labels": None, "observe_terminal": 0, "terminal_order": "identity",
+    "terminal_seed": 17, "request_path_options": False,
+}
+
+
+class EngineUnavailable(RuntimeError):
+    """The CUDA library of the engine was not built (run __graft_entry__.build())."""
+
+
+class _Info(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in ("max_sequences", "vocab", "words", "words_padded", "memory_ints", "device")]
+
+
+_lib = None
+
+
+def load_library(path: Path = LIBRARY):
+    """The engine's C ABI, loaded once; EngineUnavailable if it was never built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not path.is_file():
+        raise EngineUnavailable(f"{path} is missing: build the CUDA engine first (__graft_entry__.build())")
+    lib = ctypes.CDLL(str(path))
+    p, i32, i64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64
+    sigs = {
+        "xg_last_error": ([], ctypes.c_char_p),
+        "xg_abi_version": ([], i32),
+        "xg_create": ([p, ctypes.POINTER(XgLayout), ctypes.POINTER(XgOptions), i32, ctypes.POINTER(p)], ctypes.c_int),
+        "xg_create_from_device": ([p, ctypes.POINTER(XgLayout), ctypes.POINTER(XgOptions), i32, ctypes.POINTER(p)], ctypes.c_int),
+        "xg_destroy": ([p], ctypes.c_int),
+        "xg_info": ([p, ctypes.POINTER(_Info)], ctypes.c_int),
+        "xg_reset": ([p, p], ctypes.c_int),
+        "xg_begin": ([p, p, i32, i32, p], ctypes.c_int),
+        "xg_set_reached": ([p, i32, p, i32, p], ctypes.c_int),
+        "xg_set_version": ([p, i32, i32, p], ctypes.c_int),
+        "xg_open_span": ([p, i32, p], ctypes.c_int),
+        "xg_advance": ([p, p, i32, i32, p], ctypes.c_int),
+        "xg_sync": ([p, p, i32, p, i64, i64, p, p, i64, p], ctypes.c_int),
+        "xg_fill_mask": ([p, i32, p], ctypes.c_int),
+        "xg_mask_device": ([p, ctypes.POINTER(p)], ctypes.c_int),
+        "xg_mask_host": ([p, i32, p], ctypes.c_int),
+        "xg_states_host": ([p, i32, p], ctypes.c_int),
+        "xg_memory_host": ([p, i32, p], ctypes.c_int),
+        "xg_apply_mask": ([p, p, i32, i32, i32, i64, p, p, p, p], ctypes.c_int),
+    }
+    for name, (args, res) in sigs.items():
+        fn = getattr(lib, name)
+        fn.argtypes, fn.restype = args, res
+    if lib.xg_abi_version() != 1:
+        raise EngineUnavailable(f"{path} has ABI {lib.xg_abi_version()}, expected 1")
+    _lib = lib
+    return lib
+
+
+def _check(rc: int) -> None:
+    if rc == XG_OK:
+        return
+    message = _lib.xg_last_error().decode("utf-8", "replace")
+    if rc == XG_EINVAL:
+        raise ValueError(message)
+    if rc == XG_ENOMEM:
+        raise MemoryError(message)
+    raise RuntimeError(message)
+
+
+def _stream(stream) -> ctypes.c_void_p:
+    return ctypes.c_void_p(int(stream) if stream else 0)
+
+
+def _device_ptr(tensor, name: str, *, ndim: int | None = None, dtype=None):
+    import torch
+
+    if not isinstance(tensor, torch.Tensor):
+        raise ValueError(f"{name} must be a torch tensor on the GPU")
+    if ndim is not None and tensor.dim() != ndim:
+        raise ValueError(f"{name} must have {ndim} dimensions")
+    if dtype is not None and tensor.dtype != dtype:
+        raise ValueError(f"{name} must be {dtype}")
+    if not tensor.is_cuda and not tensor.is_pinned():
+        raise ValueError(f"{name} must be on the GPU or in pinned host memory")
+    return ctypes.c_void_p(tensor.data_ptr())
+
+
+class Engine:
+    """Shared KG tables and independent constraint slots resident on the GPU.
+
+    Construction validates the options in the reference's order
+    (src/xgraph/engine.py:817-901), packs the index (tables.pack_tables) and copies it
+    to the current CUDA device with `max_sequences` slots, all inactive."""
+
+    def __init__(
+        self,
+        index,
+        tokenizer,
+        syntax,
+        max_sequences: int,
+        *,
+        escapes: bool = True,
+        repeats: bool = True,
+        derivation: bool = False,
+        paths: bool = False,
+        bound_escapes: bool = True,
+        committed_paths: bool = False,
+        versions=None,
+        start_rank: str = "degree",
+        unquoted_starts: bool = False,
+        end_after_answer: bool = False,
+        eos_token_ids: Iterable[int] = (),
+        device_blob=None,
+        **others,
+    ) -> None:
+        self._lib = load_library()
+        if index.tokenizer_fingerprint != tokenizer.fingerprint:
+            raise IndexMismatch(
+                f"the KG index was built for tokenizer {index.tokenizer_fingerprint[:12]}, "
+                f"not the served tokenizer {tokenizer.fingerprint[:12]}"
+            )
+        if index.span_syntax != syntax:
+            raise IndexMismatch(f"the KG index was built for span syntax {index.span_syntax}, not {syntax}")
+        if not (escapes or repeats):
+            raise ValueError("repeats can only be switched off with escapes, the way out")
+        if committed_paths and not paths:
+            raise ValueError("committed_paths needs path mode (paths=True)")
+        if end_after_answer and not paths:
+            raise ValueError("end_after_answer needs path mode (paths=True)")
+        eos = tokenizer.check_eos_token_ids(eos_token_ids) if end_after_answer else frozenset()
+        for name, value in others.items():
+            if name not in _NOT_SERVED:
+                raise TypeError(f"Engine() got an unexpected keyword argument {name!r}")
+            if value != _NOT_SERVED[name]:
+                raise ValueError(f"the {name} policy is not served by this engine")
+        sitelinks_rank = check_start_rank(start_rank, index) == "sitelinks"
+        if max_sequences < 1:
+            raise ValueError(f"max_sequences must be at least 1, got {max_sequences}")
+        for name in ("opener", "separator", "closer", "escape"):
+            size = len(getattr(syntax, name).encode("utf-8"))
+            if size > MAX_DELIMITER_BYTES:
+                raise ValueError(
+                    f"the span {name} is {size} bytes in UTF-8; the engine supports at most {MAX_DELIMITER_BYTES}"
+                )
+        if versions is not None:
+            versions.check_base(index)
+        self._index, self._versions = index, versions
+        self._entity_index: dict[str, int] | None = None
+        self._tables = pack_tables(
+            index, tokenizer, syntax, escapes=escapes, versions=versions,
+            unquoted_starts=unquoted_starts, eos_token_ids=sorted(eos),
+        ) if device_blob is None else device_blob[1]
+        self._options = XgOptions(
+            escapes=int(escapes), repeats=int(repeats), derivation=int(derivation or paths),
+            paths=int(paths), bound_escapes=int(bound_escapes), committed_paths=int(committed_paths),
+            sitelinks_rank=int(sitelinks_rank), end_after_answer=int(end_after_answer),
+        )
+        handle = ctypes.c_void_p()
+        if device_blob is None:
+            blob = self._tables.blob
+            rc = self._lib.xg_create(
+                blob.ctypes.data_as(ctypes.c_void_p), ctypes.byref(self._tables.layout),
+                ctypes.byref(self._options), int(max_sequences), ctypes.byref(handle))
+        else:
+            rc = self._lib.xg_create_from_device(
+                ctypes.c_void_p(device_blob[0].data_ptr()), ctypes.byref(self._tables.layout),
+                ctypes.byref(self._options), int(max_sequences), ctypes.byref(handle))
+        _check(rc)
+        self._handle = handle
+        info = _Info()
+        _check(self._lib.xg_info(self._handle, ctypes.byref(info)))
+        self._info = info
+        self.vocab_size = info.vocab
+        self.words = info.words
+
+    def __del__(self):
+        handle = getattr(self, "_handle", None)
+        if handle and _lib is not None:
+            _lib.xg_destroy(handle)
+            self._handle = None
+
+    @property
+    def max_sequences(self) -> int:
+        return self._info.max_sequences
+
+    @property
+    def layout(self) -> XgLayout:
+        return self._tables.layout
+
+    def reset(self, stream: int = 0) -> None:
+        _check(self._lib.xg_reset(self._handle, _stream(stream)))
+
+    def _slots(self, slots):
+        import torch
+
+        if not isinstance(slots, torch.Tensor) or not slots.is_cuda or slots.dtype != torch.int32 or slots.dim() != 1:
+            raise ValueError("slots must be a 1-D int32 tensor on the GPU")
+        if len(slots) > self.max_sequences:
+            raise ValueError("more slots than max_sequences")
+        return ctypes.c_void_p(slots.data_ptr()), len(slots)
+
+    def begin(self, slots, stream: int = 0) -> None:
+        ptr, n = self._slots(slots)
+        _check(self._lib.xg_begin(self._handle, ptr, n, 1, _stream(stream)))
+
+    def end(self, slots, stream: int = 0) -> None:
+        ptr, n = self._slots(slots)
+        _check(self._lib.xg_begin(self._handle, ptr, n, 0, _stream(stream)))
+
+    def anchor(self, slot: int, entities: list[str], stream: int = 0) -> None:
+        """Derivation/path mode: bind the slot's spans to these entities' label rows."""
+        labels = self._index.labels
+        if self._entity_index is None:
+            self._entity_index = {e: n for n, e in enumerate(labels.owner_ids)}
+            owners = np.asarray(labels.owners, dtype=np.int64)
+            self._rows_order = np.argsort(owners, kind="stable")
+            self._rows_start = np.zeros(len(labels.owner_ids) + 1, dtype=np.int64)
+            np.cumsum(np.bincount(owners, minlength=len(labels.owner_ids)), out=self._rows_start[1:])
+        found = sorted(
+            int(r)
+            for e in dict.fromkeys(entities)
+            if (n := self._entity_index.get(e)) is not None
+            for r in self._rows_order[self._rows_start[n]: self._rows_start[n + 1]]
+        )
+        if not found:
+            raise ValueError(f"anchor has no writable label rows: {entities!r}")
+        rows = np.ascontiguousarray(found[:MAX_REACHED], dtype=np.int32)
+        _check(self._lib.xg_set_reached(self._handle, int(slot), rows.ctypes.data_as(ctypes.c_void_p),
+                                        len(rows), _stream(stream)))
+
+    def set_version(self, slot: int, version: str | None, stream: int = 0) -> None:
+        if self._versions is not None:
+            number = self._versions.number(version)
+        elif version is not None:
+            raise ValueError(f"no KG version {version!r}; the engine has none registered")
+        else:
+            number = 0
+        _check(self._lib.xg_set_version(self._handle, int(slot), number, _stream(stream)))
+
+    def open_span(self, slot: int, stream: int = 0) -> None:
+        _check(self._lib.xg_open_span(self._handle, int(slot), _stream(stream)))
+
+    def view(self, version: str | None):
+        if version is None:
+            return self._index
+        if self._versions is None:
+            raise ValueError(f"no KG version {version!r}; the engine has none registered")
+        return self._versions.view(self._index, version)
+
+    def advance(self, tokens, stream: int = 0) -> None:
+        """Advance slots 0..len(tokens)-1 by these tokens (1-D int32, on the GPU or host)."""
+        try:
+            import torch
+        except ImportError:  # pragma: no cover
+            torch = None
+        if torch is not None and isinstance(tokens, torch.Tensor):
+            if tokens.dtype != torch.int32 or tokens.dim() != 1:
+                raise ValueError("tokens must be a 1-D int32 array")
+            if tokens.is_cuda:
+                _check(self._lib.xg_advance(self._handle, ctypes.c_void_p(tokens.data_ptr()), len(tokens), 0,
+                                            _stream(stream)))
+                return
+            tokens = tokens.numpy()
+        host = np.ascontiguousarray(tokens, dtype=np.int32)
+        if host.ndim != 1:
+            raise ValueError("tokens must be a 1-D int32 array")
+        _check(self._lib.xg_advance(self._handle, host.ctypes.data_as(ctypes.c_void_p), len(host), 1,
+                                    _stream(stream)))
+
+    def fill_mask(self, sequences: int | None = None, stream: int = 0) -> None:
+        _check(self._lib.xg_fill_mask(self._handle, self._count(sequences), _stream(stream)))
+
+    def sync(self, slots, history, prompt_len, total_len, stream: int = 0) -> None:
+        import torch
+
+        ptr, n = self._slots(slots)
+        for name, lengths in (("prompt_len", prompt_len), ("total_len", total_len)):
+            _device_ptr(lengths, name, ndim=1, dtype=torch.int32)
+            if len(lengths) < self.max_sequences:
+                raise ValueError("prompt_len and total_len need one entry per slot")
+        _device_ptr(history, "history", ndim=2, dtype=torch.int32)
+        if history.shape[0] < self.max_sequences or history.stride(1) != 1:
+            raise ValueError("history needs one contiguous row per slot")
+        _check(self._lib.xg_sync(
+            self._handle, ptr, n, ctypes.c_void_p(history.data_ptr()), history.stride(0), history.shape[0],
+            ctypes.c_void_p(prompt_len.data_ptr()), ctypes.c_void_p(total_len.data_ptr()),
+            min(len(prompt_len), len(total_len)), _stream(stream)))
+
+    def apply_mask(self, logits, row_slots, stream: int = 0, *, local_pos=None, input_ids=None) -> None:
+        """Set every logit its slot's mask disallows (and every column past the served
+        vocabulary) to -inf, in place; rows of inactive slots and error rows are untouched."""
+        import torch
+
+        if (local_pos is None) != (input_ids is None):
+            raise ValueError("local_pos and input_ids go together")
+        if not isinstance(logits, torch.Tensor) or not logits.is_cuda or logits.dim() != 2:
+            raise ValueError("logits must be a 2-D tensor on the GPU")
+        dtype = DTYPES.get(str(logits.dtype).removeprefix("torch."))
+        if dtype is None:
+            raise ValueError("logits must be float32, bfloat16 or float16")
+        ptr, n = self._row_slots(row_slots)
+        if logits.shape[0] != n or (logits.shape[1] > 1 and logits.stride(1) != 1):
+            raise ValueError("logits need one contiguous row per entry of row_slots")
+        drafts = (ctypes.c_void_p(0), ctypes.c_void_p(0))
+        if local_pos is not None:
+            drafts = (self._row_slots(local_pos)[0], self._row_slots(input_ids)[0])
+        _check(self._lib.xg_apply_mask(
+            self._handle, ctypes.c_void_p(logits.data_ptr()), dtype, n, logits.shape[1],
+            logits.stride(0) if n > 1 else logits.shape[1], ptr, drafts[0], drafts[1], _stream(stream)))
+
+    def _row_slots(self, row_slots):
+        import torch
+
+        if (not isinstance(row_slots, torch.Tensor) or not row_slots.is_cuda
+                or row_slots.dtype != torch.int32 or row_slots.dim() != 1):
+            raise ValueError("row_slots must be a 1-D int32 tensor on the GPU")
+        return ctypes.c_void_p(row_slots.data_ptr()), len(row_slots)
+
+    @property
+    def mask(self):
+        """A device copy of the mask buffer, [max_sequences, words] int32."""
+        import torch
+
+        ptr = ctypes.c_void_p()
+        _check(self._lib.xg_mask_device(self._handle, ctypes.byref(ptr)))
+        out = torch.empty((self.max_sequences, self._info.words_padded), dtype=torch.int32, device="cuda")
+        host = self.mask_host()
+        out[:, : self.words] = torch.from_numpy(host.view(np.int32)).to(out.device)
+        return out[:, : self.words]
+
+    def mask_host(self, sequences: int | None = None) -> np.ndarray:
+        n = self._count(sequences)
+        out = np.zeros((n, self.words), dtype=np.uint32)
+        _check(self._lib.xg_mask_host(self._handle, n, out.ctypes.data_as(ctypes.c_void_p)))
+        return out.view(np.int32)
+
+    def states_host(self, sequences: int | None = None) -> dict[str, np.ndarray]:
+        n = self._count(sequences)
+        raw = np.zeros((n, STATE_INTS), dtype=np.int32)
+        _check(self._lib.xg_states_host(self._handle, n, raw.ctypes.data_as(ctypes.c_void_p)))
+        return {name: raw[:, i].copy() for i, name in enumerate(STATE_FIELDS)}
+
+    def memory_host(self, sequences: int | None = None) -> np.ndarray:
+        n = self._count(sequences)
+        out = np.zeros((n, self._info.memory_ints), dtype=np.int32)
+        _check(self._lib.xg_memory_host(self._handle, n, out.ctypes.data_as(ctypes.c_void_p)))
+        return out
+
+    def errors(self, sequences: int | None = None) -> int:
+        return int(np.count_nonzero(self.states_host(sequences)["phase"] == PHASE_ERROR))
+
+    def _count(self, sequences: int | None) -> int:
+        n = self.max_sequences if sequences is None else int(sequences)
+        if not 0 <= n <= self.max_sequences:
+            raise ValueError(f"sequences must be between 0 and max_sequences ({self.max_sequences}), got {n}")
+        return n
+
+
+@dataclass(frozen=True)
+class ClosedSpanRecord:
+    kind: str
+    entity_ids: tuple[str, ...] = ()
+    triples: tuple[tuple[str, str, str], ...] = ()
+    operator: str = ""
+    operands: tuple[str, ...] = ()
+
+    @property
+    def resolved(self) -> bool:
+        return self.kind in ("entity span", "fact span", "path span", "comparison")
+
+
+def closed_span(index, states: dict[str, np.ndarray], seq: int) -> ClosedSpanRecord:
+    """A slot's last closed span as KG ids, from the rows its state records
+    (src/xgraph/engine.py:1091-1136).  For a slot reading a KG version, index is the
+    version's view (Engine.view)."""
+    kind = CLOSED[int(states["last_kind"][seq])]
+    lo, hi = int(states["last_lo"][seq]), int(states["last_hi"][seq])
+    if kind == "entity span":
+        return ClosedSpanRecord(kind, tuple(sorted(index.labels.owner_id(r) for r in range(lo, hi))))
+    if kind != "fact span":
+        return ClosedSpanRecord(kind)
+    subjects = {index.labels.owner_id(r) for r in range(int(states["last_subj_lo"][seq]), int(states["last_subj_hi"][seq]))}
+    relations = {index.relations.owner_id(r) for r in range(int(states["last_rel_lo"][seq]), int(states["last_rel_hi"][seq]))}
+    triples = {
+        (s, r, index.labels.owner_id(row))
+        for s in subjects
+        for r in relations
+        for row in index.object_rows(s, r, lo, hi)
+    }
+    return ClosedSpanRecord(kind, (), tuple(sorted(triples)))
