@@ -151,6 +151,9 @@ XG_API int xg_sync(XgEngine* engine, const int32_t* slots, int32_t count, const 
 XG_API int xg_fill_mask(XgEngine* engine, int32_t sequences, void* stream);
 /* Engine::mask: the device mask buffer, max_sequences rows of words_padded uint32. */
 XG_API int xg_mask_device(XgEngine* engine, uint32_t** out);
+/* The device state array, max_sequences XgState records (read-only for callers; no
+ * reference counterpart beyond states_host, which copies it). */
+XG_API int xg_states_device(XgEngine* engine, XgState** out);
 /* Engine::mask_host / states_host (csrc/engine.cu:3076-3084): wait for the device, then
  * copy sequences x words mask words / sequences x XG_STATE_INTS state words. */
 XG_API int xg_mask_host(XgEngine* engine, int32_t sequences, uint32_t* out);

@@ -134,17 +134,6 @@ __global__ void fill_kernel(const __grid_constant__ Tables t) {
   for (int32_t i = threadIdx.x; i < t.words_padded; i += blockDim.x) own[i] = from ? from[i] : 0u;
 }
 
-template <typename T>
-struct NegInf;
-template <>
-struct NegInf<float> {
-  static constexpr uint32_t bits = 0xff800000u;
-};
-template <>
-struct NegInf<uint16_t> {  // bf16 and fp16 share the store path; the pattern is passed in
-  static constexpr uint32_t bits = 0u;
-};
-
 // Allowed bits of the 8 columns starting at column c (c >= 0): a 64-bit window of words.
 __device__ __forceinline__ uint32_t allowed8(const uint32_t* m, int32_t words, int64_t c) {
   const int64_t w = c >> 5;
@@ -573,6 +562,12 @@ int xg_fill_mask(XgEngine* e, int32_t sequences, void* stream) {
 int xg_mask_device(XgEngine* e, uint32_t** out) {
   if (!e || !out) return fail(XG_EINVAL, "null argument");
   *out = e->masks;
+  return XG_OK;
+}
+
+int xg_states_device(XgEngine* e, XgState** out) {
+  if (!e || !out) return fail(XG_EINVAL, "null argument");
+  *out = e->states;
   return XG_OK;
 }
 

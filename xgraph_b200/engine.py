@@ -94,6 +94,7 @@ def load_library(path: Path = LIBRARY):
         "xg_sync": ([p, p, i32, p, i64, i64, p, p, i64, p], ctypes.c_int),
         "xg_fill_mask": ([p, i32, p], ctypes.c_int),
         "xg_mask_device": ([p, ctypes.POINTER(p)], ctypes.c_int),
+        "xg_states_device": ([p, ctypes.POINTER(p)], ctypes.c_int),
         "xg_mask_host": ([p, i32, p], ctypes.c_int),
         "xg_states_host": ([p, i32, p], ctypes.c_int),
         "xg_memory_host": ([p, i32, p], ctypes.c_int),
@@ -135,6 +136,23 @@ def _device_ptr(tensor, name: str, *, ndim: int | None = None, dtype=None):
     if not tensor.is_cuda and not tensor.is_pinned():
         raise ValueError(f"{name} must be on the GPU or in pinned host memory")
     return ctypes.c_void_p(tensor.data_ptr())
+
+
+class _CudaArray:
+    """__cuda_array_interface__ holder so torch can view engine-owned device memory."""
+
+    def __init__(self, ptr: int, shape, strides, owner) -> None:
+        self.owner = owner  # keeps the engine (and its memory) alive while viewed
+        self.__cuda_array_interface__ = {
+            "shape": tuple(shape), "strides": tuple(strides), "typestr": "<i4",
+            "data": (int(ptr), False), "version": 3,
+        }
+
+
+def _device_view(ptr: int, shape, strides, device: int, owner):
+    import torch
+
+    return torch.as_tensor(_CudaArray(ptr, shape, strides, owner), device=f"cuda:{device}")
 
 
 class Engine:
@@ -370,15 +388,22 @@ class Engine:
 
     @property
     def mask(self):
-        """A device copy of the mask buffer, [max_sequences, words] int32."""
-        import torch
+        """The mask buffer on the GPU, [max_sequences, words] int32 (a zero-copy view;
+        fill_mask writes it)."""
+        return self.mask_view()[:, : self.words]
 
+    def mask_view(self):
+        """Zero-copy torch view of the mask buffer, [max_sequences, words_padded] int32."""
         ptr = ctypes.c_void_p()
         _check(self._lib.xg_mask_device(self._handle, ctypes.byref(ptr)))
-        out = torch.empty((self.max_sequences, self._info.words_padded), dtype=torch.int32, device="cuda")
-        host = self.mask_host()
-        out[:, : self.words] = torch.from_numpy(host.view(np.int32)).to(out.device)
-        return out[:, : self.words]
+        wp = self._info.words_padded
+        return _device_view(ptr.value, (self.max_sequences, wp), (wp * 4, 4), self._info.device, self)
+
+    def states_view(self):
+        """Zero-copy torch view of the device states, [max_sequences, 64] int32 (read-only use)."""
+        ptr = ctypes.c_void_p()
+        _check(self._lib.xg_states_device(self._handle, ctypes.byref(ptr)))
+        return _device_view(ptr.value, (self.max_sequences, STATE_INTS), (STATE_INTS * 4, 4), self._info.device, self)
 
     def mask_host(self, sequences: int | None = None) -> np.ndarray:
         n = self._count(sequences)

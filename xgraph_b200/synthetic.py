@@ -1,0 +1,270 @@
+"""Seeded synthetic workloads: KGs, served tokenizers and constrained token streams.
+
+No public dataset is involved.  The generator is the one the measurement plan fixes:
+entity labels are 1-3 capitalised words of 2-4 syllables from a fixed syllable list
+(homonyms included on purpose), relation labels are distinct lowercase words, triples
+are uniform (or, for the path-mode config, with Zipf out-degrees), and the served
+tokenizer is a byte-level BPE trained by the `tokenizers` library on the label corpus
+plus seeded prose, padded with non-special added tokens to the exact vocabulary size.
+
+Token streams are constrained decodes: `sample_streams` runs the engine itself as the
+sampler's constraint, one step at a time on the GPU, choosing for every row a token its
+mask allows, biased toward whole spans (open, take separators and closers, escape now
+and then) the way the reference's agreement harness walks the oracle
+(tests/test_engine.py:1903-1960).  Every token is therefore allowed by construction.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import numpy as np
+
+CONSONANTS = "bcdfghjklmnprstvz"
+VOWELS = "aeiou"
+SYLLABLES = [c + v for c in CONSONANTS for v in VOWELS] + ["an", "el", "or", "ul", "is", "en", "ay", "oo"]
+
+
+def _words(rng: np.random.Generator, n: int, syllables=(2, 4), capital=True) -> np.ndarray:
+    counts = rng.integers(syllables[0], syllables[1] + 1, size=n)
+    picks = rng.integers(0, len(SYLLABLES), size=int(counts.sum()))
+    table = np.array(SYLLABLES, dtype=object)
+    parts = table[picks]
+    out = np.empty(n, dtype=object)
+    at = 0
+    for i, c in enumerate(counts.tolist()):
+        w = "".join(parts[at: at + c])
+        out[i] = w.capitalize() if capital else w
+        at += c
+    return out
+
+
+def _labels(rng: np.random.Generator, n: int, words=(1, 3)) -> list[str]:
+    counts = rng.integers(words[0], words[1] + 1, size=n)
+    pool = _words(rng, int(counts.sum()))
+    out, at = [], 0
+    for c in counts.tolist():
+        out.append(" ".join(pool[at: at + c]))
+        at += c
+    return out
+
+
+@dataclass
+class World:
+    entities: list[tuple[str, list[str]]]
+    relations: list[tuple[str, list[str]]]
+    triples: np.ndarray  # int64 (n, 3) positions
+    sitelinks: np.ndarray
+    prose: list[str] = field(default_factory=list)
+
+
+def synthetic_world(seed: int, entities: int, relations: int, triples: int, *, labels=(1, 1),
+                    homonyms: float = 0.03, zipf: float | None = None) -> World:
+    rng = np.random.default_rng(seed)
+    label_counts = rng.integers(labels[0], labels[1] + 1, size=entities)
+    pool = _labels(rng, int(label_counts.sum()))
+    # homonyms: reuse an earlier label for a share of the labels
+    reuse = rng.random(len(pool)) < homonyms
+    sources = rng.integers(0, np.maximum(np.arange(len(pool)), 1))
+    for i in np.flatnonzero(reuse).tolist():
+        if i > 0:
+            pool[i] = pool[int(sources[i])]
+    ents, at = [], 0
+    for n, c in enumerate(label_counts.tolist()):
+        ents.append((f"Q{n}", list(dict.fromkeys(pool[at: at + c]))))
+        at += c
+    names: list[str] = []
+    seen: set[str] = set()
+    while len(names) < relations:
+        for w in _words(rng, relations, syllables=(2, 3), capital=False).tolist():
+            if w not in seen and len(names) < relations:
+                seen.add(w)
+                names.append(w)
+    rels = [(f"P{n}", [w]) for n, w in enumerate(names)]
+    if zipf is None:
+        subjects = rng.integers(0, entities, size=triples)
+    else:
+        weights = 1.0 / np.arange(1, entities + 1) ** zipf
+        order = rng.permutation(entities)
+        subjects = order[rng.choice(entities, size=triples, p=weights / weights.sum())]
+    trip = np.stack([subjects, rng.integers(0, relations, size=triples), rng.integers(0, entities, size=triples)], axis=1)
+    sitelinks = rng.integers(0, 50, size=entities)
+    prose = [" ".join(_words(rng, 10, syllables=(1, 3), capital=False).tolist()) for _ in range(2000)]
+    return World(ents, rels, trip.astype(np.int64), sitelinks, prose)
+
+
+def synthetic_tokenizer(world: World, vocab_size: int, syntax, seed: int = 0):
+    """A byte-level BPE with exactly vocab_size ids (special <|endoftext|> included):
+    the 256 byte tokens alone when vocab_size <= 257, else trained on the labels, the
+    prose and the span delimiters, then padded with non-special added tokens."""
+    from tokenizers import Tokenizer, decoders, models, pre_tokenizers, trainers
+
+    from .tokenizer import ServedTokenizer
+
+    alphabet = sorted(pre_tokenizers.ByteLevel.alphabet())
+    if vocab_size <= 257:
+        tok = Tokenizer(models.BPE({c: i for i, c in enumerate(alphabet)}, []))
+        tok.pre_tokenizer = pre_tokenizers.ByteLevel(add_prefix_space=False)
+        tok.decoder = decoders.ByteLevel()
+        if vocab_size == 257:
+            tok.add_special_tokens(["<|endoftext|>"])
+        return ServedTokenizer(tok)
+    corpus = [syntax.label_prefix + label for _, labels in world.entities + world.relations for label in labels]
+    corpus += world.prose
+    spans = [syntax.opener + syntax.label_prefix + "x" + syntax.separator + syntax.label_prefix + "y" + syntax.closer,
+             syntax.opener + syntax.escape + " x" + syntax.closer]
+    corpus += spans * 200
+    tok = Tokenizer(models.BPE())
+    tok.pre_tokenizer = pre_tokenizers.ByteLevel(add_prefix_space=False)
+    tok.decoder = decoders.ByteLevel()
+    trainer = trainers.BpeTrainer(vocab_size=vocab_size, special_tokens=["<|endoftext|>"],
+                                  initial_alphabet=pre_tokenizers.ByteLevel.alphabet(), show_progress=False)
+    tok.train_from_iterator(corpus, trainer=trainer)
+    short = vocab_size - tok.get_vocab_size(with_added_tokens=True)
+    if short > 0:
+        tok.add_tokens([f"<pad_{k}>" for k in range(short)])
+    served = ServedTokenizer(tok)
+    if served.vocab_size != vocab_size:
+        raise RuntimeError(f"tokenizer has {served.vocab_size} ids, wanted {vocab_size}")
+    return served
+
+
+@dataclass(frozen=True)
+class Config:
+    name: str
+    entities: int
+    relations: int
+    triples: int
+    vocab: int
+    rows: int
+    lengths: tuple[int, int]
+    labels: tuple[int, int] = (1, 1)
+    zipf: float | None = None
+    options: dict = field(default_factory=dict)
+    dtype: str = "bfloat16"
+
+
+CONFIGS = {
+    1: Config("toy-1k", 1_000, 20, 5_000, 256, 16, (64, 64), dtype="float32"),
+    2: Config("ordinary-20k", 20_000, 50, 100_000, 32_000, 64, (256, 256), dtype="float32"),
+    3: Config("paths-100k", 100_000, 100, 1_000_000, 128_256, 256, (64, 1024), labels=(1, 3),
+              options={"paths": True, "committed_paths": True}),
+    4: Config("paths-1m-zipf", 1_000_000, 200, 10_000_000, 128_256, 512, (64, 1024), zipf=1.1,
+              options={"paths": True, "committed_paths": True}),
+}
+
+
+@dataclass
+class Workload:
+    config: Config
+    world: World
+    served: object
+    syntax: object
+    index: object
+
+
+def build_workload(number: int, seed: int | None = None) -> Workload:
+    from .index import build_kg_index_arrays
+    from .syntax import SpanSyntax
+
+    config = CONFIGS[number]
+    syntax = SpanSyntax()
+    world = synthetic_world(number if seed is None else seed, config.entities, config.relations, config.triples,
+                            labels=config.labels, zipf=config.zipf)
+    served = synthetic_tokenizer(world, config.vocab, syntax)
+    index = build_kg_index_arrays(world.entities, world.relations, world.triples, served, syntax,
+                                  sitelinks=world.sitelinks)
+    return Workload(config, world, served, syntax, index)
+
+
+# ---------------------------------------------------------------------------------------
+# Constrained stream sampling on the GPU.
+
+def _delimiter_like(served, syntax) -> np.ndarray:
+    delims = [d.encode("utf-8") for d in (syntax.closer, syntax.separator, syntax.escape)]
+    out = np.zeros(served.vocab_size, dtype=bool)
+    for t in range(served.vocab_size):
+        b = served.token_bytes(t)
+        if b and any(d.find(b) >= 0 for d in delims):
+            out[t] = True
+    return out
+
+
+def _prose_tokens(served, world: World) -> np.ndarray:
+    out = np.zeros(served.vocab_size, dtype=bool)
+    for line in world.prose[:400]:
+        out[served.encode(" " + line)] = True
+    return out
+
+
+def sample_streams(engine, served, syntax, world: World, rows: int, steps: int, seed: int,
+                   *, p_open=0.25, p_sep=0.5, p_close=0.8, p_escape=0.05, p_unescape=0.3, record=None):
+    """Constrained random walks of `rows` slots for `steps` tokens, decoded on the GPU with
+    the engine as the constraint.  Returns (tokens [rows, steps] int32 on the GPU, allowed
+    counts [rows, steps + 1] int32: how many ids each step's mask allowed).  `record`
+    (optional set of (row, step)) collects those masks on the host for parity checks."""
+    import torch
+
+    device = torch.device("cuda")
+    gen = torch.Generator(device=device).manual_seed(seed)
+    vocab, words = served.vocab_size, engine.words
+    queues = [served.encode(" " + syntax.opener), served.encode(syntax.separator),
+              served.encode(syntax.closer), served.encode(syntax.escape)]
+    qlen = torch.tensor([len(q) for q in queues], device=device)
+    qtok = torch.zeros((4, max(len(q) for q in queues)), dtype=torch.long, device=device)
+    for k, q in enumerate(queues):
+        qtok[k, : len(q)] = torch.tensor(q)
+    special = torch.zeros(vocab, dtype=torch.bool, device=device)
+    special[list(served.special_ids)] = True
+    label_like = ~torch.from_numpy(_delimiter_like(served, syntax)).to(device) & ~special
+    prose = torch.from_numpy(_prose_tokens(served, world)).to(device)
+    engine.reset()
+    slots = torch.arange(rows, dtype=torch.int32, device=device)
+    engine.begin(slots)
+    kind = torch.full((rows,), -1, dtype=torch.long, device=device)
+    pos = torch.zeros(rows, dtype=torch.long, device=device)
+    tokens = torch.zeros((rows, steps), dtype=torch.int32, device=device)
+    counts = torch.zeros((rows, steps + 1), dtype=torch.int32, device=device)
+    shifts = torch.arange(32, device=device, dtype=torch.int32)
+    masks = engine.mask_view()
+    states = engine.states_view()
+    recorded = {}
+    for step in range(steps + 1):
+        engine.fill_mask(rows)
+        bits = ((masks[:rows].unsqueeze(-1) >> shifts) & 1).bool().reshape(rows, -1)[:, :vocab]
+        counts[:, step] = bits.sum(1, dtype=torch.int32)
+        if record:
+            for r, s in record:
+                if s == step:
+                    recorded[(r, s)] = masks[r, :words].clone()
+        if step == steps:
+            break
+        phase = states[:rows, 0].long()
+        u = torch.rand((rows, 3), generator=gen, device=device)
+        idle = kind < 0
+        can_sep = bits[:, queues[1][0]]
+        can_close = bits[:, queues[2][0]]
+        start = torch.full_like(kind, -1)
+        start = torch.where(idle & (phase == 0) & (u[:, 0] < p_open), 0, start)
+        span = idle & (phase == 1)
+        start = torch.where(span & can_sep & (u[:, 0] < p_sep), 1, start)
+        start = torch.where(span & (start < 0) & can_close & (u[:, 1] < p_close), 2, start)
+        start = torch.where(span & (start < 0) & (u[:, 2] < p_escape), 3, start)
+        start = torch.where(idle & (phase == 2) & (u[:, 0] < p_unescape), 2, start)
+        kind = torch.where(start >= 0, start, kind)
+        pos = torch.where(start >= 0, 0, pos)
+        queued = qtok[kind.clamp(min=0), pos]
+        take = (kind >= 0) & bits.gather(1, queued.unsqueeze(1)).squeeze(1)
+        prefer = torch.where((phase == 1).unsqueeze(1), label_like.unsqueeze(0), prose.unsqueeze(0)) & bits
+        prefer = torch.where(prefer.any(1, keepdim=True), prefer, bits & ~special.unsqueeze(0))
+        prefer = torch.where(prefer.any(1, keepdim=True), prefer, bits)
+        noise = torch.rand((rows, vocab), generator=gen, device=device)
+        drawn = torch.where(prefer, noise, -1.0).argmax(1)
+        choice = torch.where(take, queued, drawn)
+        pos = torch.where(take, pos + 1, 0)
+        kind = torch.where(take & (pos < qlen[kind.clamp(min=0)]), kind, -1)
+        tokens[:, step] = choice.int()
+        engine.advance(choice.int())
+    if engine.errors(rows):
+        raise RuntimeError("a sampled stream left the mask")
+    return tokens, counts, {k: v.cpu().numpy().view(np.uint32) for k, v in recorded.items()}
