@@ -268,7 +268,7 @@ def engine_arm(args) -> None:
     lengths = rng.integers(lo, hi + 1, size=pool).tolist()
     record = set()
     if rank == 0 and world == 1 and not args.no_cpu and not args.profile:
-        for row in range(0, 48):
+        for row in range(min(48, pool)):
             for s in sorted(set(rng.integers(0, lengths[row], size=4).tolist())):
                 record.add((row, int(s)))
     t0 = time.perf_counter()

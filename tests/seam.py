@@ -96,3 +96,39 @@ class SeamEngine:
 
     def view(self, version):
         return self.index if version is None else self.versions.view(self.index, version)
+
+    # Engine-shaped surface used by xgraph_b200.synthetic.sample_streams (device="cpu").
+    @property
+    def words(self):
+        return self.tables.words
+
+    def reset(self):
+        for slot in range(self.slots):
+            self.lib.xgs_begin(self.handle, slot, 0)
+
+    def fill_mask(self, n=None):
+        import torch
+
+        self._mask[:] = torch.from_numpy(self.masks().view(np.int32))
+        raw = np.zeros((self.slots, 64), dtype=np.int32)
+        self.lib.xgs_states(self.handle, self.slots, raw.ctypes.data_as(ctypes.c_void_p))
+        self._states[:] = torch.from_numpy(raw)
+
+    def mask_view(self):
+        import torch
+
+        if not hasattr(self, "_mask"):
+            self._mask = torch.zeros((self.slots, self.tables.words), dtype=torch.int32)
+            self._states = torch.zeros((self.slots, 64), dtype=torch.int32)
+        return self._mask
+
+    def states_view(self):
+        self.mask_view()
+        return self._states
+
+    def begin_all(self, slots):
+        for slot in slots.tolist():
+            self.begin(int(slot))
+
+    def errors(self, n=None):
+        return int((self.states()["phase"][: n or self.slots] == 3).sum())

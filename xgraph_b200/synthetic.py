@@ -198,14 +198,15 @@ def _prose_tokens(served, world: World) -> np.ndarray:
 
 
 def sample_streams(engine, served, syntax, world: World, rows: int, steps: int, seed: int,
-                   *, p_open=0.25, p_sep=0.5, p_close=0.8, p_escape=0.05, p_unescape=0.3, record=None):
+                   *, p_open=0.25, p_sep=0.5, p_close=0.8, p_escape=0.05, p_unescape=0.3, record=None,
+                   device: str = "cuda"):
     """Constrained random walks of `rows` slots for `steps` tokens, decoded on the GPU with
     the engine as the constraint.  Returns (tokens [rows, steps] int32 on the GPU, allowed
     counts [rows, steps + 1] int32: how many ids each step's mask allowed).  `record`
     (optional set of (row, step)) collects those masks on the host for parity checks."""
     import torch
 
-    device = torch.device("cuda")
+    device = torch.device(device)
     gen = torch.Generator(device=device).manual_seed(seed)
     vocab, words = served.vocab_size, engine.words
     queues = [served.encode(" " + syntax.opener), served.encode(syntax.separator),
@@ -263,6 +264,7 @@ def sample_streams(engine, served, syntax, world: World, rows: int, steps: int, 
         choice = torch.where(take, queued, drawn)
         pos = torch.where(take, pos + 1, 0)
         kind = torch.where(take & (pos < qlen[kind.clamp(min=0)]), kind, -1)
+        pos = torch.where(kind < 0, 0, pos)  # a finished or abandoned queue restarts at 0
         tokens[:, step] = choice.int()
         engine.advance(choice.int())
     if engine.errors(rows):
