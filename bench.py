@@ -59,6 +59,7 @@ def parse_args():
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     p.add_argument("--e2e-steps", type=int, default=32)
     p.add_argument("--profile", action="store_true", help="short run for a profiler (no CPU leg, no e2e)")
+    p.add_argument("--max-len", type=int, default=0, help="cap stream lengths (profiling runs)")
     return p.parse_args()
 
 
@@ -263,6 +264,8 @@ def engine_arm(args) -> None:
     pool = 2 * rows
     gen_engine = Engine(workload.index, workload.served, workload.syntax, pool, device_blob=(blob, meta), **options)
     lo, hi = cfg.lengths
+    if args.max_len:
+        lo, hi = min(lo, args.max_len), min(hi, args.max_len)
     max_len = hi
     rng = np.random.default_rng(args.seed + 100 + rank)
     lengths = rng.integers(lo, hi + 1, size=pool).tolist()
@@ -315,6 +318,7 @@ def engine_arm(args) -> None:
                 dist.barrier()
             clocks = Clocks(local)
             time.sleep(0.3)
+            torch.cuda.nvtx.range_push("timed")
         flush.fill_(k)  # evict the logits and tables from L2 between steps
         e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
         e0.record()
@@ -330,6 +334,8 @@ def engine_arm(args) -> None:
             step_ms.append((e0, e2))
             apply_ms.append((e1, e2))
     torch.cuda.synchronize()
+    if clocks is not None:
+        torch.cuda.nvtx.range_pop()
     clock_info = clocks.stop() if clocks else None
     errors = engine.errors()
     steps_ms = [a.elapsed_time(b) for a, b in step_ms]
