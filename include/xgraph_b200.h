@@ -80,8 +80,11 @@ typedef struct XgLayout {
   int32_t entity_rows, relation_rows, entities, relations, relation_words;
   int32_t opener_len, closer_len, separator_len, escape_len;
   int32_t versions, wide_count;
-  int32_t pad0;
+  int32_t ent_cols, rel_cols;  /* depths stored column-major in ent_col / rel_col */
+  int32_t pad0, pad1;
   int64_t ent_tok, ent_off, ent_owner, rel_tok, rel_off, rel_owner;
+  int64_t ent_col, rel_col;      /* int32 [cols][rows]: token at depth d of each row, -1 past its end */
+  int64_t ent_first, rel_first;  /* int32 [vocab + 1]: first row whose first token is >= t */
   int64_t ent_first_row, ent_rows_off, ent_rows;
   int64_t adj_off, edge_rel, edge_obj;
   int64_t sitelinks, kept_prefix;

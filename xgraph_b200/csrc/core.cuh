@@ -68,6 +68,9 @@ struct Rows {
   const int32_t* off;
   const int32_t* owner;
   int32_t count;
+  const int32_t* col;    // [cols][count]: token at depth d, -1 past the row's end
+  const int32_t* first;  // [vocab + 1]: first row whose first token is >= t
+  int32_t cols;
 };
 
 struct Delim {
@@ -110,8 +113,12 @@ struct Tables {
   XgState* states;
   int32_t* memory;
   int32_t memory_ints;
-  uint32_t* masks;           // [slots, words_padded]
-  const uint32_t** src;      // where each slot's current mask lives (null: error)
+  uint32_t* masks;           // [slots, words_padded]: each slot's own mask bits
+  // A slot's mask is base | delta: base a precomputed table row (free text, escaped span,
+  // EOS only, root or wide label mask), delta the slot's own buffer row.  Both null: the
+  // error phase (apply_mask leaves the row alone).
+  const uint32_t** base;
+  uint32_t** delta;
   int32_t* cursors;
   int32_t* active;
 };
@@ -206,13 +213,17 @@ struct TopSet {
   int32_t n;
 };
 
+// Sorts buf[0, n) ascending; entries from n to the sorted width are set to max_key().
 XG_HD void top_sort(const Warp& w, Key* buf, int32_t n) {
 #if XG_GPU
-  for (int32_t i = n + w.lane; i < kTopCap; i += 32) buf[i] = max_key();
+  int32_t width = 32;
+  while (width < n) width <<= 1;
+  for (int32_t i = n + w.lane; i < width; i += 32) buf[i] = max_key();
+  for (int32_t i = width + w.lane; i < kTopCap; i += 32) buf[i] = max_key();
   __syncwarp();
-  for (int32_t k = 2; k <= kTopCap; k <<= 1) {
+  for (int32_t k = 2; k <= width; k <<= 1) {
     for (int32_t j = k >> 1; j > 0; j >>= 1) {
-      for (int32_t i = w.lane; i < kTopCap; i += 32) {
+      for (int32_t i = w.lane; i < width; i += 32) {
         const int32_t l = i ^ j;
         if (l > i) {
           const Key x = buf[i], y = buf[l];
@@ -233,14 +244,14 @@ XG_HD void top_sort(const Warp& w, Key* buf, int32_t n) {
 #endif
 }
 
-// Sorted buffer -> its first `limit` entries that are distinct (by full key, or by the
-// high 32 bits of a when by_high); returns how many were kept.
-XG_HD int32_t top_unique(const Warp& w, Key* buf, int32_t limit, bool by_high) {
+// Sorted buf[0, n) -> its first `limit` entries that are distinct (by full key, or by
+// the high 32 bits of a when by_high); returns how many were kept.
+XG_HD int32_t top_unique(const Warp& w, Key* buf, int32_t n, int32_t limit, bool by_high) {
 #if XG_GPU
   int32_t out = 0;
   Key carry = max_key();
-  for (int32_t base = 0; base < kTopCap && out < limit; base += 32) {
-    const Key k = buf[base + w.lane];
+  for (int32_t base = 0; base < n && out < limit; base += 32) {
+    const Key k = base + w.lane < n ? buf[base + w.lane] : max_key();
     Key prev;
     prev.a = __shfl_up_sync(0xffffffffu, k.a, 1);
     prev.b = __shfl_up_sync(0xffffffffu, k.b, 1);
@@ -262,7 +273,7 @@ XG_HD int32_t top_unique(const Warp& w, Key* buf, int32_t limit, bool by_high) {
 #else
   (void)w;
   int32_t out = 0;
-  for (int32_t i = 0; i < kTopCap && out < limit; ++i) {
+  for (int32_t i = 0; i < n && out < limit; ++i) {
     const Key k = buf[i];
     if (is_max(k)) break;
     if (out > 0) {
@@ -283,7 +294,7 @@ XG_HD void top_compact(const Warp& w, TopSet& ts, int32_t mode) {
       ts.buf[i].a = (a << 32) | (a >> 32);
     });
     top_sort(w, ts.buf, ts.n);
-    int32_t n = top_unique(w, ts.buf, kTopCap, true);
+    int32_t n = top_unique(w, ts.buf, ts.n, kTopCap, true);
     warp_for(w, 0, n, [&](int32_t i) {
       const uint64_t a = ts.buf[i].a;
       ts.buf[i].a = (a << 32) | (a >> 32);
@@ -292,7 +303,7 @@ XG_HD void top_compact(const Warp& w, TopSet& ts, int32_t mode) {
     ts.n = n < kMaxSet ? n : kMaxSet;
   } else {
     top_sort(w, ts.buf, ts.n);
-    ts.n = top_unique(w, ts.buf, kMaxSet, false);
+    ts.n = top_unique(w, ts.buf, ts.n, kMaxSet, false);
   }
   warp_sync();
 }
@@ -319,23 +330,65 @@ XG_HD void top_push(const Warp& w, TopSet& ts, bool valid, const Key& k, int32_t
 
 XG_HD int32_t row_len(const Rows& r, int32_t row) { return r.off[row + 1] - r.off[row]; }
 
-// Token of a row at a depth, or -1 past its end (so a row that ends sorts first).
+// Token of a row at a depth, or -1 past its end (so a row that ends sorts first): one
+// read of the column table for the first `cols` depths.
 XG_HD int32_t column(const Rows& r, int32_t row, int32_t depth) {
+  if (depth < r.cols) return r.col[static_cast<int64_t>(depth) * r.count + row];
   const int32_t a = r.off[row];
   return depth < r.off[row + 1] - a ? r.tok[a + depth] : -1;
 }
 
-// First row in [lo, hi) whose column at depth is >= token (upper: > token).
-XG_HD int32_t bound_row(const Rows& r, int32_t lo, int32_t hi, int32_t depth, int32_t token, bool upper) {
+// The first i in [lo, hi) where pred(i) holds, for a predicate that is false then true
+// along the range (hi when it never holds).  On the GPU the warp probes 32 evenly spaced
+// rows per round (a 32-ary search: log32 rounds of one parallel load each instead of
+// log2 rounds of dependent loads).  lo and hi must be warp-uniform.
+template <class P>
+XG_HD int32_t warp_partition(const Warp& w, int32_t lo, int32_t hi, P pred) {
+#if XG_GPU
+  while (hi - lo > 32) {
+    const int32_t step = (hi - lo + 31) >> 5;
+    const int32_t probe = lo + (w.lane + 1) * step - 1;  // the last row of bucket `lane`
+    const uint32_t m = __ballot_sync(0xffffffffu, probe >= hi || pred(probe));
+    if (m == 0u) return hi;
+    const int32_t k = __ffs(m) - 1;  // the first bucket whose last row satisfies pred
+    lo += k * step;
+    hi = lo + step < hi ? lo + step : hi;
+  }
+  const int32_t i = lo + w.lane;
+  const uint32_t m = __ballot_sync(0xffffffffu, i >= hi || pred(i));
+  return m == 0u ? hi : lo + __ffs(m) - 1;
+#else
+  (void)w;
   while (lo < hi) {
     const int32_t mid = lo + ((hi - lo) >> 1);
-    const int32_t c = column(r, mid, depth);
-    if (upper ? c <= token : c < token)
-      lo = mid + 1;
-    else
+    if (pred(mid))
       hi = mid;
+    else
+      lo = mid + 1;
   }
   return lo;
+#endif
+}
+
+// First row in [lo, hi) whose column at depth is >= token (upper: > token).
+XG_HD int32_t bound_row(const Warp& w, const Rows& r, int32_t lo, int32_t hi, int32_t depth, int32_t token,
+                        bool upper) {
+  return warp_partition(w, lo, hi, [&](int32_t row) {
+    const int32_t c = column(r, row, depth);
+    return upper ? c > token : c >= token;
+  });
+}
+
+// The rows of [lo, hi) whose column at depth equals token (the typed label extended by it).
+XG_HD void narrow(const Warp& w, const Rows& r, int32_t& lo, int32_t& hi, int32_t depth, int32_t token) {
+  if (depth == 0 && lo == 0 && hi == r.count) {  // the whole index: one table read
+    lo = r.first[token];
+    hi = r.first[token + 1];
+    return;
+  }
+  const int32_t a = bound_row(w, r, lo, hi, depth, token, false);
+  hi = bound_row(w, r, a, hi, depth, token, true);
+  lo = a;
 }
 
 template <class T>
@@ -640,7 +693,7 @@ XG_HD void set_flags(const Ctx& c, XgState& s) {
     return;
   }
   const Rows& rows = s.segment == kRelation ? t.rel : t.ent;
-  s.ex_hi = s.depth == 0 ? s.lo : bound_row(rows, s.lo, s.hi, s.depth, 0, false);
+  s.ex_hi = s.depth == 0 ? s.lo : bound_row(c.w, rows, s.lo, s.hi, s.depth, 0, false);
   const bool bound = s.segment == kSubject && !unbound(t, c, s);
   if (has_candidate(c, s, s.lo, s.ex_hi)) {
     bool closes = s.segment != kRelation || t.paths;
@@ -896,8 +949,9 @@ XG_HD void advance_span(const Ctx& c, XgState& s, int32_t token) {
   int32_t lo = -1, hi = -1;
   if (s.lo >= 0) {
     const Rows& rows = s.segment == kRelation ? t.rel : t.ent;
-    lo = bound_row(rows, s.lo, s.hi, s.depth, token, false);
-    hi = bound_row(rows, lo, s.hi, s.depth, token, true);
+    lo = s.lo;
+    hi = s.hi;
+    narrow(c.w, rows, lo, hi, s.depth, token);
     if (!has_candidate(c, s, lo, hi)) lo = hi = -1;
   }
   if (close == t.closer.len) {
@@ -1035,60 +1089,57 @@ XG_HD void add_label_tokens(const Ctx& c, const XgState& s, uint32_t* out) {
   }
 }
 
-// Point src[slot] at the slot's mask: a precomputed table row outside spans, the slot's
-// own buffer (built here) inside one, none in the error phase.
+// Record the slot's mask for its current state: outside a span a precomputed table row
+// (base only); inside one the root or wide mask of an unbound label range as base (no
+// copy), and the slot's own buffer row (zeroed, then the label and delimiter tokens) as
+// delta; in the error phase neither.
 XG_HD void build_mask(const Ctx& c, const XgState& s) {
   const Tables& t = c.t;
   const int64_t stride = t.words_padded;
-  if (s.phase == kError) {
-    if (c.w.leader()) t.src[c.slot] = nullptr;
-    return;
-  }
-  if (s.phase == kFree) {
-    if (c.w.leader()) t.src[c.slot] = s.answer_complete ? t.eos_mask : t.free_mask + s.pos * stride;
-    return;
-  }
-  if (s.phase == kEscaped) {
-    if (c.w.leader()) t.src[c.slot] = t.esc_mask + s.pos * stride;
-    return;
-  }
-  uint32_t* out = t.masks + c.slot * stride;
   const uint32_t* base = nullptr;
-  bool scan = s.lo >= 0;
-  if (scan && unbound(t, c, s)) {
-    if (s.depth == 0 && s.lo == 0 && s.hi == t.ent.count) {
-      base = t.root_mask;
-      scan = false;
-    } else if ((base = wide_mask(t, s.lo, s.depth)) != nullptr) {
-      scan = false;
+  uint32_t* delta = nullptr;
+  if (s.phase == kFree) {
+    base = s.answer_complete ? t.eos_mask : t.free_mask + s.pos * stride;
+  } else if (s.phase == kEscaped) {
+    base = t.esc_mask + s.pos * stride;
+  } else if (s.phase == kSpan) {
+    delta = t.masks + c.slot * stride;
+    bool scan = s.lo >= 0;
+    if (scan && unbound(t, c, s)) {
+      if (s.depth == 0 && s.lo == 0 && s.hi == t.ent.count) {
+        base = t.root_mask;
+        scan = false;
+      } else if ((base = wide_mask(t, s.lo, s.depth)) != nullptr) {
+        scan = false;
+      }
     }
-  }
 #if XG_GPU
-  {
-    const uint4* from = reinterpret_cast<const uint4*>(base);
-    uint4* to = reinterpret_cast<uint4*>(out);
+    uint4* to = reinterpret_cast<uint4*>(delta);
     const int32_t quads = t.words_padded >> 2;
-    for (int32_t i = c.w.lane; i < quads; i += 32) to[i] = base ? from[i] : make_uint4(0u, 0u, 0u, 0u);
+    for (int32_t i = c.w.lane; i < quads; i += 32) to[i] = make_uint4(0u, 0u, 0u, 0u);
     __syncwarp();
-  }
 #else
-  for (int32_t i = 0; i < t.words_padded; ++i) out[i] = base ? base[i] : 0u;
+    for (int32_t i = 0; i < t.words_padded; ++i) delta[i] = 0u;
 #endif
-  if (scan) add_label_tokens(c, s, out);
-  if (s.close_pos > 0)
-    add_delimiter(c.w, t.closer, s.close_pos, out);
-  else if (s.flags & kMayClose)
-    add_delimiter(c.w, t.closer, 0, out);
-  if (s.sep_pos > 0)
-    add_delimiter(c.w, t.separator, s.sep_pos, out);
-  else if (s.flags & kMaySep)
-    add_delimiter(c.w, t.separator, 0, out);
-  if (s.esc_pos > 0)
-    add_delimiter(c.w, t.escape, s.esc_pos, out);
-  else if (s.flags & kMayEsc)
-    add_delimiter(c.w, t.escape, 0, out);
-  warp_sync();
-  if (c.w.leader()) t.src[c.slot] = out;
+    if (scan) add_label_tokens(c, s, delta);
+    if (s.close_pos > 0)
+      add_delimiter(c.w, t.closer, s.close_pos, delta);
+    else if (s.flags & kMayClose)
+      add_delimiter(c.w, t.closer, 0, delta);
+    if (s.sep_pos > 0)
+      add_delimiter(c.w, t.separator, s.sep_pos, delta);
+    else if (s.flags & kMaySep)
+      add_delimiter(c.w, t.separator, 0, delta);
+    if (s.esc_pos > 0)
+      add_delimiter(c.w, t.escape, s.esc_pos, delta);
+    else if (s.flags & kMayEsc)
+      add_delimiter(c.w, t.escape, 0, delta);
+    warp_sync();
+  }
+  if (c.w.leader()) {
+    t.base[c.slot] = base;
+    t.delta[c.slot] = delta;
+  }
 }
 
 }  // namespace xg

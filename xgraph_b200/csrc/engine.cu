@@ -20,7 +20,7 @@
 
 namespace xg {
 
-constexpr int32_t kWarpsPerBlock = 4;
+constexpr int32_t kWarpsPerBlock = 1;  // one row per CTA: rows spread over every SM
 constexpr int32_t kApplyThreads = 256;
 constexpr int32_t kApplyIters = 4;
 constexpr int32_t kGroupsPerChunk = kApplyThreads * kApplyIters;  // 8 columns per group
@@ -54,6 +54,9 @@ struct StepArgs {
 __global__ void __launch_bounds__(kWarpsPerBlock * 32)
     step_kernel(const __grid_constant__ Tables t, const StepArgs a) {
   __shared__ WarpShared shared[kWarpsPerBlock];
+  // Let a dependent apply_kernel launch now; it waits (griddepcontrol.wait) for this
+  // grid to complete and flush before it reads any mask.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int32_t warp = threadIdx.x >> 5;
   const int32_t i = blockIdx.x * kWarpsPerBlock + warp;
   if (i >= a.count) return;  // warp-uniform
@@ -122,48 +125,71 @@ __global__ void begin_kernel(const __grid_constant__ Tables t, const int32_t* sl
   mem[kMemFacts] = mem[kMemReached] = mem[kMemFrontier] = mem[kMemVersion] = 0;
   t.cursors[slot] = -1;
   t.active[slot] = on;
-  t.src[slot] = t.free_mask;
+  t.base[slot] = t.free_mask;
+  t.delta[slot] = nullptr;
 }
 
-// fill_mask: materialize each slot's current mask into its own buffer row.
+// fill_mask: materialize each slot's current mask (base | delta) into its own buffer row;
+// the slot then reads it as its delta alone.
 __global__ void fill_kernel(const __grid_constant__ Tables t) {
   const int32_t slot = blockIdx.x;
   uint32_t* own = t.masks + static_cast<int64_t>(slot) * t.words_padded;
-  const uint32_t* from = t.src[slot];
-  if (from == own) return;
-  for (int32_t i = threadIdx.x; i < t.words_padded; i += blockDim.x) own[i] = from ? from[i] : 0u;
+  const uint32_t* base = t.base[slot];
+  const uint32_t* delta = t.delta[slot];
+  for (int32_t i = threadIdx.x; i < t.words_padded; i += blockDim.x)
+    own[i] = (base ? base[i] : 0u) | (delta ? delta[i] : 0u);
+  __syncthreads();
+  if (threadIdx.x == 0 && (base || delta)) {
+    t.base[slot] = nullptr;
+    t.delta[slot] = own;
+  }
+}
+
+__device__ __forceinline__ uint32_t mask_word(const uint32_t* base, const uint32_t* delta, int64_t w) {
+  return (base ? __ldg(base + w) : 0u) | (delta ? delta[w] : 0u);
 }
 
 // Allowed bits of the 8 columns starting at column c (c >= 0): a 64-bit window of words.
-__device__ __forceinline__ uint32_t allowed8(const uint32_t* m, int32_t words, int64_t c) {
+__device__ __forceinline__ uint32_t allowed8(const uint32_t* base, const uint32_t* delta, int32_t words, int64_t c) {
   const int64_t w = c >> 5;
   const int32_t sh = static_cast<int32_t>(c & 31);
-  uint64_t x = w < words ? m[w] : 0u;
-  if (sh > 24 && w + 1 < words) x |= static_cast<uint64_t>(m[w + 1]) << 32;
+  uint64_t x = w < words ? mask_word(base, delta, w) : 0u;
+  if (sh > 24 && w + 1 < words) x |= static_cast<uint64_t>(mask_word(base, delta, w + 1)) << 32;
   return static_cast<uint32_t>(x >> sh) & 0xffu;
 }
 
 // -inf into every disallowed column of every row of an active, non-error slot.
-// ELT: element bytes (2 or 4); neg: the element's -inf bit pattern.
+// ELT: element bytes (2 or 4); neg: the element's -inf bit pattern.  Each thread owns
+// kApplyIters groups of 8 columns; a warp's stores cover 512 contiguous bytes.  The mask
+// reads of all groups are issued before any store (the stores may alias nothing the
+// compiler can prove, so it would not hoist them itself).
 template <int ELT>
 __global__ void __launch_bounds__(kApplyThreads)
     apply_kernel(const __grid_constant__ Tables t, char* logits, int32_t cols, int64_t stride,
                  const int32_t* row_slots, int32_t chunks, int32_t max_slots, uint32_t neg) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // masks of a preceding step kernel are complete
   const int32_t row = blockIdx.x / chunks;
   const int32_t chunk = blockIdx.x - row * chunks;
   const int32_t slot = row_slots[row];
   if (slot < 0 || slot >= max_slots || !t.active[slot]) return;
-  const uint32_t* m = t.src[slot];
-  if (m == nullptr) return;
+  const uint32_t* base = t.base[slot];
+  const uint32_t* delta = t.delta[slot];
+  if (base == nullptr && delta == nullptr) return;  // error phase: untouched
   char* out = logits + static_cast<int64_t>(row) * stride * ELT;
   const int32_t lead = static_cast<int32_t>(((16u - (reinterpret_cast<uintptr_t>(out) & 15u)) & 15u) / ELT);
   const int32_t words = t.words;
   const int64_t first = static_cast<int64_t>(chunk) * kGroupsPerChunk + threadIdx.x;
+  uint32_t allowed[kApplyIters];
+#pragma unroll
+  for (int32_t it = 0; it < kApplyIters; ++it) {
+    const int64_t c = lead + 8 * (first + it * kApplyThreads);
+    allowed[it] = c < cols ? allowed8(base, delta, words, c) : 0xffu;
+  }
 #pragma unroll
   for (int32_t it = 0; it < kApplyIters; ++it) {
     const int64_t c = lead + 8 * (first + it * kApplyThreads);
     if (c >= cols) break;
-    uint32_t blocked = ~allowed8(m, words, c) & 0xffu;
+    uint32_t blocked = ~allowed[it] & 0xffu;
     const int64_t left = cols - c;
     if (left < 8) blocked &= (1u << left) - 1u;
     if (blocked == 0u) continue;
@@ -189,8 +215,8 @@ __global__ void __launch_bounds__(kApplyThreads)
   }
   if (chunk == 0 && static_cast<int32_t>(threadIdx.x) < lead && static_cast<int32_t>(threadIdx.x) < cols) {
     const int32_t col = threadIdx.x;  // the columns before the first 16-byte boundary
-    const bool allowed = col < t.vocab && ((m[col >> 5] >> (col & 31)) & 1u);
-    if (!allowed) {
+    const bool ok = col < t.vocab && ((mask_word(base, delta, col >> 5) >> (col & 31)) & 1u);
+    if (!ok) {
       if (ELT == 2)
         *reinterpret_cast<uint16_t*>(out + 2 * col) = static_cast<uint16_t>(neg);
       else
@@ -215,7 +241,8 @@ struct XgEngine {
   XgState* states = nullptr;
   int32_t* memory = nullptr;
   uint32_t* masks = nullptr;
-  const uint32_t** src = nullptr;
+  const uint32_t** base = nullptr;
+  uint32_t** delta = nullptr;
   int32_t* cursors = nullptr;
   int32_t* active = nullptr;
   int32_t* tokens = nullptr;
@@ -258,7 +285,9 @@ int check_layout(const XgLayout& l) {
   if (l.opener_len <= 0 || l.closer_len <= 0 || l.separator_len <= 0 || l.escape_len <= 0 ||
       l.opener_len > 127 || l.closer_len > 127)
     return fail(XG_EINVAL, "layout: delimiter lengths out of range");
+  if (l.ent_cols < 1 || l.rel_cols < 1) return fail(XG_EINVAL, "layout: column tables missing");
   const int64_t required[] = {l.ent_tok, l.ent_off, l.ent_owner, l.rel_tok, l.rel_off, l.rel_owner,
+                              l.ent_col, l.rel_col, l.ent_first, l.rel_first,
                               l.ent_first_row, l.ent_rows_off, l.ent_rows, l.adj_off, l.edge_rel,
                               l.edge_obj, l.root_mask, l.free_next, l.free_mask, l.esc_next,
                               l.esc_mask, l.eos_mask, l.closer_off, l.closer_tok, l.closer_next,
@@ -279,8 +308,10 @@ void bind_tables(XgEngine* e) {
   const XgLayout& l = e->layout;
   const char* b = e->blob;
   Tables& t = e->t;
-  t.ent = Rows{at<int32_t>(b, l.ent_tok), at<int32_t>(b, l.ent_off), at<int32_t>(b, l.ent_owner), l.entity_rows};
-  t.rel = Rows{at<int32_t>(b, l.rel_tok), at<int32_t>(b, l.rel_off), at<int32_t>(b, l.rel_owner), l.relation_rows};
+  t.ent = Rows{at<int32_t>(b, l.ent_tok), at<int32_t>(b, l.ent_off), at<int32_t>(b, l.ent_owner), l.entity_rows,
+               at<int32_t>(b, l.ent_col), at<int32_t>(b, l.ent_first), l.ent_cols};
+  t.rel = Rows{at<int32_t>(b, l.rel_tok), at<int32_t>(b, l.rel_off), at<int32_t>(b, l.rel_owner), l.relation_rows,
+               at<int32_t>(b, l.rel_col), at<int32_t>(b, l.rel_first), l.rel_cols};
   t.ent_first_row = at<int32_t>(b, l.ent_first_row);
   t.ent_rows_off = at<int32_t>(b, l.ent_rows_off);
   t.ent_rows = at<int32_t>(b, l.ent_rows);
@@ -326,7 +357,8 @@ void bind_tables(XgEngine* e) {
   t.memory = e->memory;
   t.memory_ints = kMemHave + ((l.relation_words + 3) & ~3);
   t.masks = e->masks;
-  t.src = e->src;
+  t.base = e->base;
+  t.delta = e->delta;
   t.cursors = e->cursors;
   t.active = e->active;
 }
@@ -336,7 +368,8 @@ void release(XgEngine* e) {
   cudaFree(e->states);
   cudaFree(e->memory);
   cudaFree(e->masks);
-  cudaFree(const_cast<uint32_t**>(e->src));
+  cudaFree(const_cast<uint32_t**>(e->base));
+  cudaFree(e->delta);
   cudaFree(e->cursors);
   cudaFree(e->active);
   cudaFree(e->tokens);
@@ -366,7 +399,8 @@ int create(const void* blob, bool on_device, const XgLayout* layout, const XgOpt
   alloc(reinterpret_cast<void**>(&e->states), slots * sizeof(XgState));
   alloc(reinterpret_cast<void**>(&e->memory), slots * memory_ints * sizeof(int32_t));
   alloc(reinterpret_cast<void**>(&e->masks), slots * layout->words_padded * sizeof(uint32_t));
-  alloc(reinterpret_cast<void**>(&e->src), slots * sizeof(uint32_t*));
+  alloc(reinterpret_cast<void**>(&e->base), slots * sizeof(uint32_t*));
+  alloc(reinterpret_cast<void**>(&e->delta), slots * sizeof(uint32_t*));
   alloc(reinterpret_cast<void**>(&e->cursors), slots * sizeof(int32_t));
   alloc(reinterpret_cast<void**>(&e->active), slots * sizeof(int32_t));
   alloc(reinterpret_cast<void**>(&e->tokens), slots * sizeof(int32_t));
@@ -609,14 +643,24 @@ int xg_apply_mask(XgEngine* e, void* logits, int32_t dtype, int32_t rows, int32_
   const int32_t chunks = static_cast<int32_t>((groups + kGroupsPerChunk - 1) / kGroupsPerChunk);
   const int64_t blocks = static_cast<int64_t>(rows) * chunks;
   if (blocks > 0x7fffffff) return fail(XG_EINVAL, "too many logits rows");
-  cudaStream_t s = as_stream(stream);
+  cudaLaunchConfig_t config{};
+  config.gridDim = dim3(static_cast<unsigned>(blocks));
+  config.blockDim = dim3(kApplyThreads);
+  config.stream = as_stream(stream);
+  cudaLaunchAttribute attribute{};
+  attribute.id = cudaLaunchAttributeProgrammaticStreamSerialization;  // overlap our launch with the step kernel
+  attribute.val.programmaticStreamSerializationAllowed = 1;
+  config.attrs = &attribute;
+  config.numAttrs = 1;
+  char* data = static_cast<char*>(logits);
   if (dtype == XG_F32) {
-    apply_kernel<4><<<static_cast<unsigned>(blocks), kApplyThreads, 0, s>>>(
-        e->t, static_cast<char*>(logits), cols, row_stride, row_slots, chunks, e->max_sequences, 0xff800000u);
+    XG_CUDA(cudaLaunchKernelEx(&config, apply_kernel<4>, e->t, data, cols, row_stride, row_slots, chunks,
+                               e->max_sequences, 0xff800000u),
+            "apply kernel");
   } else {
-    apply_kernel<2><<<static_cast<unsigned>(blocks), kApplyThreads, 0, s>>>(
-        e->t, static_cast<char*>(logits), cols, row_stride, row_slots, chunks, e->max_sequences,
-        dtype == XG_BF16 ? 0xff80u : 0xfc00u);
+    XG_CUDA(cudaLaunchKernelEx(&config, apply_kernel<2>, e->t, data, cols, row_stride, row_slots, chunks,
+                               e->max_sequences, dtype == XG_BF16 ? 0xff80u : 0xfc00u),
+            "apply kernel");
   }
   XG_CUDA(cudaGetLastError(), "apply kernel");
   return XG_OK;

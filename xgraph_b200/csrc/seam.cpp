@@ -18,7 +18,8 @@ struct SeamEngine {
   std::vector<XgState> states;
   std::vector<int32_t> memory;
   std::vector<uint32_t> masks;
-  std::vector<const uint32_t*> src;
+  std::vector<const uint32_t*> base;
+  std::vector<uint32_t*> delta;
   std::vector<int32_t> cursors, active;
   std::vector<Key> top;
   std::vector<int32_t> scratch;
@@ -41,7 +42,8 @@ static void begin_slot(SeamEngine* e, int32_t slot, int32_t on) {
   mem[kMemFacts] = mem[kMemReached] = mem[kMemFrontier] = mem[kMemVersion] = 0;
   e->cursors[slot] = -1;
   e->active[slot] = on;
-  e->src[slot] = e->t.free_mask;
+  e->base[slot] = e->t.free_mask;
+  e->delta[slot] = nullptr;
 }
 
 extern "C" {
@@ -53,8 +55,10 @@ SeamEngine* xgs_create(const void* blob, const XgLayout* l, const XgOptions* o, 
   e->slots = slots;
   const char* b = e->blob.data();
   Tables& t = e->t;
-  t.ent = Rows{at<int32_t>(b, l->ent_tok), at<int32_t>(b, l->ent_off), at<int32_t>(b, l->ent_owner), l->entity_rows};
-  t.rel = Rows{at<int32_t>(b, l->rel_tok), at<int32_t>(b, l->rel_off), at<int32_t>(b, l->rel_owner), l->relation_rows};
+  t.ent = Rows{at<int32_t>(b, l->ent_tok), at<int32_t>(b, l->ent_off), at<int32_t>(b, l->ent_owner), l->entity_rows,
+               at<int32_t>(b, l->ent_col), at<int32_t>(b, l->ent_first), l->ent_cols};
+  t.rel = Rows{at<int32_t>(b, l->rel_tok), at<int32_t>(b, l->rel_off), at<int32_t>(b, l->rel_owner), l->relation_rows,
+               at<int32_t>(b, l->rel_col), at<int32_t>(b, l->rel_first), l->rel_cols};
   t.ent_first_row = at<int32_t>(b, l->ent_first_row);
   t.ent_rows_off = at<int32_t>(b, l->ent_rows_off);
   t.ent_rows = at<int32_t>(b, l->ent_rows);
@@ -99,7 +103,8 @@ SeamEngine* xgs_create(const void* blob, const XgLayout* l, const XgOptions* o, 
   e->states.assign(slots, XgState{});
   e->memory.assign(static_cast<size_t>(slots) * t.memory_ints, 0);
   e->masks.assign(static_cast<size_t>(slots) * l->words_padded, 0u);
-  e->src.assign(slots, nullptr);
+  e->base.assign(slots, nullptr);
+  e->delta.assign(slots, nullptr);
   e->cursors.assign(slots, -1);
   e->active.assign(slots, 0);
   e->top.assign(kTopCap, Key{});
@@ -107,7 +112,8 @@ SeamEngine* xgs_create(const void* blob, const XgLayout* l, const XgOptions* o, 
   t.states = e->states.data();
   t.memory = e->memory.data();
   t.masks = e->masks.data();
-  t.src = e->src.data();
+  t.base = e->base.data();
+  t.delta = e->delta.data();
   t.cursors = e->cursors.data();
   t.active = e->active.data();
   for (int32_t s = 0; s < slots; ++s) begin_slot(e, s, 0);
@@ -163,8 +169,10 @@ void xgs_advance(SeamEngine* e, const int32_t* tokens, int32_t count) {
 void xgs_masks(SeamEngine* e, int32_t n, uint32_t* out) {
   const int32_t words = e->layout.words;
   for (int32_t slot = 0; slot < n; ++slot) {
-    const uint32_t* from = e->src[slot];
-    for (int32_t w = 0; w < words; ++w) out[static_cast<int64_t>(slot) * words + w] = from ? from[w] : 0u;
+    const uint32_t* base = e->base[slot];
+    const uint32_t* delta = e->delta[slot];
+    for (int32_t w = 0; w < words; ++w)
+      out[static_cast<int64_t>(slot) * words + w] = (base ? base[w] : 0u) | (delta ? delta[w] : 0u);
   }
 }
 

@@ -41,9 +41,10 @@ class XgLayout(ctypes.Structure):
         + [(n, ctypes.c_int32) for n in (
             "vocab", "words", "words_padded", "entity_rows", "relation_rows", "entities",
             "relations", "relation_words", "opener_len", "closer_len", "separator_len",
-            "escape_len", "versions", "wide_count", "pad0")]
+            "escape_len", "versions", "wide_count", "ent_cols", "rel_cols", "pad0", "pad1")]
         + [(n, ctypes.c_int64) for n in (
             "ent_tok", "ent_off", "ent_owner", "rel_tok", "rel_off", "rel_owner",
+            "ent_col", "rel_col", "ent_first", "rel_first",
             "ent_first_row", "ent_rows_off", "ent_rows", "adj_off", "edge_rel", "edge_obj",
             "sitelinks", "kept_prefix", "root_mask", "wide_keys", "wide_masks",
             "free_next", "free_mask", "esc_next", "esc_mask", "eos_mask",
@@ -201,6 +202,29 @@ def quoted_rows(labels, token_bytes, syntax) -> np.ndarray:
     return out
 
 
+MAX_COLUMNS = 8
+
+
+def column_table(tokens: np.ndarray, offsets: np.ndarray) -> np.ndarray:
+    """int32 [cols, rows]: each row's token at depth d (-1 past its end), for the first
+    MAX_COLUMNS depths, so a search step over a row range reads one word."""
+    offsets = np.asarray(offsets, dtype=np.int64)
+    rows = len(offsets) - 1
+    longest = int(np.diff(offsets).max()) if rows else 1
+    cols = max(1, min(MAX_COLUMNS, longest))
+    out = np.full((cols, max(rows, 0)), -1, dtype=np.int32)
+    for d in range(cols):
+        out[d] = _row_columns(np.asarray(tokens), offsets, d)
+    return out
+
+
+def first_token_starts(tokens: np.ndarray, offsets: np.ndarray, vocab: int) -> np.ndarray:
+    """int32 [vocab + 1]: the first row whose first token is >= t (rows sorted, nonempty)."""
+    offsets = np.asarray(offsets, dtype=np.int64)
+    firsts = np.asarray(tokens)[offsets[:-1]] if len(offsets) > 1 else np.zeros(0, dtype=np.int64)
+    return np.searchsorted(firsts, np.arange(vocab + 1), side="left").astype(np.int32)
+
+
 def _int32(name: str, array) -> np.ndarray:
     a = np.asarray(array)
     if a.size and (a.min() < -(2**31) or a.max() >= 2**31):
@@ -279,11 +303,17 @@ def pack_tables(index, tokenizer, syntax, *, escapes: bool, versions=None,
         ver_adj = np.zeros(1, np.int32)
         count = 0
 
+    rel_tok = _int32("relation token", relations.tokens)
+    rel_off = _int32("relation offset", relations.offsets)
+    ent_col = column_table(ent_tok, ent_off)
+    rel_col = column_table(rel_tok, rel_off)
     arrays: dict[str, np.ndarray] = {
         "ent_tok": ent_tok, "ent_off": ent_off, "ent_owner": ent_owner,
-        "rel_tok": _int32("relation token", relations.tokens),
-        "rel_off": _int32("relation offset", relations.offsets),
+        "rel_tok": rel_tok, "rel_off": rel_off,
         "rel_owner": _int32("relation owner", relations.owners),
+        "ent_col": ent_col, "rel_col": rel_col,
+        "ent_first": first_token_starts(ent_tok, ent_off, vocab),
+        "rel_first": first_token_starts(rel_tok, rel_off, vocab),
         "ent_first_row": first_row, "ent_rows_off": _int32("entity rows", ent_rows_off),
         "ent_rows": ent_rows,
         "adj_off": _int32("adjacency offsets", index.adjacency_offsets),
@@ -333,4 +363,5 @@ def pack_tables(index, tokenizer, syntax, *, escapes: bool, versions=None,
     layout.separator_len, layout.escape_len = len(separator), len(escape)
     layout.versions = count
     layout.wide_count = len(wide_keys)
+    layout.ent_cols, layout.rel_cols = ent_col.shape[0], rel_col.shape[0]
     return PackedTables(blob=blob, layout=layout, words=words, words_padded=wp)
