@@ -94,6 +94,7 @@ typedef struct XgLayout {
   int64_t separator_off, separator_tok, separator_next;
   int64_t escape_off, escape_tok, escape_next;
   int64_t ver_off, ver_subj, ver_adj, ver_edge_rel, ver_edge_obj;
+  int64_t dstep;  /* uint64 [vocab]: packed next positions of every delimiter byte position, or -1 */
 } XgLayout;
 
 /* Span-language policies, as the reference Engine's constructor flags

@@ -101,6 +101,11 @@ struct Tables {
   const uint32_t* esc_mask;
   const uint32_t* eos_mask;
   Delim closer, separator, escape;
+  // Per token, the next byte position of every (delimiter, position) pair in one word:
+  // 4 bits at 4 * (offset of the delimiter + position), 0 = the token does not continue
+  // it (closer at offset 0, separator after it, escape after that).  Null when the
+  // delimiters are too long for 16 nibbles; the CSR lists then serve.
+  const uint64_t* dstep;
   const int32_t* ver_off;
   const int32_t* ver_subj;
   const int32_t* ver_adj;
@@ -211,6 +216,7 @@ enum TopMode : int32_t { kDistinct = 0, kEntity = 1 };
 struct TopSet {
   Key* buf;
   int32_t n;
+  int32_t pushed = 0;  // keys offered so far (n can shrink when the buffer compacts)
 };
 
 // Sorts buf[0, n) ascending; entries from n to the sorted width are set to max_key().
@@ -317,11 +323,13 @@ XG_HD void top_push(const Warp& w, TopSet& ts, bool valid, const Key& k, int32_t
   const int32_t pos = ts.n + __popc(m & ((1u << w.lane) - 1u));
   if (valid) ts.buf[pos] = k;
   ts.n += __popc(m);
+  ts.pushed += __popc(m);
   __syncwarp();
 #else
   if (!valid) return;
   if (ts.n + 1 > kTopCap) top_compact(w, ts, mode);
   ts.buf[ts.n++] = k;
+  ts.pushed += 1;
 #endif
 }
 
@@ -436,8 +444,23 @@ XG_HD Edges edges_of(const Tables& t, int32_t version, int32_t e) {
   return Edges{t.edge_rel + s, t.edge_obj + s, f - s};
 }
 
-// The objects of one relation within an adjacency list: [first, last) indexes.
+// The objects of one relation within an adjacency list: [first, last) indexes.  Short
+// lists (<= 16 edges) are scanned with independent loads instead of dependent halvings.
 XG_HD void relation_slice(const Edges& g, int32_t relation, int32_t& first, int32_t& last) {
+  if (g.n <= 16) {
+    int32_t below = 0, upto = 0;
+#pragma unroll
+    for (int32_t i = 0; i < 16; ++i) {
+      if (i < g.n) {
+        const int32_t r = g.rel[i];
+        below += r < relation;
+        upto += r <= relation;
+      }
+    }
+    first = below;
+    last = upto;
+    return;
+  }
   first = lower_index(g.rel, 0, g.n, relation);
   last = upper_index(g.rel, first, g.n, relation);
 }
@@ -591,7 +614,10 @@ XG_HD void set_have(const Ctx& c, int32_t n, E entity) {
 // Next path frontier (src/xgraph/oracle.py:1771-1786): objects of the current frontier
 // under every relation of the exact relation-label rows [rlo, rhi), each with the least
 // start rank it is reached from, kept to 64 by (rank, first row) or, with union paths,
-// by first row.  Leaves the result sorted in c.top[0, n) as ENTITY keys; returns n.
+// by first row.  Leaves the result in c.top[0, n) as ENTITY keys and returns n.  When at
+// most 64 edges were found no cap applies and no sort is needed: the keys stay as found,
+// an entity possibly more than once (once per rank it is reached with).  Every reader
+// treats the list as a set with least ranks, so the duplicates change nothing.
 XG_HD int32_t next_frontier(const Ctx& c, int32_t rlo, int32_t rhi) {
   const Tables& t = c.t;
   const int32_t version = version_of(c);
@@ -620,8 +646,33 @@ XG_HD int32_t next_frontier(const Ctx& c, int32_t rlo, int32_t rhi) {
           top_push(c.w, ts, valid, key, kEntity);
         });
   }
-  top_compact(c.w, ts, kEntity);
+  if (ts.pushed > kMaxSet) top_compact(c.w, ts, kEntity);
   return ts.n;
+}
+
+// Keep, in c.top[0, n), the keys of the least rank present (committed paths resolve to
+// what the best start reaches, src/xgraph/oracle.py:1160-1162); returns how many.
+XG_HD int32_t keep_least_rank(const Ctx& c, int32_t n) {
+  const Key least = warp_min(c.w, 0, n, [&](int32_t i) { return Key{c.top[i].a >> 32, 0u, 0u}; });
+#if XG_GPU
+  int32_t out = 0;
+  for (int32_t base = 0; base < n; base += 32) {
+    const int32_t i = base + c.w.lane;
+    const Key k = i < n ? c.top[i] : max_key();
+    const bool keep = i < n && (k.a >> 32) == least.a;
+    const uint32_t m = __ballot_sync(0xffffffffu, keep);
+    __syncwarp();
+    if (keep) c.top[out + __popc(m & ((1u << c.w.lane) - 1u))] = k;
+    out += __popc(m);
+    __syncwarp();
+  }
+  return out;
+#else
+  int32_t out = 0;
+  for (int32_t i = 0; i < n; ++i)
+    if ((c.top[i].a >> 32) == least.a) c.top[out++] = c.top[i];
+  return out;
+#endif
 }
 
 // The rows of the entities whose first rows are given by keys c.top[0, n) (low 32 bits of
@@ -841,12 +892,7 @@ XG_HD void close_span(const Ctx& c, XgState& s, int32_t llo, int32_t lhi) {
   const int32_t version = version_of(c);
   if (s.segment == kRelation) {  // a path ends
     int32_t n = next_frontier(c, llo, lhi);
-    if (t.committed && n > 0) {  // keep the least rank present (a prefix of the sorted keys)
-      const uint64_t best = c.top[0].a >> 32;
-      int32_t m = 0;
-      while (m < n && (c.top[m].a >> 32) == best) ++m;
-      n = m;
-    }
+    if (t.committed && n > 0) n = keep_least_rank(c, n);
     reach_rows_of_top(c, n);
     s.last_kind = kPathSpan;
     s.last_lo = s.last_hi = s.last_subj_lo = s.last_subj_hi = s.last_rel_lo = s.last_rel_hi = 0;
@@ -916,10 +962,23 @@ XG_HD void close_span(const Ctx& c, XgState& s, int32_t llo, int32_t lhi) {
   end_span(s, kFree);
 }
 
+// Next byte position of delimiter `which` (0 closer, 1 separator, 2 escape) after
+// `token` from byte position `pos`, or -1 when the token does not continue it.
+XG_HD int32_t delim_next(const Tables& t, uint64_t packed, int32_t which, int32_t pos, int32_t token);
+
 XG_HD int32_t delim_step(const Delim& d, int32_t pos, int32_t token) {
   const int32_t a = d.off[pos], b = d.off[pos + 1];
   const int32_t at = lower_index(d.tok, a, b, token);
   return at < b && d.tok[at] == token ? d.next[at] : -1;
+}
+
+XG_HD int32_t delim_next(const Tables& t, uint64_t packed, int32_t which, int32_t pos, int32_t token) {
+  if (t.dstep) {
+    const int32_t offset = which == 0 ? 0 : which == 1 ? t.closer.len : t.closer.len + t.separator.len;
+    const int32_t next = static_cast<int32_t>((packed >> (4 * (offset + pos))) & 15u);
+    return next ? next : -1;
+  }
+  return delim_step(which == 0 ? t.closer : which == 1 ? t.separator : t.escape, pos, token);
 }
 
 // One token inside a span (src/xgraph/oracle.py:896-1263, in-scope branches).
@@ -927,24 +986,25 @@ XG_HD void advance_span(const Ctx& c, XgState& s, int32_t token) {
   const Tables& t = c.t;
   int32_t close = -1, sep = -1, esc = -1;
   int32_t close_lo = s.close_lo, close_hi = s.close_hi, sep_lo = s.sep_lo, sep_hi = s.sep_hi;
+  const uint64_t packed = t.dstep ? t.dstep[token] : 0u;
   if (s.close_pos > 0) {
-    close = delim_step(t.closer, s.close_pos, token);
+    close = delim_next(t, packed, 0, s.close_pos, token);
   } else if (s.flags & kMayClose) {
-    close = delim_step(t.closer, 0, token);
+    close = delim_next(t, packed, 0, 0, token);
     close_lo = s.lo;
     close_hi = s.ex_hi;
   }
   if (s.sep_pos > 0) {
-    sep = delim_step(t.separator, s.sep_pos, token);
+    sep = delim_next(t, packed, 1, s.sep_pos, token);
   } else if (s.flags & kMaySep) {
-    sep = delim_step(t.separator, 0, token);
+    sep = delim_next(t, packed, 1, 0, token);
     sep_lo = s.lo;
     sep_hi = s.ex_hi;
   }
   if (s.esc_pos > 0) {
-    esc = delim_step(t.escape, s.esc_pos, token);
+    esc = delim_next(t, packed, 2, s.esc_pos, token);
   } else if (s.flags & kMayEsc) {
-    esc = delim_step(t.escape, 0, token);
+    esc = delim_next(t, packed, 2, 0, token);
   }
   int32_t lo = -1, hi = -1;
   if (s.lo >= 0) {

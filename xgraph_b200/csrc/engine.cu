@@ -22,8 +22,8 @@ namespace xg {
 
 constexpr int32_t kWarpsPerBlock = 1;  // one row per CTA: rows spread over every SM
 constexpr int32_t kApplyThreads = 256;
-constexpr int32_t kApplyIters = 4;
-constexpr int32_t kGroupsPerChunk = kApplyThreads * kApplyIters;  // 8 columns per group
+constexpr int32_t kApplyBatch = 8;        // groups of 8 columns per thread per round
+constexpr int32_t kApplyCtasPerSm = 8;    // apply grid: about one full wave of CTAs
 
 struct __align__(16) WarpShared {
   Key top[kTopCap];
@@ -159,12 +159,13 @@ __device__ __forceinline__ uint32_t allowed8(const uint32_t* base, const uint32_
 }
 
 // -inf into every disallowed column of every row of an active, non-error slot.
-// ELT: element bytes (2 or 4); neg: the element's -inf bit pattern.  Each thread owns
-// kApplyIters groups of 8 columns; a warp's stores cover 512 contiguous bytes.  The mask
-// reads of all groups are issued before any store (the stores may alias nothing the
-// compiler can prove, so it would not hoist them itself).
+// ELT: element bytes (2 or 4); neg: the element's -inf bit pattern.  A CTA owns a 1/chunks
+// share of one row, as groups of 8 columns starting at the row's first 16-byte boundary;
+// each thread takes kApplyBatch groups per round, issuing all of their mask reads before
+// any store (the stores may alias nothing the compiler can prove, so it would not hoist
+// the reads itself), and a warp's stores cover 512 contiguous bytes.
 template <int ELT>
-__global__ void __launch_bounds__(kApplyThreads)
+__global__ void __launch_bounds__(kApplyThreads, 4)
     apply_kernel(const __grid_constant__ Tables t, char* logits, int32_t cols, int64_t stride,
                  const int32_t* row_slots, int32_t chunks, int32_t max_slots, uint32_t neg) {
   asm volatile("griddepcontrol.wait;" ::: "memory");  // masks of a preceding step kernel are complete
@@ -178,37 +179,43 @@ __global__ void __launch_bounds__(kApplyThreads)
   char* out = logits + static_cast<int64_t>(row) * stride * ELT;
   const int32_t lead = static_cast<int32_t>(((16u - (reinterpret_cast<uintptr_t>(out) & 15u)) & 15u) / ELT);
   const int32_t words = t.words;
-  const int64_t first = static_cast<int64_t>(chunk) * kGroupsPerChunk + threadIdx.x;
-  uint32_t allowed[kApplyIters];
+  const int64_t groups = cols > lead ? (static_cast<int64_t>(cols) - lead + 7) / 8 : 0;
+  const int64_t share = (groups + chunks - 1) / chunks;
+  const int64_t g0 = chunk * share;
+  const int64_t g1 = g0 + share < groups ? g0 + share : groups;
+  for (int64_t round = g0 + threadIdx.x; round < g1; round += kApplyThreads * kApplyBatch) {
+    uint32_t allowed[kApplyBatch];
 #pragma unroll
-  for (int32_t it = 0; it < kApplyIters; ++it) {
-    const int64_t c = lead + 8 * (first + it * kApplyThreads);
-    allowed[it] = c < cols ? allowed8(base, delta, words, c) : 0xffu;
-  }
+    for (int32_t b = 0; b < kApplyBatch; ++b) {
+      const int64_t g = round + b * kApplyThreads;
+      allowed[b] = g < g1 ? allowed8(base, delta, words, lead + 8 * g) : 0xffu;
+    }
 #pragma unroll
-  for (int32_t it = 0; it < kApplyIters; ++it) {
-    const int64_t c = lead + 8 * (first + it * kApplyThreads);
-    if (c >= cols) break;
-    uint32_t blocked = ~allowed[it] & 0xffu;
-    const int64_t left = cols - c;
-    if (left < 8) blocked &= (1u << left) - 1u;
-    if (blocked == 0u) continue;
-    char* at = out + c * ELT;
-    if (blocked == 0xffu) {
-      if (ELT == 2) {
-        const uint32_t v = neg | (neg << 16);
-        *reinterpret_cast<uint4*>(at) = make_uint4(v, v, v, v);
+    for (int32_t b = 0; b < kApplyBatch; ++b) {
+      const int64_t g = round + b * kApplyThreads;
+      if (g >= g1) break;
+      const int64_t c = lead + 8 * g;
+      uint32_t blocked = ~allowed[b] & 0xffu;
+      const int64_t left = cols - c;
+      if (left < 8) blocked &= (1u << left) - 1u;
+      if (blocked == 0u) continue;
+      char* at = out + c * ELT;
+      if (blocked == 0xffu) {
+        if (ELT == 2) {
+          const uint32_t v = neg | (neg << 16);
+          *reinterpret_cast<uint4*>(at) = make_uint4(v, v, v, v);
+        } else {
+          *reinterpret_cast<uint4*>(at) = make_uint4(neg, neg, neg, neg);
+          *reinterpret_cast<uint4*>(at + 16) = make_uint4(neg, neg, neg, neg);
+        }
       } else {
-        *reinterpret_cast<uint4*>(at) = make_uint4(neg, neg, neg, neg);
-        *reinterpret_cast<uint4*>(at + 16) = make_uint4(neg, neg, neg, neg);
-      }
-    } else {
-      for (int32_t k = 0; k < 8; ++k) {
-        if ((blocked >> k) & 1u) {
-          if (ELT == 2)
-            *reinterpret_cast<uint16_t*>(at + 2 * k) = static_cast<uint16_t>(neg);
-          else
-            *reinterpret_cast<uint32_t*>(at + 4 * k) = neg;
+        for (int32_t k = 0; k < 8; ++k) {
+          if ((blocked >> k) & 1u) {
+            if (ELT == 2)
+              *reinterpret_cast<uint16_t*>(at + 2 * k) = static_cast<uint16_t>(neg);
+            else
+              *reinterpret_cast<uint32_t*>(at + 4 * k) = neg;
+          }
         }
       }
     }
@@ -234,6 +241,7 @@ using namespace xg;
 
 struct XgEngine {
   int device = 0;
+  int sm_count = 148;
   XgLayout layout{};
   XgOptions options{};
   int32_t max_sequences = 0;
@@ -296,7 +304,7 @@ int check_layout(const XgLayout& l) {
                               l.ver_edge_rel, l.ver_edge_obj};
   for (int64_t off : required)
     if (off < 0 || off > l.blob_bytes || off % 16) return fail(XG_EINVAL, "layout: table offset outside the blob");
-  const int64_t optional[] = {l.sitelinks, l.kept_prefix, l.wide_keys, l.wide_masks};
+  const int64_t optional[] = {l.sitelinks, l.kept_prefix, l.wide_keys, l.wide_masks, l.dstep};
   for (int64_t off : optional)
     if (off != -1 && (off < 0 || off > l.blob_bytes || off % 16))
       return fail(XG_EINVAL, "layout: optional table offset outside the blob");
@@ -333,6 +341,7 @@ void bind_tables(XgEngine* e) {
   t.separator = Delim{at<int32_t>(b, l.separator_off), at<int32_t>(b, l.separator_tok),
                       at<int32_t>(b, l.separator_next), l.separator_len};
   t.escape = Delim{at<int32_t>(b, l.escape_off), at<int32_t>(b, l.escape_tok), at<int32_t>(b, l.escape_next), l.escape_len};
+  t.dstep = at<uint64_t>(b, l.dstep);
   t.ver_off = at<int32_t>(b, l.ver_off);
   t.ver_subj = at<int32_t>(b, l.ver_subj);
   t.ver_adj = at<int32_t>(b, l.ver_adj);
@@ -389,6 +398,7 @@ int create(const void* blob, bool on_device, const XgLayout* layout, const XgOpt
   e->options = *options;
   e->max_sequences = max_sequences;
   cudaGetDevice(&e->device);
+  cudaDeviceGetAttribute(&e->sm_count, cudaDevAttrMultiProcessorCount, e->device);
   const int64_t slots = max_sequences;
   const int32_t memory_ints = kMemHave + ((layout->relation_words + 3) & ~3);
   cudaError_t err = cudaSuccess;
@@ -639,8 +649,12 @@ int xg_apply_mask(XgEngine* e, void* logits, int32_t dtype, int32_t rows, int32_
   if (!logits || !row_slots) return fail(XG_EINVAL, "null argument");
   const int elt = dtype == XG_F32 ? 4 : 2;
   if (reinterpret_cast<uintptr_t>(logits) % elt) return fail(XG_EINVAL, "logits are not aligned to their element size");
-  const int64_t groups = (static_cast<int64_t>(cols) + 7) / 8 + 1;
-  const int32_t chunks = static_cast<int32_t>((groups + kGroupsPerChunk - 1) / kGroupsPerChunk);
+  // Split each row into `chunks` CTAs so that the grid is about one wave of resident CTAs
+  // (each CTA then runs long enough to hide its few dependent pointer loads).
+  const int64_t groups = (static_cast<int64_t>(cols) + 7) / 8;
+  const int64_t per_row_max = (groups + kApplyThreads - 1) / kApplyThreads;
+  const int64_t wanted = (static_cast<int64_t>(e->sm_count) * kApplyCtasPerSm + rows - 1) / rows;
+  const int32_t chunks = static_cast<int32_t>(wanted < 1 ? 1 : wanted > per_row_max ? (per_row_max < 1 ? 1 : per_row_max) : wanted);
   const int64_t blocks = static_cast<int64_t>(rows) * chunks;
   if (blocks > 0x7fffffff) return fail(XG_EINVAL, "too many logits rows");
   cudaLaunchConfig_t config{};

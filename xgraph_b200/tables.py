@@ -50,7 +50,7 @@ class XgLayout(ctypes.Structure):
             "free_next", "free_mask", "esc_next", "esc_mask", "eos_mask",
             "closer_off", "closer_tok", "closer_next", "separator_off", "separator_tok",
             "separator_next", "escape_off", "escape_tok", "escape_next",
-            "ver_off", "ver_subj", "ver_adj", "ver_edge_rel", "ver_edge_obj")]
+            "ver_off", "ver_subj", "ver_adj", "ver_edge_rel", "ver_edge_obj", "dstep")]
     )
 
 
@@ -225,6 +225,30 @@ def first_token_starts(tokens: np.ndarray, offsets: np.ndarray, vocab: int) -> n
     return np.searchsorted(firsts, np.arange(vocab + 1), side="left").astype(np.int32)
 
 
+def packed_delimiter_steps(delimiters: list[bytes | None], token_bytes) -> np.ndarray | None:
+    """uint64 [vocab]: for every token, 4 bits per (delimiter, byte position) pair holding
+    the position after the token when its bytes continue the delimiter there (0 if not);
+    pairs are numbered delimiter by delimiter.  None when the pairs exceed 16 nibbles.
+    A delimiter given as None (escapes off) is left out: the engine never asks for it."""
+    total = sum(len(d) for d in delimiters if d is not None)
+    if total > 16 or any(d is not None and len(d) > 15 for d in delimiters):
+        return None
+    out = np.zeros(len(token_bytes), dtype=np.uint64)
+    for token, data in enumerate(token_bytes):
+        if not data:
+            continue
+        word, offset = 0, 0
+        for d in delimiters:
+            if d is None:
+                continue
+            for pos in range(len(d)):
+                if len(data) <= len(d) - pos and d.startswith(data, pos):
+                    word |= (pos + len(data)) << (4 * (offset + pos))
+            offset += len(d)
+        out[token] = word
+    return out
+
+
 def _int32(name: str, array) -> np.ndarray:
     a = np.asarray(array)
     if a.size and (a.min() < -(2**31) or a.max() >= 2**31):
@@ -332,6 +356,9 @@ def pack_tables(index, tokenizer, syntax, *, escapes: bool, versions=None,
             off, tok, nxt = np.zeros(len(delim) + 1, np.int32), np.zeros(0, np.int32), np.zeros(0, np.int32)
         arrays[f"{name}_off"], arrays[f"{name}_tok"], arrays[f"{name}_next"] = off, tok, nxt
     optional = {}
+    dstep = packed_delimiter_steps([closer, separator, escape if escapes else None], token_bytes)
+    if dstep is not None:
+        optional["dstep"] = dstep
     if index.sitelinks is not None:
         optional["sitelinks"] = _int32("sitelinks", index.sitelinks)
     if kept_prefix is not None:
@@ -350,7 +377,7 @@ def pack_tables(index, tokenizer, syntax, *, escapes: bool, versions=None,
         pad = (-len(data)) % ALIGN
         pieces.append(b"\0" * pad)
         cursor += len(data) + pad
-    for name in ("sitelinks", "kept_prefix", "wide_keys", "wide_masks"):
+    for name in ("sitelinks", "kept_prefix", "wide_keys", "wide_masks", "dstep"):
         if name not in optional:
             setattr(layout, name, -1)
     blob = np.frombuffer(b"".join(pieces) or b"\0" * ALIGN, dtype=np.uint8).copy()
