@@ -281,7 +281,12 @@ def engine_arm(args) -> None:
     sample_s = time.perf_counter() - t0
     del gen_engine
     # -- replay schedule -------------------------------------------------------------------
-    total_steps = args.warmup + args.steps
+    # W warm-up steps, K timed steps (events around each whole step), then R roofline steps
+    # with an extra event between sync and apply_mask so the apply kernel is timed alone
+    # (that event also stops the apply launch from overlapping the step kernel, so these
+    # steps are not part of the K).
+    roof_steps = min(64, args.steps)
+    total_steps = args.warmup + args.steps + roof_steps
     assigned, restarts = schedule(lengths, rows, total_steps)
     history = torch.zeros((rows, total_steps + 1), dtype=torch.int32, device=device)
     disallowed = np.zeros(total_steps, dtype=np.int64)  # sum over rows of disallowed columns
@@ -310,8 +315,10 @@ def engine_arm(args) -> None:
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
+    roof_from = args.warmup + args.steps
     for k in range(total_steps):
-        timed = k >= args.warmup
+        timed = args.warmup <= k < roof_from
+        roof = k >= roof_from
         if timed and clocks is None:
             torch.cuda.synchronize()
             if world > 1:
@@ -319,6 +326,9 @@ def engine_arm(args) -> None:
             clocks = Clocks(local)
             time.sleep(0.3)
             torch.cuda.nvtx.range_push("timed")
+        if k == roof_from and clocks is not None:
+            torch.cuda.synchronize()
+            torch.cuda.nvtx.range_pop()
         flush.fill_(k)  # evict the logits and tables from L2 between steps
         e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
         e0.record()
@@ -326,16 +336,16 @@ def engine_arm(args) -> None:
             engine.begin(restart_t[k], stream=stream)
             launches += timed
         engine.sync(slots, history, prompt[k], total[k], stream=stream)
-        e1.record()
+        if roof:
+            e1.record()
         engine.apply_mask(logits, slots, stream=stream)
         e2.record()
         launches += 2 * timed
         if timed:
             step_ms.append((e0, e2))
+        if roof:
             apply_ms.append((e1, e2))
     torch.cuda.synchronize()
-    if clocks is not None:
-        torch.cuda.nvtx.range_pop()
     clock_info = clocks.stop() if clocks else None
     errors = engine.errors()
     steps_ms = [a.elapsed_time(b) for a, b in step_ms]
@@ -349,7 +359,7 @@ def engine_arm(args) -> None:
     value = rows * world * args.steps / (job_ms / 1e3)
     # roofline of the apply kernel
     words = engine.words
-    timed_steps = range(args.warmup, total_steps)
+    timed_steps = range(roof_from, total_steps)
     bytes_per_launch = [rows * 4 * words + elt * int(disallowed[k]) for k in timed_steps]
     avg_apply_s = statistics.mean(applies) / 1e3
     achieved = statistics.mean(bytes_per_launch) / avg_apply_s / 1e9
@@ -369,7 +379,8 @@ def engine_arm(args) -> None:
         },
         "step_ms": {"median": statistics.median(steps_ms), "p90": sorted(steps_ms)[int(0.9 * len(steps_ms))],
                     "min": min(steps_ms)},
-        "apply_ms": {"median": statistics.median(applies), "mean": statistics.mean(applies)},
+        "apply_ms": {"median": statistics.median(applies), "mean": statistics.mean(applies),
+                     "steps": len(applies), "note": "separate steps after the K timed ones, event between sync and apply"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_kind": peak_kind, "traffic": None,
                      "kernel": f"apply_kernel<{elt}> ({cfg.dtype})",

@@ -22,8 +22,8 @@ namespace xg {
 
 constexpr int32_t kWarpsPerBlock = 1;  // one row per CTA: rows spread over every SM
 constexpr int32_t kApplyThreads = 256;
-constexpr int32_t kApplyBatch = 8;        // groups of 8 columns per thread per round
-constexpr int32_t kApplyCtasPerSm = 8;    // apply grid: about one full wave of CTAs
+constexpr int32_t kApplyBatch = 4;        // 1024-column segments whose loads a warp issues together
+constexpr int32_t kApplyCtasPerSm = 4;    // apply grid: CTAs per SM the row split aims at
 
 struct __align__(16) WarpShared {
   Key top[kTopCap];
@@ -158,12 +158,37 @@ __device__ __forceinline__ uint32_t allowed8(const uint32_t* base, const uint32_
   return static_cast<uint32_t>(x >> sh) & 0xffu;
 }
 
+__device__ __forceinline__ void store_neg8(char* at, uint32_t blocked, uint32_t neg, int elt) {
+  if (blocked == 0xffu) {
+    if (elt == 2) {
+      const uint32_t v = neg | (neg << 16);
+      *reinterpret_cast<uint4*>(at) = make_uint4(v, v, v, v);
+    } else {
+      *reinterpret_cast<uint4*>(at) = make_uint4(neg, neg, neg, neg);
+      *reinterpret_cast<uint4*>(at + 16) = make_uint4(neg, neg, neg, neg);
+    }
+    return;
+  }
+  for (int32_t k = 0; k < 8; ++k) {
+    if ((blocked >> k) & 1u) {
+      if (elt == 2)
+        *reinterpret_cast<uint16_t*>(at + 2 * k) = static_cast<uint16_t>(neg);
+      else
+        *reinterpret_cast<uint32_t*>(at + 4 * k) = neg;
+    }
+  }
+}
+
 // -inf into every disallowed column of every row of an active, non-error slot.
-// ELT: element bytes (2 or 4); neg: the element's -inf bit pattern.  A CTA owns a 1/chunks
-// share of one row, as groups of 8 columns starting at the row's first 16-byte boundary;
-// each thread takes kApplyBatch groups per round, issuing all of their mask reads before
-// any store (the stores may alias nothing the compiler can prove, so it would not hoist
-// the reads itself), and a warp's stores cover 512 contiguous bytes.
+// ELT: element bytes (2 or 4); neg: the element's -inf bit pattern.
+//
+// Work unit: a segment of 1024 columns, handled by one warp.  Each lane loads one mask
+// word (32 columns; base | delta), then for store j = 0..3 lane l takes the 8-column group
+// g = 32 j + l, fetching its byte of mask from the lane that loaded word g / 4 by shuffle,
+// so each store instruction of the warp writes 512 contiguous bytes (bf16) while the
+// mask costs one load per 32 columns.  A warp issues the loads of kApplyBatch segments
+// before any of their stores.  Rows whose first element is not 16-byte aligned take a
+// scalar path (contiguous vLLM logits rows always are).
 template <int ELT>
 __global__ void __launch_bounds__(kApplyThreads, 4)
     apply_kernel(const __grid_constant__ Tables t, char* logits, int32_t cols, int64_t stride,
@@ -177,57 +202,51 @@ __global__ void __launch_bounds__(kApplyThreads, 4)
   const uint32_t* delta = t.delta[slot];
   if (base == nullptr && delta == nullptr) return;  // error phase: untouched
   char* out = logits + static_cast<int64_t>(row) * stride * ELT;
-  const int32_t lead = static_cast<int32_t>(((16u - (reinterpret_cast<uintptr_t>(out) & 15u)) & 15u) / ELT);
   const int32_t words = t.words;
-  const int64_t groups = cols > lead ? (static_cast<int64_t>(cols) - lead + 7) / 8 : 0;
-  const int64_t share = (groups + chunks - 1) / chunks;
-  const int64_t g0 = chunk * share;
-  const int64_t g1 = g0 + share < groups ? g0 + share : groups;
-  for (int64_t round = g0 + threadIdx.x; round < g1; round += kApplyThreads * kApplyBatch) {
-    uint32_t allowed[kApplyBatch];
-#pragma unroll
-    for (int32_t b = 0; b < kApplyBatch; ++b) {
-      const int64_t g = round + b * kApplyThreads;
-      allowed[b] = g < g1 ? allowed8(base, delta, words, lead + 8 * g) : 0xffu;
-    }
-#pragma unroll
-    for (int32_t b = 0; b < kApplyBatch; ++b) {
-      const int64_t g = round + b * kApplyThreads;
-      if (g >= g1) break;
-      const int64_t c = lead + 8 * g;
-      uint32_t blocked = ~allowed[b] & 0xffu;
-      const int64_t left = cols - c;
-      if (left < 8) blocked &= (1u << left) - 1u;
-      if (blocked == 0u) continue;
-      char* at = out + c * ELT;
-      if (blocked == 0xffu) {
-        if (ELT == 2) {
-          const uint32_t v = neg | (neg << 16);
-          *reinterpret_cast<uint4*>(at) = make_uint4(v, v, v, v);
-        } else {
-          *reinterpret_cast<uint4*>(at) = make_uint4(neg, neg, neg, neg);
-          *reinterpret_cast<uint4*>(at + 16) = make_uint4(neg, neg, neg, neg);
-        }
-      } else {
-        for (int32_t k = 0; k < 8; ++k) {
-          if ((blocked >> k) & 1u) {
-            if (ELT == 2)
-              *reinterpret_cast<uint16_t*>(at + 2 * k) = static_cast<uint16_t>(neg);
-            else
-              *reinterpret_cast<uint32_t*>(at + 4 * k) = neg;
-          }
-        }
+  const int32_t lane = threadIdx.x & 31;
+  if ((reinterpret_cast<uintptr_t>(out) & 15u) != 0) {  // unaligned row: scalar path
+    const int64_t per = (cols + chunks - 1) / chunks;
+    const int64_t c0 = chunk * per, c1 = c0 + per < cols ? c0 + per : cols;
+    for (int64_t col = c0 + threadIdx.x; col < c1; col += blockDim.x) {
+      const bool ok = col < t.vocab && ((mask_word(base, delta, col >> 5) >> (col & 31)) & 1u);
+      if (!ok) {
+        if (ELT == 2)
+          *reinterpret_cast<uint16_t*>(out + 2 * col) = static_cast<uint16_t>(neg);
+        else
+          *reinterpret_cast<uint32_t*>(out + 4 * col) = neg;
       }
     }
+    return;
   }
-  if (chunk == 0 && static_cast<int32_t>(threadIdx.x) < lead && static_cast<int32_t>(threadIdx.x) < cols) {
-    const int32_t col = threadIdx.x;  // the columns before the first 16-byte boundary
-    const bool ok = col < t.vocab && ((mask_word(base, delta, col >> 5) >> (col & 31)) & 1u);
-    if (!ok) {
-      if (ELT == 2)
-        *reinterpret_cast<uint16_t*>(out + 2 * col) = static_cast<uint16_t>(neg);
-      else
-        *reinterpret_cast<uint32_t*>(out + 4 * col) = neg;
+  const int32_t segments = (cols + 1023) >> 10;
+  const int32_t share = (segments + chunks - 1) / chunks;
+  const int32_t s0 = chunk * share;
+  const int32_t s1 = s0 + share < segments ? s0 + share : segments;
+  const int32_t warp = threadIdx.x >> 5;
+  const int32_t warps = blockDim.x >> 5;
+  for (int32_t first = s0 + warp; first < s1; first += warps * kApplyBatch) {
+    uint32_t word[kApplyBatch];
+#pragma unroll
+    for (int32_t b = 0; b < kApplyBatch; ++b) {
+      const int32_t seg = first + b * warps;
+      const int64_t w = static_cast<int64_t>(seg) * 32 + lane;
+      word[b] = seg < s1 && w < words ? mask_word(base, delta, w) : 0u;  // past the vocabulary: blocked
+    }
+#pragma unroll
+    for (int32_t b = 0; b < kApplyBatch; ++b) {
+      const int32_t seg = first + b * warps;  // warp-uniform
+      if (seg >= s1) break;
+#pragma unroll
+      for (int32_t j = 0; j < 4; ++j) {
+        const int32_t g = 32 * j + lane;
+        const uint32_t holder = __shfl_sync(0xffffffffu, word[b], g >> 2);
+        const int64_t c = static_cast<int64_t>(seg) * 1024 + 8 * g;
+        if (c >= cols) continue;
+        uint32_t blocked = ~(holder >> (8 * (g & 3))) & 0xffu;
+        const int64_t left = cols - c;
+        if (left < 8) blocked &= (1u << left) - 1u;
+        if (blocked) store_neg8(out + c * ELT, blocked, neg, ELT);
+      }
     }
   }
 }
@@ -651,8 +670,7 @@ int xg_apply_mask(XgEngine* e, void* logits, int32_t dtype, int32_t rows, int32_
   if (reinterpret_cast<uintptr_t>(logits) % elt) return fail(XG_EINVAL, "logits are not aligned to their element size");
   // Split each row into `chunks` CTAs so that the grid is about one wave of resident CTAs
   // (each CTA then runs long enough to hide its few dependent pointer loads).
-  const int64_t groups = (static_cast<int64_t>(cols) + 7) / 8;
-  const int64_t per_row_max = (groups + kApplyThreads - 1) / kApplyThreads;
+  const int64_t per_row_max = ((static_cast<int64_t>(cols) + 1023) / 1024 + 7) / 8;  // >= 8 segments per CTA
   const int64_t wanted = (static_cast<int64_t>(e->sm_count) * kApplyCtasPerSm + rows - 1) / rows;
   const int32_t chunks = static_cast<int32_t>(wanted < 1 ? 1 : wanted > per_row_max ? (per_row_max < 1 ? 1 : per_row_max) : wanted);
   const int64_t blocks = static_cast<int64_t>(rows) * chunks;
