@@ -281,12 +281,10 @@ def engine_arm(args) -> None:
     sample_s = time.perf_counter() - t0
     del gen_engine
     # -- replay schedule -------------------------------------------------------------------
-    # W warm-up steps, K timed steps (events around each whole step), then R roofline steps
-    # with an extra event between sync and apply_mask so the apply kernel is timed alone
-    # (that event also stops the apply launch from overlapping the step kernel, so these
-    # steps are not part of the K).
-    roof_steps = min(64, args.steps)
-    total_steps = args.warmup + args.steps + roof_steps
+    # W warm-up steps, then K timed steps.  A step is begin(restarted slots) + sync_apply
+    # (sync and apply_mask fused in one kernel); events bracket the whole step, and a
+    # second pair brackets the sync_apply kernel alone (the roofline's kernel).
+    total_steps = args.warmup + args.steps
     assigned, restarts = schedule(lengths, rows, total_steps)
     history = torch.zeros((rows, total_steps + 1), dtype=torch.int32, device=device)
     disallowed = np.zeros(total_steps, dtype=np.int64)  # sum over rows of disallowed columns
@@ -315,10 +313,8 @@ def engine_arm(args) -> None:
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    roof_from = args.warmup + args.steps
     for k in range(total_steps):
-        timed = args.warmup <= k < roof_from
-        roof = k >= roof_from
+        timed = k >= args.warmup
         if timed and clocks is None:
             torch.cuda.synchronize()
             if world > 1:
@@ -326,26 +322,22 @@ def engine_arm(args) -> None:
             clocks = Clocks(local)
             time.sleep(0.3)
             torch.cuda.nvtx.range_push("timed")
-        if k == roof_from and clocks is not None:
-            torch.cuda.synchronize()
-            torch.cuda.nvtx.range_pop()
         flush.fill_(k)  # evict the logits and tables from L2 between steps
         e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
         e0.record()
         if restart_t[k] is not None:
             engine.begin(restart_t[k], stream=stream)
             launches += timed
-        engine.sync(slots, history, prompt[k], total[k], stream=stream)
-        if roof:
-            e1.record()
-        engine.apply_mask(logits, slots, stream=stream)
+        e1.record()
+        engine.sync_apply(slots, history, prompt[k], total[k], logits, stream=stream)
         e2.record()
-        launches += 2 * timed
+        launches += timed
         if timed:
             step_ms.append((e0, e2))
-        if roof:
             apply_ms.append((e1, e2))
     torch.cuda.synchronize()
+    if clocks is not None:
+        torch.cuda.nvtx.range_pop()
     clock_info = clocks.stop() if clocks else None
     errors = engine.errors()
     steps_ms = [a.elapsed_time(b) for a, b in step_ms]
@@ -359,8 +351,10 @@ def engine_arm(args) -> None:
     value = rows * world * args.steps / (job_ms / 1e3)
     # roofline of the apply kernel
     words = engine.words
-    timed_steps = range(roof_from, total_steps)
-    bytes_per_launch = [rows * 4 * words + elt * int(disallowed[k]) for k in timed_steps]
+    timed_steps = range(args.warmup, total_steps)
+    # algorithmic bytes of one sync_apply launch: per row the state read+write and token
+    # (516 B), the bitmask read once (4 * words) and the -inf stores (elt * disallowed)
+    bytes_per_launch = [rows * (516 + 4 * words) + elt * int(disallowed[k]) for k in timed_steps]
     avg_apply_s = statistics.mean(applies) / 1e3
     achieved = statistics.mean(bytes_per_launch) / avg_apply_s / 1e9
     peak, peak_kind = measured_peak()
@@ -379,11 +373,11 @@ def engine_arm(args) -> None:
         },
         "step_ms": {"median": statistics.median(steps_ms), "p90": sorted(steps_ms)[int(0.9 * len(steps_ms))],
                     "min": min(steps_ms)},
-        "apply_ms": {"median": statistics.median(applies), "mean": statistics.mean(applies),
-                     "steps": len(applies), "note": "separate steps after the K timed ones, event between sync and apply"},
+        "kernel_ms": {"median": statistics.median(applies), "mean": statistics.mean(applies),
+                      "note": "sync_apply kernel alone (events around it), over the K timed steps"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_kind": peak_kind, "traffic": None,
-                     "kernel": f"apply_kernel<{elt}> ({cfg.dtype})",
+                     "kernel": f"sync_apply_kernel<{elt}> ({cfg.dtype}): sync + mask + apply fused",
                      "algorithmic_bytes_per_launch": statistics.mean(bytes_per_launch)},
         "gpu_launches": launches,
         "clocks": clock_info,
@@ -426,8 +420,7 @@ def e2e_leg(engine, workload, history, restart_t, prompt, total, slots, rows, vo
         dev_logits.copy_(host_logits, non_blocking=True)
         if restart_t[k] is not None:
             engine.begin(restart_t[k], stream=stream)
-        engine.sync(slots, dev_hist, prompt[k], total[k], stream=stream)
-        engine.apply_mask(dev_logits, slots, stream=stream)
+        engine.sync_apply(slots, dev_hist, prompt[k], total[k], dev_logits, stream=stream)
         out_logits.copy_(dev_logits, non_blocking=True)
     end.record()
     torch.cuda.synchronize()

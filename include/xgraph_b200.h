@@ -169,6 +169,14 @@ XG_API int xg_memory_host(XgEngine* engine, int32_t sequences, int32_t* out);
  * slots in the error phase are left untouched.  logits: device, dtype XG_F32/XG_BF16/XG_F16,
  * rows x cols with row_stride elements between rows.  row_slots: device int32[rows].
  * local_pos/input_ids: device int32[rows] for speculative draft rows, or both NULL. */
+/* sync then apply_mask in one launch, for a step without speculative draft rows: logits row
+ * i belongs to slots[i] (rows x cols, row_stride elements apart); the other arguments are
+ * xg_sync's.  Same results as xg_sync followed by xg_apply_mask with row_slots = slots.
+ * The reference has no fused call (its adapter calls sync, then apply_mask). */
+XG_API int xg_sync_apply(XgEngine* engine, const int32_t* slots, int32_t count, const int32_t* history,
+                         int64_t history_stride, int64_t history_rows, const int32_t* prompt_len,
+                         const int32_t* total_len, int64_t lengths_count, void* logits, int32_t dtype,
+                         int32_t cols, int64_t row_stride, void* stream);
 XG_API int xg_apply_mask(XgEngine* engine, void* logits, int32_t dtype, int32_t rows, int32_t cols,
                   int64_t row_stride, const int32_t* row_slots, const int32_t* local_pos,
                   const int32_t* input_ids, void* stream);

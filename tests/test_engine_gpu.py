@@ -184,3 +184,36 @@ def test_out_of_range_arguments_raise_value_error():
         engine.advance(np.zeros(3, dtype=np.int32))
     with pytest.raises(ValueError):
         engine.begin(torch.arange(3, dtype=torch.int32, device="cuda"))
+
+
+@pytest.mark.parametrize("dtype", ["bfloat16", "float32"])
+def test_sync_apply_equals_sync_then_apply_mask(dtype):
+    """The fused step gives the states, masks and logits of sync followed by apply_mask."""
+    import torch
+
+    case = next(c for c in golden_walks() if c["name"] == "bpe_committed")
+    sequences = case["sequences"]
+    n = len(sequences)
+    fused, _, served = engine_for(case)
+    plain, _, _ = engine_for(case)
+    start(fused, sequences)
+    start(plain, sequences)
+    steps = len(sequences[0]["tokens"])
+    history = torch.zeros((n, steps), dtype=torch.int32, device="cuda")
+    for k, seq in enumerate(sequences):
+        history[k] = torch.tensor(seq["tokens"], dtype=torch.int32)
+    slots = torch.arange(n, dtype=torch.int32, device="cuda")
+    prompt_len = torch.zeros(n, dtype=torch.int32, device="cuda")
+    gen = torch.Generator(device="cuda").manual_seed(3)
+    for step in range(0, steps, 7):
+        total = torch.full((n,), min(step + 7, steps), dtype=torch.int32, device="cuda")
+        logits = torch.randn((n, served.vocab_size + 9), generator=gen, device="cuda").to(getattr(torch, dtype))
+        a, b = logits.clone(), logits.clone()
+        fused.sync_apply(slots, history, prompt_len, total, a)
+        plain.sync(slots, history, prompt_len, total)
+        plain.apply_mask(b, slots)
+        assert torch.equal(a.view(torch.int16 if dtype == "bfloat16" else torch.int32),
+                           b.view(torch.int16 if dtype == "bfloat16" else torch.int32)), step
+        sa, sb = fused.states_host(), plain.states_host()
+        for field in sa:
+            np.testing.assert_array_equal(sa[field], sb[field], field)

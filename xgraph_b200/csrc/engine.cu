@@ -24,6 +24,7 @@ constexpr int32_t kWarpsPerBlock = 1;  // one row per CTA: rows spread over ever
 constexpr int32_t kApplyThreads = 256;
 constexpr int32_t kApplyBatch = 4;        // 1024-column segments whose loads a warp issues together
 constexpr int32_t kApplyCtasPerSm = 4;    // apply grid: CTAs per SM the row split aims at
+constexpr int32_t kFusedThreads = 256;    // sync_apply: warp 0 advances, all 8 warps write
 
 struct __align__(16) WarpShared {
   Key top[kTopCap];
@@ -179,16 +180,66 @@ __device__ __forceinline__ void store_neg8(char* at, uint32_t blocked, uint32_t 
   }
 }
 
-// -inf into every disallowed column of every row of an active, non-error slot.
-// ELT: element bytes (2 or 4); neg: the element's -inf bit pattern.
+// -inf into the disallowed columns of segments [s0, s1) (1024 columns each) of one
+// logits row whose first element is 16-byte aligned; the calling warps split them.
 //
-// Work unit: a segment of 1024 columns, handled by one warp.  Each lane loads one mask
-// word (32 columns; base | delta), then for store j = 0..3 lane l takes the 8-column group
-// g = 32 j + l, fetching its byte of mask from the lane that loaded word g / 4 by shuffle,
-// so each store instruction of the warp writes 512 contiguous bytes (bf16) while the
-// mask costs one load per 32 columns.  A warp issues the loads of kApplyBatch segments
-// before any of their stores.  Rows whose first element is not 16-byte aligned take a
-// scalar path (contiguous vLLM logits rows always are).
+// Each lane loads one mask word (32 columns; base | delta), then for store j = 0..3 lane l
+// takes the 8-column group g = 32 j + l, fetching its byte of mask from the lane that
+// loaded word g / 4 by shuffle, so each store instruction of the warp writes 512
+// contiguous bytes (bf16) while the mask costs one load per 32 columns.  A warp issues
+// the loads of kApplyBatch segments before any of their stores (the stores may alias
+// nothing the compiler can prove, so it would not hoist the loads itself).
+template <int ELT>
+__device__ __forceinline__ void apply_segments(const Tables& t, char* out, int32_t cols, const uint32_t* base,
+                                               const uint32_t* delta, uint32_t neg, int32_t s0, int32_t s1,
+                                               int32_t warp, int32_t warps) {
+  const int32_t lane = threadIdx.x & 31;
+  const int32_t words = t.words;
+  for (int32_t first = s0 + warp; first < s1; first += warps * kApplyBatch) {
+    uint32_t word[kApplyBatch];
+#pragma unroll
+    for (int32_t b = 0; b < kApplyBatch; ++b) {
+      const int32_t seg = first + b * warps;
+      const int32_t w = seg * 32 + lane;
+      word[b] = seg < s1 && w < words ? mask_word(base, delta, w) : 0u;  // past the vocabulary: blocked
+    }
+#pragma unroll
+    for (int32_t b = 0; b < kApplyBatch; ++b) {
+      const int32_t seg = first + b * warps;  // warp-uniform
+      if (seg >= s1) break;
+#pragma unroll
+      for (int32_t j = 0; j < 4; ++j) {
+        const int32_t g = 32 * j + lane;
+        const uint32_t holder = __shfl_sync(0xffffffffu, word[b], g >> 2);
+        const int32_t c = seg * 1024 + 8 * g;
+        if (c >= cols) continue;
+        uint32_t blocked = ~(holder >> (8 * (g & 3))) & 0xffu;
+        const int32_t left = cols - c;
+        if (left < 8) blocked &= (1u << left) - 1u;
+        if (blocked) store_neg8(out + static_cast<int64_t>(c) * ELT, blocked, neg, ELT);
+      }
+    }
+  }
+}
+
+// Columns [c0, c1) of a row whose start is not 16-byte aligned, one element per thread.
+template <int ELT>
+__device__ __forceinline__ void apply_scalar(const Tables& t, char* out, int64_t c0, int64_t c1,
+                                             const uint32_t* base, const uint32_t* delta, uint32_t neg) {
+  for (int64_t col = c0 + threadIdx.x; col < c1; col += blockDim.x) {
+    const bool ok = col < t.vocab && ((mask_word(base, delta, col >> 5) >> (col & 31)) & 1u);
+    if (!ok) {
+      if (ELT == 2)
+        *reinterpret_cast<uint16_t*>(out + 2 * col) = static_cast<uint16_t>(neg);
+      else
+        *reinterpret_cast<uint32_t*>(out + 4 * col) = neg;
+    }
+  }
+}
+
+// apply_mask: -inf into every disallowed column of every row of an active, non-error
+// slot; a CTA owns a 1/chunks share of one row.  ELT: element bytes (2 or 4); neg: the
+// element's -inf bit pattern.
 template <int ELT>
 __global__ void __launch_bounds__(kApplyThreads, 4)
     apply_kernel(const __grid_constant__ Tables t, char* logits, int32_t cols, int64_t stride,
@@ -202,53 +253,54 @@ __global__ void __launch_bounds__(kApplyThreads, 4)
   const uint32_t* delta = t.delta[slot];
   if (base == nullptr && delta == nullptr) return;  // error phase: untouched
   char* out = logits + static_cast<int64_t>(row) * stride * ELT;
-  const int32_t words = t.words;
-  const int32_t lane = threadIdx.x & 31;
-  if ((reinterpret_cast<uintptr_t>(out) & 15u) != 0) {  // unaligned row: scalar path
+  if ((reinterpret_cast<uintptr_t>(out) & 15u) != 0) {
     const int64_t per = (cols + chunks - 1) / chunks;
-    const int64_t c0 = chunk * per, c1 = c0 + per < cols ? c0 + per : cols;
-    for (int64_t col = c0 + threadIdx.x; col < c1; col += blockDim.x) {
-      const bool ok = col < t.vocab && ((mask_word(base, delta, col >> 5) >> (col & 31)) & 1u);
-      if (!ok) {
-        if (ELT == 2)
-          *reinterpret_cast<uint16_t*>(out + 2 * col) = static_cast<uint16_t>(neg);
-        else
-          *reinterpret_cast<uint32_t*>(out + 4 * col) = neg;
-      }
-    }
+    const int64_t c0 = chunk * per;
+    apply_scalar<ELT>(t, out, c0, c0 + per < cols ? c0 + per : cols, base, delta, neg);
     return;
   }
   const int32_t segments = (cols + 1023) >> 10;
   const int32_t share = (segments + chunks - 1) / chunks;
   const int32_t s0 = chunk * share;
-  const int32_t s1 = s0 + share < segments ? s0 + share : segments;
-  const int32_t warp = threadIdx.x >> 5;
-  const int32_t warps = blockDim.x >> 5;
-  for (int32_t first = s0 + warp; first < s1; first += warps * kApplyBatch) {
-    uint32_t word[kApplyBatch];
-#pragma unroll
-    for (int32_t b = 0; b < kApplyBatch; ++b) {
-      const int32_t seg = first + b * warps;
-      const int64_t w = static_cast<int64_t>(seg) * 32 + lane;
-      word[b] = seg < s1 && w < words ? mask_word(base, delta, w) : 0u;  // past the vocabulary: blocked
+  apply_segments<ELT>(t, out, cols, base, delta, neg, s0, s0 + share < segments ? s0 + share : segments,
+                      threadIdx.x >> 5, blockDim.x >> 5);
+}
+
+// sync + apply_mask fused for the step where logits row i belongs to slots[i] (no draft
+// rows): warp 0 of CTA i consumes the slot's new history tokens and rebuilds its mask, then
+// all warps of the CTA write the row's -inf.  One launch per decoding step; a row's stores
+// overlap other rows' state-machine latency.
+template <int ELT>
+__global__ void __launch_bounds__(kFusedThreads)
+    sync_apply_kernel(const __grid_constant__ Tables t, const StepArgs a, char* logits, int32_t cols,
+                      int64_t stride, uint32_t neg) {
+  __shared__ WarpShared shared;
+  const int32_t i = blockIdx.x;
+  const int32_t slot = a.slots[i];
+  if (!t.active[slot]) return;  // block-uniform: inactive rows are neither advanced nor masked
+  if (threadIdx.x < 32) {
+    Ctx c = make_ctx(t, slot, shared);
+    int32_t cursor = t.cursors[slot] < 0 ? a.prompt_len[slot] : t.cursors[slot];
+    const int32_t end = a.total_len[slot];
+    if (cursor < end) {
+      XgState s = t.states[slot];
+      const int32_t* tokens = a.history + a.stride * slot;
+      for (; cursor < end; ++cursor) advance_state(c, s, tokens[cursor]);
+      store_state(t, slot, s);
+      build_mask(c, s);
     }
-#pragma unroll
-    for (int32_t b = 0; b < kApplyBatch; ++b) {
-      const int32_t seg = first + b * warps;  // warp-uniform
-      if (seg >= s1) break;
-#pragma unroll
-      for (int32_t j = 0; j < 4; ++j) {
-        const int32_t g = 32 * j + lane;
-        const uint32_t holder = __shfl_sync(0xffffffffu, word[b], g >> 2);
-        const int64_t c = static_cast<int64_t>(seg) * 1024 + 8 * g;
-        if (c >= cols) continue;
-        uint32_t blocked = ~(holder >> (8 * (g & 3))) & 0xffu;
-        const int64_t left = cols - c;
-        if (left < 8) blocked &= (1u << left) - 1u;
-        if (blocked) store_neg8(out + c * ELT, blocked, neg, ELT);
-      }
-    }
+    if (threadIdx.x == 0) t.cursors[slot] = cursor;
   }
+  __syncthreads();
+  const uint32_t* base = t.base[slot];
+  const uint32_t* delta = t.delta[slot];
+  if (base == nullptr && delta == nullptr) return;  // error phase: untouched
+  char* out = logits + static_cast<int64_t>(i) * stride * ELT;
+  if ((reinterpret_cast<uintptr_t>(out) & 15u) != 0) {
+    apply_scalar<ELT>(t, out, 0, cols, base, delta, neg);
+    return;
+  }
+  apply_segments<ELT>(t, out, cols, base, delta, neg, 0, (cols + 1023) >> 10, threadIdx.x >> 5, blockDim.x >> 5);
 }
 
 }  // namespace xg
@@ -655,6 +707,38 @@ int xg_memory_host(XgEngine* e, int32_t sequences, int32_t* out) {
   if (!e || (!out && sequences)) return fail(XG_EINVAL, "null argument");
   if (sequences < 0 || sequences > e->max_sequences) return fail(XG_EINVAL, "sequences out of range");
   return copy_host(out, e->memory, static_cast<size_t>(sequences) * e->t.memory_ints * sizeof(int32_t));
+}
+
+int xg_sync_apply(XgEngine* e, const int32_t* slots, int32_t count, const int32_t* history, int64_t history_stride,
+                  int64_t history_rows, const int32_t* prompt_len, const int32_t* total_len, int64_t lengths_count,
+                  void* logits, int32_t dtype, int32_t cols, int64_t row_stride, void* stream) {
+  if (!e) return fail(XG_EINVAL, "null engine");
+  if (count < 0 || count > e->max_sequences) return fail(XG_EINVAL, "more slots than max_sequences");
+  if (lengths_count < e->max_sequences) return fail(XG_EINVAL, "prompt_len and total_len need one entry per slot");
+  if (history_rows < e->max_sequences || history_stride < 0)
+    return fail(XG_EINVAL, "history needs one contiguous row per slot");
+  if (cols < 0 || row_stride < cols) return fail(XG_EINVAL, "logits need one contiguous row per slot");
+  if (dtype != XG_F32 && dtype != XG_BF16 && dtype != XG_F16) return fail(XG_EINVAL, "logits must be float32, bfloat16 or float16");
+  if (count == 0) return XG_OK;
+  if (!slots || !history || !prompt_len || !total_len || !logits) return fail(XG_EINVAL, "null argument");
+  const int elt = dtype == XG_F32 ? 4 : 2;
+  if (reinterpret_cast<uintptr_t>(logits) % elt) return fail(XG_EINVAL, "logits are not aligned to their element size");
+  StepArgs a{};
+  a.slots = slots;
+  a.history = history;
+  a.stride = history_stride;
+  a.prompt_len = prompt_len;
+  a.total_len = total_len;
+  a.count = count;
+  cudaStream_t s = as_stream(stream);
+  char* data = static_cast<char*>(logits);
+  if (dtype == XG_F32)
+    sync_apply_kernel<4><<<count, kFusedThreads, 0, s>>>(e->t, a, data, cols, row_stride, 0xff800000u);
+  else
+    sync_apply_kernel<2><<<count, kFusedThreads, 0, s>>>(e->t, a, data, cols, row_stride,
+                                                         dtype == XG_BF16 ? 0xff80u : 0xfc00u);
+  XG_CUDA(cudaGetLastError(), "sync_apply kernel");
+  return XG_OK;
 }
 
 int xg_apply_mask(XgEngine* e, void* logits, int32_t dtype, int32_t rows, int32_t cols, int64_t row_stride,

@@ -99,6 +99,7 @@ def load_library(path: Path = LIBRARY):
         "xg_states_host": ([p, i32, p], ctypes.c_int),
         "xg_memory_host": ([p, i32, p], ctypes.c_int),
         "xg_apply_mask": ([p, p, i32, i32, i32, i64, p, p, p, p], ctypes.c_int),
+        "xg_sync_apply": ([p, p, i32, p, i64, i64, p, p, i64, p, i32, i32, i64, p], ctypes.c_int),
     }
     for name, (args, res) in sigs.items():
         fn = getattr(lib, name)
@@ -355,6 +356,32 @@ class Engine:
             self._handle, ptr, n, ctypes.c_void_p(history.data_ptr()), history.stride(0), history.shape[0],
             ctypes.c_void_p(prompt_len.data_ptr()), ctypes.c_void_p(total_len.data_ptr()),
             min(len(prompt_len), len(total_len)), _stream(stream)))
+
+    def sync_apply(self, slots, history, prompt_len, total_len, logits, stream: int = 0) -> None:
+        """`sync` then `apply_mask(logits, slots)` in one kernel launch, for a step without
+        speculative draft rows (logits row i belongs to slots[i])."""
+        import torch
+
+        ptr, n = self._slots(slots)
+        for name, lengths in (("prompt_len", prompt_len), ("total_len", total_len)):
+            _device_ptr(lengths, name, ndim=1, dtype=torch.int32)
+            if len(lengths) < self.max_sequences:
+                raise ValueError("prompt_len and total_len need one entry per slot")
+        _device_ptr(history, "history", ndim=2, dtype=torch.int32)
+        if history.shape[0] < self.max_sequences or history.stride(1) != 1:
+            raise ValueError("history needs one contiguous row per slot")
+        if not isinstance(logits, torch.Tensor) or not logits.is_cuda or logits.dim() != 2:
+            raise ValueError("logits must be a 2-D tensor on the GPU")
+        dtype = DTYPES.get(str(logits.dtype).removeprefix("torch."))
+        if dtype is None:
+            raise ValueError("logits must be float32, bfloat16 or float16")
+        if logits.shape[0] != n or (logits.shape[1] > 1 and logits.stride(1) != 1):
+            raise ValueError("logits need one contiguous row per entry of slots")
+        _check(self._lib.xg_sync_apply(
+            self._handle, ptr, n, ctypes.c_void_p(history.data_ptr()), history.stride(0), history.shape[0],
+            ctypes.c_void_p(prompt_len.data_ptr()), ctypes.c_void_p(total_len.data_ptr()),
+            min(len(prompt_len), len(total_len)), ctypes.c_void_p(logits.data_ptr()), dtype, logits.shape[1],
+            logits.stride(0) if n > 1 else logits.shape[1], _stream(stream)))
 
     def apply_mask(self, logits, row_slots, stream: int = 0, *, local_pos=None, input_ids=None) -> None:
         """Set every logit its slot's mask disallows (and every column past the served
