@@ -16,12 +16,18 @@
 
 #include "layout.h"
 
+// XG_HD: small helpers, inlined.  XG_COLD: the rare, heavy transitions (closing a span,
+// changing segment, frontiers, sorts), kept out of line so that the per-token hot path
+// stays a few kilobytes of code: a decode step starts with a cold instruction cache, and
+// every fetch of a cold code line costs an HBM round trip.
 #if defined(__CUDACC__)
 #define XG_HD __device__ __forceinline__
+#define XG_COLD __device__ __noinline__
 #define XG_GPU 1
 #else
 #include <algorithm>
 #define XG_HD inline
+#define XG_COLD inline
 #define XG_GPU 0
 #endif
 
@@ -220,7 +226,7 @@ struct TopSet {
 };
 
 // Sorts buf[0, n) ascending; entries from n to the sorted width are set to max_key().
-XG_HD void top_sort(const Warp& w, Key* buf, int32_t n) {
+XG_COLD void top_sort(const Warp& w, Key* buf, int32_t n) {
 #if XG_GPU
   int32_t width = 32;
   while (width < n) width <<= 1;
@@ -252,7 +258,7 @@ XG_HD void top_sort(const Warp& w, Key* buf, int32_t n) {
 
 // Sorted buf[0, n) -> its first `limit` entries that are distinct (by full key, or by
 // the high 32 bits of a when by_high); returns how many were kept.
-XG_HD int32_t top_unique(const Warp& w, Key* buf, int32_t n, int32_t limit, bool by_high) {
+XG_COLD int32_t top_unique(const Warp& w, Key* buf, int32_t n, int32_t limit, bool by_high) {
 #if XG_GPU
   int32_t out = 0;
   Key carry = max_key();
@@ -292,7 +298,7 @@ XG_HD int32_t top_unique(const Warp& w, Key* buf, int32_t n, int32_t limit, bool
 #endif
 }
 
-XG_HD void top_compact(const Warp& w, TopSet& ts, int32_t mode) {
+XG_COLD void top_compact(const Warp& w, TopSet& ts, int32_t mode) {
   if (mode == kEntity) {
     // (rank, row) -> (row, rank): the least rank of each entity comes first.
     warp_for(w, 0, ts.n, [&](int32_t i) {
@@ -618,7 +624,7 @@ XG_HD void set_have(const Ctx& c, int32_t n, E entity) {
 // most 64 edges were found no cap applies and no sort is needed: the keys stay as found,
 // an entity possibly more than once (once per rank it is reached with).  Every reader
 // treats the list as a set with least ranks, so the duplicates change nothing.
-XG_HD int32_t next_frontier(const Ctx& c, int32_t rlo, int32_t rhi) {
+XG_COLD int32_t next_frontier(const Ctx& c, int32_t rlo, int32_t rhi) {
   const Tables& t = c.t;
   const int32_t version = version_of(c);
   const int32_t* ents = c.mem + kMemFrontierEnt;
@@ -652,7 +658,7 @@ XG_HD int32_t next_frontier(const Ctx& c, int32_t rlo, int32_t rhi) {
 
 // Keep, in c.top[0, n), the keys of the least rank present (committed paths resolve to
 // what the best start reaches, src/xgraph/oracle.py:1160-1162); returns how many.
-XG_HD int32_t keep_least_rank(const Ctx& c, int32_t n) {
+XG_COLD int32_t keep_least_rank(const Ctx& c, int32_t n) {
   const Key least = warp_min(c.w, 0, n, [&](int32_t i) { return Key{c.top[i].a >> 32, 0u, 0u}; });
 #if XG_GPU
   int32_t out = 0;
@@ -678,7 +684,7 @@ XG_HD int32_t keep_least_rank(const Ctx& c, int32_t n) {
 // The rows of the entities whose first rows are given by keys c.top[0, n) (low 32 bits of
 // a), sorted, first 64 (src/xgraph/oracle.py:697-703 _rows_for, capped as reached).
 // Writes them to the slot's reached list.
-XG_HD void reach_rows_of_top(const Ctx& c, int32_t n) {
+XG_COLD void reach_rows_of_top(const Ctx& c, int32_t n) {
   const Tables& t = c.t;
   int32_t* firsts = c.scratch + 2 * kMaxSet + 2 + 2 * kMaxSet;  // after starts/ptrs
   warp_for(c.w, 0, n, [&](int32_t i) { firsts[i] = static_cast<int32_t>(c.top[i].a & 0xffffffffu); });
@@ -701,7 +707,7 @@ XG_HD void reach_rows_of_top(const Ctx& c, int32_t n) {
 }
 
 // Write the frontier held as ENTITY keys in c.top[0, n) into slot memory.
-XG_HD void store_frontier(const Ctx& c, int32_t n) {
+XG_COLD void store_frontier(const Ctx& c, int32_t n) {
   const Tables& t = c.t;
   int32_t* ents = c.mem + kMemFrontierEnt;
   int32_t* ranks = c.mem + kMemFrontierRank;
@@ -725,7 +731,7 @@ XG_HD bool subject_candidate(const Ctx& c, bool bound, int32_t row) {
 
 // Whether the flags' "separator after a relation" holds in path mode: some entity of the
 // capped next frontier has triples.
-XG_HD bool frontier_goes_on(const Ctx& c, int32_t rlo, int32_t rhi) {
+XG_COLD bool frontier_goes_on(const Ctx& c, int32_t rlo, int32_t rhi) {
   const int32_t n = next_frontier(c, rlo, rhi);
   const int32_t version = version_of(c);
   const Tables& t = c.t;
@@ -799,7 +805,7 @@ XG_HD void end_span(XgState& s, int32_t phase) {
 }
 
 // The separator completed after the label rows [llo, lhi) (src/xgraph/oracle.py:1805-1922).
-XG_HD void next_segment(const Ctx& c, XgState& s, int32_t llo, int32_t lhi) {
+XG_COLD void next_segment(const Ctx& c, XgState& s, int32_t llo, int32_t lhi) {
   const Tables& t = c.t;
   const int32_t version = version_of(c);
   if (s.segment == kSubject) {
@@ -887,7 +893,7 @@ XG_HD void next_segment(const Ctx& c, XgState& s, int32_t llo, int32_t lhi) {
 }
 
 // The closer completed after the label rows [llo, lhi) (src/xgraph/oracle.py:1115-1214).
-XG_HD void close_span(const Ctx& c, XgState& s, int32_t llo, int32_t lhi) {
+XG_COLD void close_span(const Ctx& c, XgState& s, int32_t llo, int32_t lhi) {
   const Tables& t = c.t;
   const int32_t version = version_of(c);
   if (s.segment == kRelation) {  // a path ends
@@ -1104,7 +1110,7 @@ XG_HD void add_delimiter(const Warp& w, const Delim& d, int32_t pos, uint32_t* o
 
 // Label tokens that keep a live label branch alive: the column at `depth` of every
 // candidate row in [lo, hi) that continues past it.
-XG_HD void add_label_tokens(const Ctx& c, const XgState& s, uint32_t* out) {
+XG_COLD void add_label_tokens(const Ctx& c, const XgState& s, uint32_t* out) {
   const Tables& t = c.t;
   const int32_t d = s.depth, lo = s.lo, hi = s.hi;
   if (s.segment == kSubject) {
