@@ -231,35 +231,22 @@ def engine_arm(args) -> None:
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900), device_id=device)
     # -- index: built once on rank 0, device tables broadcast over NCCL --------------------
+    build_s = 0.0
+    workload = packed = None
     if rank == 0:
         t0 = time.perf_counter()
         workload = make_workload(args.config, args.seed)
+        packed = pack_tables(workload.index, workload.served, workload.syntax, escapes=True)
         build_s = time.perf_counter() - t0
-    else:
-        workload, build_s = None, 0.0
     if world > 1:
-        box = [workload]
-        dist.broadcast_object_list(box, src=0, device=device)
-        workload = box[0]
+        from xgraph_b200.replicas import broadcast_index
+
+        replica = broadcast_index(workload, packed, device)
+        workload, blob, meta = replica.payload, replica.blob, replica.packed
+    else:
+        blob, meta = torch.from_numpy(packed.blob).to(device), packed
     cfg = workload.config
     options = dict(cfg.options)
-    if rank == 0:
-        packed = pack_tables(workload.index, workload.served, workload.syntax, escapes=True)
-        blob = torch.from_numpy(packed.blob).to(device)
-        meta = packed
-    else:
-        meta = None
-    if world > 1:
-        box = [meta if rank == 0 else None]
-        if rank == 0:
-            box[0] = type(meta)(blob=np.zeros(0, np.uint8), layout=meta.layout, words=meta.words,
-                                words_padded=meta.words_padded)
-        dist.broadcast_object_list(box, src=0, device=device)
-        meta = box[0] if rank != 0 else meta
-        size = torch.tensor([meta.layout.blob_bytes], dtype=torch.int64, device=device)
-        if rank != 0:
-            blob = torch.empty(int(size.item()), dtype=torch.uint8, device=device)
-        dist.broadcast(blob, src=0)
     rows = cfg.rows
     pool = 2 * rows
     gen_engine = Engine(workload.index, workload.served, workload.syntax, pool, device_blob=(blob, meta), **options)
