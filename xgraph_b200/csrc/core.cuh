@@ -79,12 +79,20 @@ struct Rows {
   int32_t cols;
 };
 
+
+// A span delimiter inside spans: per byte position p, the sorted tokens continuing it
+// from p and where they end.  The CSR offsets of the first positions are also carried
+// by value (`at`, kernel-parameter space) so the mask builder reads no offset from memory.
 struct Delim {
   const int32_t* off;
   const int32_t* tok;
   const int32_t* next;
   int32_t len;
+  int32_t at[17];  // off[0 .. min(len, 16)]
 };
+
+XG_HD int32_t delim_begin(const Delim& d, int32_t pos) { return pos < 17 ? d.at[pos] : d.off[pos]; }
+XG_HD int32_t delim_end(const Delim& d, int32_t pos) { return pos + 1 < 17 ? d.at[pos + 1] : d.off[pos + 1]; }
 
 // Device (or host-seam) view of the packed tables plus the per-slot buffers.
 struct Tables {
@@ -973,7 +981,7 @@ XG_COLD void close_span(const Ctx& c, XgState& s, int32_t llo, int32_t lhi) {
 XG_HD int32_t delim_next(const Tables& t, uint64_t packed, int32_t which, int32_t pos, int32_t token);
 
 XG_HD int32_t delim_step(const Delim& d, int32_t pos, int32_t token) {
-  const int32_t a = d.off[pos], b = d.off[pos + 1];
+  const int32_t a = delim_begin(d, pos), b = delim_end(d, pos);
   const int32_t at = lower_index(d.tok, a, b, token);
   return at < b && d.tok[at] == token ? d.next[at] : -1;
 }
@@ -1105,7 +1113,7 @@ XG_HD const uint32_t* wide_mask(const Tables& t, int32_t lo, int32_t depth) {
 }
 
 XG_HD void add_delimiter(const Warp& w, const Delim& d, int32_t pos, uint32_t* out) {
-  warp_for(w, d.off[pos], d.off[pos + 1], [&](int32_t i) { set_bit(out, d.tok[i]); });
+  warp_for(w, delim_begin(d, pos), delim_end(d, pos), [&](int32_t i) { set_bit(out, d.tok[i]); });
 }
 
 // Label tokens that keep a live label branch alive: the column at `depth` of every

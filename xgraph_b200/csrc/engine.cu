@@ -383,6 +383,18 @@ int check_layout(const XgLayout& l) {
   return XG_OK;
 }
 
+// The first CSR offsets of a delimiter's lists, read from the blob wherever it lives.
+int fill_delimiter_offsets(Delim& d, const char* blob, int64_t offset, const void* host_blob) {
+  const int32_t n = (d.len + 1) < 17 ? d.len + 1 : 17;
+  for (int32_t k = 0; k < 17; ++k) d.at[k] = 0;
+  if (host_blob) {
+    std::memcpy(d.at, static_cast<const char*>(host_blob) + offset, n * sizeof(int32_t));
+    return XG_OK;
+  }
+  XG_CUDA(cudaMemcpy(d.at, blob + offset, n * sizeof(int32_t), cudaMemcpyDeviceToHost), "delimiter offsets");
+  return XG_OK;
+}
+
 void bind_tables(XgEngine* e) {
   const XgLayout& l = e->layout;
   const char* b = e->blob;
@@ -499,6 +511,16 @@ int create(const void* blob, bool on_device, const XgLayout* layout, const XgOpt
     return cuda_fail(err, "engine upload");
   }
   bind_tables(e);
+  {
+    const void* host = on_device ? nullptr : blob;
+    int rc = fill_delimiter_offsets(e->t.closer, e->blob, layout->closer_off, host);
+    if (!rc) rc = fill_delimiter_offsets(e->t.separator, e->blob, layout->separator_off, host);
+    if (!rc) rc = fill_delimiter_offsets(e->t.escape, e->blob, layout->escape_off, host);
+    if (rc) {
+      release(e);
+      return rc;
+    }
+  }
   begin_kernel<<<static_cast<unsigned>((slots + 127) / 128), 128>>>(e->t, nullptr, max_sequences, 0, max_sequences);
   err = cudaGetLastError();
   if (err == cudaSuccess) err = cudaDeviceSynchronize();

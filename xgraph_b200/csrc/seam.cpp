@@ -80,6 +80,9 @@ SeamEngine* xgs_create(const void* blob, const XgLayout* l, const XgOptions* o, 
   t.separator = Delim{at<int32_t>(b, l->separator_off), at<int32_t>(b, l->separator_tok), at<int32_t>(b, l->separator_next),
                       l->separator_len};
   t.escape = Delim{at<int32_t>(b, l->escape_off), at<int32_t>(b, l->escape_tok), at<int32_t>(b, l->escape_next), l->escape_len};
+  for (Delim* d : {&t.closer, &t.separator, &t.escape}) {
+    for (int32_t k = 0; k < 17; ++k) d->at[k] = k <= d->len ? d->off[k] : 0;
+  }
   t.dstep = at<uint64_t>(b, l->dstep);
   t.ver_off = at<int32_t>(b, l->ver_off);
   t.ver_subj = at<int32_t>(b, l->ver_subj);
