@@ -95,6 +95,7 @@ typedef struct XgLayout {
   int64_t escape_off, escape_tok, escape_next;
   int64_t ver_off, ver_subj, ver_adj, ver_edge_rel, ver_edge_obj;
   int64_t dstep;  /* uint64 [vocab]: packed next positions of every delimiter byte position, or -1 */
+  int64_t row_degree;  /* int32 [entity_rows]: base-KG adjacency entries of each label row's owner */
 } XgLayout;
 
 /* Span-language policies, as the reference Engine's constructor flags

@@ -98,6 +98,7 @@ XG_HD int32_t delim_end(const Delim& d, int32_t pos) { return pos + 1 < 17 ? d.a
 struct Tables {
   Rows ent, rel;
   const int32_t* ent_first_row;
+  const int32_t* row_degree;   // base-KG degree of each label row's owner (one load, no owner hop)
   const int32_t* ent_rows_off;
   const int32_t* ent_rows;
   const int32_t* adj_off;
@@ -481,6 +482,20 @@ XG_HD void relation_slice(const Edges& g, int32_t relation, int32_t& first, int3
 
 XG_HD int32_t degree(const Tables& t, int32_t version, int32_t e) { return edges_of(t, version, e).n; }
 
+// Degree of a label row's owner in the slot's KG version: the row-indexed base table when
+// the slot reads the base KG, else the version's list for edited subjects.
+XG_HD int32_t row_degree(const Tables& t, int32_t version, int32_t row) {
+  return version == 0 ? t.row_degree[row] : degree(t, version, t.ent.owner[row]);
+}
+
+XG_HD void prefetch_l1(const void* p) {
+#if XG_GPU
+  asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
+#else
+  (void)p;
+#endif
+}
+
 // Best-connected order key (src/xgraph/oracle.py:1736-1747): most sitelinks (with the
 // sitelink rank), then most adjacency entries in the slot's version, then first row.
 XG_HD Key connected_key(const Tables& t, int32_t version, int32_t row) {
@@ -774,7 +789,7 @@ XG_HD void set_flags(const Ctx& c, XgState& s) {
     if (s.segment == kSubject) {
       const int32_t version = version_of(c);
       separates = !answers_path(t, s) && warp_any(c.w, s.lo, s.ex_hi, [&](int32_t row) {
-                    return subject_candidate(c, bound, row) && degree(t, version, t.ent.owner[row]) > 0;
+                    return subject_candidate(c, bound, row) && row_degree(t, version, row) > 0;
                   });
     } else if (s.segment == kRelation) {
       separates = !t.paths || (s.hops < kMaxHops && frontier_goes_on(c, s.lo, s.ex_hi));
@@ -1059,6 +1074,37 @@ XG_HD void advance_span(const Ctx& c, XgState& s, int32_t token) {
     s.lo = s.hi = -1;
   }
   set_flags(c, s);
+}
+
+// Start the loads a label step in this state will need (the current range's columns at the
+// typed depth and the next, owners and row degrees, the slot's memory row, the delimiter
+// lists) before the token that drives it is known: none depends on the token, and each
+// would otherwise be a cold dependent load on the step's critical path.
+XG_HD void prefetch_span(const Ctx& c, const XgState& s) {
+#if XG_GPU
+  const Tables& t = c.t;
+  const int32_t lane = c.w.lane;
+  const int32_t mem_lines = (t.memory_ints + 31) >> 5;
+  if (lane < mem_lines) prefetch_l1(c.mem + lane * 32);
+  if (lane < 3) {
+    const Delim& d = lane == 0 ? t.closer : lane == 1 ? t.separator : t.escape;
+    prefetch_l1(d.tok + d.at[0]);
+  }
+  if (s.lo < 0 || s.hi - s.lo > 64) return;
+  const Rows& r = s.segment == kRelation ? t.rel : t.ent;
+  for (int32_t row = s.lo + lane; row < s.hi; row += 32) {
+    if (s.depth < r.cols) prefetch_l1(r.col + static_cast<int64_t>(s.depth) * r.count + row);
+    if (s.depth + 1 < r.cols) prefetch_l1(r.col + static_cast<int64_t>(s.depth + 1) * r.count + row);
+    prefetch_l1(r.owner + row);
+    if (s.segment == kSubject) {
+      prefetch_l1(t.row_degree + row);
+      if (t.kept_prefix) prefetch_l1(t.kept_prefix + row);
+    }
+  }
+#else
+  (void)c;
+  (void)s;
+#endif
 }
 
 XG_HD bool eos_allowed(const Tables& t, int32_t token) {

@@ -73,9 +73,13 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
       return;
     }
     const int32_t* tokens = a.history + a.stride * slot;
-    for (; cursor < end; ++cursor) advance_state(c, s, tokens[cursor]);
+    for (; cursor < end; ++cursor) {
+      if (s.phase == kSpan) prefetch_span(c, s);
+      advance_state(c, s, tokens[cursor]);
+    }
     if ((threadIdx.x & 31) == 0) t.cursors[slot] = cursor;
   } else {
+    if (s.phase == kSpan) prefetch_span(c, s);
     advance_state(c, s, a.tokens[i]);
   }
   store_state(t, slot, s);
@@ -285,7 +289,10 @@ __global__ void __launch_bounds__(kFusedThreads)
     if (cursor < end) {
       XgState s = t.states[slot];
       const int32_t* tokens = a.history + a.stride * slot;
-      for (; cursor < end; ++cursor) advance_state(c, s, tokens[cursor]);
+      for (; cursor < end; ++cursor) {
+        if (s.phase == kSpan) prefetch_span(c, s);
+        advance_state(c, s, tokens[cursor]);
+      }
       store_state(t, slot, s);
       build_mask(c, s);
     }
@@ -366,7 +373,7 @@ int check_layout(const XgLayout& l) {
     return fail(XG_EINVAL, "layout: delimiter lengths out of range");
   if (l.ent_cols < 1 || l.rel_cols < 1) return fail(XG_EINVAL, "layout: column tables missing");
   const int64_t required[] = {l.ent_tok, l.ent_off, l.ent_owner, l.rel_tok, l.rel_off, l.rel_owner,
-                              l.ent_col, l.rel_col, l.ent_first, l.rel_first,
+                              l.ent_col, l.rel_col, l.ent_first, l.rel_first, l.row_degree,
                               l.ent_first_row, l.ent_rows_off, l.ent_rows, l.adj_off, l.edge_rel,
                               l.edge_obj, l.root_mask, l.free_next, l.free_mask, l.esc_next,
                               l.esc_mask, l.eos_mask, l.closer_off, l.closer_tok, l.closer_next,
@@ -404,6 +411,7 @@ void bind_tables(XgEngine* e) {
   t.rel = Rows{at<int32_t>(b, l.rel_tok), at<int32_t>(b, l.rel_off), at<int32_t>(b, l.rel_owner), l.relation_rows,
                at<int32_t>(b, l.rel_col), at<int32_t>(b, l.rel_first), l.rel_cols};
   t.ent_first_row = at<int32_t>(b, l.ent_first_row);
+  t.row_degree = at<int32_t>(b, l.row_degree);
   t.ent_rows_off = at<int32_t>(b, l.ent_rows_off);
   t.ent_rows = at<int32_t>(b, l.ent_rows);
   t.adj_off = at<int32_t>(b, l.adj_off);

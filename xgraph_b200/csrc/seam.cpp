@@ -60,6 +60,7 @@ SeamEngine* xgs_create(const void* blob, const XgLayout* l, const XgOptions* o, 
   t.rel = Rows{at<int32_t>(b, l->rel_tok), at<int32_t>(b, l->rel_off), at<int32_t>(b, l->rel_owner), l->relation_rows,
                at<int32_t>(b, l->rel_col), at<int32_t>(b, l->rel_first), l->rel_cols};
   t.ent_first_row = at<int32_t>(b, l->ent_first_row);
+  t.row_degree = at<int32_t>(b, l->row_degree);
   t.ent_rows_off = at<int32_t>(b, l->ent_rows_off);
   t.ent_rows = at<int32_t>(b, l->ent_rows);
   t.adj_off = at<int32_t>(b, l->adj_off);
