@@ -96,6 +96,7 @@ typedef struct XgLayout {
   int64_t ver_off, ver_subj, ver_adj, ver_edge_rel, ver_edge_obj;
   int64_t dstep;  /* uint64 [vocab]: packed next positions of every delimiter byte position, or -1 */
   int64_t row_degree;  /* int32 [entity_rows]: base-KG adjacency entries of each label row's owner */
+  int64_t row_first;   /* int32 [entity_rows]: first label row of each label row's owner */
 } XgLayout;
 
 /* Span-language policies, as the reference Engine's constructor flags

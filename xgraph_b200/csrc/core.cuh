@@ -52,11 +52,16 @@ enum MemoryField : int32_t {
   kMemReached = 1,    // reached rows (<= 64); 0 = no binding yet
   kMemFrontier = 2,   // path frontier entities (<= 64)
   kMemVersion = 3,    // KG version the slot reads (0 = base)
+  kMemPendingLo = 4,  // the next frontier cached for relation-label rows [lo, hi) (lo -1: none)
+  kMemPendingHi = 5,
+  kMemPendingCount = 6,
   kMemFactRows = 8,                           // 64 x (subject key, relation key, object key)
   kMemReachedRows = kMemFactRows + 3 * kMaxSet,  // 64 sorted label rows
   kMemFrontierEnt = kMemReachedRows + kMaxSet,   // 64 entities
   kMemFrontierRank = kMemFrontierEnt + kMaxSet,  // their start ranks
-  kMemHave = kMemFrontierRank + kMaxSet,         // relation bitmap
+  kMemPendingRank = kMemFrontierRank + kMaxSet,  // cached next frontier: ranks
+  kMemPendingFirst = kMemPendingRank + kMaxSet,  //   and first label rows
+  kMemHave = kMemPendingFirst + kMaxSet,         // relation bitmap
 };
 
 struct Key {
@@ -98,6 +103,7 @@ XG_HD int32_t delim_end(const Delim& d, int32_t pos) { return pos + 1 < 17 ? d.a
 struct Tables {
   Rows ent, rel;
   const int32_t* ent_first_row;
+  const int32_t* row_first;    // first label row of each label row's owner (one load, no owner hop)
   const int32_t* row_degree;   // base-KG degree of each label row's owner (one load, no owner hop)
   const int32_t* ent_rows_off;
   const int32_t* ent_rows;
@@ -621,23 +627,30 @@ XG_HD void for_each_slice_item(const Ctx& c, int32_t count, S slice, I item) {
 }
 
 // Writes the bitmap of relations that these entities have (reads entity(k) for k < n).
+// All (entity, edge) pairs are spread over the lanes: one bit per edge (repeats are free).
 template <class E>
 XG_HD void set_have(const Ctx& c, int32_t n, E entity) {
   const Tables& t = c.t;
   int32_t* have = c.mem + kMemHave;
   warp_for(c.w, 0, t.relation_words, [&](int32_t i) { have[i] = 0; });
   const int32_t version = version_of(c);
-  warp_for(c.w, 0, n, [&](int32_t k) {
-    const int32_t e = entity(k);
-    if (e < 0) return;
-    const Edges g = edges_of(t, version, e);
-    int32_t i = 0;
-    while (i < g.n) {  // one bit per run of equal relations
-      const int32_t r = g.rel[i];
-      set_bit(reinterpret_cast<uint32_t*>(have), r);
-      i = upper_index(g.rel, i, g.n, r);
-    }
-  });
+  for_each_slice_item(
+      c, n,
+      [&](int32_t k, const int32_t*& p, int32_t& len) {
+        const int32_t e = entity(k);
+        if (e < 0) {
+          p = nullptr;
+          len = 0;
+          return;
+        }
+        const Edges g = edges_of(t, version, e);
+        p = g.rel;
+        len = g.n;
+      },
+      [&](bool valid, int32_t, int32_t relation) {
+        if (valid) set_bit(reinterpret_cast<uint32_t*>(have), relation);
+      });
+  warp_sync();
 }
 
 // Next path frontier (src/xgraph/oracle.py:1771-1786): objects of the current frontier
@@ -668,7 +681,7 @@ XG_COLD int32_t next_frontier(const Ctx& c, int32_t rlo, int32_t rhi) {
         [&](bool valid, int32_t k, int32_t object) {
           Key key{0, 0, 0};
           if (valid) {
-            const uint32_t first = static_cast<uint32_t>(t.ent_first_row[t.ent.owner[object]]);
+            const uint32_t first = static_cast<uint32_t>(t.row_first[object]);
             const uint64_t rank = t.committed ? static_cast<uint32_t>(ranks[k]) : 0u;
             key.a = (rank << 32) | first;
           }
@@ -729,6 +742,9 @@ XG_COLD void reach_rows_of_top(const Ctx& c, int32_t n) {
   warp_sync();
 }
 
+// Forget the next frontier cached by frontier_goes_on (the frontier or version changed).
+XG_HD void drop_cached_frontier(const Ctx& c) { mem_store(c, kMemPendingLo, -1); }
+
 // Write the frontier held as ENTITY keys in c.top[0, n) into slot memory.
 XG_COLD void store_frontier(const Ctx& c, int32_t n) {
   const Tables& t = c.t;
@@ -740,6 +756,7 @@ XG_COLD void store_frontier(const Ctx& c, int32_t n) {
     ranks[i] = static_cast<int32_t>(a >> 32);
   });
   mem_store(c, kMemFrontier, n);
+  drop_cached_frontier(c);
   warp_sync();
 }
 
@@ -752,14 +769,43 @@ XG_HD bool subject_candidate(const Ctx& c, bool bound, int32_t row) {
   return at < n && reached[at] == row;
 }
 
+// The next frontier through relation-label rows [rlo, rhi) into c.top[0, n): the copy
+// cached in slot memory when the same label was just tested for the separator flag (the
+// frontier has not changed since: every frontier or version change drops the cache),
+// else computed.
+XG_COLD int32_t cached_frontier(const Ctx& c, int32_t rlo, int32_t rhi) {
+  if (c.mem[kMemPendingLo] == rlo && c.mem[kMemPendingHi] == rhi) {
+    const int32_t n = c.mem[kMemPendingCount];
+    const int32_t* ranks = c.mem + kMemPendingRank;
+    const int32_t* firsts = c.mem + kMemPendingFirst;
+    warp_for(c.w, 0, n, [&](int32_t i) {
+      c.top[i] = Key{(static_cast<uint64_t>(static_cast<uint32_t>(ranks[i])) << 32) | static_cast<uint32_t>(firsts[i]), 0u, 0u};
+    });
+    return n;
+  }
+  return next_frontier(c, rlo, rhi);
+}
+
 // Whether the flags' "separator after a relation" holds in path mode: some entity of the
-// capped next frontier has triples.
+// capped next frontier has triples.  The frontier is kept for the transition that follows.
 XG_COLD bool frontier_goes_on(const Ctx& c, int32_t rlo, int32_t rhi) {
   const int32_t n = next_frontier(c, rlo, rhi);
   const int32_t version = version_of(c);
   const Tables& t = c.t;
+  int32_t* ranks = c.mem + kMemPendingRank;
+  int32_t* firsts = c.mem + kMemPendingFirst;
+  warp_for(c.w, 0, n, [&](int32_t i) {
+    ranks[i] = static_cast<int32_t>(c.top[i].a >> 32);
+    firsts[i] = static_cast<int32_t>(c.top[i].a & 0xffffffffu);
+  });
+  if (c.w.leader()) {
+    c.mem[kMemPendingLo] = rlo;
+    c.mem[kMemPendingHi] = rhi;
+    c.mem[kMemPendingCount] = n;
+  }
+  warp_sync();
   return warp_any(c.w, 0, n, [&](int32_t i) {
-    return degree(t, version, t.ent.owner[static_cast<int32_t>(c.top[i].a & 0xffffffffu)]) > 0;
+    return row_degree(t, version, static_cast<int32_t>(c.top[i].a & 0xffffffffu)) > 0;
   });
 }
 
@@ -845,7 +891,7 @@ XG_COLD void next_segment(const Ctx& c, XgState& s, int32_t llo, int32_t lhi) {
           if (t.committed)
             k = connected_key(t, version, row);
           else
-            k = Key{static_cast<uint64_t>(static_cast<uint32_t>(t.ent_first_row[t.ent.owner[row]])), 0u, 0u};
+            k = Key{static_cast<uint64_t>(static_cast<uint32_t>(t.row_first[row])), 0u, 0u};
         }
         top_push(c.w, ts, valid, k, kDistinct);
 #else
@@ -853,7 +899,7 @@ XG_COLD void next_segment(const Ctx& c, XgState& s, int32_t llo, int32_t lhi) {
           const bool valid = subject_candidate(c, bound, row) && degree(t, version, t.ent.owner[row]) > 0;
           if (!valid) continue;
           const Key k = t.committed ? connected_key(t, version, row)
-                                    : Key{static_cast<uint64_t>(static_cast<uint32_t>(t.ent_first_row[t.ent.owner[row]])), 0u, 0u};
+                                    : Key{static_cast<uint64_t>(static_cast<uint32_t>(t.row_first[row])), 0u, 0u};
           top_push(c.w, ts, true, k, kDistinct);
         }
 #endif
@@ -872,6 +918,7 @@ XG_COLD void next_segment(const Ctx& c, XgState& s, int32_t llo, int32_t lhi) {
         }
       });
       mem_store(c, kMemFrontier, n);
+      drop_cached_frontier(c);
       warp_sync();
       set_have(c, n, [&](int32_t k) { return ents[k]; });
       s.subj_lo = llo;
@@ -895,7 +942,7 @@ XG_COLD void next_segment(const Ctx& c, XgState& s, int32_t llo, int32_t lhi) {
     s.segment = kRelation;
     s.hops = 1;
   } else if (t.paths) {
-    const int32_t n = next_frontier(c, llo, lhi);
+    const int32_t n = cached_frontier(c, llo, lhi);
     store_frontier(c, n);
     const int32_t* ents = c.mem + kMemFrontierEnt;
     set_have(c, n, [&](int32_t k) { return ents[k]; });
@@ -920,7 +967,7 @@ XG_COLD void close_span(const Ctx& c, XgState& s, int32_t llo, int32_t lhi) {
   const Tables& t = c.t;
   const int32_t version = version_of(c);
   if (s.segment == kRelation) {  // a path ends
-    int32_t n = next_frontier(c, llo, lhi);
+    int32_t n = cached_frontier(c, llo, lhi);
     if (t.committed && n > 0) n = keep_least_rank(c, n);
     reach_rows_of_top(c, n);
     s.last_kind = kPathSpan;
@@ -969,11 +1016,11 @@ XG_COLD void close_span(const Ctx& c, XgState& s, int32_t llo, int32_t lhi) {
           const int32_t i = base + c.w.lane;
           const bool valid = i < y;
           Key k{0, 0, 0};
-          if (valid) k.a = static_cast<uint32_t>(t.ent_first_row[t.ent.owner[g.obj[i]]]);
+          if (valid) k.a = static_cast<uint32_t>(t.row_first[g.obj[i]]);
           top_push(c.w, ts, valid, k, kDistinct);
 #else
           for (int32_t i = base; i < y && i < base + 32; ++i)
-            top_push(c.w, ts, true, Key{static_cast<uint32_t>(t.ent_first_row[t.ent.owner[g.obj[i]]]), 0u, 0u}, kDistinct);
+            top_push(c.w, ts, true, Key{static_cast<uint32_t>(t.row_first[g.obj[i]]), 0u, 0u}, kDistinct);
 #endif
         }
       }

@@ -102,13 +102,19 @@ __global__ void __launch_bounds__(32) slot_kernel(const __grid_constant__ Tables
       open_span(c, s);
     }
   } else if (a.op == 1) {
-    if (c.w.leader()) c.mem[kMemVersion] = a.value;
+    if (c.w.leader()) {
+      c.mem[kMemVersion] = a.value;
+      c.mem[kMemPendingLo] = -1;
+    }
     __syncwarp();
     if (s.phase == kSpan) set_flags(c, s);  // a KG read changed under the open span
   } else {
     if (threadIdx.x < a.count) c.mem[kMemReachedRows + threadIdx.x] = a.rows[threadIdx.x];
     if (threadIdx.x + 32 < a.count) c.mem[kMemReachedRows + threadIdx.x + 32] = a.rows[threadIdx.x + 32];
-    if (c.w.leader()) c.mem[kMemReached] = a.count;
+    if (c.w.leader()) {
+      c.mem[kMemReached] = a.count;
+      c.mem[kMemPendingLo] = -1;
+    }
     __syncwarp();
     if (s.phase == kSpan) set_flags(c, s);
   }
@@ -128,6 +134,7 @@ __global__ void begin_kernel(const __grid_constant__ Tables t, const int32_t* sl
   for (int32_t k = 0; k < XG_STATE_INTS; ++k) words[k] = 0;
   int32_t* mem = t.memory + static_cast<int64_t>(slot) * t.memory_ints;
   mem[kMemFacts] = mem[kMemReached] = mem[kMemFrontier] = mem[kMemVersion] = 0;
+  mem[kMemPendingLo] = -1;
   t.cursors[slot] = -1;
   t.active[slot] = on;
   t.base[slot] = t.free_mask;
@@ -281,13 +288,22 @@ __global__ void __launch_bounds__(kFusedThreads)
   __shared__ WarpShared shared;
   const int32_t i = blockIdx.x;
   const int32_t slot = a.slots[i];
-  if (!t.active[slot]) return;  // block-uniform: inactive rows are neither advanced nor masked
+  // Issue warp 0's loads of the slot's cursor, lengths and state together with the active
+  // flag rather than after the branch on it: one memory round trip instead of two.
+  const int32_t on = t.active[slot];
+  int32_t cursor = 0, end = 0;
+  XgState s;
+  if (threadIdx.x < 32) {
+    const int32_t stored = t.cursors[slot];
+    const int32_t prompt = a.prompt_len[slot];
+    end = a.total_len[slot];
+    s = t.states[slot];
+    cursor = stored < 0 ? prompt : stored;
+  }
+  if (!on) return;  // block-uniform: inactive rows are neither advanced nor masked
   if (threadIdx.x < 32) {
     Ctx c = make_ctx(t, slot, shared);
-    int32_t cursor = t.cursors[slot] < 0 ? a.prompt_len[slot] : t.cursors[slot];
-    const int32_t end = a.total_len[slot];
     if (cursor < end) {
-      XgState s = t.states[slot];
       const int32_t* tokens = a.history + a.stride * slot;
       for (; cursor < end; ++cursor) {
         if (s.phase == kSpan) prefetch_span(c, s);
@@ -373,7 +389,7 @@ int check_layout(const XgLayout& l) {
     return fail(XG_EINVAL, "layout: delimiter lengths out of range");
   if (l.ent_cols < 1 || l.rel_cols < 1) return fail(XG_EINVAL, "layout: column tables missing");
   const int64_t required[] = {l.ent_tok, l.ent_off, l.ent_owner, l.rel_tok, l.rel_off, l.rel_owner,
-                              l.ent_col, l.rel_col, l.ent_first, l.rel_first, l.row_degree,
+                              l.ent_col, l.rel_col, l.ent_first, l.rel_first, l.row_degree, l.row_first,
                               l.ent_first_row, l.ent_rows_off, l.ent_rows, l.adj_off, l.edge_rel,
                               l.edge_obj, l.root_mask, l.free_next, l.free_mask, l.esc_next,
                               l.esc_mask, l.eos_mask, l.closer_off, l.closer_tok, l.closer_next,
@@ -412,6 +428,7 @@ void bind_tables(XgEngine* e) {
                at<int32_t>(b, l.rel_col), at<int32_t>(b, l.rel_first), l.rel_cols};
   t.ent_first_row = at<int32_t>(b, l.ent_first_row);
   t.row_degree = at<int32_t>(b, l.row_degree);
+  t.row_first = at<int32_t>(b, l.row_first);
   t.ent_rows_off = at<int32_t>(b, l.ent_rows_off);
   t.ent_rows = at<int32_t>(b, l.ent_rows);
   t.adj_off = at<int32_t>(b, l.adj_off);

@@ -40,6 +40,7 @@ static void begin_slot(SeamEngine* e, int32_t slot, int32_t on) {
   std::memset(&e->states[slot], 0, sizeof(XgState));
   int32_t* mem = e->memory.data() + static_cast<int64_t>(slot) * e->t.memory_ints;
   mem[kMemFacts] = mem[kMemReached] = mem[kMemFrontier] = mem[kMemVersion] = 0;
+  mem[kMemPendingLo] = -1;
   e->cursors[slot] = -1;
   e->active[slot] = on;
   e->base[slot] = e->t.free_mask;
@@ -61,6 +62,7 @@ SeamEngine* xgs_create(const void* blob, const XgLayout* l, const XgOptions* o, 
                at<int32_t>(b, l->rel_col), at<int32_t>(b, l->rel_first), l->rel_cols};
   t.ent_first_row = at<int32_t>(b, l->ent_first_row);
   t.row_degree = at<int32_t>(b, l->row_degree);
+  t.row_first = at<int32_t>(b, l->row_first);
   t.ent_rows_off = at<int32_t>(b, l->ent_rows_off);
   t.ent_rows = at<int32_t>(b, l->ent_rows);
   t.adj_off = at<int32_t>(b, l->adj_off);
@@ -132,6 +134,7 @@ void xgs_begin(SeamEngine* e, int32_t slot, int32_t on) { begin_slot(e, slot, on
 void xgs_set_version(SeamEngine* e, int32_t slot, int32_t version) {
   Ctx c = ctx(e, slot);
   c.mem[kMemVersion] = version;
+  c.mem[kMemPendingLo] = -1;
   XgState s = e->states[slot];
   if (s.phase == kSpan) set_flags(c, s);
   e->states[slot] = s;
@@ -143,6 +146,7 @@ void xgs_set_reached(SeamEngine* e, int32_t slot, const int32_t* rows, int32_t c
   if (count > kMaxSet) count = kMaxSet;
   for (int32_t i = 0; i < count; ++i) c.mem[kMemReachedRows + i] = rows[i];
   c.mem[kMemReached] = count;
+  c.mem[kMemPendingLo] = -1;
   XgState s = e->states[slot];
   if (s.phase == kSpan) set_flags(c, s);
   e->states[slot] = s;

@@ -50,7 +50,8 @@ class XgLayout(ctypes.Structure):
             "free_next", "free_mask", "esc_next", "esc_mask", "eos_mask",
             "closer_off", "closer_tok", "closer_next", "separator_off", "separator_tok",
             "separator_next", "escape_off", "escape_tok", "escape_next",
-            "ver_off", "ver_subj", "ver_adj", "ver_edge_rel", "ver_edge_obj", "dstep", "row_degree")]
+            "ver_off", "ver_subj", "ver_adj", "ver_edge_rel", "ver_edge_obj", "dstep", "row_degree",
+            "row_first")]
     )
 
 
@@ -339,6 +340,7 @@ def pack_tables(index, tokenizer, syntax, *, escapes: bool, versions=None,
         "ent_first": first_token_starts(ent_tok, ent_off, vocab),
         "rel_first": first_token_starts(rel_tok, rel_off, vocab),
         "ent_first_row": first_row, "ent_rows_off": _int32("entity rows", ent_rows_off),
+        "row_first": first_row[owners64] if labels.num_rows else np.zeros(0, np.int32),
         "row_degree": _int32("row degrees", np.diff(np.asarray(index.adjacency_offsets, dtype=np.int64))[owners64]
                              if labels.num_rows else np.zeros(0, np.int64)),
         "ent_rows": ent_rows,
