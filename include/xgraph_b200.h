@@ -97,6 +97,12 @@ typedef struct XgLayout {
   int64_t dstep;  /* uint64 [vocab]: packed next positions of every delimiter byte position, or -1 */
   int64_t row_degree;  /* int32 [entity_rows]: base-KG adjacency entries of each label row's owner */
   int64_t row_first;   /* int32 [entity_rows]: first label row of each label row's owner */
+  int64_t run_off;     /* int32 [entities + 1]: each entity's relation runs in `runs` (CSR) */
+  int64_t runs;        /* int32 [runs + 1][2]: (relation, first edge) of each run of equal relations in an
+                          entity's adjacency; the last pair (INT32_MAX, edges) closes the final run */
+  int64_t run_rel;     /* int32 [runs]: the relation of each run (the first column of `runs`) */
+  int64_t edge_first;  /* int32 [edges]: first label row of each edge's object entity, bit 31 set when
+                          that entity has no triples in the base KG */
 } XgLayout;
 
 /* Span-language policies, as the reference Engine's constructor flags

@@ -38,6 +38,8 @@ def library():
         getattr(lib, name).restype = None
     lib.xgs_memory_ints.argtypes = [p]
     lib.xgs_memory_ints.restype = i32
+    lib.xgs_relation_slice.argtypes = [p, i32, i32, i32, p]
+    lib.xgs_relation_slice.restype = None
     return lib
 
 
@@ -64,6 +66,11 @@ class SeamEngine:
     def __del__(self):
         if getattr(self, "handle", None):
             self.lib.xgs_destroy(self.handle)
+
+    def relation_slice(self, entity, relation, version=0):
+        out = np.zeros(3, dtype=np.int32)
+        self.lib.xgs_relation_slice(self.handle, version, entity, relation, out.ctypes.data_as(ctypes.c_void_p))
+        return int(out[0]), int(out[1]), int(out[2])
 
     def begin(self, slot):
         self.lib.xgs_begin(self.handle, slot, 1)

@@ -19,15 +19,21 @@
 // XG_HD: small helpers, inlined.  XG_COLD: the rare, heavy transitions (closing a span,
 // changing segment, frontiers, sorts), kept out of line so that the per-token hot path
 // stays a few kilobytes of code: a decode step starts with a cold instruction cache, and
-// every fetch of a cold code line costs an HBM round trip.
+// every fetch of a cold code line costs an HBM round trip.  XG_SHARED: helpers that one
+// step calls from several places (candidate tests, row bounds, adjacency lookups), kept
+// as one out-of-line copy so that each of their code lines is fetched once per step.
+// Loops are kept rolled (#pragma unroll 1) for the same reason, except short scans whose
+// loads must issue together.
 #if defined(__CUDACC__)
 #define XG_HD __device__ __forceinline__
 #define XG_COLD __device__ __noinline__
+#define XG_SHARED __device__ __noinline__
 #define XG_GPU 1
 #else
 #include <algorithm>
 #define XG_HD inline
 #define XG_COLD inline
+#define XG_SHARED inline
 #define XG_GPU 0
 #endif
 
@@ -36,6 +42,7 @@ namespace xg {
 constexpr int32_t kMaxSet = 64;       // MAX_FACTS == MAX_REACHED (src/xgraph/oracle.py:172-175)
 constexpr int32_t kMaxHops = 8;       // MAX_PATH_RELATIONS (src/xgraph/oracle.py:177)
 constexpr int32_t kTopCap = 256;      // per-warp candidate buffer of the top-64 selections
+constexpr int32_t kItemBatch = 1;     // rounds of slice items whose loads are issued together
 constexpr int32_t kScratchInts = 2 * kMaxSet + 2 + 2 * kMaxSet + kMaxSet;
 constexpr int8_t kReject = -1;
 constexpr int8_t kComplete = -2;
@@ -110,6 +117,10 @@ struct Tables {
   const int32_t* adj_off;
   const int32_t* edge_rel;
   const int32_t* edge_obj;
+  const int32_t* run_off;     // [entities + 1]: each entity's relation runs (CSR)
+  const int32_t* runs;        // [runs + 1][2]: (relation, first edge), closed by (INT32_MAX, edges)
+  const int32_t* run_rel;     // [runs]: the relation of each run
+  const int32_t* edge_first;  // [edges]: object's first label row, bit 31 = the object has no triples
   const int32_t* sitelinks;    // null unless the sitelink rank is on
   const int32_t* kept_prefix;  // null unless some rows are not unbound candidates
   const uint32_t* root_mask;
@@ -167,6 +178,7 @@ XG_HD void warp_sync() {
 template <class F>
 XG_HD bool warp_any(const Warp& w, int32_t begin, int32_t end, F f) {
 #if XG_GPU
+  #pragma unroll 1
   for (int32_t base = begin; base < end; base += 32) {
     const int32_t i = base + w.lane;
     const bool hit = i < end && f(i);
@@ -175,6 +187,7 @@ XG_HD bool warp_any(const Warp& w, int32_t begin, int32_t end, F f) {
   return false;
 #else
   (void)w;
+  #pragma unroll 1
   for (int32_t i = begin; i < end; ++i)
     if (f(i)) return true;
   return false;
@@ -185,10 +198,12 @@ XG_HD bool warp_any(const Warp& w, int32_t begin, int32_t end, F f) {
 template <class F>
 XG_HD void warp_for(const Warp& w, int32_t begin, int32_t end, F f) {
 #if XG_GPU
+  #pragma unroll 1
   for (int32_t i = begin + w.lane; i < end; i += 32) f(i);
   __syncwarp();
 #else
   (void)w;
+  #pragma unroll 1
   for (int32_t i = begin; i < end; ++i) f(i);
 #endif
 }
@@ -198,10 +213,12 @@ template <class F>
 XG_HD Key warp_min(const Warp& w, int32_t begin, int32_t end, F key) {
   Key best = max_key();
 #if XG_GPU
+  #pragma unroll 1
   for (int32_t i = begin + w.lane; i < end; i += 32) {
     const Key k = key(i);
     if (key_less(k, best)) best = k;
   }
+  #pragma unroll 1
   for (int32_t d = 16; d > 0; d >>= 1) {
     Key o;
     o.a = __shfl_xor_sync(0xffffffffu, best.a, d);
@@ -211,6 +228,7 @@ XG_HD Key warp_min(const Warp& w, int32_t begin, int32_t end, F key) {
   }
 #else
   (void)w;
+  #pragma unroll 1
   for (int32_t i = begin; i < end; ++i) {
     const Key k = key(i);
     if (key_less(k, best)) best = k;
@@ -244,12 +262,18 @@ struct TopSet {
 XG_COLD void top_sort(const Warp& w, Key* buf, int32_t n) {
 #if XG_GPU
   int32_t width = 32;
+  #pragma unroll 1
   while (width < n) width <<= 1;
+  #pragma unroll 1
   for (int32_t i = n + w.lane; i < width; i += 32) buf[i] = max_key();
+  #pragma unroll 1
   for (int32_t i = width + w.lane; i < kTopCap; i += 32) buf[i] = max_key();
   __syncwarp();
+  #pragma unroll 1
   for (int32_t k = 2; k <= width; k <<= 1) {
+    #pragma unroll 1
     for (int32_t j = k >> 1; j > 0; j >>= 1) {
+      #pragma unroll 1
       for (int32_t i = w.lane; i < width; i += 32) {
         const int32_t l = i ^ j;
         if (l > i) {
@@ -267,6 +291,7 @@ XG_COLD void top_sort(const Warp& w, Key* buf, int32_t n) {
 #else
   (void)w;
   std::sort(buf, buf + n, key_less);
+  #pragma unroll 1
   for (int32_t i = n; i < kTopCap; ++i) buf[i] = max_key();
 #endif
 }
@@ -277,6 +302,7 @@ XG_COLD int32_t top_unique(const Warp& w, Key* buf, int32_t n, int32_t limit, bo
 #if XG_GPU
   int32_t out = 0;
   Key carry = max_key();
+  #pragma unroll 1
   for (int32_t base = 0; base < n && out < limit; base += 32) {
     const Key k = base + w.lane < n ? buf[base + w.lane] : max_key();
     Key prev;
@@ -300,6 +326,7 @@ XG_COLD int32_t top_unique(const Warp& w, Key* buf, int32_t n, int32_t limit, bo
 #else
   (void)w;
   int32_t out = 0;
+  #pragma unroll 1
   for (int32_t i = 0; i < n && out < limit; ++i) {
     const Key k = buf[i];
     if (is_max(k)) break;
@@ -374,6 +401,7 @@ XG_HD int32_t column(const Rows& r, int32_t row, int32_t depth) {
 template <class P>
 XG_HD int32_t warp_partition(const Warp& w, int32_t lo, int32_t hi, P pred) {
 #if XG_GPU
+  #pragma unroll 1
   while (hi - lo > 32) {
     const int32_t step = (hi - lo + 31) >> 5;
     const int32_t probe = lo + (w.lane + 1) * step - 1;  // the last row of bucket `lane`
@@ -388,6 +416,7 @@ XG_HD int32_t warp_partition(const Warp& w, int32_t lo, int32_t hi, P pred) {
   return m == 0u ? hi : lo + __ffs(m) - 1;
 #else
   (void)w;
+  #pragma unroll 1
   while (lo < hi) {
     const int32_t mid = lo + ((hi - lo) >> 1);
     if (pred(mid))
@@ -400,7 +429,7 @@ XG_HD int32_t warp_partition(const Warp& w, int32_t lo, int32_t hi, P pred) {
 }
 
 // First row in [lo, hi) whose column at depth is >= token (upper: > token).
-XG_HD int32_t bound_row(const Warp& w, const Rows& r, int32_t lo, int32_t hi, int32_t depth, int32_t token,
+XG_SHARED int32_t bound_row(const Warp& w, const Rows& r, int32_t lo, int32_t hi, int32_t depth, int32_t token,
                         bool upper) {
   return warp_partition(w, lo, hi, [&](int32_t row) {
     const int32_t c = column(r, row, depth);
@@ -409,7 +438,7 @@ XG_HD int32_t bound_row(const Warp& w, const Rows& r, int32_t lo, int32_t hi, in
 }
 
 // The rows of [lo, hi) whose column at depth equals token (the typed label extended by it).
-XG_HD void narrow(const Warp& w, const Rows& r, int32_t& lo, int32_t& hi, int32_t depth, int32_t token) {
+XG_SHARED void narrow(const Warp& w, const Rows& r, int32_t& lo, int32_t& hi, int32_t depth, int32_t token) {
   if (depth == 0 && lo == 0 && hi == r.count) {  // the whole index: one table read
     lo = r.first[token];
     hi = r.first[token + 1];
@@ -422,6 +451,7 @@ XG_HD void narrow(const Warp& w, const Rows& r, int32_t& lo, int32_t& hi, int32_
 
 template <class T>
 XG_HD int32_t lower_index(const T* a, int32_t lo, int32_t hi, T value) {
+  #pragma unroll 1
   while (lo < hi) {
     const int32_t mid = lo + ((hi - lo) >> 1);
     if (a[mid] < value)
@@ -434,6 +464,7 @@ XG_HD int32_t lower_index(const T* a, int32_t lo, int32_t hi, T value) {
 
 template <class T>
 XG_HD int32_t upper_index(const T* a, int32_t lo, int32_t hi, T value) {
+  #pragma unroll 1
   while (lo < hi) {
     const int32_t mid = lo + ((hi - lo) >> 1);
     if (a[mid] <= value)
@@ -444,46 +475,79 @@ XG_HD int32_t upper_index(const T* a, int32_t lo, int32_t hi, T value) {
   return lo;
 }
 
+XG_HD void prefetch_l1(const void* p) {
+#if XG_GPU
+  asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
+#else
+  (void)p;
+#endif
+}
+
 struct Edges {
   const int32_t* rel;
   const int32_t* obj;
+  const int32_t* first;  // base KG: the edges' folded first rows (edge_first); null for a version's list
   int32_t n;
+  int32_t start;         // base KG: index of the first edge
+  int32_t run0, runs;    // base KG: the entity's relation runs [run0, run0 + runs); runs -1 otherwise
 };
 
 // An entity's adjacency in a KG version: the version's own list for an edited subject,
 // else the base CSR slice (src/xgraph/kgversions.py:14-21, the layout both share).
-XG_HD Edges edges_of(const Tables& t, int32_t version, int32_t e) {
+XG_SHARED Edges edges_of(const Tables& t, int32_t version, int32_t e) {
   if (version > 0) {
     const int32_t a = t.ver_off[version - 1], b = t.ver_off[version];
     const int32_t at = lower_index(t.ver_subj, a, b, e);
     if (at < b && t.ver_subj[at] == e) {
       const int32_t s = t.ver_adj[at], f = t.ver_adj[at + 1];
-      return Edges{t.ver_edge_rel + s, t.ver_edge_obj + s, f - s};
+      return Edges{t.ver_edge_rel + s, t.ver_edge_obj + s, nullptr, f - s, s, 0, -1};
     }
   }
   const int32_t s = t.adj_off[e], f = t.adj_off[e + 1];
-  return Edges{t.edge_rel + s, t.edge_obj + s, f - s};
+  const int32_t r0 = t.run_off[e], r1 = t.run_off[e + 1];
+  return Edges{t.edge_rel + s, t.edge_obj + s, t.edge_first + s, f - s, s, r0, r1 - r0};
 }
 
-// The objects of one relation within an adjacency list: [first, last) indexes.  Short
-// lists (<= 16 edges) are scanned with independent loads instead of dependent halvings.
-XG_HD void relation_slice(const Edges& g, int32_t relation, int32_t& first, int32_t& last) {
-  if (g.n <= 16) {
-    int32_t below = 0, upto = 0;
-#pragma unroll
-    for (int32_t i = 0; i < 16; ++i) {
-      if (i < g.n) {
-        const int32_t r = g.rel[i];
-        below += r < relation;
-        upto += r <= relation;
-      }
-    }
-    first = below;
-    last = upto;
+// First label row of the object of edge i of g (bit 31 of the folded table cleared).
+XG_HD int32_t edge_first_row(const Tables& t, const Edges& g, int32_t i) {
+  return g.first ? g.first[i] & 0x7fffffff : t.row_first[g.obj[i]];
+}
+
+// The objects of one relation within an adjacency list: [first, last) indexes (equal when
+// the relation is absent).  In the base KG the entity's relation runs are searched: while
+// more than 16 remain, 15 evenly spaced pivots narrow them to one bucket; the pivots' lines
+// are prefetched together and then compared, so a round costs one memory latency and the
+// loops stay rolled (short code: a step's instruction fetches start cold).  A version's
+// own list is searched by halving.
+XG_SHARED void relation_slice(const Tables& t, const Edges& g, int32_t relation, int32_t& first, int32_t& last) {
+  first = last = 0;
+  if (g.runs < 0) {
+    first = lower_index(g.rel, 0, g.n, relation);
+    last = upper_index(g.rel, first, g.n, relation);
     return;
   }
-  first = lower_index(g.rel, 0, g.n, relation);
-  last = upper_index(g.rel, first, g.n, relation);
+  int32_t lo = g.run0, n = g.runs;
+#pragma unroll 1
+  while (n > 16) {
+    const int32_t step = (n + 15) >> 4;
+#pragma unroll 1
+    for (int32_t j = 0; j < 15 && (j + 1) * step <= n; ++j) prefetch_l1(t.run_rel + lo + (j + 1) * step - 1);
+    int32_t skip = 0;
+#pragma unroll 1
+    while (skip < 15 && (skip + 1) * step <= n && t.run_rel[lo + (skip + 1) * step - 1] < relation) ++skip;
+    lo += skip * step;
+    n = n - skip * step < step ? n - skip * step : step;
+  }
+  // the <= 16 runs left and the one after them (its first edge ends the match)
+  prefetch_l1(t.runs + 2 * lo);
+  prefetch_l1(t.runs + 2 * (lo + n));
+  int32_t j = 0;
+#pragma unroll 1
+  while (j < n && t.runs[2 * (lo + j)] < relation) ++j;
+  if (j < n && t.runs[2 * (lo + j)] == relation) {
+    first = t.runs[2 * (lo + j) + 1] - g.start;
+    last = t.runs[2 * (lo + j) + 3] - g.start;
+  }
 }
 
 XG_HD int32_t degree(const Tables& t, int32_t version, int32_t e) { return edges_of(t, version, e).n; }
@@ -494,17 +558,9 @@ XG_HD int32_t row_degree(const Tables& t, int32_t version, int32_t row) {
   return version == 0 ? t.row_degree[row] : degree(t, version, t.ent.owner[row]);
 }
 
-XG_HD void prefetch_l1(const void* p) {
-#if XG_GPU
-  asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
-#else
-  (void)p;
-#endif
-}
-
 // Best-connected order key (src/xgraph/oracle.py:1736-1747): most sitelinks (with the
 // sitelink rank), then most adjacency entries in the slot's version, then first row.
-XG_HD Key connected_key(const Tables& t, int32_t version, int32_t row) {
+XG_SHARED Key connected_key(const Tables& t, int32_t version, int32_t row) {
   const int32_t e = t.ent.owner[row];
   const uint32_t links = t.sitelinks ? static_cast<uint32_t>(t.sitelinks[e]) : 0u;
   const uint32_t deg = static_cast<uint32_t>(degree(t, version, e));
@@ -547,7 +603,7 @@ XG_HD bool answers_path(const Tables& t, const XgState& s) { return t.paths && s
 
 // Whether some candidate row of the state's segment lies in [lo, hi)
 // (src/xgraph/oracle.py:830-894: _candidates / _segment_candidates).
-XG_HD bool has_candidate(const Ctx& c, const XgState& s, int32_t lo, int32_t hi) {
+XG_SHARED bool has_candidate(const Ctx& c, const XgState& s, int32_t lo, int32_t hi) {
   const Tables& t = c.t;
   if (lo >= hi) return false;
   if (s.segment == kSubject) {
@@ -566,7 +622,7 @@ XG_HD bool has_candidate(const Ctx& c, const XgState& s, int32_t lo, int32_t hi)
     const int32_t r = t.rel.owner[s.rel_lo + p % relations];
     const Edges g = edges_of(t, version, e);
     int32_t a, b;
-    relation_slice(g, r, a, b);
+    relation_slice(t, g, r, a, b);
     const int32_t x = lower_index(g.obj, a, b, lo);
     return x < b && g.obj[x] < hi;
   });
@@ -579,15 +635,30 @@ XG_HD void for_each_slice_item(const Ctx& c, int32_t count, S slice, I item) {
 #if XG_GPU
   int32_t* starts = c.scratch;                       // [65]
   const int32_t** ptrs = reinterpret_cast<const int32_t**>(c.scratch + 2 * kMaxSet + 2);  // [64]
+  #pragma unroll 1
   for (int32_t base = 0; base < count; base += 64) {
-    const int32_t k0 = base + c.w.lane, k1 = base + 32 + c.w.lane;
+    // slices base + lane and base + 32 + lane, in a loop so that the slice code (often
+    // long: an adjacency lookup) appears once
     const int32_t* p0 = nullptr;
     const int32_t* p1 = nullptr;
     int32_t n0 = 0, n1 = 0;
-    if (k0 < count) slice(k0, p0, n0);
-    if (k1 < count) slice(k1, p1, n1);
+#pragma unroll 1
+    for (int32_t h = 0; h < 2; ++h) {
+      const int32_t k = base + 32 * h + c.w.lane;
+      const int32_t* p = nullptr;
+      int32_t n = 0;
+      if (k < count) slice(k, p, n);
+      if (h == 0) {
+        p0 = p;
+        n0 = n;
+      } else {
+        p1 = p;
+        n1 = n;
+      }
+    }
     // inclusive scan of n0 over lanes, then of n1 continuing after the first half
     int32_t x0 = n0, x1 = n1;
+    #pragma unroll 1
     for (int32_t d = 1; d < 32; d <<= 1) {
       const int32_t y0 = __shfl_up_sync(0xffffffffu, x0, d);
       const int32_t y1 = __shfl_up_sync(0xffffffffu, x1, d);
@@ -604,32 +675,44 @@ XG_HD void for_each_slice_item(const Ctx& c, int32_t count, S slice, I item) {
     ptrs[32 + c.w.lane] = p1;
     if (c.w.lane == 0) starts[64] = total;
     __syncwarp();
-    for (int32_t g0 = 0; g0 < total; g0 += 32) {
-      const int32_t g = g0 + c.w.lane;
-      const bool valid = g < total;
-      int32_t k = 0, value = 0;
-      if (valid) {
-        k = upper_index(starts, 0, 64, g) - 1;
-        value = ptrs[k][g - starts[k]];
+    // kItemBatch rounds of loads are issued before their items run (item may store, and
+    // the compiler would not move a later round's load above that store).
+    #pragma unroll 1
+    for (int32_t g0 = 0; g0 < total; g0 += 32 * kItemBatch) {
+      int32_t k[kItemBatch], value[kItemBatch];
+#pragma unroll
+      for (int32_t b = 0; b < kItemBatch; ++b) {
+        const int32_t g = g0 + 32 * b + c.w.lane;
+        k[b] = 0;
+        value[b] = 0;
+        if (g < total) {
+          k[b] = upper_index(starts, 0, 64, g) - 1;
+          value[b] = ptrs[k[b]][g - starts[k[b]]];
+        }
       }
-      item(valid, base + k, value);
+#pragma unroll
+      for (int32_t b = 0; b < kItemBatch; ++b) {
+        if (g0 + 32 * b >= total) break;  // warp-uniform
+        item(g0 + 32 * b + c.w.lane < total, base + k[b], value[b]);
+      }
     }
     __syncwarp();
   }
 #else
+  #pragma unroll 1
   for (int32_t k = 0; k < count; ++k) {
     const int32_t* p = nullptr;
     int32_t n = 0;
     slice(k, p, n);
+    #pragma unroll 1
     for (int32_t i = 0; i < n; ++i) item(true, k, p[i]);
   }
 #endif
 }
 
-// Writes the bitmap of relations that these entities have (reads entity(k) for k < n).
-// All (entity, edge) pairs are spread over the lanes: one bit per edge (repeats are free).
-template <class E>
-XG_HD void set_have(const Ctx& c, int32_t n, E entity) {
+// Writes the bitmap of relations that the entities entity[0, n) have.  All (entity,
+// relation run) pairs are spread over the lanes (edges for a version's own list).
+XG_COLD void set_have(const Ctx& c, int32_t n, const int32_t* entity) {
   const Tables& t = c.t;
   int32_t* have = c.mem + kMemHave;
   warp_for(c.w, 0, t.relation_words, [&](int32_t i) { have[i] = 0; });
@@ -637,15 +720,14 @@ XG_HD void set_have(const Ctx& c, int32_t n, E entity) {
   for_each_slice_item(
       c, n,
       [&](int32_t k, const int32_t*& p, int32_t& len) {
-        const int32_t e = entity(k);
-        if (e < 0) {
-          p = nullptr;
-          len = 0;
-          return;
+        const Edges g = edges_of(t, version, entity[k]);
+        if (g.runs >= 0) {  // one bit per relation run
+          p = t.run_rel + g.run0;
+          len = g.runs;
+        } else {
+          p = g.rel;
+          len = g.n;
         }
-        const Edges g = edges_of(t, version, e);
-        p = g.rel;
-        len = g.n;
       },
       [&](bool valid, int32_t, int32_t relation) {
         if (valid) set_bit(reinterpret_cast<uint32_t*>(have), relation);
@@ -666,7 +748,9 @@ XG_COLD int32_t next_frontier(const Ctx& c, int32_t rlo, int32_t rhi) {
   const int32_t* ents = c.mem + kMemFrontierEnt;
   const int32_t* ranks = c.mem + kMemFrontierRank;
   const int32_t count = c.mem[kMemFrontier];
+  const bool folded = version == 0;  // every list is a base-KG slice with folded first rows
   TopSet ts{c.top, 0};
+  #pragma unroll 1
   for (int32_t rr = rlo; rr < rhi; ++rr) {
     const int32_t relation = t.rel.owner[rr];
     for_each_slice_item(
@@ -674,16 +758,20 @@ XG_COLD int32_t next_frontier(const Ctx& c, int32_t rlo, int32_t rhi) {
         [&](int32_t k, const int32_t*& p, int32_t& n) {
           const Edges g = edges_of(t, version, ents[k]);
           int32_t a, b;
-          relation_slice(g, relation, a, b);
-          p = g.obj + a;
+          relation_slice(t, g, relation, a, b);
+          p = (folded ? g.first : g.obj) + a;
           n = b - a;
         },
-        [&](bool valid, int32_t k, int32_t object) {
+        [&](bool valid, int32_t k, int32_t value) {
           Key key{0, 0, 0};
           if (valid) {
-            const uint32_t first = static_cast<uint32_t>(t.row_first[object]);
+            // folded: value is the first row with the no-triples bit; pad 1 = has triples,
+            // 2 = has none, 0 = not known here (a version's list)
+            const uint32_t first = folded ? static_cast<uint32_t>(value) & 0x7fffffffu
+                                          : static_cast<uint32_t>(t.row_first[value]);
             const uint64_t rank = t.committed ? static_cast<uint32_t>(ranks[k]) : 0u;
             key.a = (rank << 32) | first;
+            key.pad = folded ? 1u + (static_cast<uint32_t>(value) >> 31) : 0u;
           }
           top_push(c.w, ts, valid, key, kEntity);
         });
@@ -698,6 +786,7 @@ XG_COLD int32_t keep_least_rank(const Ctx& c, int32_t n) {
   const Key least = warp_min(c.w, 0, n, [&](int32_t i) { return Key{c.top[i].a >> 32, 0u, 0u}; });
 #if XG_GPU
   int32_t out = 0;
+  #pragma unroll 1
   for (int32_t base = 0; base < n; base += 32) {
     const int32_t i = base + c.w.lane;
     const Key k = i < n ? c.top[i] : max_key();
@@ -711,6 +800,7 @@ XG_COLD int32_t keep_least_rank(const Ctx& c, int32_t n) {
   return out;
 #else
   int32_t out = 0;
+  #pragma unroll 1
   for (int32_t i = 0; i < n; ++i)
     if ((c.top[i].a >> 32) == least.a) c.top[out++] = c.top[i];
   return out;
@@ -805,13 +895,15 @@ XG_COLD bool frontier_goes_on(const Ctx& c, int32_t rlo, int32_t rhi) {
   }
   warp_sync();
   return warp_any(c.w, 0, n, [&](int32_t i) {
+    const uint32_t known = c.top[i].pad;
+    if (known) return known == 1u;
     return row_degree(t, version, static_cast<int32_t>(c.top[i].a & 0xffffffffu)) > 0;
   });
 }
 
 // Which delimiter branches may start after the state's typed label
 // (src/xgraph/oracle.py:1039-1113: closes, separates, and the escape condition).
-XG_HD void set_flags(const Ctx& c, XgState& s) {
+XG_SHARED void set_flags(const Ctx& c, XgState& s) {
   const Tables& t = c.t;
   s.flags = 0;
   if (s.lo < 0) {
@@ -882,6 +974,7 @@ XG_COLD void next_segment(const Ctx& c, XgState& s, int32_t llo, int32_t lhi) {
     if (t.paths) {
       // starts: every candidate with triples in best-connected order, kept to 64
       TopSet ts{c.top, 0};
+      #pragma unroll 1
       for (int32_t base = llo; base < lhi; base += 32) {
 #if XG_GPU
         const int32_t row = base + c.w.lane;
@@ -895,6 +988,7 @@ XG_COLD void next_segment(const Ctx& c, XgState& s, int32_t llo, int32_t lhi) {
         }
         top_push(c.w, ts, valid, k, kDistinct);
 #else
+        #pragma unroll 1
         for (int32_t row = base; row < lhi && row < base + 32; ++row) {
           const bool valid = subject_candidate(c, bound, row) && degree(t, version, t.ent.owner[row]) > 0;
           if (!valid) continue;
@@ -920,7 +1014,7 @@ XG_COLD void next_segment(const Ctx& c, XgState& s, int32_t llo, int32_t lhi) {
       mem_store(c, kMemFrontier, n);
       drop_cached_frontier(c);
       warp_sync();
-      set_have(c, n, [&](int32_t k) { return ents[k]; });
+      set_have(c, n, ents);
       s.subj_lo = llo;
       s.subj_hi = lhi;
     } else if (t.derivation) {
@@ -932,11 +1026,11 @@ XG_COLD void next_segment(const Ctx& c, XgState& s, int32_t llo, int32_t lhi) {
       const int32_t row = static_cast<int32_t>(best.b);
       s.subj_lo = row;
       s.subj_hi = row + 1;
-      set_have(c, 1, [&](int32_t) { return t.ent.owner[row]; });
+      set_have(c, 1, t.ent.owner + row);
     } else {
       s.subj_lo = llo;
       s.subj_hi = lhi;
-      set_have(c, lhi - llo, [&](int32_t k) { return t.ent.owner[llo + k]; });
+      set_have(c, lhi - llo, t.ent.owner + llo);
     }
     s.subj_key = llo;
     s.segment = kRelation;
@@ -945,7 +1039,7 @@ XG_COLD void next_segment(const Ctx& c, XgState& s, int32_t llo, int32_t lhi) {
     const int32_t n = cached_frontier(c, llo, lhi);
     store_frontier(c, n);
     const int32_t* ents = c.mem + kMemFrontierEnt;
-    set_have(c, n, [&](int32_t k) { return ents[k]; });
+    set_have(c, n, ents);
     s.hops += 1;
   } else {
     s.rel_lo = llo;
@@ -1003,24 +1097,27 @@ XG_COLD void close_span(const Ctx& c, XgState& s, int32_t llo, int32_t lhi) {
       const int32_t relations = s.rel_hi - s.rel_lo;
       TopSet ts{c.top, 0};
       // entities reached, as first rows, kept distinct (at most 64 needed for 64 rows)
+      #pragma unroll 1
       for (int32_t p = 0; p < (s.subj_hi - s.subj_lo) * relations; ++p) {
         const int32_t e = t.ent.owner[s.subj_lo + p / relations];
         const int32_t r = t.rel.owner[s.rel_lo + p % relations];
         const Edges g = edges_of(t, version, e);
         int32_t a, b;
-        relation_slice(g, r, a, b);
+        relation_slice(t, g, r, a, b);
         const int32_t x = lower_index(g.obj, a, b, llo);
         const int32_t y = lower_index(g.obj, x, b, lhi);
+        #pragma unroll 1
         for (int32_t base = x; base < y; base += 32) {
 #if XG_GPU
           const int32_t i = base + c.w.lane;
           const bool valid = i < y;
           Key k{0, 0, 0};
-          if (valid) k.a = static_cast<uint32_t>(t.row_first[g.obj[i]]);
+          if (valid) k.a = static_cast<uint32_t>(edge_first_row(t, g, i));
           top_push(c.w, ts, valid, k, kDistinct);
 #else
+          #pragma unroll 1
           for (int32_t i = base; i < y && i < base + 32; ++i)
-            top_push(c.w, ts, true, Key{static_cast<uint32_t>(t.row_first[g.obj[i]]), 0u, 0u}, kDistinct);
+            top_push(c.w, ts, true, Key{static_cast<uint32_t>(edge_first_row(t, g, i)), 0u, 0u}, kDistinct);
 #endif
         }
       }
@@ -1139,6 +1236,7 @@ XG_HD void prefetch_span(const Ctx& c, const XgState& s) {
   }
   if (s.lo < 0 || s.hi - s.lo > 64) return;
   const Rows& r = s.segment == kRelation ? t.rel : t.ent;
+  #pragma unroll 1
   for (int32_t row = s.lo + lane; row < s.hi; row += 32) {
     if (s.depth < r.cols) prefetch_l1(r.col + static_cast<int64_t>(s.depth) * r.count + row);
     if (s.depth + 1 < r.cols) prefetch_l1(r.col + static_cast<int64_t>(s.depth + 1) * r.count + row);
@@ -1205,7 +1303,7 @@ XG_HD const uint32_t* wide_mask(const Tables& t, int32_t lo, int32_t depth) {
   return nullptr;
 }
 
-XG_HD void add_delimiter(const Warp& w, const Delim& d, int32_t pos, uint32_t* out) {
+XG_SHARED void add_delimiter(const Warp& w, const Delim& d, int32_t pos, uint32_t* out) {
   warp_for(w, delim_begin(d, pos), delim_end(d, pos), [&](int32_t i) { set_bit(out, d.tok[i]); });
 }
 
@@ -1240,12 +1338,13 @@ XG_COLD void add_label_tokens(const Ctx& c, const XgState& s, uint32_t* out) {
   } else {
     const int32_t relations = s.rel_hi - s.rel_lo;
     const int32_t version = version_of(c);
+    #pragma unroll 1
     for (int32_t p = 0; p < (s.subj_hi - s.subj_lo) * relations; ++p) {
       const int32_t e = t.ent.owner[s.subj_lo + p / relations];
       const int32_t r = t.rel.owner[s.rel_lo + p % relations];
       const Edges g = edges_of(t, version, e);
       int32_t a, b;
-      relation_slice(g, r, a, b);
+      relation_slice(t, g, r, a, b);
       const int32_t x = lower_index(g.obj, a, b, lo);
       const int32_t y = lower_index(g.obj, x, b, hi);
       warp_for(c.w, x, y, [&](int32_t i) {
@@ -1283,24 +1382,24 @@ XG_HD void build_mask(const Ctx& c, const XgState& s) {
 #if XG_GPU
     uint4* to = reinterpret_cast<uint4*>(delta);
     const int32_t quads = t.words_padded >> 2;
+    #pragma unroll 1
     for (int32_t i = c.w.lane; i < quads; i += 32) to[i] = make_uint4(0u, 0u, 0u, 0u);
     __syncwarp();
 #else
+    #pragma unroll 1
     for (int32_t i = 0; i < t.words_padded; ++i) delta[i] = 0u;
 #endif
     if (scan) add_label_tokens(c, s, delta);
-    if (s.close_pos > 0)
-      add_delimiter(c.w, t.closer, s.close_pos, delta);
-    else if (s.flags & kMayClose)
-      add_delimiter(c.w, t.closer, 0, delta);
-    if (s.sep_pos > 0)
-      add_delimiter(c.w, t.separator, s.sep_pos, delta);
-    else if (s.flags & kMaySep)
-      add_delimiter(c.w, t.separator, 0, delta);
-    if (s.esc_pos > 0)
-      add_delimiter(c.w, t.escape, s.esc_pos, delta);
-    else if (s.flags & kMayEsc)
-      add_delimiter(c.w, t.escape, 0, delta);
+    // each delimiter branch: its next tokens from where it stands, or from its start when
+    // the flags let it begin here
+    const int32_t close = s.close_pos > 0 ? s.close_pos : (s.flags & kMayClose) ? 0 : -1;
+    const int32_t sep = s.sep_pos > 0 ? s.sep_pos : (s.flags & kMaySep) ? 0 : -1;
+    const int32_t esc = s.esc_pos > 0 ? s.esc_pos : (s.flags & kMayEsc) ? 0 : -1;
+#pragma unroll 1
+    for (int32_t which = 0; which < 3; ++which) {
+      const int32_t pos = which == 0 ? close : which == 1 ? sep : esc;
+      if (pos >= 0) add_delimiter(c.w, which == 0 ? t.closer : which == 1 ? t.separator : t.escape, pos, delta);
+    }
     warp_sync();
   }
   if (c.w.leader()) {

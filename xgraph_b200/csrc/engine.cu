@@ -390,6 +390,7 @@ int check_layout(const XgLayout& l) {
   if (l.ent_cols < 1 || l.rel_cols < 1) return fail(XG_EINVAL, "layout: column tables missing");
   const int64_t required[] = {l.ent_tok, l.ent_off, l.ent_owner, l.rel_tok, l.rel_off, l.rel_owner,
                               l.ent_col, l.rel_col, l.ent_first, l.rel_first, l.row_degree, l.row_first,
+                              l.run_off, l.runs, l.run_rel, l.edge_first,
                               l.ent_first_row, l.ent_rows_off, l.ent_rows, l.adj_off, l.edge_rel,
                               l.edge_obj, l.root_mask, l.free_next, l.free_mask, l.esc_next,
                               l.esc_mask, l.eos_mask, l.closer_off, l.closer_tok, l.closer_next,
@@ -434,6 +435,10 @@ void bind_tables(XgEngine* e) {
   t.adj_off = at<int32_t>(b, l.adj_off);
   t.edge_rel = at<int32_t>(b, l.edge_rel);
   t.edge_obj = at<int32_t>(b, l.edge_obj);
+  t.run_off = at<int32_t>(b, l.run_off);
+  t.runs = at<int32_t>(b, l.runs);
+  t.run_rel = at<int32_t>(b, l.run_rel);
+  t.edge_first = at<int32_t>(b, l.edge_first);
   t.sitelinks = e->options.sitelinks_rank ? at<int32_t>(b, l.sitelinks) : nullptr;
   t.kept_prefix = at<int32_t>(b, l.kept_prefix);
   t.root_mask = at<uint32_t>(b, l.root_mask);

@@ -68,6 +68,10 @@ SeamEngine* xgs_create(const void* blob, const XgLayout* l, const XgOptions* o, 
   t.adj_off = at<int32_t>(b, l->adj_off);
   t.edge_rel = at<int32_t>(b, l->edge_rel);
   t.edge_obj = at<int32_t>(b, l->edge_obj);
+  t.run_off = at<int32_t>(b, l->run_off);
+  t.runs = at<int32_t>(b, l->runs);
+  t.run_rel = at<int32_t>(b, l->run_rel);
+  t.edge_first = at<int32_t>(b, l->edge_first);
   t.sitelinks = o->sitelinks_rank ? at<int32_t>(b, l->sitelinks) : nullptr;
   t.kept_prefix = at<int32_t>(b, l->kept_prefix);
   t.root_mask = at<uint32_t>(b, l->root_mask);
@@ -194,5 +198,13 @@ void xgs_memory(SeamEngine* e, int32_t n, int32_t* out) {
 }
 
 int32_t xgs_memory_ints(SeamEngine* e) { return e->t.memory_ints; }
+
+// The edge range [out[0], out[1]) of `relation` in entity's adjacency (relative to the
+// entity's first edge) and out[2] = the adjacency length, in KG version `version`.
+void xgs_relation_slice(SeamEngine* e, int32_t version, int32_t entity, int32_t relation, int32_t* out) {
+  const Edges g = edges_of(e->t, version, entity);
+  relation_slice(e->t, g, relation, out[0], out[1]);
+  out[2] = g.n;
+}
 
 }  // extern "C"

@@ -51,7 +51,7 @@ class XgLayout(ctypes.Structure):
             "closer_off", "closer_tok", "closer_next", "separator_off", "separator_tok",
             "separator_next", "escape_off", "escape_tok", "escape_next",
             "ver_off", "ver_subj", "ver_adj", "ver_edge_rel", "ver_edge_obj", "dstep", "row_degree",
-            "row_first")]
+            "row_first", "run_off", "runs", "run_rel", "edge_first")]
     )
 
 
@@ -265,6 +265,41 @@ class PackedTables:
     words_padded: int
 
 
+def _relation_runs(index, entities: int, first_row: np.ndarray, ent_owner: np.ndarray) -> dict:
+    """Per entity, its adjacency cut into runs of one relation (the edges are sorted by
+    relation within an entity): `run_off` [entities + 1] CSR offsets, `runs` the (relation,
+    first edge) pairs closed by (INT32_MAX, edges), `run_rel` their relations alone; and
+    `edge_first`, the first label row of each edge's object with bit 31 set when the object
+    entity has no triples.  A lookup of one relation's objects then scans an entity's runs,
+    not its edges, and the next path frontier reads its keys without an owner hop."""
+    offsets = np.asarray(index.adjacency_offsets, dtype=np.int64)
+    rel = np.asarray(index.edge_relations, dtype=np.int32)
+    obj = np.asarray(index.edge_objects, dtype=np.int64)
+    edges = len(rel)
+    degree = np.diff(offsets)
+    subject = np.repeat(np.arange(len(degree), dtype=np.int64), degree)
+    starts = np.ones(edges, dtype=bool)
+    if edges:
+        starts[1:] = (rel[1:] != rel[:-1]) | (subject[1:] != subject[:-1])
+    run_start = np.flatnonzero(starts)
+    run_off = np.zeros(len(degree) + 1, dtype=np.int64)
+    np.cumsum(np.bincount(subject[run_start], minlength=len(degree)), out=run_off[1:])
+    runs = np.empty((len(run_start) + 1, 2), dtype=np.int32)
+    runs[:-1, 0] = rel[run_start]
+    runs[:-1, 1] = _int32("run starts", run_start)
+    runs[-1] = (np.iinfo(np.int32).max, _int32("edges", np.array([edges]))[0])
+    if edges:
+        owner = ent_owner.astype(np.int64)[obj]
+        first = first_row[owner].astype(np.int64)
+        if (first < 0).any():
+            raise ValueError("an edge object has no label row")
+        edge_first = (first | (np.where(degree[owner] == 0, 1, 0) << 31)).astype(np.uint32).view(np.int32)
+    else:
+        edge_first = np.zeros(0, np.int32)
+    return {"run_off": _int32("run offsets", run_off), "runs": runs,
+            "run_rel": np.ascontiguousarray(runs[:-1, 0]), "edge_first": edge_first}
+
+
 def pack_tables(index, tokenizer, syntax, *, escapes: bool, versions=None,
                 unquoted_starts: bool = False, eos_token_ids=()) -> PackedTables:
     vocab = tokenizer.vocab_size
@@ -344,6 +379,7 @@ def pack_tables(index, tokenizer, syntax, *, escapes: bool, versions=None,
         "row_degree": _int32("row degrees", np.diff(np.asarray(index.adjacency_offsets, dtype=np.int64))[owners64]
                              if labels.num_rows else np.zeros(0, np.int64)),
         "ent_rows": ent_rows,
+        **_relation_runs(index, entities, first_row, ent_owner),
         "adj_off": _int32("adjacency offsets", index.adjacency_offsets),
         "edge_rel": _int32("edge relations", index.edge_relations),
         "edge_obj": _int32("edge objects", index.edge_objects),
