@@ -172,11 +172,6 @@ XG_API int xg_mask_host(XgEngine* engine, int32_t sequences, uint32_t* out);
 XG_API int xg_states_host(XgEngine* engine, int32_t sequences, int32_t* out);
 /* Diagnostic: wait, then copy the slots' memory (facts, reached rows, frontier, version). */
 XG_API int xg_memory_host(XgEngine* engine, int32_t sequences, int32_t* out);
-/* Engine::apply_mask (csrc/engine.cu:2990-3037): in place, logits[r, c] = -inf for every
- * column c its slot's mask disallows and every c >= vocab; rows of inactive slots and of
- * slots in the error phase are left untouched.  logits: device, dtype XG_F32/XG_BF16/XG_F16,
- * rows x cols with row_stride elements between rows.  row_slots: device int32[rows].
- * local_pos/input_ids: device int32[rows] for speculative draft rows, or both NULL. */
 /* sync then apply_mask in one launch, for a step without speculative draft rows: logits row
  * i belongs to slots[i] (rows x cols, row_stride elements apart); the other arguments are
  * xg_sync's.  Same results as xg_sync followed by xg_apply_mask with row_slots = slots.
@@ -185,6 +180,17 @@ XG_API int xg_sync_apply(XgEngine* engine, const int32_t* slots, int32_t count, 
                          int64_t history_stride, int64_t history_rows, const int32_t* prompt_len,
                          const int32_t* total_len, int64_t lengths_count, void* logits, int32_t dtype,
                          int32_t cols, int64_t row_stride, void* stream);
+/* Engine::apply_mask (csrc/engine.cu:2990-3037): in place, logits[r, c] = -inf for every
+ * column c its slot's mask disallows and every c >= vocab; rows of inactive slots and of
+ * slots in the error phase are left untouched.  logits: device, dtype XG_F32/XG_BF16/XG_F16,
+ * rows x cols with row_stride elements between rows.  row_slots: device int32[rows].
+ * local_pos/input_ids: device int32[rows] for speculative draft rows, or both NULL.  With
+ * draft rows (csrc/engine.cu:2353-2360), row r at offset k = local_pos[r] of its request's
+ * rows is masked as if input_ids[r - k + 1 .. r] had been committed to its slot, whose state
+ * does not move; a row whose drafts reach the error phase, or with k < 0 or k > r, is left
+ * untouched.  The engine keeps scratch for the largest row count seen (memory and mask rows,
+ * about 4 * (words + 600) bytes per row), allocated on the first call with more rows, after
+ * synchronizing `stream`. */
 XG_API int xg_apply_mask(XgEngine* engine, void* logits, int32_t dtype, int32_t rows, int32_t cols,
                   int64_t row_stride, const int32_t* row_slots, const int32_t* local_pos,
                   const int32_t* input_ids, void* stream);

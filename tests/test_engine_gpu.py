@@ -217,3 +217,67 @@ def test_sync_apply_equals_sync_then_apply_mask(dtype):
         sa, sb = fused.states_host(), plain.states_host()
         for field in sa:
             np.testing.assert_array_equal(sa[field], sb[field], field)
+
+
+@pytest.mark.parametrize("name", ["bpe_norepeat", "bpe_committed", "crowd_committed", "toy_derivation"])
+def test_draft_rows_mask_as_if_committed(name):
+    """apply_mask with local_pos/input_ids (src/xgraph/engine.py:1012-1031): row k of a
+    request's block has the mask of its slot's state after the block's first k drafts (the
+    golden walk's mask k steps later), the slot's state does not move, a row after a
+    disallowed draft and a row whose offset reaches before row 0 are left untouched."""
+    import torch
+
+    case = next(c for c in golden_walks() if c["name"] == name)
+    sequences = case["sequences"]
+    engine, _, served = engine_for(case)
+    start(engine, sequences)
+    vocab = served.vocab_size
+    steps = len(sequences[0]["tokens"])
+    drafts = 5
+    gen = torch.Generator(device="cuda").manual_seed(11)
+    done = 0
+    for committed in (0, 17, steps - drafts - 1):
+        for step in range(done, committed):
+            engine.advance(np.array([seq["tokens"][step] for seq in sequences], dtype=np.int32))
+        done = committed
+        before = engine.states_host()
+        row_slots, local_pos, input_ids, expect = [], [], [], []
+        for k, seq in enumerate(sequences):
+            for j in range(drafts + 1):
+                row_slots.append(k)
+                local_pos.append(j)
+                fed = seq["tokens"][committed + j - 1] if committed + j > 0 else 0
+                input_ids.append(fed)
+                expect.append(unpack(golden_masks()[f"{name}/{k}"][committed + j], vocab))
+        # one more request on slot 0 whose first draft is disallowed: its rows stay untouched
+        allowed0 = unpack(golden_masks()[f"{name}/0"][committed], vocab)
+        bad = next(t for t in range(vocab) if t not in allowed0) if len(allowed0) < vocab else None
+        if bad is not None:
+            for j in range(3):
+                row_slots.append(0)
+                local_pos.append(j)
+                input_ids.append(bad if j == 1 else sequences[0]["tokens"][committed])
+                expect.append(expect[0] if j == 0 else None)
+        # an offset that reaches before row 0
+        row_slots.append(0)
+        local_pos.append(len(row_slots))
+        input_ids.append(0)
+        expect.append(None)
+        rows = len(row_slots)
+        cols = vocab + 3
+        logits = torch.randn((rows, cols), generator=gen, device="cuda")
+        original = logits.clone()
+        as_t = lambda v: torch.tensor(v, dtype=torch.int32, device="cuda")  # noqa: E731
+        engine.apply_mask(logits, as_t(row_slots), local_pos=as_t(local_pos), input_ids=as_t(input_ids))
+        got, was = logits.cpu().numpy(), original.cpu().numpy()
+        for r, want in enumerate(expect):
+            if want is None:
+                np.testing.assert_array_equal(got[r], was[r], err_msg=f"row {r} should be untouched")
+                continue
+            allowed = np.zeros(cols, dtype=bool)
+            allowed[sorted(want)] = True
+            assert np.all(np.isneginf(got[r][~allowed])), (name, committed, r)
+            np.testing.assert_array_equal(got[r][allowed], was[r][allowed])
+        after = engine.states_host()
+        for field in before:
+            np.testing.assert_array_equal(before[field], after[field], field)

@@ -1355,11 +1355,16 @@ XG_COLD void add_label_tokens(const Ctx& c, const XgState& s, uint32_t* out) {
   }
 }
 
-// Record the slot's mask for its current state: outside a span a precomputed table row
-// (base only); inside one the root or wide mask of an unbound label range as base (no
-// copy), and the slot's own buffer row (zeroed, then the label and delimiter tokens) as
-// delta; in the error phase neither.
-XG_HD void build_mask(const Ctx& c, const XgState& s) {
+// A mask as base | delta (either may be null; both null: the error phase, nothing masked).
+struct MaskRef {
+  const uint32_t* base;
+  uint32_t* delta;
+};
+
+// The mask of a state: outside a span a precomputed table row (base only); inside one the
+// root or wide mask of an unbound label range as base (no copy), and the buffer `own`
+// (zeroed, then the label and delimiter tokens) as delta; in the error phase neither.
+XG_HD MaskRef compose_mask(const Ctx& c, const XgState& s, uint32_t* own) {
   const Tables& t = c.t;
   const int64_t stride = t.words_padded;
   const uint32_t* base = nullptr;
@@ -1369,7 +1374,7 @@ XG_HD void build_mask(const Ctx& c, const XgState& s) {
   } else if (s.phase == kEscaped) {
     base = t.esc_mask + s.pos * stride;
   } else if (s.phase == kSpan) {
-    delta = t.masks + c.slot * stride;
+    delta = own;
     bool scan = s.lo >= 0;
     if (scan && unbound(t, c, s)) {
       if (s.depth == 0 && s.lo == 0 && s.hi == t.ent.count) {
@@ -1402,9 +1407,16 @@ XG_HD void build_mask(const Ctx& c, const XgState& s) {
     }
     warp_sync();
   }
+  return MaskRef{base, delta};
+}
+
+// Record the slot's mask for its current state, its own buffer row as the delta.
+XG_HD void build_mask(const Ctx& c, const XgState& s) {
+  const Tables& t = c.t;
+  const MaskRef m = compose_mask(c, s, t.masks + c.slot * static_cast<int64_t>(t.words_padded));
   if (c.w.leader()) {
-    t.base[c.slot] = base;
-    t.delta[c.slot] = delta;
+    t.base[c.slot] = m.base;
+    t.delta[c.slot] = m.delta;
   }
 }
 

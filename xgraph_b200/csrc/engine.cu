@@ -326,6 +326,68 @@ __global__ void __launch_bounds__(kFusedThreads)
   apply_segments<ELT>(t, out, cols, base, delta, neg, 0, (cols + 1023) >> 10, threadIdx.x >> 5, blockDim.x >> 5);
 }
 
+
+// Speculative draft rows (apply_mask with local_pos and input_ids): a request owns
+// consecutive logits rows, one per draft position; row r at offset k = local_pos[r] is
+// masked as if the tokens fed at the request's rows r - k + 1 .. r (input_ids) had been
+// committed to slot row_slots[r], in scratch: a copy of the slot's memory row and a mask
+// row of its own (src/xgraph/engine.py:1012-1031, csrc/engine.cu:2353-2360).  The slot's
+// state and memory do not move.  A row whose drafts reach the error phase, or whose offset
+// reaches before the first row, is left untouched.  Offset 0 reads the slot's own mask.
+struct DraftArgs {
+  const int32_t* row_slots;
+  const int32_t* local_pos;
+  const int32_t* input_ids;
+  int32_t max_slots;
+  int32_t* scratch_memory;  // [rows, memory_ints]
+  uint32_t* scratch_masks;  // [rows, words_padded]
+};
+
+// Scratch bytes per draft row: its memory row and its mask row (both 16-byte multiples).
+inline int64_t draft_row_bytes(const Tables& t) {
+  return (static_cast<int64_t>(t.memory_ints) + t.words_padded) * 4;
+}
+
+template <int ELT>
+__global__ void __launch_bounds__(kFusedThreads)
+    draft_apply_kernel(const __grid_constant__ Tables t, const DraftArgs d, char* logits, int32_t cols,
+                       int64_t stride, uint32_t neg) {
+  __shared__ WarpShared shared;
+  __shared__ MaskRef mask;
+  const int32_t row = blockIdx.x;
+  const int32_t slot = d.row_slots[row];
+  if (slot < 0 || slot >= d.max_slots || !t.active[slot]) return;  // block-uniform
+  if (threadIdx.x < 32) {
+    const int32_t lane = threadIdx.x;
+    const int32_t k = d.local_pos[row];
+    MaskRef m{nullptr, nullptr};
+    if (k == 0) {
+      m = MaskRef{t.base[slot], t.delta[slot]};
+    } else if (k > 0 && k <= row) {
+      int32_t* memory = d.scratch_memory + static_cast<int64_t>(row) * t.memory_ints;
+      const int32_t* own = t.memory + static_cast<int64_t>(slot) * t.memory_ints;
+#pragma unroll 1
+      for (int32_t i = lane; i < t.memory_ints; i += 32) memory[i] = own[i];
+      __syncwarp();
+      Ctx c{t, Warp{lane}, slot, memory, shared.top, shared.scratch};
+      XgState s = t.states[slot];
+#pragma unroll 1
+      for (int32_t j = 1; j <= k && s.phase != kError; ++j) advance_state(c, s, d.input_ids[row - k + j]);
+      if (s.phase != kError) m = compose_mask(c, s, d.scratch_masks + static_cast<int64_t>(row) * t.words_padded);
+    }
+    if (lane == 0) mask = m;
+  }
+  __syncthreads();
+  const MaskRef m = mask;
+  if (m.base == nullptr && m.delta == nullptr) return;  // error: untouched
+  char* out = logits + static_cast<int64_t>(row) * stride * ELT;
+  if ((reinterpret_cast<uintptr_t>(out) & 15u) != 0) {
+    apply_scalar<ELT>(t, out, 0, cols, m.base, m.delta, neg);
+    return;
+  }
+  apply_segments<ELT>(t, out, cols, m.base, m.delta, neg, 0, (cols + 1023) >> 10, threadIdx.x >> 5, blockDim.x >> 5);
+}
+
 }  // namespace xg
 
 // ===========================================================================================
@@ -348,6 +410,8 @@ struct XgEngine {
   int32_t* cursors = nullptr;
   int32_t* active = nullptr;
   int32_t* tokens = nullptr;
+  char* draft_scratch = nullptr;  // apply_mask's draft rows: [rows] memory rows, then [rows] mask rows
+  int32_t draft_capacity = 0;     // rows it holds
   Tables t{};
 };
 
@@ -495,6 +559,7 @@ void release(XgEngine* e) {
   cudaFree(e->cursors);
   cudaFree(e->active);
   cudaFree(e->tokens);
+  cudaFree(e->draft_scratch);
   delete e;
 }
 
@@ -579,6 +644,29 @@ int launch_step(XgEngine* e, const StepArgs& a, void* stream) {
   step_kernel<<<static_cast<unsigned>((a.count + kWarpsPerBlock - 1) / kWarpsPerBlock), kWarpsPerBlock * 32, 0,
                 as_stream(stream)>>>(e->t, a);
   XG_CUDA(cudaGetLastError(), "step kernel");
+  return XG_OK;
+}
+
+char* data_of(void* logits) { return static_cast<char*>(logits); }
+
+// Launch the draft-row kernel with scratch for `rows` rows at `scratch` (memory rows first).
+int launch_drafts(XgEngine* e, char* logits, int32_t dtype, int32_t rows, int32_t cols, int64_t row_stride,
+                  const int32_t* row_slots, const int32_t* local_pos, const int32_t* input_ids, char* scratch,
+                  void* stream) {
+  DraftArgs d{};
+  d.row_slots = row_slots;
+  d.local_pos = local_pos;
+  d.input_ids = input_ids;
+  d.max_slots = e->max_sequences;
+  d.scratch_memory = reinterpret_cast<int32_t*>(scratch);
+  d.scratch_masks = reinterpret_cast<uint32_t*>(scratch + static_cast<int64_t>(rows) * e->t.memory_ints * 4);
+  cudaStream_t s = as_stream(stream);
+  if (dtype == XG_F32)
+    draft_apply_kernel<4><<<rows, kFusedThreads, 0, s>>>(e->t, d, logits, cols, row_stride, 0xff800000u);
+  else
+    draft_apply_kernel<2><<<rows, kFusedThreads, 0, s>>>(e->t, d, logits, cols, row_stride,
+                                                          dtype == XG_BF16 ? 0xff80u : 0xfc00u);
+  XG_CUDA(cudaGetLastError(), "draft apply kernel");
   return XG_OK;
 }
 
@@ -797,13 +885,32 @@ int xg_apply_mask(XgEngine* e, void* logits, int32_t dtype, int32_t rows, int32_
                   const int32_t* row_slots, const int32_t* local_pos, const int32_t* input_ids, void* stream) {
   if (!e) return fail(XG_EINVAL, "null engine");
   if ((local_pos == nullptr) != (input_ids == nullptr)) return fail(XG_EINVAL, "local_pos and input_ids go together");
-  if (local_pos) return fail(XG_EINVAL, "speculative draft rows are not supported by this engine version");
   if (rows < 0 || cols < 0 || row_stride < cols) return fail(XG_EINVAL, "logits need one contiguous row per entry of row_slots");
   if (dtype != XG_F32 && dtype != XG_BF16 && dtype != XG_F16) return fail(XG_EINVAL, "logits must be float32, bfloat16 or float16");
   if (rows == 0 || cols == 0) return XG_OK;
   if (!logits || !row_slots) return fail(XG_EINVAL, "null argument");
   const int elt = dtype == XG_F32 ? 4 : 2;
   if (reinterpret_cast<uintptr_t>(logits) % elt) return fail(XG_EINVAL, "logits are not aligned to their element size");
+  if (local_pos) {
+    // draft rows: scratch for every row, grown (never shrunk) when a call has more rows
+    // than any before it (the reference grows its row buffers the same way,
+    // csrc/engine.cu:3006-3014)
+    if (rows > e->draft_capacity) {
+      XG_CUDA(cudaStreamSynchronize(as_stream(stream)), "draft scratch growth");
+      cudaFree(e->draft_scratch);
+      e->draft_scratch = nullptr;
+      e->draft_capacity = 0;
+      const cudaError_t err = cudaMalloc(&e->draft_scratch, static_cast<size_t>(rows) * draft_row_bytes(e->t));
+      if (err != cudaSuccess) {
+        e->draft_scratch = nullptr;
+        cudaGetLastError();
+        return fail(XG_ENOMEM, std::string("draft scratch allocation failed: ") + cudaGetErrorString(err));
+      }
+      e->draft_capacity = rows;
+    }
+    return launch_drafts(e, data_of(logits), dtype, rows, cols, row_stride, row_slots, local_pos, input_ids,
+                         e->draft_scratch, stream);
+  }
   // Split each row into `chunks` CTAs so that the grid is about one wave of resident CTAs
   // (each CTA then runs long enough to hide its few dependent pointer loads).
   const int64_t per_row_max = ((static_cast<int64_t>(cols) + 1023) / 1024 + 7) / 8;  // >= 8 segments per CTA

@@ -385,7 +385,15 @@ class Engine:
 
     def apply_mask(self, logits, row_slots, stream: int = 0, *, local_pos=None, input_ids=None) -> None:
         """Set every logit its slot's mask disallows (and every column past the served
-        vocabulary) to -inf, in place; rows of inactive slots and error rows are untouched."""
+        vocabulary) to -inf, in place; rows of inactive slots and error rows are untouched.
+
+        Under speculative decoding a request owns consecutive rows, one per draft position
+        (src/xgraph/engine.py:1012-1031): local_pos[i] is row i's offset among its
+        request's rows and input_ids[i] the token fed at row i (the last committed token at
+        offset 0, then the drafts).  Row i is masked as if the tokens fed at its request's
+        earlier rows after the first had been committed; the slot's state does not move.
+        A row whose drafts leave the language (the error phase), or whose offset reaches
+        before row 0, is left untouched."""
         import torch
 
         if (local_pos is None) != (input_ids is None):
@@ -400,17 +408,21 @@ class Engine:
             raise ValueError("logits need one contiguous row per entry of row_slots")
         drafts = (ctypes.c_void_p(0), ctypes.c_void_p(0))
         if local_pos is not None:
-            drafts = (self._row_slots(local_pos)[0], self._row_slots(input_ids)[0])
+            pos_ptr, pos_n = self._row_slots(local_pos, "local_pos")
+            ids_ptr, ids_n = self._row_slots(input_ids, "input_ids")
+            if pos_n != n or ids_n != n:
+                raise ValueError("local_pos and input_ids need one entry per logits row")
+            drafts = (pos_ptr, ids_ptr)
         _check(self._lib.xg_apply_mask(
             self._handle, ctypes.c_void_p(logits.data_ptr()), dtype, n, logits.shape[1],
             logits.stride(0) if n > 1 else logits.shape[1], ptr, drafts[0], drafts[1], _stream(stream)))
 
-    def _row_slots(self, row_slots):
+    def _row_slots(self, row_slots, name="row_slots"):
         import torch
 
         if (not isinstance(row_slots, torch.Tensor) or not row_slots.is_cuda
-                or row_slots.dtype != torch.int32 or row_slots.dim() != 1):
-            raise ValueError("row_slots must be a 1-D int32 tensor on the GPU")
+                or row_slots.dtype != torch.int32 or row_slots.dim() != 1 or not row_slots.is_contiguous()):
+            raise ValueError(f"{name} must be a contiguous 1-D int32 tensor on the GPU")
         return ctypes.c_void_p(row_slots.data_ptr()), len(row_slots)
 
     @property
