@@ -194,6 +194,21 @@ XG_API int xg_sync_apply(XgEngine* engine, const int32_t* slots, int32_t count, 
 XG_API int xg_apply_mask(XgEngine* engine, void* logits, int32_t dtype, int32_t rows, int32_t cols,
                   int64_t row_stride, const int32_t* row_slots, const int32_t* local_pos,
                   const int32_t* input_ids, void* stream);
+/* No counterpart in the reference: xg_apply_mask for draft rows (local_pos and input_ids
+ * required) that allocates nothing, for callers that may not allocate device memory while
+ * they decode (a serving loop whose framework has already claimed the free memory for its
+ * own pools, or code that must not take the synchronizing growth path of xg_apply_mask).
+ * Its scratch is one static 8 MiB device array in this library, shared by every call on
+ * the device: a call with more rows than fit (4 * (words + 600) bytes per row) fails with
+ * XG_EINVAL and launches nothing.  No part of the array needs to start at zero (each row's
+ * memory copy and mask row is written before it is read).  Calls whose kernels overlap on
+ * the GPU (other streams, other engines, other threads) race on the array: order them.
+ * The first call on a device looks the array's address up (cudaGetSymbolAddress, with the
+ * engine's device current), which may also load the library's device code; make that first
+ * call before any stream capture.  Same results as xg_apply_mask with the same arguments. */
+XG_API int xg_apply_mask_noalloc(XgEngine* engine, void* logits, int32_t dtype, int32_t rows, int32_t cols,
+                                 int64_t row_stride, const int32_t* row_slots, const int32_t* local_pos,
+                                 const int32_t* input_ids, void* stream);
 
 #ifdef __cplusplus
 }

@@ -14,6 +14,7 @@
 
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include "core.cuh"
@@ -390,6 +391,11 @@ __global__ void __launch_bounds__(kFusedThreads)
 
 }  // namespace xg
 
+// Scratch of xg_apply_mask_noalloc: one array in this library's device image per device,
+// shared by every call on that device (its size is the entry point's whole budget).
+constexpr int64_t kNoAllocScratchBytes = 8ll << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
 // ===========================================================================================
 // C ABI
 
@@ -648,6 +654,28 @@ int launch_step(XgEngine* e, const StepArgs& a, void* stream) {
 }
 
 char* data_of(void* logits) { return static_cast<char*>(logits); }
+
+// g_noalloc_scratch's device address, looked up once per device (with that device current).
+constexpr int kNoAllocDevices = 64;
+std::mutex g_noalloc_lock;
+char* g_noalloc_address[kNoAllocDevices] = {};
+
+int noalloc_scratch(int device, char** out) {
+  if (device < 0 || device >= kNoAllocDevices) return fail(XG_EINVAL, "device ordinal out of range");
+  std::lock_guard<std::mutex> hold(g_noalloc_lock);
+  if (g_noalloc_address[device] == nullptr) {
+    void* address = nullptr;
+    const cudaError_t err = cudaGetSymbolAddress(&address, g_noalloc_scratch);
+    if (err != cudaSuccess || address == nullptr) {
+      cudaGetLastError();
+      return fail(XG_ECUDA, std::string("static draft scratch: cudaGetSymbolAddress failed: ") +
+                                cudaGetErrorString(err));
+    }
+    g_noalloc_address[device] = static_cast<char*>(address);
+  }
+  *out = g_noalloc_address[device];
+  return XG_OK;
+}
 
 // Launch the draft-row kernel with scratch for `rows` rows at `scratch` (memory rows first).
 int launch_drafts(XgEngine* e, char* logits, int32_t dtype, int32_t rows, int32_t cols, int64_t row_stride,
@@ -939,6 +967,35 @@ int xg_apply_mask(XgEngine* e, void* logits, int32_t dtype, int32_t rows, int32_
   }
   XG_CUDA(cudaGetLastError(), "apply kernel");
   return XG_OK;
+}
+
+int xg_apply_mask_noalloc(XgEngine* e, void* logits, int32_t dtype, int32_t rows, int32_t cols, int64_t row_stride,
+                          const int32_t* row_slots, const int32_t* local_pos, const int32_t* input_ids,
+                          void* stream) {
+  if (!e) return fail(XG_EINVAL, "null engine");
+  if (!local_pos || !input_ids)
+    return fail(XG_EINVAL, "xg_apply_mask_noalloc masks draft rows: local_pos and input_ids are required");
+  if (rows < 0 || cols < 0 || row_stride < cols) return fail(XG_EINVAL, "logits need one contiguous row per entry of row_slots");
+  if (dtype != XG_F32 && dtype != XG_BF16 && dtype != XG_F16) return fail(XG_EINVAL, "logits must be float32, bfloat16 or float16");
+  const int64_t per_row = draft_row_bytes(e->t);
+  if (static_cast<int64_t>(rows) * per_row > kNoAllocScratchBytes)
+    return fail(XG_EINVAL, std::to_string(rows) + " draft rows need " + std::to_string(rows * per_row) +
+                               " bytes of scratch; xg_apply_mask_noalloc has " + std::to_string(kNoAllocScratchBytes) +
+                               " (at most " + std::to_string(kNoAllocScratchBytes / per_row) +
+                               " rows with this vocabulary); use xg_apply_mask");
+  if (rows == 0 || cols == 0) return XG_OK;
+  if (!logits || !row_slots) return fail(XG_EINVAL, "null argument");
+  const int elt = dtype == XG_F32 ? 4 : 2;
+  if (reinterpret_cast<uintptr_t>(logits) % elt) return fail(XG_EINVAL, "logits are not aligned to their element size");
+  int device = -1;
+  XG_CUDA(cudaGetDevice(&device), "current device");
+  if (device != e->device)
+    return fail(XG_EINVAL, "call xg_apply_mask_noalloc with the engine's device current (device " +
+                               std::to_string(e->device) + ", current " + std::to_string(device) + ")");
+  char* scratch = nullptr;
+  if (int rc = noalloc_scratch(device, &scratch)) return rc;
+  return launch_drafts(e, data_of(logits), dtype, rows, cols, row_stride, row_slots, local_pos, input_ids, scratch,
+                       stream);
 }
 
 }  // extern "C"
