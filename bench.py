@@ -363,7 +363,7 @@ def engine_arm(args) -> None:
         "kernel_ms": {"median": statistics.median(applies), "mean": statistics.mean(applies),
                       "note": "sync_apply kernel alone (events around it), over the K timed steps"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "peak_kind": peak_kind, "traffic": None,
+                     "peak_kind": peak_kind, **recorded_traffic(args.config, cfg.dtype),
                      "kernel": f"sync_apply_kernel<{elt}> ({cfg.dtype}): sync + mask + apply fused",
                      "algorithmic_bytes_per_launch": statistics.mean(bytes_per_launch)},
         "gpu_launches": launches,
@@ -420,6 +420,22 @@ def e2e_leg(engine, workload, history, restart_t, prompt, total, slots, rows, vo
 
 # ---------------------------------------------------------------------------------------
 # reference arm: the oracle port on the host cores
+
+def recorded_traffic(config: int, dtype: str) -> dict:
+    """DRAM bytes per launch of the fused kernel from the committed ncu capture of the same
+    kernel on the same rows and vocabulary (profiles/sync_apply_paths100k.json), or None
+    for another workload.  The capture's logits writes stay in L2 during the kernel."""
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "profiles", "sync_apply_paths100k.json")
+    if config != 3 or dtype != "bfloat16":
+        return {"traffic": None}
+    try:
+        with open(path) as f:
+            data = json.load(f)
+        return {"traffic": statistics.mean(data["dram_bytes_per_launch"]),
+                "traffic_source": f"ncu capture, {data['workload']}: dram__bytes_read.sum + dram__bytes_write.sum"}
+    except (OSError, KeyError, ValueError):
+        return {"traffic": None}
+
 
 def reference_arm(args) -> None:
     rank, world, _ = dist_env()
