@@ -103,6 +103,7 @@ typedef struct XgLayout {
   int64_t run_rel;     /* int32 [runs]: the relation of each run (the first column of `runs`) */
   int64_t edge_first;  /* int32 [edges]: first label row of each edge's object entity, bit 31 set when
                           that entity has no triples in the base KG */
+  int64_t row_sitelinks; /* int32 [entity_rows]: sitelinks of each label row's owner, or -1 */
 } XgLayout;
 
 /* Span-language policies, as the reference Engine's constructor flags

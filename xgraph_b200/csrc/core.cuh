@@ -43,6 +43,7 @@ constexpr int32_t kMaxSet = 64;       // MAX_FACTS == MAX_REACHED (src/xgraph/or
 constexpr int32_t kMaxHops = 8;       // MAX_PATH_RELATIONS (src/xgraph/oracle.py:177)
 constexpr int32_t kTopCap = 256;      // per-warp candidate buffer of the top-64 selections
 constexpr int32_t kItemBatch = 1;     // rounds of slice items whose loads are issued together
+constexpr int32_t kLoadBatch = 4;     // warp_for_loaded: rounds whose loads are issued together
 constexpr int32_t kScratchInts = 2 * kMaxSet + 2 + 2 * kMaxSet + kMaxSet;
 constexpr int8_t kReject = -1;
 constexpr int8_t kComplete = -2;
@@ -122,6 +123,7 @@ struct Tables {
   const int32_t* run_rel;     // [runs]: the relation of each run
   const int32_t* edge_first;  // [edges]: object's first label row, bit 31 = the object has no triples
   const int32_t* sitelinks;    // null unless the sitelink rank is on
+  const int32_t* row_sitelinks;  // the same per label row (no owner hop); null unless the rank is on
   const int32_t* kept_prefix;  // null unless some rows are not unbound candidates
   const uint32_t* root_mask;
   const int64_t* wide_keys;
@@ -209,6 +211,34 @@ XG_HD void warp_for(const Warp& w, int32_t begin, int32_t end, F f) {
 }
 
 // The least key(i) over i in [begin, end) (max_key() when empty).
+// warp_for over [begin, end) whose body is split into load(i), independent memory reads,
+// and use(i, loaded): the loads of kLoadBatch rounds are issued together before their
+// uses run, so a long range costs one memory round trip per kLoadBatch rounds while the
+// loop's code stays short.
+template <class L, class U>
+XG_HD void warp_for_loaded(const Warp& w, int32_t begin, int32_t end, L load, U use) {
+#if XG_GPU
+#pragma unroll 1
+  for (int32_t base = begin; base < end; base += 32 * kLoadBatch) {
+    decltype(load(0)) v[kLoadBatch];
+#pragma unroll
+    for (int32_t b = 0; b < kLoadBatch; ++b) {
+      const int32_t i = base + 32 * b + w.lane;
+      if (i < end) v[b] = load(i);
+    }
+#pragma unroll
+    for (int32_t b = 0; b < kLoadBatch; ++b) {
+      const int32_t i = base + 32 * b + w.lane;
+      if (i < end) use(i, v[b]);
+    }
+  }
+#else
+  (void)w;
+#pragma unroll 1
+  for (int32_t i = begin; i < end; ++i) use(i, load(i));
+#endif
+}
+
 template <class F>
 XG_HD Key warp_min(const Warp& w, int32_t begin, int32_t end, F key) {
   Key best = max_key();
@@ -444,6 +474,18 @@ XG_SHARED void narrow(const Warp& w, const Rows& r, int32_t& lo, int32_t& hi, in
     hi = r.first[token + 1];
     return;
   }
+#if XG_GPU
+  if (hi - lo <= 32) {  // both bounds from one load per lane
+    const int32_t row = lo + w.lane;
+    const int32_t col = row < hi ? column(r, row, depth) : 0x7fffffff;
+    const uint32_t ge = __ballot_sync(0xffffffffu, col >= token);
+    const uint32_t gt = __ballot_sync(0xffffffffu, col > token);
+    const int32_t a = ge ? lo + __ffs(ge) - 1 : hi;
+    hi = gt ? lo + __ffs(gt) - 1 : hi;
+    lo = a;
+    return;
+  }
+#endif
   const int32_t a = bound_row(w, r, lo, hi, depth, token, false);
   hi = bound_row(w, r, a, hi, depth, token, true);
   lo = a;
@@ -560,10 +602,18 @@ XG_HD int32_t row_degree(const Tables& t, int32_t version, int32_t row) {
 
 // Best-connected order key (src/xgraph/oracle.py:1736-1747): most sitelinks (with the
 // sitelink rank), then most adjacency entries in the slot's version, then first row.
+// In the base KG both counts come from row-indexed tables (one round of loads, no owner
+// hop).
 XG_SHARED Key connected_key(const Tables& t, int32_t version, int32_t row) {
-  const int32_t e = t.ent.owner[row];
-  const uint32_t links = t.sitelinks ? static_cast<uint32_t>(t.sitelinks[e]) : 0u;
-  const uint32_t deg = static_cast<uint32_t>(degree(t, version, e));
+  uint32_t links, deg;
+  if (version == 0) {
+    links = t.row_sitelinks ? static_cast<uint32_t>(t.row_sitelinks[row]) : 0u;
+    deg = static_cast<uint32_t>(t.row_degree[row]);
+  } else {
+    const int32_t e = t.ent.owner[row];
+    links = t.sitelinks ? static_cast<uint32_t>(t.sitelinks[e]) : 0u;
+    deg = static_cast<uint32_t>(degree(t, version, e));
+  }
   return Key{(static_cast<uint64_t>(~links) << 32) | static_cast<uint64_t>(~deg), static_cast<uint32_t>(row), 0u};
 }
 
@@ -825,7 +875,7 @@ XG_COLD void reach_rows_of_top(const Ctx& c, int32_t n) {
       [&](bool valid, int32_t, int32_t row) {
         top_push(c.w, ts, valid, Key{static_cast<uint64_t>(static_cast<uint32_t>(row)), 0u, 0u}, kDistinct);
       });
-  top_compact(c.w, ts, kDistinct);
+  if (ts.pushed > 1) top_compact(c.w, ts, kDistinct);  // one key or none: nothing to order
   int32_t* reached = c.mem + kMemReachedRows;
   warp_for(c.w, 0, ts.n, [&](int32_t i) { reached[i] = static_cast<int32_t>(ts.buf[i].a); });
   mem_store(c, kMemReached, ts.n);
@@ -978,7 +1028,7 @@ XG_COLD void next_segment(const Ctx& c, XgState& s, int32_t llo, int32_t lhi) {
       for (int32_t base = llo; base < lhi; base += 32) {
 #if XG_GPU
         const int32_t row = base + c.w.lane;
-        const bool valid = row < lhi && subject_candidate(c, bound, row) && degree(t, version, t.ent.owner[row]) > 0;
+        const bool valid = row < lhi && subject_candidate(c, bound, row) && row_degree(t, version, row) > 0;
         Key k{0, 0, 0};
         if (valid) {
           if (t.committed)
@@ -990,7 +1040,7 @@ XG_COLD void next_segment(const Ctx& c, XgState& s, int32_t llo, int32_t lhi) {
 #else
         #pragma unroll 1
         for (int32_t row = base; row < lhi && row < base + 32; ++row) {
-          const bool valid = subject_candidate(c, bound, row) && degree(t, version, t.ent.owner[row]) > 0;
+          const bool valid = subject_candidate(c, bound, row) && row_degree(t, version, row) > 0;
           if (!valid) continue;
           const Key k = t.committed ? connected_key(t, version, row)
                                     : Key{static_cast<uint64_t>(static_cast<uint32_t>(t.row_first[row])), 0u, 0u};
@@ -998,7 +1048,7 @@ XG_COLD void next_segment(const Ctx& c, XgState& s, int32_t llo, int32_t lhi) {
         }
 #endif
       }
-      top_compact(c.w, ts, kDistinct);
+      if (ts.pushed > 1) top_compact(c.w, ts, kDistinct);  // one key or none: nothing to order
       int32_t* ents = c.mem + kMemFrontierEnt;
       int32_t* ranks = c.mem + kMemFrontierRank;
       const int32_t n = ts.n;
@@ -1020,7 +1070,7 @@ XG_COLD void next_segment(const Ctx& c, XgState& s, int32_t llo, int32_t lhi) {
     } else if (t.derivation) {
       // one subject: the best-connected candidate with triples
       const Key best = warp_min(c.w, llo, lhi, [&](int32_t row) {
-        if (!subject_candidate(c, bound, row) || degree(t, version, t.ent.owner[row]) == 0) return max_key();
+        if (!subject_candidate(c, bound, row) || row_degree(t, version, row) == 0) return max_key();
         return connected_key(t, version, row);
       });
       const int32_t row = static_cast<int32_t>(best.b);
@@ -1121,7 +1171,7 @@ XG_COLD void close_span(const Ctx& c, XgState& s, int32_t llo, int32_t lhi) {
 #endif
         }
       }
-      top_compact(c.w, ts, kDistinct);
+      if (ts.pushed > 1) top_compact(c.w, ts, kDistinct);  // one key or none: nothing to order
       reach_rows_of_top(c, ts.n);
     }
     s.last_kind = kFactSpan;
@@ -1303,8 +1353,23 @@ XG_HD const uint32_t* wide_mask(const Tables& t, int32_t lo, int32_t depth) {
   return nullptr;
 }
 
-XG_SHARED void add_delimiter(const Warp& w, const Delim& d, int32_t pos, uint32_t* out) {
-  warp_for(w, delim_begin(d, pos), delim_end(d, pos), [&](int32_t i) { set_bit(out, d.tok[i]); });
+// The tokens that continue the closer, separator and escape branches from byte positions
+// close, sep and esc (-1: that branch is not live), as one lane-parallel loop over the
+// three token lists (their loads issue together).
+XG_SHARED void add_delimiters(const Ctx& c, int32_t close, int32_t sep, int32_t esc, uint32_t* out) {
+  const Tables& t = c.t;
+  const int32_t a0 = close >= 0 ? delim_begin(t.closer, close) : 0;
+  const int32_t n0 = close >= 0 ? delim_end(t.closer, close) - a0 : 0;
+  const int32_t a1 = sep >= 0 ? delim_begin(t.separator, sep) : 0;
+  const int32_t n1 = sep >= 0 ? delim_end(t.separator, sep) - a1 : 0;
+  const int32_t a2 = esc >= 0 ? delim_begin(t.escape, esc) : 0;
+  const int32_t n2 = esc >= 0 ? delim_end(t.escape, esc) - a2 : 0;
+  warp_for_loaded(
+      c.w, 0, n0 + n1 + n2,
+      [&](int32_t i) {
+        return i < n0 ? t.closer.tok[a0 + i] : i < n0 + n1 ? t.separator.tok[a1 + i - n0] : t.escape.tok[a2 + i - n0 - n1];
+      },
+      [&](int32_t, int32_t token) { set_bit(out, token); });
 }
 
 // Label tokens that keep a live label branch alive: the column at `depth` of every
@@ -1314,12 +1379,11 @@ XG_COLD void add_label_tokens(const Ctx& c, const XgState& s, uint32_t* out) {
   const int32_t d = s.depth, lo = s.lo, hi = s.hi;
   if (s.segment == kSubject) {
     if (unbound(t, c, s)) {
-      warp_for(c.w, lo, hi, [&](int32_t row) {
-        if (kept_row(t, row)) {
-          const int32_t tok = column(t.ent, row, d);
-          if (tok >= 0) set_bit(out, tok);
-        }
-      });
+      warp_for_loaded(
+          c.w, lo, hi, [&](int32_t row) { return kept_row(t, row) ? column(t.ent, row, d) : -1; },
+          [&](int32_t, int32_t tok) {
+            if (tok >= 0) set_bit(out, tok);
+          });
     } else {
       const int32_t* reached = c.mem + kMemReachedRows;
       warp_for(c.w, 0, reached_count(c), [&](int32_t i) {
@@ -1331,10 +1395,14 @@ XG_COLD void add_label_tokens(const Ctx& c, const XgState& s, uint32_t* out) {
       });
     }
   } else if (s.segment == kRelation) {
-    warp_for(c.w, lo, hi, [&](int32_t row) {
-      const int32_t tok = column(t.rel, row, d);
-      if (tok >= 0 && has_relation(c, t.rel.owner[row])) set_bit(out, tok);
-    });
+    struct TokenOwner {
+      int32_t tok, owner;
+    };
+    warp_for_loaded(
+        c.w, lo, hi, [&](int32_t row) { return TokenOwner{column(t.rel, row, d), t.rel.owner[row]}; },
+        [&](int32_t, TokenOwner x) {
+          if (x.tok >= 0 && has_relation(c, x.owner)) set_bit(out, x.tok);
+        });
   } else {
     const int32_t relations = s.rel_hi - s.rel_lo;
     const int32_t version = version_of(c);
@@ -1400,11 +1468,7 @@ XG_HD MaskRef compose_mask(const Ctx& c, const XgState& s, uint32_t* own) {
     const int32_t close = s.close_pos > 0 ? s.close_pos : (s.flags & kMayClose) ? 0 : -1;
     const int32_t sep = s.sep_pos > 0 ? s.sep_pos : (s.flags & kMaySep) ? 0 : -1;
     const int32_t esc = s.esc_pos > 0 ? s.esc_pos : (s.flags & kMayEsc) ? 0 : -1;
-#pragma unroll 1
-    for (int32_t which = 0; which < 3; ++which) {
-      const int32_t pos = which == 0 ? close : which == 1 ? sep : esc;
-      if (pos >= 0) add_delimiter(c.w, which == 0 ? t.closer : which == 1 ? t.separator : t.escape, pos, delta);
-    }
+    add_delimiters(c, close, sep, esc, delta);
     warp_sync();
   }
   return MaskRef{base, delta};

@@ -469,7 +469,7 @@ int check_layout(const XgLayout& l) {
                               l.ver_edge_rel, l.ver_edge_obj};
   for (int64_t off : required)
     if (off < 0 || off > l.blob_bytes || off % 16) return fail(XG_EINVAL, "layout: table offset outside the blob");
-  const int64_t optional[] = {l.sitelinks, l.kept_prefix, l.wide_keys, l.wide_masks, l.dstep};
+  const int64_t optional[] = {l.sitelinks, l.row_sitelinks, l.kept_prefix, l.wide_keys, l.wide_masks, l.dstep};
   for (int64_t off : optional)
     if (off != -1 && (off < 0 || off > l.blob_bytes || off % 16))
       return fail(XG_EINVAL, "layout: optional table offset outside the blob");
@@ -510,6 +510,7 @@ void bind_tables(XgEngine* e) {
   t.run_rel = at<int32_t>(b, l.run_rel);
   t.edge_first = at<int32_t>(b, l.edge_first);
   t.sitelinks = e->options.sitelinks_rank ? at<int32_t>(b, l.sitelinks) : nullptr;
+  t.row_sitelinks = e->options.sitelinks_rank ? at<int32_t>(b, l.row_sitelinks) : nullptr;
   t.kept_prefix = at<int32_t>(b, l.kept_prefix);
   t.root_mask = at<uint32_t>(b, l.root_mask);
   t.wide_keys = at<int64_t>(b, l.wide_keys);
@@ -575,7 +576,7 @@ int create(const void* blob, bool on_device, const XgLayout* layout, const XgOpt
   *out = nullptr;
   if (max_sequences < 1) return fail(XG_EINVAL, "max_sequences must be at least 1, got " + std::to_string(max_sequences));
   if (int rc = check_layout(*layout)) return rc;
-  if (options->sitelinks_rank && layout->sitelinks < 0)
+  if (options->sitelinks_rank && (layout->sitelinks < 0 || layout->row_sitelinks < 0))
     return fail(XG_EINVAL, "the sitelink rank needs a KG index with sitelink counts");
   XgEngine* e = new XgEngine();
   e->layout = *layout;

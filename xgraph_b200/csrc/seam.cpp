@@ -73,6 +73,7 @@ SeamEngine* xgs_create(const void* blob, const XgLayout* l, const XgOptions* o, 
   t.run_rel = at<int32_t>(b, l->run_rel);
   t.edge_first = at<int32_t>(b, l->edge_first);
   t.sitelinks = o->sitelinks_rank ? at<int32_t>(b, l->sitelinks) : nullptr;
+  t.row_sitelinks = o->sitelinks_rank ? at<int32_t>(b, l->row_sitelinks) : nullptr;
   t.kept_prefix = at<int32_t>(b, l->kept_prefix);
   t.root_mask = at<uint32_t>(b, l->root_mask);
   t.wide_keys = at<int64_t>(b, l->wide_keys);

@@ -51,7 +51,8 @@ class XgLayout(ctypes.Structure):
             "closer_off", "closer_tok", "closer_next", "separator_off", "separator_tok",
             "separator_next", "escape_off", "escape_tok", "escape_next",
             "ver_off", "ver_subj", "ver_adj", "ver_edge_rel", "ver_edge_obj", "dstep", "row_degree",
-            "row_first", "run_off", "runs", "run_rel", "edge_first")]
+            "row_first", "run_off", "runs", "run_rel", "edge_first",
+            "row_sitelinks")]
     )
 
 
@@ -401,6 +402,7 @@ def pack_tables(index, tokenizer, syntax, *, escapes: bool, versions=None,
         optional["dstep"] = dstep
     if index.sitelinks is not None:
         optional["sitelinks"] = _int32("sitelinks", index.sitelinks)
+        optional["row_sitelinks"] = optional["sitelinks"][owners64] if labels.num_rows else np.zeros(0, np.int32)
     if kept_prefix is not None:
         optional["kept_prefix"] = kept_prefix
     if len(wide_keys):
@@ -417,7 +419,7 @@ def pack_tables(index, tokenizer, syntax, *, escapes: bool, versions=None,
         pad = (-len(data)) % ALIGN
         pieces.append(b"\0" * pad)
         cursor += len(data) + pad
-    for name in ("sitelinks", "kept_prefix", "wide_keys", "wide_masks", "dstep"):
+    for name in ("sitelinks", "row_sitelinks", "kept_prefix", "wide_keys", "wide_masks", "dstep"):
         if name not in optional:
             setattr(layout, name, -1)
     blob = np.frombuffer(b"".join(pieces) or b"\0" * ALIGN, dtype=np.uint8).copy()
