@@ -17,17 +17,17 @@
 #include "layout.h"
 
 // XG_HD: small helpers, inlined.  XG_COLD: the rare, heavy transitions (closing a span,
-// changing segment, frontiers, sorts), kept out of line so that the per-token hot path
-// stays a few kilobytes of code: a decode step starts with a cold instruction cache, and
-// every fetch of a cold code line costs an HBM round trip.  XG_SHARED: helpers that one
-// step calls from several places (candidate tests, row bounds, adjacency lookups), kept
-// as one out-of-line copy so that each of their code lines is fetched once per step.
-// Loops are kept rolled (#pragma unroll 1) for the same reason, except short scans whose
-// loads must issue together.
+// changing segment, frontiers, sorts) and the adjacency lookups they share, kept out of
+// line so that the per-token path stays a few kilobytes of code: a decode step starts
+// with its code out of the instruction caches and out of L2, and every jump to a code
+// line not yet fetched costs a memory round trip (straight-line code streams in well).
+// XG_SHARED: helpers of the per-token path (candidate tests, row bounds, flags), inlined
+// into it.  Loops are kept rolled (#pragma unroll 1) except short scans whose loads must
+// issue together.
 #if defined(__CUDACC__)
 #define XG_HD __device__ __forceinline__
 #define XG_COLD __device__ __noinline__
-#define XG_SHARED __device__ __noinline__
+#define XG_SHARED __device__ __forceinline__
 #define XG_GPU 1
 #else
 #include <algorithm>
@@ -536,7 +536,7 @@ struct Edges {
 
 // An entity's adjacency in a KG version: the version's own list for an edited subject,
 // else the base CSR slice (src/xgraph/kgversions.py:14-21, the layout both share).
-XG_SHARED Edges edges_of(const Tables& t, int32_t version, int32_t e) {
+XG_COLD Edges edges_of(const Tables& t, int32_t version, int32_t e) {
   if (version > 0) {
     const int32_t a = t.ver_off[version - 1], b = t.ver_off[version];
     const int32_t at = lower_index(t.ver_subj, a, b, e);
@@ -557,11 +557,11 @@ XG_HD int32_t edge_first_row(const Tables& t, const Edges& g, int32_t i) {
 
 // The objects of one relation within an adjacency list: [first, last) indexes (equal when
 // the relation is absent).  In the base KG the entity's relation runs are searched: while
-// more than 16 remain, 15 evenly spaced pivots narrow them to one bucket; the pivots' lines
-// are prefetched together and then compared, so a round costs one memory latency and the
-// loops stay rolled (short code: a step's instruction fetches start cold).  A version's
-// own list is searched by halving.
-XG_SHARED void relation_slice(const Tables& t, const Edges& g, int32_t relation, int32_t& first, int32_t& last) {
+// more than 16 remain, 15 evenly spaced pivots (loaded together) narrow them to one
+// bucket; the <= 16 runs left are scanned four (relation, first edge) pairs per round of
+// independent loads, so a lookup costs one or two memory round trips with short, rolled
+// code.  A version's own list is searched by halving.
+XG_COLD void relation_slice(const Tables& t, const Edges& g, int32_t relation, int32_t& first, int32_t& last) {
   first = last = 0;
   if (g.runs < 0) {
     first = lower_index(g.rel, 0, g.n, relation);
@@ -572,23 +572,37 @@ XG_SHARED void relation_slice(const Tables& t, const Edges& g, int32_t relation,
 #pragma unroll 1
   while (n > 16) {
     const int32_t step = (n + 15) >> 4;
-#pragma unroll 1
-    for (int32_t j = 0; j < 15 && (j + 1) * step <= n; ++j) prefetch_l1(t.run_rel + lo + (j + 1) * step - 1);
     int32_t skip = 0;
-#pragma unroll 1
-    while (skip < 15 && (skip + 1) * step <= n && t.run_rel[lo + (skip + 1) * step - 1] < relation) ++skip;
+#pragma unroll
+    for (int32_t j = 0; j < 15; ++j) {
+      const int32_t p = (j + 1) * step;  // bucket j ends before p
+      skip += p <= n && t.run_rel[lo + p - 1] < relation;
+    }
     lo += skip * step;
     n = n - skip * step < step ? n - skip * step : step;
   }
-  // the <= 16 runs left and the one after them (its first edge ends the match)
-  prefetch_l1(t.runs + 2 * lo);
-  prefetch_l1(t.runs + 2 * (lo + n));
-  int32_t j = 0;
+  // runs[2 k] is run k's relation, runs[2 k + 1] its first edge; the run after the last
+  // one of the window closes it (the table ends with a sentinel run)
 #pragma unroll 1
-  while (j < n && t.runs[2 * (lo + j)] < relation) ++j;
-  if (j < n && t.runs[2 * (lo + j)] == relation) {
-    first = t.runs[2 * (lo + j) + 1] - g.start;
-    last = t.runs[2 * (lo + j) + 3] - g.start;
+  for (int32_t j = 0; j < n; j += 4) {
+    int32_t rel[4], at[5];
+#pragma unroll
+    for (int32_t b = 0; b < 4; ++b) {
+      const bool in = j + b < n;
+      rel[b] = in ? t.runs[2 * (lo + j + b)] : 0x7fffffff;
+      at[b] = in ? t.runs[2 * (lo + j + b) + 1] : 0;
+    }
+    at[4] = t.runs[2 * (lo + (j + 4 < n ? j + 4 : n)) + 1];
+#pragma unroll
+    for (int32_t b = 0; b < 4; ++b) {
+      if (rel[b] >= relation) {
+        if (rel[b] == relation) {
+          first = at[b] - g.start;
+          last = (b < 3 && j + b + 1 < n ? at[b + 1] : at[4]) - g.start;  // the next run's first edge
+        }
+        return;
+      }
+    }
   }
 }
 
@@ -857,6 +871,49 @@ XG_COLD int32_t keep_least_rank(const Ctx& c, int32_t n) {
 #endif
 }
 
+#if XG_GPU
+// The distinct values among buf[0, n).a (n <= 64, each below 2^31) in ascending order into
+// out[0, m); returns m.  A bitonic network over 64 values held two per lane and exchanged
+// by shuffles: no shared-memory traffic and ~300 instructions, against a shared-memory
+// sort of 16-byte keys.
+XG_COLD int32_t sort_unique64(const Warp& w, const Key* buf, int32_t n, int32_t* out) {
+  const int32_t lane = w.lane;
+  int32_t v0 = lane < n ? static_cast<int32_t>(buf[lane].a) : 0x7fffffff;
+  int32_t v1 = lane + 32 < n ? static_cast<int32_t>(buf[lane + 32].a) : 0x7fffffff;
+#pragma unroll 1
+  for (int32_t k = 2; k <= 64; k <<= 1) {
+#pragma unroll 1
+    for (int32_t j = k >> 1; j > 0; j >>= 1) {
+      if (j == 32) {  // partners in the two halves of the same lane (k == 64: ascending)
+        const int32_t lo = v0 < v1 ? v0 : v1;
+        v1 = v0 < v1 ? v1 : v0;
+        v0 = lo;
+        continue;
+      }
+      const int32_t o0 = __shfl_xor_sync(0xffffffffu, v0, j);
+      const int32_t o1 = __shfl_xor_sync(0xffffffffu, v1, j);
+      const bool low = (lane & j) == 0;  // this element is the lower index of its pair
+      const bool up0 = (lane & k) == 0, up1 = ((lane + 32) & k) == 0;
+      v0 = (low == up0) ? (v0 < o0 ? v0 : o0) : (v0 < o0 ? o0 : v0);
+      v1 = (low == up1) ? (v1 < o1 ? v1 : o1) : (v1 < o1 ? o1 : v1);
+    }
+  }
+  // keep the first of each run of equal values (index order: lanes of v0, then of v1)
+  int32_t p0 = __shfl_up_sync(0xffffffffu, v0, 1);
+  int32_t p1 = __shfl_up_sync(0xffffffffu, v1, 1);
+  const int32_t last0 = __shfl_sync(0xffffffffu, v0, 31);
+  if (lane == 0) p1 = last0;
+  const bool keep0 = v0 != 0x7fffffff && (lane == 0 || v0 != p0);
+  const bool keep1 = v1 != 0x7fffffff && v1 != p1;
+  const uint32_t m0 = __ballot_sync(0xffffffffu, keep0), m1 = __ballot_sync(0xffffffffu, keep1);
+  const uint32_t below = (1u << lane) - 1u;
+  if (keep0) out[__popc(m0 & below)] = v0;
+  if (keep1) out[__popc(m0) + __popc(m1 & below)] = v1;
+  __syncwarp();
+  return __popc(m0) + __popc(m1);
+}
+#endif
+
 // The rows of the entities whose first rows are given by keys c.top[0, n) (low 32 bits of
 // a), sorted, first 64 (src/xgraph/oracle.py:697-703 _rows_for, capped as reached).
 // Writes them to the slot's reached list.
@@ -875,8 +932,16 @@ XG_COLD void reach_rows_of_top(const Ctx& c, int32_t n) {
       [&](bool valid, int32_t, int32_t row) {
         top_push(c.w, ts, valid, Key{static_cast<uint64_t>(static_cast<uint32_t>(row)), 0u, 0u}, kDistinct);
       });
-  if (ts.pushed > 1) top_compact(c.w, ts, kDistinct);  // one key or none: nothing to order
   int32_t* reached = c.mem + kMemReachedRows;
+#if XG_GPU
+  if (ts.pushed <= 64) {  // every row is still in the buffer: sort them in registers
+    const int32_t m = sort_unique64(c.w, ts.buf, ts.n, reached);
+    mem_store(c, kMemReached, m);
+    warp_sync();
+    return;
+  }
+#endif
+  if (ts.pushed > 1) top_compact(c.w, ts, kDistinct);  // one key or none: nothing to order
   warp_for(c.w, 0, ts.n, [&](int32_t i) { reached[i] = static_cast<int32_t>(ts.buf[i].a); });
   mem_store(c, kMemReached, ts.n);
   warp_sync();
@@ -1283,6 +1348,17 @@ XG_HD void prefetch_span(const Ctx& c, const XgState& s) {
   if (lane < 3) {
     const Delim& d = lane == 0 ? t.closer : lane == 1 ? t.separator : t.escape;
     prefetch_l1(d.tok + d.at[0]);
+  }
+  if (s.segment == kRelation && t.paths && c.mem[kMemVersion] == 0) {
+    // a relation label of a path: the next frontier will read each frontier entity's
+    // adjacency and run offsets; start their lines now (the entities' read from the slot's
+    // memory overlaps the token's)
+    const int32_t count = c.mem[kMemFrontier];
+    if (lane < count) {
+      const int32_t e = c.mem[kMemFrontierEnt + lane];
+      prefetch_l1(t.adj_off + e);
+      prefetch_l1(t.run_off + e);
+    }
   }
   if (s.lo < 0 || s.hi - s.lo > 64) return;
   const Rows& r = s.segment == kRelation ? t.rel : t.ent;

@@ -75,13 +75,15 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
     }
     const int32_t* tokens = a.history + a.stride * slot;
     for (; cursor < end; ++cursor) {
+      const int32_t token = tokens[cursor];  // in flight while the state's reads are started
       if (s.phase == kSpan) prefetch_span(c, s);
-      advance_state(c, s, tokens[cursor]);
+      advance_state(c, s, token);
     }
     if ((threadIdx.x & 31) == 0) t.cursors[slot] = cursor;
   } else {
+    const int32_t token = a.tokens[i];
     if (s.phase == kSpan) prefetch_span(c, s);
-    advance_state(c, s, a.tokens[i]);
+    advance_state(c, s, token);
   }
   store_state(t, slot, s);
   build_mask(c, s);
@@ -307,8 +309,9 @@ __global__ void __launch_bounds__(kFusedThreads)
     if (cursor < end) {
       const int32_t* tokens = a.history + a.stride * slot;
       for (; cursor < end; ++cursor) {
+        const int32_t token = tokens[cursor];  // in flight while the state's reads are started
         if (s.phase == kSpan) prefetch_span(c, s);
-        advance_state(c, s, tokens[cursor]);
+        advance_state(c, s, token);
       }
       store_state(t, slot, s);
       build_mask(c, s);
