@@ -271,7 +271,9 @@ def engine_arm(args) -> None:
     # W warm-up steps, then K timed steps.  A step is begin(restarted slots) + sync_apply
     # (sync and apply_mask fused in one kernel); events bracket the whole step, and a
     # second pair brackets the sync_apply kernel alone (the roofline's kernel).
-    total_steps = args.warmup + args.steps
+    # then (outside the profile mode) up to 128 more steps without the flush: the warm figure
+    warm_steps = 0 if args.profile else min(args.steps, 128)
+    total_steps = args.warmup + args.steps + warm_steps
     assigned, restarts = schedule(lengths, rows, total_steps)
     history = torch.zeros((rows, total_steps + 1), dtype=torch.int32, device=device)
     disallowed = np.zeros(total_steps, dtype=np.int64)  # sum over rows of disallowed columns
@@ -295,13 +297,14 @@ def engine_arm(args) -> None:
     engine.reset()
     stream = torch.cuda.current_stream(device).cuda_stream
     launches = 0
-    step_ms, apply_ms = [], []
+    step_ms, apply_ms, warm_ms = [], [], []
     clocks = None
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     for k in range(total_steps):
-        timed = k >= args.warmup
+        timed = args.warmup <= k < args.warmup + args.steps
+        warm = k >= args.warmup + args.steps
         if timed and clocks is None:
             torch.cuda.synchronize()
             if world > 1:
@@ -309,7 +312,8 @@ def engine_arm(args) -> None:
             clocks = Clocks(local)
             time.sleep(0.3)
             torch.cuda.nvtx.range_push("timed")
-        flush.fill_(k)  # evict the logits and tables from L2 between steps
+        if not warm:
+            flush.fill_(k)  # evict the logits and tables from L2 between steps
         e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
         e0.record()
         if restart_t[k] is not None:
@@ -322,6 +326,8 @@ def engine_arm(args) -> None:
         if timed:
             step_ms.append((e0, e2))
             apply_ms.append((e1, e2))
+        elif warm:
+            warm_ms.append((e0, e2))
     torch.cuda.synchronize()
     if clocks is not None:
         torch.cuda.nvtx.range_pop()
@@ -329,6 +335,7 @@ def engine_arm(args) -> None:
     errors = engine.errors()
     steps_ms = [a.elapsed_time(b) for a, b in step_ms]
     applies = [a.elapsed_time(b) for a, b in apply_ms]
+    warms = [a.elapsed_time(b) for a, b in warm_ms]
     my_time = sum(steps_ms)
     time_t = torch.tensor([my_time], dtype=torch.float64, device=device)
     if world > 1:
@@ -360,6 +367,10 @@ def engine_arm(args) -> None:
         },
         "step_ms": {"median": statistics.median(steps_ms), "p90": sorted(steps_ms)[int(0.9 * len(steps_ms))],
                     "min": min(steps_ms)},
+        "warm": ({"ms_per_step": statistics.median(warms), "value": rows * 1e3 / statistics.median(warms),
+                  "unit": UNIT, "steps": len(warms),
+                  "note": "the same replay continued without the L2 flush (median step, this rank)"}
+                 if warms else None),
         "kernel_ms": {"median": statistics.median(applies), "mean": statistics.mean(applies),
                       "note": "sync_apply kernel alone (events around it), over the K timed steps"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
