@@ -199,10 +199,11 @@ XG_API int xg_apply_mask(XgEngine* engine, void* logits, int32_t dtype, int32_t 
  * required) that allocates nothing, for callers that may not allocate device memory while
  * they decode (a serving loop whose framework has already claimed the free memory for its
  * own pools, or code that must not take the synchronizing growth path of xg_apply_mask).
- * Its scratch is one static 8 MiB device array in this library, shared by every call on
- * the device: a call with more rows than fit (4 * (words + 600) bytes per row) fails with
- * XG_EINVAL and launches nothing.  No part of the array needs to start at zero (each row's
- * memory copy and mask row is written before it is read).  Calls whose kernels overlap on
+ * Its scratch is one static 8 MiB device array in this library, which every GPU that loads
+ * the library holds until the process exits, shared by every call on the device: a call
+ * with more rows than fit (4 * (words + 600) bytes per row) fails with XG_EINVAL and
+ * launches nothing.  The array keeps the last call's contents; no part of it needs to
+ * start at zero (each row's memory copy and mask row is written before it is read).  Calls whose kernels overlap on
  * the GPU (other streams, other engines, other threads) race on the array: order them.
  * The first call on a device looks the array's address up (cudaGetSymbolAddress, with the
  * engine's device current), which may also load the library's device code; make that first
