@@ -217,6 +217,9 @@ def test_sync_apply_equals_sync_then_apply_mask(dtype):
         sa, sb = fused.states_host(), plain.states_host()
         for field in sa:
             np.testing.assert_array_equal(sa[field], sb[field], field)
+        fused.fill_mask()
+        plain.fill_mask()
+        np.testing.assert_array_equal(fused.mask_host(), plain.mask_host())  # the recorded masks too
 
 
 @pytest.mark.parametrize("name", ["bpe_norepeat", "bpe_committed", "crowd_committed", "toy_derivation"])

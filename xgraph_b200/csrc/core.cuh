@@ -641,6 +641,9 @@ struct Ctx {
   int32_t* mem;     // slot memory
   Key* top;         // per-warp buffer of kTopCap keys
   int32_t* scratch; // per-warp: kScratchInts ints (slice starts, slice pointers, entity rows)
+  // optional copy of the tokens that start the closer, separator and escape (their lists at
+  // byte position 0, in that order), e.g. in shared memory; null: read the tables
+  const int32_t* delim0 = nullptr;
 };
 
 XG_HD int32_t version_of(const Ctx& c) { return c.mem[kMemVersion]; }
@@ -1440,11 +1443,14 @@ XG_SHARED void add_delimiters(const Ctx& c, int32_t close, int32_t sep, int32_t 
   const int32_t n1 = sep >= 0 ? delim_end(t.separator, sep) - a1 : 0;
   const int32_t a2 = esc >= 0 ? delim_begin(t.escape, esc) : 0;
   const int32_t n2 = esc >= 0 ? delim_end(t.escape, esc) - a2 : 0;
+  // a branch at its start reads the copied start lists when there is a copy
+  const int32_t c0 = t.closer.at[1] - t.closer.at[0], c1 = t.separator.at[1] - t.separator.at[0];
+  const int32_t* p0 = c.delim0 && close == 0 ? c.delim0 : t.closer.tok + a0;
+  const int32_t* p1 = c.delim0 && sep == 0 ? c.delim0 + c0 : t.separator.tok + a1;
+  const int32_t* p2 = c.delim0 && esc == 0 ? c.delim0 + c0 + c1 : t.escape.tok + a2;
   warp_for_loaded(
       c.w, 0, n0 + n1 + n2,
-      [&](int32_t i) {
-        return i < n0 ? t.closer.tok[a0 + i] : i < n0 + n1 ? t.separator.tok[a1 + i - n0] : t.escape.tok[a2 + i - n0 - n1];
-      },
+      [&](int32_t i) { return i < n0 ? p0[i] : i < n0 + n1 ? p1[i - n0] : p2[i - n0 - n1]; },
       [&](int32_t, int32_t token) { set_bit(out, token); });
 }
 
@@ -1462,13 +1468,15 @@ XG_COLD void add_label_tokens(const Ctx& c, const XgState& s, uint32_t* out) {
           });
     } else {
       const int32_t* reached = c.mem + kMemReachedRows;
-      warp_for(c.w, 0, reached_count(c), [&](int32_t i) {
-        const int32_t row = reached[i];
-        if (row >= lo && row < hi) {
-          const int32_t tok = column(t.ent, row, d);
-          if (tok >= 0) set_bit(out, tok);
-        }
-      });
+      warp_for_loaded(
+          c.w, 0, reached_count(c),
+          [&](int32_t i) {
+            const int32_t row = reached[i];
+            return row >= lo && row < hi ? column(t.ent, row, d) : -1;
+          },
+          [&](int32_t, int32_t tok) {
+            if (tok >= 0) set_bit(out, tok);
+          });
     }
   } else if (s.segment == kRelation) {
     struct TokenOwner {
@@ -1507,8 +1515,9 @@ struct MaskRef {
 
 // The mask of a state: outside a span a precomputed table row (base only); inside one the
 // root or wide mask of an unbound label range as base (no copy), and the buffer `own`
-// (zeroed, then the label and delimiter tokens) as delta; in the error phase neither.
-XG_HD MaskRef compose_mask(const Ctx& c, const XgState& s, uint32_t* own) {
+// (zeroed unless `zeroed`, then the label and delimiter tokens) as delta; in the error
+// phase neither.
+XG_HD MaskRef compose_mask(const Ctx& c, const XgState& s, uint32_t* own, bool zeroed = false) {
   const Tables& t = c.t;
   const int64_t stride = t.words_padded;
   const uint32_t* base = nullptr;
@@ -1528,16 +1537,18 @@ XG_HD MaskRef compose_mask(const Ctx& c, const XgState& s, uint32_t* own) {
         scan = false;
       }
     }
+    if (!zeroed) {  // (a caller may hand over a buffer it has cleared already)
 #if XG_GPU
-    uint4* to = reinterpret_cast<uint4*>(delta);
-    const int32_t quads = t.words_padded >> 2;
-    #pragma unroll 1
-    for (int32_t i = c.w.lane; i < quads; i += 32) to[i] = make_uint4(0u, 0u, 0u, 0u);
-    __syncwarp();
+      uint4* to = reinterpret_cast<uint4*>(delta);
+      const int32_t quads = t.words_padded >> 2;
+#pragma unroll 1
+      for (int32_t i = c.w.lane; i < quads; i += 32) to[i] = make_uint4(0u, 0u, 0u, 0u);
+      __syncwarp();
 #else
-    #pragma unroll 1
-    for (int32_t i = 0; i < t.words_padded; ++i) delta[i] = 0u;
+#pragma unroll 1
+      for (int32_t i = 0; i < t.words_padded; ++i) delta[i] = 0u;
 #endif
+    }
     if (scan) add_label_tokens(c, s, delta);
     // each delimiter branch: its next tokens from where it stands, or from its start when
     // the flags let it begin here

@@ -26,6 +26,7 @@ constexpr int32_t kApplyThreads = 256;
 constexpr int32_t kApplyBatch = 4;        // 1024-column segments whose loads a warp issues together
 constexpr int32_t kApplyCtasPerSm = 4;    // apply grid: CTAs per SM the row split aims at
 constexpr int32_t kFusedThreads = 256;    // sync_apply: warp 0 advances, all 8 warps write
+constexpr int32_t kDelimCopy = 1024;      // sync_apply: delimiter start tokens copied to shared memory
 
 struct __align__(16) WarpShared {
   Key top[kTopCap];
@@ -37,8 +38,15 @@ __device__ __forceinline__ Ctx make_ctx(const Tables& t, int32_t slot, WarpShare
              t.memory + static_cast<int64_t>(slot) * t.memory_ints, sh.top, sh.scratch};
 }
 
+// Every lane holds the same state: lane k stores words k and k + 32 (two coalesced stores
+// instead of one lane storing all 64 words).
 __device__ __forceinline__ void store_state(const Tables& t, int32_t slot, const XgState& s) {
-  if ((threadIdx.x & 31) == 0) t.states[slot] = s;
+  static_assert(sizeof(XgState) == 64 * sizeof(int32_t), "XgState is 64 words");
+  const int32_t lane = threadIdx.x & 31;
+  const int32_t* from = reinterpret_cast<const int32_t*>(&s);
+  int32_t* to = reinterpret_cast<int32_t*>(t.states + slot);
+  to[lane] = from[lane];
+  to[lane + 32] = from[lane + 32];
   __syncwarp();
 }
 
@@ -289,6 +297,9 @@ __global__ void __launch_bounds__(kFusedThreads)
     sync_apply_kernel(const __grid_constant__ Tables t, const StepArgs a, char* logits, int32_t cols,
                       int64_t stride, uint32_t neg) {
   __shared__ WarpShared shared;
+  __shared__ MaskRef use;                               // the mask this CTA applies
+  __shared__ int32_t delim0[kDelimCopy];                // tokens that start each delimiter
+  extern __shared__ __align__(16) uint32_t composed[];  // [words_padded]: a delta built this step
   const int32_t i = blockIdx.x;
   const int32_t slot = a.slots[i];
   // Issue warp 0's loads of the slot's cursor, lengths and state together with the active
@@ -304,8 +315,27 @@ __global__ void __launch_bounds__(kFusedThreads)
     cursor = stored < 0 ? prompt : stored;
   }
   if (!on) return;  // block-uniform: inactive rows are neither advanced nor masked
+  uint32_t* const own = t.masks + static_cast<int64_t>(slot) * t.words_padded;  // the slot's delta row
+  // Warps 1..7, idle while warp 0 runs the state machine, clear the shared delta row and
+  // copy the delimiters' start tokens, then arrive at barrier 1, which warp 0 waits at
+  // before it composes the mask.
+  const int32_t c0 = t.closer.at[1] - t.closer.at[0], c1 = t.separator.at[1] - t.separator.at[0];
+  const int32_t c2 = t.escape.at[1] - t.escape.at[0];
+  const bool copied = c0 + c1 + c2 <= kDelimCopy;
+  if (threadIdx.x >= 32) {
+    uint4* to = reinterpret_cast<uint4*>(composed);
+    for (int32_t k = threadIdx.x - 32; k < (t.words_padded >> 2); k += blockDim.x - 32) to[k] = make_uint4(0u, 0u, 0u, 0u);
+    if (copied) {
+      for (int32_t k = threadIdx.x - 32; k < c0 + c1 + c2; k += blockDim.x - 32)
+        delim0[k] = k < c0 ? t.closer.tok[t.closer.at[0] + k]
+                           : k < c0 + c1 ? t.separator.tok[t.separator.at[0] + k - c0]
+                                         : t.escape.tok[t.escape.at[0] + k - c0 - c1];
+    }
+    asm volatile("bar.arrive 1, %0;" ::"r"(blockDim.x) : "memory");
+  }
   if (threadIdx.x < 32) {
     Ctx c = make_ctx(t, slot, shared);
+    if (copied) c.delim0 = delim0;
     if (cursor < end) {
       const int32_t* tokens = a.history + a.stride * slot;
       for (; cursor < end; ++cursor) {
@@ -314,13 +344,29 @@ __global__ void __launch_bounds__(kFusedThreads)
         advance_state(c, s, token);
       }
       store_state(t, slot, s);
-      build_mask(c, s);
+      asm volatile("bar.sync 1, %0;" ::"r"(blockDim.x) : "memory");
+      // the delta is composed in shared memory (setting bits there is much cheaper than in
+      // global memory); the CTA copies it to the slot's row below
+      const MaskRef m = compose_mask(c, s, composed, true);
+      if (threadIdx.x == 0) {
+        t.base[slot] = m.base;
+        t.delta[slot] = m.delta ? own : nullptr;
+        use = m;
+      }
+    } else {  // no new token: the slot's recorded mask
+      asm volatile("bar.sync 1, %0;" ::"r"(blockDim.x) : "memory");
+      if (threadIdx.x == 0) use = MaskRef{t.base[slot], t.delta[slot]};
     }
     if (threadIdx.x == 0) t.cursors[slot] = cursor;
   }
   __syncthreads();
-  const uint32_t* base = t.base[slot];
-  const uint32_t* delta = t.delta[slot];
+  const uint32_t* base = use.base;
+  const uint32_t* delta = use.delta;
+  if (delta == composed) {  // keep the slot's delta row current for later readers
+    const uint4* from = reinterpret_cast<const uint4*>(composed);
+    uint4* to = reinterpret_cast<uint4*>(own);
+    for (int32_t k = threadIdx.x; k < (t.words_padded >> 2); k += blockDim.x) to[k] = from[k];
+  }
   if (base == nullptr && delta == nullptr) return;  // error phase: untouched
   char* out = logits + static_cast<int64_t>(i) * stride * ELT;
   if ((reinterpret_cast<uintptr_t>(out) & 15u) != 0) {
@@ -420,6 +466,7 @@ struct XgEngine {
   int32_t* active = nullptr;
   int32_t* tokens = nullptr;
   char* draft_scratch = nullptr;  // apply_mask's draft rows: [rows] memory rows, then [rows] mask rows
+  size_t composed_bytes = 0;      // sync_apply's dynamic shared memory: one mask row
   int32_t draft_capacity = 0;     // rows it holds
   Tables t{};
 };
@@ -616,6 +663,15 @@ int create(const void* blob, bool on_device, const XgLayout* layout, const XgOpt
     return cuda_fail(err, "engine upload");
   }
   bind_tables(e);
+  e->composed_bytes = static_cast<size_t>(layout->words_padded) * sizeof(uint32_t);
+  for (const void* kernel : {reinterpret_cast<const void*>(sync_apply_kernel<4>),
+                             reinterpret_cast<const void*>(sync_apply_kernel<2>)}) {
+    err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(e->composed_bytes));
+    if (err != cudaSuccess) {
+      release(e);
+      return cuda_fail(err, "sync_apply shared memory (vocabulary too large for one mask row on chip)");
+    }
+  }
   {
     const void* host = on_device ? nullptr : blob;
     int rc = fill_delimiter_offsets(e->t.closer, e->blob, layout->closer_off, host);
@@ -905,10 +961,10 @@ int xg_sync_apply(XgEngine* e, const int32_t* slots, int32_t count, const int32_
   cudaStream_t s = as_stream(stream);
   char* data = static_cast<char*>(logits);
   if (dtype == XG_F32)
-    sync_apply_kernel<4><<<count, kFusedThreads, 0, s>>>(e->t, a, data, cols, row_stride, 0xff800000u);
+    sync_apply_kernel<4><<<count, kFusedThreads, e->composed_bytes, s>>>(e->t, a, data, cols, row_stride, 0xff800000u);
   else
-    sync_apply_kernel<2><<<count, kFusedThreads, 0, s>>>(e->t, a, data, cols, row_stride,
-                                                         dtype == XG_BF16 ? 0xff80u : 0xfc00u);
+    sync_apply_kernel<2><<<count, kFusedThreads, e->composed_bytes, s>>>(e->t, a, data, cols, row_stride,
+                                                                         dtype == XG_BF16 ? 0xff80u : 0xfc00u);
   XG_CUDA(cudaGetLastError(), "sync_apply kernel");
   return XG_OK;
 }
