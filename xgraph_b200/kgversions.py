@@ -13,8 +13,10 @@ version k (1-based; 0 is the base) owns ``subjects[offsets[k-1]:offsets[k]]``
 
 from __future__ import annotations
 
+import json
 from collections.abc import Iterable, Mapping
 from dataclasses import dataclass
+from pathlib import Path
 
 import numpy as np
 
@@ -173,3 +175,43 @@ def build_kg_versions(index: KGIndex, versions: Mapping[str, Iterable[Edit]]) ->
         edge_objects=join(obj_parts),
         base_fingerprint=index.base_fingerprint,
     )
+
+
+VERSIONS_FILE = "kg-versions.json"
+VERSIONS_FORMAT = "xgraph-b200-versions-1"
+
+
+def write_kg_versions(directory, versions: Mapping[str, Iterable[Edit]], index: KGIndex) -> None:
+    """Write named edit sets as a version file of this library's format: kg-versions.json in
+    `directory`, each version's (subject, relation, object-or-None) id triples in order,
+    bound to the index's base fingerprint (the reference's files are out of its scope)."""
+    directory = Path(directory)
+    directory.mkdir(parents=True, exist_ok=True)
+    listed = [{"name": name, "edits": [[s, r, o] for s, r, o in edits]} for name, edits in versions.items()]
+    header = {"format": VERSIONS_FORMAT, "base_fingerprint": index.base_fingerprint, "versions": listed}
+    (directory / VERSIONS_FILE).write_text(json.dumps(header) + "\n", encoding="utf-8")
+
+
+def _version_header(directory) -> dict:
+    path = Path(directory) / VERSIONS_FILE
+    if not path.is_file():
+        raise ValueError(f"{directory} holds no {VERSIONS_FILE}")
+    header = json.loads(path.read_text(encoding="utf-8"))
+    if header.get("format") != VERSIONS_FORMAT:
+        raise ValueError(f"{path} is of format {header.get('format')!r}; this library reads {VERSIONS_FORMAT!r}")
+    return header
+
+
+def version_names(directory) -> list[str]:
+    """The names a version file registers, in order (its header alone is read)."""
+    return [entry["name"] for entry in _version_header(directory)["versions"]]
+
+
+def load_kg_versions(directory, index: KGIndex) -> KGVersions:
+    """Read a version file written by write_kg_versions and build its versions for `index`
+    (which must be the index the file was written for)."""
+    header = _version_header(directory)
+    if header.get("base_fingerprint") != index.base_fingerprint:
+        raise IndexMismatch(f"the KG versions in {directory} were written for another KG index")
+    edits = {entry["name"]: [tuple(e) for e in entry["edits"]] for entry in header["versions"]}
+    return build_kg_versions(index, edits)
