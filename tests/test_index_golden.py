@@ -50,3 +50,30 @@ def test_prefix_range_matches_linear_scan():
     for prefix in prefixes:
         hits = [r for r, row in enumerate(rows) if row[: len(prefix)] == prefix]
         assert labels.prefix_range(prefix) == (hits[0], hits[-1] + 1)
+
+
+def test_reads_the_reference_on_disk_index():
+    """An index saved by the reference's own save_kg_index (tests/golden/reference_index_toy,
+    made by tests/golden/make_reference_index.py) loads with the arrays this library builds
+    for the same world, and packs into the same device tables."""
+    from pathlib import Path
+
+    from tests.conftest import world, world_index
+    from xgraph_b200.index import load_kg_index
+    from xgraph_b200.syntax import SpanSyntax
+    from xgraph_b200.tables import pack_tables
+
+    loaded = load_kg_index(Path(__file__).parent / "golden" / "reference_index_toy")
+    built = world_index("toy", True)
+    for part in ("labels", "relations"):
+        a, b = getattr(loaded, part), getattr(built, part)
+        assert a.owner_ids == b.owner_ids
+        for name in ("tokens", "offsets", "owners"):
+            np.testing.assert_array_equal(getattr(a, name), getattr(b, name))
+    for name in ("adjacency_offsets", "edge_relations", "edge_objects", "sitelinks"):
+        np.testing.assert_array_equal(getattr(loaded, name), getattr(built, name))
+    assert loaded.span_syntax == SpanSyntax() and loaded.unwritable_triples == built.unwritable_triples
+    _, served, _ = world("toy")
+    a = pack_tables(loaded, served, loaded.span_syntax, escapes=True)
+    b = pack_tables(built, served, built.span_syntax, escapes=True)
+    np.testing.assert_array_equal(a.blob, b.blob)

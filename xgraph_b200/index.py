@@ -422,11 +422,21 @@ def save_kg_index(index: KGIndex, directory: str | Path) -> None:
     (directory / "kg-index.json").write_text(json.dumps(header) + "\n", encoding="utf-8")
 
 
+REFERENCE_INDEX_FORMAT = 1
+"""The reference's saved-index layout (src/xgraph/index.py:711), which load_kg_index reads."""
+
+
 def load_kg_index(directory: str | Path) -> KGIndex:
+    """Read a KG index saved by save_kg_index, or by the reference's save_kg_index (one .npy
+    file per array and kg-index.json, src/xgraph/index.py:731-903).  A reference index that
+    carries a date table, verdicts or initial-case aliases (policies this engine does not
+    serve) is refused."""
     directory = Path(directory)
     header = json.loads((directory / "kg-index.json").read_text(encoding="utf-8"))
+    if header.get("format") == REFERENCE_INDEX_FORMAT:
+        return _load_reference_index(directory, header)
     if header.get("format") != "xgraph-b200-index-1":
-        raise ValueError(f"{directory} holds no index of this library's format")
+        raise ValueError(f"{directory} holds no index of this library's or the reference's format")
     data = np.load(directory / "kg-index.npz")
     syntax = SpanSyntax(**header["span_syntax"])
 
@@ -445,3 +455,44 @@ def load_kg_index(directory: str | Path) -> KGIndex:
         span_syntax=syntax, sitelinks=data["sitelinks"] if "sitelinks" in data else None,
         base_fingerprint=header["base_fingerprint"],
     )
+
+
+def _load_reference_index(directory: Path, header: dict) -> KGIndex:
+    """The reference's saved index (format 1) as this library's KGIndex; its recorded base
+    fingerprint is kept when it has one, else this library's is computed."""
+    for key in ("dates", "verdicts", "initial_case_aliases"):
+        if header.get(key):
+            raise ValueError(f"{directory}: the index carries {key}, which this engine does not serve")
+
+    def array(name: str) -> np.ndarray:
+        file = directory / f"{name}.npy"
+        if not file.is_file():
+            raise ValueError(f"{directory} misses {file.name}")
+        return np.load(file)
+
+    known = SpanSyntax.__dataclass_fields__
+    syntax_fields = {k: tuple(v) if isinstance(v, list) else v for k, v in header.get("span_syntax", {}).items()
+                     if k in known}
+    syntax = SpanSyntax(**syntax_fields)
+
+    def part(name: str) -> LabelIndex:
+        return LabelIndex(
+            tokens=array(f"{name}.tokens"), offsets=array(f"{name}.offsets"), owners=array(f"{name}.owners"),
+            owner_ids=tuple(header[name]["owner_ids"]), tokenizer_fingerprint=header["tokenizer_fingerprint"],
+            excluded=tuple(ExcludedLabel(*e) for e in header[name]["excluded"]),
+        )
+
+    labels, relations = part("labels"), part("relations")
+    offsets, edge_rel, edge_obj = array("adjacency_offsets"), array("edge_relations"), array("edge_objects")
+    sitelinks = array("sitelinks") if header.get("sitelinks") else None
+    fingerprint = header.get("base_fingerprint") or _fingerprint({
+        "labels.tokens": labels.tokens, "labels.offsets": labels.offsets, "labels.owners": labels.owners,
+        "labels.ids": list(labels.owner_ids), "relations.tokens": relations.tokens,
+        "relations.offsets": relations.offsets, "relations.owners": relations.owners,
+        "relations.ids": list(relations.owner_ids), "adjacency_offsets": offsets, "edge_relations": edge_rel,
+        "edge_objects": edge_obj, "tokenizer": header["tokenizer_fingerprint"], "syntax": repr(syntax),
+        "sitelinks": sitelinks if sitelinks is not None else "none",
+    })
+    return KGIndex(labels=labels, relations=relations, adjacency_offsets=offsets, edge_relations=edge_rel,
+                   edge_objects=edge_obj, unwritable_triples=header["unwritable_triples"], span_syntax=syntax,
+                   sitelinks=sitelinks, base_fingerprint=fingerprint)
