@@ -26,6 +26,7 @@ constexpr int32_t kApplyThreads = 256;
 constexpr int32_t kApplyBatch = 4;        // 1024-column segments whose loads a warp issues together
 constexpr int32_t kApplyCtasPerSm = 4;    // apply grid: CTAs per SM the row split aims at
 constexpr int32_t kFusedThreads = 256;    // sync_apply: warp 0 advances, all 8 warps write
+constexpr int32_t kFusedRegisters = 128;  // sync_apply: room for a whole state in registers (2 CTAs/SM)
 constexpr int32_t kDelimCopy = 1024;      // sync_apply: delimiter start tokens copied to shared memory
 
 struct __align__(16) WarpShared {
@@ -36,6 +37,26 @@ struct __align__(16) WarpShared {
 __device__ __forceinline__ Ctx make_ctx(const Tables& t, int32_t slot, WarpShared& sh) {
   return Ctx{t, Warp{static_cast<int32_t>(threadIdx.x & 31)}, slot,
              t.memory + static_cast<int64_t>(slot) * t.memory_ints, sh.top, sh.scratch};
+}
+
+// A slot's state into every lane of the warp: lane k loads words k and k + 32 (two
+// coalesced loads), then each word is broadcast by a shuffle (every lane holds the whole
+// state, in registers).
+__device__ __forceinline__ XgState load_state(const Tables& t, int32_t slot) {
+  static_assert(sizeof(XgState) == 64 * sizeof(int32_t), "XgState is 64 words");
+  const int32_t lane = threadIdx.x & 31;
+  const int32_t* from = reinterpret_cast<const int32_t*>(t.states + slot);
+  const int32_t lo = from[lane], hi = from[lane + 32];
+  union {
+    XgState s;
+    int32_t w[64];
+  } u;
+#pragma unroll
+  for (int32_t k = 0; k < 32; ++k) {
+    u.w[k] = __shfl_sync(0xffffffffu, lo, k);
+    u.w[k + 32] = __shfl_sync(0xffffffffu, hi, k);
+  }
+  return u.s;
 }
 
 // Every lane holds the same state: lane k stores words k and k + 32 (two coalesced stores
@@ -293,7 +314,7 @@ __global__ void __launch_bounds__(kApplyThreads, 4)
 // all warps of the CTA write the row's -inf.  One launch per decoding step; a row's stores
 // overlap other rows' state-machine latency.
 template <int ELT>
-__global__ void __launch_bounds__(kFusedThreads)
+__global__ void __maxnreg__(kFusedRegisters)
     sync_apply_kernel(const __grid_constant__ Tables t, const StepArgs a, char* logits, int32_t cols,
                       int64_t stride, uint32_t neg) {
   __shared__ WarpShared shared;
@@ -311,7 +332,7 @@ __global__ void __launch_bounds__(kFusedThreads)
     const int32_t stored = t.cursors[slot];
     const int32_t prompt = a.prompt_len[slot];
     end = a.total_len[slot];
-    s = t.states[slot];
+    s = load_state(t, slot);
     cursor = stored < 0 ? prompt : stored;
   }
   if (!on) return;  // block-uniform: inactive rows are neither advanced nor masked
