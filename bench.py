@@ -13,7 +13,9 @@ bench replays outputs (src/xgraph/bench.py:82-139): per step `sync` over the tok
 history in place, then `apply_mask` on the logits.
 
 One timed step = begin(restarted slots) + sync + apply_mask, on one stream, bracketed by
-CUDA events; L2 is flushed (a 512 MiB write) between steps outside the events.  value =
+CUDA events; L2 is flushed (a 512 MiB write) between steps outside the events.  The
+stream is held by a bounded device spin before the timed steps while the host queues
+them, so host launch latency never lands between a step's events.  value =
 rows x steps / time (rows.steps/s), whole job over all ranks (max time over ranks).
 roofline: the apply kernel (its own events) against the measured HBM copy bandwidth,
 algorithmic bytes = sum over rows of 4*words (mask read) + 2*disallowed columns
@@ -45,6 +47,9 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "mask+advance rows.steps/s at B=256, V=128,256 (bf16 logits)"
 UNIT = "rows.steps/s"
+
+
+HOLD_CYCLES_PER_STEP = 1_000_000  # ~0.5 ms of device time per queued step: far above the host's launch time
 
 
 def parse_args():
@@ -312,6 +317,10 @@ def engine_arm(args) -> None:
             clocks = Clocks(local)
             time.sleep(0.3)
             torch.cuda.nvtx.range_push("timed")
+        if k == args.warmup or k == args.warmup + args.steps:
+            # hold the stream (a bounded spin, outside every event pair) while the host
+            # queues the leg's steps, so host launch latency never falls inside a step
+            torch.cuda._sleep(HOLD_CYCLES_PER_STEP * (args.steps if timed else warm_steps))
         if not warm:
             flush.fill_(k)  # evict the logits and tables from L2 between steps
         e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
