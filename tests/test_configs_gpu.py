@@ -1,0 +1,118 @@
+"""The serving step (sync_apply) at the benchmark configurations, against the oracle.
+
+Streams are constrained decodes sampled on the GPU under the engine's own masks
+(xgraph_b200.synthetic.sample_streams, as bench.py makes them); a fresh engine then
+replays them the way the serving step runs, one sync_apply launch per step over the
+token history in place (the reference's serving loop: src/xgraph/vllm.py:607-631 over
+csrc/engine.cu:2057-2074, 2562-2587).  At full size, on every row at every step:
+
+* the apply contract (csrc/engine.cu:2340-2346, 2562-2587): a column keeps its logit bit
+  for bit or becomes -inf, nothing else;
+* the number of columns kept equals the allowed count the sampling engine's own mask had
+  at that step (its advance + fill_mask path): two device paths agree everywhere.
+
+Against the oracle (oracle/oracle.py, the restatement of src/xgraph/oracle.py), advanced
+over the same tokens: the device state's public projection at every step of the checked
+rows (tests/agreement.py, as the reference's agreement harness,
+tests/test_engine.py:1588-1730), and the kept columns as a set equal to Oracle.allowed —
+at every step of every row for config 1 (V = 256), at seeded sampled steps for configs 2
+(V = 32,000), 3 and 4 (V = 128,256; config 4 is 1 M entities with 10 M Zipf-distributed
+triples, 512 rows), where each allowed set is a V-wide scan on the host.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from tests.agreement import assert_agrees, engine_state, expected_state
+from tests.conftest import state_record
+
+pytestmark = pytest.mark.gpu
+
+# config, rows replayed, steps, rows checked against the oracle, masks sampled per checked row
+# (None: every step)
+CASES = [(1, 16, 64, 16, None), (2, 64, 160, 8, 3), (3, 256, 160, 6, 2), (4, 512, 128, 4, 2)]
+
+
+def projection(states: dict, row: int, view, need_sets: bool) -> dict:
+    """engine_state, without the subject/relation sets where the comparison does not read
+    them (enumerating a wide subject range over a 100 k-entity index is slow on the host)."""
+    if need_sets:
+        return engine_state(states, row, view)
+    from xgraph_b200.engine import closed_span
+
+    field = {name: int(values[row]) for name, values in states.items()}
+    closed = closed_span(view, states, row)
+    return {**field, "subjects": set(), "relations": set(),
+            "last": None if closed.kind == "none" else (closed.kind, closed.entity_ids, closed.triples),
+            "resolved": closed.resolved}
+
+
+@pytest.mark.parametrize("config, rows, steps, checked, per_row", CASES)
+def test_sync_apply_agrees_with_oracle_at_benchmark_config(config, rows, steps, checked, per_row):
+    import torch
+
+    from oracle.oracle import Oracle
+    from xgraph_b200.engine import Engine
+    from xgraph_b200.syntax import SpanSyntax
+    from xgraph_b200.synthetic import build_workload, sample_streams
+
+    w = build_workload(config)
+    syntax = SpanSyntax()
+    options = dict(w.config.options)
+    paths = options.get("paths", False)
+    vocab = w.served.vocab_size
+    sampler = Engine(w.index, w.served, syntax, rows, **options)
+    tokens, counts, _ = sample_streams(sampler, w.served, syntax, w.world, rows, steps, seed=100 + config)
+    del sampler
+
+    rng = np.random.default_rng(200 + config)
+    checked_rows = sorted(rng.choice(rows, size=checked, replace=False).tolist())
+    sampled = {r: set(range(steps + 1)) if per_row is None
+               else set(rng.choice(steps + 1, size=per_row, replace=False).tolist()) for r in checked_rows}
+
+    dtype = getattr(torch, w.config.dtype)
+    bits = torch.int16 if dtype.itemsize == 2 else torch.int32
+    gen = torch.Generator(device="cuda").manual_seed(300 + config)
+    source = (torch.randn((rows, vocab), generator=gen, device="cuda") * 2.0).to(dtype)
+    engine = Engine(w.index, w.served, syntax, rows, **options)
+    engine.reset()
+    slots = torch.arange(rows, dtype=torch.int32, device="cuda")
+    engine.begin(slots)
+    prompt = torch.zeros(rows, dtype=torch.int32, device="cuda")
+    states_at, kept_at = [], {}
+    spans = 0
+    for k in range(steps + 1):  # total length k: the state after k tokens, the mask for token k
+        total = torch.full((rows,), k, dtype=torch.int32, device="cuda")
+        logits = source.clone()
+        engine.sync_apply(slots, tokens, prompt, total, logits)
+        blocked = torch.isneginf(logits)
+        same = logits.view(bits) == source.view(bits)
+        assert bool((blocked | same).all()), ("a column is neither its logit nor -inf", k)
+        kept = (~blocked).sum(1, dtype=torch.int32)
+        assert torch.equal(kept, counts[:, k]), ("kept columns differ from the sampling engine's mask", k)
+        states = engine.states_host(rows)
+        states_at.append({name: values[checked_rows].copy() for name, values in states.items()})
+        spans += int((states["phase"] == 1).sum())
+        for r in checked_rows:
+            if k in sampled[r]:
+                kept_at[(r, k)] = np.flatnonzero((~blocked[r]).cpu().numpy())
+    assert engine.errors() == 0
+    assert spans > rows * steps // 10  # the replay spends real time inside spans
+
+    oracle = Oracle(w.index, w.served, syntax, **options)
+    host_tokens = tokens.cpu().numpy()
+    for j, r in enumerate(checked_rows):
+        state = oracle.initial_state()
+        for k in range(steps + 1):
+            where = (config, r, k)
+            expected = expected_state(state_record(state), w.index, syntax)
+            need_sets = expected["phase"] == 1 and expected.get("segment", 0) != 0 and not paths
+            got = projection({name: values[j: j + 1] for name, values in states_at[k].items()}, 0, w.index,
+                             need_sets)
+            assert_agrees(expected, got, paths, where)
+            if (r, k) in kept_at:
+                assert set(kept_at[(r, k)].tolist()) == set(oracle.allowed(state)), ("allowed set", where)
+            if k < steps:
+                state = oracle.advance(state, int(host_tokens[r, k]))
