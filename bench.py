@@ -375,7 +375,7 @@ def engine_arm(args) -> None:
             "parallelism": f"rows sharded, {world} replica(s), index broadcast once over NCCL",
         },
         "step_ms": {"median": statistics.median(steps_ms), "p90": sorted(steps_ms)[int(0.9 * len(steps_ms))],
-                    "min": min(steps_ms)},
+                    "min": min(steps_ms), "max": max(steps_ms)},
         "warm": ({"ms_per_step": statistics.median(warms), "value": rows * 1e3 / statistics.median(warms),
                   "unit": UNIT, "steps": len(warms),
                   "note": "the same replay continued without the L2 flush (median step, this rank)"}

@@ -383,6 +383,16 @@ __global__ void __maxnreg__(kFusedRegisters)
   __syncthreads();
   const uint32_t* base = use.base;
   const uint32_t* delta = use.delta;
+  {
+    // The mask rows the -inf writes read from global memory (a table row, or the slot's
+    // recorded delta row), prefetched into L1 line by line now: the row's later rounds of
+    // mask loads then hit L1 instead of each waiting on L2 or HBM.
+    const int32_t lines = (t.words + 31) >> 5;  // 128-byte lines of a mask row
+    for (int32_t k = threadIdx.x; k < lines; k += blockDim.x) {
+      if (base) asm volatile("prefetch.global.L1 [%0];" ::"l"(base + 32 * k));
+      if (delta && delta != composed) asm volatile("prefetch.global.L1 [%0];" ::"l"(delta + 32 * k));
+    }
+  }
   if (delta == composed) {  // keep the slot's delta row current for later readers
     const uint4* from = reinterpret_cast<const uint4*>(composed);
     uint4* to = reinterpret_cast<uint4*>(own);
