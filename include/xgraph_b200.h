@@ -212,6 +212,26 @@ XG_API int xg_apply_mask_noalloc(XgEngine* engine, void* logits, int32_t dtype, 
                                  int64_t row_stride, const int32_t* row_slots, const int32_t* local_pos,
                                  const int32_t* input_ids, void* stream);
 
+/* Device-side build of a KG index's adjacency; it replaces the host build of the same
+ * arrays (src/xgraph/index.py:403-516, whose edge step turns every position triple into
+ * one edge per label row of its object, deduplicated and sorted by (subject, relation,
+ * object row)).  All arrays are device memory: triples as three int32 position arrays of
+ * length `triples`; the entities' label rows as CSR (row_offsets int64 [entities + 1],
+ * row_list int32: each entity's label rows in row order); writable uint8 [relation_count]
+ * (1 where the relation has a relation label row).  A triple is writable when its subject
+ * and object have label rows and its relation is writable; *unwritable counts the others.
+ * Called with offsets == NULL it only sizes: *edges = the edge count before
+ * deduplication, the capacity the edge arrays need.  Called with offsets int64
+ * [entities + 1] and edge_relations / edge_objects int32 [capacity], it writes the CSR
+ * and *edges = the edge count.  A position out of range fails with XG_EINVAL.  Device
+ * scratch is allocated and freed on `stream` (stream-ordered); the call synchronizes the
+ * stream before it returns. */
+XG_API int xg_build_adjacency(const int32_t* subjects, const int32_t* relations, const int32_t* objects,
+                              int64_t triples, const int64_t* row_offsets, const int32_t* row_list, int32_t entities,
+                              int32_t label_rows, const uint8_t* writable, int32_t relation_count, int64_t capacity,
+                              int64_t* offsets, int32_t* edge_relations, int32_t* edge_objects, int64_t* edges,
+                              int64_t* unwritable, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

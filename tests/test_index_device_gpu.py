@@ -1,0 +1,92 @@
+"""The device-side adjacency build (xg_build_adjacency) against the host build.
+
+The reference builds a KG index's edges on the host (src/xgraph/index.py:403-516); the
+library's device build must give the same arrays: CSR offsets per subject entity, edge
+relations and object label rows sorted by (subject, relation, object row) without
+duplicates, and the same count of unwritable triples (subject or object without label
+rows, relation without a relation row).  Equal arrays give equal index fingerprints.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def both(entities, relations, triples, served, syntax, sitelinks=None):
+    from xgraph_b200.index import build_kg_index_arrays
+
+    host = build_kg_index_arrays(entities, relations, triples, served, syntax, sitelinks=sitelinks)
+    device = build_kg_index_arrays(entities, relations, triples, served, syntax, sitelinks=sitelinks, device="cuda")
+    return host, device
+
+
+def assert_same(host, device):
+    np.testing.assert_array_equal(host.adjacency_offsets, device.adjacency_offsets)
+    np.testing.assert_array_equal(host.edge_relations, device.edge_relations)
+    np.testing.assert_array_equal(host.edge_objects, device.edge_objects)
+    assert host.adjacency_offsets.dtype == device.adjacency_offsets.dtype == np.int64
+    assert host.edge_relations.dtype == device.edge_relations.dtype == np.int32
+    assert host.edge_objects.dtype == device.edge_objects.dtype == np.int32
+    assert host.unwritable_triples == device.unwritable_triples
+    assert host.base_fingerprint == device.base_fingerprint
+
+
+@pytest.mark.parametrize("zipf", [None, 1.3])
+def test_device_adjacency_equals_host_on_synthetic_worlds(zipf):
+    from xgraph_b200.syntax import SpanSyntax
+    from xgraph_b200.synthetic import synthetic_tokenizer, synthetic_world
+
+    syntax = SpanSyntax()
+    world = synthetic_world(11, 3000, 80, 60000, labels=(1, 3), zipf=zipf)
+    served = synthetic_tokenizer(world, 4000, syntax)
+    host, device = both(world.entities, world.relations, world.triples, served, syntax, world.sitelinks)
+    assert len(host.edge_objects) > len(world.triples) // 2
+    assert_same(host, device)
+
+
+def test_device_adjacency_equals_host_at_the_path_benchmark_size():
+    from xgraph_b200.synthetic import build_workload
+
+    host = build_workload(3)
+    device = build_workload(3, device="cuda")
+    assert_same(host.index, device.index)
+
+
+def test_unwritable_triples_duplicates_and_empty_kg():
+    from xgraph_b200.syntax import SpanSyntax
+    from xgraph_b200.synthetic import synthetic_tokenizer, synthetic_world
+
+    syntax = SpanSyntax()
+    served = synthetic_tokenizer(synthetic_world(5, 300, 10, 900), 2000, syntax)
+    entities = [("a", ["Alpha"]), ("b", ["Beta", "Bee"]), ("c", [f"bad {syntax.closer} label"]), ("d", [])]
+    relations = [("r", ["likes"]), ("q", [f"no {syntax.opener}"])]
+    triples = np.array([
+        (0, 0, 1), (0, 0, 1), (1, 0, 0),  # a duplicate collapses
+        (0, 0, 2), (2, 0, 0), (3, 0, 0),  # subject or object without label rows
+        (0, 1, 1),                        # relation without a relation row
+    ])
+    host, device = both(entities, relations, triples, served, syntax)
+    assert host.unwritable_triples == 4
+    assert list(host.edge_objects) == [1, 2, 0]
+    assert_same(host, device)
+    empty_host, empty_device = both(entities, relations, np.zeros((0, 3), dtype=np.int64), served, syntax)
+    assert len(empty_device.edge_objects) == 0 and not empty_device.adjacency_offsets.any()
+    assert_same(empty_host, empty_device)
+
+
+def test_out_of_range_position_is_a_value_error():
+    """The check kernel tests every position against its bound before it reads anything
+    indexed by it, and the call fails with XG_EINVAL (ValueError)."""
+    from xgraph_b200.index import _adjacency_device, label_rows
+    from xgraph_b200.syntax import SpanSyntax
+    from xgraph_b200.synthetic import synthetic_tokenizer, synthetic_world
+
+    syntax = SpanSyntax()
+    served = synthetic_tokenizer(synthetic_world(5, 300, 10, 900), 2000, syntax)
+    labels = label_rows([("a", ["Alpha"]), ("b", ["Beta"])], served, syntax)
+    writable = np.ones(1, dtype=bool)
+    with pytest.raises(ValueError, match="out of range"):
+        _adjacency_device(labels, writable, np.array([0]), np.array([0]), np.array([2]), 2, "cuda")

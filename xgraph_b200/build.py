@@ -17,7 +17,7 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parent
-SOURCES = [HERE / "csrc" / "engine.cu"]
+SOURCES = [HERE / "csrc" / "engine.cu", HERE / "csrc" / "build.cu"]
 DEPENDS = SOURCES + [HERE / "csrc" / "core.cuh", HERE / "csrc" / "layout.h", ROOT / "include" / "xgraph_b200.h"]
 OUTPUT = HERE / "libxgraph_b200.so"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -511,6 +511,14 @@ int fail(int code, const std::string& message) {
   return code;
 }
 
+}  // namespace
+
+// The adjacency builder (build.cu) reports its errors through the same last-error slot;
+// not exported from the library.
+extern "C" int xg_set_error(int code, const char* message) { return fail(code, message); }
+
+namespace {
+
 int cuda_fail(cudaError_t e, const char* what) {
   cudaGetLastError();  // clear a non-sticky error so the next call starts clean
   return fail(XG_ECUDA, std::string(what) + ": " + cudaGetErrorString(e));

@@ -100,6 +100,7 @@ def load_library(path: Path = LIBRARY):
         "xg_memory_host": ([p, i32, p], ctypes.c_int),
         "xg_apply_mask": ([p, p, i32, i32, i32, i64, p, p, p, p], ctypes.c_int),
         "xg_sync_apply": ([p, p, i32, p, i64, i64, p, p, i64, p, i32, i32, i64, p], ctypes.c_int),
+        "xg_build_adjacency": ([p, p, p, i64, p, p, i32, i32, p, i32, i64, p, p, p, p, p, p], ctypes.c_int),
     }
     for name, (args, res) in sigs.items():
         fn = getattr(lib, name)

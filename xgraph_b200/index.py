@@ -293,6 +293,50 @@ def _adjacency(
     return offsets, rel_out.astype(np.int32), rows_out.astype(np.int32), unwritable
 
 
+def _adjacency_device(
+    labels: LabelIndex, writable_relations: np.ndarray, subjects: np.ndarray,
+    relations: np.ndarray, objects: np.ndarray, entities: int, device,
+) -> tuple[np.ndarray, np.ndarray, np.ndarray, int]:
+    """_adjacency's arrays built on a GPU by the library's xg_build_adjacency (expand,
+    radix sort, unique and CSR scan on the device), copied back to the host."""
+    import ctypes
+
+    import torch
+
+    from .engine import _check, load_library
+
+    lib = load_library()
+    device = torch.device(device)
+    if device.type != "cuda":
+        raise ValueError(f"the device adjacency build needs a CUDA device, got {device}")
+    row_offsets, row_list = entity_row_lists(labels)
+    with torch.cuda.device(device):
+        def put(array, dtype):
+            return torch.from_numpy(np.ascontiguousarray(array)).to(device=device, dtype=dtype)
+
+        s, r, o = put(subjects, torch.int32), put(relations, torch.int32), put(objects, torch.int32)
+        offsets_in, rows_in = put(row_offsets, torch.int64), put(row_list, torch.int32)
+        writable = put(np.asarray(writable_relations, dtype=np.uint8), torch.uint8)
+        stream = ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+        edges, unwritable = ctypes.c_int64(), ctypes.c_int64()
+
+        def ptr(t):
+            return ctypes.c_void_p(t.data_ptr())
+
+        head = (ptr(s), ptr(r), ptr(o), len(subjects), ptr(offsets_in), ptr(rows_in), entities, labels.num_rows,
+                ptr(writable), len(writable_relations))
+        _check(lib.xg_build_adjacency(*head, 0, None, None, None, ctypes.byref(edges), ctypes.byref(unwritable), stream))
+        capacity = edges.value
+        offsets = torch.empty(entities + 1, dtype=torch.int64, device=device)
+        edge_rel = torch.empty(max(capacity, 1), dtype=torch.int32, device=device)
+        edge_obj = torch.empty(max(capacity, 1), dtype=torch.int32, device=device)
+        _check(lib.xg_build_adjacency(*head, capacity, ptr(offsets), ptr(edge_rel), ptr(edge_obj), ctypes.byref(edges),
+                                      ctypes.byref(unwritable), stream))
+        n = edges.value
+        return (offsets.cpu().numpy(), edge_rel[:n].cpu().numpy(), edge_obj[:n].cpu().numpy(),
+                int(unwritable.value))
+
+
 def build_kg_index_arrays(
     entities: Sequence[tuple[str, Sequence[str]]],
     relations: Sequence[tuple[str, Sequence[str]]],
@@ -300,9 +344,12 @@ def build_kg_index_arrays(
     tokenizer: ServedTokenizer,
     syntax: SpanSyntax,
     sitelinks: np.ndarray | Sequence[int] | None = None,
+    device=None,
 ) -> KGIndex:
     """The KG index of entities and relations given as (id, labels) and triples given as
-    an int (n, 3) array of (subject position, relation position, object position)."""
+    an int (n, 3) array of (subject position, relation position, object position).
+    `device` (a CUDA device): the edge arrays are built there by the library (the same
+    arrays as the host build's); None builds everything on the host."""
     triples = np.asarray(triples, dtype=np.int64).reshape(-1, 3)
     if len(triples) and (
         triples.min() < 0
@@ -315,9 +362,14 @@ def build_kg_index_arrays(
     relation_index = label_rows(relations, tokenizer, syntax)
     writable = np.zeros(len(relations), dtype=bool)
     writable[np.asarray(relation_index.owners, dtype=np.int64)] = True
-    offsets, edge_rel, edge_obj, unwritable = _adjacency(
-        labels, writable, triples[:, 0], triples[:, 1], triples[:, 2], len(entities)
-    )
+    if device is None:
+        offsets, edge_rel, edge_obj, unwritable = _adjacency(
+            labels, writable, triples[:, 0], triples[:, 1], triples[:, 2], len(entities)
+        )
+    else:
+        offsets, edge_rel, edge_obj, unwritable = _adjacency_device(
+            labels, writable, triples[:, 0], triples[:, 1], triples[:, 2], len(entities), device
+        )
     counts = None if sitelinks is None else sitelink_array(sitelinks, len(entities))
     parts = {
         "labels.tokens": labels.tokens, "labels.offsets": labels.offsets,

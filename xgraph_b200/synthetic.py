@@ -163,7 +163,9 @@ class Workload:
     index: object
 
 
-def build_workload(number: int, seed: int | None = None) -> Workload:
+def build_workload(number: int, seed: int | None = None, device=None) -> Workload:
+    """Config `number`'s world, served tokenizer and KG index (seeded by `seed`, default
+    the config number); `device` builds the index's edge arrays on that GPU."""
     from .index import build_kg_index_arrays
     from .syntax import SpanSyntax
 
@@ -173,7 +175,7 @@ def build_workload(number: int, seed: int | None = None) -> Workload:
                             labels=config.labels, zipf=config.zipf)
     served = synthetic_tokenizer(world, config.vocab, syntax)
     index = build_kg_index_arrays(world.entities, world.relations, world.triples, served, syntax,
-                                  sitelinks=world.sitelinks)
+                                  sitelinks=world.sitelinks, device=device)
     return Workload(config, world, served, syntax, index)
 
 
