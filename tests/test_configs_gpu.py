@@ -116,3 +116,118 @@ def test_sync_apply_agrees_with_oracle_at_benchmark_config(config, rows, steps, 
                 assert set(kept_at[(r, k)].tolist()) == set(oracle.allowed(state)), ("allowed set", where)
             if k < steps:
                 state = oracle.advance(state, int(host_tokens[r, k]))
+
+
+def test_sync_apply_with_per_request_kg_versions():
+    """Continuous batching with KG versions (the benchmark's versions configuration):
+    every request carries 0-256 seeded add/remove-triple edits as its own KG version
+    (registered when the engine is built), V = 151,936, path mode with committed paths.
+    Each slot serves one request, then is re-begun mid-replay for a second request with
+    another version (begin + set_version at admission, as the reference's serving loop
+    does).  The world is 2 k entities and 20 k triples rather than 1 M / 10 M: a request's
+    ~100-200 edited subjects are then a fair share of the subjects its spans name (on a
+    large world the walks almost never meet an edited subject, and the versions would go
+    unread), and the oracle builds each checked request's version graphs; the device path
+    reads versions the same way at any size.  Checked as above: the apply contract and agreement with the
+    sampling engine (each request sampled in its own row under its version) on every row
+    at every step; state projections and sampled allowed sets against the oracle holding
+    the checked requests' versions; and the same replay on the base KG masks some rows
+    differently (the versions are read)."""
+    import torch
+
+    from oracle.oracle import Oracle
+    from xgraph_b200.engine import Engine
+    from xgraph_b200.index import build_kg_index_arrays
+    from xgraph_b200.kgversions import build_kg_versions
+    from xgraph_b200.syntax import SpanSyntax
+    from xgraph_b200.synthetic import (object_sets, request_edits, sample_streams, synthetic_tokenizer,
+                                       synthetic_world)
+
+    syntax = SpanSyntax()
+    world = synthetic_world(505, 2_000, 40, 20_000, labels=(1, 3))
+    served = synthetic_tokenizer(world, 151_936, syntax)
+    assert served.vocab_size == 151_936
+    index = build_kg_index_arrays(world.entities, world.relations, world.triples, served, syntax,
+                                  sitelinks=world.sitelinks)
+    rng = np.random.default_rng(505)
+    slots, steps = 32, 160
+    pairs = object_sets(world)
+    edits = {f"request-{i}": request_edits(world, pairs, rng, int(rng.integers(0, 257))) for i in range(2 * slots)}
+    names = list(edits)
+    versions = build_kg_versions(index, edits)
+    options = {"paths": True, "committed_paths": True}
+    vocab = served.vocab_size
+
+    sampler = Engine(index, served, syntax, 2 * slots, versions=versions, **options)
+    tokens, counts, _ = sample_streams(sampler, served, syntax, world, 2 * slots, steps, seed=505, versions=names)
+    del sampler
+    # slot j serves request j for switch[j] tokens, then request slots + j
+    switch = np.clip(rng.geometric(1 / 60, size=slots), 8, steps - 8)
+    history = torch.zeros((slots, steps), dtype=torch.int32, device="cuda")
+    for j in range(slots):
+        history[j, : switch[j]] = tokens[j, : switch[j]]
+        history[j, switch[j]:] = tokens[slots + j, : steps - switch[j]]
+
+    gen = torch.Generator(device="cuda").manual_seed(606)
+    source = (torch.randn((slots, vocab), generator=gen, device="cuda") * 2.0).to(torch.bfloat16)
+    engine = Engine(index, served, syntax, slots, versions=versions, **options)
+    engine.reset()
+    rows = torch.arange(slots, dtype=torch.int32, device="cuda")
+    engine.begin(rows)
+    for j in range(slots):
+        engine.set_version(j, names[j])
+    checked = sorted(rng.choice(slots, size=4, replace=False).tolist())
+    sampled = {j: {int(rng.integers(0, switch[j])), int(rng.integers(switch[j], steps + 1))} for j in checked}
+    base = Engine(index, served, syntax, slots, **options)  # the same replay on the base KG
+    base.reset()
+    base.begin(rows)
+    states_at, kept_at = [], {}
+    differs = 0
+    switch_t = torch.from_numpy(switch).to("cuda")
+    request_of = torch.arange(slots, device="cuda")
+    for k in range(steps + 1):
+        restarted = [j for j in range(slots) if switch[j] == k]
+        if restarted:
+            engine.begin(torch.tensor(restarted, dtype=torch.int32, device="cuda"))
+            base.begin(torch.tensor(restarted, dtype=torch.int32, device="cuda"))
+            for j in restarted:
+                engine.set_version(j, names[slots + j])
+        prompt = torch.full((slots,), k, dtype=torch.int32, device="cuda")
+        total = torch.full((slots,), k, dtype=torch.int32, device="cuda")
+        logits = source.clone()
+        engine.sync_apply(rows, history, prompt, total, logits)
+        unversioned = source.clone()
+        base.sync_apply(rows, history, prompt, total, unversioned)
+        differs += int((torch.isneginf(unversioned) != torch.isneginf(logits)).any(1).sum())
+        blocked = torch.isneginf(logits)
+        same = logits.view(torch.int16) == source.view(torch.int16)
+        assert bool((blocked | same).all()), ("a column is neither its logit nor -inf", k)
+        second = k >= switch_t
+        expected = torch.where(second, counts[request_of + slots, (k - switch_t).clamp(min=0)],
+                               counts[request_of, min(k, steps)])
+        assert torch.equal((~blocked).sum(1, dtype=torch.int32), expected), ("kept columns", k)
+        states = engine.states_host(slots)
+        states_at.append({name: values[checked].copy() for name, values in states.items()})
+        for j in checked:
+            if k in sampled[j]:
+                kept_at[(j, k)] = np.flatnonzero((~blocked[j]).cpu().numpy())
+    assert engine.errors() == 0
+    assert differs > 0  # the versions changed some rows' masks in this replay
+
+    host_history = history.cpu().numpy()
+    for n, j in enumerate(checked):
+        first, later = names[j], names[slots + j]
+        oracle = Oracle(index, served, syntax, versions={first: edits[first], later: edits[later]}, **options)
+        state = oracle.initial_state(first)
+        for k in range(steps + 1):
+            if k == switch[j]:
+                state = oracle.initial_state(later)
+            where = ("versions", j, k)
+            view = versions.view(index, state.version)
+            expected_fields = expected_state(state_record(state), index, syntax)
+            got = projection({name: values[n: n + 1] for name, values in states_at[k].items()}, 0, view, False)
+            assert_agrees(expected_fields, got, True, where)
+            if (j, k) in kept_at:
+                assert set(kept_at[(j, k)].tolist()) == set(oracle.allowed(state)), ("allowed set", where)
+            if k < steps:
+                state = oracle.advance(state, int(host_history[j, k]))

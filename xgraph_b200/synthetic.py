@@ -93,6 +93,44 @@ def synthetic_world(seed: int, entities: int, relations: int, triples: int, *, l
     return World(ents, rels, trip.astype(np.int64), sitelinks, prose)
 
 
+def object_sets(world: World) -> dict[tuple[int, int], set[int]]:
+    """The world's (subject, relation) pairs with their object positions."""
+    pairs: dict[tuple[int, int], set[int]] = {}
+    for s, r, o in np.asarray(world.triples).tolist():
+        pairs.setdefault((s, r), set()).add(o)
+    return pairs
+
+
+def request_edits(world: World, pairs: dict[tuple[int, int], set[int]], rng: np.random.Generator,
+                  count: int) -> list[tuple[str, str, str | None]]:
+    """`count` seeded add/remove-triple edits of one request, written as the reference's
+    pair-replacement edits (src/xgraph/kgversions.py:203-216): adding o to the pair (s, r)
+    writes the pair's objects with o, removing o writes them without it (the pair deleted,
+    object None, when none remain); one request's edits to a pair accumulate.  Half the
+    edits touch pairs the world has (removing one of their objects, or adding one)."""
+    entities, relations = len(world.entities), len(world.relations)
+    known = list(pairs) if pairs else []
+    changed: dict[tuple[int, int], set[int]] = {}
+    for _ in range(count):
+        if known and rng.random() < 0.5:
+            pair = known[int(rng.integers(len(known)))]
+        else:
+            pair = (int(rng.integers(entities)), int(rng.integers(relations)))
+        objects = changed.setdefault(pair, set(pairs.get(pair, ())))
+        if objects and rng.random() < 0.5:
+            objects.discard(sorted(objects)[int(rng.integers(len(objects)))])
+        else:
+            objects.add(int(rng.integers(entities)))
+    edits: list[tuple[str, str, str | None]] = []
+    for (s, r), objects in changed.items():
+        sid, rid = world.entities[s][0], world.relations[r][0]
+        if objects:
+            edits.extend((sid, rid, world.entities[o][0]) for o in sorted(objects))
+        else:
+            edits.append((sid, rid, None))
+    return edits
+
+
 def synthetic_tokenizer(world: World, vocab_size: int, syntax, seed: int = 0):
     """A byte-level BPE with exactly vocab_size ids (special <|endoftext|> included):
     the 256 byte tokens alone when vocab_size <= 257, else trained on the labels, the
@@ -201,11 +239,12 @@ def _prose_tokens(served, world: World) -> np.ndarray:
 
 def sample_streams(engine, served, syntax, world: World, rows: int, steps: int, seed: int,
                    *, p_open=0.25, p_sep=0.5, p_close=0.8, p_escape=0.05, p_unescape=0.3, record=None,
-                   device: str = "cuda"):
+                   device: str = "cuda", versions=None):
     """Constrained random walks of `rows` slots for `steps` tokens, decoded on the GPU with
     the engine as the constraint.  Returns (tokens [rows, steps] int32 on the GPU, allowed
     counts [rows, steps + 1] int32: how many ids each step's mask allowed).  `record`
-    (optional set of (row, step)) collects those masks on the host for parity checks."""
+    (optional set of (row, step)) collects those masks on the host for parity checks;
+    `versions` (optional, one KG version name or None per row) pins each row's version."""
     import torch
 
     device = torch.device(device)
@@ -224,6 +263,8 @@ def sample_streams(engine, served, syntax, world: World, rows: int, steps: int, 
     engine.reset()
     slots = torch.arange(rows, dtype=torch.int32, device=device)
     engine.begin(slots)
+    for row, name in enumerate(versions or ()):
+        engine.set_version(row, name)
     kind = torch.full((rows,), -1, dtype=torch.long, device=device)
     pos = torch.zeros(rows, dtype=torch.long, device=device)
     tokens = torch.zeros((rows, steps), dtype=torch.int32, device=device)
