@@ -353,6 +353,23 @@ __global__ void __maxnreg__(kFusedRegisters)
                                          : t.escape.tok[t.escape.at[0] + k - c0 - c1];
     }
     asm volatile("bar.arrive 1, %0;" ::"r"(blockDim.x) : "memory");
+    // A relation label of a path (base KG): the next frontier reads each frontier entity's
+    // relation runs and its edges' folded first rows, two dependent round trips deep in
+    // warp 0's transition.  Start those lines into L1 now, one thread per entity (the
+    // slot's stored state and frontier are read here; the lines are only hints, and every
+    // address is checked to lie in its table).
+    const XgState* stored = t.states + slot;
+    const int32_t* mem = t.memory + static_cast<int64_t>(slot) * t.memory_ints;
+    if (t.paths && stored->phase == kSpan && stored->segment == kRelation && mem[kMemVersion] == 0) {
+      const int32_t count = mem[kMemFrontier] < kMaxSet ? mem[kMemFrontier] : kMaxSet;
+      for (int32_t k = threadIdx.x - 32; k < count; k += blockDim.x - 32) {
+        const int32_t e = mem[kMemFrontierEnt + k];
+        if (e < 0 || e >= t.entities) continue;
+        const int32_t r0 = t.run_off[e], r1 = t.run_off[e + 1], e0 = t.adj_off[e], e1 = t.adj_off[e + 1];
+        for (int32_t x = 2 * r0; x <= 2 * r1 + 1 && x < 2 * r0 + 4 * 32; x += 32) prefetch_l1(t.runs + x);
+        for (int32_t x = e0; x < e1 && x < e0 + 8 * 32; x += 32) prefetch_l1(t.edge_first + x);
+      }
+    }
   }
   if (threadIdx.x < 32) {
     Ctx c = make_ctx(t, slot, shared);
