@@ -106,6 +106,8 @@ struct Scratch {  // stream-ordered device allocations, released on every return
   explicit Scratch(cudaStream_t s) : stream(s) {}
   template <class T>
   cudaError_t get(T** p, size_t bytes) {
+    *p = nullptr;
+    if (n == static_cast<int>(sizeof(held) / sizeof(held[0]))) return cudaErrorMemoryAllocation;  // table full
     void* q = nullptr;
     const cudaError_t e = cudaMallocAsync(&q, bytes ? bytes : 1, stream);
     if (e == cudaSuccess) held[n++] = q;
