@@ -342,6 +342,7 @@ def engine_arm(args) -> None:
         torch.cuda.nvtx.range_pop()
     clock_info = clocks.stop() if clocks else None
     errors = engine.errors()
+    apply_alone = None if args.profile else apply_leg(engine, logits, slots, flush, stream, args.steps, elt)
     steps_ms = [a.elapsed_time(b) for a, b in step_ms]
     applies = [a.elapsed_time(b) for a, b in apply_ms]
     warms = [a.elapsed_time(b) for a, b in warm_ms]
@@ -386,6 +387,7 @@ def engine_arm(args) -> None:
                      "peak_kind": peak_kind, **recorded_traffic(args.config, cfg.dtype),
                      "kernel": f"sync_apply_kernel<{elt}> ({cfg.dtype}): sync + mask + apply fused",
                      "algorithmic_bytes_per_launch": statistics.mean(bytes_per_launch)},
+        "apply_mask_alone": apply_alone,
         "gpu_launches": launches,
         "clocks": clock_info,
         "errors": errors,
@@ -403,6 +405,39 @@ def engine_arm(args) -> None:
         streams = tokens.cpu().numpy().tolist()
         result["cpu_baseline"] = cpu_baseline(workload, streams, recorded, args.cpu_seconds)
     print(json.dumps(result), flush=True)
+
+
+def apply_leg(engine, logits, slots, flush, stream, steps, elt):
+    """The bandwidth kernel alone: apply_mask (apply_kernel) over the same rows with the
+    masks the replay left, `steps` launches with L2 flushed between them, CUDA events
+    around each launch.  Algorithmic bytes per launch: the mask words read once per row and
+    the -inf stores (counted from one launch on finite logits)."""
+    import torch
+
+    probe = torch.zeros_like(logits)
+    engine.apply_mask(probe, slots, stream=stream)
+    disallowed = int(torch.isneginf(probe).sum())
+    del probe
+    rows, words = logits.shape[0], engine.words
+    bytes_per_launch = rows * 4 * words + elt * disallowed
+    times = []
+    for k in range(max(3, steps // 4) + 3):
+        flush.fill_(k)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        engine.apply_mask(logits, slots, stream=stream)
+        e1.record()
+        if k >= 3:  # three warm-up launches
+            times.append((e0, e1))
+    torch.cuda.synchronize()
+    ms = [a.elapsed_time(b) for a, b in times]
+    mean_s = statistics.mean(ms) / 1e3
+    achieved = bytes_per_launch / mean_s / 1e9
+    peak, peak_kind = measured_peak()
+    return {"kernel": f"apply_kernel<{elt}>", "launches": len(ms), "ms_median": statistics.median(ms),
+            "ms_mean": statistics.mean(ms), "algorithmic_bytes_per_launch": bytes_per_launch,
+            "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_kind": peak_kind,
+            "note": "apply_mask alone on the replay's final masks, L2 flushed between launches"}
 
 
 def e2e_leg(engine, workload, history, restart_t, prompt, total, slots, rows, vocab, device, steps, dtype):
