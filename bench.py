@@ -20,7 +20,8 @@ rows x steps / time (rows.steps/s), whole job over all ranks (max time over rank
 roofline: the apply kernel (its own events) against the measured HBM copy bandwidth,
 algorithmic bytes = sum over rows of 4*words (mask read) + 2*disallowed columns
 (the -inf stores).  e2e: the same step through the public API with host buffers
-(tokens and logits copied in from pinned memory, masked logits copied back).
+(tokens and logits copied in from pinned memory, masked logits copied back, the uploads
+and downloads of neighbouring steps overlapped on two copy streams).
 cpu_baseline / --impl reference: the oracle (oracle/oracle.py, a restatement of the
 reference's CPU Oracle) on the host cores, per row-step allowed set + masked logits +
 advance, on a bounded sample of the same streams; its masks are also checked against
@@ -442,35 +443,58 @@ def apply_leg(engine, logits, slots, flush, stream, steps, elt):
 
 def e2e_leg(engine, workload, history, restart_t, prompt, total, slots, rows, vocab, device, steps, dtype):
     """The same steps through the public API with host buffers: each step copies its
-    tokens and logits in from pinned host memory and the masked logits back out."""
+    tokens and logits in from pinned host memory and the masked logits back out.  The
+    copies run the way a serving loop overlaps them: step k + 1's inputs go up on a copy
+    stream while step k's masked logits come down on another (PCIe is full duplex), with
+    two device buffers and events ordering each step's upload, step and download."""
     import torch
 
     host_tokens = history[:, :steps].t().contiguous().cpu().pin_memory()
     host_logits = (torch.randn((rows, vocab)) * 2.0).to(dtype).pin_memory()
     out_logits = torch.empty_like(host_logits).pin_memory()
     dev_hist = torch.zeros_like(history)
-    dev_logits = torch.empty((rows, vocab), dtype=dtype, device=device)
-    staging = torch.empty(rows, dtype=torch.int32, device=device)
-    stream = torch.cuda.current_stream(device).cuda_stream
+    dev_logits = [torch.empty((rows, vocab), dtype=dtype, device=device) for _ in range(2)]
+    staging = [torch.empty(rows, dtype=torch.int32, device=device) for _ in range(2)]
+    up, down = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    compute = torch.cuda.current_stream(device)
+    stream = compute.cuda_stream
     engine.reset()
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record()
+    start.record(compute)
+    up.wait_event(start)
+    down.wait_event(start)
+    uploaded = [torch.cuda.Event() for _ in range(steps)]
+    stepped = [torch.cuda.Event() for _ in range(steps)]
+    downloaded = [None, None]
     for k in range(steps):
-        staging.copy_(host_tokens[k], non_blocking=True)
-        dev_hist[:, k] = staging
-        dev_logits.copy_(host_logits, non_blocking=True)
+        b = k & 1
+        with torch.cuda.stream(up):
+            if downloaded[b] is not None:
+                up.wait_event(downloaded[b])  # buffer b's previous result is on the host
+            staging[b].copy_(host_tokens[k], non_blocking=True)
+            dev_logits[b].copy_(host_logits, non_blocking=True)
+            uploaded[k].record(up)
+        compute.wait_event(uploaded[k])
+        dev_hist[:, k] = staging[b]
         if restart_t[k] is not None:
             engine.begin(restart_t[k], stream=stream)
-        engine.sync_apply(slots, dev_hist, prompt[k], total[k], dev_logits, stream=stream)
-        out_logits.copy_(dev_logits, non_blocking=True)
-    end.record()
+        engine.sync_apply(slots, dev_hist, prompt[k], total[k], dev_logits[b], stream=stream)
+        stepped[k].record(compute)
+        with torch.cuda.stream(down):
+            down.wait_event(stepped[k])
+            out_logits.copy_(dev_logits[b], non_blocking=True)
+            downloaded[b] = torch.cuda.Event()
+            downloaded[b].record(down)
+    compute.wait_stream(down)
+    end.record(compute)
     torch.cuda.synchronize()
     ms = start.elapsed_time(end)
     return {"value": rows * steps / (ms / 1e3), "unit": UNIT,
             "h2d_bytes_per_step": rows * 4 + rows * vocab * host_logits.element_size(),
             "d2h_bytes_per_step": rows * vocab * host_logits.element_size(),
-            "steps": steps, "ms_per_step": ms / steps}
+            "steps": steps, "ms_per_step": ms / steps,
+            "copies": "inputs up and results down on two copy streams, overlapped across steps"}
 
 
 # ---------------------------------------------------------------------------------------
