@@ -90,3 +90,17 @@ def test_out_of_range_position_is_a_value_error():
     writable = np.ones(1, dtype=bool)
     with pytest.raises(ValueError, match="out of range"):
         _adjacency_device(labels, writable, np.array([0]), np.array([0]), np.array([2]), 2, "cuda")
+
+
+def test_kg_directory_builds_the_same_index_on_the_device():
+    from pathlib import Path
+
+    from tests.conftest import world
+    from xgraph_b200.index import build_kg_directory_index
+    from xgraph_b200.syntax import SpanSyntax
+
+    _, served, _ = world("rand_bpe")
+    kg = Path(__file__).parent / "golden" / "kg_directory_toy"
+    host = build_kg_directory_index(kg, served, SpanSyntax())
+    device = build_kg_directory_index(kg, served, SpanSyntax(), device="cuda")
+    assert_same(host, device)

@@ -77,3 +77,62 @@ def test_reads_the_reference_on_disk_index():
     a = pack_tables(loaded, served, loaded.span_syntax, escapes=True)
     b = pack_tables(built, served, built.span_syntax, escapes=True)
     np.testing.assert_array_equal(a.blob, b.blob)
+
+
+def _rand_bpe_served():
+    from tests.conftest import world
+
+    _, served, _ = world("rand_bpe")
+    return served
+
+
+def test_builds_the_reference_kg_directory_index():
+    """A KG directory in the reference's layout (tests/golden/kg_directory_toy: spread-out
+    item numbers, an alias-only property, triples naming unknown items and properties,
+    sitelink counts) builds the index the reference's own directory builder saved from it
+    (tests/golden/kg_directory_toy_index, both made by tests/golden/make_kg_directory.py):
+    the same arrays, unwritable count and packed device tables."""
+    from pathlib import Path
+
+    from xgraph_b200.index import build_kg_directory_index, load_kg_index
+    from xgraph_b200.syntax import SpanSyntax
+    from xgraph_b200.tables import pack_tables
+
+    golden = Path(__file__).parent / "golden"
+    served = _rand_bpe_served()
+    built = build_kg_directory_index(golden / "kg_directory_toy", served, SpanSyntax())
+    saved = load_kg_index(golden / "kg_directory_toy_index")
+    for part in ("labels", "relations"):
+        a, b = getattr(built, part), getattr(saved, part)
+        assert a.owner_ids == b.owner_ids
+        for name in ("tokens", "offsets", "owners"):
+            np.testing.assert_array_equal(getattr(a, name), getattr(b, name))
+    for name in ("adjacency_offsets", "edge_relations", "edge_objects", "sitelinks"):
+        np.testing.assert_array_equal(getattr(built, name), getattr(saved, name))
+    assert built.unwritable_triples == saved.unwritable_triples == 2
+    a = pack_tables(built, served, built.span_syntax, escapes=True)
+    b = pack_tables(saved, served, saved.span_syntax, escapes=True)
+    np.testing.assert_array_equal(a.blob, b.blob)
+
+
+def test_kg_directory_errors_and_relation_names(tmp_path):
+    import json
+
+    from xgraph_b200.index import build_kg_directory_index, relation_names
+    from xgraph_b200.kg import KGFormatError
+    from xgraph_b200.syntax import SpanSyntax
+
+    rows = [("P1", "head of state", "label"), ("P2", "office held", "label"), ("P2", "Head of State", "alias"),
+            ("P2", "chief", "alias"), ("P3", "leader", "label"), ("P3", "chief", "alias")]
+    assert relation_names(rows) == {"P1": ["head of state"], "P2": ["office held", "chief"],
+                                    "P3": ["leader", "chief"]}
+    assert relation_names(rows, unique_aliases=True) == {"P1": ["head of state"], "P2": ["office held"],
+                                                         "P3": ["leader"]}
+    served = _rand_bpe_served()
+    with pytest.raises(KGFormatError, match="missing"):
+        build_kg_directory_index(tmp_path, served, SpanSyntax())
+    (tmp_path / "entity_labels.jsonl").write_text(json.dumps(["E7", "Ba", "label"]) + "\n", encoding="utf-8")
+    (tmp_path / "relation_labels.jsonl").write_text(json.dumps(["P1", "author", "label"]) + "\n", encoding="utf-8")
+    np.save(tmp_path / "triples.npy", np.zeros((0, 3), dtype=np.int32))
+    with pytest.raises(KGFormatError, match="Q<number>"):
+        build_kg_directory_index(tmp_path, served, SpanSyntax())

@@ -433,6 +433,90 @@ def build_kg_index(
     )
 
 
+def relation_names(rows, unique_aliases: bool = False) -> dict[str, list[str]]:
+    """Each property's names from relation label rows (property, label, kind), labels
+    first (src/xgraph/wikidata.py:835-857): an alias that is, ignoring case, another
+    property's label is dropped, and with unique_aliases so is an alias several
+    properties share (a path naming it would follow every one of them)."""
+    rows = [tuple(row) for row in rows]
+    labels = {label.casefold(): prop for prop, label, kind in rows if kind == "label"}
+    owners: dict[str, set[str]] = {}
+    for prop, label, kind in rows:
+        if kind != "label":
+            owners.setdefault(label.casefold(), set()).add(prop)
+    names: dict[str, list[str]] = {}
+    for prop, label, kind in sorted(rows, key=lambda row: row[2] != "label"):
+        if kind != "label" and labels.get(label.casefold(), prop) != prop:
+            continue
+        if kind != "label" and unique_aliases and len(owners[label.casefold()]) > 1:
+            continue
+        names.setdefault(prop, []).append(label)
+    return names
+
+
+KG_DIRECTORY_FILES = ("entity_labels.jsonl", "relation_labels.jsonl", "triples.npy")
+SITELINK_COUNTS = "sitelink_counts.npy"
+
+
+def build_kg_directory_index(
+    kg: str | Path, tokenizer: ServedTokenizer, syntax: SpanSyntax, unique_aliases: bool = False, device=None,
+) -> KGIndex:
+    """The KG index of a KG directory in the reference's layout (src/xgraph/wikidata.py:
+    859-1037): entity_labels.jsonl and relation_labels.jsonl hold one JSON list [id,
+    label, "label" | "alias"] per line (items Q<n>, properties P<n>), triples.npy the
+    (subject item, property, object item) numbers, sitelink_counts.npy (optional) [item,
+    count] rows.  Entities are the items with a label row, in item-number order, each with
+    its labels in file order; relations the properties relation_names keeps, in number
+    order; a triple naming an item or property without one is unwritable, like a triple
+    whose subject, object or relation has no label row.  The arrays equal the reference
+    builder's; `device` builds the edge arrays on that GPU.  The directory's date tables
+    and RDF ids feed policies this engine does not serve and are not read."""
+    kg = Path(kg)
+    for name in KG_DIRECTORY_FILES:
+        if not (kg / name).is_file():
+            raise KGFormatError(f"{kg} is not a KG directory: {name} is missing")
+
+    def records(name: str) -> list[tuple]:
+        with (kg / name).open(encoding="utf-8") as lines:
+            return [tuple(json.loads(line)) for line in lines if line.strip()]
+
+    def number(identifier: str, prefix: str) -> int:
+        if not (isinstance(identifier, str) and identifier[:1] == prefix and identifier[1:].isdigit()):
+            raise KGFormatError(f"{kg}: {identifier!r} is not a {prefix}<number> id")
+        return int(identifier[1:])
+
+    labels_of: dict[int, list[str]] = {}
+    for identifier, label, _kind in records("entity_labels.jsonl"):
+        labels_of.setdefault(number(identifier, "Q"), []).append(label)
+    items = np.array(sorted(labels_of), dtype=np.int64)
+    entities = [(f"Q{n}", labels_of[n]) for n in items.tolist()]
+    names = relation_names(records("relation_labels.jsonl"), unique_aliases)
+    properties = sorted(names, key=lambda p: number(p, "P"))
+    relations = [(p, names[p]) for p in properties]
+    numbers = np.array([number(p, "P") for p in properties], dtype=np.int64)
+
+    def positions(known: np.ndarray, wanted: np.ndarray) -> np.ndarray:
+        if not len(known):
+            return np.full(len(wanted), -1, dtype=np.int64)
+        at = np.minimum(np.searchsorted(known, wanted), len(known) - 1)
+        return np.where(known[at] == wanted, at, -1)
+
+    raw = np.asarray(np.load(kg / "triples.npy"), dtype=np.int64).reshape(-1, 3)
+    found = np.stack([positions(items, raw[:, 0]), positions(numbers, raw[:, 1]), positions(items, raw[:, 2])], axis=1)
+    known = (found >= 0).all(axis=1)
+    sitelinks = None
+    if (kg / SITELINK_COUNTS).is_file():
+        table = np.asarray(np.load(kg / SITELINK_COUNTS), dtype=np.int64).reshape(-1, 2)
+        order = np.argsort(table[:, 0], kind="stable")
+        at = positions(table[order, 0], items)
+        sitelinks = np.where(at >= 0, table[order, 1][np.maximum(at, 0)] if len(table) else 0, 0)
+    index = build_kg_index_arrays(entities, relations, found[known], tokenizer, syntax, sitelinks=sitelinks,
+                                  device=device)
+    from dataclasses import replace
+
+    return replace(index, unwritable_triples=index.unwritable_triples + int((~known).sum()))
+
+
 START_RANKS = ("degree", "sitelinks")
 
 
