@@ -24,7 +24,7 @@ import bisect
 import hashlib
 import json
 from collections.abc import Mapping, Sequence
-from dataclasses import dataclass, field
+from dataclasses import dataclass, field, replace
 from pathlib import Path
 
 import numpy as np
@@ -512,8 +512,6 @@ def build_kg_directory_index(
         sitelinks = np.where(at >= 0, table[order, 1][np.maximum(at, 0)] if len(table) else 0, 0)
     index = build_kg_index_arrays(entities, relations, found[known], tokenizer, syntax, sitelinks=sitelinks,
                                   device=device)
-    from dataclasses import replace
-
     return replace(index, unwritable_triples=index.unwritable_triples + int((~known).sum()))
 
 
