@@ -395,8 +395,15 @@ def engine_arm(args) -> None:
         "setup_s": {"workload_build": build_s, "stream_sampling": sample_s},
     }
     if not args.profile:
-        result["e2e"] = e2e_leg(engine, workload, history, restart_t, prompt, total, slots, rows, vocab, device,
-                                min(args.e2e_steps, total_steps), dtype)
+        e2e = e2e_leg(engine, workload, history, restart_t, prompt, total, slots, rows, vocab, device,
+                      min(args.e2e_steps, total_steps), dtype)
+        if world > 1:  # whole job: every rank's rows over the slowest rank's time
+            e2e_t = torch.tensor([e2e["ms_per_step"]], dtype=torch.float64, device=device)
+            dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
+            e2e["ms_per_step"] = float(e2e_t.item())
+            e2e["value"] = rows * world * 1e3 / e2e["ms_per_step"]
+            e2e["timing"] = "max over ranks of each rank's end-to-end time; value over all ranks' rows"
+        result["e2e"] = e2e
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
