@@ -67,3 +67,49 @@ def _begin_adapter(seam):
             plain(int(slot))
 
     return begin
+
+
+def test_request_edits_are_pair_replacements_the_versions_apply():
+    """The seeded per-request edits (the versions benchmark configuration) are the
+    reference's pair-replacement edits (src/xgraph/kgversions.py:203-216): in the built
+    version every touched (subject, relation) pair holds exactly the label rows of its
+    edits' objects (none when the pair was emptied), and untouched pairs keep the base
+    KG's objects."""
+    from xgraph_b200.index import build_kg_index_arrays
+    from xgraph_b200.kgversions import build_kg_versions
+    from xgraph_b200.syntax import SpanSyntax
+    from xgraph_b200.synthetic import object_sets, request_edits, synthetic_tokenizer, synthetic_world
+
+    syntax = SpanSyntax()
+    world = synthetic_world(21, 400, 12, 3000, labels=(1, 2))
+    served = synthetic_tokenizer(world, 1500, syntax)
+    index = build_kg_index_arrays(world.entities, world.relations, world.triples, served, syntax)
+    pairs = object_sets(world)
+    assert request_edits(world, pairs, np.random.default_rng(0), 0) == []
+    edits = request_edits(world, pairs, np.random.default_rng(3), 120)
+    view = build_kg_versions(index, {"r": edits}).view(index, "r")
+    entity_at = {e: k for k, (e, _) in enumerate(world.entities)}
+    rows_of: dict[int, list[int]] = {}
+    for row, owner in enumerate(index.labels.owners):
+        rows_of.setdefault(int(owner), []).append(row)
+    touched: dict[tuple[str, str], set[str]] = {}
+    emptied = 0
+    for s, r, o in edits:
+        touched.setdefault((s, r), set())
+        if o is None:
+            emptied += 1
+        else:
+            touched[(s, r)].add(o)
+    assert touched and emptied
+    for (s, r), objects in touched.items():
+        if not rows_of.get(entity_at[s]):
+            continue  # a subject without label rows: the edit is unwritable
+        expected = {row for o in objects for row in rows_of.get(entity_at[o], [])}
+        assert set(view.object_rows(s, r)) == expected, (s, r)
+    relation_id = [r for r, _ in world.relations]
+    for (s, r), objects in list(pairs.items())[:200]:
+        sid, rid = world.entities[s][0], relation_id[r]
+        if (sid, rid) in touched or not rows_of.get(s):
+            continue
+        expected = {row for o in objects for row in rows_of.get(o, [])}
+        assert set(view.object_rows(sid, rid)) == expected, (sid, rid)
