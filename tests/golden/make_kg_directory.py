@@ -11,8 +11,11 @@ From the rand_bpe world of worlds.json.gz it writes, next to this script:
                            [id, label, "label" | "alias"] per line), triples.npy (int32
                            item/property numbers), sitelink_counts.npy ([item, count] rows)
   kg_directory_toy_index/  the reference's build_index output (its on-disk index format)
-Item numbers are spread out (Q10, Q13, ...), and a few triples name items or properties
-that have no label rows, so the position lookup and the unwritable count are exercised.
+  kg_directory_toy_index_unique/  the same with unique_aliases
+Item numbers are spread out (Q10, Q13, ...), a few triples name items or properties that
+have no label rows, and the relation rows hold an alias-only property, an alias that is
+another property's label and an alias two properties share, so the position lookup, the
+unwritable count and the relation-name rules are exercised.
 """
 
 from __future__ import annotations
@@ -59,6 +62,11 @@ def main() -> None:
             for k, label in enumerate(labels):
                 f.write(json.dumps([f"P{prop[r]}", label, "label" if k == 0 else "alias"]) + "\n")
         f.write(json.dumps(["P3", "unused alias", "alias"]) + "\n")  # a property with no label
+        first, second, third = (f"P{prop[r]}" for r, _ in world["relations"][:3])
+        label_of_second = world["relations"][1][1][0]
+        f.write(json.dumps([first, label_of_second.upper(), "alias"]) + "\n")  # another property's label
+        f.write(json.dumps([second, "shared name", "alias"]) + "\n")  # an alias two properties share
+        f.write(json.dumps([third, "shared name", "alias"]) + "\n")
     triples = [(item[s], prop[r], item[o]) for s, r, o in world["triples"]]
     triples += [(99999, prop[world["relations"][0][0]], item[world["entities"][0][0]]),
                 (item[world["entities"][1][0]], 3, item[world["entities"][2][0]]),
@@ -68,7 +76,11 @@ def main() -> None:
     np.save(kg / "sitelink_counts.npy", np.array(counts, dtype=np.int64))
     served = ServedTokenizer(Tokenizer.from_str(world["tokenizer"]))
     build_index(kg, served, SpanSyntax(), out)
-    print("wrote", kg, "and", out)
+    unique = HERE / "kg_directory_toy_index_unique"
+    if unique.exists():
+        shutil.rmtree(unique)
+    build_index(kg, served, SpanSyntax(), unique, unique_aliases=True)
+    print("wrote", kg, out, "and", unique)
 
 
 if __name__ == "__main__":

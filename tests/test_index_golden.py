@@ -86,12 +86,15 @@ def _rand_bpe_served():
     return served
 
 
-def test_builds_the_reference_kg_directory_index():
+@pytest.mark.parametrize("unique", [False, True])
+def test_builds_the_reference_kg_directory_index(unique):
     """A KG directory in the reference's layout (tests/golden/kg_directory_toy: spread-out
     item numbers, an alias-only property, triples naming unknown items and properties,
-    sitelink counts) builds the index the reference's own directory builder saved from it
-    (tests/golden/kg_directory_toy_index, both made by tests/golden/make_kg_directory.py):
-    the same arrays, unwritable count and packed device tables."""
+    sitelink counts, aliases that are another property's label or shared by two) builds the
+    index the reference's own directory builder saved from it, with and without
+    unique_aliases (tests/golden/kg_directory_toy_index[_unique], all made by
+    tests/golden/make_kg_directory.py): the same arrays, unwritable count and packed
+    device tables."""
     from pathlib import Path
 
     from xgraph_b200.index import build_kg_directory_index, load_kg_index
@@ -100,8 +103,8 @@ def test_builds_the_reference_kg_directory_index():
 
     golden = Path(__file__).parent / "golden"
     served = _rand_bpe_served()
-    built = build_kg_directory_index(golden / "kg_directory_toy", served, SpanSyntax())
-    saved = load_kg_index(golden / "kg_directory_toy_index")
+    built = build_kg_directory_index(golden / "kg_directory_toy", served, SpanSyntax(), unique_aliases=unique)
+    saved = load_kg_index(golden / ("kg_directory_toy_index_unique" if unique else "kg_directory_toy_index"))
     for part in ("labels", "relations"):
         a, b = getattr(built, part), getattr(saved, part)
         assert a.owner_ids == b.owner_ids
