@@ -139,3 +139,24 @@ def test_kg_directory_errors_and_relation_names(tmp_path):
     np.save(tmp_path / "triples.npy", np.zeros((0, 3), dtype=np.int32))
     with pytest.raises(KGFormatError, match="Q<number>"):
         build_kg_directory_index(tmp_path, served, SpanSyntax())
+
+
+def test_directory_index_command_saves_what_the_builder_returns(tmp_path):
+    import gzip
+    import json
+    from pathlib import Path
+
+    from xgraph_b200.index import build_kg_directory_index, load_kg_index, main
+    from xgraph_b200.syntax import SpanSyntax
+
+    golden = Path(__file__).parent / "golden"
+    with gzip.open(golden / "worlds.json.gz", "rt", encoding="utf-8") as f:
+        (tmp_path / "tokenizer.json").write_text(json.load(f)["rand_bpe"]["tokenizer"], encoding="utf-8")
+    main(["--kg", str(golden / "kg_directory_toy"), "--tokenizer", str(tmp_path / "tokenizer.json"),
+          "--out", str(tmp_path / "index"), "--unique-aliases"])
+    saved = load_kg_index(tmp_path / "index")
+    built = build_kg_directory_index(golden / "kg_directory_toy", _rand_bpe_served(), SpanSyntax(), unique_aliases=True)
+    assert saved.base_fingerprint == built.base_fingerprint
+    for name in ("adjacency_offsets", "edge_relations", "edge_objects", "sitelinks"):
+        np.testing.assert_array_equal(getattr(saved, name), getattr(built, name))
+    assert saved.relations.owner_ids == built.relations.owner_ids

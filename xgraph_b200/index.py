@@ -630,3 +630,33 @@ def _load_reference_index(directory: Path, header: dict) -> KGIndex:
     return KGIndex(labels=labels, relations=relations, adjacency_offsets=offsets, edge_relations=edge_rel,
                    edge_objects=edge_obj, unwritable_triples=header["unwritable_triples"], span_syntax=syntax,
                    sitelinks=sitelinks, base_fingerprint=fingerprint)
+
+
+def main(argv: list[str] | None = None) -> None:
+    """Build and save the KG index of a KG directory (the reference's
+    `python -m xgraph.wikidata index`, src/xgraph/wikidata.py:1040-1139, for the
+    policies this engine serves); --device builds the edge arrays on that GPU."""
+    import argparse
+
+    from .syntax import preset
+    from .tokenizer import ServedTokenizer
+
+    parser = argparse.ArgumentParser(prog="python -m xgraph_b200.index", description=main.__doc__)
+    parser.add_argument("--kg", type=Path, required=True, help="KG directory (entity/relation label rows, triples)")
+    parser.add_argument("--tokenizer", type=Path, required=True, help="served tokenizer.json")
+    parser.add_argument("--out", type=Path, required=True, help="KG index directory to write")
+    parser.add_argument("--syntax", default="brackets", help="span syntax preset the index is built for")
+    parser.add_argument("--unique-aliases", action="store_true",
+                        help="drop relation aliases that several properties share")
+    parser.add_argument("--device", default=None, help="a CUDA device for the edge build (default: the host)")
+    args = parser.parse_args(argv)
+    index = build_kg_directory_index(args.kg, ServedTokenizer.from_file(args.tokenizer), preset(args.syntax),
+                                     unique_aliases=args.unique_aliases, device=args.device)
+    save_kg_index(index, args.out)
+    print(f"{args.out}: {len(index.labels.owner_ids):,} entities, {index.labels.num_rows:,} label rows, "
+          f"{len(index.relations.owner_ids):,} relations, {len(index.edge_objects):,} edges, "
+          f"{index.unwritable_triples:,} unwritable triples")
+
+
+if __name__ == "__main__":
+    main()
