@@ -113,3 +113,36 @@ def test_request_edits_are_pair_replacements_the_versions_apply():
             continue
         expected = {row for o in objects for row in rows_of.get(o, [])}
         assert set(view.object_rows(sid, rid)) == expected, (sid, rid)
+
+
+def test_seam_masks_equal_the_oracle_at_the_ordinary_benchmark_size():
+    """The kernel logic compiled for the host (tests/seam.py) on the ordinary benchmark
+    configuration's world (20 k entities, 50 relations, 100 k triples, a 32,000-id BPE):
+    three constrained streams of 40 tokens sampled under its own masks, and at every step
+    the full allowed set equals the oracle's."""
+    import torch
+
+    from oracle.oracle import Oracle
+    from tests.conftest import unpack
+    from tests.seam import SeamEngine
+    from xgraph_b200.synthetic import build_workload, sample_streams
+
+    w = build_workload(2)
+    rows, steps = 3, 40
+    seam = SeamEngine(w.index, w.served, w.syntax, rows, **w.config.options)
+    seam.begin = _begin_adapter(seam)
+    record = {(r, k) for r in range(rows) for k in range(steps + 1)}
+    tokens, _, recorded = sample_streams(seam, w.served, w.syntax, w.world, rows, steps, seed=12,
+                                         device="cpu", record=record)
+    oracle = Oracle(w.index, w.served, w.syntax, **w.config.options)
+    spans = 0
+    for r in range(rows):
+        state = oracle.initial_state()
+        for k in range(steps + 1):
+            words = recorded[(r, k)].numpy().astype(np.uint32) if isinstance(recorded[(r, k)], torch.Tensor) \
+                else np.asarray(recorded[(r, k)], dtype=np.uint32)
+            assert unpack(words, w.served.vocab_size) == set(oracle.allowed(state)), (r, k)
+            if k < steps:
+                state = oracle.advance(state, int(tokens[r, k]))
+                spans += state.phase.value == "span"
+    assert spans > rows * steps // 10
