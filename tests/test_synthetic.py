@@ -120,8 +120,6 @@ def test_seam_masks_equal_the_oracle_at_the_ordinary_benchmark_size():
     configuration's world (20 k entities, 50 relations, 100 k triples, a 32,000-id BPE):
     three constrained streams of 40 tokens sampled under its own masks, and at every step
     the full allowed set equals the oracle's."""
-    import torch
-
     from oracle.oracle import Oracle
     from tests.conftest import unpack
     from tests.seam import SeamEngine
@@ -139,9 +137,38 @@ def test_seam_masks_equal_the_oracle_at_the_ordinary_benchmark_size():
     for r in range(rows):
         state = oracle.initial_state()
         for k in range(steps + 1):
-            words = recorded[(r, k)].numpy().astype(np.uint32) if isinstance(recorded[(r, k)], torch.Tensor) \
-                else np.asarray(recorded[(r, k)], dtype=np.uint32)
+            words = np.asarray(recorded[(r, k)]).astype(np.uint32)
             assert unpack(words, w.served.vocab_size) == set(oracle.allowed(state)), (r, k)
+            if k < steps:
+                state = oracle.advance(state, int(tokens[r, k]))
+                spans += state.phase.value == "span"
+    assert spans > rows * steps // 10
+
+
+def test_seam_masks_equal_the_oracle_at_the_path_benchmark_size():
+    """The same at the path benchmark configuration (100 k entities with 1-3 labels, 1 M
+    triples, paths with committed paths, V = 128,256): two streams of 60 tokens, the full
+    allowed set compared with the oracle's at every fourth step (a 128 k-wide scan each)."""
+    from oracle.oracle import Oracle
+    from tests.conftest import unpack
+    from tests.seam import SeamEngine
+    from xgraph_b200.synthetic import build_workload, sample_streams
+
+    w = build_workload(3)
+    rows, steps = 2, 60
+    seam = SeamEngine(w.index, w.served, w.syntax, rows, **w.config.options)
+    seam.begin = _begin_adapter(seam)
+    record = {(r, k) for r in range(rows) for k in range(0, steps + 1, 4)}
+    tokens, _, recorded = sample_streams(seam, w.served, w.syntax, w.world, rows, steps, seed=13,
+                                         device="cpu", record=record)
+    oracle = Oracle(w.index, w.served, w.syntax, **w.config.options)
+    spans = 0
+    for r in range(rows):
+        state = oracle.initial_state()
+        for k in range(steps + 1):
+            if (r, k) in recorded:
+                words = np.asarray(recorded[(r, k)]).astype(np.uint32)
+                assert unpack(words, w.served.vocab_size) == set(oracle.allowed(state)), (r, k)
             if k < steps:
                 state = oracle.advance(state, int(tokens[r, k]))
                 spans += state.phase.value == "span"
