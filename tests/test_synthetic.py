@@ -173,3 +173,57 @@ def test_seam_masks_equal_the_oracle_at_the_path_benchmark_size():
                 state = oracle.advance(state, int(tokens[r, k]))
                 spans += state.phase.value == "span"
     assert spans > rows * steps // 10
+
+
+def test_seam_masks_equal_the_oracle_with_per_request_kg_versions():
+    """The versions configuration on the host-compiled kernel logic: three requests, each
+    with 0-256 seeded add/remove edits as its own KG version, V = 151,936, paths with
+    committed paths, on a 2 k-entity world (so the edits meet the walks): every sixth
+    step's full allowed set equals the oracle's for the request's version, and the same
+    streams replayed on the base KG mask some step differently."""
+    from oracle.oracle import Oracle
+    from tests.conftest import unpack
+    from tests.seam import SeamEngine
+    from xgraph_b200.index import build_kg_index_arrays
+    from xgraph_b200.kgversions import build_kg_versions
+    from xgraph_b200.syntax import SpanSyntax
+    from xgraph_b200.synthetic import (object_sets, request_edits, sample_streams, synthetic_tokenizer,
+                                       synthetic_world)
+
+    syntax = SpanSyntax()
+    world = synthetic_world(505, 2_000, 40, 20_000, labels=(1, 3))
+    served = synthetic_tokenizer(world, 151_936, syntax)
+    index = build_kg_index_arrays(world.entities, world.relations, world.triples, served, syntax,
+                                  sitelinks=world.sitelinks)
+    rng = np.random.default_rng(55)
+    rows, steps, every = 3, 48, 6
+    pairs = object_sets(world)
+    edits = {f"request-{i}": request_edits(world, pairs, rng, int(rng.integers(0, 257))) for i in range(rows)}
+    names = list(edits)
+    options = {"paths": True, "committed_paths": True}
+    seam = SeamEngine(index, served, syntax, rows, versions=build_kg_versions(index, edits), **options)
+    seam.begin = _begin_adapter(seam)
+    record = {(r, k) for r in range(rows) for k in range(steps + 1)}
+    tokens, _, recorded = sample_streams(seam, served, syntax, world, rows, steps, seed=56, device="cpu",
+                                         record=record, versions=names)
+    # the same streams on the base KG mask some step differently: the versions are read
+    base = SeamEngine(index, served, syntax, rows, **options)
+    for r in range(rows):
+        base.begin(r)
+    differs = 0
+    host_tokens = np.asarray(tokens)
+    for k in range(steps + 1):
+        masks = base.masks()
+        differs += sum(not np.array_equal(masks[r], np.asarray(recorded[(r, k)]).astype(np.uint32)) for r in range(rows))
+        if k < steps:
+            base.advance(host_tokens[:, k])
+    assert differs > 0
+    oracle = Oracle(index, served, syntax, versions=edits, **options)
+    for r in range(rows):
+        state = oracle.initial_state(names[r])
+        for k in range(steps + 1):
+            if k % every == 0:
+                words = np.asarray(recorded[(r, k)]).astype(np.uint32)
+                assert unpack(words, served.vocab_size) == set(oracle.allowed(state)), (r, k)
+            if k < steps:
+                state = oracle.advance(state, int(host_tokens[r, k]))
