@@ -50,3 +50,28 @@ def test_engine_constructor_fails_loudly_without_the_library(monkeypatch, tmp_pa
     monkeypatch.setattr(engine, "_lib", None)
     with pytest.raises(engine.EngineUnavailable):
         engine.load_library(tmp_path / "missing.so")
+
+
+def test_adjacency_build_rejects_bad_arguments_before_any_device_work():
+    """xg_build_adjacency checks its outputs, sizes and pointers on the host and fails with
+    XG_EINVAL (ValueError) before touching the GPU."""
+    from xgraph_b200.engine import _check, load_library
+
+    lib = load_library()
+    edges, unwritable = ctypes.c_int64(), ctypes.c_int64()
+    fake = ctypes.c_void_p(16)  # never dereferenced: every call below fails its host checks first
+    cases = [
+        ((fake, fake, fake, 1, fake, fake, 2, 2, fake, 1, 0, None, None, None, None, ctypes.byref(unwritable), None),
+         "null edges"),
+        ((fake, fake, fake, -1, fake, fake, 2, 2, fake, 1, 0, None, None, None, ctypes.byref(edges),
+          ctypes.byref(unwritable), None), "negative size"),
+        ((None, fake, fake, 3, fake, fake, 2, 2, fake, 1, 0, None, None, None, ctypes.byref(edges),
+          ctypes.byref(unwritable), None), "null triples"),
+        ((fake, fake, fake, 3, None, fake, 2, 2, fake, 1, 0, None, None, None, ctypes.byref(edges),
+          ctypes.byref(unwritable), None), "null label rows"),
+        ((fake, fake, fake, 3, fake, fake, 1 << 30, 1 << 30, fake, 1 << 30, 0, None, None, None, ctypes.byref(edges),
+          ctypes.byref(unwritable), None), "too large"),
+    ]
+    for args, message in cases:
+        with pytest.raises(ValueError, match=message):
+            _check(lib.xg_build_adjacency(*args))
