@@ -82,6 +82,19 @@ def make_workload(config: int, seed: int):
     return build_workload(config, seed)
 
 
+def admissions_tensor(slots: list[int], device):
+    """Device admission records (xgraph_b200.engine.ADMISSION_INTS int32 each) beginning
+    these slots on the base KG."""
+    import torch
+
+    from xgraph_b200.engine import ADMISSION_INTS
+
+    records = np.zeros((len(slots), ADMISSION_INTS), dtype=np.int32)
+    records[:, 0] = slots
+    records[:, 1] = 1
+    return torch.from_numpy(records).to(device)
+
+
 def schedule(lengths: list[int], rows: int, steps: int):
     """Per slot, the streams it replays back to back (stream ids) and, per step, the
     slots that start a new stream (replenishment)."""
@@ -146,75 +159,182 @@ def measured_peak() -> tuple[float, str]:
 
 
 # ---------------------------------------------------------------------------------------
-# CPU baseline: the oracle port on the host cores (spawned workers).
+# Token streams: the committed fixture both arms replay (tests/golden/make_streams.py made
+# it with the engine's sampler on a GPU; tests/test_streams_fixture.py checks every token
+# against the oracle).  Configurations without a fixture sample their streams on the GPU.
 
-def _cpu_worker(args):
-    index, served, options, jobs, budget = args
+STREAM_FIXTURES = {3: ROOT / "tests" / "golden" / "streams_paths100k.npz"}
+
+
+def load_streams(config: int, workload):
+    """(tokens [P, L] int32, lengths [P] int32, allowed counts [P, L + 1] int32) of the
+    configuration's fixture, or None when it has none."""
+    path = STREAM_FIXTURES.get(config)
+    if path is None or not path.is_file():
+        return None
+    data = np.load(path)
+    if int(data["config"]) != config or int(data["vocab"]) != workload.served.vocab_size:
+        raise RuntimeError(f"{path} was made for another workload")
+    if str(data["fingerprint"]) != workload.served.fingerprint:
+        raise RuntimeError(f"{path} was made with another tokenizer")
+    return data["tokens"].astype(np.int32), data["lengths"].astype(np.int32), data["allowed"].astype(np.int32)
+
+
+def row_plan(rows: int, lengths, steps: int, offset: int = 0):
+    """Per row, the (stream, position) it replays at each step: row r replays streams
+    offset + r, offset + r + rows, ... back to back (a finished request's slot takes the
+    next one, as a serving batch does)."""
+    n = len(lengths)
+    plan = np.zeros((rows, steps, 2), dtype=np.int64)
+    for r in range(rows):
+        sid, at = (offset + r) % n, 0
+        for k in range(steps):
+            if at >= lengths[sid]:
+                sid, at = (sid + rows) % n, 0
+            plan[r, k] = (sid, at)
+            at += 1
+    return plan
+
+
+# ---------------------------------------------------------------------------------------
+# The oracle on the host cores (spawned workers): the CPU baseline of the engine arm and
+# the whole of the reference arm.  Worker w owns rows w, w + workers, ...; at every step
+# each of its rows takes its next token, and one of them (in turn) takes it the way a
+# CPU decoding loop would (allowed set, masked logits, advance: examples/sampling_loop.py
+# of the reference), the others by advance alone.  Throughput = full row-steps / wall time.
+
+_WORKER = {}
+
+
+def _worker_init(index, served, syntax, options, tokens, vocab):
     from oracle.oracle import Oracle
-    from xgraph_b200.syntax import SpanSyntax
 
-    oracle = Oracle(index, served, SpanSyntax(), **options)
-    vocab = served.vocab_size
-    rng = np.random.default_rng(len(jobs))
-    logits_src = rng.normal(0.0, 2.0, size=vocab).astype(np.float32)
-    done, spent, mismatches = 0, 0.0, 0
-    started = time.perf_counter()
-    for tokens, sampled, masks in jobs:
-        state = oracle.initial_state()
-        for step, token in enumerate(tokens):
-            if step in sampled:
-                t0 = time.perf_counter()
-                allowed = oracle.allowed(state)
-                mask = np.zeros(vocab, dtype=bool)
-                mask[list(allowed)] = True
-                logits = logits_src.copy()
-                logits[~mask] = -np.inf
-                state = oracle.advance(state, token)
-                spent += time.perf_counter() - t0
-                done += 1
-                words = masks[step]
-                bits = np.unpackbits(words.view(np.uint8), bitorder="little")[:vocab].astype(bool)
-                mismatches += int((bits != mask).any())
-            else:
-                state = oracle.advance(state, token)
-            if time.perf_counter() - started > budget:
-                break
-        if time.perf_counter() - started > budget:
+    _WORKER["oracle"] = Oracle(index, served, syntax, **options)
+    _WORKER["tokens"] = tokens
+    _WORKER["vocab"] = vocab
+    _WORKER["states"] = {}
+    rng = np.random.default_rng(0)
+    _WORKER["logits"] = rng.normal(0.0, 2.0, size=vocab).astype(np.float32)
+
+
+def _worker_step(job):
+    """One step of one worker: job = (rows: [(row, stream, position)], full row index,
+    mask words expected at the full row-step or None).  Returns (seconds of the full
+    row-step, mask mismatch 0/1/None)."""
+    oracle, tokens, vocab = _WORKER["oracle"], _WORKER["tokens"], _WORKER["vocab"]
+    states = _WORKER["states"]
+    rows, full, expected = job
+    spent, mismatch = 0.0, None
+    for row, sid, pos in rows:
+        if pos == 0 or row not in states:
+            states[row] = oracle.initial_state()
+        token = int(tokens[sid, pos])
+        if row == full:
+            t0 = time.perf_counter()
+            state = states[row]
+            allowed = oracle.allowed(state)
+            mask = np.zeros(vocab, dtype=bool)
+            mask[list(allowed)] = True
+            logits = _WORKER["logits"].copy()
+            logits[~mask] = -np.inf
+            states[row] = oracle.advance(state, token)
+            spent = time.perf_counter() - t0
+            if expected is not None:
+                bits = np.unpackbits(expected.view(np.uint8), bitorder="little")[:vocab].astype(bool)
+                mismatch = int((bits != mask).any())
+        else:
+            states[row] = oracle.advance(states[row], token)
+    return spent, mismatch
+
+
+def _worker_main(conn, init_args):
+    _worker_init(*init_args)
+    conn.send("ready")
+    while True:
+        job = conn.recv()
+        if job is None:
             break
-    return done, spent, mismatches
+        conn.send(_worker_step(job))
 
 
-def cpu_baseline(workload, streams, recorded, budget: float, workers: int | None = None) -> dict:
+def oracle_leg(workload, tokens, lengths, rows: int, steps: int, warmup: int, *, budget: float | None = None,
+               expected: dict | None = None, workers: int | None = None) -> dict:
+    """The oracle replaying rows x (warmup + steps) of the streams on `workers` spawned
+    processes, each owning a fixed set of rows; a step waits for every worker.  With
+    `budget` (seconds) the timed steps stop early once it is spent.  expected:
+    {(stream, position): mask words} to check the full row-steps against."""
     import multiprocessing as mp
 
     cores = os.cpu_count() or 1
-    workers = workers or max(1, min(cores, 32))
-    jobs = [[] for _ in range(workers)]
-    by_row: dict[int, list[int]] = {}
-    for (row, step) in recorded:
-        by_row.setdefault(row, []).append(step)
-    for k, (row, steps) in enumerate(sorted(by_row.items())):
-        last = max(steps)
-        jobs[k % workers].append((streams[row][: last + 1], set(steps), {s: recorded[(row, s)] for s in steps}))
-    options = dict(workload.config.options)
+    workers = workers or max(1, min(cores, 32, rows))
+    plan = row_plan(rows, lengths, warmup + steps)
+    owned = [list(range(w, rows, workers)) for w in range(workers)]
+    init = (workload.index, workload.served, workload.syntax, dict(workload.config.options), tokens,
+            workload.served.vocab_size)
     ctx = mp.get_context("spawn")
-    t0 = time.perf_counter()
-    with ctx.Pool(workers) as pool:
-        results = pool.map(_cpu_worker, [(workload.index, workload.served, options, j, budget) for j in jobs])
-    wall = time.perf_counter() - t0
-    done = sum(r[0] for r in results)
-    spent = sum(r[1] for r in results)
-    mismatches = sum(r[2] for r in results)
-    per_core = done / spent if spent else 0.0
+    t_setup = time.perf_counter()
+    pipes, procs = [], []
+    for _ in range(workers):
+        here, there = ctx.Pipe()
+        proc = ctx.Process(target=_worker_main, args=(there, init), daemon=True)
+        proc.start()
+        pipes.append(here)
+        procs.append(proc)
+    try:
+        for conn in pipes:
+            if conn.recv() != "ready":
+                raise RuntimeError("an oracle worker failed to start")
+        setup = time.perf_counter() - t_setup
+        done = mismatches = checked = timed = 0
+        busy = wall = 0.0
+        for k in range(warmup + steps):
+            jobs = []
+            for mine in owned:
+                full = mine[k % len(mine)]
+                want = None
+                if expected is not None:
+                    want = expected.get((int(plan[full, k, 0]), int(plan[full, k, 1])))
+                jobs.append(([(r, int(plan[r, k, 0]), int(plan[r, k, 1])) for r in mine], full, want))
+            t0 = time.perf_counter()
+            for conn, job in zip(pipes, jobs):
+                conn.send(job)
+            results = [conn.recv() for conn in pipes]
+            elapsed = time.perf_counter() - t0
+            if k >= warmup:
+                wall += elapsed
+                timed += 1
+                done += workers
+                busy += sum(r[0] for r in results)
+            for _, m in results:
+                if m is not None:
+                    checked += 1
+                    mismatches += m
+            if budget is not None and k >= warmup and wall > budget:
+                break
+    finally:
+        for conn in pipes:
+            try:
+                conn.send(None)
+            except OSError:
+                pass
+        for proc in procs:
+            proc.join(timeout=30)
+            if proc.is_alive():
+                proc.terminate()
+    return {"row_steps": done, "steps": timed, "wall_s": wall, "busy_s": busy, "workers": workers,
+            "setup_s": setup, "checked": checked, "mismatches": mismatches}
+
+
+def cpu_baseline(workload, tokens, lengths, rows: int, expected: dict, budget: float) -> dict:
+    leg = oracle_leg(workload, tokens, lengths, rows, steps=10_000, warmup=2, budget=budget, expected=expected)
+    value = leg["row_steps"] / leg["wall_s"] if leg["wall_s"] else 0.0
     return {
-        "value": per_core * workers,
-        "unit": UNIT,
-        "cores": workers,
-        "kind": "port",
-        "sample": (f"{done} row-steps (oracle allowed set + masked logits + advance, V={workload.served.vocab_size}) "
-                   f"at sampled positions of {len(by_row)} engine streams; {workers} spawned workers, "
-                   f"value = per-core throughput x workers; wall {wall:.0f} s incl. oracle build"),
-        "parity_sample": {"row_steps": done, "mask_mismatches": mismatches},
+        "value": value, "unit": UNIT, "cores": leg["workers"], "kind": "port",
+        "sample": (f"{leg['row_steps']} row-steps of the same streams (oracle allowed set + masked logits + "
+                   f"advance, V={workload.served.vocab_size:,}) over {leg['steps']} steps on {leg['workers']} "
+                   f"spawned workers; value = row-steps / wall seconds ({leg['wall_s']:.1f} s)"),
+        "per_core_value": leg["row_steps"] / leg["busy_s"] if leg["busy_s"] else 0.0,
+        "parity_sample": {"row_steps": leg["checked"], "mask_mismatches": leg["mismatches"]},
     }
 
 
@@ -255,42 +375,46 @@ def engine_arm(args) -> None:
     options = dict(cfg.options)
     rows = cfg.rows
     pool = 2 * rows
-    gen_engine = Engine(workload.index, workload.served, workload.syntax, pool, device_blob=(blob, meta), **options)
+    vocab = workload.served.vocab_size
     lo, hi = cfg.lengths
     if args.max_len:
         lo, hi = min(lo, args.max_len), min(hi, args.max_len)
-    max_len = hi
-    rng = np.random.default_rng(args.seed + 100 + rank)
-    lengths = rng.integers(lo, hi + 1, size=pool).tolist()
-    record = set()
-    if rank == 0 and world == 1 and not args.no_cpu and not args.profile:
-        for row in range(min(48, pool)):
-            for s in sorted(set(rng.integers(0, lengths[row], size=4).tolist())):
-                record.add((row, int(s)))
+    # -- token streams: the committed fixture (rank r replays its own rotation of it) or,
+    # for a configuration without one, constrained decodes sampled on the GPU
     t0 = time.perf_counter()
-    tokens, counts, recorded = sample_streams(gen_engine, workload.served, workload.syntax, workload.world,
-                                              pool, max_len, seed=args.seed + rank, record=record)
-    torch.cuda.synchronize()
+    fixture = load_streams(args.config, workload)
+    if fixture is not None:
+        all_tokens, all_lengths, all_allowed = fixture
+        pick = [(rank * rows + j) % len(all_lengths) for j in range(pool)]
+        tokens_np, lengths, counts_h = all_tokens[pick], all_lengths[pick], all_allowed[pick]
+        streams_source = f"fixture {STREAM_FIXTURES[args.config].name}"
+    else:
+        gen_engine = Engine(workload.index, workload.served, workload.syntax, pool, device_blob=(blob, meta), **options)
+        rng = np.random.default_rng(args.seed + 100 + rank)
+        lengths = rng.integers(cfg.lengths[0], cfg.lengths[1] + 1, size=pool)
+        sampled, counts, _ = sample_streams(gen_engine, workload.served, workload.syntax, workload.world,
+                                            pool, cfg.lengths[1], seed=args.seed + rank)
+        tokens_np, counts_h = sampled.cpu().numpy(), counts.cpu().numpy()
+        del gen_engine
+        streams_source = "sampled on the GPU with the engine's masks (no fixture for this configuration)"
+    if args.max_len:
+        lengths = np.minimum(lengths, args.max_len)
+    lengths = np.maximum(lengths, 1)
     sample_s = time.perf_counter() - t0
-    del gen_engine
     # -- replay schedule -------------------------------------------------------------------
-    # W warm-up steps, then K timed steps.  A step is begin(restarted slots) + sync_apply
-    # (sync and apply_mask fused in one kernel); events bracket the whole step, and a
-    # second pair brackets the sync_apply kernel alone (the roofline's kernel).
-    # then (outside the profile mode) up to 128 more steps without the flush: the warm figure
+    # W warm-up steps, then K timed steps, then (outside the profile mode) up to 128 more
+    # steps without the flush: the warm figure.  Row r replays pool streams r, r + rows, ...
+    # back to back; a step is one sync_apply launch (sync + apply_mask fused, the step's
+    # admissions folded in), bracketed by CUDA events.
     warm_steps = 0 if args.profile else min(args.steps, 128)
     total_steps = args.warmup + args.steps + warm_steps
-    assigned, restarts = schedule(lengths, rows, total_steps)
-    history = torch.zeros((rows, total_steps + 1), dtype=torch.int32, device=device)
-    disallowed = np.zeros(total_steps, dtype=np.int64)  # sum over rows of disallowed columns
-    counts_h = counts.cpu().numpy()
-    vocab = workload.served.vocab_size
-    for slot, parts in enumerate(assigned):
-        for sid, at in parts:
-            n = min(lengths[sid], total_steps - at)
-            history[slot, at: at + n] = tokens[sid, :n]
-            disallowed[at: at + n] += vocab - counts_h[sid, 1: n + 1]
-    restart_t = [torch.tensor(r, dtype=torch.int32, device=device) if r else None for r in restarts]
+    plan = row_plan(rows, lengths, total_steps)
+    sid, pos = plan[:, :, 0], plan[:, :, 1]
+    history = torch.from_numpy(np.ascontiguousarray(tokens_np[sid, pos], dtype=np.int32)).to(device)
+    disallowed = (vocab - counts_h[sid, pos + 1]).sum(axis=0).astype(np.int64)  # per step, over rows
+    restarts = [np.flatnonzero(pos[:, k] == 0).tolist() for k in range(total_steps)]
+    # a request joining a slot is an admission (begin, base KG) folded into that step's launch
+    restart_t = [admissions_tensor(r, device) if r else None for r in restarts]
     prompt = [torch.full((rows,), k, dtype=torch.int32, device=device) for k in range(total_steps)]
     total = [torch.full((rows,), k + 1, dtype=torch.int32, device=device) for k in range(total_steps)]
     slots = torch.arange(rows, dtype=torch.int32, device=device)
@@ -326,11 +450,8 @@ def engine_arm(args) -> None:
             flush.fill_(k)  # evict the logits and tables from L2 between steps
         e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
         e0.record()
-        if restart_t[k] is not None:
-            engine.begin(restart_t[k], stream=stream)
-            launches += timed
         e1.record()
-        engine.sync_apply(slots, history, prompt[k], total[k], logits, stream=stream)
+        engine.sync_apply(slots, history, prompt[k], total[k], logits, stream=stream, admissions=restart_t[k])
         e2.record()
         launches += timed
         if timed:
@@ -367,15 +488,10 @@ def engine_arm(args) -> None:
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": job_ms / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int32", "data": "synthetic",
-        "config": {
-            "workload": (f"{cfg.name} (config {args.config}): {cfg.entities:,} entities, {cfg.relations} relations, "
-                         f"{cfg.triples:,} triples, V={vocab:,}, {rows} rows/GPU, stream lengths U[{lo},{hi}] "
-                         f"replenished, paths+committed_paths, escapes on"),
-            "rows_per_gpu": rows, "vocab": vocab, "logits_dtype": cfg.dtype, "logits": f"{cfg.dtype} [rows, V] ~ N(0,2)",
-            "l2": "flushed between steps (512 MiB write, outside the timed region)",
-            "timed_region": "begin(restarted slots) + sync + apply_mask per step, CUDA events, max over ranks",
-            "parallelism": f"rows sharded, {world} replica(s), index broadcast once over NCCL",
-        },
+        "config": workload_config(cfg, args.config, rows, vocab, lo, hi, world),
+        "timed_region": "one sync_apply launch per step (admissions of joining requests, sync, apply_mask), "
+                        "CUDA events on the launching stream, max over ranks",
+        "streams": streams_source,
         "step_ms": {"median": statistics.median(steps_ms), "p90": sorted(steps_ms)[int(0.9 * len(steps_ms))],
                     "min": min(steps_ms), "max": max(steps_ms)},
         "warm": ({"ms_per_step": statistics.median(warms), "value": rows * 1e3 / statistics.median(warms),
@@ -383,10 +499,12 @@ def engine_arm(args) -> None:
                   "note": "the same replay continued without the L2 flush (median step, this rank)"}
                  if warms else None),
         "kernel_ms": {"median": statistics.median(applies), "mean": statistics.mean(applies),
-                      "note": "sync_apply kernel alone (events around it), over the K timed steps"},
+                      "note": "the step's one launch (events around it), over the K timed steps"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "peak_kind": peak_kind, **recorded_traffic(args.config, cfg.dtype),
-                     "kernel": f"sync_apply_kernel<{elt}> ({cfg.dtype}): sync + mask + apply fused",
+                     "peak_kind": peak_kind, **recorded_traffic(args.config, cfg.dtype, args.max_len),
+                     "level": ("L2: the -inf writes land in the 126 MB L2 during the launch and reach HBM "
+                               "when later writes evict them"),
+                     "kernel": f"step_apply_kernel<{elt}> ({cfg.dtype}): admissions + sync + mask + apply fused",
                      "algorithmic_bytes_per_launch": statistics.mean(bytes_per_launch)},
         "apply_mask_alone": apply_alone,
         "gpu_launches": launches,
@@ -409,10 +527,35 @@ def engine_arm(args) -> None:
         dist.destroy_process_group()
     if rank != 0:
         return
-    if world == 1 and not args.no_cpu and not args.profile and recorded:
-        streams = tokens.cpu().numpy().tolist()
-        result["cpu_baseline"] = cpu_baseline(workload, streams, recorded, args.cpu_seconds)
+    if world == 1 and not args.no_cpu and not args.profile:
+        expected = replay_masks(engine, tokens_np, lengths, rows, CPU_CHECK_STEPS)
+        result["cpu_baseline"] = cpu_baseline(workload, tokens_np, lengths, rows, expected, args.cpu_seconds)
     print(json.dumps(result), flush=True)
+
+
+CPU_CHECK_STEPS = 96  # the CPU leg's first steps, whose full row-steps are checked against the engine's masks
+
+
+def replay_masks(engine, tokens, lengths, rows: int, steps: int) -> dict:
+    """{(stream, position): mask words} for the first `steps` positions of streams 0..rows-1
+    (the streams the oracle leg's rows start with), from the engine replaying them with
+    advance + fill_mask (the mask before each position's token)."""
+    import torch
+
+    engine.reset()
+    device = torch.device("cuda", torch.cuda.current_device())
+    engine.begin(torch.arange(rows, dtype=torch.int32, device=device))
+    view = engine.mask_view()
+    out = {}
+    steps = min(steps, int(np.max(lengths[:rows])))
+    for at in range(steps):
+        engine.fill_mask(rows)
+        live = [r for r in range(rows) if at < lengths[r]]
+        words = view[:rows, : engine.words].cpu().numpy().view(np.uint32)
+        for r in live:
+            out[(r, at)] = words[r].copy()
+        engine.advance(np.ascontiguousarray(tokens[:rows, at], dtype=np.int32))
+    return out
 
 
 def apply_leg(engine, logits, slots, flush, stream, steps, elt):
@@ -484,9 +627,8 @@ def e2e_leg(engine, workload, history, restart_t, prompt, total, slots, rows, vo
             uploaded[k].record(up)
         compute.wait_event(uploaded[k])
         dev_hist[:, k] = staging[b]
-        if restart_t[k] is not None:
-            engine.begin(restart_t[k], stream=stream)
-        engine.sync_apply(slots, dev_hist, prompt[k], total[k], dev_logits[b], stream=stream)
+        engine.sync_apply(slots, dev_hist, prompt[k], total[k], dev_logits[b], stream=stream,
+                          admissions=restart_t[k])
         stepped[k].record(compute)
         with torch.cuda.stream(down):
             down.wait_event(stepped[k])
@@ -507,61 +649,93 @@ def e2e_leg(engine, workload, history, restart_t, prompt, total, slots, rows, vo
 # ---------------------------------------------------------------------------------------
 # reference arm: the oracle port on the host cores
 
-def recorded_traffic(config: int, dtype: str) -> dict:
-    """DRAM bytes per launch of the fused kernel from the committed ncu capture of the same
-    kernel on the same rows and vocabulary (profiles/sync_apply_paths100k.json), or None
-    for another workload.  The capture's logits writes stay in L2 during the kernel."""
-    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "profiles", "sync_apply_paths100k.json")
-    if config != 3 or dtype != "bfloat16":
+TRAFFIC_RECORD = ROOT / "profiles" / "step_apply_paths100k.json"
+
+
+def recorded_traffic(config: int, dtype: str, max_len: int) -> dict:
+    """DRAM bytes per launch of the fused step as ncu recorded them for this workload
+    (config 3, bf16, full stream lengths) with the command the record names; a record, not a
+    measurement of this run (ncu cannot count inside a timed run), and None for any other
+    workload."""
+    if config != 3 or dtype != "bfloat16" or max_len:
         return {"traffic": None}
     try:
-        with open(path) as f:
-            data = json.load(f)
+        data = json.loads(TRAFFIC_RECORD.read_text())
         return {"traffic": statistics.mean(data["dram_bytes_per_launch"]),
-                "traffic_source": f"ncu capture, {data['workload']}: dram__bytes_read.sum + dram__bytes_write.sum"}
+                "traffic_source": (f"recorded, not measured in this run: ncu dram__bytes_read.sum + "
+                                   f"dram__bytes_write.sum of {data['workload']} ({data['command']}, "
+                                   f"kernel source {data['kernel_source']})")}
     except (OSError, KeyError, ValueError):
         return {"traffic": None}
 
 
+REFERENCE_BUDGET_S = 150.0
+
+
 def reference_arm(args) -> None:
+    """The reference's CPU implementation of the path (its Oracle, restated in oracle/) on
+    the host cores, replaying the same committed streams as the engine arm: rows of the
+    workload split over spawned workers, each step one full row-step per worker (allowed set,
+    masked logits, advance) and advance alone for its other rows.  Loads nothing of the
+    engine (no CUDA library).  Under torchrun only rank 0 runs."""
     rank, world, _ = dist_env()
     if rank != 0:
         return
-    import torch
-
-    from xgraph_b200.engine import Engine
-    from xgraph_b200.synthetic import sample_streams
-
     workload = make_workload(args.config, args.seed)
     cfg = workload.config
-    rows = cfg.rows
-    rng = np.random.default_rng(args.seed + 100)
-    lengths = rng.integers(cfg.lengths[0], cfg.lengths[1] + 1, size=rows).tolist()
-    # streams are sampled as in the engine arm (the CPU only replays them)
-    engine = Engine(workload.index, workload.served, workload.syntax, rows, **cfg.options)
-    record = set()
-    for row in range(rows):
-        for s in sorted(set(rng.integers(0, lengths[row], size=2).tolist())):
-            record.add((row, int(s)))
-    tokens, _, recorded = sample_streams(engine, workload.served, workload.syntax, workload.world, rows,
-                                         cfg.lengths[1], seed=args.seed, record=record)
-    streams = tokens.cpu().numpy().tolist()
-    del engine
-    torch.cuda.empty_cache()
-    budget = max(20.0, min(150.0, 0.3 * (args.steps + args.warmup)))
-    base = cpu_baseline(workload, streams, recorded, budget)
-    value = base["value"]
+    fixture = load_streams(args.config, workload)
+    if fixture is None:
+        print(json.dumps({"impl": "reference", "unavailable": f"no committed token streams for config {args.config}"}))
+        return
+    tokens, lengths, _ = fixture
+    rows, pool = cfg.rows, 2 * cfg.rows
+    lo, hi = cfg.lengths
+    if args.max_len:
+        lo, hi = min(lo, args.max_len), min(hi, args.max_len)
+        lengths = np.minimum(lengths, args.max_len)
+    # every timed step takes about one V-wide allowed set per worker (about a second): the
+    # timed steps stop after REFERENCE_BUDGET_S so that a long --steps still ends in minutes
+    leg = oracle_leg(workload, tokens[:pool], lengths[:pool], rows, steps=args.steps, warmup=args.warmup,
+                     budget=REFERENCE_BUDGET_S)
+    value = leg["row_steps"] / leg["wall_s"] if leg["wall_s"] else 0.0
     result = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
-        "steps": base["parity_sample"]["row_steps"], "warmup": 0,
-        "ms_per_step": 1e3 * rows / value if value else None, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "int32", "data": "synthetic",
-        "config": {"workload": f"{cfg.name} (config {args.config}), {rows} rows, V={workload.served.vocab_size:,}",
-                   "note": "CPU oracle port on the host cores; each step a bounded sample of row-steps"},
-        "cpu_baseline": base,
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": leg["steps"],
+        "warmup": args.warmup, "ms_per_step": 1e3 * leg["wall_s"] / max(leg["steps"], 1), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int32", "data": "synthetic",
+        "config": workload_config(cfg, args.config, rows, workload.served.vocab_size, lo, hi, world),
+        "cpu_baseline": {
+            "value": value, "unit": UNIT, "cores": leg["workers"], "kind": "port",
+            "sample": (f"each step {leg['workers']} full row-steps (oracle allowed set + masked logits + advance, "
+                       f"V={workload.served.vocab_size:,}), one per worker, while every row of the batch advances; "
+                       f"value = full row-steps / wall seconds over the {leg['steps']} timed steps"),
+            "per_core_value": leg["row_steps"] / leg["busy_s"] if leg["busy_s"] else 0.0,
+        },
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "setup_s": {"oracle_workers": leg["setup_s"]},
+        "streams": f"fixture {STREAM_FIXTURES[args.config].name}",
+        "engine_library_loaded": engine_library_loaded(),
     }
     print(json.dumps(result), flush=True)
+
+
+def engine_library_loaded() -> bool:
+    """Whether this process mapped the engine's CUDA library (the reference arm must not)."""
+    try:
+        return "libxgraph_b200" in Path("/proc/self/maps").read_text()
+    except OSError:
+        return False
+
+
+def workload_config(cfg, number: int, rows: int, vocab: int, lo: int, hi: int, world: int) -> dict:
+    """The `config` object of both arms' lines (the workload, not how an arm runs it)."""
+    return {
+        "workload": (f"{cfg.name} (config {number}): {cfg.entities:,} entities, {cfg.relations} relations, "
+                     f"{cfg.triples:,} triples, V={vocab:,}, {rows} rows/GPU, stream lengths U[{lo},{hi}] "
+                     f"replenished, paths+committed_paths, escapes on"),
+        "rows_per_gpu": rows, "vocab": vocab, "logits_dtype": cfg.dtype, "logits": f"{cfg.dtype} [rows, V] ~ N(0,2)",
+        "l2": "GPU arm: flushed between steps (512 MiB write, outside the timed region)",
+        "parallelism": f"rows sharded, {world} replica(s), index broadcast once over NCCL",
+    }
 
 
 def main() -> None:

@@ -118,6 +118,21 @@ typedef struct XgInfo {
   int32_t max_sequences, vocab, words, words_padded, memory_ints, device;
 } XgInfo;
 
+/* One request's admission into a slot, applied in the reference adapter's order
+ * (src/xgraph/vllm.py:569-605 apply_staged_writes): begin (on = 1) or end (on = 0), then the
+ * anchor rows (derivation / path mode: sorted, distinct label rows; the first 64 count),
+ * then the KG version (0 = base), then open_span.  Field meanings are those of
+ * Engine::begin, set_reached, set_version and open_span (csrc/engine.cu:2818-2876, 2955). */
+#define XG_MAX_ANCHORS 64
+typedef struct XgAdmission {
+  int32_t slot;
+  int32_t on;
+  int32_t version;
+  int32_t open_span;
+  int32_t anchor_count;
+  int32_t anchors[XG_MAX_ANCHORS];
+} XgAdmission;
+
 typedef struct XgEngine XgEngine;
 
 /* Message of this thread's last failed call ("" if none). */
@@ -181,6 +196,28 @@ XG_API int xg_sync_apply(XgEngine* engine, const int32_t* slots, int32_t count, 
                          int64_t history_stride, int64_t history_rows, const int32_t* prompt_len,
                          const int32_t* total_len, int64_t lengths_count, void* logits, int32_t dtype,
                          int32_t cols, int64_t row_stride, void* stream);
+/* xg_sync_apply with the step's admissions folded into the same launch: admissions[0 ..
+ * admit_count) (distinct slots; host memory when admissions_on_host != 0, else device
+ * memory) are applied first, exactly as xg_admit would, then every listed slot syncs and
+ * its logits row is masked.  One launch per decoding step whether or not requests join.
+ * The reference's adapter reaches the same state with begin / set_reached / set_version /
+ * open_span calls before sync (src/xgraph/vllm.py:569-631).  Host admissions are copied
+ * into an engine buffer on `stream` (calls on one engine must be ordered on one stream);
+ * device admissions with a field out of range are skipped and counted by xg_faults. */
+XG_API int xg_sync_apply_admit(XgEngine* engine, const int32_t* slots, int32_t count, const int32_t* history,
+                               int64_t history_stride, int64_t history_rows, const int32_t* prompt_len,
+                               const int32_t* total_len, int64_t lengths_count, void* logits, int32_t dtype,
+                               int32_t cols, int64_t row_stride, const XgAdmission* admissions,
+                               int32_t admit_count, int32_t admissions_on_host, void* stream);
+/* One launch for a batch of admissions (the reference's apply_staged_writes loop of begin,
+ * set_reached, set_version and open_span calls, one launch per slot and op each): applies
+ * admissions[0 .. count) (distinct slots; host memory when on_host != 0) and rebuilds
+ * each admitted slot's mask. */
+XG_API int xg_admit(XgEngine* engine, const XgAdmission* admissions, int32_t count, int32_t on_host, void* stream);
+/* Device-side faults recorded since the last call, then cleared (waits for the device):
+ * bit 0 a grid barrier of the fused step gave up waiting (bounded wait), bit 1 a device
+ * admission with a field out of range was skipped.  0 in normal operation. */
+XG_API int xg_faults(XgEngine* engine, int32_t* out);
 /* Engine::apply_mask (csrc/engine.cu:2990-3037): in place, logits[r, c] = -inf for every
  * column c its slot's mask disallows and every c >= vocab; rows of inactive slots and of
  * slots in the error phase are left untouched.  logits: device, dtype XG_F32/XG_BF16/XG_F16,

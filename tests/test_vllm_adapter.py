@@ -51,15 +51,15 @@ def test_unserved_settings_are_refused():
             adapter.check_served_settings({name: value})
 
 
-def test_replayed_tokens():
+def test_tail_cover():
     table = {1: b"ab", 2: b"c", 3: b" \xe2\x9f\xa6", 4: None}
     tb = table.get
-    assert adapter.replayed_tokens([1, 2], tb, b"c") == 1
-    assert adapter.replayed_tokens([1, 2], tb, b"bc") == 2  # the first token is replayed whole
-    assert adapter.replayed_tokens([1, 2], tb, b"abc") == 2
-    assert adapter.replayed_tokens([1, 2], tb, b"xc") is None
-    assert adapter.replayed_tokens([4, 2], tb, b"bc") is None
-    assert adapter.replayed_tokens([2], tb, b"abc") is None
+    assert adapter.tail_cover([1, 2], tb, b"c") == 1
+    assert adapter.tail_cover([1, 2], tb, b"bc") == 2  # the first token is replayed whole
+    assert adapter.tail_cover([1, 2], tb, b"abc") == 2
+    assert adapter.tail_cover([1, 2], tb, b"xc") is None
+    assert adapter.tail_cover([4, 2], tb, b"bc") is None
+    assert adapter.tail_cover([2], tb, b"abc") is None
 
 
 def test_replay_statuses():
@@ -95,26 +95,42 @@ def test_version_file_round_trip(tmp_path):
         np.testing.assert_array_equal(getattr(loaded, field), getattr(built, field))
 
 
-def test_admissions_are_applied_in_order():
-    calls = []
+def test_admissions_become_one_record_per_slot():
+    """The step's admissions: one record per slot (the latest request; a slot also ended in
+    the round ends), applied in the next step's launch, or by one admit launch when a second
+    round comes first."""
+    from xgraph_b200.engine import Admission
+
+    admitted = []
 
     class FakeEngine:
-        def __getattr__(self, name):
-            return lambda *args: calls.append((name, *[a.tolist() if hasattr(a, "tolist") else a for a in args[:-1]]))
+        def admission_records(self, admissions):
+            return list(admissions)
 
-    import torch
+        def admit(self, records, stream):
+            admitted.append(records)
 
     proc = object.__new__(adapter.XGraphLogitsProcessor)
-    proc._engine, proc._torch = FakeEngine(), torch
-    proc._req_states = SimpleNamespace(device="cpu")
-    proc._pending, proc._replaying, proc._admission_order = {}, {}, 0
-    proc._stream = lambda: 0
+    proc._engine, proc._stream = FakeEngine(), lambda: 0
+    proc._staged, proc._folded, proc._prefills = {}, None, {}
     assert proc.add_request(3, params(xgraph=1, xgraph_anchor=["Q1"], xgraph_kg_version="v1"))
     assert not proc.add_request(1, params())
     assert proc.add_request(0, params(xgraph=1, xgraph_open=1))
+    assert proc.add_request(2, params(xgraph=1, xgraph_prefill="\u27e6 Ada"))
     proc.apply_staged_writes()
-    assert calls == [("begin", [3, 0]), ("end", [1]), ("anchor", 3, ["Q1"]), ("set_version", 3, "v1"), ("open_span", 0)]
-    assert not proc._pending
+    assert proc._folded == [Admission(0, True, (), None, True), Admission(1, False),
+                            Admission(2, True), Admission(3, True, ("Q1",), "v1", False)]
+    assert list(proc._prefills) == [2] and not proc._staged and not admitted
+    assert not proc.add_request(2, params())  # slot 2's next request opts out: no replay
+    assert proc.add_request(1, params(xgraph=1))
+    proc.apply_staged_writes()
+    assert admitted == [[Admission(0, True, (), None, True), Admission(1, False), Admission(2, True),
+                         Admission(3, True, ("Q1",), "v1", False)]]
+    assert proc._folded == [Admission(1, True), Admission(2, False)] and not proc._prefills
+    proc.add_request(4, params(xgraph=1))
+    proc.add_request(4, params())  # admitted and ended in one round: it ends
+    proc.add_request(4, params(xgraph=1))
+    assert proc._staged[4].ended
 
 
 # -- GPU ---------------------------------------------------------------------------------
@@ -291,7 +307,7 @@ def test_replayed_prefill_continues_from_the_replayed_state(tmp_path, monkeypatc
     plain = Engine(world_index(case["world"], False), served, proc.engine_syntax, 1, **options)
     want = []
     for k in range(n - 2):
-        count = adapter.replayed_tokens(encoded[k], served.token_bytes, prefills[k].encode("utf-8"))
+        count = adapter.tail_cover(encoded[k], served.token_bytes, prefills[k].encode("utf-8"))
         plain.reset()
         plain.begin(torch.zeros(1, dtype=torch.int32, device="cuda"))
         for token in encoded[k][len(encoded[k]) - count:]:

@@ -10,6 +10,7 @@ from importlib import import_module
 _EXPORTS = {
     "Engine": "engine",
     "EngineUnavailable": "engine",
+    "Admission": "engine",
     "closed_span": "engine",
     "Entity": "kg",
     "Relation": "kg",

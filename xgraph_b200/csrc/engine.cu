@@ -223,21 +223,54 @@ __device__ __forceinline__ void store_neg8(char* at, uint32_t blocked, uint32_t 
   }
 }
 
+#ifndef XG_BULK_STORES
+#define XG_BULK_STORES 1
+#endif
+
+// A run of -inf elements in shared memory (4 KB: one segment of fp32, two of bf16), the
+// source of the bulk stores below.  Filled once per CTA; the proxy fence makes the generic
+// writes visible to the asynchronous (TMA) proxy after the next CTA barrier.
+constexpr int32_t kBlockedRunWords = 1024;
+
+template <int ELT>
+__device__ __forceinline__ void fill_blocked_run(uint32_t* run, uint32_t neg, int32_t first = 0) {
+  const uint32_t v = ELT == 2 ? (neg | (neg << 16)) : neg;
+  for (int32_t k = static_cast<int32_t>(threadIdx.x) - first; k < kBlockedRunWords; k += blockDim.x - first) run[k] = v;
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// One bulk (TMA) copy of `bytes` (a multiple of 16) from shared to global memory, both
+// 16-byte aligned; completed by bulk_drain.
+__device__ __forceinline__ void bulk_store(void* to, const void* from, uint32_t bytes) {
+  const uint32_t source = static_cast<uint32_t>(__cvta_generic_to_shared(from));
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(to), "r"(source), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void bulk_drain() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
 // -inf into the disallowed columns of segments [s0, s1) (1024 columns each) of one
 // logits row whose first element is 16-byte aligned; the calling warps split them.
 //
 // Each lane loads one mask word (32 columns; base | delta), then for store j = 0..3 lane l
 // takes the 8-column group g = 32 j + l, fetching its byte of mask from the lane that
 // loaded word g / 4 by shuffle, so each store instruction of the warp writes 512
-// contiguous bytes (bf16) while the mask costs one load per 32 columns.  A warp issues
-// the loads of kApplyBatch segments before any of their stores (the stores may alias
-// nothing the compiler can prove, so it would not hoist the loads itself).
+// contiguous bytes (bf16) while the mask costs one load per 32 columns.  A segment with no
+// allowed column (most of a row inside a span) is written instead by one bulk copy of the
+// shared -inf run `blocked` (when given), issued by lane 0: one instruction for the
+// segment, leaving the SM's load/store pipe to the partial segments.  A warp issues the
+// loads of kApplyBatch segments before any of their stores (the stores may alias nothing
+// the compiler can prove, so it would not hoist the loads itself).
 template <int ELT>
 __device__ __forceinline__ void apply_segments(const Tables& t, char* out, int32_t cols, const uint32_t* base,
                                                const uint32_t* delta, uint32_t neg, int32_t s0, int32_t s1,
-                                               int32_t warp, int32_t warps) {
+                                               int32_t warp, int32_t warps, const uint32_t* blocked) {
   const int32_t lane = threadIdx.x & 31;
   const int32_t words = t.words;
+  bool issued = false;
   for (int32_t first = s0 + warp; first < s1; first += warps * kApplyBatch) {
     uint32_t word[kApplyBatch];
 #pragma unroll
@@ -250,19 +283,29 @@ __device__ __forceinline__ void apply_segments(const Tables& t, char* out, int32
     for (int32_t b = 0; b < kApplyBatch; ++b) {
       const int32_t seg = first + b * warps;  // warp-uniform
       if (seg >= s1) break;
+#if XG_BULK_STORES
+      if (blocked && (seg + 1) * 1024 <= cols && __ballot_sync(0xffffffffu, word[b] != 0u) == 0u) {
+        if (lane == 0) {
+          bulk_store(out + static_cast<int64_t>(seg) * 1024 * ELT, blocked, 1024 * ELT);
+          issued = true;
+        }
+        continue;
+      }
+#endif
 #pragma unroll
       for (int32_t j = 0; j < 4; ++j) {
         const int32_t g = 32 * j + lane;
         const uint32_t holder = __shfl_sync(0xffffffffu, word[b], g >> 2);
         const int32_t c = seg * 1024 + 8 * g;
         if (c >= cols) continue;
-        uint32_t blocked = ~(holder >> (8 * (g & 3))) & 0xffu;
+        uint32_t blocked_bits = ~(holder >> (8 * (g & 3))) & 0xffu;
         const int32_t left = cols - c;
-        if (left < 8) blocked &= (1u << left) - 1u;
-        if (blocked) store_neg8(out + static_cast<int64_t>(c) * ELT, blocked, neg, ELT);
+        if (left < 8) blocked_bits &= (1u << left) - 1u;
+        if (blocked_bits) store_neg8(out + static_cast<int64_t>(c) * ELT, blocked_bits, neg, ELT);
       }
     }
   }
+  if (issued) bulk_drain();
 }
 
 // Columns [c0, c1) of a row whose start is not 16-byte aligned, one element per thread.
@@ -306,83 +349,188 @@ __global__ void __launch_bounds__(kApplyThreads, 4)
   const int32_t share = (segments + chunks - 1) / chunks;
   const int32_t s0 = chunk * share;
   apply_segments<ELT>(t, out, cols, base, delta, neg, s0, s0 + share < segments ? s0 + share : segments,
-                      threadIdx.x >> 5, blockDim.x >> 5);
+                      threadIdx.x >> 5, blockDim.x >> 5, nullptr);
 }
 
-// sync + apply_mask fused for the step where logits row i belongs to slots[i] (no draft
-// rows): warp 0 of CTA i consumes the slot's new history tokens and rebuilds its mask, then
-// all warps of the CTA write the row's -inf.  One launch per decoding step; a row's stores
-// overlap other rows' state-machine latency.
+// ---------------------------------------------------------------------------------------
+// Admission of one request into a slot (a warp; lane 0 writes the slot's buffers): begin or
+// end, then anchors, then the KG version, then open_span, in the reference adapter's order
+// (src/xgraph/vllm.py:569-605; begin = csrc/engine.cu:2027-2053, the rest 2840-2876, 2955).
+// Returns false, touching nothing, when a field is out of range (counted in *faults, bit 1).
+__device__ bool admit_slot(const Ctx& c, XgState& s, const XgAdmission& a, int32_t* faults) {
+  const Tables& t = c.t;
+  const int32_t lane = c.w.lane;
+  const int32_t on = a.on, version = a.version, anchors = a.anchor_count;
+  bool bad = version < 0 || version > t.versions || anchors < 0 || anchors > kMaxSet;
+  if (!bad && on) {
+    const int32_t k0 = lane, k1 = lane + 32;
+    const int32_t r0 = k0 < anchors ? a.anchors[k0] : 0, p0 = k0 > 0 && k0 < anchors ? a.anchors[k0 - 1] : -1;
+    const int32_t r1 = k1 < anchors ? a.anchors[k1] : 0, p1 = k1 < anchors ? a.anchors[k1 - 1] : -1;
+    const bool wrong = (k0 < anchors && (r0 < 0 || r0 >= t.ent.count || r0 <= p0)) ||
+                       (k1 < anchors && (r1 < 0 || r1 >= t.ent.count || r1 <= p1));
+    bad = __any_sync(0xffffffffu, wrong);
+  }
+  if (bad) {
+    if (c.w.leader()) atomicOr(faults, 2);
+    return false;
+  }
+  int32_t* words = reinterpret_cast<int32_t*>(&s);
+#pragma unroll
+  for (int32_t k = 0; k < XG_STATE_INTS; ++k) words[k] = 0;
+  if (on) {
+    if (lane < anchors) c.mem[kMemReachedRows + lane] = a.anchors[lane];
+    if (lane + 32 < anchors) c.mem[kMemReachedRows + lane + 32] = a.anchors[lane + 32];
+  }
+  if (c.w.leader()) {
+    c.mem[kMemFacts] = c.mem[kMemFrontier] = 0;
+    c.mem[kMemReached] = on ? anchors : 0;
+    c.mem[kMemVersion] = on ? version : 0;
+    c.mem[kMemPendingLo] = -1;
+    t.cursors[c.slot] = -1;
+    t.active[c.slot] = on ? 1 : 0;
+    t.base[c.slot] = t.free_mask;
+    t.delta[c.slot] = nullptr;
+  }
+  __syncwarp();
+  if (on && a.open_span) open_span(c, s);  // reads the anchors and version just written
+  return true;
+}
+
+// admit: one warp per admission; the slot's state and mask are rebuilt.
+__global__ void __launch_bounds__(32)
+    admit_kernel(const __grid_constant__ Tables t, const XgAdmission* admit, int32_t max_slots, int32_t* faults) {
+  __shared__ WarpShared shared;
+  const XgAdmission& a = admit[blockIdx.x];
+  const int32_t slot = a.slot;
+  if (slot < 0 || slot >= max_slots) {
+    if (threadIdx.x == 0) atomicOr(faults, 2);
+    return;
+  }
+  Ctx c = make_ctx(t, slot, shared);
+  XgState s;
+  if (!admit_slot(c, s, a, faults)) return;
+  store_state(t, slot, s);
+  if (a.on) build_mask(c, s);
+}
+
+// ---------------------------------------------------------------------------------------
+// The fused decoding step: sync + apply_mask for the step where logits row i belongs to
+// slots[i] (no draft rows), with the step's admissions applied first.  Warp 0 of CTA i
+// applies row i's admission (if any), consumes the slot's new history tokens and rebuilds
+// its mask; then all warps of the CTA write the row's -inf.  One launch per decoding step;
+// a row's stores overlap other rows' state-machine latency.  An admission whose slot is
+// not a row of the step is applied by CTA (its index mod the grid) after its own row.
+
+struct FusedArgs {
+  StepArgs a;
+  const XgAdmission* admit;  // this step's admissions (distinct slots) or null
+  int32_t admit_count;
+  int32_t max_slots;
+  char* logits;
+  int64_t stride;
+  int32_t cols;
+  uint32_t neg;
+  int32_t* faults;
+};
+
 template <int ELT>
 __global__ void __maxnreg__(kFusedRegisters)
-    sync_apply_kernel(const __grid_constant__ Tables t, const StepArgs a, char* logits, int32_t cols,
-                      int64_t stride, uint32_t neg) {
+    sync_apply_kernel(const __grid_constant__ Tables t, const __grid_constant__ FusedArgs f) {
   __shared__ WarpShared shared;
   __shared__ MaskRef use;                               // the mask this CTA applies
   __shared__ int32_t delim0[kDelimCopy];                // tokens that start each delimiter
+  __shared__ __align__(128) uint32_t blocked_run[kBlockedRunWords];
   extern __shared__ __align__(16) uint32_t composed[];  // [words_padded]: a delta built this step
   const int32_t i = blockIdx.x;
-  const int32_t slot = a.slots[i];
-  // Issue warp 0's loads of the slot's cursor, lengths and state together with the active
-  // flag rather than after the branch on it: one memory round trip instead of two.
-  const int32_t on = t.active[slot];
-  int32_t cursor = 0, end = 0;
+  const int32_t slot = f.a.slots[i];
+  const bool valid = slot >= 0 && slot < f.max_slots;
+  // Warp 0's loads of the slot's cursor, lengths and state are issued together with the
+  // active flag (and the admission search) rather than after the branch on it.
+  const int32_t was_on = valid ? t.active[slot] : 0;
+  if (!was_on && f.admit_count == 0) return;  // block-uniform: inactive rows are neither advanced nor masked
+  int32_t found = -1, cursor = 0, end = 0, prompt = 0;
   XgState s;
-  if (threadIdx.x < 32) {
+  if (threadIdx.x < 32 && valid) {
+    // the first 32 admissions' slots load with the state (one round trip for both)
+    const int32_t lane = threadIdx.x;
+    const int32_t listed = lane < f.admit_count ? f.admit[lane].slot : -1;
     const int32_t stored = t.cursors[slot];
-    const int32_t prompt = a.prompt_len[slot];
-    end = a.total_len[slot];
+    prompt = f.a.prompt_len[slot];
+    end = f.a.total_len[slot];
     s = load_state(t, slot);
     cursor = stored < 0 ? prompt : stored;
+    uint32_t ballot = __ballot_sync(0xffffffffu, listed == slot);
+    int32_t at = 0;
+#pragma unroll 1
+    while (ballot == 0u && at + 32 < f.admit_count) {
+      at += 32;
+      ballot = __ballot_sync(0xffffffffu, at + lane < f.admit_count && f.admit[at + lane].slot == slot);
+    }
+    if (ballot) found = at + __ffs(ballot) - 1;
   }
-  if (!on) return;  // block-uniform: inactive rows are neither advanced nor masked
-  uint32_t* const own = t.masks + static_cast<int64_t>(slot) * t.words_padded;  // the slot's delta row
-  // Warps 1..7, idle while warp 0 runs the state machine, clear the shared delta row and
-  // copy the delimiters' start tokens, then arrive at barrier 1, which warp 0 waits at
-  // before it composes the mask.
+  uint32_t* const own = t.masks + static_cast<int64_t>(valid ? slot : 0) * t.words_padded;  // the slot's delta row
+  // Warps 1..7, idle while warp 0 runs the state machine, clear the shared delta row, fill
+  // the -inf run and copy the delimiters' start tokens, then arrive at barrier 1, which
+  // warp 0 waits at before it composes the mask.
   const int32_t c0 = t.closer.at[1] - t.closer.at[0], c1 = t.separator.at[1] - t.separator.at[0];
   const int32_t c2 = t.escape.at[1] - t.escape.at[0];
   const bool copied = c0 + c1 + c2 <= kDelimCopy;
   if (threadIdx.x >= 32) {
     uint4* to = reinterpret_cast<uint4*>(composed);
     for (int32_t k = threadIdx.x - 32; k < (t.words_padded >> 2); k += blockDim.x - 32) to[k] = make_uint4(0u, 0u, 0u, 0u);
+    fill_blocked_run<ELT>(blocked_run, f.neg, 32);
     if (copied) {
       for (int32_t k = threadIdx.x - 32; k < c0 + c1 + c2; k += blockDim.x - 32)
         delim0[k] = k < c0 ? t.closer.tok[t.closer.at[0] + k]
                            : k < c0 + c1 ? t.separator.tok[t.separator.at[0] + k - c0]
                                          : t.escape.tok[t.escape.at[0] + k - c0 - c1];
     }
+    __syncwarp();
     asm volatile("bar.arrive 1, %0;" ::"r"(blockDim.x) : "memory");
     // A relation label of a path (base KG): the next frontier reads each frontier entity's
     // relation runs and its edges' folded first rows, two dependent round trips deep in
     // warp 0's transition.  Start those lines into L1 now, one thread per entity (the
     // slot's stored state and frontier are read here; the lines are only hints, and every
     // address is checked to lie in its table).
-    const XgState* stored = t.states + slot;
-    const int32_t* mem = t.memory + static_cast<int64_t>(slot) * t.memory_ints;
-    if (t.paths && stored->phase == kSpan && stored->segment == kRelation && mem[kMemVersion] == 0) {
-      const int32_t count = mem[kMemFrontier] < kMaxSet ? mem[kMemFrontier] : kMaxSet;
-      for (int32_t k = threadIdx.x - 32; k < count; k += blockDim.x - 32) {
-        const int32_t e = mem[kMemFrontierEnt + k];
-        if (e < 0 || e >= t.entities) continue;
-        const int32_t r0 = t.run_off[e], r1 = t.run_off[e + 1], e0 = t.adj_off[e], e1 = t.adj_off[e + 1];
-        for (int32_t x = 2 * r0; x <= 2 * r1 + 1 && x < 2 * r0 + 4 * 32; x += 32) prefetch_l1(t.runs + x);
-        for (int32_t x = e0; x < e1 && x < e0 + 8 * 32; x += 32) prefetch_l1(t.edge_first + x);
+    if (was_on) {
+      const XgState* stored = t.states + slot;
+      const int32_t* mem = t.memory + static_cast<int64_t>(slot) * t.memory_ints;
+      if (t.paths && stored->phase == kSpan && stored->segment == kRelation && mem[kMemVersion] == 0) {
+        const int32_t count = mem[kMemFrontier] < kMaxSet ? mem[kMemFrontier] : kMaxSet;
+        for (int32_t k = threadIdx.x - 32; k < count; k += blockDim.x - 32) {
+          const int32_t e = mem[kMemFrontierEnt + k];
+          if (e < 0 || e >= t.entities) continue;
+          const int32_t r0 = t.run_off[e], r1 = t.run_off[e + 1], e0 = t.adj_off[e], e1 = t.adj_off[e + 1];
+          for (int32_t x = 2 * r0; x <= 2 * r1 + 1 && x < 2 * r0 + 4 * 32; x += 32) prefetch_l1(t.runs + x);
+          for (int32_t x = e0; x < e1 && x < e0 + 8 * 32; x += 32) prefetch_l1(t.edge_first + x);
+        }
       }
     }
-  }
-  if (threadIdx.x < 32) {
-    Ctx c = make_ctx(t, slot, shared);
+  } else {
+    Ctx c = make_ctx(t, valid ? slot : 0, shared);
     if (copied) c.delim0 = delim0;
-    if (cursor < end) {
-      const int32_t* tokens = a.history + a.stride * slot;
+    bool changed = false;
+    int32_t on = was_on;
+    if (found >= 0 && admit_slot(c, s, f.admit[found], f.faults)) {
+      changed = true;
+      on = f.admit[found].on;
+      cursor = prompt;
+    }
+    if (on && cursor < end) {
+      const int32_t* tokens = f.a.history + f.a.stride * slot;
       for (; cursor < end; ++cursor) {
         const int32_t token = tokens[cursor];  // in flight while the state's reads are started
         if (s.phase == kSpan) prefetch_span(c, s);
         advance_state(c, s, token);
       }
-      store_state(t, slot, s);
-      asm volatile("bar.sync 1, %0;" ::"r"(blockDim.x) : "memory");
+      changed = true;
+    }
+    if (changed) store_state(t, slot, s);
+    __syncwarp();
+    asm volatile("bar.sync 1, %0;" ::"r"(blockDim.x) : "memory");
+    if (!on) {
+      if (threadIdx.x == 0) use = MaskRef{nullptr, nullptr};  // inactive: untouched
+    } else if (changed) {
       // the delta is composed in shared memory (setting bits there is much cheaper than in
       // global memory); the CTA copies it to the slot's row below
       const MaskRef m = compose_mask(c, s, composed, true);
@@ -392,10 +540,9 @@ __global__ void __maxnreg__(kFusedRegisters)
         use = m;
       }
     } else {  // no new token: the slot's recorded mask
-      asm volatile("bar.sync 1, %0;" ::"r"(blockDim.x) : "memory");
       if (threadIdx.x == 0) use = MaskRef{t.base[slot], t.delta[slot]};
     }
-    if (threadIdx.x == 0) t.cursors[slot] = cursor;
+    if (threadIdx.x == 0 && on) t.cursors[slot] = cursor;
   }
   __syncthreads();
   const uint32_t* base = use.base;
@@ -415,15 +562,34 @@ __global__ void __maxnreg__(kFusedRegisters)
     uint4* to = reinterpret_cast<uint4*>(own);
     for (int32_t k = threadIdx.x; k < (t.words_padded >> 2); k += blockDim.x) to[k] = from[k];
   }
-  if (base == nullptr && delta == nullptr) return;  // error phase: untouched
-  char* out = logits + static_cast<int64_t>(i) * stride * ELT;
-  if ((reinterpret_cast<uintptr_t>(out) & 15u) != 0) {
-    apply_scalar<ELT>(t, out, 0, cols, base, delta, neg);
-    return;
+  if (base != nullptr || delta != nullptr) {  // else inactive or error phase: untouched
+    char* out = f.logits + static_cast<int64_t>(i) * f.stride * ELT;
+    if ((reinterpret_cast<uintptr_t>(out) & 15u) != 0)
+      apply_scalar<ELT>(t, out, 0, f.cols, base, delta, f.neg);
+    else
+      apply_segments<ELT>(t, out, f.cols, base, delta, f.neg, 0, (f.cols + 1023) >> 10, threadIdx.x >> 5,
+                          blockDim.x >> 5, blocked_run);
   }
-  apply_segments<ELT>(t, out, cols, base, delta, neg, 0, (cols + 1023) >> 10, threadIdx.x >> 5, blockDim.x >> 5);
+  // admissions whose slot is not a row of this step (CTA i takes i, i + grid, ...)
+  if (threadIdx.x < 32) {
+#pragma unroll 1
+    for (int32_t j = i; j < f.admit_count; j += gridDim.x) {
+      const int32_t other = f.admit[j].slot;
+      const bool row = warp_any(Warp{static_cast<int32_t>(threadIdx.x)}, 0, f.a.count,
+                                [&](int32_t r) { return f.a.slots[r] == other; });
+      if (row) continue;
+      if (other < 0 || other >= f.max_slots) {
+        if (threadIdx.x == 0) atomicOr(f.faults, 2);
+        continue;
+      }
+      Ctx c = make_ctx(t, other, shared);
+      XgState x;
+      if (!admit_slot(c, x, f.admit[j], f.faults)) continue;
+      store_state(t, other, x);
+      if (f.admit[j].on) build_mask(c, x);
+    }
+  }
 }
-
 
 // Speculative draft rows (apply_mask with local_pos and input_ids): a request owns
 // consecutive logits rows, one per draft position; row r at offset k = local_pos[r] is
@@ -483,7 +649,8 @@ __global__ void __launch_bounds__(kFusedThreads)
     apply_scalar<ELT>(t, out, 0, cols, m.base, m.delta, neg);
     return;
   }
-  apply_segments<ELT>(t, out, cols, m.base, m.delta, neg, 0, (cols + 1023) >> 10, threadIdx.x >> 5, blockDim.x >> 5);
+  apply_segments<ELT>(t, out, cols, m.base, m.delta, neg, 0, (cols + 1023) >> 10, threadIdx.x >> 5, blockDim.x >> 5,
+                      nullptr);
 }
 
 }  // namespace xg
@@ -514,8 +681,10 @@ struct XgEngine {
   int32_t* active = nullptr;
   int32_t* tokens = nullptr;
   char* draft_scratch = nullptr;  // apply_mask's draft rows: [rows] memory rows, then [rows] mask rows
-  size_t composed_bytes = 0;      // sync_apply's dynamic shared memory: one mask row
   int32_t draft_capacity = 0;     // rows it holds
+  int32_t* faults = nullptr;      // device-side faults (xg_faults)
+  XgAdmission* admissions = nullptr;  // staging of host admissions: max_sequences entries
+  size_t composed_bytes = 0;      // sync_apply's dynamic shared memory: one mask row
   Tables t{};
 };
 
@@ -673,6 +842,8 @@ void release(XgEngine* e) {
   cudaFree(e->active);
   cudaFree(e->tokens);
   cudaFree(e->draft_scratch);
+  cudaFree(e->faults);
+  cudaFree(e->admissions);
   delete e;
 }
 
@@ -705,6 +876,8 @@ int create(const void* blob, bool on_device, const XgLayout* layout, const XgOpt
   alloc(reinterpret_cast<void**>(&e->cursors), slots * sizeof(int32_t));
   alloc(reinterpret_cast<void**>(&e->active), slots * sizeof(int32_t));
   alloc(reinterpret_cast<void**>(&e->tokens), slots * sizeof(int32_t));
+  alloc(reinterpret_cast<void**>(&e->faults), sizeof(int32_t));
+  alloc(reinterpret_cast<void**>(&e->admissions), slots * sizeof(XgAdmission));
   if (err != cudaSuccess) {
     release(e);
     cudaGetLastError();
@@ -714,6 +887,7 @@ int create(const void* blob, bool on_device, const XgLayout* layout, const XgOpt
                    on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice);
   if (err == cudaSuccess) err = cudaMemset(e->memory, 0, slots * memory_ints * sizeof(int32_t));
   if (err == cudaSuccess) err = cudaMemset(e->masks, 0, slots * layout->words_padded * sizeof(uint32_t));
+  if (err == cudaSuccess) err = cudaMemset(e->faults, 0, sizeof(int32_t));
   if (err != cudaSuccess) {
     release(e);
     return cuda_fail(err, "engine upload");
@@ -811,6 +985,48 @@ int launch_drafts(XgEngine* e, char* logits, int32_t dtype, int32_t rows, int32_
     draft_apply_kernel<2><<<rows, kFusedThreads, 0, s>>>(e->t, d, logits, cols, row_stride,
                                                           dtype == XG_BF16 ? 0xff80u : 0xfc00u);
   XG_CUDA(cudaGetLastError(), "draft apply kernel");
+  return XG_OK;
+}
+
+// Host admissions are checked, then copied into the engine's staging buffer on `stream`;
+// device admissions are used in place (the kernels skip and count entries out of range).
+int stage_admissions(XgEngine* e, const XgAdmission* admissions, int32_t count, int32_t on_host, void* stream,
+                     const XgAdmission** out) {
+  *out = nullptr;
+  if (count < 0 || count > e->max_sequences)
+    return fail(XG_EINVAL, "admissions must number between 0 and max_sequences (" + std::to_string(e->max_sequences) +
+                               "), got " + std::to_string(count));
+  if (count == 0) return XG_OK;
+  if (!admissions) return fail(XG_EINVAL, "null admissions");
+  if (!on_host) {
+    *out = admissions;
+    return XG_OK;
+  }
+  for (int32_t j = 0; j < count; ++j) {
+    const XgAdmission& a = admissions[j];
+    if (int rc = check_slot(e, a.slot)) return rc;
+    for (int32_t k = 0; k < j; ++k)
+      if (admissions[k].slot == a.slot) return fail(XG_EINVAL, "two admissions name slot " + std::to_string(a.slot));
+    if (a.on != 0 && a.on != 1) return fail(XG_EINVAL, "admission `on` must be 0 or 1");
+    if (a.version < 0 || a.version > e->layout.versions)
+      return fail(XG_EINVAL, "KG version must be between 0 and " + std::to_string(e->layout.versions) + ", got " +
+                                 std::to_string(a.version));
+    if (a.anchor_count < 0 || a.anchor_count > XG_MAX_ANCHORS)
+      return fail(XG_EINVAL, "an admission holds 0 to 64 anchor rows");
+    for (int32_t k = 0; k < a.anchor_count; ++k)
+      if (a.anchors[k] < 0 || a.anchors[k] >= e->layout.entity_rows || (k > 0 && a.anchors[k] <= a.anchors[k - 1]))
+        return fail(XG_EINVAL, "anchor rows must be sorted, distinct label rows of the index");
+  }
+  XG_CUDA(cudaMemcpyAsync(e->admissions, admissions, count * sizeof(XgAdmission), cudaMemcpyHostToDevice,
+                          as_stream(stream)),
+          "admission upload");
+  *out = e->admissions;
+  return XG_OK;
+}
+
+int launch_admit(XgEngine* e, const XgAdmission* admit, int32_t count, void* stream) {
+  admit_kernel<<<count, 32, 0, as_stream(stream)>>>(e->t, admit, e->max_sequences, e->faults);
+  XG_CUDA(cudaGetLastError(), "admit kernel");
   return XG_OK;
 }
 
@@ -996,6 +1212,15 @@ int xg_memory_host(XgEngine* e, int32_t sequences, int32_t* out) {
 int xg_sync_apply(XgEngine* e, const int32_t* slots, int32_t count, const int32_t* history, int64_t history_stride,
                   int64_t history_rows, const int32_t* prompt_len, const int32_t* total_len, int64_t lengths_count,
                   void* logits, int32_t dtype, int32_t cols, int64_t row_stride, void* stream) {
+  return xg_sync_apply_admit(e, slots, count, history, history_stride, history_rows, prompt_len, total_len,
+                             lengths_count, logits, dtype, cols, row_stride, nullptr, 0, 0, stream);
+}
+
+int xg_sync_apply_admit(XgEngine* e, const int32_t* slots, int32_t count, const int32_t* history,
+                        int64_t history_stride, int64_t history_rows, const int32_t* prompt_len,
+                        const int32_t* total_len, int64_t lengths_count, void* logits, int32_t dtype, int32_t cols,
+                        int64_t row_stride, const XgAdmission* admissions, int32_t admit_count,
+                        int32_t admissions_on_host, void* stream) {
   if (!e) return fail(XG_EINVAL, "null engine");
   if (count < 0 || count > e->max_sequences) return fail(XG_EINVAL, "more slots than max_sequences");
   if (lengths_count < e->max_sequences) return fail(XG_EINVAL, "prompt_len and total_len need one entry per slot");
@@ -1003,25 +1228,53 @@ int xg_sync_apply(XgEngine* e, const int32_t* slots, int32_t count, const int32_
     return fail(XG_EINVAL, "history needs one contiguous row per slot");
   if (cols < 0 || row_stride < cols) return fail(XG_EINVAL, "logits need one contiguous row per slot");
   if (dtype != XG_F32 && dtype != XG_BF16 && dtype != XG_F16) return fail(XG_EINVAL, "logits must be float32, bfloat16 or float16");
-  if (count == 0) return XG_OK;
+  if (static_cast<int64_t>(count) * ((cols + 1023) / 1024) > 0x7fffffff) return fail(XG_EINVAL, "too many logits rows");
+  const XgAdmission* admit = nullptr;
+  if (int rc = stage_admissions(e, admissions, admit_count, admissions_on_host, stream, &admit)) return rc;
+  if (count == 0) {
+    if (admit_count == 0) return XG_OK;
+    return launch_admit(e, admit, admit_count, stream);  // nothing to step: the admissions alone
+  }
   if (!slots || !history || !prompt_len || !total_len || !logits) return fail(XG_EINVAL, "null argument");
   const int elt = dtype == XG_F32 ? 4 : 2;
   if (reinterpret_cast<uintptr_t>(logits) % elt) return fail(XG_EINVAL, "logits are not aligned to their element size");
-  StepArgs a{};
-  a.slots = slots;
-  a.history = history;
-  a.stride = history_stride;
-  a.prompt_len = prompt_len;
-  a.total_len = total_len;
-  a.count = count;
+  FusedArgs f{};
+  f.a.slots = slots;
+  f.a.history = history;
+  f.a.stride = history_stride;
+  f.a.prompt_len = prompt_len;
+  f.a.total_len = total_len;
+  f.a.count = count;
+  f.admit = admit;
+  f.admit_count = admit_count;
+  f.max_slots = e->max_sequences;
+  f.logits = static_cast<char*>(logits);
+  f.stride = row_stride;
+  f.cols = cols;
+  f.neg = dtype == XG_F32 ? 0xff800000u : dtype == XG_BF16 ? 0xff80u : 0xfc00u;
+  f.faults = e->faults;
   cudaStream_t s = as_stream(stream);
-  char* data = static_cast<char*>(logits);
-  if (dtype == XG_F32)
-    sync_apply_kernel<4><<<count, kFusedThreads, e->composed_bytes, s>>>(e->t, a, data, cols, row_stride, 0xff800000u);
+  if (elt == 4)
+    sync_apply_kernel<4><<<count, kFusedThreads, e->composed_bytes, s>>>(e->t, f);
   else
-    sync_apply_kernel<2><<<count, kFusedThreads, e->composed_bytes, s>>>(e->t, a, data, cols, row_stride,
-                                                                         dtype == XG_BF16 ? 0xff80u : 0xfc00u);
+    sync_apply_kernel<2><<<count, kFusedThreads, e->composed_bytes, s>>>(e->t, f);
   XG_CUDA(cudaGetLastError(), "sync_apply kernel");
+  return XG_OK;
+}
+
+int xg_admit(XgEngine* e, const XgAdmission* admissions, int32_t count, int32_t on_host, void* stream) {
+  if (!e) return fail(XG_EINVAL, "null engine");
+  const XgAdmission* admit = nullptr;
+  if (int rc = stage_admissions(e, admissions, count, on_host, stream, &admit)) return rc;
+  if (count == 0) return XG_OK;
+  return launch_admit(e, admit, count, stream);
+}
+
+int xg_faults(XgEngine* e, int32_t* out) {
+  if (!e || !out) return fail(XG_EINVAL, "null argument");
+  XG_CUDA(cudaDeviceSynchronize(), "engine step");
+  XG_CUDA(cudaMemcpy(out, e->faults, sizeof(int32_t), cudaMemcpyDeviceToHost), "copy to host");
+  XG_CUDA(cudaMemset(e->faults, 0, sizeof(int32_t)), "fault reset");
   return XG_OK;
 }
 
@@ -1081,7 +1334,6 @@ int xg_apply_mask(XgEngine* e, void* logits, int32_t dtype, int32_t rows, int32_
                                e->max_sequences, dtype == XG_BF16 ? 0xff80u : 0xfc00u),
             "apply kernel");
   }
-  XG_CUDA(cudaGetLastError(), "apply kernel");
   return XG_OK;
 }
 

@@ -44,6 +44,9 @@ STATE_INTS = 64
 LIBRARY = Path(__file__).resolve().parent / "libxgraph_b200.so"
 
 XG_OK, XG_EINVAL, XG_ECUDA, XG_ENOMEM = 0, 1, 2, 3
+ADMISSION_INTS = 5 + MAX_REACHED
+"""int32 words of one admission record (XgAdmission: slot, on, version, open_span,
+anchor_count, 64 anchor rows)."""
 DTYPES = {"float32": 0, "bfloat16": 1, "float16": 2}
 
 # Reference constructor options this engine does not serve, with their neutral values.
@@ -100,6 +103,9 @@ def load_library(path: Path = LIBRARY):
         "xg_memory_host": ([p, i32, p], ctypes.c_int),
         "xg_apply_mask": ([p, p, i32, i32, i32, i64, p, p, p, p], ctypes.c_int),
         "xg_sync_apply": ([p, p, i32, p, i64, i64, p, p, i64, p, i32, i32, i64, p], ctypes.c_int),
+        "xg_sync_apply_admit": ([p, p, i32, p, i64, i64, p, p, i64, p, i32, i32, i64, p, i32, i32, p], ctypes.c_int),
+        "xg_admit": ([p, p, i32, i32, p], ctypes.c_int),
+        "xg_faults": ([p, ctypes.POINTER(i32)], ctypes.c_int),
         "xg_build_adjacency": ([p, p, p, i64, p, p, i32, i32, p, i32, i64, p, p, p, p, p, p], ctypes.c_int),
     }
     for name, (args, res) in sigs.items():
@@ -281,6 +287,12 @@ class Engine:
 
     def anchor(self, slot: int, entities: list[str], stream: int = 0) -> None:
         """Derivation/path mode: bind the slot's spans to these entities' label rows."""
+        rows = self._anchor_rows(entities)
+        _check(self._lib.xg_set_reached(self._handle, int(slot), rows.ctypes.data_as(ctypes.c_void_p),
+                                        len(rows), _stream(stream)))
+
+    def _anchor_rows(self, entities) -> np.ndarray:
+        """The first 64 label rows (sorted) of these entities; ValueError when they have none."""
         labels = self._index.labels
         if self._entity_index is None:
             self._entity_index = {e: n for n, e in enumerate(labels.owner_ids)}
@@ -296,17 +308,70 @@ class Engine:
         )
         if not found:
             raise ValueError(f"anchor has no writable label rows: {entities!r}")
-        rows = np.ascontiguousarray(found[:MAX_REACHED], dtype=np.int32)
-        _check(self._lib.xg_set_reached(self._handle, int(slot), rows.ctypes.data_as(ctypes.c_void_p),
-                                        len(rows), _stream(stream)))
+        return np.ascontiguousarray(found[:MAX_REACHED], dtype=np.int32)
+
+    def _version_number(self, version: str | None) -> int:
+        if self._versions is not None:
+            return self._versions.number(version)
+        if version is not None:
+            raise ValueError(f"no KG version {version!r}; the engine has none registered")
+        return 0
+
+    def admission_records(self, admissions: Iterable[Admission]) -> np.ndarray:
+        """XgAdmission records [n, ADMISSION_INTS] int32 for these admissions (anchor
+        entities to label rows, version names to numbers), checked as the single calls check
+        them; a device copy of the result can be handed to `admit` / `sync_apply` directly."""
+        admissions = list(admissions)
+        out = np.zeros((len(admissions), ADMISSION_INTS), dtype=np.int32)
+        for k, a in enumerate(admissions):
+            if not 0 <= int(a.slot) < self.max_sequences:
+                raise ValueError(f"slot must be between 0 and max_sequences - 1, got {a.slot}")
+            out[k, 0], out[k, 1] = int(a.slot), int(bool(a.on))
+            if a.on:
+                out[k, 2] = self._version_number(a.version)
+                out[k, 3] = int(bool(a.open_span))
+                if a.anchors:
+                    rows = self._anchor_rows(a.anchors)
+                    out[k, 4] = len(rows)
+                    out[k, 5: 5 + len(rows)] = rows
+        if len(set(out[:, 0].tolist())) != len(out):
+            raise ValueError("two admissions name the same slot")
+        return out
+
+    def _admission_args(self, admissions):
+        """(pointer, count, on_host, keep-alive) of admissions given as Admission objects, a
+        host record array or a device int32 tensor of records."""
+        import torch
+
+        if admissions is None:
+            return ctypes.c_void_p(0), 0, 0, None
+        if isinstance(admissions, torch.Tensor):
+            if (not admissions.is_cuda or admissions.dtype != torch.int32 or admissions.dim() != 2
+                    or admissions.shape[1] != ADMISSION_INTS or not admissions.is_contiguous()):
+                raise ValueError(f"device admissions must be a contiguous int32 [n, {ADMISSION_INTS}] GPU tensor")
+            return ctypes.c_void_p(admissions.data_ptr()), admissions.shape[0], 0, admissions
+        records = admissions if isinstance(admissions, np.ndarray) else self.admission_records(admissions)
+        records = np.ascontiguousarray(records, dtype=np.int32)
+        if records.ndim != 2 or records.shape[1] != ADMISSION_INTS:
+            raise ValueError(f"admission records must be int32 [n, {ADMISSION_INTS}]")
+        return records.ctypes.data_as(ctypes.c_void_p), records.shape[0], 1, records
+
+    def admit(self, admissions, stream: int = 0) -> None:
+        """Apply a batch of admissions (Admission objects, their records, or a device record
+        tensor) in one kernel launch; each admitted slot's mask is rebuilt."""
+        ptr, n, on_host, keep = self._admission_args(admissions)
+        _check(self._lib.xg_admit(self._handle, ptr, n, on_host, _stream(stream)))
+        del keep
+
+    def faults(self) -> int:
+        """Device-side faults since the last call (waits; bit 0 a fused step's grid barrier
+        gave up waiting, bit 1 a device admission out of range was skipped); 0 normally."""
+        out = ctypes.c_int32()
+        _check(self._lib.xg_faults(self._handle, ctypes.byref(out)))
+        return int(out.value)
 
     def set_version(self, slot: int, version: str | None, stream: int = 0) -> None:
-        if self._versions is not None:
-            number = self._versions.number(version)
-        elif version is not None:
-            raise ValueError(f"no KG version {version!r}; the engine has none registered")
-        else:
-            number = 0
+        number = self._version_number(version)
         _check(self._lib.xg_set_version(self._handle, int(slot), number, _stream(stream)))
 
     def open_span(self, slot: int, stream: int = 0) -> None:
@@ -358,9 +423,10 @@ class Engine:
             ctypes.c_void_p(prompt_len.data_ptr()), ctypes.c_void_p(total_len.data_ptr()),
             min(len(prompt_len), len(total_len)), _stream(stream)))
 
-    def sync_apply(self, slots, history, prompt_len, total_len, logits, stream: int = 0) -> None:
+    def sync_apply(self, slots, history, prompt_len, total_len, logits, stream: int = 0, *, admissions=None) -> None:
         """`sync` then `apply_mask(logits, slots)` in one kernel launch, for a step without
-        speculative draft rows (logits row i belongs to slots[i])."""
+        speculative draft rows (logits row i belongs to slots[i]); `admissions` (as for
+        `admit`) are applied first in the same launch."""
         import torch
 
         ptr, n = self._slots(slots)
@@ -378,11 +444,13 @@ class Engine:
             raise ValueError("logits must be float32, bfloat16 or float16")
         if logits.shape[0] != n or (logits.shape[1] > 1 and logits.stride(1) != 1):
             raise ValueError("logits need one contiguous row per entry of slots")
-        _check(self._lib.xg_sync_apply(
+        aptr, an, on_host, keep = self._admission_args(admissions)
+        _check(self._lib.xg_sync_apply_admit(
             self._handle, ptr, n, ctypes.c_void_p(history.data_ptr()), history.stride(0), history.shape[0],
             ctypes.c_void_p(prompt_len.data_ptr()), ctypes.c_void_p(total_len.data_ptr()),
             min(len(prompt_len), len(total_len)), ctypes.c_void_p(logits.data_ptr()), dtype, logits.shape[1],
-            logits.stride(0) if n > 1 else logits.shape[1], _stream(stream)))
+            logits.stride(0) if n > 1 else logits.shape[1], aptr, an, on_host, _stream(stream)))
+        del keep
 
     def apply_mask(self, logits, row_slots, stream: int = 0, *, local_pos=None, input_ids=None) -> None:
         """Set every logit its slot's mask disallows (and every column past the served
@@ -471,6 +539,20 @@ class Engine:
         if not 0 <= n <= self.max_sequences:
             raise ValueError(f"sequences must be between 0 and max_sequences ({self.max_sequences}), got {n}")
         return n
+
+
+@dataclass(frozen=True)
+class Admission:
+    """One request joining (on=True) or leaving (on=False) a slot between steps, applied in
+    the reference adapter's order (src/xgraph/vllm.py:569-605): begin or end, then the
+    anchor entities (derivation / path mode), then the KG version by name (None = base),
+    then open_span."""
+
+    slot: int
+    on: bool = True
+    anchors: tuple[str, ...] = ()
+    version: str | None = None
+    open_span: bool = False
 
 
 @dataclass(frozen=True)

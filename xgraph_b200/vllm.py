@@ -39,6 +39,7 @@ from __future__ import annotations
 
 import os
 import sys
+from dataclasses import dataclass
 from typing import Any
 
 try:
@@ -95,30 +96,42 @@ class XGraphWorkerExtension:
         return collect_replay_status(self, keys)
 
 
-def replay_statuses(llm, keys: list[str]) -> dict[str, dict]:
-    """The replay outcome of each key over all workers (src/xgraph/vllm.py:150-196): a
-    decline on any worker wins; a key every worker confirms is replayed; anything else
-    (no answer, a worker that did not see the key) is unconfirmed."""
-    unavailable = "worker replay status unavailable"
+DECLINES = ("tail mismatch", "disallowed")
+
+
+def _worker_receipts(llm, keys: list[str]) -> tuple[list, str]:
+    """Every worker's {key: outcome} answer to the replay-status RPC, with the reason to give
+    for a key no answer settles."""
+    call = getattr(llm, "collective_rpc", None)
+    if not callable(call):
+        return [], "worker replay status unavailable"
     try:
-        rpc = getattr(llm, "collective_rpc", None)
-        results = rpc("xgraph_collect_replay_status", args=(keys,), timeout=30) if callable(rpc) else []
+        answers = call("xgraph_collect_replay_status", args=(keys,), timeout=30)
     except Exception as error:  # the outcome is reported, not raised
-        results = []
-        unavailable = f"worker replay status failed: {type(error).__name__}: {str(error)[:512]}"
-    if not isinstance(results, (list, tuple)):
-        results, unavailable = [], "invalid worker replay status response"
-    statuses = {}
+        return [], f"worker replay status failed: {type(error).__name__}: {str(error)[:512]}"
+    if not isinstance(answers, (list, tuple)):
+        return [], "invalid worker replay status response"
+    return list(answers), "worker replay status unavailable"
+
+
+def replay_statuses(llm, keys: list[str]) -> dict[str, dict]:
+    """The replay outcome of each key over all workers (the reference's
+    src/xgraph/vllm.py:150-196 reports the same three kinds): declined when some worker
+    declined it (that worker's reason), replayed when every worker answered and each says
+    replayed, else unconfirmed (an answer missing or unreadable)."""
+    answers, missing = _worker_receipts(llm, keys)
+    readable = [a for a in answers if isinstance(a, dict)]
+    out: dict[str, dict] = {}
     for key in keys:
-        values = [item[key] for item in results if isinstance(item, dict) and key in item]
-        declined = next((v for v in values if v in ("tail mismatch", "disallowed")), None)
-        if declined is not None:
-            statuses[key] = {"replay_status": "declined", "replay_reason": declined, "declined": True}
-        elif results and len(values) == len(results) and all(v == "replayed" for v in values):
-            statuses[key] = {"replay_status": "replayed"}
+        outcomes = [a.get(key) for a in readable]
+        reason = next((o for o in outcomes if o in DECLINES), None)
+        if reason is not None:
+            out[key] = {"replay_status": "declined", "replay_reason": reason, "declined": True}
+        elif answers and len(readable) == len(answers) and all(o == "replayed" for o in outcomes):
+            out[key] = {"replay_status": "replayed"}
         else:
-            statuses[key] = {"replay_status": "unconfirmed", "replay_reason": unavailable, "error": True}
-    return statuses
+            out[key] = {"replay_status": "unconfirmed", "replay_reason": missing, "error": True}
+    return out
 
 
 def _version_names(path: str) -> list[str]:
@@ -130,26 +143,27 @@ def _version_names(path: str) -> list[str]:
     return _REGISTERED[path]
 
 
-def replayed_tokens(tail: list[int], token_bytes, prefill: bytes) -> int | None:
-    """How many of the last tokens of `tail` to replay for a prompt ending with `prefill`:
-    the fewest whose bytes (token_bytes: a token's bytes, None for a special token) cover
-    it, or None if their bytes do not end with it (src/xgraph/vllm.py:233-245)."""
-    written = b""
-    for count, token in enumerate(reversed(tail), start=1):
+def tail_cover(tail: list[int], token_bytes, prefill: bytes) -> int | None:
+    """The number k of trailing tokens of `tail` to replay so that the prompt's end holds
+    `prefill`: the smallest k whose tokens' bytes are at least as long as it, accepted only
+    if those bytes end with it and none of the k tokens is special (token_bytes(t) is None
+    for a special token); None declines the replay."""
+    sizes = []
+    for token in reversed(tail):
         data = token_bytes(token)
         if data is None:
             return None
-        written = data + written
-        if len(written) >= len(prefill):
-            return count if written.endswith(prefill) else None
+        sizes.append(data)
+        if sum(map(len, sizes)) >= len(prefill):
+            return len(sizes) if b"".join(reversed(sizes)).endswith(prefill) else None
     return None
 
 
-def _setting(name: str) -> str:
-    value = os.environ.get(name)
-    if not value:
-        raise RuntimeError(f"{name} is not set; the xgraph logits processor needs it")
-    return value
+def _required_env(name: str) -> str:
+    """An environment setting the processor cannot start without."""
+    if value := os.environ.get(name):
+        return value
+    raise RuntimeError(f"the xgraph logits processor needs the environment setting {name}")
 
 
 def check_served_settings(environ=os.environ) -> None:
@@ -170,24 +184,43 @@ def _is_zero(value: str | None, off: str) -> bool:
         return False
 
 
-class PendingRequest:
-    """One slot's staged admission (in admission order), then its delayed prefill replay."""
+def _flag(extra: dict, name: str):
+    """A 0/1 per-request argument (absent: None); any other value is refused."""
+    value = extra.get(name)
+    if value is None or (not isinstance(value, float) and value in (0, 1)):
+        return value
+    raise ValueError(f"the per-request argument {name!r} takes 0 or 1, not {value!r}")
 
-    def __init__(self) -> None:
-        self.admissions: list[tuple[int, bool]] = []
-        self.anchor: list[str] | None = None
-        self.version: str | None = None
-        self.opened = False
-        self.prefill: bytes | None = None
-        self.replay_id: str | None = None
-        self.order: dict[str, int] = {}
 
-    def stage(self, name: str, value: Any, order: int) -> None:
-        if value is None:
-            self.order.pop(name, None)
-        else:
-            self.order.setdefault(name, order)
-        setattr(self, name, value)
+def _needs_engine(engine: bool, name: str) -> None:
+    if not engine:
+        raise ValueError(f"{name!r} only applies to requests that set {OPT_IN!r} to 1")
+
+
+def _check_version_argument(version) -> None:
+    """A KG version named by a request must be one of XGRAPH_KG_VERSIONS."""
+    if version is None:
+        return
+    if not isinstance(version, str):
+        raise ValueError(f"{KG_VERSION!r} is a KG version's name, not {version!r}")
+    path = os.environ.get(VERSIONS)
+    if not path:
+        raise ValueError(f"{KG_VERSION!r} asks for {version!r} but {VERSIONS} registers no KG versions")
+    names = _version_names(path)
+    if version not in names:
+        raise ValueError(f"{version!r} is not a registered KG version (those are {names})")
+
+
+@dataclass
+class Staged:
+    """What a slot's admissions since the last step leave it with: the latest admitted
+    request (Admission: begin or end, anchors, version, open) and its prefill to replay.
+    A slot that was also ended during the step ends (the adapter begins before it ends)."""
+
+    admission: Any
+    ended: bool = False
+    prefill: bytes | None = None
+    replay_id: str | None = None
 
 
 class XGraphLogitsProcessor(_Base):
@@ -207,8 +240,8 @@ class XGraphLogitsProcessor(_Base):
         from xgraph_b200.tokenizer import ServedTokenizer
 
         check_served_settings()
-        index = load_kg_index(_setting("XGRAPH_KG_INDEX"))
-        tokenizer = ServedTokenizer.from_file(_setting("XGRAPH_TOKENIZER"))
+        index = load_kg_index(_required_env("XGRAPH_KG_INDEX"))
+        tokenizer = ServedTokenizer.from_file(_required_env("XGRAPH_TOKENIZER"))
         versions = None
         if os.environ.get(VERSIONS):
             from xgraph_b200.kgversions import load_kg_versions
@@ -247,9 +280,9 @@ class XGraphLogitsProcessor(_Base):
             end_after_answer=end_after_answer,
             eos_token_ids=eos_token_ids,
         )
-        self._pending: dict[int, PendingRequest] = {}
-        self._replaying: dict[int, PendingRequest] = {}
-        self._admission_order = 0
+        self._staged: dict[int, Staged] = {}   # slot -> admissions since the last apply_staged_writes
+        self._folded = None                    # admission records the next step's launch applies
+        self._prefills: dict[int, Staged] = {}  # slot -> a prefill to replay before its first sync
         self.replays = dict.fromkeys(REPLAYS, 0)
 
     @property
@@ -264,148 +297,141 @@ class XGraphLogitsProcessor(_Base):
 
     @classmethod
     def validate_params(cls, sampling_params: Any) -> None:
-        """The reference's per-request argument checks (src/xgraph/vllm.py:442-516) for the
-        served arguments; arguments of unserved policies are refused."""
+        """Refuse a request whose per-request arguments the engine cannot honour (the
+        arguments and what they accept are the reference's, src/xgraph/vllm.py:442-516, for
+        the served policies); arguments of unserved policies are refused by name."""
         extra = sampling_params.extra_args or {}
-        value = extra.get(OPT_IN)
-        if value not in (None, 0, 1) or isinstance(value, float):
-            raise ValueError(f"the per-request argument {OPT_IN!r} must be 0 or 1, got {value!r}")
-        for name in _UNSERVED_ARGS:
-            if name in extra:
-                raise ValueError(f"the per-request argument {name!r} is not served by the xgraph_b200 engine")
+        engine = _flag(extra, OPT_IN) == 1
+        unserved = [name for name in _UNSERVED_ARGS if name in extra]
+        if unserved:
+            raise ValueError(f"{unserved[0]!r} belongs to a policy the xgraph_b200 engine does not serve")
         question = extra.get(QUESTION)
-        if question is not None and (not isinstance(question, str) or not question.strip()):
-            raise ValueError(f"the per-request argument {QUESTION!r} must be the question text")
-        stop = extra.get(STOP)
-        if stop is not None and (type(stop) is not int or stop != 0):
-            raise ValueError(f"the per-request argument {STOP!r} only accepts 0, got {stop!r}")
-        if stop is not None and value != 1:
-            raise ValueError(f"{STOP} needs the engine: set {OPT_IN!r} to 1")
-        opened = extra.get(OPEN)
-        if opened not in (None, 0, 1) or isinstance(opened, float):
-            raise ValueError(f"the per-request argument {OPEN!r} must be 0 or 1, got {opened!r}")
-        if opened and value != 1:
-            raise ValueError(f"{OPEN} needs the engine: set the per-request argument {OPT_IN!r} to 1")
+        if question is not None and not (isinstance(question, str) and question.strip()):
+            raise ValueError(f"{QUESTION!r} must be the question's text, not {question!r}")
+        if STOP in extra:
+            if type(extra[STOP]) is not int or extra[STOP] != 0:
+                raise ValueError(f"{STOP!r} can only be 0 (STOP is off in this engine), not {extra[STOP]!r}")
+            _needs_engine(engine, STOP)
+        opened = _flag(extra, OPEN)
+        if opened:
+            _needs_engine(engine, OPEN)
         prefill = extra.get(PREFILL)
-        if REPLAY_ID in extra and (not isinstance(extra[REPLAY_ID], str) or not extra[REPLAY_ID] or not prefill):
-            raise ValueError(f"{REPLAY_ID} needs a nonempty string and {PREFILL}")
+        if REPLAY_ID in extra:
+            key = extra[REPLAY_ID]
+            if not (isinstance(key, str) and key) or not prefill:
+                raise ValueError(f"{REPLAY_ID!r} is a nonempty string key and goes with {PREFILL!r}")
         if prefill is not None:
-            if not isinstance(prefill, str) or not prefill:
-                raise ValueError(f"the per-request argument {PREFILL!r} must be the text the prompt ends "
-                                 f"with, got {prefill!r}")
-            if value != 1:
-                raise ValueError(f"{PREFILL} needs the engine: set the per-request argument {OPT_IN!r} to 1")
+            if not (isinstance(prefill, str) and prefill):
+                raise ValueError(f"{PREFILL!r} is the text the prompt ends with, not {prefill!r}")
+            _needs_engine(engine, PREFILL)
             if opened:
-                raise ValueError(f"{PREFILL} and {OPEN} exclude each other: replay the opener")
-        version = extra.get(KG_VERSION)
-        if version is None:
-            return
-        if not isinstance(version, str):
-            raise ValueError(f"the per-request argument {KG_VERSION!r} must be a KG version's name, got {version!r}")
-        if not os.environ.get(VERSIONS):
-            raise ValueError(f"{KG_VERSION} names {version!r}, but no KG versions are registered "
-                             f"({VERSIONS} is not set)")
-        names = _version_names(os.environ[VERSIONS])
-        if version not in names:
-            raise ValueError(f"no KG version {version!r}; the registered ones are {names}")
+                raise ValueError(f"{PREFILL!r} replays the opener itself; it cannot go with {OPEN!r}")
+        _check_version_argument(extra.get(KG_VERSION))
 
     def add_request(self, req_idx: int, sampling_params: Any) -> bool:
         """Stage the admission of a request to slot `req_idx`; True when it opted in."""
+        from xgraph_b200.engine import Admission
+
         extra = sampling_params.extra_args or {}
         on = bool(extra.get(OPT_IN))
-        order = self._admission_order
-        self._admission_order += 1
-        pending = self._pending.setdefault(req_idx, PendingRequest())
-        pending.admissions.append((order, on))
-        if on and ANCHOR in extra:
-            pending.stage("anchor", [str(e) for e in extra[ANCHOR]], order)
-        pending.stage("version", str(extra[KG_VERSION]) if on and extra.get(KG_VERSION) else None, order)
-        pending.opened = bool(on and extra.get(OPEN))
+        earlier = self._staged.get(req_idx)
+        entry = Staged(Admission(req_idx, False), ended=True) if not on else Staged(Admission(
+            req_idx, True, tuple(str(e) for e in extra.get(ANCHOR) or ()),
+            str(extra[KG_VERSION]) if extra.get(KG_VERSION) else None, bool(extra.get(OPEN))))
+        entry.ended |= bool(earlier and earlier.ended)
         if on and extra.get(PREFILL):
-            pending.prefill = str(extra[PREFILL]).encode("utf-8")
-            pending.replay_id = extra.get(REPLAY_ID) or None
-            self._replaying[req_idx] = pending
-        else:
-            self._replaying.pop(req_idx, None)
+            entry.prefill = str(extra[PREFILL]).encode("utf-8")
+            entry.replay_id = extra.get(REPLAY_ID) or None
+        self._staged[req_idx] = entry
         return on
 
     def apply_staged_writes(self) -> None:
-        """Begin (or end) the admitted slots in admission order, then set their anchors and
-        versions and open the spans of `xgraph_open` requests."""
-        admissions = sorted((order, slot, on) for slot, pending in self._pending.items()
-                            for order, on in pending.admissions)
-        for on, start in ((True, self._engine.begin), (False, self._engine.end)):
-            slots = [slot for _, slot, enabled in admissions if enabled == on]
-            if slots:
-                start(self._slots(slots), self._stream())
-        for field, method in (("anchor", "anchor"), ("version", "set_version")):
-            writes = sorted((pending.order[field], slot, getattr(pending, field))
-                            for slot, pending in self._pending.items() if field in pending.order)
-            for _, slot, value in writes:
-                getattr(self._engine, method)(slot, value, self._stream())
-        for slot in sorted(slot for slot, pending in self._pending.items() if pending.opened):
-            self._engine.open_span(slot, self._stream())
-        self._pending.clear()
+        """Turn the staged admissions into one admission record per slot.  They are applied
+        in the next step's launch (Engine.sync_apply with admissions), or by one admit launch
+        when that step needs them earlier (a prefill to replay, draft rows)."""
+        from xgraph_b200.engine import Admission
+
+        if not self._staged:
+            return
+        if self._folded is not None:  # a second round before any step: the first goes now
+            self._engine.admit(self._folded, self._stream())
+            self._folded = None
+        admissions = []
+        for slot, entry in sorted(self._staged.items()):
+            admissions.append(Admission(slot, False) if entry.ended else entry.admission)
+            if entry.prefill is not None and not entry.ended:
+                self._prefills[slot] = entry
+            else:
+                self._prefills.pop(slot, None)
+        self._staged.clear()
+        self._folded = self._engine.admission_records(admissions)
 
     def apply(self, logits: Any, ctx: Any) -> Any:
         """Advance every opted-in slot of the step over its newly committed tokens and set the
-        logits its mask disallows to -inf, in place (src/xgraph/vllm.py:607-631)."""
+        logits its mask disallows to -inf, in place (the reference adapter's step,
+        src/xgraph/vllm.py:607-631), with the step's admissions applied first."""
         int32 = self._torch.int32
         state = self._req_states
         stream = self._stream()
-        if self._replaying:  # before the slots' first sync: their cursors are still unset
-            self._replay(stream)
+        drafts = ctx.expanded_idx_mapping.shape[0] != ctx.idx_mapping.shape[0]
+        if self._folded is not None and (drafts or self._prefills):
+            self._engine.admit(self._folded, stream)
+            self._folded = None
+        if self._prefills:  # before the slots' first sync: their cursors are still unset
+            self._replay_prefills(stream)
         slots = ctx.idx_mapping.to(int32)
-        if ctx.expanded_idx_mapping.shape[0] == ctx.idx_mapping.shape[0]:  # no drafts: one launch
+        if not drafts:  # one launch: admissions, sync and the masks
+            folded, self._folded = self._folded, None
             self._engine.sync_apply(slots, state.all_token_ids.gpu, state.prompt_len.gpu, state.total_len.gpu,
-                                    logits, stream)
+                                    logits, stream, admissions=folded)
         else:
             self._engine.sync(slots, state.all_token_ids.gpu, state.prompt_len.gpu, state.total_len.gpu, stream)
             self._engine.apply_mask(logits, ctx.expanded_idx_mapping.to(int32), stream,
                                     local_pos=ctx.expanded_local_pos.to(int32), input_ids=ctx.input_ids.to(int32))
         return logits
 
-    def _replay(self, stream: int) -> None:
-        """Advance each slot with a pending prefill over the prompt tokens that hold it, then
-        decline (end) those whose tail does not match or whose replay hit a token outside the
-        mask (src/xgraph/vllm.py:633-680)."""
+    def _replay_prefills(self, stream: int) -> None:
+        """Each admitted slot with a prefill consumes the prompt tokens that spell it (sync
+        over [prompt_len - k, prompt_len)), as if the model had written them; a prompt that
+        does not end with the prefill's bytes, or a replay that leaves the language, ends
+        the slot (the request is served unmasked) and is counted and reported."""
         from xgraph_b200.engine import PHASE_ERROR
-        from xgraph_b200.vllm import _REPLAY_RESULTS as results
+        from xgraph_b200.vllm import _REPLAY_RESULTS as outcomes
 
         torch, state = self._torch, self._req_states
-        pending, self._replaying = self._replaying, {}
-        history = state.all_token_ids.gpu
-        start = torch.zeros_like(state.prompt_len.gpu)
-        stop = torch.zeros_like(state.prompt_len.gpu)
-        replayed, declined = [], []
-        for slot, request in sorted(pending.items()):
-            prefill = request.prefill
-            end = int(state.prompt_len.gpu[slot])
-            tail = history[slot, max(0, end - len(prefill)): end].tolist()
-            count = replayed_tokens(tail, self._tokenizer.token_bytes, prefill)
-            if count is None:
-                declined.append((slot, "tail mismatch"))
+        todo, self._prefills = sorted(self._prefills.items()), {}
+        prompt_end = state.prompt_len.gpu
+        begin_at, end_at = torch.zeros_like(prompt_end), torch.zeros_like(prompt_end)
+        outcome: dict[int, str] = {}
+        live = []
+        for slot, entry in todo:
+            end = int(prompt_end[slot])
+            tail = state.all_token_ids.gpu[slot, max(0, end - len(entry.prefill)): end].tolist()
+            k = tail_cover(tail, self._tokenizer.token_bytes, entry.prefill)
+            if k is None:
+                outcome[slot] = "tail mismatch"
                 continue
-            start[slot], stop[slot] = end - count, end
-            replayed.append(slot)
-        if replayed:  # sync from start to stop: the cursors then stand at the prompt's end
-            self._engine.sync(self._slots(replayed), history, start, stop, stream)
-            phases = self._engine.states_host(max(replayed) + 1)["phase"]
-            for slot in replayed:
-                if phases[slot] == PHASE_ERROR:
-                    declined.append((slot, "disallowed"))
+            begin_at[slot], end_at[slot] = end - k, end
+            live.append(slot)
+        if live:  # afterwards the slots' cursors stand at their prompts' ends
+            self._engine.sync(self._slots(live), state.all_token_ids.gpu, begin_at, end_at, stream)
+            phase = self._engine.states_host(max(live) + 1)["phase"]
+            for slot in live:
+                outcome[slot] = "disallowed" if phase[slot] == PHASE_ERROR else "replayed"
+        ended = sorted(slot for slot, result in outcome.items() if result != "replayed")
+        if ended:
+            self._engine.end(self._slots(ended), stream)
+        for slot, entry in todo:
+            result = outcome[slot]
+            self.replays[result] += 1
+            if entry.replay_id:
+                if result == "replayed":
+                    outcomes.setdefault(entry.replay_id, result)  # a decline stays a decline
                 else:
-                    self.replays["replayed"] += 1
-                    if key := pending[slot].replay_id:
-                        results.setdefault(key, "replayed")  # a re-admission never erases a decline
-        if declined:
-            self._engine.end(self._slots([slot for slot, _ in declined]), stream)
-            for slot, reason in declined:
-                self.replays[reason] += 1
-                if key := pending[slot].replay_id:
-                    results[key] = reason
-                print(f"xgraph: declined the replayed prefill of the request in slot {slot} ({reason}); "
-                      f"it is left unmasked. Replays so far: {self.replays}", file=sys.stderr, flush=True)
+                    outcomes[entry.replay_id] = result
+            if result != "replayed":
+                print(f"xgraph: slot {slot}: the replayed prefill was declined ({result}); the request "
+                      f"runs unmasked. Replays: {self.replays}", file=sys.stderr, flush=True)
 
     def _slots(self, slots: list[int]) -> Any:
         return self._torch.tensor(slots, dtype=self._torch.int32, device=self._req_states.device)
