@@ -42,11 +42,17 @@ import time
 from pathlib import Path
 
 import numpy as np
+from dataclasses import dataclass
 
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "mask+advance rows.steps/s at B=256, V=128,256 (bf16 logits)"
+
+
+def metric_of(config: int, rows: int, vocab: int) -> str:
+    """The headline metric's name (config 3); another configuration names its own batch."""
+    return METRIC if config == 3 else f"mask+advance rows.steps/s at B={rows}, V={vocab:,} (bf16 logits)"
 UNIT = "rows.steps/s"
 
 
@@ -82,34 +88,17 @@ def make_workload(config: int, seed: int):
     return build_workload(config, seed)
 
 
-def admissions_tensor(slots: list[int], device):
+def admissions_tensor(joined: list[tuple[int, int]], device):
     """Device admission records (xgraph_b200.engine.ADMISSION_INTS int32 each) beginning
-    these slots on the base KG."""
+    each (slot, KG version number) pair's slot on that version (0 = the base KG)."""
     import torch
 
     from xgraph_b200.engine import ADMISSION_INTS
 
-    records = np.zeros((len(slots), ADMISSION_INTS), dtype=np.int32)
-    records[:, 0] = slots
-    records[:, 1] = 1
+    records = np.zeros((len(joined), ADMISSION_INTS), dtype=np.int32)
+    for k, (slot, version) in enumerate(joined):
+        records[k, :3] = (slot, 1, version)
     return torch.from_numpy(records).to(device)
-
-
-def schedule(lengths: list[int], rows: int, steps: int):
-    """Per slot, the streams it replays back to back (stream ids) and, per step, the
-    slots that start a new stream (replenishment)."""
-    assigned = [[] for _ in range(rows)]
-    restarts = [[] for _ in range(steps)]
-    next_stream = 0
-    for slot in range(rows):
-        at = 0
-        while at < steps:
-            sid = next_stream % len(lengths)
-            next_stream += 1
-            assigned[slot].append((sid, at))
-            restarts[at].append(slot)
-            at += lengths[sid]
-    return assigned, restarts
 
 
 class Clocks:
@@ -206,10 +195,11 @@ def row_plan(rows: int, lengths, steps: int, offset: int = 0):
 _WORKER = {}
 
 
-def _worker_init(index, served, syntax, options, tokens, vocab):
+def _worker_init(index, served, syntax, options, tokens, vocab, versions=None, row_versions=None):
     from oracle.oracle import Oracle
 
-    _WORKER["oracle"] = Oracle(index, served, syntax, **options)
+    _WORKER["oracle"] = Oracle(index, served, syntax, versions=versions, **options)
+    _WORKER["row_versions"] = row_versions
     _WORKER["tokens"] = tokens
     _WORKER["vocab"] = vocab
     _WORKER["states"] = {}
@@ -227,7 +217,8 @@ def _worker_step(job):
     spent, mismatch = 0.0, None
     for row, sid, pos in rows:
         if pos == 0 or row not in states:
-            states[row] = oracle.initial_state()
+            versions = _WORKER.get("row_versions")
+            states[row] = oracle.initial_state(versions[row] if versions else None)
         token = int(tokens[sid, pos])
         if row == full:
             t0 = time.perf_counter()
@@ -258,7 +249,8 @@ def _worker_main(conn, init_args):
 
 
 def oracle_leg(workload, tokens, lengths, rows: int, steps: int, warmup: int, *, budget: float | None = None,
-               expected: dict | None = None, workers: int | None = None) -> dict:
+               expected: dict | None = None, workers: int | None = None, versions: dict | None = None,
+               row_versions: list | None = None) -> dict:
     """The oracle replaying rows x (warmup + steps) of the streams on `workers` spawned
     processes, each owning a fixed set of rows; a step waits for every worker.  With
     `budget` (seconds) the timed steps stop early once it is spent.  expected:
@@ -270,7 +262,7 @@ def oracle_leg(workload, tokens, lengths, rows: int, steps: int, warmup: int, *,
     plan = row_plan(rows, lengths, warmup + steps)
     owned = [list(range(w, rows, workers)) for w in range(workers)]
     init = (workload.index, workload.served, workload.syntax, dict(workload.config.options), tokens,
-            workload.served.vocab_size)
+            workload.served.vocab_size, versions, row_versions)
     ctx = mp.get_context("spawn")
     t_setup = time.perf_counter()
     pipes, procs = [], []
@@ -341,12 +333,124 @@ def cpu_baseline(workload, tokens, lengths, rows: int, expected: dict, budget: f
 # ---------------------------------------------------------------------------------------
 # engine arm
 
+@dataclass
+class Replay:
+    """What the timed loop replays: the engine's slots, each step's rows (slots, in logits
+    row order), admissions and token history (history[slot, k] is the token slot `slot`
+    consumes at step k), the disallowed columns summed over each step's rows (for the
+    roofline's algorithmic bytes), the KG versions to register, and how the streams came."""
+
+    slots: int
+    history: object
+    step_slots: list
+    admissions: list
+    live: list
+    disallowed: np.ndarray
+    versions: list
+    streams_source: str
+    cpu: dict
+
+
+def fixture_replay(args, workload, device, rank: int, total_steps: int, blob_meta, lo_hi) -> Replay:
+    """Configs 1-4: rows replay token streams back to back (the committed fixture, rank r its
+    own rotation of it, or streams sampled on the GPU when the configuration has none); a
+    request joining a slot is an admission (begin, base KG) folded into its step's launch."""
+    import torch
+
+    from xgraph_b200.engine import Engine
+    from xgraph_b200.synthetic import sample_streams
+
+    cfg = workload.config
+    rows, pool, vocab = cfg.rows, 2 * cfg.rows, workload.served.vocab_size
+    fixture = load_streams(args.config, workload)
+    if fixture is not None:
+        all_tokens, all_lengths, all_allowed = fixture
+        pick = [(rank * rows + j) % len(all_lengths) for j in range(pool)]
+        tokens_np, lengths, counts_h = all_tokens[pick], all_lengths[pick], all_allowed[pick]
+        source = f"fixture {STREAM_FIXTURES[args.config].name}"
+    else:
+        gen_engine = Engine(workload.index, workload.served, workload.syntax, pool, device_blob=blob_meta,
+                            **cfg.options)
+        rng = np.random.default_rng(args.seed + 100 + rank)
+        lengths = rng.integers(cfg.lengths[0], cfg.lengths[1] + 1, size=pool)
+        sampled, counts, _ = sample_streams(gen_engine, workload.served, workload.syntax, workload.world,
+                                            pool, cfg.lengths[1], seed=args.seed + rank)
+        tokens_np, counts_h = sampled.cpu().numpy(), counts.cpu().numpy()
+        del gen_engine
+        source = "sampled on the GPU with the engine's masks (no fixture for this configuration)"
+    lengths = np.maximum(np.minimum(lengths, lo_hi[1]), 1)
+    plan = row_plan(rows, lengths, total_steps)
+    sid, pos = plan[:, :, 0], plan[:, :, 1]
+    history = torch.from_numpy(np.ascontiguousarray(tokens_np[sid, pos], dtype=np.int32)).to(device)
+    disallowed = (vocab - counts_h[sid, pos + 1]).sum(axis=0).astype(np.int64)
+    every = torch.arange(rows, dtype=torch.int32, device=device)
+    admissions = []
+    for k in range(total_steps):
+        joined = np.flatnonzero(pos[:, k] == 0).tolist()
+        admissions.append(admissions_tensor([(slot, 0) for slot in joined], device) if joined else None)
+    return Replay(rows, history, [every] * total_steps, admissions, [rows] * total_steps, disallowed, [], source,
+                  {"tokens": tokens_np, "lengths": lengths})
+
+
+def versions_replay(args, workload, device, rank: int, total_steps: int, blob_meta) -> Replay:
+    """The versions configuration: continuous batching on this GPU's share of the arrivals
+    (synthetic.arrival_schedule: Poisson, geometric lengths, ragged batches), each request
+    carrying 0..max_edits seeded add/remove edits as its own KG version, registered with the
+    engine (Engine.add_version, between steps, outside the timed launches) and selected by
+    the request's admission; streams sampled on the GPU under each request's version."""
+    import torch
+
+    from xgraph_b200.engine import Engine
+    from xgraph_b200.synthetic import arrival_schedule, object_sets, request_edits, sample_streams
+
+    cfg = workload.config
+    vocab = workload.served.vocab_size
+    sched = arrival_schedule(cfg, total_steps, args.seed, rank)
+    admitted = [r for r in range(len(sched.arrival)) if sched.slot[r] >= 0]
+    pairs = object_sets(workload.world)
+    rng = np.random.default_rng(args.seed * 7919 + rank)
+    edits = {f"request-{rank}-{r}": request_edits(workload.world, pairs, rng, int(rng.integers(0, cfg.max_edits + 1)))
+             for r in admitted}
+    names = list(edits)
+    steps = max(sched.length[r] for r in admitted)
+    gen_engine = Engine(workload.index, workload.served, workload.syntax, len(admitted), device_blob=blob_meta,
+                        **cfg.options)
+    t0 = time.perf_counter()
+    for name in names:
+        gen_engine.add_version(name, edits[name])
+    torch.cuda.synchronize()
+    add_ms = 1e3 * (time.perf_counter() - t0) / max(len(names), 1)
+    tokens, counts, _ = sample_streams(gen_engine, workload.served, workload.syntax, workload.world, len(admitted),
+                                       steps, seed=args.seed + 31 * rank, versions=names)
+    tokens_np, counts_h = tokens.cpu().numpy(), counts.cpu().numpy()
+    del gen_engine
+    rows = cfg.rows
+    history = np.zeros((rows, total_steps), dtype=np.int32)
+    disallowed = np.zeros(total_steps, dtype=np.int64)
+    joins: list[list[tuple[int, int]]] = [[] for _ in range(total_steps)]
+    for j, r in enumerate(admitted):
+        slot, k0 = sched.slot[r], sched.start[r]
+        n = min(sched.length[r], total_steps - k0)
+        history[slot, k0: k0 + n] = tokens_np[j, :n]
+        disallowed[k0: k0 + n] += vocab - counts_h[j, 1: n + 1]
+        joins[k0].append((slot, j))
+    version_of = {j: j + 1 for j in range(len(admitted))}  # numbers in the replay engine: added in this order
+    admissions = [admissions_tensor([(slot, version_of[j]) for slot, j in joined], device) if joined else None
+                  for joined in joins]
+    step_slots = [torch.tensor(live, dtype=torch.int32, device=device) for live in sched.live]
+    return Replay(rows, torch.from_numpy(history).to(device), step_slots, admissions,
+                  [len(live) for live in sched.live], disallowed, [(name, edits[name]) for name in names],
+                  f"sampled on the GPU under each request's version ({len(admitted)} requests)",
+                  {"add_version_ms": add_ms, "requests": len(admitted),
+                   "edits_mean": float(np.mean([len(e) for e in edits.values()])) if edits else 0.0,
+                   "tokens": tokens_np, "names": names, "edits": edits, "lengths": [sched.length[r] for r in admitted]})
+
+
 def engine_arm(args) -> None:
     import torch
     import torch.distributed as dist
 
     from xgraph_b200.engine import Engine
-    from xgraph_b200.synthetic import sample_streams
     from xgraph_b200.tables import pack_tables
 
     rank, world, local = dist_env()
@@ -373,61 +477,37 @@ def engine_arm(args) -> None:
         blob, meta = torch.from_numpy(packed.blob).to(device), packed
     cfg = workload.config
     options = dict(cfg.options)
-    rows = cfg.rows
-    pool = 2 * rows
     vocab = workload.served.vocab_size
     lo, hi = cfg.lengths
     if args.max_len:
         lo, hi = min(lo, args.max_len), min(hi, args.max_len)
-    # -- token streams: the committed fixture (rank r replays its own rotation of it) or,
-    # for a configuration without one, constrained decodes sampled on the GPU
-    t0 = time.perf_counter()
-    fixture = load_streams(args.config, workload)
-    if fixture is not None:
-        all_tokens, all_lengths, all_allowed = fixture
-        pick = [(rank * rows + j) % len(all_lengths) for j in range(pool)]
-        tokens_np, lengths, counts_h = all_tokens[pick], all_lengths[pick], all_allowed[pick]
-        streams_source = f"fixture {STREAM_FIXTURES[args.config].name}"
-    else:
-        gen_engine = Engine(workload.index, workload.served, workload.syntax, pool, device_blob=(blob, meta), **options)
-        rng = np.random.default_rng(args.seed + 100 + rank)
-        lengths = rng.integers(cfg.lengths[0], cfg.lengths[1] + 1, size=pool)
-        sampled, counts, _ = sample_streams(gen_engine, workload.served, workload.syntax, workload.world,
-                                            pool, cfg.lengths[1], seed=args.seed + rank)
-        tokens_np, counts_h = sampled.cpu().numpy(), counts.cpu().numpy()
-        del gen_engine
-        streams_source = "sampled on the GPU with the engine's masks (no fixture for this configuration)"
-    if args.max_len:
-        lengths = np.minimum(lengths, args.max_len)
-    lengths = np.maximum(lengths, 1)
-    sample_s = time.perf_counter() - t0
-    # -- replay schedule -------------------------------------------------------------------
     # W warm-up steps, then K timed steps, then (outside the profile mode) up to 128 more
-    # steps without the flush: the warm figure.  Row r replays pool streams r, r + rows, ...
-    # back to back; a step is one sync_apply launch (sync + apply_mask fused, the step's
-    # admissions folded in), bracketed by CUDA events.
+    # steps without the flush: the warm figure.  A step is one sync_apply launch (the step's
+    # admissions, sync and apply_mask fused), bracketed by CUDA events.
     warm_steps = 0 if args.profile else min(args.steps, 128)
     total_steps = args.warmup + args.steps + warm_steps
-    plan = row_plan(rows, lengths, total_steps)
-    sid, pos = plan[:, :, 0], plan[:, :, 1]
-    history = torch.from_numpy(np.ascontiguousarray(tokens_np[sid, pos], dtype=np.int32)).to(device)
-    disallowed = (vocab - counts_h[sid, pos + 1]).sum(axis=0).astype(np.int64)  # per step, over rows
-    restarts = [np.flatnonzero(pos[:, k] == 0).tolist() for k in range(total_steps)]
-    # a request joining a slot is an admission (begin, base KG) folded into that step's launch
-    restart_t = [admissions_tensor(r, device) if r else None for r in restarts]
+    t0 = time.perf_counter()
+    if cfg.arrivals:
+        replay = versions_replay(args, workload, device, rank, total_steps, (blob, meta))
+    else:
+        replay = fixture_replay(args, workload, device, rank, total_steps, (blob, meta), (lo, hi))
+    sample_s = time.perf_counter() - t0
+    rows, history = replay.slots, replay.history
     prompt = [torch.full((rows,), k, dtype=torch.int32, device=device) for k in range(total_steps)]
     total = [torch.full((rows,), k + 1, dtype=torch.int32, device=device) for k in range(total_steps)]
-    slots = torch.arange(rows, dtype=torch.int32, device=device)
     gen = torch.Generator(device=device).manual_seed(7)
     dtype = getattr(torch, cfg.dtype)
     elt = torch.empty(0, dtype=dtype).element_size()
     logits = (torch.randn((rows, vocab), generator=gen, device=device) * 2.0).to(dtype)
     flush = torch.empty(512 * 1024 * 1024 // 4, dtype=torch.int32, device=device)
     engine = Engine(workload.index, workload.served, workload.syntax, rows, device_blob=(blob, meta), **options)
+    for name, edits in replay.versions:
+        engine.add_version(name, edits)
     engine.reset()
     stream = torch.cuda.current_stream(device).cuda_stream
     launches = 0
-    step_ms, apply_ms, warm_ms = [], [], []
+    step_ms, warm_ms = [], []
+    timed_rows = warm_rows = 0
     clocks = None
     if world > 1:
         dist.barrier()
@@ -448,78 +528,83 @@ def engine_arm(args) -> None:
             torch.cuda._sleep(HOLD_CYCLES_PER_STEP * (args.steps if timed else warm_steps))
         if not warm:
             flush.fill_(k)  # evict the logits and tables from L2 between steps
-        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        n = replay.live[k]
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
+        engine.sync_apply(replay.step_slots[k], history, prompt[k], total[k], logits[:n], stream=stream,
+                          admissions=replay.admissions[k])
         e1.record()
-        engine.sync_apply(slots, history, prompt[k], total[k], logits, stream=stream, admissions=restart_t[k])
-        e2.record()
-        launches += timed
         if timed:
-            step_ms.append((e0, e2))
-            apply_ms.append((e1, e2))
+            launches += 1
+            timed_rows += n
+            step_ms.append((e0, e1))
         elif warm:
-            warm_ms.append((e0, e2))
+            warm_rows += n
+            warm_ms.append((e0, e1))
     torch.cuda.synchronize()
     if clocks is not None:
         torch.cuda.nvtx.range_pop()
     clock_info = clocks.stop() if clocks else None
     errors = engine.errors()
-    apply_alone = None if args.profile else apply_leg(engine, logits, slots, flush, stream, args.steps, elt)
+    faults = engine.faults()
+    last_slots = replay.step_slots[total_steps - 1]
+    apply_alone = (None if args.profile else
+                   apply_leg(engine, logits[: len(last_slots)], last_slots, flush, stream, args.steps, elt))
     steps_ms = [a.elapsed_time(b) for a, b in step_ms]
-    applies = [a.elapsed_time(b) for a, b in apply_ms]
     warms = [a.elapsed_time(b) for a, b in warm_ms]
-    my_time = sum(steps_ms)
-    time_t = torch.tensor([my_time], dtype=torch.float64, device=device)
+    time_t = torch.tensor([sum(steps_ms)], dtype=torch.float64, device=device)
+    rows_t = torch.tensor([timed_rows], dtype=torch.float64, device=device)
     if world > 1:
         dist.all_reduce(time_t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(rows_t, op=dist.ReduceOp.SUM)
         dist.barrier()
     job_ms = float(time_t.item())
-    value = rows * world * args.steps / (job_ms / 1e3)
-    # roofline of the apply kernel
-    words = engine.words
-    timed_steps = range(args.warmup, total_steps)
-    # algorithmic bytes of one sync_apply launch: per row the state read+write and token
+    value = float(rows_t.item()) / (job_ms / 1e3)  # every rank's rows over the slowest rank's time
+    # algorithmic bytes of one launch: per row of the step the state read+write and token
     # (516 B), the bitmask read once (4 * words) and the -inf stores (elt * disallowed)
-    bytes_per_launch = [rows * (516 + 4 * words) + elt * int(disallowed[k]) for k in timed_steps]
-    avg_apply_s = statistics.mean(applies) / 1e3
-    achieved = statistics.mean(bytes_per_launch) / avg_apply_s / 1e9
+    words = engine.words
+    timed_steps = range(args.warmup, args.warmup + args.steps)
+    bytes_per_launch = [replay.live[k] * (516 + 4 * words) + elt * int(replay.disallowed[k]) for k in timed_steps]
+    achieved = statistics.mean(bytes_per_launch) / (statistics.mean(steps_ms) / 1e3) / 1e9
     peak, peak_kind = measured_peak()
     result = {
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "metric": metric_of(args.config, rows, vocab), "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": job_ms / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int32", "data": "synthetic",
         "config": workload_config(cfg, args.config, rows, vocab, lo, hi, world),
         "timed_region": "one sync_apply launch per step (admissions of joining requests, sync, apply_mask), "
                         "CUDA events on the launching stream, max over ranks",
-        "streams": streams_source,
+        "streams": replay.streams_source,
+        "rows_per_step": timed_rows / args.steps,
         "step_ms": {"median": statistics.median(steps_ms), "p90": sorted(steps_ms)[int(0.9 * len(steps_ms))],
                     "min": min(steps_ms), "max": max(steps_ms)},
-        "warm": ({"ms_per_step": statistics.median(warms), "value": rows * 1e3 / statistics.median(warms),
+        "warm": ({"ms_per_step": statistics.median(warms), "value": warm_rows / (sum(warms) / 1e3),
                   "unit": UNIT, "steps": len(warms),
                   "note": "the same replay continued without the L2 flush (median step, this rank)"}
                  if warms else None),
-        "kernel_ms": {"median": statistics.median(applies), "mean": statistics.mean(applies),
-                      "note": "the step's one launch (events around it), over the K timed steps"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_kind": peak_kind, **recorded_traffic(args.config, cfg.dtype, args.max_len),
                      "level": ("L2: the -inf writes land in the 126 MB L2 during the launch and reach HBM "
                                "when later writes evict them"),
-                     "kernel": f"step_apply_kernel<{elt}> ({cfg.dtype}): admissions + sync + mask + apply fused",
+                     "kernel": f"sync_apply_kernel<{elt}> ({cfg.dtype}): admissions + sync + mask + apply fused",
                      "algorithmic_bytes_per_launch": statistics.mean(bytes_per_launch)},
         "apply_mask_alone": apply_alone,
         "gpu_launches": launches,
         "clocks": clock_info,
         "errors": errors,
-        "setup_s": {"workload_build": build_s, "stream_sampling": sample_s},
+        "device_faults": faults,
+        "setup_s": {"workload_build": build_s, "streams": sample_s},
     }
+    if "add_version_ms" in replay.cpu:
+        result["versions"] = {k: replay.cpu[k] for k in ("requests", "edits_mean", "add_version_ms")}
     if not args.profile:
-        e2e = e2e_leg(engine, workload, history, restart_t, prompt, total, slots, rows, vocab, device,
-                      min(args.e2e_steps, total_steps), dtype)
+        e2e = e2e_leg(engine, replay, prompt, total, vocab, device, min(args.e2e_steps, total_steps), dtype)
         if world > 1:  # whole job: every rank's rows over the slowest rank's time
             e2e_t = torch.tensor([e2e["ms_per_step"]], dtype=torch.float64, device=device)
             dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
             e2e["ms_per_step"] = float(e2e_t.item())
-            e2e["value"] = rows * world * 1e3 / e2e["ms_per_step"]
+            e2e["value"] = e2e["rows_per_step"] * world * 1e3 / e2e["ms_per_step"]
             e2e["timing"] = "max over ranks of each rank's end-to-end time; value over all ranks' rows"
         result["e2e"] = e2e
     if world > 1:
@@ -528,8 +613,12 @@ def engine_arm(args) -> None:
     if rank != 0:
         return
     if world == 1 and not args.no_cpu and not args.profile:
-        expected = replay_masks(engine, tokens_np, lengths, rows, CPU_CHECK_STEPS)
-        result["cpu_baseline"] = cpu_baseline(workload, tokens_np, lengths, rows, expected, args.cpu_seconds)
+        if "add_version_ms" in replay.cpu:
+            result["cpu_baseline"] = versions_cpu_baseline(workload, replay, args.cpu_seconds)
+        else:
+            tokens_np, lengths = replay.cpu["tokens"], replay.cpu["lengths"]
+            expected = replay_masks(engine, tokens_np, lengths, rows, CPU_CHECK_STEPS)
+            result["cpu_baseline"] = cpu_baseline(workload, tokens_np, lengths, rows, expected, args.cpu_seconds)
     print(json.dumps(result), flush=True)
 
 
@@ -591,14 +680,17 @@ def apply_leg(engine, logits, slots, flush, stream, steps, elt):
             "note": "apply_mask alone on the replay's final masks, L2 flushed between launches"}
 
 
-def e2e_leg(engine, workload, history, restart_t, prompt, total, slots, rows, vocab, device, steps, dtype):
+def e2e_leg(engine, replay, prompt, total, vocab, device, steps, dtype):
     """The same steps through the public API with host buffers: each step copies its
-    tokens and logits in from pinned host memory and the masked logits back out.  The
-    copies run the way a serving loop overlaps them: step k + 1's inputs go up on a copy
+    tokens and its rows' logits in from pinned host memory and the masked logits back out.
+    The copies run the way a serving loop overlaps them: step k + 1's inputs go up on a copy
     stream while step k's masked logits come down on another (PCIe is full duplex), with
     two device buffers and events ordering each step's upload, step and download."""
     import torch
 
+    rows = replay.slots
+    history = replay.history
+    live = replay.live[:steps]
     host_tokens = history[:, :steps].t().contiguous().cpu().pin_memory()
     host_logits = (torch.randn((rows, vocab)) * 2.0).to(dtype).pin_memory()
     out_logits = torch.empty_like(host_logits).pin_memory()
@@ -618,32 +710,53 @@ def e2e_leg(engine, workload, history, restart_t, prompt, total, slots, rows, vo
     stepped = [torch.cuda.Event() for _ in range(steps)]
     downloaded = [None, None]
     for k in range(steps):
-        b = k & 1
+        b, n = k & 1, live[k]
         with torch.cuda.stream(up):
             if downloaded[b] is not None:
                 up.wait_event(downloaded[b])  # buffer b's previous result is on the host
             staging[b].copy_(host_tokens[k], non_blocking=True)
-            dev_logits[b].copy_(host_logits, non_blocking=True)
+            dev_logits[b][:n].copy_(host_logits[:n], non_blocking=True)
             uploaded[k].record(up)
         compute.wait_event(uploaded[k])
         dev_hist[:, k] = staging[b]
-        engine.sync_apply(slots, dev_hist, prompt[k], total[k], dev_logits[b], stream=stream,
-                          admissions=restart_t[k])
+        engine.sync_apply(replay.step_slots[k], dev_hist, prompt[k], total[k], dev_logits[b][:n], stream=stream,
+                          admissions=replay.admissions[k])
         stepped[k].record(compute)
         with torch.cuda.stream(down):
             down.wait_event(stepped[k])
-            out_logits.copy_(dev_logits[b], non_blocking=True)
+            out_logits[:n].copy_(dev_logits[b][:n], non_blocking=True)
             downloaded[b] = torch.cuda.Event()
             downloaded[b].record(down)
     compute.wait_stream(down)
     end.record(compute)
     torch.cuda.synchronize()
     ms = start.elapsed_time(end)
-    return {"value": rows * steps / (ms / 1e3), "unit": UNIT,
-            "h2d_bytes_per_step": rows * 4 + rows * vocab * host_logits.element_size(),
-            "d2h_bytes_per_step": rows * vocab * host_logits.element_size(),
-            "steps": steps, "ms_per_step": ms / steps,
+    element = host_logits.element_size()
+    mean_rows = sum(live) / steps
+    return {"value": sum(live) / (ms / 1e3), "unit": UNIT,
+            "h2d_bytes_per_step": int(rows * 4 + mean_rows * vocab * element),
+            "d2h_bytes_per_step": int(mean_rows * vocab * element),
+            "steps": steps, "ms_per_step": ms / steps, "rows_per_step": mean_rows,
             "copies": "inputs up and results down on two copy streams, overlapped across steps"}
+
+
+def versions_cpu_baseline(workload, replay, budget: float, workers: int = 4) -> dict:
+    """The oracle on the host cores for the versions configuration: `workers` processes, each
+    holding the KG versions of the requests it replays (a 10 M-edge oracle per process, so few
+    of them), every step one full row-step per worker; value = row-steps / wall seconds."""
+    names, edits, tokens = replay.cpu["names"], replay.cpu["edits"], replay.cpu["tokens"]
+    lengths = np.asarray(replay.cpu["lengths"], dtype=np.int32)
+    rows = min(len(names), 2 * workers)
+    chosen = {names[r]: edits[names[r]] for r in range(rows)}
+    leg = oracle_leg(workload, tokens[:rows], lengths[:rows], rows, steps=10_000, warmup=1, budget=budget,
+                     workers=workers, versions=chosen, row_versions=names[:rows])
+    value = leg["row_steps"] / leg["wall_s"] if leg["wall_s"] else 0.0
+    return {"value": value, "unit": UNIT, "cores": leg["workers"], "kind": "port",
+            "sample": (f"{leg['row_steps']} row-steps of {rows} requests, each under its own KG version (oracle "
+                       f"allowed set + masked logits + advance, V={workload.served.vocab_size:,}) over "
+                       f"{leg['steps']} steps on {leg['workers']} spawned workers; value = row-steps / wall seconds"),
+            "per_core_value": leg["row_steps"] / leg["busy_s"] if leg["busy_s"] else 0.0,
+            "oracle_setup_s": leg["setup_s"]}
 
 
 # ---------------------------------------------------------------------------------------
@@ -699,7 +812,7 @@ def reference_arm(args) -> None:
                      budget=REFERENCE_BUDGET_S)
     value = leg["row_steps"] / leg["wall_s"] if leg["wall_s"] else 0.0
     result = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": leg["steps"],
+        "impl": "reference", "metric": metric_of(args.config, rows, workload.served.vocab_size), "value": value, "unit": UNIT, "n_gpus": world, "steps": leg["steps"],
         "warmup": args.warmup, "ms_per_step": 1e3 * leg["wall_s"] / max(leg["steps"], 1), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int32", "data": "synthetic",
         "config": workload_config(cfg, args.config, rows, workload.served.vocab_size, lo, hi, world),
@@ -728,10 +841,15 @@ def engine_library_loaded() -> bool:
 
 def workload_config(cfg, number: int, rows: int, vocab: int, lo: int, hi: int, world: int) -> dict:
     """The `config` object of both arms' lines (the workload, not how an arm runs it)."""
+    if cfg.arrivals:
+        batching = (f"Poisson arrivals {cfg.arrivals:,.0f} req/s over {cfg.gpus} GPUs on a {cfg.step_ms} ms step "
+                    f"clock, output lengths Geometric(mean {cfg.mean_length:.0f}) capped at {hi}, up to {rows} live "
+                    f"rows/GPU, 0-{cfg.max_edits} seeded add/remove edits per request as its own KG version")
+    else:
+        batching = f"{rows} rows/GPU, stream lengths U[{lo},{hi}] replenished"
     return {
         "workload": (f"{cfg.name} (config {number}): {cfg.entities:,} entities, {cfg.relations} relations, "
-                     f"{cfg.triples:,} triples, V={vocab:,}, {rows} rows/GPU, stream lengths U[{lo},{hi}] "
-                     f"replenished, paths+committed_paths, escapes on"),
+                     f"{cfg.triples:,} triples, V={vocab:,}, {batching}, paths+committed_paths, escapes on"),
         "rows_per_gpu": rows, "vocab": vocab, "logits_dtype": cfg.dtype, "logits": f"{cfg.dtype} [rows, V] ~ N(0,2)",
         "l2": "GPU arm: flushed between steps (512 MiB write, outside the timed region)",
         "parallelism": f"rows sharded, {world} replica(s), index broadcast once over NCCL",

@@ -159,7 +159,24 @@ XG_API int xg_begin(XgEngine* engine, const int32_t* slots, int32_t count, int32
 /* Engine::set_reached (csrc/engine.cu:2840-2860): anchor rows (host int32, sorted; the
  * first 64 are kept). */
 XG_API int xg_set_reached(XgEngine* engine, int32_t slot, const int32_t* rows, int32_t count, void* stream);
-/* Engine::set_version (csrc/engine.cu:2864-2876): 0 = base KG, 1..versions. */
+/* Register one KG version while the engine runs (no blob rebuild); the reference registers
+ * versions only when an engine is built (src/xgraph/engine.py versions=, csrc/engine.cu:
+ * 477-491 reads them), with the same layout per version (src/xgraph/kgversions.py:14-21,
+ * 203-303): `count` sorted edited subjects (entity positions), each with its whole edge
+ * list in the new version, edges subjects' adjacency[i] .. adjacency[i + 1] (adjacency:
+ * count + 1 offsets from 0) of edge_relations / edge_objects (relation positions, object
+ * label rows), sorted by (relation, object row).  Host arrays, checked, then copied into the
+ * engine's version arena on `stream` (which grows, and frees its old buffers in stream
+ * order, when full).  *version receives the number slots select with xg_set_version or an
+ * admission: the lowest number a dropped version left free, else the next one.  Calls that
+ * add or drop versions must be ordered with the engine's kernels (one stream). */
+XG_API int xg_add_version(XgEngine* engine, const int32_t* subjects, int32_t count, const int64_t* adjacency,
+                          const int32_t* edge_relations, const int32_t* edge_objects, void* stream,
+                          int32_t* version);
+/* Forget a registered version: slots still selecting it read the base KG from the next launch
+ * on; its number is reused by a later xg_add_version. */
+XG_API int xg_drop_version(XgEngine* engine, int32_t version, void* stream);
+/* Engine::set_version (csrc/engine.cu:2864-2876): 0 = base KG, else a registered version. */
 XG_API int xg_set_version(XgEngine* engine, int32_t slot, int32_t version, void* stream);
 /* Engine::open_span (csrc/engine.cu:2955-2962): the slot starts inside a span. */
 XG_API int xg_open_span(XgEngine* engine, int32_t slot, void* stream);
@@ -244,7 +261,10 @@ XG_API int xg_apply_mask(XgEngine* engine, void* logits, int32_t dtype, int32_t 
  * the GPU (other streams, other engines, other threads) race on the array: order them.
  * The first call on a device looks the array's address up (cudaGetSymbolAddress, with the
  * engine's device current), which may also load the library's device code; make that first
- * call before any stream capture.  Same results as xg_apply_mask with the same arguments. */
+ * call before any stream capture.  The address is kept for the life of the process: after a
+ * cudaDeviceReset (which destroys the context holding the array) the process must reload the
+ * library before it calls this function again.  Same results as xg_apply_mask with the same
+ * arguments. */
 XG_API int xg_apply_mask_noalloc(XgEngine* engine, void* logits, int32_t dtype, int32_t rows, int32_t cols,
                                  int64_t row_stride, const int32_t* row_slots, const int32_t* local_pos,
                                  const int32_t* input_ids, void* stream);

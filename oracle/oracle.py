@@ -95,19 +95,28 @@ class OracleState:
 
 
 class _Graph:
-    """One KG version as plain edges (src/xgraph/oracle.py:344-364)."""
+    """One KG version's plain edges (src/xgraph/oracle.py:344-364), by subject.  A version
+    holds only the subjects its edits touch and reads every other subject from the base
+    graph: the same edge set as the reference's full copy, without copying it."""
 
-    def __init__(self, edges: set[tuple[str, str, int]]) -> None:
-        self.edges = frozenset(edges)
-        self.outgoing: dict[str, list[tuple[str, str, int]]] = {}
-        for edge in edges:
-            self.outgoing.setdefault(edge[0], []).append(edge)
-        self.degree = {s: len(v) for s, v in self.outgoing.items()}
-        self.has_triples = frozenset(self.degree)
+    def __init__(self, outgoing: dict[str, list[tuple[str, str, int]]], base: _Graph | None = None) -> None:
+        self._outgoing = outgoing
+        self._base = base
+
+    def edges_of(self, subject: str):
+        if self._base is not None and subject not in self._outgoing:
+            return self._base.edges_of(subject)
+        return self._outgoing.get(subject, ())
+
+    def degree(self, subject: str) -> int:
+        return len(self.edges_of(subject))
+
+    def has_triples(self, subject: str) -> bool:
+        return self.degree(subject) > 0
 
     def from_subjects(self, subjects):
         for s in subjects:
-            yield from self.outgoing.get(s, ())
+            yield from self.edges_of(s)
 
 
 @dataclass
@@ -192,7 +201,11 @@ class Oracle:
             for e in range(a, b):
                 edges.add((subject, relations.owner_ids[int(index.edge_relations[e])],
                            int(index.edge_objects[e])))
-        self._graphs: dict[str | None, _Graph] = {None: _Graph(edges)}
+        outgoing: dict[str, list[tuple[str, str, int]]] = {}
+        for edge in edges:
+            outgoing.setdefault(edge[0], []).append(edge)
+        base = _Graph(outgoing)
+        self._graphs: dict[str | None, _Graph] = {None: base}
         # A version replaces every edge of an edited pair (src/xgraph/oracle.py:588-624).
         writable = {owner for _, owner in self._relation_rows}
         for name, edits in (versions or {}).items():
@@ -200,14 +213,18 @@ class Oracle:
                 raise ValueError(f"a KG version needs a non-empty name, got {name!r}")
             edits = list(edits)
             pairs = {(s, r) for s, r, _ in edits}
-            kept = {(s, r, o) for s, r, o in edges if (s, r) not in pairs}
             added = {
                 (s, r, row)
                 for s, r, o in edits
                 if s in self._rows_of and r in writable
                 for row in self._rows_of.get(o, ())
             }
-            self._graphs[name] = _Graph(kept | added)
+            touched: dict[str, set[tuple[str, str, int]]] = {s: set() for s, _ in pairs}
+            for s in touched:  # the subject's edges outside the edited pairs
+                touched[s].update(e for e in base.edges_of(s) if (s, e[1]) not in pairs)
+            for edge in added:
+                touched[edge[0]].add(edge)
+            self._graphs[name] = _Graph({s: list(v) for s, v in touched.items()}, base)
         self._derivation = derivation or paths
         self._paths = paths
         self._bound_escapes = bound_escapes
@@ -354,11 +371,11 @@ class Oracle:
         graph = self._graph(state)
         separates = False
         if state.segment is Segment.SUBJECT:
-            separates = not self._answers_path(state) and any(e in graph.has_triples for e, _ in complete)
+            separates = not self._answers_path(state) and any(graph.has_triples(e) for e, _ in complete)
         elif state.segment is Segment.RELATION and complete:
             separates = not self._paths or (
                 len(state.written) - 1 < MAX_PATH_RELATIONS - 1
-                and any(e in graph.has_triples for e in self._frontier(state, state.typed))
+                and any(graph.has_triples(e) for e in self._frontier(state, state.typed))
             )
         escapes = self._escapes and state.typed is not None and self._may_escape(state)
         return _SpanContext(complete, closes, separates, escapes)
@@ -439,8 +456,8 @@ class Oracle:
             return ClosedSpan((label,), tuple(sorted(e for e, _ in rows)), (), True)
         objects = {row: entity for entity, row in rows}
         triples = {
-            (s, r, objects[o]) for s, r, o in self._graph(state).edges
-            if s in state.subjects and r in state.relations and o in objects
+            (s, r, objects[o]) for s, r, o in self._graph(state).from_subjects(state.subjects)
+            if r in state.relations and o in objects
         }
         return ClosedSpan((*state.written, label), (), tuple(sorted(triples)), True)
 
@@ -449,8 +466,8 @@ class Oracle:
         return self._bound_escapes or not bound
 
     def _best_connected(self, state: OracleState, rows) -> list[str]:
-        degree, sitelinks = self._graph(state).degree, self._sitelinks
-        ordered = sorted(rows, key=lambda p: (-sitelinks.get(p[0], 0), -degree.get(p[0], 0), p[1]))
+        graph, sitelinks = self._graph(state), self._sitelinks
+        ordered = sorted(rows, key=lambda p: (-sitelinks.get(p[0], 0), -graph.degree(p[0]), p[1]))
         return list(dict.fromkeys(e for e, _ in ordered))
 
     def _kept(self, ranks: dict[str, int]) -> dict[str, int]:
@@ -477,8 +494,8 @@ class Oracle:
     def _reached(self, state: OracleState, label) -> frozenset[int]:
         rows = {row for _, _, row in self._candidates(state, label, exact=True)}
         entities = {
-            self._entity_rows[o][1] for s, r, o in self._graph(state).edges
-            if s in state.subjects and r in state.relations and o in rows
+            self._entity_rows[o][1] for s, r, o in self._graph(state).from_subjects(state.subjects)
+            if r in state.relations and o in rows
         }
         reached = [row for row, (_, e) in enumerate(self._entity_rows) if e in entities]
         return frozenset(reached[:MAX_REACHED])
@@ -489,7 +506,7 @@ class Oracle:
         written = (*state.written, label)
         graph = self._graph(state)
         if state.segment is Segment.SUBJECT:
-            subjects = frozenset(e for e in items if e in graph.has_triples)
+            subjects = frozenset(e for e in items if graph.has_triples(e))
             ranks: dict[str, int] = {}
             if self._paths:
                 starts = self._best_connected(state, [(e, r) for e, r in candidates if e in subjects])

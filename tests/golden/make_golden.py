@@ -3,7 +3,7 @@
 Run in a container that holds the reference checkout (it is imported read-only,
 without writing bytecode):
 
-    python tests/golden/make_golden.py --reference /root/reference
+    python tests/golden/make_golden.py --reference <reference checkout>
 
 It writes three fixtures next to this script:
 
@@ -375,7 +375,7 @@ def index_arrays(root: Path, worlds: dict) -> dict:
 
 def main() -> None:
     parser = argparse.ArgumentParser()
-    parser.add_argument("--reference", type=Path, default=Path("/root/reference"))
+    parser.add_argument("--reference", type=Path, required=True, help="the reference checkout")
     args = parser.parse_args()
     os.environ["PYTHONDONTWRITEBYTECODE"] = "1"
     root = load_reference(args.reference)

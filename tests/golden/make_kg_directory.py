@@ -4,7 +4,7 @@ against it (src/xgraph/wikidata.py:859-1037).
 
 Run in a container that holds the reference checkout (imported read-only, no bytecode):
 
-    python tests/golden/make_kg_directory.py --reference /root/reference
+    python tests/golden/make_kg_directory.py --reference <reference checkout>
 
 From the rand_bpe world of worlds.json.gz it writes, next to this script:
   kg_directory_toy/        entity_labels.jsonl and relation_labels.jsonl (one JSON list
@@ -34,7 +34,7 @@ HERE = Path(__file__).resolve().parent
 
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__)
-    parser.add_argument("--reference", type=Path, default=Path("/root/reference"))
+    parser.add_argument("--reference", type=Path, required=True, help="the reference checkout")
     args = parser.parse_args()
     sys.dont_write_bytecode = True
     sys.path[:0] = [str(args.reference / "src"), str(args.reference)]

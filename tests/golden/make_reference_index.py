@@ -4,7 +4,7 @@ file per array plus kg-index.json, src/xgraph/index.py:731-903).
 
 Run in a container that holds the reference checkout (imported read-only, no bytecode):
 
-    python tests/golden/make_reference_index.py --reference /root/reference
+    python tests/golden/make_reference_index.py --reference <reference checkout>
 
 It writes reference_index_toy/ next to this script from worlds.json.gz.
 """
@@ -22,7 +22,7 @@ HERE = Path(__file__).resolve().parent
 
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__)
-    parser.add_argument("--reference", type=Path, default=Path("/root/reference"))
+    parser.add_argument("--reference", type=Path, required=True, help="the reference checkout")
     args = parser.parse_args()
     sys.dont_write_bytecode = True
     sys.path[:0] = [str(args.reference / "src"), str(args.reference)]

@@ -25,7 +25,9 @@ def admissions_of(sequences, *, on=True):
             for k, seq in enumerate(sequences)]
 
 
-def assert_same_slots(a, b, n):
+def assert_same_slots(a, b, n, *, same_numbers=True):
+    """Equal states, masks and memory counts (and KG version numbers, unless the engines
+    registered their versions in different orders)."""
     sa, sb = a.states_host(n), b.states_host(n)
     for field in sa:
         np.testing.assert_array_equal(sa[field], sb[field], field)
@@ -33,7 +35,9 @@ def assert_same_slots(a, b, n):
     b.fill_mask(n)
     np.testing.assert_array_equal(a.mask_host(n), b.mask_host(n))
     ma, mb = a.memory_host(n), b.memory_host(n)
-    np.testing.assert_array_equal(ma[:, :4], mb[:, :4])  # facts, reached, frontier, version
+    np.testing.assert_array_equal(ma[:, :3], mb[:, :3])  # facts, reached, frontier
+    if same_numbers:
+        np.testing.assert_array_equal(ma[:, 3], mb[:, 3])  # the KG version number
 
 
 @pytest.mark.parametrize("name", ["toy_derivation", "bpe_committed", "crowd_committed", "bytes_paths"])

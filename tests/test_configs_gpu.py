@@ -30,9 +30,9 @@ from tests.conftest import state_record
 
 pytestmark = pytest.mark.gpu
 
-# config, rows replayed, steps, rows checked against the oracle, masks sampled per checked row
-# (None: every step)
-CASES = [(1, 16, 64, 16, None), (2, 64, 160, 8, 3), (3, 256, 160, 6, 2), (4, 512, 128, 4, 2)]
+# config, rows replayed, steps, whole allowed sets checked against the oracle (None: every
+# row at every step); the state projections are checked at every step of every row
+CASES = [(1, 16, 64, None), (2, 64, 160, 48), (3, 256, 160, 64), (4, 512, 128, 48)]
 
 
 def projection(states: dict, row: int, view, need_sets: bool) -> dict:
@@ -49,8 +49,44 @@ def projection(states: dict, row: int, view, need_sets: bool) -> dict:
             "resolved": closed.resolved}
 
 
-@pytest.mark.parametrize("config, rows, steps, checked, per_row", CASES)
-def test_sync_apply_agrees_with_oracle_at_benchmark_config(config, rows, steps, checked, per_row):
+_ORACLE = {}
+
+
+def _oracle_init(index, served, syntax, options):
+    from oracle.oracle import Oracle
+
+    _ORACLE["oracle"] = Oracle(index, served, syntax, **options)
+
+
+def _allowed_after(job):
+    """The oracle's allowed set after `tokens` (a row's stream up to the checked step)."""
+    oracle = _ORACLE["oracle"]
+    state = oracle.initial_state()
+    for token in job:
+        state = oracle.advance(state, int(token))
+    return sorted(oracle.allowed(state))
+
+
+def oracle_allowed_sets(workload, syntax, options, prefixes: list, workers: int) -> list:
+    """The oracle's allowed sets after each token prefix, on spawned CPU workers (started
+    with spawn: a forked child of a CUDA process can hang)."""
+    import multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    with ctx.Pool(workers, initializer=_oracle_init,
+                  initargs=(workload.index, workload.served, syntax, options)) as pool:
+        return pool.map(_allowed_after, prefixes, chunksize=1)
+
+
+@pytest.mark.parametrize("config, rows, steps, sampled_sets", CASES)
+def test_sync_apply_agrees_with_oracle_at_benchmark_config(config, rows, steps, sampled_sets):
+    """GPU-sampled streams replayed through the fused step one token at a time.  Every row at
+    every step: each column keeps its logit bit for bit or becomes -inf, and the state
+    projection equals the oracle's after the same tokens (the oracle advanced over every
+    token of every row); whole allowed sets (the -inf pattern) equal the oracle's at seeded
+    (row, step) samples (every row and step at the toy size), computed on spawned workers."""
+    import os
+
     import torch
 
     from oracle.oracle import Oracle
@@ -64,13 +100,15 @@ def test_sync_apply_agrees_with_oracle_at_benchmark_config(config, rows, steps, 
     paths = options.get("paths", False)
     vocab = w.served.vocab_size
     sampler = Engine(w.index, w.served, syntax, rows, **options)
-    tokens, counts, _ = sample_streams(sampler, w.served, syntax, w.world, rows, steps, seed=100 + config)
+    tokens, _, _ = sample_streams(sampler, w.served, syntax, w.world, rows, steps, seed=100 + config)
     del sampler
 
     rng = np.random.default_rng(200 + config)
-    checked_rows = sorted(rng.choice(rows, size=checked, replace=False).tolist())
-    sampled = {r: set(range(steps + 1)) if per_row is None
-               else set(rng.choice(steps + 1, size=per_row, replace=False).tolist()) for r in checked_rows}
+    if sampled_sets is None:
+        sampled = {(r, k) for r in range(rows) for k in range(steps + 1)}
+    else:
+        picks = rng.choice(rows * (steps + 1), size=sampled_sets, replace=False).tolist()
+        sampled = {(p // (steps + 1), p % (steps + 1)) for p in picks}
 
     dtype = getattr(torch, w.config.dtype)
     bits = torch.int16 if dtype.itemsize == 2 else torch.int32
@@ -90,30 +128,30 @@ def test_sync_apply_agrees_with_oracle_at_benchmark_config(config, rows, steps, 
         blocked = torch.isneginf(logits)
         same = logits.view(bits) == source.view(bits)
         assert bool((blocked | same).all()), ("a column is neither its logit nor -inf", k)
-        kept = (~blocked).sum(1, dtype=torch.int32)
-        assert torch.equal(kept, counts[:, k]), ("kept columns differ from the sampling engine's mask", k)
         states = engine.states_host(rows)
-        states_at.append({name: values[checked_rows].copy() for name, values in states.items()})
+        states_at.append(states)
         spans += int((states["phase"] == 1).sum())
-        for r in checked_rows:
-            if k in sampled[r]:
-                kept_at[(r, k)] = np.flatnonzero((~blocked[r]).cpu().numpy())
-    assert engine.errors() == 0
+        for r in range(rows):
+            if (r, k) in sampled:
+                kept_at[(r, k)] = np.flatnonzero((~blocked[r]).cpu().numpy()).tolist()
+    assert engine.errors() == 0 and engine.faults() == 0
     assert spans > rows * steps // 10  # the replay spends real time inside spans
 
-    oracle = Oracle(w.index, w.served, syntax, **options)
     host_tokens = tokens.cpu().numpy()
-    for j, r in enumerate(checked_rows):
+    order = sorted(kept_at)
+    workers = max(1, min(os.cpu_count() or 1, 8 if config >= 4 else 16, len(order)))
+    allowed = oracle_allowed_sets(w, syntax, options, [host_tokens[r, :k] for r, k in order], workers)
+    for (r, k), want in zip(order, allowed, strict=True):
+        assert kept_at[(r, k)] == want, ("allowed set", config, r, k)
+
+    oracle = Oracle(w.index, w.served, syntax, **options)
+    for r in range(rows):
         state = oracle.initial_state()
         for k in range(steps + 1):
             where = (config, r, k)
             expected = expected_state(state_record(state), w.index, syntax)
             need_sets = expected["phase"] == 1 and expected.get("segment", 0) != 0 and not paths
-            got = projection({name: values[j: j + 1] for name, values in states_at[k].items()}, 0, w.index,
-                             need_sets)
-            assert_agrees(expected, got, paths, where)
-            if (r, k) in kept_at:
-                assert set(kept_at[(r, k)].tolist()) == set(oracle.allowed(state)), ("allowed set", where)
+            assert_agrees(expected, projection(states_at[k], r, w.index, need_sets), paths, where)
             if k < steps:
                 state = oracle.advance(state, int(host_tokens[r, k]))
 

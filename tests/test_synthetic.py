@@ -4,6 +4,8 @@ token by token with the oracle."""
 
 from __future__ import annotations
 
+import itertools
+
 import numpy as np
 
 
@@ -107,7 +109,7 @@ def test_request_edits_are_pair_replacements_the_versions_apply():
         expected = {row for o in objects for row in rows_of.get(entity_at[o], [])}
         assert set(view.object_rows(s, r)) == expected, (s, r)
     relation_id = [r for r, _ in world.relations]
-    for (s, r), objects in list(pairs.items())[:200]:
+    for (s, r), objects in list(itertools.islice(pairs.items(), 200)):
         sid, rid = world.entities[s][0], relation_id[r]
         if (sid, rid) in touched or not rows_of.get(s):
             continue
@@ -227,3 +229,29 @@ def test_seam_masks_equal_the_oracle_with_per_request_kg_versions():
                 assert unpack(words, served.vocab_size) == set(oracle.allowed(state)), (r, k)
             if k < steps:
                 state = oracle.advance(state, int(host_tokens[r, k]))
+
+
+def test_arrival_schedule_serves_every_request_in_ragged_batches():
+    """The versions configuration's continuous batching: Poisson arrivals, geometric lengths,
+    first come first served into at most `rows` slots; a slot is never shared, a request
+    holds its slot for exactly its length, and the batch starts full."""
+    from xgraph_b200.synthetic import CONFIGS, arrival_schedule
+
+    cfg = CONFIGS[5]
+    steps = 400
+    a = arrival_schedule(cfg, steps, seed=5)
+    assert len(a.live[0]) == cfg.rows and all(len(live) <= cfg.rows for live in a.live)
+    owner = {}
+    for k in range(steps):
+        for slot, r in a.admitted[k]:
+            assert a.slot[r] == slot and a.start[r] == k >= a.arrival[r]
+        for slot in a.live[k]:
+            r = next(r for r in range(len(a.slot)) if a.slot[r] == slot and a.start[r] <= k < a.start[r] + a.length[r])
+            owner.setdefault((slot, r), 0)
+            owner[(slot, r)] += 1
+    for (slot, r), held in owner.items():
+        assert held == min(a.length[r], steps - a.start[r])
+    lengths = np.array(a.length)
+    assert 150 < lengths.mean() < 350 and lengths.max() <= cfg.lengths[1]
+    rate = (len(a.arrival) - cfg.rows) / (steps - 1)
+    assert 0.35 < rate < 0.65  # 2,000 req/s over 8 GPUs at a 2 ms step: 0.5 per step

@@ -140,7 +140,10 @@ struct Tables {
   // it (closer at offset 0, separator after it, escape after that).  Null when the
   // delimiters are too long for 16 nibbles; the CSR lists then serve.
   const uint64_t* dstep;
-  const int32_t* ver_off;
+  // KG versions: version v (1..versions) owns the sorted edited subjects
+  // ver_subj[ver_range[2v - 2] .. ver_range[2v - 1]); subject i's whole edge list is
+  // ver_edge_*[ver_adj[i] .. ver_adj[i + 1]) (an empty range: v reads the base KG).
+  const int32_t* ver_range;
   const int32_t* ver_subj;
   const int32_t* ver_adj;
   const int32_t* ver_edge_rel;
@@ -538,7 +541,7 @@ struct Edges {
 // else the base CSR slice (src/xgraph/kgversions.py:14-21, the layout both share).
 XG_COLD Edges edges_of(const Tables& t, int32_t version, int32_t e) {
   if (version > 0) {
-    const int32_t a = t.ver_off[version - 1], b = t.ver_off[version];
+    const int32_t a = t.ver_range[2 * version - 2], b = t.ver_range[2 * version - 1];
     const int32_t at = lower_index(t.ver_subj, a, b, e);
     if (at < b && t.ver_subj[at] == e) {
       const int32_t s = t.ver_adj[at], f = t.ver_adj[at + 1];

@@ -12,10 +12,12 @@
 // state changes, so apply_mask is a single bandwidth kernel.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include "core.cuh"
 
@@ -665,6 +667,29 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch
 
 using namespace xg;
 
+// One KG version as the host keeps it (so that the device arena can be rebuilt): its
+// sorted edited subjects, their adjacency offsets (count + 1, from 0) and edges.
+struct HostVersion {
+  std::vector<int32_t> subjects, adjacency, relations, objects;
+  bool live = false;
+};
+
+// The engine's KG versions on the device, outside the index blob so that versions can be
+// added and dropped between steps: version id v owns subjects [range[2v-2], range[2v-1])
+// of `subjects`, whose edges `adjacency` (absolute offsets, one past the last subject too)
+// points into `relations` / `objects`.  Versions are appended; a dropped version's space is
+// reclaimed when the arena is next rebuilt (on growth), from the host copies.
+struct VersionArena {
+  int32_t* range = nullptr;
+  int32_t* subjects = nullptr;
+  int32_t* adjacency = nullptr;
+  int32_t* relations = nullptr;
+  int32_t* objects = nullptr;
+  int64_t id_cap = 0, subject_cap = 0, edge_cap = 0;
+  int64_t subjects_used = 0, edges_used = 0;
+  std::vector<HostVersion> versions;  // id - 1
+};
+
 struct XgEngine {
   int device = 0;
   int sm_count = 148;
@@ -685,6 +710,7 @@ struct XgEngine {
   int32_t* faults = nullptr;      // device-side faults (xg_faults)
   XgAdmission* admissions = nullptr;  // staging of host admissions: max_sequences entries
   size_t composed_bytes = 0;      // sync_apply's dynamic shared memory: one mask row
+  VersionArena arena;
   Tables t{};
 };
 
@@ -764,6 +790,140 @@ int fill_delimiter_offsets(Delim& d, const char* blob, int64_t offset, const voi
   return XG_OK;
 }
 
+void bind_versions(XgEngine* e) {
+  const VersionArena& a = e->arena;
+  e->t.ver_range = a.range;
+  e->t.ver_subj = a.subjects;
+  e->t.ver_adj = a.adjacency;
+  e->t.ver_edge_rel = a.relations;
+  e->t.ver_edge_obj = a.objects;
+  e->t.versions = static_cast<int32_t>(a.versions.size());
+}
+
+// Append live version `id` at the arena's end (capacity checked by the caller).
+int place_version(XgEngine* e, int32_t id, cudaStream_t stream) {
+  VersionArena& a = e->arena;
+  const HostVersion& v = a.versions[id - 1];
+  const int64_t n = static_cast<int64_t>(v.subjects.size()), m = static_cast<int64_t>(v.relations.size());
+  std::vector<int32_t> absolute(v.adjacency.size());
+  for (size_t i = 0; i < absolute.size(); ++i) absolute[i] = static_cast<int32_t>(a.edges_used + v.adjacency[i]);
+  const int32_t range[2] = {static_cast<int32_t>(a.subjects_used), static_cast<int32_t>(a.subjects_used + n)};
+  // pageable sources: each copy is staged before the call returns, so the temporaries may go
+  if (n) XG_CUDA(cudaMemcpyAsync(a.subjects + a.subjects_used, v.subjects.data(), n * 4, cudaMemcpyHostToDevice, stream),
+                 "version upload");
+  XG_CUDA(cudaMemcpyAsync(a.adjacency + a.subjects_used, absolute.data(), (n + 1) * 4, cudaMemcpyHostToDevice, stream),
+          "version upload");
+  if (m) {
+    XG_CUDA(cudaMemcpyAsync(a.relations + a.edges_used, v.relations.data(), m * 4, cudaMemcpyHostToDevice, stream),
+            "version upload");
+    XG_CUDA(cudaMemcpyAsync(a.objects + a.edges_used, v.objects.data(), m * 4, cudaMemcpyHostToDevice, stream),
+            "version upload");
+  }
+  XG_CUDA(cudaMemcpyAsync(a.range + 2 * (id - 1), range, sizeof(range), cudaMemcpyHostToDevice, stream), "version upload");
+  a.subjects_used += n;
+  a.edges_used += m;
+  return XG_OK;
+}
+
+// A fresh arena holding every live version contiguously, with room for at least `ids`
+// versions, `subjects` subjects and `edges` edges; the old buffers are freed in stream
+// order (after the work already queued on `stream` that may read them).
+int rebuild_versions(XgEngine* e, int64_t ids, int64_t subjects, int64_t edges, cudaStream_t stream) {
+  VersionArena& a = e->arena;
+  VersionArena fresh;
+  fresh.versions.swap(a.versions);
+  int64_t live_subjects = 0, live_edges = 0;
+  for (const HostVersion& v : fresh.versions) {
+    if (!v.live) continue;
+    live_subjects += static_cast<int64_t>(v.subjects.size());
+    live_edges += static_cast<int64_t>(v.relations.size());
+  }
+  fresh.id_cap = std::max<int64_t>({16, ids, 2 * a.id_cap});
+  fresh.subject_cap = std::max<int64_t>({1024, subjects, live_subjects, 2 * a.subject_cap});
+  fresh.edge_cap = std::max<int64_t>({4096, edges, live_edges, 2 * a.edge_cap});
+  if (fresh.subject_cap + 1 > 0x7fffffff || fresh.edge_cap > 0x7fffffff)
+    return fail(XG_EINVAL, "KG versions: more than 2^31 edited subjects or edges");
+  cudaError_t err = cudaSuccess;
+  auto alloc = [&](int32_t** p, int64_t count) {
+    if (err == cudaSuccess) err = cudaMallocAsync(reinterpret_cast<void**>(p), count * sizeof(int32_t), stream);
+  };
+  alloc(&fresh.range, 2 * fresh.id_cap);
+  alloc(&fresh.subjects, fresh.subject_cap);
+  alloc(&fresh.adjacency, fresh.subject_cap + 1);
+  alloc(&fresh.relations, fresh.edge_cap);
+  alloc(&fresh.objects, fresh.edge_cap);
+  if (err == cudaSuccess) err = cudaMemsetAsync(fresh.range, 0, 2 * fresh.id_cap * sizeof(int32_t), stream);
+  if (err == cudaSuccess) err = cudaMemsetAsync(fresh.adjacency, 0, sizeof(int32_t), stream);
+  if (err != cudaSuccess) {
+    for (int32_t* p : {fresh.range, fresh.subjects, fresh.adjacency, fresh.relations, fresh.objects})
+      if (p) cudaFreeAsync(p, stream);
+    a.versions.swap(fresh.versions);
+    cudaGetLastError();
+    return fail(XG_ENOMEM, std::string("KG version arena: ") + cudaGetErrorString(err));
+  }
+  std::swap(a, fresh);  // `fresh` now holds the old buffers
+  for (int32_t id = 1; id <= static_cast<int32_t>(a.versions.size()); ++id)
+    if (a.versions[id - 1].live)
+      if (int rc = place_version(e, id, stream)) return rc;
+  for (int32_t* p : {fresh.range, fresh.subjects, fresh.adjacency, fresh.relations, fresh.objects})
+    if (p) cudaFreeAsync(p, stream);
+  bind_versions(e);
+  return XG_OK;
+}
+
+// Host checks of one version's arrays (the layout build_kg_versions writes).
+int check_version(const XgEngine* e, const int32_t* subjects, int32_t count, const int64_t* adjacency,
+                  const int32_t* relations, const int32_t* objects) {
+  if (count < 0 || (count > 0 && (!subjects || !adjacency))) return fail(XG_EINVAL, "KG version: null arrays");
+  if (count > 0 && adjacency[0] != 0) return fail(XG_EINVAL, "KG version: adjacency must start at 0");
+  if (count > 0 && adjacency[count] > 0 && (!relations || !objects)) return fail(XG_EINVAL, "KG version: null edges");
+  for (int32_t i = 0; i < count; ++i) {
+    if (subjects[i] < 0 || subjects[i] >= e->layout.entities || (i > 0 && subjects[i] <= subjects[i - 1]))
+      return fail(XG_EINVAL, "KG version: subjects must be sorted, distinct entity positions");
+    if (adjacency[i + 1] < adjacency[i]) return fail(XG_EINVAL, "KG version: adjacency must not decrease");
+    for (int64_t k = adjacency[i]; k < adjacency[i + 1]; ++k) {
+      if (relations[k] < 0 || relations[k] >= e->layout.relations || objects[k] < 0 ||
+          objects[k] >= e->layout.entity_rows)
+        return fail(XG_EINVAL, "KG version: an edge names no relation or label row of the index");
+      if (k > adjacency[i] && (relations[k] < relations[k - 1] ||
+                               (relations[k] == relations[k - 1] && objects[k] <= objects[k - 1])))
+        return fail(XG_EINVAL, "KG version: a subject's edges must be sorted by (relation, object row), distinct");
+    }
+  }
+  if (count > 0 && adjacency[count] > 0x7fffffff) return fail(XG_EINVAL, "KG version: too many edges");
+  return XG_OK;
+}
+
+// Register a version (host arrays): the lowest dropped id is reused, else a new one.
+int add_version(XgEngine* e, const int32_t* subjects, int32_t count, const int64_t* adjacency,
+                const int32_t* relations, const int32_t* objects, cudaStream_t stream, int32_t* out) {
+  if (int rc = check_version(e, subjects, count, adjacency, relations, objects)) return rc;
+  VersionArena& a = e->arena;
+  int32_t id = 1;
+  while (id <= static_cast<int32_t>(a.versions.size()) && a.versions[id - 1].live) ++id;
+  if (id > static_cast<int32_t>(a.versions.size())) a.versions.emplace_back();
+  HostVersion& v = a.versions[id - 1];
+  const int64_t edges = count > 0 ? adjacency[count] : 0;
+  v.subjects.assign(subjects, subjects + count);
+  v.adjacency.resize(static_cast<size_t>(count) + 1);
+  for (int32_t i = 0; i <= count; ++i) v.adjacency[i] = count > 0 ? static_cast<int32_t>(adjacency[i]) : 0;
+  v.relations.assign(relations, relations + edges);
+  v.objects.assign(objects, objects + edges);
+  v.live = true;
+  int rc = XG_OK;
+  if (id > a.id_cap || a.subjects_used + count + 1 > a.subject_cap || a.edges_used + edges > a.edge_cap)
+    rc = rebuild_versions(e, id, a.subjects_used + count + 1, a.edges_used + edges, stream);
+  else
+    rc = place_version(e, id, stream);
+  if (rc) {
+    v = HostVersion{};
+    return rc;
+  }
+  bind_versions(e);
+  *out = id;
+  return XG_OK;
+}
+
 void bind_tables(XgEngine* e) {
   const XgLayout& l = e->layout;
   const char* b = e->blob;
@@ -801,12 +961,7 @@ void bind_tables(XgEngine* e) {
                       at<int32_t>(b, l.separator_next), l.separator_len};
   t.escape = Delim{at<int32_t>(b, l.escape_off), at<int32_t>(b, l.escape_tok), at<int32_t>(b, l.escape_next), l.escape_len};
   t.dstep = at<uint64_t>(b, l.dstep);
-  t.ver_off = at<int32_t>(b, l.ver_off);
-  t.ver_subj = at<int32_t>(b, l.ver_subj);
-  t.ver_adj = at<int32_t>(b, l.ver_adj);
-  t.ver_edge_rel = at<int32_t>(b, l.ver_edge_rel);
-  t.ver_edge_obj = at<int32_t>(b, l.ver_edge_obj);
-  t.versions = l.versions;
+  bind_versions(e);
   t.vocab = l.vocab;
   t.words = l.words;
   t.words_padded = l.words_padded;
@@ -844,7 +999,48 @@ void release(XgEngine* e) {
   cudaFree(e->draft_scratch);
   cudaFree(e->faults);
   cudaFree(e->admissions);
+  for (void* p : {static_cast<void*>(e->arena.range), static_cast<void*>(e->arena.subjects),
+                  static_cast<void*>(e->arena.adjacency), static_cast<void*>(e->arena.relations),
+                  static_cast<void*>(e->arena.objects)})
+    cudaFree(p);
   delete e;
+}
+
+// The versions packed in the index blob become the arena's first ids (1..versions).
+int load_blob_versions(XgEngine* e, const void* host_blob) {
+  const XgLayout& l = e->layout;
+  auto read = [&](int64_t offset, int64_t count, std::vector<int32_t>& out) -> int {
+    out.resize(static_cast<size_t>(count));
+    if (count == 0) return XG_OK;
+    if (host_blob) {
+      std::memcpy(out.data(), static_cast<const char*>(host_blob) + offset, count * sizeof(int32_t));
+      return XG_OK;
+    }
+    XG_CUDA(cudaMemcpy(out.data(), e->blob + offset, count * sizeof(int32_t), cudaMemcpyDeviceToHost), "version read");
+    return XG_OK;
+  };
+  std::vector<int32_t> off, subj, adj, rel, obj;
+  if (int rc = read(l.ver_off, static_cast<int64_t>(l.versions) + 1, off)) return rc;
+  const int64_t subjects = off.empty() ? 0 : off.back();
+  if (int rc = read(l.ver_subj, subjects, subj)) return rc;
+  if (int rc = read(l.ver_adj, subjects + 1, adj)) return rc;
+  const int64_t edges = adj.empty() ? 0 : adj.back();
+  if (int rc = read(l.ver_edge_rel, edges, rel)) return rc;
+  if (int rc = read(l.ver_edge_obj, edges, obj)) return rc;
+  VersionArena& a = e->arena;
+  a.versions.assign(static_cast<size_t>(l.versions), HostVersion{});
+  for (int32_t v = 0; v < l.versions; ++v) {
+    HostVersion& h = a.versions[v];
+    const int32_t s0 = off[v], s1 = off[v + 1];
+    if (s0 < 0 || s1 < s0 || s1 > subjects) return fail(XG_EINVAL, "layout: version offsets out of order");
+    h.subjects.assign(subj.begin() + s0, subj.begin() + s1);
+    h.adjacency.resize(static_cast<size_t>(s1 - s0) + 1);
+    for (int32_t i = s0; i <= s1; ++i) h.adjacency[i - s0] = adj[i] - adj[s0];
+    h.relations.assign(rel.begin() + adj[s0], rel.begin() + adj[s1]);
+    h.objects.assign(obj.begin() + adj[s0], obj.begin() + adj[s1]);
+    h.live = true;
+  }
+  return rebuild_versions(e, l.versions, subjects + 1, edges, nullptr);
 }
 
 int create(const void* blob, bool on_device, const XgLayout* layout, const XgOptions* options,
@@ -893,6 +1089,10 @@ int create(const void* blob, bool on_device, const XgLayout* layout, const XgOpt
     return cuda_fail(err, "engine upload");
   }
   bind_tables(e);
+  if (int rc = load_blob_versions(e, on_device ? nullptr : blob)) {
+    release(e);
+    return rc;
+  }
   e->composed_bytes = static_cast<size_t>(layout->words_padded) * sizeof(uint32_t);
   for (const void* kernel : {reinterpret_cast<const void*>(sync_apply_kernel<4>),
                              reinterpret_cast<const void*>(sync_apply_kernel<2>)}) {
@@ -1008,8 +1208,8 @@ int stage_admissions(XgEngine* e, const XgAdmission* admissions, int32_t count, 
     for (int32_t k = 0; k < j; ++k)
       if (admissions[k].slot == a.slot) return fail(XG_EINVAL, "two admissions name slot " + std::to_string(a.slot));
     if (a.on != 0 && a.on != 1) return fail(XG_EINVAL, "admission `on` must be 0 or 1");
-    if (a.version < 0 || a.version > e->layout.versions)
-      return fail(XG_EINVAL, "KG version must be between 0 and " + std::to_string(e->layout.versions) + ", got " +
+    if (a.version < 0 || a.version > e->t.versions || (a.version > 0 && !e->arena.versions[a.version - 1].live))
+      return fail(XG_EINVAL, "KG version must be 0 or a registered version up to " + std::to_string(e->t.versions) + ", got " +
                                  std::to_string(a.version));
     if (a.anchor_count < 0 || a.anchor_count > XG_MAX_ANCHORS)
       return fail(XG_EINVAL, "an admission holds 0 to 64 anchor rows");
@@ -1105,8 +1305,8 @@ int xg_set_reached(XgEngine* e, int32_t slot, const int32_t* rows, int32_t count
 int xg_set_version(XgEngine* e, int32_t slot, int32_t version, void* stream) {
   if (!e) return fail(XG_EINVAL, "null engine");
   if (int rc = check_slot(e, slot)) return rc;
-  if (version < 0 || version > e->layout.versions)
-    return fail(XG_EINVAL, "KG version must be between 0 and " + std::to_string(e->layout.versions) + ", got " +
+  if (version < 0 || version > e->t.versions || (version > 0 && !e->arena.versions[version - 1].live))
+    return fail(XG_EINVAL, "KG version must be 0 or a registered version up to " + std::to_string(e->t.versions) + ", got " +
                                std::to_string(version));
   SlotArgs a{};
   a.slot = slot;
@@ -1268,6 +1468,24 @@ int xg_admit(XgEngine* e, const XgAdmission* admissions, int32_t count, int32_t 
   if (int rc = stage_admissions(e, admissions, count, on_host, stream, &admit)) return rc;
   if (count == 0) return XG_OK;
   return launch_admit(e, admit, count, stream);
+}
+
+int xg_add_version(XgEngine* e, const int32_t* subjects, int32_t count, const int64_t* adjacency,
+                   const int32_t* edge_relations, const int32_t* edge_objects, void* stream, int32_t* version) {
+  if (!e || !version) return fail(XG_EINVAL, "null argument");
+  return add_version(e, subjects, count, adjacency, edge_relations, edge_objects, as_stream(stream), version);
+}
+
+int xg_drop_version(XgEngine* e, int32_t version, void* stream) {
+  if (!e) return fail(XG_EINVAL, "null engine");
+  VersionArena& a = e->arena;
+  if (version < 1 || version > static_cast<int32_t>(a.versions.size()) || !a.versions[version - 1].live)
+    return fail(XG_EINVAL, "no registered KG version " + std::to_string(version));
+  static const int32_t empty[2] = {0, 0};
+  XG_CUDA(cudaMemcpyAsync(a.range + 2 * (version - 1), empty, sizeof(empty), cudaMemcpyHostToDevice, as_stream(stream)),
+          "version drop");
+  a.versions[version - 1] = HostVersion{};
+  return XG_OK;
 }
 
 int xg_faults(XgEngine* e, int32_t* out) {

@@ -23,6 +23,7 @@ struct SeamEngine {
   std::vector<int32_t> cursors, active;
   std::vector<Key> top;
   std::vector<int32_t> scratch;
+  std::vector<int32_t> ver_range;  // the blob's cumulative version offsets as (begin, end) pairs
   Tables t{};
 };
 
@@ -92,7 +93,13 @@ SeamEngine* xgs_create(const void* blob, const XgLayout* l, const XgOptions* o, 
     for (int32_t k = 0; k < 17; ++k) d->at[k] = k <= d->len ? d->off[k] : 0;
   }
   t.dstep = at<uint64_t>(b, l->dstep);
-  t.ver_off = at<int32_t>(b, l->ver_off);
+  const int32_t* ver_off = at<int32_t>(b, l->ver_off);
+  for (int32_t v = 0; v < l->versions; ++v) {
+    e->ver_range.push_back(ver_off[v]);
+    e->ver_range.push_back(ver_off[v + 1]);
+  }
+  e->ver_range.push_back(0);  // never empty
+  t.ver_range = e->ver_range.data();
   t.ver_subj = at<int32_t>(b, l->ver_subj);
   t.ver_adj = at<int32_t>(b, l->ver_adj);
   t.ver_edge_rel = at<int32_t>(b, l->ver_edge_rel);

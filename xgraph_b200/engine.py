@@ -106,6 +106,8 @@ def load_library(path: Path = LIBRARY):
         "xg_sync_apply_admit": ([p, p, i32, p, i64, i64, p, p, i64, p, i32, i32, i64, p, i32, i32, p], ctypes.c_int),
         "xg_admit": ([p, p, i32, i32, p], ctypes.c_int),
         "xg_faults": ([p, ctypes.POINTER(i32)], ctypes.c_int),
+        "xg_add_version": ([p, p, i32, p, p, p, p, ctypes.POINTER(i32)], ctypes.c_int),
+        "xg_drop_version": ([p, i32, p], ctypes.c_int),
         "xg_build_adjacency": ([p, p, p, i64, p, p, i32, i32, p, i32, i64, p, p, p, p, p, p], ctypes.c_int),
     }
     for name, (args, res) in sigs.items():
@@ -223,6 +225,8 @@ class Engine:
         if versions is not None:
             versions.check_base(index)
         self._index, self._versions = index, versions
+        self._added: dict[str, tuple[int, object]] = {}  # versions registered while running: name -> (number, view data)
+        self._builder = None
         self._entity_index: dict[str, int] | None = None
         self._tables = pack_tables(
             index, tokenizer, syntax, escapes=escapes, versions=versions,
@@ -311,11 +315,52 @@ class Engine:
         return np.ascontiguousarray(found[:MAX_REACHED], dtype=np.int32)
 
     def _version_number(self, version: str | None) -> int:
-        if self._versions is not None:
+        if version is None:
+            return 0
+        if version in self._added:
+            return self._added[version][0]
+        if self._versions is not None and version in self._versions.names:
             return self._versions.number(version)
-        if version is not None:
-            raise ValueError(f"no KG version {version!r}; the engine has none registered")
-        return 0
+        raise ValueError(f"no KG version {version!r}; the registered ones are {self.version_names()}")
+
+    def version_names(self) -> list[str]:
+        """Every KG version slots may select: those the engine was built with, then those
+        added since (and not dropped)."""
+        return [*(self._versions.names if self._versions is not None else ()), *self._added]
+
+    def add_version(self, name: str, edits, stream: int = 0) -> int:
+        """Register a KG version while the engine runs: the base with every edited (subject,
+        relation) pair's objects replaced (the reference's pair-replacement edits,
+        src/xgraph/kgversions.py:203-303), copied into the engine's device version arena on
+        `stream` without rebuilding the shared tables.  Returns the version's number; slots
+        then select it by name (set_version, Admission.version)."""
+        from .kgversions import KGVersions, VersionBuilder
+
+        if not isinstance(name, str) or not name:
+            raise ValueError(f"a KG version needs a non-empty name, got {name!r}")
+        if name in self._added or (self._versions is not None and name in self._versions.names):
+            raise ValueError(f"KG version {name!r} is registered already")
+        if self._builder is None:
+            self._builder = VersionBuilder(self._index)
+        subjects, adjacency, relations, objects, stats = self._builder.overlay(name, edits)
+        number = ctypes.c_int32()
+        _check(self._lib.xg_add_version(
+            self._handle, subjects.ctypes.data_as(ctypes.c_void_p), len(subjects),
+            adjacency.ctypes.data_as(ctypes.c_void_p), relations.ctypes.data_as(ctypes.c_void_p),
+            objects.ctypes.data_as(ctypes.c_void_p), _stream(stream), ctypes.byref(number)))
+        single = KGVersions(names=(name,), stats=(stats,), offsets=np.array([0, len(subjects)], dtype=np.int64),
+                            subjects=subjects, adjacency=adjacency, edge_relations=relations,
+                            edge_objects=objects, base_fingerprint=self._index.base_fingerprint)
+        self._added[name] = (int(number.value), single)
+        return int(number.value)
+
+    def drop_version(self, name: str, stream: int = 0) -> None:
+        """Forget a version added with add_version (its number is reused later); slots still
+        selecting it read the base KG from the next step on."""
+        if name not in self._added:
+            raise ValueError(f"no KG version {name!r} was added to this engine")
+        _check(self._lib.xg_drop_version(self._handle, self._added[name][0], _stream(stream)))
+        del self._added[name]
 
     def admission_records(self, admissions: Iterable[Admission]) -> np.ndarray:
         """XgAdmission records [n, ADMISSION_INTS] int32 for these admissions (anchor
@@ -380,8 +425,10 @@ class Engine:
     def view(self, version: str | None):
         if version is None:
             return self._index
-        if self._versions is None:
-            raise ValueError(f"no KG version {version!r}; the engine has none registered")
+        if version in self._added:
+            return self._added[version][1].view(self._index, version)
+        if self._versions is None or version not in self._versions.names:
+            raise ValueError(f"no KG version {version!r}; the registered ones are {self.version_names()}")
         return self._versions.view(self._index, version)
 
     def advance(self, tokens, stream: int = 0) -> None:

@@ -102,77 +102,94 @@ class VersionView:
         return [int(o) for o in objects[x:y]]
 
 
-def build_kg_versions(index: KGIndex, versions: Mapping[str, Iterable[Edit]]) -> KGVersions:
-    named = {
-        name: [(str(s), str(r), None if o is None else str(o)) for s, r, o in edits]
-        for name, edits in versions.items()
-    }
-    for name in named:
-        if not isinstance(name, str) or not name:
-            raise ValueError(f"a KG version needs a non-empty name, got {name!r}")
-    entity_at = {e: n for n, e in enumerate(index.labels.owner_ids)}
-    relation_at = {r: n for n, r in enumerate(index.relations.owner_ids)}
-    owners = np.asarray(index.labels.owners, dtype=np.int64)
-    row_count = np.bincount(owners, minlength=len(index.labels.owner_ids))
-    order = np.argsort(owners, kind="stable")
-    row_start = np.zeros(len(row_count) + 1, dtype=np.int64)
-    np.cumsum(row_count, out=row_start[1:])
-    writable = set(np.unique(np.asarray(index.relations.owners)).tolist())
+class VersionBuilder:
+    """Builds versions of one KG index, one at a time (the lookups from ids to positions and
+    label rows are made once): each is the base with every edited (subject, relation) pair's
+    objects replaced, written as its edited subjects' whole edge lists."""
 
-    def rows_of(entity: int | None) -> list[int]:
+    def __init__(self, index: KGIndex) -> None:
+        self.index = index
+        self.entity_at = {e: n for n, e in enumerate(index.labels.owner_ids)}
+        self.relation_at = {r: n for n, r in enumerate(index.relations.owner_ids)}
+        owners = np.asarray(index.labels.owners, dtype=np.int64)
+        self.row_count = np.bincount(owners, minlength=len(index.labels.owner_ids))
+        self.order = np.argsort(owners, kind="stable")
+        self.row_start = np.zeros(len(self.row_count) + 1, dtype=np.int64)
+        np.cumsum(self.row_count, out=self.row_start[1:])
+        self.writable = set(np.unique(np.asarray(index.relations.owners)).tolist())
+
+    def rows_of(self, entity: int | None) -> list[int]:
         if entity is None:
             return []
-        return order[row_start[entity]: row_start[entity + 1]].tolist()
+        return self.order[self.row_start[entity]: self.row_start[entity + 1]].tolist()
 
-    offsets, subjects, adjacency = [0], [], [0]
-    rel_parts: list[np.ndarray] = []
-    obj_parts: list[np.ndarray] = []
-    stats = []
-    for name, edits in named.items():
+    def overlay(self, name: str, edits: Iterable[Edit]):
+        """(subjects int32, adjacency int64 [subjects + 1] from 0, edge_relations int32,
+        edge_objects int32, VersionStats) of one version."""
+        edits = [(str(s), str(r), None if o is None else str(o)) for s, r, o in edits]
         replaced: dict[int, dict[int, set[int]]] = {}
         unwritable = 0
         for s, r, o in edits:
-            subject, relation = entity_at.get(s), relation_at.get(r)
-            if subject is None or row_count[subject] == 0 or relation not in writable:
+            subject, relation = self.entity_at.get(s), self.relation_at.get(r)
+            if subject is None or self.row_count[subject] == 0 or relation not in self.writable:
                 unwritable += 1
                 continue
-            rows = rows_of(entity_at.get(o)) if o is not None else []
+            rows = self.rows_of(self.entity_at.get(o)) if o is not None else []
             if o is not None and not rows:
                 unwritable += 1
             replaced.setdefault(subject, {}).setdefault(relation, set()).update(rows)
-        edges = 0
+        subjects, adjacency, rel_parts, obj_parts = [], [0], [], []
         for subject in sorted(replaced):
-            rels, objs = index.edges_at(subject)
+            rels, objs = self.index.edges_at(subject)
             rels = np.asarray(rels, dtype=np.int64)
             objs = np.asarray(objs, dtype=np.int64)
             keep = ~np.isin(rels, list(replaced[subject]))
             added = np.array(
                 [(r, row) for r, rows in replaced[subject].items() for row in rows], dtype=np.int64
             ).reshape(-1, 2)
-            pairs = np.concatenate([np.stack([rels[keep], objs[keep]], axis=1), added])
-            pairs = np.unique(pairs, axis=0)
+            pairs = np.unique(np.concatenate([np.stack([rels[keep], objs[keep]], axis=1), added]), axis=0)
             rel_parts.append(pairs[:, 0].astype(np.int32))
             obj_parts.append(pairs[:, 1].astype(np.int32))
             subjects.append(subject)
             adjacency.append(adjacency[-1] + len(pairs))
-            edges += len(pairs)
-        offsets.append(len(subjects))
-        stats.append(VersionStats(
-            name=name, edits=len(edits), pairs=sum(len(v) for v in replaced.values()),
-            unwritable_edits=unwritable, subjects=len(replaced), edges=edges,
-        ))
+        stats = VersionStats(name=name, edits=len(edits), pairs=sum(len(v) for v in replaced.values()),
+                             unwritable_edits=unwritable, subjects=len(replaced), edges=adjacency[-1])
+        return (np.array(subjects, dtype=np.int32), np.array(adjacency, dtype=np.int64), _join(rel_parts),
+                _join(obj_parts), stats)
 
-    def join(parts: list[np.ndarray]) -> np.ndarray:
-        return np.concatenate(parts) if parts else np.zeros(0, dtype=np.int32)
 
+def _join(parts: list[np.ndarray]) -> np.ndarray:
+    return np.concatenate(parts) if parts else np.zeros(0, dtype=np.int32)
+
+
+def build_kg_versions(index: KGIndex, versions: Mapping[str, Iterable[Edit]],
+                      builder: VersionBuilder | None = None) -> KGVersions:
+    for name in versions:
+        if not isinstance(name, str) or not name:
+            raise ValueError(f"a KG version needs a non-empty name, got {name!r}")
+    builder = builder or VersionBuilder(index)
+    offsets, subjects, adjacency = [0], [], [np.zeros(1, dtype=np.int64)]
+    rel_parts: list[np.ndarray] = []
+    obj_parts: list[np.ndarray] = []
+    stats = []
+    edges = 0
+    for name, edits in versions.items():
+        subj, adj, rel, obj, stat = builder.overlay(name, edits)
+        subjects.append(subj)
+        adjacency.append(adj[1:] + edges)
+        rel_parts.append(rel)
+        obj_parts.append(obj)
+        edges += int(adj[-1])
+        offsets.append(offsets[-1] + len(subj))
+        stats.append(stat)
     return KGVersions(
-        names=tuple(named),
+        names=tuple(versions),
         stats=tuple(stats),
         offsets=np.array(offsets, dtype=np.int64),
-        subjects=np.array(subjects, dtype=np.int32),
-        adjacency=np.array(adjacency, dtype=np.int64),
-        edge_relations=join(rel_parts),
-        edge_objects=join(obj_parts),
+        subjects=_join(subjects).astype(np.int32),
+        adjacency=np.concatenate(adjacency).astype(np.int64),
+        edge_relations=_join(rel_parts),
+        edge_objects=_join(obj_parts),
         base_fingerprint=index.base_fingerprint,
     )
 

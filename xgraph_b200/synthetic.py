@@ -93,15 +93,46 @@ def synthetic_world(seed: int, entities: int, relations: int, triples: int, *, l
     return World(ents, rels, trip.astype(np.int64), sitelinks, prose)
 
 
-def object_sets(world: World) -> dict[tuple[int, int], set[int]]:
+class PairIndex:
+    """The world's distinct (subject, relation) pairs with their object positions, held as
+    sorted numpy arrays (a 10 M-triple world needs no Python set per pair)."""
+
+    def __init__(self, triples: np.ndarray, relations: int) -> None:
+        t = np.asarray(triples, dtype=np.int64).reshape(-1, 3)
+        t = t[np.lexsort((t[:, 2], t[:, 1], t[:, 0]))]
+        self._relations = max(int(relations), 1)
+        key = t[:, 0] * self._relations + t[:, 1]
+        self.keys, self._starts = np.unique(key, return_index=True)
+        self._ends = np.append(self._starts[1:], len(key))
+        self._objects = t[:, 2]
+
+    def __len__(self) -> int:
+        return len(self.keys)
+
+    def random_pair(self, rng: np.random.Generator) -> tuple[int, int]:
+        key = int(self.keys[int(rng.integers(len(self.keys)))])
+        return key // self._relations, key % self._relations
+
+    def items(self):
+        """((subject, relation), objects) of every pair, in (subject, relation) order."""
+        for k, key in enumerate(self.keys.tolist()):
+            yield (key // self._relations, key % self._relations), set(
+                self._objects[self._starts[k]: self._ends[k]].tolist())
+
+    def objects(self, pair: tuple[int, int]) -> set[int]:
+        key = pair[0] * self._relations + pair[1]
+        at = int(np.searchsorted(self.keys, key))
+        if at == len(self.keys) or int(self.keys[at]) != key:
+            return set()
+        return set(self._objects[self._starts[at]: self._ends[at]].tolist())
+
+
+def object_sets(world: World) -> PairIndex:
     """The world's (subject, relation) pairs with their object positions."""
-    pairs: dict[tuple[int, int], set[int]] = {}
-    for s, r, o in np.asarray(world.triples).tolist():
-        pairs.setdefault((s, r), set()).add(o)
-    return pairs
+    return PairIndex(world.triples, len(world.relations))
 
 
-def request_edits(world: World, pairs: dict[tuple[int, int], set[int]], rng: np.random.Generator,
+def request_edits(world: World, pairs: PairIndex, rng: np.random.Generator,
                   count: int) -> list[tuple[str, str, str | None]]:
     """`count` seeded add/remove-triple edits of one request, written as the reference's
     pair-replacement edits (src/xgraph/kgversions.py:203-216): adding o to the pair (s, r)
@@ -109,14 +140,13 @@ def request_edits(world: World, pairs: dict[tuple[int, int], set[int]], rng: np.
     object None, when none remain); one request's edits to a pair accumulate.  Half the
     edits touch pairs the world has (removing one of their objects, or adding one)."""
     entities, relations = len(world.entities), len(world.relations)
-    known = list(pairs) if pairs else []
     changed: dict[tuple[int, int], set[int]] = {}
     for _ in range(count):
-        if known and rng.random() < 0.5:
-            pair = known[int(rng.integers(len(known)))]
+        if len(pairs) and rng.random() < 0.5:
+            pair = pairs.random_pair(rng)
         else:
             pair = (int(rng.integers(entities)), int(rng.integers(relations)))
-        objects = changed.setdefault(pair, set(pairs.get(pair, ())))
+        objects = changed.setdefault(pair, pairs.objects(pair))
         if objects and rng.random() < 0.5:
             objects.discard(sorted(objects)[int(rng.integers(len(objects)))])
         else:
@@ -180,6 +210,14 @@ class Config:
     zipf: float | None = None
     options: dict = field(default_factory=dict)
     dtype: str = "bfloat16"
+    # continuous batching (the versions configuration): requests per second over the whole
+    # job, the GPUs it is spread over, the simulated decode step, the geometric mean output
+    # length and the most seeded edits (a private KG version) per request
+    arrivals: float | None = None
+    gpus: int = 1
+    step_ms: float = 0.0
+    mean_length: float = 0.0
+    max_edits: int = 0
 
 
 CONFIGS = {
@@ -189,7 +227,65 @@ CONFIGS = {
               options={"paths": True, "committed_paths": True}),
     4: Config("paths-1m-zipf", 1_000_000, 200, 10_000_000, 128_256, 512, (64, 1024), zipf=1.1,
               options={"paths": True, "committed_paths": True}),
+    # 2,000 requests/s over 8 GPUs, one decode step every 2 ms: 0.5 arrivals per step per
+    # GPU against 128 rows whose requests last 256 steps on average, so the live batch
+    # hovers at its 128-row cap (1,024 over the 8 GPUs)
+    5: Config("versions-1m", 1_000_000, 200, 10_000_000, 151_936, 128, (1, 1024), zipf=1.1,
+              options={"paths": True, "committed_paths": True}, arrivals=2000.0, gpus=8, step_ms=2.0,
+              mean_length=256.0, max_edits=256),
 }
+
+
+@dataclass
+class Arrivals:
+    """A continuous-batching replay on one GPU: per request its arrival step, output length
+    and (once admitted) slot and first step; per step the requests admitted (slot, request)
+    and the slots live in it, in slot order."""
+
+    arrival: list[int]
+    length: list[int]
+    slot: list[int]
+    start: list[int]
+    admitted: list[list[tuple[int, int]]]
+    live: list[list[int]]
+
+
+def arrival_schedule(config: Config, steps: int, seed: int, rank: int = 0, *, max_length: int | None = None) -> Arrivals:
+    """Poisson arrivals at config.arrivals / config.gpus requests per second on a clock of
+    one step every config.step_ms, output lengths Geometric(mean config.mean_length) (capped
+    at max_length, default the configuration's longest), served first come first served in
+    config.rows slots: a request leaves its slot after its last token and a waiting request
+    takes it at the next step.  The batch starts full (the geometric length is memoryless,
+    so the requests live at step 0 are as long as any), and the steps' batches are ragged."""
+    rng = np.random.default_rng(seed * 1009 + rank)
+    cap = max_length or config.lengths[1]
+    rate = config.arrivals / config.gpus * config.step_ms / 1000.0
+    counts = np.concatenate([[config.rows], rng.poisson(rate, size=steps - 1)]) if steps else np.zeros(0, int)
+    arrival = np.repeat(np.arange(steps), counts).tolist()
+    length = np.minimum(rng.geometric(1.0 / config.mean_length, size=len(arrival)), cap).tolist()
+    slot, start = [-1] * len(arrival), [-1] * len(arrival)
+    free = list(range(config.rows - 1, -1, -1))
+    ends: dict[int, list[int]] = {}
+    waiting, admitted, live, nxt = [], [], [], 0
+    occupant: dict[int, int] = {}
+    for k in range(steps):
+        for s in ends.pop(k, []):
+            del occupant[s]
+            free.append(s)
+        free.sort(reverse=True)
+        while nxt < len(arrival) and arrival[nxt] <= k:
+            waiting.append(nxt)
+            nxt += 1
+        joined = []
+        while waiting and free:
+            r, s = waiting.pop(0), free.pop()
+            slot[r], start[r] = s, k
+            occupant[s] = r
+            ends.setdefault(k + length[r], []).append(s)
+            joined.append((s, r))
+        admitted.append(joined)
+        live.append(sorted(occupant))
+    return Arrivals(arrival, length, slot, start, admitted, live)
 
 
 @dataclass
