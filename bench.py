@@ -762,7 +762,7 @@ def versions_cpu_baseline(workload, replay, budget: float, workers: int = 4) -> 
 # ---------------------------------------------------------------------------------------
 # reference arm: the oracle port on the host cores
 
-TRAFFIC_RECORD = ROOT / "profiles" / "step_apply_paths100k.json"
+TRAFFIC_RECORD = ROOT / "profiles" / "sync_apply_paths100k.json"
 
 
 def recorded_traffic(config: int, dtype: str, max_len: int) -> dict:
