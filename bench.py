@@ -72,6 +72,8 @@ def parse_args():
     p.add_argument("--e2e-steps", type=int, default=32)
     p.add_argument("--profile", action="store_true", help="short run for a profiler (no CPU leg, no e2e)")
     p.add_argument("--max-len", type=int, default=0, help="cap stream lengths (profiling runs)")
+    p.add_argument("--synchronized", action="store_true",
+                   help="every row enters its first stream at position 0 at step 0 (default: seeded positions)")
     return p.parse_args()
 
 
@@ -169,14 +171,23 @@ def load_streams(config: int, workload):
     return data["tokens"].astype(np.int32), data["lengths"].astype(np.int32), data["allowed"].astype(np.int32)
 
 
-def row_plan(rows: int, lengths, steps: int, offset: int = 0):
+def entry_offsets(lengths, rows: int, seed: int):
+    """Where each row enters its first stream: a seeded position uniform in the stream, so
+    that the batch is in its replenished steady state (requests at every point of their
+    output, as in a serving batch) from the first timed step rather than all starting
+    together.  The tokens before it are consumed before the steps (enter_rows)."""
+    rng = np.random.default_rng(seed)
+    return np.array([int(rng.integers(0, max(int(lengths[r]), 1))) for r in range(rows)], dtype=np.int64)
+
+
+def row_plan(rows: int, lengths, steps: int, offset: int = 0, start=None):
     """Per row, the (stream, position) it replays at each step: row r replays streams
     offset + r, offset + r + rows, ... back to back (a finished request's slot takes the
-    next one, as a serving batch does)."""
+    next one, as a serving batch does), entering its first one at position start[r]."""
     n = len(lengths)
     plan = np.zeros((rows, steps, 2), dtype=np.int64)
     for r in range(rows):
-        sid, at = (offset + r) % n, 0
+        sid, at = (offset + r) % n, 0 if start is None else int(start[r])
         for k in range(steps):
             if at >= lengths[sid]:
                 sid, at = (sid + rows) % n, 0
@@ -219,6 +230,8 @@ def _worker_step(job):
         if pos == 0 or row not in states:
             versions = _WORKER.get("row_versions")
             states[row] = oracle.initial_state(versions[row] if versions else None)
+            for earlier in tokens[sid, :pos]:  # a row entering its stream mid-way: the prefix first
+                states[row] = oracle.advance(states[row], int(earlier))
         token = int(tokens[sid, pos])
         if row == full:
             t0 = time.perf_counter()
@@ -250,7 +263,7 @@ def _worker_main(conn, init_args):
 
 def oracle_leg(workload, tokens, lengths, rows: int, steps: int, warmup: int, *, budget: float | None = None,
                expected: dict | None = None, workers: int | None = None, versions: dict | None = None,
-               row_versions: list | None = None) -> dict:
+               row_versions: list | None = None, start=None) -> dict:
     """The oracle replaying rows x (warmup + steps) of the streams on `workers` spawned
     processes, each owning a fixed set of rows; a step waits for every worker.  With
     `budget` (seconds) the timed steps stop early once it is spent.  expected:
@@ -259,7 +272,7 @@ def oracle_leg(workload, tokens, lengths, rows: int, steps: int, warmup: int, *,
 
     cores = os.cpu_count() or 1
     workers = workers or max(1, min(cores, 32, rows))
-    plan = row_plan(rows, lengths, warmup + steps)
+    plan = row_plan(rows, lengths, warmup + steps, start=start)
     owned = [list(range(w, rows, workers)) for w in range(workers)]
     init = (workload.index, workload.served, workload.syntax, dict(workload.config.options), tokens,
             workload.served.vocab_size, versions, row_versions)
@@ -317,8 +330,9 @@ def oracle_leg(workload, tokens, lengths, rows: int, steps: int, warmup: int, *,
             "setup_s": setup, "checked": checked, "mismatches": mismatches}
 
 
-def cpu_baseline(workload, tokens, lengths, rows: int, expected: dict, budget: float) -> dict:
-    leg = oracle_leg(workload, tokens, lengths, rows, steps=10_000, warmup=2, budget=budget, expected=expected)
+def cpu_baseline(workload, tokens, lengths, rows: int, expected: dict, budget: float, start=None) -> dict:
+    leg = oracle_leg(workload, tokens, lengths, rows, steps=10_000, warmup=2, budget=budget, expected=expected,
+                     start=start)
     value = leg["row_steps"] / leg["wall_s"] if leg["wall_s"] else 0.0
     return {
         "value": value, "unit": UNIT, "cores": leg["workers"], "kind": "port",
@@ -349,6 +363,21 @@ class Replay:
     versions: list
     streams_source: str
     cpu: dict
+    start: np.ndarray | None = None  # per slot, the history column of step 0 (tokens before it: a prefix)
+
+
+def enter_rows(engine, replay, device) -> None:
+    """Before step 0: rows that enter their first stream mid-way begin and consume the
+    stream's earlier tokens (one sync over each row's prefix, outside every timed region)."""
+    import torch
+
+    if replay.start is None or not replay.start.any():
+        return
+    rows = replay.slots
+    every = torch.arange(rows, dtype=torch.int32, device=device)
+    engine.admit(admissions_tensor([(r, 0) for r in range(rows)], device))
+    zeros = torch.zeros(rows, dtype=torch.int32, device=device)
+    engine.sync(every, replay.history, zeros, torch.from_numpy(replay.start.astype(np.int32)).to(device))
 
 
 def fixture_replay(args, workload, device, rank: int, total_steps: int, blob_meta, lo_hi) -> Replay:
@@ -379,9 +408,16 @@ def fixture_replay(args, workload, device, rank: int, total_steps: int, blob_met
         del gen_engine
         source = "sampled on the GPU with the engine's masks (no fixture for this configuration)"
     lengths = np.maximum(np.minimum(lengths, lo_hi[1]), 1)
-    plan = row_plan(rows, lengths, total_steps)
+    start = None if args.synchronized else entry_offsets(lengths, rows, args.seed + 500 + rank)
+    plan = row_plan(rows, lengths, total_steps, start=start)
     sid, pos = plan[:, :, 0], plan[:, :, 1]
-    history = torch.from_numpy(np.ascontiguousarray(tokens_np[sid, pos], dtype=np.int32)).to(device)
+    first = np.zeros(rows, dtype=np.int64) if start is None else start
+    steps_np = np.ascontiguousarray(tokens_np[sid, pos], dtype=np.int32)
+    history_np = np.zeros((rows, int(first.max()) + total_steps), dtype=np.int32)
+    for r in range(rows):  # row r: its first stream's prefix, then the tokens of its steps
+        history_np[r, : first[r]] = tokens_np[r, : first[r]]
+        history_np[r, first[r]: first[r] + total_steps] = steps_np[r]
+    history = torch.from_numpy(history_np).to(device)
     disallowed = (vocab - counts_h[sid, pos + 1]).sum(axis=0).astype(np.int64)
     every = torch.arange(rows, dtype=torch.int32, device=device)
     admissions = []
@@ -389,7 +425,7 @@ def fixture_replay(args, workload, device, rank: int, total_steps: int, blob_met
         joined = np.flatnonzero(pos[:, k] == 0).tolist()
         admissions.append(admissions_tensor([(slot, 0) for slot in joined], device) if joined else None)
     return Replay(rows, history, [every] * total_steps, admissions, [rows] * total_steps, disallowed, [], source,
-                  {"tokens": tokens_np, "lengths": lengths})
+                  {"tokens": tokens_np, "lengths": lengths}, first)
 
 
 def versions_replay(args, workload, device, rank: int, total_steps: int, blob_meta) -> Replay:
@@ -493,8 +529,9 @@ def engine_arm(args) -> None:
         replay = fixture_replay(args, workload, device, rank, total_steps, (blob, meta), (lo, hi))
     sample_s = time.perf_counter() - t0
     rows, history = replay.slots, replay.history
-    prompt = [torch.full((rows,), k, dtype=torch.int32, device=device) for k in range(total_steps)]
-    total = [torch.full((rows,), k + 1, dtype=torch.int32, device=device) for k in range(total_steps)]
+    first = torch.from_numpy((replay.start if replay.start is not None else np.zeros(rows)).astype(np.int32)).to(device)
+    prompt = [first + k for k in range(total_steps)]  # a joining request's first token is its step's column
+    total = [first + (k + 1) for k in range(total_steps)]
     gen = torch.Generator(device=device).manual_seed(7)
     dtype = getattr(torch, cfg.dtype)
     elt = torch.empty(0, dtype=dtype).element_size()
@@ -504,6 +541,7 @@ def engine_arm(args) -> None:
     for name, edits in replay.versions:
         engine.add_version(name, edits)
     engine.reset()
+    enter_rows(engine, replay, device)
     stream = torch.cuda.current_stream(device).cuda_stream
     launches = 0
     step_ms, warm_ms = [], []
@@ -572,7 +610,7 @@ def engine_arm(args) -> None:
         "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": job_ms / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int32", "data": "synthetic",
-        "config": workload_config(cfg, args.config, rows, vocab, lo, hi, world),
+        "config": workload_config(cfg, args.config, rows, vocab, lo, hi, world, args.synchronized),
         "timed_region": "one sync_apply launch per step (admissions of joining requests, sync, apply_mask), "
                         "CUDA events on the launching stream, max over ranks",
         "streams": replay.streams_source,
@@ -617,32 +655,35 @@ def engine_arm(args) -> None:
             result["cpu_baseline"] = versions_cpu_baseline(workload, replay, args.cpu_seconds)
         else:
             tokens_np, lengths = replay.cpu["tokens"], replay.cpu["lengths"]
-            expected = replay_masks(engine, tokens_np, lengths, rows, CPU_CHECK_STEPS)
-            result["cpu_baseline"] = cpu_baseline(workload, tokens_np, lengths, rows, expected, args.cpu_seconds)
+            expected = replay_masks(engine, tokens_np, lengths, rows, CPU_CHECK_STEPS, replay.start)
+            result["cpu_baseline"] = cpu_baseline(workload, tokens_np, lengths, rows, expected, args.cpu_seconds,
+                                                  replay.start)
     print(json.dumps(result), flush=True)
 
 
 CPU_CHECK_STEPS = 96  # the CPU leg's first steps, whose full row-steps are checked against the engine's masks
 
 
-def replay_masks(engine, tokens, lengths, rows: int, steps: int) -> dict:
-    """{(stream, position): mask words} for the first `steps` positions of streams 0..rows-1
-    (the streams the oracle leg's rows start with), from the engine replaying them with
-    advance + fill_mask (the mask before each position's token)."""
+def replay_masks(engine, tokens, lengths, rows: int, steps: int, start=None) -> dict:
+    """{(stream, position): mask words} for `steps` positions of streams 0..rows-1 from where
+    the oracle leg's rows enter them (start, default 0), from the engine replaying the
+    streams with advance + fill_mask (the mask before each position's token)."""
     import torch
 
+    first = np.zeros(rows, dtype=np.int64) if start is None else np.asarray(start)
     engine.reset()
     device = torch.device("cuda", torch.cuda.current_device())
     engine.begin(torch.arange(rows, dtype=torch.int32, device=device))
     view = engine.mask_view()
     out = {}
-    steps = min(steps, int(np.max(lengths[:rows])))
-    for at in range(steps):
+    horizon = int(min(np.max(first + steps), np.max(lengths[:rows])))
+    for at in range(horizon):
         engine.fill_mask(rows)
-        live = [r for r in range(rows) if at < lengths[r]]
-        words = view[:rows, : engine.words].cpu().numpy().view(np.uint32)
-        for r in live:
-            out[(r, at)] = words[r].copy()
+        keep = [r for r in range(rows) if first[r] <= at < min(first[r] + steps, lengths[r])]
+        if keep:
+            words = view[:rows, : engine.words].cpu().numpy().view(np.uint32)
+            for r in keep:
+                out[(r, at)] = words[r].copy()
         engine.advance(np.ascontiguousarray(tokens[:rows, at], dtype=np.int32))
     return out
 
@@ -691,16 +732,22 @@ def e2e_leg(engine, replay, prompt, total, vocab, device, steps, dtype):
     rows = replay.slots
     history = replay.history
     live = replay.live[:steps]
-    host_tokens = history[:, :steps].t().contiguous().cpu().pin_memory()
+    first = replay.start if replay.start is not None else np.zeros(rows, dtype=np.int64)
+    width = history.shape[1]
+    # step k of row r is history column first[r] + k: its flat index, one gather per step
+    flat = [torch.from_numpy(np.arange(rows) * width + first + k).to(device) for k in range(steps)]
+    host_np = history.cpu().numpy()
+    host_tokens = torch.from_numpy(np.stack([host_np[np.arange(rows), first + k] for k in range(steps)])).pin_memory()
     host_logits = (torch.randn((rows, vocab)) * 2.0).to(dtype).pin_memory()
     out_logits = torch.empty_like(host_logits).pin_memory()
-    dev_hist = torch.zeros_like(history)
+    dev_hist = history.clone()  # the prefixes; each step's column is uploaded again in its step
     dev_logits = [torch.empty((rows, vocab), dtype=dtype, device=device) for _ in range(2)]
     staging = [torch.empty(rows, dtype=torch.int32, device=device) for _ in range(2)]
     up, down = torch.cuda.Stream(device), torch.cuda.Stream(device)
     compute = torch.cuda.current_stream(device)
     stream = compute.cuda_stream
     engine.reset()
+    enter_rows(engine, replay, device)
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record(compute)
@@ -718,7 +765,7 @@ def e2e_leg(engine, replay, prompt, total, vocab, device, steps, dtype):
             dev_logits[b][:n].copy_(host_logits[:n], non_blocking=True)
             uploaded[k].record(up)
         compute.wait_event(uploaded[k])
-        dev_hist[:, k] = staging[b]
+        dev_hist.view(-1).index_copy_(0, flat[k], staging[b])
         engine.sync_apply(replay.step_slots[k], dev_hist, prompt[k], total[k], dev_logits[b][:n], stream=stream,
                           admissions=replay.admissions[k])
         stepped[k].record(compute)
@@ -808,14 +855,16 @@ def reference_arm(args) -> None:
         lengths = np.minimum(lengths, args.max_len)
     # every timed step takes about one V-wide allowed set per worker (about a second): the
     # timed steps stop after REFERENCE_BUDGET_S so that a long --steps still ends in minutes
+    start = None if args.synchronized else entry_offsets(lengths[:pool], rows, args.seed + 500)
     leg = oracle_leg(workload, tokens[:pool], lengths[:pool], rows, steps=args.steps, warmup=args.warmup,
-                     budget=REFERENCE_BUDGET_S)
+                     budget=REFERENCE_BUDGET_S, start=start)
     value = leg["row_steps"] / leg["wall_s"] if leg["wall_s"] else 0.0
     result = {
         "impl": "reference", "metric": metric_of(args.config, rows, workload.served.vocab_size), "value": value, "unit": UNIT, "n_gpus": world, "steps": leg["steps"],
         "warmup": args.warmup, "ms_per_step": 1e3 * leg["wall_s"] / max(leg["steps"], 1), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int32", "data": "synthetic",
-        "config": workload_config(cfg, args.config, rows, workload.served.vocab_size, lo, hi, world),
+        "config": workload_config(cfg, args.config, rows, workload.served.vocab_size, lo, hi, world,
+                                  args.synchronized),
         "cpu_baseline": {
             "value": value, "unit": UNIT, "cores": leg["workers"], "kind": "port",
             "sample": (f"each step {leg['workers']} full row-steps (oracle allowed set + masked logits + advance, "
@@ -839,14 +888,16 @@ def engine_library_loaded() -> bool:
         return False
 
 
-def workload_config(cfg, number: int, rows: int, vocab: int, lo: int, hi: int, world: int) -> dict:
+def workload_config(cfg, number: int, rows: int, vocab: int, lo: int, hi: int, world: int,
+                    synchronized: bool = False) -> dict:
     """The `config` object of both arms' lines (the workload, not how an arm runs it)."""
     if cfg.arrivals:
         batching = (f"Poisson arrivals {cfg.arrivals:,.0f} req/s over {cfg.gpus} GPUs on a {cfg.step_ms} ms step "
                     f"clock, output lengths Geometric(mean {cfg.mean_length:.0f}) capped at {hi}, up to {rows} live "
                     f"rows/GPU, 0-{cfg.max_edits} seeded add/remove edits per request as its own KG version")
     else:
-        batching = f"{rows} rows/GPU, stream lengths U[{lo},{hi}] replenished"
+        entry = "all at position 0" if synchronized else "each at a seeded position of its first stream"
+        batching = f"{rows} rows/GPU, stream lengths U[{lo},{hi}] replenished, rows entering {entry}"
     return {
         "workload": (f"{cfg.name} (config {number}): {cfg.entities:,} entities, {cfg.relations} relations, "
                      f"{cfg.triples:,} triples, V={vocab:,}, {batching}, paths+committed_paths, escapes on"),

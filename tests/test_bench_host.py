@@ -48,3 +48,16 @@ def test_oracle_leg_replays_and_checks_against_the_kernel_logic():
     assert leg["steps"] == 6 and leg["row_steps"] == 12 and leg["workers"] == 2
     assert leg["checked"] == 14 and leg["mismatches"] == 0  # warm-up row-steps are checked too
     assert leg["wall_s"] > 0 and torch is not None
+
+
+def test_rows_enter_their_first_stream_at_seeded_positions():
+    lengths = np.array([5, 9, 3, 7])
+    start = bench.entry_offsets(lengths, 2, seed=4)
+    assert start.tolist() == bench.entry_offsets(lengths, 2, seed=4).tolist()  # seeded
+    assert all(0 <= start[r] < lengths[r] for r in range(2))
+    plan = bench.row_plan(2, lengths, 12, start=start)
+    for r in range(2):
+        assert plan[r, 0].tolist() == [r, start[r]]  # row r enters stream r at its offset
+        # then runs to the stream's end and takes the next one from its start
+        left = int(lengths[r] - start[r])
+        assert plan[r, left].tolist() == [r + 2, 0]

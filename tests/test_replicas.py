@@ -57,12 +57,17 @@ def test_two_gloo_ranks_receive_identical_replicas():
     assert results[0][2] > 0
 
 
-def test_schedule_replenishes_every_slot():
+def test_replay_plan_replenishes_every_slot():
+    """Every slot replays whole streams back to back: each step's position lies inside its
+    stream, positions advance by one, and a new stream starts at 0 right after one ends."""
     import bench
 
-    lengths = list(np.random.default_rng(0).integers(3, 9, size=10))
-    assigned, restarts = bench.schedule(lengths, rows=4, steps=30)
-    for slot, parts in enumerate(assigned):
-        starts = [at for _, at in parts]
-        assert starts[0] == 0 and all(b - a == lengths[sid] for (sid, a), b in zip(parts, starts[1:]))
-        assert all(slot in restarts[at] for at in starts)
+    lengths = np.random.default_rng(0).integers(3, 9, size=10)
+    plan = bench.row_plan(4, lengths, 30, start=bench.entry_offsets(lengths, 4, seed=1))
+    for r in range(4):
+        for k in range(30):
+            sid, pos = plan[r, k]
+            assert 0 <= pos < lengths[sid]
+            if k:
+                psid, ppos = plan[r, k - 1]
+                assert (sid, pos) == (psid, ppos + 1) or (pos == 0 and ppos == lengths[psid] - 1)
