@@ -588,6 +588,9 @@ def engine_arm(args) -> None:
     last_slots = replay.step_slots[total_steps - 1]
     apply_alone = (None if args.profile else
                    apply_leg(engine, logits[: len(last_slots)], last_slots, flush, stream, args.steps, elt))
+    policies = (None if args.profile else
+                policies_leg(workload, replay, (blob, meta), options, prompt, total, flush, stream, device,
+                             args.warmup, args.steps, dtype, gen))
     steps_ms = [a.elapsed_time(b) for a, b in step_ms]
     warms = [a.elapsed_time(b) for a, b in warm_ms]
     time_t = torch.tensor([sum(steps_ms)], dtype=torch.float64, device=device)
@@ -628,6 +631,7 @@ def engine_arm(args) -> None:
                      "kernel": f"sync_apply_kernel<{elt}> ({cfg.dtype}): admissions + sync + mask + apply fused",
                      "algorithmic_bytes_per_launch": statistics.mean(bytes_per_launch)},
         "apply_mask_alone": apply_alone,
+        "policies_on": policies,
         "gpu_launches": launches,
         "clocks": clock_info,
         "errors": errors,
@@ -719,6 +723,53 @@ def apply_leg(engine, logits, slots, flush, stream, steps, elt):
             "ms_mean": statistics.mean(ms), "algorithmic_bytes_per_launch": bytes_per_launch,
             "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_kind": peak_kind,
             "note": "apply_mask alone on the replay's final masks, L2 flushed between launches"}
+
+
+POLICY_RELEASE_MASS = 0.35
+POLICY_ESCAPE_BIAS = -0.75
+
+
+def policies_leg(workload, replay, blob_meta, options, prompt, total, flush, stream, device, warmup, steps,
+                 dtype, gen):
+    """The same replay through an engine with apply_mask's logit policies on (release below
+    POLICY_RELEASE_MASS of allowed mass, POLICY_ESCAPE_BIAS on the committing tokens): each
+    span row whose escape marker can go on reads its whole logits row once for its allowed
+    mass before its -inf writes.  Fresh N(0, 2) logits every step (copied in outside the
+    timed region, then L2 flushed); one sync_apply launch per step between CUDA events."""
+    import torch
+
+    from xgraph_b200.engine import Engine
+
+    engine = Engine(workload.index, workload.served, workload.syntax, replay.slots, device_blob=blob_meta,
+                    release_mass=POLICY_RELEASE_MASS, escape_bias=POLICY_ESCAPE_BIAS, **options)
+    for name, edits in replay.versions:
+        engine.add_version(name, edits)
+    engine.reset()
+    enter_rows(engine, replay, device)
+    vocab = workload.served.vocab_size
+    fresh = (torch.randn((replay.slots, vocab), generator=gen, device=device) * 2.0).to(dtype)
+    logits = torch.empty_like(fresh)
+    times, rows = [], 0
+    for k in range(warmup + steps):
+        logits.copy_(fresh)
+        flush.fill_(k)
+        n = replay.live[k]
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        engine.sync_apply(replay.step_slots[k], replay.history, prompt[k], total[k], logits[:n], stream=stream,
+                          admissions=replay.admissions[k])
+        e1.record()
+        if k >= warmup:
+            times.append((e0, e1))
+            rows += n
+    torch.cuda.synchronize()
+    ms = [a.elapsed_time(b) for a, b in times]
+    faults = engine.faults()
+    return {"release_mass": POLICY_RELEASE_MASS, "escape_bias": POLICY_ESCAPE_BIAS, "steps": len(ms),
+            "ms_per_step": statistics.mean(ms), "ms_median": statistics.median(ms),
+            "value": rows / (sum(ms) / 1e3), "unit": UNIT, "device_faults": faults,
+            "note": "the timed replay again with release and escape bias on (one rank), fresh logits per step, "
+                    "L2 flushed; span rows read their logits row for the allowed mass"}
 
 
 def e2e_leg(engine, replay, prompt, total, vocab, device, steps, dtype):

@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define XG_ABI_VERSION 1
+#define XG_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define XG_API __attribute__((visibility("default")))
@@ -107,11 +107,28 @@ typedef struct XgLayout {
 } XgLayout;
 
 /* Span-language policies, as the reference Engine's constructor flags
- * (src/xgraph/engine.py:582-623).  Expressions, STOP, observation, menu, audit,
- * release and escape-bias policies are not part of this engine. */
+ * (src/xgraph/engine.py:582-623).  Expressions, STOP, observation, menu and audit policies
+ * are not part of this engine.
+ *
+ * The logit policies of apply_mask (and of the sync_apply steps, which include it), as the
+ * native Engine's arguments (csrc/engine.cu:2601, 2668-2671):
+ *   release_log_mass  log of the release mass (< 0), -INFINITY when off: inside a span, a
+ *                     row whose logits put less than exp(release_log_mass) of their softmax
+ *                     (over the served vocabulary, at the logits' own temperature) on the
+ *                     allowed set may write only the escape marker's next tokens;
+ *   release_top       1: the same for a row whose own top token (lowest column among
+ *                     equal maxima) is disallowed;
+ *   escape_bias       added to the logits of the tokens that commit to the escape marker
+ *                     inside a span (they start it and continue neither the label, the
+ *                     separator nor the closer); 0 when off.  16-bit logits hold the sum
+ *                     rounded to nearest.
+ * Release needs escapes.  A released row's mask is used for that call only: the slot's
+ * recorded mask (xg_fill_mask, xg_mask_host) is the ordinary one. */
 typedef struct XgOptions {
   int32_t escapes, repeats, derivation, paths, bound_escapes, committed_paths;
   int32_t sitelinks_rank, end_after_answer;
+  int32_t release_top;
+  float release_log_mass, escape_bias;
 } XgOptions;
 
 typedef struct XgInfo {
@@ -288,6 +305,32 @@ XG_API int xg_build_adjacency(const int32_t* subjects, const int32_t* relations,
                               int32_t label_rows, const uint8_t* writable, int32_t relation_count, int64_t capacity,
                               int64_t* offsets, int32_t* edge_relations, int32_t* edge_objects, int64_t* edges,
                               int64_t* unwritable, void* stream);
+
+/* Device-side label rows of a KG index; it replaces the host build of the same arrays
+ * (src/xgraph/index.py:167-233: every label, written as label prefix + label and encoded by
+ * the served tokenizer, is admitted under exact-v1 -- no special token, a nonempty
+ * encoding, known bytes for every token, and token bytes equal to the written bytes -- and
+ * the admitted labels become rows sorted as (token sequence, owner position) tuples).
+ * Device arrays: label i's token ids token_ids[token_off[i] .. token_off[i + 1]) (token_off
+ * int64 [labels + 1], token_ids int32 [token_count]), its written bytes
+ * text[text_off[i] .. text_off[i + 1]) (text_off int64 [labels + 1], text uint8
+ * [text_bytes]), its owner position owners[i] in [0, owner_count); the served vocabulary's
+ * bytes as CSR over `vocab` ids (vocab_off int64 [vocab + 1], vocab_bytes uint8
+ * [vocab_byte_count]) with vocab_kind int8 [vocab] (0 known bytes, 1 special, 2 unknown
+ * bytes; ids outside [0, vocab) have unknown bytes).  Outputs: status int32 [labels] (0
+ * admitted, 1 a special token, 2 an empty encoding, 3 a token with unknown bytes, 4 the
+ * bytes do not round-trip: the reference's checks in its order), row_offsets int64
+ * [labels + 1], row_tokens int32 [token_count] and row_owners int32 [labels] for the
+ * first *rows rows (*tokens tokens), host outputs.  Offsets outside their arrays or an owner
+ * out of range fail with XG_EINVAL.  Scratch is stream-ordered on `stream`; the call
+ * synchronizes the stream before it returns. */
+XG_API int xg_build_label_rows(int32_t labels, const int64_t* token_off, const int32_t* token_ids,
+                               int64_t token_count, const int64_t* text_off, const uint8_t* text,
+                               int64_t text_bytes, const int32_t* owners, int32_t owner_count,
+                               int32_t vocab, const int64_t* vocab_off, const uint8_t* vocab_bytes,
+                               int64_t vocab_byte_count, const int8_t* vocab_kind, int32_t* status,
+                               int64_t* row_offsets, int32_t* row_tokens, int32_t* row_owners,
+                               int32_t* rows, int64_t* tokens, void* stream);
 
 #ifdef __cplusplus
 }

@@ -40,6 +40,8 @@ def library():
     lib.xgs_memory_ints.restype = i32
     lib.xgs_relation_slice.argtypes = [p, i32, i32, i32, p]
     lib.xgs_relation_slice.restype = None
+    lib.xgs_escape_policy.argtypes = [p, i32, p, p, p, p, i32]
+    lib.xgs_escape_policy.restype = i32
     return lib
 
 
@@ -58,7 +60,7 @@ class SeamEngine:
                                  paths=int(paths), bound_escapes=int(bound_escapes),
                                  committed_paths=int(committed_paths),
                                  sitelinks_rank=int(start_rank == "sitelinks"),
-                                 end_after_answer=int(end_after_answer))
+                                 end_after_answer=int(end_after_answer), release_log_mass=-np.inf)
         self.slots = slots
         self.handle = self.lib.xgs_create(self.tables.blob.ctypes.data_as(ctypes.c_void_p),
                                           ctypes.byref(self.tables.layout), ctypes.byref(self.options), slots)
@@ -66,6 +68,17 @@ class SeamEngine:
     def __del__(self):
         if getattr(self, "handle", None):
             self.lib.xgs_destroy(self.handle)
+
+    def escape_policy(self, slot, cap=4096):
+        """(escape position or -1, tokens that commit the slot to the escape marker, the
+        escape marker's next tokens from that position) as the kernels compute them."""
+        commits, released = np.zeros(cap, dtype=np.int32), np.zeros(cap, dtype=np.int32)
+        counts = np.zeros(2, dtype=np.int32)
+        pos = self.lib.xgs_escape_policy(
+            self.handle, slot, commits.ctypes.data_as(ctypes.c_void_p), counts[0:].ctypes.data_as(ctypes.c_void_p),
+            released.ctypes.data_as(ctypes.c_void_p), counts[1:].ctypes.data_as(ctypes.c_void_p), cap)
+        assert counts.max() <= cap
+        return int(pos), set(commits[: counts[0]].tolist()), set(released[: counts[1]].tolist())
 
     def relation_slice(self, entity, relation, version=0):
         out = np.zeros(3, dtype=np.int32)

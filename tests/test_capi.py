@@ -31,7 +31,36 @@ def test_library_exports_every_declared_function():
     for name in declared():
         assert hasattr(lib, name), name
     lib.xg_abi_version.restype = ctypes.c_int32
-    assert lib.xg_abi_version() == 1
+    from xgraph_b200.engine import ABI_VERSION
+
+    assert lib.xg_abi_version() == ABI_VERSION
+    assert f"#define XG_ABI_VERSION {ABI_VERSION}\n" in (ROOT / "include" / "xgraph_b200.h").read_text()
+
+
+def test_ctypes_structures_match_the_header(tmp_path):
+    """The ctypes mirrors of XgOptions and XgLayout have the header's field offsets and
+    sizes (a C program built with gcc against the header prints them)."""
+    import subprocess
+
+    from xgraph_b200.tables import XgLayout, XgOptions
+
+    lines = []
+    for struct in (XgOptions, XgLayout):
+        name = struct.__name__
+        lines.append(f'printf("{name} size %zu\\n", sizeof({name}));')
+        for field, _ in struct._fields_:
+            lines.append(f'printf("{name} {field} %zu\\n", offsetof({name}, {field}));')
+    source = tmp_path / "offsets.c"
+    source.write_text('#include <stddef.h>\n#include <stdio.h>\n#include "xgraph_b200.h"\nint main(void) {\n'
+                      + "\n".join(lines) + "\nreturn 0;\n}\n")
+    binary = tmp_path / "offsets"
+    subprocess.run(["gcc", "-std=c11", "-I", str(ROOT / "include"), str(source), "-o", str(binary)], check=True)
+    printed = subprocess.run([str(binary)], check=True, capture_output=True, text=True).stdout.split("\n")
+    for struct in (XgOptions, XgLayout):
+        name = struct.__name__
+        assert f"{name} size {ctypes.sizeof(struct)}" in printed
+        for field, _ in struct._fields_:
+            assert f"{name} {field} {getattr(struct, field).offset}" in printed, (name, field)
 
 
 def test_null_engine_calls_fail_with_einval():

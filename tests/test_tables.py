@@ -80,3 +80,35 @@ def test_relation_slice_matches_edge_lists(hub_world):
                 assert (first, last) == (lo, hi), (e, r)
             checked += 1
     assert checked > 10000
+
+
+def test_byte_table_is_the_token_byte_view():
+    """ServedTokenizer.byte_table (the device label build's vocabulary) holds every id's
+    bytes and its class: special ids, ids without bytes, and the rest."""
+    from tests.conftest import golden_worlds, world
+
+    for name in golden_worlds():
+        _, served, _ = world(name)
+        offsets, data, kind = served.byte_table()
+        assert len(offsets) == len(kind) + 1 and offsets[-1] == len(data)
+        for t in range(len(kind)):
+            b = served.token_bytes(t)
+            if t in served.special_ids:
+                assert kind[t] == 1
+            elif b is None:
+                assert kind[t] == 2
+            else:
+                assert kind[t] == 0 and bytes(data[offsets[t]:offsets[t + 1]]) == b
+
+
+def test_label_exclusion_test_equals_the_syntax_rule():
+    """The compiled exclusion test of the label build equals SpanSyntax.excludes."""
+    from xgraph_b200.index import _excluder
+    from xgraph_b200.syntax import PRESETS, SpanSyntax
+
+    labels = ["Marie Curie", "a ⟧ b", "x · y", "q ⁇", "earlier: x", "later:x", "same:", "p |q", "[[x]]", "a|b",
+              "</kg>", "【x", 'say "x"', " ⟦", "plain", "ear lier:", "", " "]
+    for syntax in [SpanSyntax(), *PRESETS.values(), SpanSyntax(operators=(), operand_separator="")]:
+        excludes = _excluder(syntax)
+        for label in labels:
+            assert excludes(label) == syntax.excludes(label), (syntax, label)

@@ -43,9 +43,9 @@ def test_invalid_arguments_raise(extra, monkeypatch):
 
 
 def test_unserved_settings_are_refused():
-    adapter.check_served_settings({"XGRAPH_PATHS": "1", "XGRAPH_RELEASE_MASS": "0", "XGRAPH_RELATIONS": "frontier",
-                                   "XGRAPH_ESCAPE_BIAS": "0.0"})
-    for name, value in [("XGRAPH_RELEASE_MASS", "0.2"), ("XGRAPH_STOP", "residual-goal"), ("XGRAPH_AUDIT", "1"),
+    adapter.check_served_settings({"XGRAPH_PATHS": "1", "XGRAPH_RELEASE_MASS": "0.2", "XGRAPH_RELATIONS": "frontier",
+                                   "XGRAPH_ESCAPE_BIAS": "-2.5", "XGRAPH_RELEASE_TOP": "1", "XGRAPH_OBSERVE": "0.0"})
+    for name, value in [("XGRAPH_MENU", "3"), ("XGRAPH_STOP", "residual-goal"), ("XGRAPH_AUDIT", "1"),
                         ("XGRAPH_RELATIONS", "successor"), ("XGRAPH_EXPRESSIONS", "1"), ("XGRAPH_OBSERVE", "4")]:
         with pytest.raises(ValueError, match=name):
             adapter.check_served_settings({name: value})

@@ -88,6 +88,118 @@ __global__ void decode_kernel(const uint64_t* keys, const int64_t* count, int32_
   }
 }
 
+// ---------------------------------------------------------------------------------------
+// Label rows (src/xgraph/index.py:167-233): exact-v1 admission of every encoded label, then
+// the admitted labels ordered as (token sequence, owner position) tuples.
+//   admit   one warp per label: a special token (status 1), an empty encoding (2), a token
+//           without known bytes (3), else its tokens' bytes against the written label
+//           (label prefix + label, UTF-8): 4 when they differ, 0 admitted; offsets or ids
+//           outside their arrays count in bad and give status -1;
+//   select  the admitted labels, in input order (CUB);
+//   sort    LSD over stable radix sorts: by owner, then by the token at each depth from the
+//           deepest to the first, where a label already ended sorts first (key 0), as a
+//           shorter tuple sorts before its extensions;
+//   gather  each row's length, scanned into offsets, then its tokens and owner.
+
+// Bytes class of each vocabulary id: 0 known bytes, 1 special, 2 unknown bytes.
+constexpr int8_t kKnownBytes = 0, kSpecial = 1, kUnknownBytes = 2;
+
+__global__ void admit_labels_kernel(int32_t labels, const int64_t* token_off, const int32_t* ids, int64_t id_count,
+                                    const int64_t* text_off, const uint8_t* text, int64_t text_bytes,
+                                    const int32_t* owners, int32_t owner_count, int32_t vocab,
+                                    const int64_t* vocab_off, const uint8_t* vocab_bytes, int64_t vocab_byte_count,
+                                    const int8_t* vocab_kind, int32_t* status, int32_t* selected, uint8_t* admitted,
+                                    int32_t* length, unsigned long long* bad) {
+  const int32_t lane = threadIdx.x & 31;
+  const int64_t warps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t i = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5; i < labels; i += warps) {
+    const int64_t t0 = token_off[i], t1 = token_off[i + 1], b0 = text_off[i], b1 = text_off[i + 1];
+    const int32_t owner = owners[i];
+    int32_t code = 0;
+    if (t0 < 0 || t1 < t0 || t1 > id_count || b0 < 0 || b1 < b0 || b1 > text_bytes || owner < 0 ||
+        owner >= owner_count) {
+      code = -1;
+    } else {
+      bool special = false, unknown = false, broken = false;
+      long long bytes = 0;
+      for (int64_t j = t0 + lane; j < t1; j += 32) {
+        const int32_t id = ids[j];
+        const int8_t kind = id >= 0 && id < vocab ? vocab_kind[id] : kUnknownBytes;
+        special |= kind == kSpecial;
+        unknown |= kind == kUnknownBytes;
+        if (kind == kKnownBytes) {
+          const int64_t v0 = vocab_off[id], v1 = vocab_off[id + 1];
+          broken |= v0 < 0 || v1 < v0 || v1 > vocab_byte_count;
+          bytes += v1 - v0;
+        }
+      }
+      special = __any_sync(0xffffffffu, special);
+      unknown = __any_sync(0xffffffffu, unknown);
+      broken = __any_sync(0xffffffffu, broken);
+      for (int32_t d = 16; d > 0; d >>= 1) bytes += __shfl_xor_sync(0xffffffffu, bytes, d);
+      code = special ? 1 : t1 == t0 ? 2 : unknown ? 3 : broken ? -1 : bytes != b1 - b0 ? 4 : 0;
+      // the bytes, token by token (the loop is warp-uniform), lanes over each token's bytes
+      int64_t at = b0;
+      for (int64_t j = t0; j < t1 && code == 0; ++j) {
+        const int32_t id = ids[j];
+        const int64_t v0 = vocab_off[id], n = vocab_off[id + 1] - v0;
+        bool differ = false;
+        for (int64_t k = lane; k < n; k += 32) differ |= vocab_bytes[v0 + k] != text[at + k];
+        if (__any_sync(0xffffffffu, differ)) code = 4;
+        at += n;
+      }
+    }
+    if (lane == 0) {
+      status[i] = code;
+      selected[i] = static_cast<int32_t>(i);
+      admitted[i] = code == 0;
+      length[i] = code == 0 ? static_cast<int32_t>(t1 - t0) : 0;
+      if (code < 0) atomicAdd(bad, 1ull);
+    }
+  }
+}
+
+// keys[k] for sorted position k of the admitted labels: the owner (depth < 0), or the token
+// at `depth` plus one (0 where the label has ended).
+__global__ void label_keys_kernel(const int32_t* order, const int64_t* count, const int64_t* token_off,
+                                  const int32_t* ids, const int32_t* owners, int32_t depth, uint32_t* keys) {
+  const int64_t n = *count;
+  for (int64_t k = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; k < n;
+       k += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int32_t i = order[k];
+    if (depth < 0) {
+      keys[k] = static_cast<uint32_t>(owners[i]);
+    } else {
+      const int64_t at = token_off[i] + depth;
+      keys[k] = at < token_off[i + 1] ? static_cast<uint32_t>(ids[at]) + 1u : 0u;
+    }
+  }
+}
+
+__global__ void row_lengths_kernel(const int32_t* order, const int64_t* count, const int64_t* token_off,
+                                   const int32_t* owners, int64_t* lengths, int32_t* row_owners) {
+  const int64_t n = *count;
+  for (int64_t k = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; k < n;
+       k += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int32_t i = order[k];
+    lengths[k] = token_off[i + 1] - token_off[i];
+    row_owners[k] = owners[i];
+  }
+}
+
+// One warp per row: its tokens to their place in the row-ordered token array.
+__global__ void row_tokens_kernel(const int32_t* order, const int64_t* count, const int64_t* token_off,
+                                  const int32_t* ids, const int64_t* row_offsets, int32_t* row_tokens) {
+  const int64_t n = *count;
+  const int32_t lane = threadIdx.x & 31;
+  const int64_t warps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t k = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5; k < n; k += warps) {
+    const int32_t i = order[k];
+    const int64_t from = token_off[i], len = token_off[i + 1] - from, to = row_offsets[k];
+    for (int64_t j = lane; j < len; j += 32) row_tokens[to + j] = ids[from + j];
+  }
+}
+
 }  // namespace build
 }  // namespace xg
 
@@ -221,5 +333,107 @@ extern "C" XG_API int xg_build_adjacency(const int32_t* subjects, const int32_t*
                   "adjacency offsets");
   XG_BUILD_CUDA(cudaMemcpyAsync(edges, count, sizeof(int64_t), cudaMemcpyDeviceToHost, s), "adjacency count");
   XG_BUILD_CUDA(cudaStreamSynchronize(s), "adjacency build");
+  return XG_OK;
+}
+
+extern "C" XG_API int xg_build_label_rows(int32_t labels, const int64_t* token_off, const int32_t* token_ids,
+                                          int64_t token_count, const int64_t* text_off, const uint8_t* text,
+                                          int64_t text_bytes, const int32_t* owners, int32_t owner_count,
+                                          int32_t vocab, const int64_t* vocab_off, const uint8_t* vocab_bytes,
+                                          int64_t vocab_byte_count, const int8_t* vocab_kind, int32_t* status,
+                                          int64_t* row_offsets, int32_t* row_tokens, int32_t* row_owners,
+                                          int32_t* rows, int64_t* tokens, void* stream) {
+  if (!rows || !tokens) return build_fail(XG_EINVAL, "null rows or tokens output");
+  if (labels < 0 || token_count < 0 || text_bytes < 0 || owner_count < 0 || vocab <= 0 || vocab_byte_count < 0)
+    return build_fail(XG_EINVAL, "negative size or empty vocabulary");
+  if (!token_off || !text_off || !vocab_off || !vocab_kind || !status || !row_offsets ||
+      (labels > 0 && (!owners || !row_owners)) || (token_count > 0 && (!token_ids || !row_tokens)) ||
+      (text_bytes > 0 && !text) || (vocab_byte_count > 0 && !vocab_bytes))
+    return build_fail(XG_EINVAL, "null label, text or vocabulary array");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  *rows = 0;
+  *tokens = 0;
+  XG_BUILD_CUDA(cudaMemsetAsync(row_offsets, 0, sizeof(int64_t), s), "label rows");
+  if (labels == 0) {
+    XG_BUILD_CUDA(cudaStreamSynchronize(s), "label rows");
+    return XG_OK;
+  }
+  Scratch scratch(s);
+  int32_t *selected = nullptr, *order = nullptr, *swap = nullptr, *length = nullptr, *longest = nullptr;
+  uint8_t* admitted = nullptr;
+  int64_t* count = nullptr;
+  unsigned long long* bad = nullptr;
+  uint32_t *keys = nullptr, *keys_out = nullptr;
+  int64_t* lengths = nullptr;
+  XG_BUILD_CUDA(scratch.get(&selected, sizeof(int32_t) * labels), "label scratch");
+  XG_BUILD_CUDA(scratch.get(&order, sizeof(int32_t) * labels), "label scratch");
+  XG_BUILD_CUDA(scratch.get(&swap, sizeof(int32_t) * labels), "label scratch");
+  XG_BUILD_CUDA(scratch.get(&length, sizeof(int32_t) * labels), "label scratch");
+  XG_BUILD_CUDA(scratch.get(&admitted, labels), "label scratch");
+  XG_BUILD_CUDA(scratch.get(&count, 3 * sizeof(int64_t)), "label scratch");  // count, longest, bad: 8 bytes each
+  longest = reinterpret_cast<int32_t*>(count + 1);
+  bad = reinterpret_cast<unsigned long long*>(count + 2);
+  XG_BUILD_CUDA(scratch.get(&keys, sizeof(uint32_t) * labels), "label scratch");
+  XG_BUILD_CUDA(scratch.get(&keys_out, sizeof(uint32_t) * labels), "label scratch");
+  XG_BUILD_CUDA(scratch.get(&lengths, sizeof(int64_t) * labels), "label scratch");
+  XG_BUILD_CUDA(cudaMemsetAsync(bad, 0, sizeof(unsigned long long), s), "label scratch");
+  admit_labels_kernel<<<grid_for(static_cast<int64_t>(labels) * 32), kThreads, 0, s>>>(
+      labels, token_off, token_ids, token_count, text_off, text, text_bytes, owners, owner_count, vocab, vocab_off,
+      vocab_bytes, vocab_byte_count, vocab_kind, status, selected, admitted, length, bad);
+  XG_BUILD_CUDA(cudaGetLastError(), "label admission kernel");
+  const int32_t token_bits = bits_for(static_cast<int64_t>(vocab) + 1), owner_bits = bits_for(owner_count);
+  size_t select_bytes = 0, max_bytes = 0, sort_bytes = 0, scan_bytes = 0;
+  XG_BUILD_CUDA(cub::DeviceSelect::Flagged(nullptr, select_bytes, selected, admitted, order, count, labels, s),
+                "label select");
+  XG_BUILD_CUDA(cub::DeviceReduce::Max(nullptr, max_bytes, length, longest, labels, s), "label lengths");
+  XG_BUILD_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, sort_bytes, keys, keys_out, order, swap, labels, 0,
+                                                token_bits > owner_bits ? token_bits : owner_bits, s),
+                "label sort");
+  XG_BUILD_CUDA(cub::DeviceScan::InclusiveSum(nullptr, scan_bytes, lengths, row_offsets + 1, labels, s),
+                "label offsets");
+  size_t need = select_bytes > max_bytes ? select_bytes : max_bytes;
+  need = need > sort_bytes ? need : sort_bytes;
+  need = need > scan_bytes ? need : scan_bytes;
+  void* work = nullptr;
+  XG_BUILD_CUDA(scratch.get(&work, need), "label scratch");
+  XG_BUILD_CUDA(cub::DeviceSelect::Flagged(work, select_bytes, selected, admitted, order, count, labels, s),
+                "label select");
+  XG_BUILD_CUDA(cub::DeviceReduce::Max(work, max_bytes, length, longest, labels, s), "label lengths");
+  int64_t admitted_rows = 0;
+  int32_t depth_count = 0;
+  unsigned long long bad_host = 0;
+  XG_BUILD_CUDA(cudaMemcpyAsync(&admitted_rows, count, sizeof(int64_t), cudaMemcpyDeviceToHost, s), "label count");
+  XG_BUILD_CUDA(cudaMemcpyAsync(&depth_count, longest, sizeof(int32_t), cudaMemcpyDeviceToHost, s), "label count");
+  XG_BUILD_CUDA(cudaMemcpyAsync(&bad_host, bad, sizeof(bad_host), cudaMemcpyDeviceToHost, s), "label count");
+  XG_BUILD_CUDA(cudaStreamSynchronize(s), "label count");
+  if (bad_host) return build_fail(XG_EINVAL, "label or vocabulary offsets outside their arrays, or an owner out of range");
+  if (admitted_rows == 0) {
+    XG_BUILD_CUDA(cudaStreamSynchronize(s), "label rows");
+    return XG_OK;
+  }
+  const int n = static_cast<int>(admitted_rows);
+  // LSD: the owner first (least significant), then depths from the deepest to the first
+  for (int32_t depth = -1; depth < depth_count; ++depth) {
+    const int32_t d = depth < 0 ? -1 : depth_count - 1 - depth;
+    label_keys_kernel<<<grid_for(n), kThreads, 0, s>>>(order, count, token_off, token_ids, owners, d, keys);
+    XG_BUILD_CUDA(cudaGetLastError(), "label key kernel");
+    XG_BUILD_CUDA(cub::DeviceRadixSort::SortPairs(work, sort_bytes, keys, keys_out, order, swap, n, 0,
+                                                  d < 0 ? (owner_bits > 0 ? owner_bits : 1) : token_bits, s),
+                  "label sort");
+    int32_t* t = order;
+    order = swap;
+    swap = t;
+  }
+  row_lengths_kernel<<<grid_for(n), kThreads, 0, s>>>(order, count, token_off, owners, lengths, row_owners);
+  XG_BUILD_CUDA(cudaGetLastError(), "label length kernel");
+  XG_BUILD_CUDA(cub::DeviceScan::InclusiveSum(work, scan_bytes, lengths, row_offsets + 1, n, s), "label offsets");
+  row_tokens_kernel<<<grid_for(static_cast<int64_t>(n) * 32), kThreads, 0, s>>>(order, count, token_off, token_ids,
+                                                                              row_offsets, row_tokens);
+  XG_BUILD_CUDA(cudaGetLastError(), "label token kernel");
+  int64_t total = 0;
+  XG_BUILD_CUDA(cudaMemcpyAsync(&total, row_offsets + n, sizeof(int64_t), cudaMemcpyDeviceToHost, s), "label count");
+  XG_BUILD_CUDA(cudaStreamSynchronize(s), "label rows");
+  *rows = n;
+  *tokens = total;
   return XG_OK;
 }

@@ -151,6 +151,11 @@ struct Tables {
   int32_t versions;
   int32_t vocab, words, words_padded, entities, relations, relation_words;
   int32_t escapes, repeats, derivation, paths, bound_escapes, committed, end_after_answer;
+  // apply_mask's logit policies (off: release_on 0, escape_bias 0): release a span row to
+  // the escape marker when its log allowed mass is below release_log_mass, or (release_top)
+  // when its own top token is disallowed; add escape_bias to the tokens that commit to it.
+  float release_log_mass, escape_bias;
+  int32_t release_top, release_on;
   // per-slot engine buffers
   XgState* states;
   int32_t* memory;
@@ -1571,6 +1576,45 @@ XG_HD void build_mask(const Ctx& c, const XgState& s) {
   if (c.w.leader()) {
     t.base[c.slot] = m.base;
     t.delta[c.slot] = m.delta;
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// apply_mask's logit policies, release and escape bias (csrc/engine.cu:2416-2450 of the
+// reference: where a span row's escape marker stands, and which tokens commit to it).
+
+// The byte position the row's escape marker goes on from -- where it stands once started,
+// 0 where it may start here (a live label with escapes allowed) -- when some token takes it
+// further; -1 outside a span or with no way on.  A released row may write only the
+// marker's next tokens from there.
+XG_HD int32_t escape_position(const Tables& t, const XgState& s) {
+  if (s.phase != kSpan) return -1;
+  const int32_t pos = s.esc_pos;
+  if (delim_end(t.escape, pos) <= delim_begin(t.escape, pos)) return -1;
+  return pos > 0 || (s.flags & kMayEsc) ? pos : -1;
+}
+
+// f(token), on every lane, for each token that commits the row to the escape marker: where
+// the marker may start and has not, each token that starts it and continues neither the
+// label nor the separator or closer (live, or startable here).  The tokens are distinct
+// and all allowed in the row's mask.
+template <class F>
+XG_HD void for_each_escape_commit(const Ctx& c, const XgState& s, F f) {
+  const Tables& t = c.t;
+  if (s.phase != kSpan || s.esc_pos != 0 || !(s.flags & kMayEsc)) return;
+  const int32_t close = s.close_pos > 0 ? s.close_pos : (s.flags & kMayClose) ? 0 : -1;
+  const int32_t sep = s.sep_pos > 0 ? s.sep_pos : (s.flags & kMaySep) ? 0 : -1;
+  const Rows& rows = s.segment == kRelation ? t.rel : t.ent;
+  const int32_t a = delim_begin(t.escape, 0), b = delim_end(t.escape, 0);
+#pragma unroll 1
+  for (int32_t i = a; i < b; ++i) {
+    const int32_t token = t.escape.tok[i];
+    if (close >= 0 && delim_step(t.closer, close, token) >= 0) continue;
+    if (sep >= 0 && delim_step(t.separator, sep, token) >= 0) continue;
+    int32_t lo = s.lo, hi = s.hi;
+    narrow(c.w, rows, lo, hi, s.depth, token);
+    if (has_candidate(c, s, lo, hi)) continue;
+    f(token);
   }
 }
 

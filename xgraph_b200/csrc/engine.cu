@@ -1,15 +1,17 @@
 // sm_100a kernels and the C ABI of the KG constraint engine.
 //
-// Per decoding step the serving path runs two kernels:
-//   step_kernel   one warp per request row: consume the row's new tokens (advance or
-//                 sync over the token history in place) and rebuild the row's
-//                 allowed-token bitmask for its new state (core.cuh);
-//   apply_kernel  a flat grid over (logits row, 8192-column chunk): read 8 mask bits per
-//                 thread and write -inf over every disallowed column with 16-byte stores,
-//                 leaving allowed columns untouched (HBM-write bound).
-// The reference runs the same step as sync_kernel + row_mask_kernel + apply_kernel
-// (csrc/engine.cu:2057-2074, 2372-2451, 2562-2587); here the mask is built where the
-// state changes, so apply_mask is a single bandwidth kernel.
+// Per decoding step the serving path runs one kernel, sync_apply_kernel: a CTA per request
+// row whose warp 0 applies the row's admission, consumes its new tokens and rebuilds its
+// allowed-token bitmask (core.cuh), after which all eight warps write -inf over the row's
+// disallowed columns.  The separate entry points run the same pieces apart: step_kernel
+// (one warp per row: advance or sync, mask rebuilt where the state changes) and
+// apply_kernel (a flat grid over row chunks writing -inf, HBM-write bound); draft rows and
+// the logit policies (release, escape bias), which need a whole row per CTA, use
+// draft_apply_kernel.  The reference runs a step as sync_kernel + row_mask_kernel +
+// [escape_bias_kernel] + [release_kernel] + apply_kernel (csrc/engine.cu:2057-2074,
+// 2372-2587).
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -325,6 +327,162 @@ __device__ __forceinline__ void apply_scalar(const Tables& t, char* out, int64_t
   }
 }
 
+// ---------------------------------------------------------------------------------------
+// Logit policies of apply_mask: escape bias and release (csrc/engine.cu:2416-2552 of the
+// reference).  A row's CTA runs them between building its mask and writing its -inf:
+// warp 0 adds the bias, then the whole CTA reads the row once for its allowed mass and, if
+// the row is released, replaces the mask it writes with the escape marker's next tokens.
+
+// One logit as fp32 (ELT 2: bfloat16, or float16 when f16) and back, rounded to nearest.
+template <int ELT>
+__device__ __forceinline__ float load_logit(const char* at, bool f16) {
+  if (ELT == 4) return *reinterpret_cast<const float*>(at);
+  const uint16_t bits = *reinterpret_cast<const uint16_t*>(at);
+  return f16 ? __half2float(__ushort_as_half(bits)) : __uint_as_float(static_cast<uint32_t>(bits) << 16);
+}
+
+template <int ELT>
+__device__ __forceinline__ void store_logit(char* at, float value, bool f16) {
+  if (ELT == 4)
+    *reinterpret_cast<float*>(at) = value;
+  else if (f16)
+    *reinterpret_cast<__half*>(at) = __float2half_rn(value);
+  else
+    *reinterpret_cast<__nv_bfloat16*>(at) = __float2bfloat16_rn(value);
+}
+
+// Warp: escape_bias added to the row's tokens that commit to the escape marker (all
+// allowed, so none of the row's -inf writes touches them).
+template <int ELT>
+__device__ void add_escape_bias(const Ctx& c, const XgState& s, char* out, int32_t cols, bool f16) {
+  for_each_escape_commit(c, s, [&](int32_t token) {
+    if (c.w.leader() && token < cols) {
+      char* at = out + static_cast<int64_t>(token) * ELT;
+      store_logit<ELT>(at, load_logit<ELT>(at, f16) + c.t.escape_bias, f16);
+    }
+  });
+}
+
+// A row's softmax mass in one pass: the top logit (lowest column among equal maxima), and
+// the sums of exp(logit - top) over all columns and over the allowed ones, kept relative
+// to the running top and rescaled when it rises.  exp(y) is taken as exp2(y · log2 e) (one
+// multiply before the exp2 unit).  The reference reads the row twice (the top first, then
+// the sums with expf); the sums agree to a few float roundings.
+struct RowMass {
+  float top;
+  int32_t at;
+  float all, allowed;
+};
+
+constexpr float kLog2E = 1.4426950408889634f;  // log2(e)
+
+__device__ __forceinline__ float exp_of(float y) { return exp2f(y * kLog2E); }
+
+__device__ __forceinline__ void mass_add(RowMass& m, float x, int32_t col, bool ok) {
+  if (x > m.top) {  // NaN never rises
+    const float scale = m.top == -INFINITY ? 0.0f : exp_of(m.top - x);
+    m.all *= scale;
+    m.allowed *= scale;
+    m.top = x;
+    m.at = col;
+  }
+  // below a top of -inf only -inf (adds 0) or NaN (carried, as the reference's sum carries it)
+  const float e = m.top == -INFINITY ? (x != x ? x : 0.0f) : exp_of(x - m.top);
+  m.all += e;
+  if (ok) m.allowed += e;
+}
+
+__device__ __forceinline__ RowMass mass_merge(const RowMass& a, const RowMass& b) {
+  const bool second = b.top > a.top || (b.top == a.top && b.at < a.at);
+  const float top = second ? b.top : a.top;
+  const float fa = a.top == -INFINITY ? 0.0f : exp_of(a.top - top);
+  const float fb = b.top == -INFINITY ? 0.0f : exp_of(b.top - top);
+  return RowMass{top, second ? b.at : a.at, a.all * fa + b.all * fb, a.allowed * fa + b.allowed * fb};
+}
+
+// The 16-byte vector k of a logits row into the running mass (columns k·per ..).
+template <int ELT>
+__device__ __forceinline__ void mass_vector(RowMass& m, const uint4& v, int32_t col, uint32_t bits, bool f16) {
+  constexpr int32_t per = 16 / ELT;
+  const uint32_t lanes[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int32_t j = 0; j < per; ++j) {
+    float x;
+    if (ELT == 4) {
+      x = __uint_as_float(lanes[j]);
+    } else {
+      const uint32_t half = (lanes[j >> 1] >> (16 * (j & 1))) & 0xffffu;
+      x = f16 ? __half2float(__ushort_as_half(static_cast<uint16_t>(half))) : __uint_as_float(half << 16);
+    }
+    mass_add(m, x, col + j, (bits >> j) & 1u);
+  }
+}
+
+constexpr int32_t kMassBatch = 4;  // 16-byte loads a thread issues before it uses them
+
+// Whole CTA (every thread gets the same answer): whether the row, columns [0, cols) of the
+// served vocabulary under the mask base | delta, is released (csrc/engine.cu:2479-2552).
+template <int ELT>
+__device__ bool release_row(const Tables& t, const char* out, int32_t cols, const uint32_t* base,
+                            const uint32_t* delta, bool f16) {
+  __shared__ RowMass partial[32];
+  RowMass m{-INFINITY, 0, 0.0f, 0.0f};
+  int32_t tail = 0;  // columns before it were read as 16-byte vectors
+  if ((reinterpret_cast<uintptr_t>(out) & 15u) == 0) {
+    constexpr int32_t per = 16 / ELT;
+    const int32_t vectors = cols / per;
+    const int32_t stride = blockDim.x;
+    // kMassBatch loads in flight per thread; a thread's columns still rise (ties keep the
+    // first)
+    for (int32_t k0 = threadIdx.x; k0 < vectors; k0 += stride * kMassBatch) {
+      uint4 v[kMassBatch];
+#pragma unroll
+      for (int32_t b = 0; b < kMassBatch; ++b) {
+        const int32_t k = k0 + b * stride;
+        v[b] = k < vectors ? *reinterpret_cast<const uint4*>(out + static_cast<int64_t>(k) * 16)
+                           : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int32_t b = 0; b < kMassBatch; ++b) {
+        const int32_t k = k0 + b * stride;
+        if (k < vectors) mass_vector<ELT>(m, v[b], k * per, allowed8(base, delta, t.words, k * per), f16);
+      }
+    }
+    tail = vectors * per;
+  }
+  for (int32_t col = tail + threadIdx.x; col < cols; col += blockDim.x)
+    mass_add(m, load_logit<ELT>(out + static_cast<int64_t>(col) * ELT, f16), col,
+             (mask_word(base, delta, col >> 5) >> (col & 31)) & 1u);
+#pragma unroll
+  for (int32_t d = 16; d > 0; d >>= 1) {
+    const RowMass o{__shfl_xor_sync(0xffffffffu, m.top, d), __shfl_xor_sync(0xffffffffu, m.at, d),
+                    __shfl_xor_sync(0xffffffffu, m.all, d), __shfl_xor_sync(0xffffffffu, m.allowed, d)};
+    m = mass_merge(m, o);
+  }
+  const int32_t warps = blockDim.x >> 5;
+  if ((threadIdx.x & 31) == 0) partial[threadIdx.x >> 5] = m;
+  __syncthreads();
+  RowMass r = partial[0];
+  for (int32_t w = 1; w < warps; ++w) r = mass_merge(r, partial[w]);
+  __syncthreads();  // partial may be reused by the caller's next row
+  if (!isfinite(r.top)) return false;  // no defined distribution: never released
+  const bool top_allowed = (mask_word(base, delta, r.at >> 5) >> (r.at & 31)) & 1u;
+  return (t.release_top && !top_allowed) || logf(r.allowed) - logf(r.all) < t.release_log_mass;
+}
+
+// Whole CTA: `words` (words_padded, shared) becomes the mask of the escape marker's next
+// tokens from byte position pos.
+__device__ void released_mask(const Tables& t, int32_t pos, uint32_t* words) {
+  for (int32_t k = threadIdx.x; k < t.words_padded; k += blockDim.x) words[k] = 0u;
+  __syncthreads();
+  const int32_t a = delim_begin(t.escape, pos), b = delim_end(t.escape, pos);
+  for (int32_t i = a + threadIdx.x; i < b; i += blockDim.x) {
+    const int32_t token = t.escape.tok[i];
+    atomicOr(words + (token >> 5), 1u << (token & 31));
+  }
+  __syncthreads();
+}
+
 // apply_mask: -inf into every disallowed column of every row of an active, non-error
 // slot; a CTA owns a 1/chunks share of one row.  ELT: element bytes (2 or 4); neg: the
 // element's -inf bit pattern.
@@ -440,12 +598,14 @@ __global__ void __maxnreg__(kFusedRegisters)
     sync_apply_kernel(const __grid_constant__ Tables t, const __grid_constant__ FusedArgs f) {
   __shared__ WarpShared shared;
   __shared__ MaskRef use;                               // the mask this CTA applies
+  __shared__ int32_t escape_at;                         // release: the row's escape position, or -1
   __shared__ int32_t delim0[kDelimCopy];                // tokens that start each delimiter
   __shared__ __align__(128) uint32_t blocked_run[kBlockedRunWords];
   extern __shared__ __align__(16) uint32_t composed[];  // [words_padded]: a delta built this step
   const int32_t i = blockIdx.x;
   const int32_t slot = f.a.slots[i];
   const bool valid = slot >= 0 && slot < f.max_slots;
+  const bool f16 = ELT == 2 && f.neg == 0xfc00u;
   // Warp 0's loads of the slot's cursor, lengths and state are issued together with the
   // active flag (and the admission search) rather than after the branch on it.
   const int32_t was_on = valid ? t.active[slot] : 0;
@@ -489,6 +649,17 @@ __global__ void __maxnreg__(kFusedRegisters)
     }
     __syncwarp();
     asm volatile("bar.arrive 1, %0;" ::"r"(blockDim.x) : "memory");
+    // Release reads the whole logits row of a span row: start it into L2 now, while warp 0
+    // runs the state machine (a row that was in a span before this step's tokens; the
+    // prefetch is only a hint, in 32 KB pieces of the 16-byte aligned row).
+    if (t.release_on && was_on && t.states[slot].phase == kSpan) {
+      const char* row = f.logits + static_cast<int64_t>(i) * f.stride * ELT;
+      const int64_t bytes = (reinterpret_cast<uintptr_t>(row) & 15u) == 0 ? (static_cast<int64_t>(min(f.cols, t.vocab)) * ELT) & ~15ll : 0;
+      for (int64_t at = static_cast<int64_t>(threadIdx.x - 32) * 32768; at < bytes; at += static_cast<int64_t>(blockDim.x - 32) * 32768) {
+        const uint32_t piece = static_cast<uint32_t>(bytes - at < 32768 ? bytes - at : 32768);
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(row + at), "r"(piece) : "memory");
+      }
+    }
     // A relation label of a path (base KG): the next frontier reads each frontier entity's
     // relation runs and its edges' folded first rows, two dependent round trips deep in
     // warp 0's transition.  Start those lines into L1 now, one thread per entity (the
@@ -545,6 +716,15 @@ __global__ void __maxnreg__(kFusedRegisters)
       if (threadIdx.x == 0) use = MaskRef{t.base[slot], t.delta[slot]};
     }
     if (threadIdx.x == 0 && on) t.cursors[slot] = cursor;
+    // logit policies of a span row: the escape bias now (before any warp reads the row),
+    // release after the barrier
+    int32_t at = -1;
+    if (on && s.phase == kSpan && (t.release_on || t.escape_bias != 0.0f)) {
+      at = escape_position(t, s);
+      if (t.escape_bias != 0.0f)
+        add_escape_bias<ELT>(c, s, f.logits + static_cast<int64_t>(i) * f.stride * ELT, f.cols, f16);
+    }
+    if (threadIdx.x == 0) escape_at = at;
   }
   __syncthreads();
   const uint32_t* base = use.base;
@@ -563,6 +743,15 @@ __global__ void __maxnreg__(kFusedRegisters)
     const uint4* from = reinterpret_cast<const uint4*>(composed);
     uint4* to = reinterpret_cast<uint4*>(own);
     for (int32_t k = threadIdx.x; k < (t.words_padded >> 2); k += blockDim.x) to[k] = from[k];
+  }
+  // release (block-uniform): the released mask replaces the composed one in shared memory
+  // for this call only (release_row's barriers order every thread's copy above before it)
+  if (escape_at >= 0 && t.release_on &&
+      release_row<ELT>(t, f.logits + static_cast<int64_t>(i) * f.stride * ELT, min(f.cols, t.vocab), base, delta,
+                       f16)) {
+    released_mask(t, escape_at, composed);
+    base = nullptr;
+    delta = composed;
   }
   if (base != nullptr || delta != nullptr) {  // else inactive or error phase: untouched
     char* out = f.logits + static_cast<int64_t>(i) * f.stride * ELT;
@@ -620,15 +809,28 @@ __global__ void __launch_bounds__(kFusedThreads)
                        int64_t stride, uint32_t neg) {
   __shared__ WarpShared shared;
   __shared__ MaskRef mask;
+  __shared__ int32_t escape_at;                         // release: the row's escape position, or -1
+  extern __shared__ __align__(16) uint32_t released[];  // [words_padded] when release is on
   const int32_t row = blockIdx.x;
   const int32_t slot = d.row_slots[row];
   if (slot < 0 || slot >= d.max_slots || !t.active[slot]) return;  // block-uniform
+  const bool f16 = ELT == 2 && neg == 0xfc00u;
+  const bool policies = t.release_on || t.escape_bias != 0.0f;
+  char* out = logits + static_cast<int64_t>(row) * stride * ELT;
   if (threadIdx.x < 32) {
     const int32_t lane = threadIdx.x;
-    const int32_t k = d.local_pos[row];
+    const int32_t k = d.local_pos ? d.local_pos[row] : 0;
     MaskRef m{nullptr, nullptr};
+    int32_t at = -1;
+    // the logit policies of a span row: its escape position for release, and the bias now
+    auto policy = [&](const Ctx& c, const XgState& s) {
+      if (!policies || s.phase != kSpan) return;
+      at = escape_position(t, s);
+      if (t.escape_bias != 0.0f) add_escape_bias<ELT>(c, s, out, cols, f16);
+    };
     if (k == 0) {
       m = MaskRef{t.base[slot], t.delta[slot]};
+      if (policies) policy(make_ctx(t, slot, shared), t.states[slot]);
     } else if (k > 0 && k <= row) {
       int32_t* memory = d.scratch_memory + static_cast<int64_t>(row) * t.memory_ints;
       const int32_t* own = t.memory + static_cast<int64_t>(slot) * t.memory_ints;
@@ -639,14 +841,23 @@ __global__ void __launch_bounds__(kFusedThreads)
       XgState s = t.states[slot];
 #pragma unroll 1
       for (int32_t j = 1; j <= k && s.phase != kError; ++j) advance_state(c, s, d.input_ids[row - k + j]);
-      if (s.phase != kError) m = compose_mask(c, s, d.scratch_masks + static_cast<int64_t>(row) * t.words_padded);
+      if (s.phase != kError) {
+        m = compose_mask(c, s, d.scratch_masks + static_cast<int64_t>(row) * t.words_padded);
+        policy(c, s);
+      }
     }
-    if (lane == 0) mask = m;
+    if (lane == 0) {
+      mask = m;
+      escape_at = at;
+    }
   }
   __syncthreads();
-  const MaskRef m = mask;
+  MaskRef m = mask;
   if (m.base == nullptr && m.delta == nullptr) return;  // error: untouched
-  char* out = logits + static_cast<int64_t>(row) * stride * ELT;
+  if (escape_at >= 0 && t.release_on && release_row<ELT>(t, out, min(cols, t.vocab), m.base, m.delta, f16)) {
+    released_mask(t, escape_at, released);
+    m = MaskRef{nullptr, released};
+  }
   if ((reinterpret_cast<uintptr_t>(out) & 15u) != 0) {
     apply_scalar<ELT>(t, out, 0, cols, m.base, m.delta, neg);
     return;
@@ -976,6 +1187,10 @@ void bind_tables(XgEngine* e) {
   t.bound_escapes = o.bound_escapes;
   t.committed = o.committed_paths;
   t.end_after_answer = o.end_after_answer;
+  t.release_log_mass = o.release_log_mass;
+  t.release_top = o.release_top != 0;
+  t.release_on = o.release_top != 0 || o.release_log_mass > -INFINITY;
+  t.escape_bias = o.escape_bias;
   t.states = e->states;
   t.memory = e->memory;
   t.memory_ints = kMemHave + ((l.relation_words + 3) & ~3);
@@ -1051,6 +1266,10 @@ int create(const void* blob, bool on_device, const XgLayout* layout, const XgOpt
   if (int rc = check_layout(*layout)) return rc;
   if (options->sitelinks_rank && (layout->sitelinks < 0 || layout->row_sitelinks < 0))
     return fail(XG_EINVAL, "the sitelink rank needs a KG index with sitelink counts");
+  if (!(options->release_log_mass < 0.0f))
+    return fail(XG_EINVAL, "release_log_mass must be the log of a mass in (0, 1), or -INFINITY when off");
+  if ((options->release_top || options->release_log_mass > -INFINITY) && !options->escapes)
+    return fail(XG_EINVAL, "release needs escapes: it releases to the escape marker");
   XgEngine* e = new XgEngine();
   e->layout = *layout;
   e->options = *options;
@@ -1095,7 +1314,9 @@ int create(const void* blob, bool on_device, const XgLayout* layout, const XgOpt
   }
   e->composed_bytes = static_cast<size_t>(layout->words_padded) * sizeof(uint32_t);
   for (const void* kernel : {reinterpret_cast<const void*>(sync_apply_kernel<4>),
-                             reinterpret_cast<const void*>(sync_apply_kernel<2>)}) {
+                             reinterpret_cast<const void*>(sync_apply_kernel<2>),
+                             reinterpret_cast<const void*>(draft_apply_kernel<4>),
+                             reinterpret_cast<const void*>(draft_apply_kernel<2>)}) {
     err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(e->composed_bytes));
     if (err != cudaSuccess) {
       release(e);
@@ -1167,7 +1388,8 @@ int noalloc_scratch(int device, char** out) {
   return XG_OK;
 }
 
-// Launch the draft-row kernel with scratch for `rows` rows at `scratch` (memory rows first).
+// Launch the row kernel: draft rows with scratch for `rows` rows at `scratch` (memory rows
+// first), or, without local_pos, every row at its slot's own state (no scratch).
 int launch_drafts(XgEngine* e, char* logits, int32_t dtype, int32_t rows, int32_t cols, int64_t row_stride,
                   const int32_t* row_slots, const int32_t* local_pos, const int32_t* input_ids, char* scratch,
                   void* stream) {
@@ -1176,14 +1398,17 @@ int launch_drafts(XgEngine* e, char* logits, int32_t dtype, int32_t rows, int32_
   d.local_pos = local_pos;
   d.input_ids = input_ids;
   d.max_slots = e->max_sequences;
-  d.scratch_memory = reinterpret_cast<int32_t*>(scratch);
-  d.scratch_masks = reinterpret_cast<uint32_t*>(scratch + static_cast<int64_t>(rows) * e->t.memory_ints * 4);
+  if (scratch) {
+    d.scratch_memory = reinterpret_cast<int32_t*>(scratch);
+    d.scratch_masks = reinterpret_cast<uint32_t*>(scratch + static_cast<int64_t>(rows) * e->t.memory_ints * 4);
+  }
   cudaStream_t s = as_stream(stream);
+  const size_t released = e->t.release_on ? e->composed_bytes : 0;  // a released row's mask
   if (dtype == XG_F32)
-    draft_apply_kernel<4><<<rows, kFusedThreads, 0, s>>>(e->t, d, logits, cols, row_stride, 0xff800000u);
+    draft_apply_kernel<4><<<rows, kFusedThreads, released, s>>>(e->t, d, logits, cols, row_stride, 0xff800000u);
   else
-    draft_apply_kernel<2><<<rows, kFusedThreads, 0, s>>>(e->t, d, logits, cols, row_stride,
-                                                          dtype == XG_BF16 ? 0xff80u : 0xfc00u);
+    draft_apply_kernel<2><<<rows, kFusedThreads, released, s>>>(e->t, d, logits, cols, row_stride,
+                                                                 dtype == XG_BF16 ? 0xff80u : 0xfc00u);
   XG_CUDA(cudaGetLastError(), "draft apply kernel");
   return XG_OK;
 }
@@ -1526,6 +1751,11 @@ int xg_apply_mask(XgEngine* e, void* logits, int32_t dtype, int32_t rows, int32_
     return launch_drafts(e, data_of(logits), dtype, rows, cols, row_stride, row_slots, local_pos, input_ids,
                          e->draft_scratch, stream);
   }
+  // The logit policies need a whole row per CTA: the row kernel, every row at its slot's
+  // own state (no drafts, no scratch).
+  if (e->t.release_on || e->t.escape_bias != 0.0f)
+    return launch_drafts(e, data_of(logits), dtype, rows, cols, row_stride, row_slots, nullptr, nullptr, nullptr,
+                         stream);
   // Split each row into `chunks` CTAs so that the grid is about one wave of resident CTAs
   // (each CTA then runs long enough to hide its few dependent pointer loads).
   const int64_t per_row_max = ((static_cast<int64_t>(cols) + 1023) / 1024 + 7) / 8;  // >= 8 segments per CTA

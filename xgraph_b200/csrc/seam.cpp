@@ -207,6 +207,32 @@ void xgs_memory(SeamEngine* e, int32_t n, int32_t* out) {
 
 int32_t xgs_memory_ints(SeamEngine* e) { return e->t.memory_ints; }
 
+// apply_mask's logit policies for a slot: returns its escape position (-1: release leaves
+// it alone); the tokens that commit it to the escape marker go to commits[0 .. *count) and
+// the escape marker's next tokens from that position (its released mask) to
+// released[0 .. *released_count), each list cut at cap.
+int32_t xgs_escape_policy(SeamEngine* e, int32_t slot, int32_t* commits, int32_t* count, int32_t* released,
+                          int32_t* released_count, int32_t cap) {
+  const Ctx c = ctx(e, slot);
+  const XgState& s = e->states[slot];
+  int32_t n = 0;
+  for_each_escape_commit(c, s, [&](int32_t token) {
+    if (n < cap) commits[n] = token;
+    ++n;
+  });
+  *count = n;
+  const int32_t pos = escape_position(e->t, s);
+  n = 0;
+  if (pos >= 0) {
+    for (int32_t i = delim_begin(e->t.escape, pos); i < delim_end(e->t.escape, pos); ++i) {
+      if (n < cap) released[n] = e->t.escape.tok[i];
+      ++n;
+    }
+  }
+  *released_count = n;
+  return pos;
+}
+
 // The edge range [out[0], out[1]) of `relation` in entity's adjacency (relative to the
 // entity's first edge) and out[2] = the adjacency length, in KG version `version`.
 void xgs_relation_slice(SeamEngine* e, int32_t version, int32_t entity, int32_t relation, int32_t* out) {

@@ -16,6 +16,7 @@ reference accepts it); host token arrays may also be numpy.
 from __future__ import annotations
 
 import ctypes
+import math
 from collections.abc import Iterable
 from dataclasses import dataclass
 from pathlib import Path
@@ -44,6 +45,8 @@ STATE_INTS = 64
 LIBRARY = Path(__file__).resolve().parent / "libxgraph_b200.so"
 
 XG_OK, XG_EINVAL, XG_ECUDA, XG_ENOMEM = 0, 1, 2, 3
+ABI_VERSION = 2
+"""XG_ABI_VERSION of include/xgraph_b200.h that these bindings follow."""
 ADMISSION_INTS = 5 + MAX_REACHED
 """int32 words of one admission record (XgAdmission: slot, on, version, open_span,
 anchor_count, 64 anchor rows)."""
@@ -51,7 +54,7 @@ DTYPES = {"float32": 0, "bfloat16": 1, "float16": 2}
 
 # Reference constructor options this engine does not serve, with their neutral values.
 _NOT_SERVED = {
-    "release_mass": 0.0, "release_top": False, "escape_bias": 0.0, "expressions": False,
+    "expressions": False,
     "stop": None, "relations": "frontier", "observe": 0, "observe_width": 0,
     "observe_defer": 0, "menu_close_next": False, "observe_select": False,
     "observe_answer": False, "observe_required": False, "observe_no_loop": False,
@@ -109,12 +112,14 @@ def load_library(path: Path = LIBRARY):
         "xg_add_version": ([p, p, i32, p, p, p, p, ctypes.POINTER(i32)], ctypes.c_int),
         "xg_drop_version": ([p, i32, p], ctypes.c_int),
         "xg_build_adjacency": ([p, p, p, i64, p, p, i32, i32, p, i32, i64, p, p, p, p, p, p], ctypes.c_int),
+        "xg_build_label_rows": ([i32, p, p, i64, p, p, i64, p, i32, i32, p, p, i64, p, p, p, p, p, p, p, p],
+                                ctypes.c_int),
     }
     for name, (args, res) in sigs.items():
         fn = getattr(lib, name)
         fn.argtypes, fn.restype = args, res
-    if lib.xg_abi_version() != 1:
-        raise EngineUnavailable(f"{path} has ABI {lib.xg_abi_version()}, expected 1")
+    if lib.xg_abi_version() != ABI_VERSION:
+        raise EngineUnavailable(f"{path} has ABI {lib.xg_abi_version()}, expected {ABI_VERSION} (rebuild it)")
     _lib = lib
     return lib
 
@@ -170,7 +175,16 @@ class Engine:
 
     Construction validates the options in the reference's order
     (src/xgraph/engine.py:817-901), packs the index (tables.pack_tables) and copies it
-    to the current CUDA device with `max_sequences` slots, all inactive."""
+    to the current CUDA device with `max_sequences` slots, all inactive.
+
+    The logit policies act in apply_mask (and sync_apply, which includes it) inside spans,
+    as the reference's (src/xgraph/engine.py:626-640): with release_mass > 0 a row whose
+    logits put less than that share of their softmax (over the served vocabulary, at the
+    logits' own temperature) on the allowed set, and with release_top a row whose own top
+    token is disallowed, may write only the escape marker's next tokens; release is per
+    call and leaves the slot's recorded mask alone.  escape_bias is added to the logits of
+    the tokens that commit to the escape marker (16-bit logits hold the sum rounded to
+    nearest)."""
 
     def __init__(
         self,
@@ -181,7 +195,10 @@ class Engine:
         *,
         escapes: bool = True,
         repeats: bool = True,
+        release_mass: float = 0.0,
+        release_top: bool = False,
         derivation: bool = False,
+        escape_bias: float = 0.0,
         paths: bool = False,
         bound_escapes: bool = True,
         committed_paths: bool = False,
@@ -214,6 +231,10 @@ class Engine:
             if value != _NOT_SERVED[name]:
                 raise ValueError(f"the {name} policy is not served by this engine")
         sitelinks_rank = check_start_rank(start_rank, index) == "sitelinks"
+        if not escapes and (release_mass > 0 or release_top):
+            raise ValueError("release needs escapes: it releases to the escape marker")
+        if not 0.0 <= release_mass < 1.0:
+            raise ValueError(f"release_mass must be in [0, 1), got {release_mass}")
         if max_sequences < 1:
             raise ValueError(f"max_sequences must be at least 1, got {max_sequences}")
         for name in ("opener", "separator", "closer", "escape"):
@@ -236,6 +257,9 @@ class Engine:
             escapes=int(escapes), repeats=int(repeats), derivation=int(derivation or paths),
             paths=int(paths), bound_escapes=int(bound_escapes), committed_paths=int(committed_paths),
             sitelinks_rank=int(sitelinks_rank), end_after_answer=int(end_after_answer),
+            release_top=int(bool(release_top)),
+            release_log_mass=math.log(release_mass) if release_mass > 0 else -math.inf,
+            escape_bias=float(escape_bias),
         )
         handle = ctypes.c_void_p()
         if device_blob is None:

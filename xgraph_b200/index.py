@@ -23,6 +23,7 @@ from __future__ import annotations
 import bisect
 import hashlib
 import json
+import re
 from collections.abc import Mapping, Sequence
 from dataclasses import dataclass, field, replace
 from pathlib import Path
@@ -128,15 +129,39 @@ def _sorted_rows(rows: list[tuple[list[int], int]]) -> list[int]:
     return np.lexsort(keys).tolist()
 
 
+def _excluder(syntax: SpanSyntax):
+    """SpanSyntax.excludes as one compiled test: a delimiter or the operand separator
+    anywhere in the written label, or an operator at its start."""
+    inner = [*syntax.delimiters, *([syntax.operand_separator] if syntax.operand_separator else [])]
+    anywhere = re.compile("|".join(re.escape(d) for d in inner))
+    starts = tuple(syntax.label_prefix + op for op in syntax.operators)
+    prefix = syntax.label_prefix
+
+    def excludes(label: str) -> bool:
+        written = prefix + label
+        return anywhere.search(written) is not None or (bool(starts) and written.startswith(starts))
+
+    return excludes
+
+
+ADMISSION_REASONS = {1: "label contains a special token", 2: "empty label encoding",
+                     3: "label contains a token with unknown bytes", 4: "label bytes do not round-trip"}
+"""Reasons of the exact-v1 admission failures, by the device build's status code."""
+
+
 def label_rows(
     items: Sequence[Entity | Relation] | Sequence[tuple[str, Sequence[str]]],
     tokenizer: ServedTokenizer,
     syntax: SpanSyntax,
+    device=None,
 ) -> LabelIndex:
-    """The label index over these items' labels (src/xgraph/index.py:181-233)."""
+    """The label index over these items' labels (src/xgraph/index.py:181-233).  With
+    `device` (a CUDA device) the admission checks, the row sort and the row arrays run
+    there (xg_build_label_rows); the tokenizer encodes on the host either way."""
     pairs: list[tuple[str, int]] = []
     excluded: list[ExcludedLabel] = []
     ids: list[str] = []
+    excludes = _excluder(syntax)
     for position, item in enumerate(items):
         item_id, labels = (item.id, item.labels) if hasattr(item, "id") else item
         ids.append(item_id)
@@ -147,11 +172,17 @@ def label_rows(
             seen.add(label)
             if not label.strip():
                 excluded.append(ExcludedLabel(item_id, label, "blank label"))
-            elif syntax.excludes(label):
+            elif excludes(label):
                 excluded.append(ExcludedLabel(item_id, label, "label contains span syntax"))
             else:
                 pairs.append((label, position))
     encoded = tokenizer.encode_batch([syntax.label_prefix + label for label, _ in pairs])
+    if device is not None:
+        tokens, offsets, owners, status = _label_rows_device(pairs, encoded, len(ids), tokenizer, syntax, device)
+        excluded.extend(ExcludedLabel(ids[pairs[i][1]], pairs[i][0], ADMISSION_REASONS[int(status[i])])
+                        for i in np.flatnonzero(status))
+        return LabelIndex(tokens=tokens, offsets=offsets, owners=owners, owner_ids=tuple(ids),
+                          tokenizer_fingerprint=tokenizer.fingerprint, excluded=tuple(excluded))
     rows: list[tuple[list[int], int]] = []
     for (label, position), tokens in zip(pairs, encoded, strict=True):
         reason = _exact_v1_error(label, tokens, tokenizer, syntax)
@@ -175,6 +206,59 @@ def label_rows(
         tokenizer_fingerprint=tokenizer.fingerprint,
         excluded=tuple(excluded),
     )
+
+
+def _label_rows_device(pairs, encoded, owner_count: int, tokenizer: ServedTokenizer, syntax: SpanSyntax, device):
+    """label_rows' admission and row arrays on a GPU (xg_build_label_rows): (tokens,
+    offsets, owners, status per pair), the same arrays as the host build's."""
+    import ctypes
+    import itertools
+
+    import torch
+
+    from .engine import _check, load_library
+
+    lib = load_library()
+    device = torch.device(device)
+    if device.type != "cuda":
+        raise ValueError(f"the device label build needs a CUDA device, got {device}")
+    n = len(pairs)
+    lengths = np.fromiter(map(len, encoded), dtype=np.int64, count=n)
+    token_off = np.zeros(n + 1, dtype=np.int64)
+    np.cumsum(lengths, out=token_off[1:])
+    token_ids = np.fromiter(itertools.chain.from_iterable(encoded), dtype=np.int32, count=int(token_off[-1]))
+    written = [(syntax.label_prefix + label).encode("utf-8") for label, _ in pairs]
+    text_off = np.zeros(n + 1, dtype=np.int64)
+    np.cumsum(np.fromiter(map(len, written), dtype=np.int64, count=n), out=text_off[1:])
+    text = np.frombuffer(bytearray(b"".join(written)), dtype=np.uint8)
+    owners = np.fromiter((position for _, position in pairs), dtype=np.int32, count=n)
+    vocab_off, vocab_bytes, vocab_kind = tokenizer.byte_table()
+    with torch.cuda.device(device):
+        def put(array, dtype):
+            return torch.from_numpy(np.ascontiguousarray(array)).to(device=device, dtype=dtype)
+
+        def ptr(t):
+            return ctypes.c_void_p(t.data_ptr())
+
+        d_token_off, d_ids = put(token_off, torch.int64), put(token_ids, torch.int32)
+        d_text_off, d_text = put(text_off, torch.int64), put(text, torch.uint8)
+        d_owners = put(owners, torch.int32)
+        d_vocab_off, d_vocab_bytes = put(vocab_off, torch.int64), put(vocab_bytes, torch.uint8)
+        d_kind = put(vocab_kind, torch.int8)
+        status = torch.empty(max(n, 1), dtype=torch.int32, device=device)
+        row_offsets = torch.empty(n + 1, dtype=torch.int64, device=device)
+        row_tokens = torch.empty(max(len(token_ids), 1), dtype=torch.int32, device=device)
+        row_owners = torch.empty(max(n, 1), dtype=torch.int32, device=device)
+        rows, total = ctypes.c_int32(), ctypes.c_int64()
+        stream = ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+        _check(lib.xg_build_label_rows(
+            n, ptr(d_token_off), ptr(d_ids), len(token_ids), ptr(d_text_off), ptr(d_text), len(text), ptr(d_owners),
+            owner_count, len(vocab_kind), ptr(d_vocab_off), ptr(d_vocab_bytes), len(vocab_bytes), ptr(d_kind),
+            ptr(status), ptr(row_offsets), ptr(row_tokens), ptr(row_owners), ctypes.byref(rows), ctypes.byref(total),
+            stream))
+        r, t = rows.value, total.value
+        return (row_tokens[:t].cpu().numpy(), row_offsets[: r + 1].cpu().numpy(), row_owners[:r].cpu().numpy(),
+                status[:n].cpu().numpy())
 
 
 def entity_row_lists(labels: LabelIndex) -> tuple[np.ndarray, np.ndarray]:
@@ -358,8 +442,8 @@ def build_kg_index_arrays(
         or triples[:, 1].max() >= len(relations)
     ):
         raise KGFormatError("triples name entity or relation positions outside the KG")
-    labels = label_rows(entities, tokenizer, syntax)
-    relation_index = label_rows(relations, tokenizer, syntax)
+    labels = label_rows(entities, tokenizer, syntax, device=device)
+    relation_index = label_rows(relations, tokenizer, syntax, device=device)
     writable = np.zeros(len(relations), dtype=bool)
     writable[np.asarray(relation_index.owners, dtype=np.int64)] = True
     if device is None:

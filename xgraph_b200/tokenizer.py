@@ -139,6 +139,23 @@ class ServedTokenizer:
     def token_bytes(self, token: int) -> bytes | None:
         return self._token_bytes[token] if 0 <= token < len(self._token_bytes) else None
 
+    def byte_table(self):
+        """Every id of the byte view as CSR: (offsets int64 [n + 1], bytes uint8, kind int8
+        [n]: 0 known bytes, 1 special, 2 unknown bytes), n = the ids the view covers."""
+        import numpy as np
+
+        cached = getattr(self, "_byte_table", None)
+        if cached is None:
+            table = self._token_bytes
+            kind = np.array([1 if t in self._special_ids else 2 if b is None else 0 for t, b in enumerate(table)],
+                            dtype=np.int8)
+            lengths = np.fromiter((0 if b is None else len(b) for b in table), dtype=np.int64, count=len(table))
+            offsets = np.zeros(len(table) + 1, dtype=np.int64)
+            np.cumsum(lengths, out=offsets[1:])
+            data = np.frombuffer(bytearray(b"".join(b for b in table if b is not None)), dtype=np.uint8)
+            cached = self._byte_table = (offsets, data, kind)
+        return cached
+
     def all_token_bytes(self) -> list[bytes | None]:
         """Every id's bytes, in id order (a copy)."""
         return list(self._token_bytes[: self.vocab_size]) + [None] * max(

@@ -25,11 +25,11 @@ which the engine replays as if the model had written it; a prompt whose last tok
 end with the text's bytes, or a replayed token the mask disallows, declines the request,
 which is then left unmasked), `xgraph_replay_id` (the key under which a replay's outcome is
 kept for `replay_statuses`).  Engine settings: XGRAPH_ESCAPES, XGRAPH_REPEATS,
-XGRAPH_DERIVATION, XGRAPH_PATHS, XGRAPH_BOUND_ESCAPES, XGRAPH_COMMITTED_PATHS,
-XGRAPH_START_RANK, XGRAPH_UNQUOTED_STARTS, XGRAPH_END_AFTER_ANSWER.  The reference's
-research policies (release, escape bias, STOP, expressions, observations, menus, audit,
-relation supports, per-request path options) are not served by this engine: a setting or
-argument that asks for one is refused with a ValueError naming it.
+XGRAPH_RELEASE_MASS, XGRAPH_RELEASE_TOP, XGRAPH_DERIVATION, XGRAPH_ESCAPE_BIAS, XGRAPH_PATHS,
+XGRAPH_BOUND_ESCAPES, XGRAPH_COMMITTED_PATHS, XGRAPH_START_RANK, XGRAPH_UNQUOTED_STARTS,
+XGRAPH_END_AFTER_ANSWER.  The reference's research policies (STOP, expressions,
+observations, menus, audit, relation supports, per-request path options) are not served by
+this engine: a setting or argument that asks for one is refused with a ValueError naming it.
 
 This module imports only the standard library at import time: vLLM also calls
 validate_params in its frontend process.
@@ -68,7 +68,6 @@ REPLAYS = ("replayed", "tail mismatch", "disallowed")
 
 _UNSERVED_ARGS = ("xgraph_relation_ranks", "xgraph_path_options")
 _UNSERVED_SETTINGS = {  # setting: the value that keeps the policy off
-    "XGRAPH_RELEASE_MASS": "0", "XGRAPH_RELEASE_TOP": "0", "XGRAPH_ESCAPE_BIAS": "0",
     "XGRAPH_EXPRESSIONS": "0", "XGRAPH_STOP": "", "XGRAPH_OBSERVE": "0", "XGRAPH_OBSERVE_SELECT": "0",
     "XGRAPH_OBSERVE_ANSWER": "0", "XGRAPH_OBSERVE_WIDTH": "0", "XGRAPH_OBSERVE_DEFER": "0",
     "XGRAPH_OBSERVE_TERMINAL": "0", "XGRAPH_MENU": "0", "XGRAPH_MENU_CLOSE_NEXT": "0", "XGRAPH_AUDIT": "0",
@@ -270,7 +269,14 @@ class XGraphLogitsProcessor(_Base):
             index, tokenizer, index.span_syntax, req_states.max_num_reqs,
             escapes=os.environ.get("XGRAPH_ESCAPES", "1") != "0",
             repeats=os.environ.get("XGRAPH_REPEATS", "1") != "0",
+            # release a span's step to the escape marker when the model puts less than
+            # XGRAPH_RELEASE_MASS on the allowed set, or (XGRAPH_RELEASE_TOP=1) when its
+            # own top token is disallowed; XGRAPH_ESCAPE_BIAS is added to the logits of
+            # the tokens that commit to the escape (src/xgraph/vllm.py:319-329)
+            release_mass=float(os.environ.get("XGRAPH_RELEASE_MASS", "0")),
+            release_top=os.environ.get("XGRAPH_RELEASE_TOP", "0") == "1",
             derivation=os.environ.get("XGRAPH_DERIVATION", "0") == "1",
+            escape_bias=float(os.environ.get("XGRAPH_ESCAPE_BIAS", "0")),
             paths=os.environ.get("XGRAPH_PATHS", "0") == "1",
             bound_escapes=os.environ.get("XGRAPH_BOUND_ESCAPES", "1") == "1",
             committed_paths=os.environ.get("XGRAPH_COMMITTED_PATHS", "0") == "1",
