@@ -72,6 +72,8 @@ def parse_args():
     p.add_argument("--e2e-steps", type=int, default=32)
     p.add_argument("--profile", action="store_true", help="short run for a profiler (no CPU leg, no e2e)")
     p.add_argument("--max-len", type=int, default=0, help="cap stream lengths (profiling runs)")
+    p.add_argument("--policies", action="store_true",
+                   help="time the step with apply_mask's logit policies on (release, escape bias; fresh logits per step)")
     p.add_argument("--synchronized", action="store_true",
                    help="every row enters its first stream at position 0 at step 0 (default: seeded positions)")
     return p.parse_args()
@@ -513,6 +515,8 @@ def engine_arm(args) -> None:
         blob, meta = torch.from_numpy(packed.blob).to(device), packed
     cfg = workload.config
     options = dict(cfg.options)
+    if args.policies:
+        options.update(release_mass=POLICY_RELEASE_MASS, escape_bias=POLICY_ESCAPE_BIAS)
     vocab = workload.served.vocab_size
     lo, hi = cfg.lengths
     if args.max_len:
@@ -536,6 +540,7 @@ def engine_arm(args) -> None:
     dtype = getattr(torch, cfg.dtype)
     elt = torch.empty(0, dtype=dtype).element_size()
     logits = (torch.randn((rows, vocab), generator=gen, device=device) * 2.0).to(dtype)
+    fresh = logits.clone() if args.policies else None  # the release mass reads the logits: fresh ones each step
     flush = torch.empty(512 * 1024 * 1024 // 4, dtype=torch.int32, device=device)
     engine = Engine(workload.index, workload.served, workload.syntax, rows, device_blob=(blob, meta), **options)
     for name, edits in replay.versions:
@@ -564,6 +569,8 @@ def engine_arm(args) -> None:
             # hold the stream (a bounded spin, outside every event pair) while the host
             # queues the leg's steps, so host launch latency never falls inside a step
             torch.cuda._sleep(HOLD_CYCLES_PER_STEP * (args.steps if timed else warm_steps))
+        if fresh is not None:
+            logits.copy_(fresh)
         if not warm:
             flush.fill_(k)  # evict the logits and tables from L2 between steps
         n = replay.live[k]
@@ -588,7 +595,7 @@ def engine_arm(args) -> None:
     last_slots = replay.step_slots[total_steps - 1]
     apply_alone = (None if args.profile else
                    apply_leg(engine, logits[: len(last_slots)], last_slots, flush, stream, args.steps, elt))
-    policies = (None if args.profile else
+    policies = (None if args.profile or args.policies else
                 policies_leg(workload, replay, (blob, meta), options, prompt, total, flush, stream, device,
                              args.warmup, args.steps, dtype, gen))
     steps_ms = [a.elapsed_time(b) for a, b in step_ms]
@@ -613,7 +620,9 @@ def engine_arm(args) -> None:
         "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": job_ms / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int32", "data": "synthetic",
-        "config": workload_config(cfg, args.config, rows, vocab, lo, hi, world, args.synchronized),
+        "config": {**workload_config(cfg, args.config, rows, vocab, lo, hi, world, args.synchronized),
+                   **({"policies": {"release_mass": POLICY_RELEASE_MASS, "escape_bias": POLICY_ESCAPE_BIAS}}
+                      if args.policies else {})},
         "timed_region": "one sync_apply launch per step (admissions of joining requests, sync, apply_mask), "
                         "CUDA events on the launching stream, max over ranks",
         "streams": replay.streams_source,

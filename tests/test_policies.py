@@ -353,12 +353,15 @@ def test_a_started_escape_marker_is_released_to_its_continuation():
 @pytest.mark.gpu
 @pytest.mark.parametrize("name", ["toy_ordinary", "bpe_paths", "crowd_committed", "bytes_derivation"])
 @pytest.mark.parametrize("dtype", ["float32", "bfloat16"])
-def test_release_and_bias_agree_with_the_oracle_along_golden_walks(name, dtype):
+@pytest.mark.parametrize("path", ["apply_mask", "sync_apply"])
+def test_release_and_bias_agree_with_the_oracle_along_golden_walks(name, dtype, path):
     """Every step of a golden walk, every sequence, random logits whose allowed columns are
     lifted by a random amount per row (so that the allowed mass spreads over (0, 1)): the
     row the kernels write equals the one built from the oracle's allowed, released and
     committing sets and the float64 mass of the biased logits.  Rows whose mass lies within
-    1e-4 of the threshold (where float32 sums may round either way) may take either side."""
+    1e-4 of the threshold (where float32 sums may round either way) may take either side.
+    Through advance + apply_mask (the row kernel), and through one fused sync_apply step per
+    token (rows already in a span take their mass while the state machine runs)."""
     import torch
 
     from oracle.oracle import Phase
@@ -394,6 +397,8 @@ def test_release_and_bias_agree_with_the_oracle_along_golden_walks(name, dtype):
     torch_dtype = getattr(torch, dtype)
     seen = {"released": 0, "kept": 0, "near": 0, "biased": 0}
     steps = len(sequences[0]["tokens"])
+    history = torch.tensor([seq["tokens"] for seq in sequences], dtype=torch.int32, device="cuda")
+    zeros = torch.zeros(n, dtype=torch.int32, device="cuda")
     for step in range(steps + 1):
         allowed = [oracle.allowed(state) for state in states]
         raw = rng.normal(0.0, 2.0, (n, vocab)).astype(np.float32)
@@ -402,7 +407,10 @@ def test_release_and_bias_agree_with_the_oracle_along_golden_walks(name, dtype):
         logits = torch.from_numpy(raw).to(torch_dtype)
         before = logits.float().numpy()
         device = logits.cuda()
-        engine.apply_mask(device, slots)
+        if path == "sync_apply":  # the step's token (the previous one) consumed in the same launch
+            engine.sync_apply(slots, history, zeros, torch.full_like(zeros, step), device)
+        else:
+            engine.apply_mask(device, slots)
         got = device.cpu().float().numpy()
         for k, state in enumerate(states):
             released, commits = policy_sets(oracle, state, pieces) if state.phase is Phase.SPAN else (set(), set())
@@ -429,7 +437,8 @@ def test_release_and_bias_agree_with_the_oracle_along_golden_walks(name, dtype):
             seen["biased"] += bool(commits)
         if step < steps:
             tokens = [seq["tokens"][step] for seq in sequences]
-            engine.advance(np.array(tokens, dtype=np.int32))
+            if path == "apply_mask":
+                engine.advance(np.array(tokens, dtype=np.int32))
             states = [oracle.advance(s, t) for s, t in zip(states, tokens)]
     assert engine.faults() == 0
     assert seen["released"] > 0 and seen["kept"] > 0 and seen["biased"] > 0, seen

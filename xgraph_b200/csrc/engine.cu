@@ -351,123 +351,345 @@ __device__ __forceinline__ void store_logit(char* at, float value, bool f16) {
     *reinterpret_cast<__nv_bfloat16*>(at) = __float2bfloat16_rn(value);
 }
 
-// Warp: escape_bias added to the row's tokens that commit to the escape marker (all
-// allowed, so none of the row's -inf writes touches them).
+// A logit rounded to the row's element type (the value a 16-bit row holds).
 template <int ELT>
-__device__ void add_escape_bias(const Ctx& c, const XgState& s, char* out, int32_t cols, bool f16) {
+__device__ __forceinline__ float rounded(float value, bool f16) {
+  if (ELT == 4) return value;
+  return f16 ? __half2float(__float2half_rn(value)) : __bfloat162float(__float2bfloat16_rn(value));
+}
+
+// One biased logit: its column and its value before and after.
+struct BiasEdit {
+  int32_t col;
+  float before, after;
+};
+constexpr int32_t kMaxEdits = 64;  // edits a row records (more: its mass is read again whole)
+
+// Warp: escape_bias added to the row's tokens that commit to the escape marker (all
+// allowed, so none of the row's -inf writes touches them); with `edits`, lane 0 records
+// each change there (count in *edit_count, which may exceed kMaxEdits).
+template <int ELT>
+__device__ void add_escape_bias(const Ctx& c, const XgState& s, char* out, int32_t cols, bool f16,
+                                BiasEdit* edits = nullptr, int32_t* edit_count = nullptr) {
   for_each_escape_commit(c, s, [&](int32_t token) {
     if (c.w.leader() && token < cols) {
       char* at = out + static_cast<int64_t>(token) * ELT;
-      store_logit<ELT>(at, load_logit<ELT>(at, f16) + c.t.escape_bias, f16);
+      const float before = load_logit<ELT>(at, f16);
+      const float after = rounded<ELT>(before + c.t.escape_bias, f16);
+      store_logit<ELT>(at, after, f16);
+      if (edits) {
+        const int32_t n = (*edit_count)++;
+        if (n < kMaxEdits) edits[n] = BiasEdit{token, before, after};
+      }
     }
   });
 }
 
 // A row's softmax mass in one pass: the top logit (lowest column among equal maxima), and
-// the sums of exp(logit - top) over all columns and over the allowed ones, kept relative
-// to the running top and rescaled when it rises.  exp(y) is taken as exp2(y · log2 e) (one
-// multiply before the exp2 unit).  The reference reads the row twice (the top first, then
-// the sums with expf); the sums agree to a few float roundings.
+// the sums of exp(logit - anchor) over all columns and over the allowed ones.  The anchor
+// is a value the pass has seen, at most kAnchorSpan below its top: it moves up (rescaling
+// the sums) only when a value exceeds it by more, so a group's exponentials wait on
+// nothing but that rare test, and no sum can overflow (128 K terms of at most e^64).  The
+// release test reads the ratio allowed / all, which the anchor does not change.  exp(y)
+// is 2^(y · log2 e) on the special-function unit (ex2.approx, relative error below 2^-22;
+// results under 2^-126 flush to zero, below what any sum holding the anchor's own 1 can
+// see).  The reference reads the row twice (the top first, then the sums with expf); the
+// ratios agree to a few float roundings.
 struct RowMass {
   float top;
   int32_t at;
+  float anchor;
   float all, allowed;
 };
 
 constexpr float kLog2E = 1.4426950408889634f;  // log2(e)
+constexpr float kAnchorSpan = 64.0f;
 
-__device__ __forceinline__ float exp_of(float y) { return exp2f(y * kLog2E); }
+__device__ __forceinline__ float ex2(float y) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(y));
+  return r;
+}
 
+__device__ __forceinline__ float exp_of(float y) { return ex2(y * kLog2E); }
+
+// The anchor raised to `to` (a value above anchor + kAnchorSpan; the first finite value).
+__device__ __forceinline__ void raise_anchor(RowMass& m, float to) {
+  const float scale = m.anchor == -INFINITY ? 0.0f : exp_of(m.anchor - to);
+  m.all *= scale;
+  m.allowed *= scale;
+  m.anchor = to;
+}
+
+// One column (the unaligned and ragged ends of a row).
 __device__ __forceinline__ void mass_add(RowMass& m, float x, int32_t col, bool ok) {
   if (x > m.top) {  // NaN never rises
-    const float scale = m.top == -INFINITY ? 0.0f : exp_of(m.top - x);
-    m.all *= scale;
-    m.allowed *= scale;
     m.top = x;
     m.at = col;
   }
-  // below a top of -inf only -inf (adds 0) or NaN (carried, as the reference's sum carries it)
-  const float e = m.top == -INFINITY ? (x != x ? x : 0.0f) : exp_of(x - m.top);
+  if (x > m.anchor + kAnchorSpan) raise_anchor(m, x);
+  // below an anchor of -inf only -inf (adds 0) or NaN (carried, as the reference's sum carries it)
+  const float e = m.anchor == -INFINITY ? (x != x ? x : 0.0f) : exp_of(x - m.anchor);
   m.all += e;
   if (ok) m.allowed += e;
 }
 
 __device__ __forceinline__ RowMass mass_merge(const RowMass& a, const RowMass& b) {
   const bool second = b.top > a.top || (b.top == a.top && b.at < a.at);
-  const float top = second ? b.top : a.top;
-  const float fa = a.top == -INFINITY ? 0.0f : exp_of(a.top - top);
-  const float fb = b.top == -INFINITY ? 0.0f : exp_of(b.top - top);
-  return RowMass{top, second ? b.at : a.at, a.all * fa + b.all * fb, a.allowed * fa + b.allowed * fb};
+  const float anchor = fmaxf(a.anchor, b.anchor);
+  const float fa = a.anchor == -INFINITY ? 0.0f : exp_of(a.anchor - anchor);
+  const float fb = b.anchor == -INFINITY ? 0.0f : exp_of(b.anchor - anchor);
+  return RowMass{second ? b.top : a.top, second ? b.at : a.at, anchor, a.all * fa + b.all * fb,
+                 a.allowed * fa + b.allowed * fb};
 }
 
-// The 16-byte vector k of a logits row into the running mass (columns k·per ..).
-template <int ELT>
-__device__ __forceinline__ void mass_vector(RowMass& m, const uint4& v, int32_t col, uint32_t bits, bool f16) {
-  constexpr int32_t per = 16 / ELT;
-  const uint32_t lanes[4] = {v.x, v.y, v.z, v.w};
+// One 32-column group of a logits row (2·ELT 16-byte vectors; bits: its allowed columns)
+// into the running mass: the group's maximum, the two rare tests (a new top, a raised
+// anchor), then 32 independent exponentials summed as a tree.
+template <int ELT, bool MASKED>
+__device__ __forceinline__ void mass_group(RowMass& m, const uint4* v, int32_t col, uint32_t bits, bool f16) {
+  float x[32];
 #pragma unroll
-  for (int32_t j = 0; j < per; ++j) {
-    float x;
-    if (ELT == 4) {
-      x = __uint_as_float(lanes[j]);
-    } else {
-      const uint32_t half = (lanes[j >> 1] >> (16 * (j & 1))) & 0xffffu;
-      x = f16 ? __half2float(__ushort_as_half(static_cast<uint16_t>(half))) : __uint_as_float(half << 16);
+  for (int32_t q = 0; q < 2 * ELT; ++q) {
+    const uint32_t lanes[4] = {v[q].x, v[q].y, v[q].z, v[q].w};
+#pragma unroll
+    for (int32_t j = 0; j < 16 / ELT; ++j) {
+      float& y = x[q * (16 / ELT) + j];
+      if (ELT == 4) {
+        y = __uint_as_float(lanes[j]);
+      } else {
+        const uint32_t half = (lanes[j >> 1] >> (16 * (j & 1))) & 0xffffu;
+        y = f16 ? __half2float(__ushort_as_half(static_cast<uint16_t>(half))) : __uint_as_float(half << 16);
+      }
     }
-    mass_add(m, x, col + j, (bits >> j) & 1u);
   }
+  float top = x[0];
+#pragma unroll
+  for (int32_t j = 1; j < 32; ++j) top = fmaxf(top, x[j]);  // NaN is passed over, as by ">"
+  if (top > m.top) {
+    int32_t first = 31;
+#pragma unroll
+    for (int32_t j = 31; j >= 0; --j)
+      if (x[j] == top) first = j;
+    m.top = top;
+    m.at = col + first;
+  }
+  if (top > m.anchor + kAnchorSpan) raise_anchor(m, top);
+  if (m.anchor == -INFINITY) {  // only -inf and NaN so far: NaN is carried
+#pragma unroll
+    for (int32_t j = 0; j < 32; ++j) {
+      if (x[j] != x[j]) {
+        m.all += x[j];
+        if (MASKED && ((bits >> j) & 1u)) m.allowed += x[j];
+      }
+    }
+    return;
+  }
+  const float shift = m.anchor * kLog2E;
+#pragma unroll
+  for (int32_t j = 0; j < 32; ++j) {
+    const float e = ex2(fmaf(x[j], kLog2E, -shift));
+    x[j] = e;  // reuse: the exponential of column j
+  }
+  float all[8], allowed[8];
+#pragma unroll
+  for (int32_t k = 0; k < 8; ++k) {
+    all[k] = (x[k] + x[k + 8]) + (x[k + 16] + x[k + 24]);
+    if (MASKED)
+      allowed[k] = (((bits >> k) & 1u) ? x[k] : 0.0f) + (((bits >> (k + 8)) & 1u) ? x[k + 8] : 0.0f) +
+                   ((((bits >> (k + 16)) & 1u) ? x[k + 16] : 0.0f) + (((bits >> (k + 24)) & 1u) ? x[k + 24] : 0.0f));
+  }
+  m.all += ((all[0] + all[1]) + (all[2] + all[3])) + ((all[4] + all[5]) + (all[6] + all[7]));
+  if (MASKED)
+    m.allowed += ((allowed[0] + allowed[1]) + (allowed[2] + allowed[3])) +
+                 ((allowed[4] + allowed[5]) + (allowed[6] + allowed[7]));
 }
 
 constexpr int32_t kMassBatch = 4;  // 16-byte loads a thread issues before it uses them
 
-// Whole CTA (every thread gets the same answer): whether the row, columns [0, cols) of the
-// served vocabulary under the mask base | delta, is released (csrc/engine.cu:2479-2552).
+// The mass passes stream a row through shared memory with cp.async: each thread owns the
+// 32-column groups g = thread (mod threads) (one mask word each; 64 bytes of bf16, 128 of
+// fp32) and keeps kRingBytes of them in flight in its own slots of the CTA's ring, so a
+// CTA has ~64 KB of its row in flight instead of the few KB its registers could hold.
+// Completion is the hardware's (cp.async.wait_group counts the thread's own copy groups);
+// no thread waits on another.
+constexpr int32_t kRingBytes = 256;  // per thread
+
+__device__ __forceinline__ void async_copy16(void* to, const void* from) {
+  const uint32_t dst = static_cast<uint32_t>(__cvta_generic_to_shared(to));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(from) : "memory");
+}
+__device__ __forceinline__ void async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// 32-column group g of the row (16-byte aligned) into `slot`.
 template <int ELT>
-__device__ bool release_row(const Tables& t, const char* out, int32_t cols, const uint32_t* base,
-                            const uint32_t* delta, bool f16) {
-  __shared__ RowMass partial[32];
-  RowMass m{-INFINITY, 0, 0.0f, 0.0f};
-  int32_t tail = 0;  // columns before it were read as 16-byte vectors
+__device__ __forceinline__ void copy_group(uint8_t* slot, const char* row, int32_t g) {
+  const char* from = row + static_cast<int64_t>(g) * 32 * ELT;
+#pragma unroll
+  for (int32_t q = 0; q < 2 * ELT; ++q) async_copy16(slot + 16 * q, from + 16 * q);
+}
+
+// Per thread: the mass of the columns thread `thread` of `threads` takes: its 32-column
+// groups of a 16-byte aligned row through its ring slots (`ring`: kRingBytes), then the
+// ragged end; every column of an unaligned row one by one.  Allowed bits from base | delta
+// when MASKED.
+template <int ELT, bool MASKED>
+__device__ RowMass thread_mass(const Tables& t, const char* out, int32_t cols, const uint32_t* base,
+                               const uint32_t* delta, bool f16, int32_t thread, int32_t threads, uint8_t* ring) {
+  constexpr bool masked = MASKED;
+  RowMass m{-INFINITY, 0, -INFINITY, 0.0f, 0.0f};
+  int32_t tail = 0;  // columns before it were read as whole groups
   if ((reinterpret_cast<uintptr_t>(out) & 15u) == 0) {
-    constexpr int32_t per = 16 / ELT;
-    const int32_t vectors = cols / per;
-    const int32_t stride = blockDim.x;
-    // kMassBatch loads in flight per thread; a thread's columns still rise (ties keep the
-    // first)
-    for (int32_t k0 = threadIdx.x; k0 < vectors; k0 += stride * kMassBatch) {
-      uint4 v[kMassBatch];
+    constexpr int32_t group_bytes = 32 * ELT, depth = kRingBytes / group_bytes;
+    const int32_t groups = cols / 32;
 #pragma unroll
-      for (int32_t b = 0; b < kMassBatch; ++b) {
-        const int32_t k = k0 + b * stride;
-        v[b] = k < vectors ? *reinterpret_cast<const uint4*>(out + static_cast<int64_t>(k) * 16)
-                           : make_uint4(0u, 0u, 0u, 0u);
-      }
-#pragma unroll
-      for (int32_t b = 0; b < kMassBatch; ++b) {
-        const int32_t k = k0 + b * stride;
-        if (k < vectors) mass_vector<ELT>(m, v[b], k * per, allowed8(base, delta, t.words, k * per), f16);
-      }
+    for (int32_t d = 0; d < depth; ++d) {  // always `depth` commits, so that the wait count holds
+      const int32_t g = thread + d * threads;
+      if (g < groups) copy_group<ELT>(ring + d * group_bytes, out, g);
+      async_commit();
     }
-    tail = vectors * per;
+    for (int32_t i = 0;; ++i) {
+      const int32_t g = thread + i * threads;
+      if (g >= groups) break;
+      const uint32_t bits = masked ? mask_word(base, delta, g) : 0u;  // in flight during the wait
+      uint8_t* slot = ring + (i % depth) * group_bytes;
+      async_wait<depth - 1>();  // the oldest of the thread's groups has landed
+      uint4 v[2 * ELT];
+#pragma unroll
+      for (int32_t q = 0; q < 2 * ELT; ++q) v[q] = *reinterpret_cast<const uint4*>(slot + 16 * q);
+      mass_group<ELT, MASKED>(m, v, g * 32, bits, f16);
+      const int32_t next = g + depth * threads;  // the slot's values are used: refill it
+      if (next < groups) copy_group<ELT>(slot, out, next);
+      async_commit();
+    }
+    async_wait<0>();
+    tail = groups * 32;
   }
-  for (int32_t col = tail + threadIdx.x; col < cols; col += blockDim.x)
+  for (int32_t col = tail + thread; col < cols; col += threads)
     mass_add(m, load_logit<ELT>(out + static_cast<int64_t>(col) * ELT, f16), col,
-             (mask_word(base, delta, col >> 5) >> (col & 31)) & 1u);
+             masked && ((mask_word(base, delta, col >> 5) >> (col & 31)) & 1u));
+  return m;
+}
+
+// The merge of a warp's masses, in every lane.
+__device__ __forceinline__ RowMass warp_mass(RowMass m) {
 #pragma unroll
   for (int32_t d = 16; d > 0; d >>= 1) {
     const RowMass o{__shfl_xor_sync(0xffffffffu, m.top, d), __shfl_xor_sync(0xffffffffu, m.at, d),
-                    __shfl_xor_sync(0xffffffffu, m.all, d), __shfl_xor_sync(0xffffffffu, m.allowed, d)};
+                    __shfl_xor_sync(0xffffffffu, m.anchor, d), __shfl_xor_sync(0xffffffffu, m.all, d),
+                    __shfl_xor_sync(0xffffffffu, m.allowed, d)};
     m = mass_merge(m, o);
   }
+  return m;
+}
+
+// Whether a row of this mass is released (csrc/engine.cu:2536-2552): its log allowed mass
+// under the release mass, or (release_top) its top column disallowed; never for a row
+// whose top is not finite (no defined distribution).
+__device__ __forceinline__ bool released_by(const Tables& t, const RowMass& r, const uint32_t* base,
+                                            const uint32_t* delta) {
+  if (!isfinite(r.top)) return false;
+  const bool top_allowed = (mask_word(base, delta, r.at >> 5) >> (r.at & 31)) & 1u;
+  return (t.release_top && !top_allowed) || logf(r.allowed) - logf(r.all) < t.release_log_mass;
+}
+
+// Whole CTA (every thread gets the same answer): whether the row, columns [0, cols) of the
+// served vocabulary under the mask base | delta, is released (csrc/engine.cu:2479-2552),
+// from one pass over the row.
+template <int ELT>
+__device__ bool release_row(const Tables& t, const char* out, int32_t cols, const uint32_t* base,
+                            const uint32_t* delta, bool f16, uint8_t* ring) {
+  __shared__ RowMass partial[32];
+  const RowMass m = warp_mass(thread_mass<ELT, true>(t, out, cols, base, delta, f16, threadIdx.x, blockDim.x,
+                                                     ring + threadIdx.x * kRingBytes));
   const int32_t warps = blockDim.x >> 5;
   if ((threadIdx.x & 31) == 0) partial[threadIdx.x >> 5] = m;
   __syncthreads();
   RowMass r = partial[0];
   for (int32_t w = 1; w < warps; ++w) r = mass_merge(r, partial[w]);
   __syncthreads();  // partial may be reused by the caller's next row
-  if (!isfinite(r.top)) return false;  // no defined distribution: never released
-  const bool top_allowed = (mask_word(base, delta, r.at >> 5) >> (r.at & 31)) & 1u;
-  return (t.release_top && !top_allowed) || logf(r.allowed) - logf(r.all) < t.release_log_mass;
+  return released_by(t, r, base, delta);
+}
+
+// Per thread: the sum of exp(logit - anchor) over the allowed columns among the 32-column
+// groups thread `thread` of `threads` takes (their mask words loaded kMassBatch at a time;
+// only groups holding an allowed column are read), then the ragged end.
+template <int ELT>
+__device__ float thread_allowed_sum(const Tables& t, const char* out, int32_t cols, const uint32_t* base,
+                                    const uint32_t* delta, float anchor, bool f16, int32_t thread, int32_t threads) {
+  constexpr int32_t per = 16 / ELT;
+  const int32_t groups = (reinterpret_cast<uintptr_t>(out) & 15u) == 0 ? cols / 32 : 0;
+  const float shift = anchor * kLog2E;
+  float sum = 0.0f;
+  for (int32_t g0 = thread; g0 < groups; g0 += threads * kMassBatch) {
+    uint32_t bits[kMassBatch];
+#pragma unroll
+    for (int32_t b = 0; b < kMassBatch; ++b) {
+      const int32_t g = g0 + b * threads;
+      bits[b] = g < groups ? mask_word(base, delta, g) : 0u;
+    }
+#pragma unroll 1
+    for (int32_t b = 0; b < kMassBatch; ++b) {
+      if (bits[b] == 0u) continue;
+      const int32_t g = g0 + b * threads;
+      uint4 v[2 * ELT];
+#pragma unroll
+      for (int32_t q = 0; q < 2 * ELT; ++q)
+        v[q] = *reinterpret_cast<const uint4*>(out + static_cast<int64_t>(g) * 32 * ELT + 16 * q);
+#pragma unroll
+      for (int32_t q = 0; q < 2 * ELT; ++q) {
+        const uint32_t lanes[4] = {v[q].x, v[q].y, v[q].z, v[q].w};
+#pragma unroll
+        for (int32_t j = 0; j < per; ++j) {
+          if (!((bits[b] >> (q * per + j)) & 1u)) continue;
+          float x;
+          if (ELT == 4) {
+            x = __uint_as_float(lanes[j]);
+          } else {
+            const uint32_t half = (lanes[j >> 1] >> (16 * (j & 1))) & 0xffffu;
+            x = f16 ? __half2float(__ushort_as_half(static_cast<uint16_t>(half))) : __uint_as_float(half << 16);
+          }
+          sum += ex2(fmaf(x, kLog2E, -shift));
+        }
+      }
+    }
+  }
+  for (int32_t col = groups * 32 + thread; col < cols; col += threads)
+    if ((mask_word(base, delta, col >> 5) >> (col & 31)) & 1u)
+      sum += exp_of(load_logit<ELT>(out + static_cast<int64_t>(col) * ELT, f16) - anchor);
+  return sum;
+}
+
+// Whole CTA: whether the row is released, given `early`: the row's top and sum of all
+// columns, read before its bias (by the warps idle during the state machine), and the
+// bias edits since.  An edit at or above the top (or more edits than were recorded) leaves
+// the top unknown: the row is read again whole.  Otherwise the sum takes each edit's
+// change and the allowed sum is read from the vectors holding allowed columns only.
+template <int ELT>
+__device__ bool release_row_after(const Tables& t, const char* out, int32_t cols, const uint32_t* base,
+                                  const uint32_t* delta, bool f16, RowMass early, const BiasEdit* edits,
+                                  int32_t edit_count, uint8_t* ring) {
+  __shared__ float partial[32];
+  bool whole = edit_count > kMaxEdits || !isfinite(early.top);
+  for (int32_t e = 0; e < edit_count && e < kMaxEdits && !whole; ++e) {
+    const BiasEdit& x = edits[e];
+    if (!(x.before < early.top && x.after < early.top)) whole = true;  // (NaN: whole too)
+    else early.all += exp_of(x.after - early.anchor) - exp_of(x.before - early.anchor);
+  }
+  if (whole) return release_row<ELT>(t, out, cols, base, delta, f16, ring);  // block-uniform
+  float sum = thread_allowed_sum<ELT>(t, out, cols, base, delta, early.anchor, f16, threadIdx.x, blockDim.x);
+#pragma unroll
+  for (int32_t d = 16; d > 0; d >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, d);
+  const int32_t warps = blockDim.x >> 5;
+  if ((threadIdx.x & 31) == 0) partial[threadIdx.x >> 5] = sum;
+  __syncthreads();
+  float allowed = 0.0f;
+  for (int32_t w = 0; w < warps; ++w) allowed += partial[w];
+  __syncthreads();
+  early.allowed = allowed;
+  return released_by(t, early, base, delta);
 }
 
 // Whole CTA: `words` (words_padded, shared) becomes the mask of the escape marker's next
@@ -599,6 +821,10 @@ __global__ void __maxnreg__(kFusedRegisters)
   __shared__ WarpShared shared;
   __shared__ MaskRef use;                               // the mask this CTA applies
   __shared__ int32_t escape_at;                         // release: the row's escape position, or -1
+  __shared__ RowMass early_mass[kFusedThreads / 32 - 1];  // release: warps 1..7's pass over the row
+  __shared__ int32_t early_ready;                       //   done (the row was in a span before the step)
+  __shared__ BiasEdit edits[kMaxEdits];                 // the escape bias's tokens and changes to the row
+  __shared__ int32_t edit_count;
   __shared__ int32_t delim0[kDelimCopy];                // tokens that start each delimiter
   __shared__ __align__(128) uint32_t blocked_run[kBlockedRunWords];
   extern __shared__ __align__(16) uint32_t composed[];  // [words_padded]: a delta built this step
@@ -611,6 +837,7 @@ __global__ void __maxnreg__(kFusedRegisters)
   const int32_t was_on = valid ? t.active[slot] : 0;
   if (!was_on && f.admit_count == 0) return;  // block-uniform: inactive rows are neither advanced nor masked
   int32_t found = -1, cursor = 0, end = 0, prompt = 0;
+  bool bias_row = false;  // warp 0: the row has more bias tokens than the list holds
   XgState s;
   if (threadIdx.x < 32 && valid) {
     // the first 32 admissions' slots load with the state (one round trip for both)
@@ -649,13 +876,21 @@ __global__ void __maxnreg__(kFusedRegisters)
     }
     __syncwarp();
     asm volatile("bar.arrive 1, %0;" ::"r"(blockDim.x) : "memory");
-    // Release reads the whole logits row of a span row: start it into L2 now, while warp 0
-    // runs the state machine (a row that was in a span before this step's tokens; the
-    // prefetch is only a hint, in 32 KB pieces of the 16-byte aligned row).
-    if (t.release_on && was_on && t.states[slot].phase == kSpan) {
-      const char* row = f.logits + static_cast<int64_t>(i) * f.stride * ELT;
-      const int64_t bytes = (reinterpret_cast<uintptr_t>(row) & 15u) == 0 ? (static_cast<int64_t>(min(f.cols, t.vocab)) * ELT) & ~15ll : 0;
-      for (int64_t at = static_cast<int64_t>(threadIdx.x - 32) * 32768; at < bytes; at += static_cast<int64_t>(blockDim.x - 32) * 32768) {
+    // Release reads the whole logits row of a span row.  For a row that was in a span
+    // before this step's tokens (most span rows of a step; 16-byte aligned), these warps
+    // start the row into L2 (bulk prefetches of 32 KB pieces, hints only) and take its top
+    // and the sum over all its columns now, while warp 0 runs the state machine; after the
+    // mask only the allowed columns remain to be read (release_row_after).  Other rows take
+    // the whole pass after the mask (also taking rows that stay in free text measured
+    // slower: their reads compete with every row's -inf writes for HBM).
+    const char* row = f.logits + static_cast<int64_t>(i) * f.stride * ELT;
+    const int32_t served = min(f.cols, t.vocab);
+    const bool early = t.release_on && was_on && t.states[slot].phase == kSpan &&
+                       (reinterpret_cast<uintptr_t>(row) & 15u) == 0;
+    if (early) {
+      const int64_t bytes = (static_cast<int64_t>(served) * ELT) & ~15ll;
+      for (int64_t at = static_cast<int64_t>(threadIdx.x - 32) * 32768; at < bytes;
+           at += static_cast<int64_t>(blockDim.x - 32) * 32768) {
         const uint32_t piece = static_cast<uint32_t>(bytes - at < 32768 ? bytes - at : 32768);
         asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(row + at), "r"(piece) : "memory");
       }
@@ -679,6 +914,13 @@ __global__ void __maxnreg__(kFusedRegisters)
         }
       }
     }
+    if (early) {
+      uint8_t* ring = reinterpret_cast<uint8_t*>(composed + t.words_padded) + threadIdx.x * kRingBytes;
+      const RowMass m = warp_mass(thread_mass<ELT, false>(t, row, served, nullptr, nullptr, f16, threadIdx.x - 32,
+                                                          blockDim.x - 32, ring));
+      if ((threadIdx.x & 31) == 0) early_mass[(threadIdx.x >> 5) - 1] = m;
+    }
+    if (threadIdx.x == 32) early_ready = early;
   } else {
     Ctx c = make_ctx(t, valid ? slot : 0, shared);
     if (copied) c.delim0 = delim0;
@@ -716,15 +958,22 @@ __global__ void __maxnreg__(kFusedRegisters)
       if (threadIdx.x == 0) use = MaskRef{t.base[slot], t.delta[slot]};
     }
     if (threadIdx.x == 0 && on) t.cursors[slot] = cursor;
-    // logit policies of a span row: the escape bias now (before any warp reads the row),
-    // release after the barrier
-    int32_t at = -1;
-    if (on && s.phase == kSpan && (t.release_on || t.escape_bias != 0.0f)) {
-      at = escape_position(t, s);
-      if (t.escape_bias != 0.0f)
-        add_escape_bias<ELT>(c, s, f.logits + static_cast<int64_t>(i) * f.stride * ELT, f.cols, f16);
+    // logit policies of a span row: its escape position for release, and the tokens the
+    // bias goes to (their logits change after the barrier, once warps 1..7 have read the
+    // row; more than kMaxEdits tokens: warp 0 finds them again then)
+    const bool policies = on && s.phase == kSpan && (t.release_on || t.escape_bias != 0.0f);
+    int32_t commits = 0;
+    if (policies && t.escape_bias != 0.0f) {
+      for_each_escape_commit(c, s, [&](int32_t token) {
+        if (threadIdx.x == 0 && commits < kMaxEdits) edits[commits].col = token;
+        ++commits;
+      });
     }
-    if (threadIdx.x == 0) escape_at = at;
+    bias_row = commits > kMaxEdits;
+    if (threadIdx.x == 0) {
+      escape_at = policies ? escape_position(t, s) : -1;
+      edit_count = commits;
+    }
   }
   __syncthreads();
   const uint32_t* base = use.base;
@@ -744,14 +993,41 @@ __global__ void __maxnreg__(kFusedRegisters)
     uint4* to = reinterpret_cast<uint4*>(own);
     for (int32_t k = threadIdx.x; k < (t.words_padded >> 2); k += blockDim.x) to[k] = from[k];
   }
+  char* const row_out = f.logits + static_cast<int64_t>(i) * f.stride * ELT;
+  if (bias_row) {  // warp 0, more tokens than were listed (the slot's state is in its registers)
+    const Ctx c = make_ctx(t, slot, shared);
+    add_escape_bias<ELT>(c, s, row_out, f.cols, f16);
+  } else if (static_cast<int32_t>(threadIdx.x) < edit_count) {  // one listed token per thread
+    BiasEdit& e = edits[threadIdx.x];
+    if (e.col < f.cols) {
+      char* at = row_out + static_cast<int64_t>(e.col) * ELT;
+      e.before = load_logit<ELT>(at, f16);
+      e.after = rounded<ELT>(e.before + t.escape_bias, f16);
+      store_logit<ELT>(at, e.after, f16);
+    } else {
+      e.before = e.after = 0.0f;  // past the row: no change (and past the mass's columns)
+    }
+  }
   // release (block-uniform): the released mask replaces the composed one in shared memory
-  // for this call only (release_row's barriers order every thread's copy above before it)
-  if (escape_at >= 0 && t.release_on &&
-      release_row<ELT>(t, f.logits + static_cast<int64_t>(i) * f.stride * ELT, min(f.cols, t.vocab), base, delta,
-                       f16)) {
-    released_mask(t, escape_at, composed);
-    base = nullptr;
-    delta = composed;
+  // for this call only (the barriers below order every thread's copy above before it)
+  if (escape_at >= 0 && t.release_on) {
+    __syncthreads();  // the bias is written and its edits recorded
+    const int32_t served = min(f.cols, t.vocab);
+    bool released;
+    if (early_ready) {
+      RowMass early = early_mass[0];
+      for (int32_t w = 1; w < kFusedThreads / 32 - 1; ++w) early = mass_merge(early, early_mass[w]);
+      released = release_row_after<ELT>(t, row_out, served, base, delta, f16, early, edits, edit_count,
+                                        reinterpret_cast<uint8_t*>(composed + t.words_padded));
+    } else {
+      released = release_row<ELT>(t, row_out, served, base, delta, f16,
+                                  reinterpret_cast<uint8_t*>(composed + t.words_padded));
+    }
+    if (released) {
+      released_mask(t, escape_at, composed);
+      base = nullptr;
+      delta = composed;
+    }
   }
   if (base != nullptr || delta != nullptr) {  // else inactive or error phase: untouched
     char* out = f.logits + static_cast<int64_t>(i) * f.stride * ELT;
@@ -810,7 +1086,7 @@ __global__ void __launch_bounds__(kFusedThreads)
   __shared__ WarpShared shared;
   __shared__ MaskRef mask;
   __shared__ int32_t escape_at;                         // release: the row's escape position, or -1
-  extern __shared__ __align__(16) uint32_t released[];  // [words_padded] when release is on
+  extern __shared__ __align__(16) uint32_t released[];  // release on: [words_padded], then the mass ring
   const int32_t row = blockIdx.x;
   const int32_t slot = d.row_slots[row];
   if (slot < 0 || slot >= d.max_slots || !t.active[slot]) return;  // block-uniform
@@ -854,7 +1130,9 @@ __global__ void __launch_bounds__(kFusedThreads)
   __syncthreads();
   MaskRef m = mask;
   if (m.base == nullptr && m.delta == nullptr) return;  // error: untouched
-  if (escape_at >= 0 && t.release_on && release_row<ELT>(t, out, min(cols, t.vocab), m.base, m.delta, f16)) {
+  if (escape_at >= 0 && t.release_on &&
+      release_row<ELT>(t, out, min(cols, t.vocab), m.base, m.delta, f16,
+                       reinterpret_cast<uint8_t*>(released + t.words_padded))) {
     released_mask(t, escape_at, released);
     m = MaskRef{nullptr, released};
   }
@@ -1312,7 +1590,9 @@ int create(const void* blob, bool on_device, const XgLayout* layout, const XgOpt
     release(e);
     return rc;
   }
-  e->composed_bytes = static_cast<size_t>(layout->words_padded) * sizeof(uint32_t);
+  // one mask row; with release on, then the mass passes' ring (kRingBytes per thread)
+  e->composed_bytes = static_cast<size_t>(layout->words_padded) * sizeof(uint32_t) +
+                      (e->t.release_on ? static_cast<size_t>(kFusedThreads) * kRingBytes : 0);
   for (const void* kernel : {reinterpret_cast<const void*>(sync_apply_kernel<4>),
                              reinterpret_cast<const void*>(sync_apply_kernel<2>),
                              reinterpret_cast<const void*>(draft_apply_kernel<4>),
@@ -1403,7 +1683,7 @@ int launch_drafts(XgEngine* e, char* logits, int32_t dtype, int32_t rows, int32_
     d.scratch_masks = reinterpret_cast<uint32_t*>(scratch + static_cast<int64_t>(rows) * e->t.memory_ints * 4);
   }
   cudaStream_t s = as_stream(stream);
-  const size_t released = e->t.release_on ? e->composed_bytes : 0;  // a released row's mask
+  const size_t released = e->t.release_on ? e->composed_bytes : 0;  // a released row's mask and the ring
   if (dtype == XG_F32)
     draft_apply_kernel<4><<<rows, kFusedThreads, released, s>>>(e->t, d, logits, cols, row_stride, 0xff800000u);
   else
