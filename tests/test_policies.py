@@ -442,3 +442,115 @@ def test_release_and_bias_agree_with_the_oracle_along_golden_walks(name, dtype, 
             states = [oracle.advance(s, t) for s, t in zip(states, tokens)]
     assert engine.faults() == 0
     assert seen["released"] > 0 and seen["kept"] > 0 and seen["biased"] > 0, seen
+
+
+_WORKER = {}
+
+
+def _policy_worker_init(index, served, syntax, options):
+    from oracle.oracle import Oracle
+
+    _WORKER["oracle"] = Oracle(index, served, syntax, **options)
+    _WORKER["pieces"] = escape_pieces(served, syntax)
+
+
+def _policy_sets_after(prefix):
+    """The oracle after a token prefix: (allowed, released, committing, in a span, the
+    escape marker started)."""
+    from oracle.oracle import Phase
+
+    oracle = _WORKER["oracle"]
+    state = oracle.initial_state()
+    for token in prefix:
+        state = oracle.advance(state, int(token))
+    span = state.phase is Phase.SPAN
+    released, commits = policy_sets(oracle, state, _WORKER["pieces"]) if span else (set(), set())
+    return sorted(oracle.allowed(state)), sorted(released), sorted(commits), span, bool(state.escaping)
+
+
+@pytest.mark.gpu
+def test_policies_agree_with_the_oracle_at_the_path_benchmark_size():
+    """paths-100k (config 3: 100 k entities, 1 M triples, V = 128,256), 64 rows of GPU-sampled
+    streams replayed through the fused step one token per step with release (0.35) and
+    escape bias (-0.75) on, bf16 logits.  Every row at every step keeps each column's logit
+    bit for bit, takes exactly the biased value, or becomes -inf.  At 48 seeded (row, step)
+    samples, 40 of them inside spans, the written row equals the one built from the
+    oracle's allowed, released and committing sets and a float64 mass of the biased logits
+    (the sampled rows' allowed columns lifted by a seeded amount so that masses spread
+    around the threshold; either side within 1e-4 of it)."""
+    import multiprocessing as mp
+
+    import torch
+
+    from xgraph_b200.engine import Engine
+    from xgraph_b200.synthetic import build_workload, sample_streams
+
+    rows, steps, bias, threshold = 64, 96, -0.75, 0.35
+    w = build_workload(3)
+    syntax, options, vocab = w.syntax, dict(w.config.options), w.served.vocab_size
+    sampler = Engine(w.index, w.served, syntax, rows, **options)
+    tokens, _, _ = sample_streams(sampler, w.served, syntax, w.world, rows, steps, seed=103)
+    slots = torch.arange(rows, dtype=torch.int32, device="cuda")
+    prompt = torch.zeros(rows, dtype=torch.int32, device="cuda")
+    # which (row, step) pairs are in a span: a replay without the policies
+    sampler.reset()
+    sampler.begin(slots)
+    phases = []
+    for k in range(steps + 1):
+        sampler.sync(slots, tokens, prompt, torch.full((rows,), k, dtype=torch.int32, device="cuda"))
+        phases.append(sampler.states_host(rows)["phase"].copy())
+    del sampler
+    rng = np.random.default_rng(17)
+    span_pairs = [(r, k) for k in range(steps + 1) for r in range(rows) if phases[k][r] == 1]
+    free_pairs = [(r, k) for k in range(steps + 1) for r in range(rows) if phases[k][r] != 1]
+    picks = [span_pairs[i] for i in rng.choice(len(span_pairs), 40, replace=False)]
+    picks += [free_pairs[i] for i in rng.choice(len(free_pairs), 8, replace=False)]
+    host_tokens = tokens.cpu().numpy()
+    with mp.get_context("spawn").Pool(8, initializer=_policy_worker_init,
+                                      initargs=(w.index, w.served, syntax, options)) as pool:
+        expected = dict(zip(picks, pool.map(_policy_sets_after, [host_tokens[r, :k] for r, k in picks],
+                                            chunksize=1)))
+    engine = Engine(w.index, w.served, syntax, rows, release_mass=threshold, escape_bias=bias, **options)
+    engine.reset()
+    engine.begin(slots)
+    seen = {"released": 0, "kept": 0, "near": 0, "biased": 0, "free": 0}
+    for k in range(steps + 1):
+        raw = rng.normal(0.0, 2.0, (rows, vocab)).astype(np.float32)
+        for (r, kk), (allowed, *_rest) in expected.items():
+            if kk == k:
+                raw[r, allowed] += rng.uniform(4.0, 14.0)
+        before_t = torch.from_numpy(raw).to(torch.bfloat16)
+        logits = before_t.cuda()
+        engine.sync_apply(slots, tokens, prompt, torch.full((rows,), k, dtype=torch.int32, device="cuda"), logits)
+        got = logits.cpu()
+        before = before_t.float().numpy()
+        got_f = got.float().numpy()
+        biased = torch.tensor(before + np.float32(bias)).to(torch.bfloat16).float().numpy()
+        ok = (got.view(torch.int16) == before_t.view(torch.int16)).numpy() | np.isneginf(got_f) | (got_f == biased)
+        assert ok.all(), ("a column is neither its logit, its biased logit nor -inf", k)
+        for (r, kk), (allowed, released, commits, span, escaping) in expected.items():
+            if kk != k:
+                continue
+            commits = set() if escaping else set(commits)
+            row = before[r].copy()
+            for t in commits:
+                row[t] = biased[r, t]
+            outcomes = [False]
+            if released:
+                release, mass = release_reference(row, set(allowed), vocab, math.log(threshold), False)
+                near = abs(mass - math.log(threshold)) < 1e-4
+                outcomes = [False, True] if near else [release]
+                seen["near"] += near
+            matches = []
+            for outcome in outcomes:
+                keep = sorted(released if outcome else allowed)
+                want = np.full(vocab, -np.inf, dtype=np.float32)
+                want[keep] = row[keep]
+                matches.append(np.array_equal(got_f[r], want))
+            assert any(matches), (r, k, outcomes, span)
+            seen["released"] += outcomes == [True]
+            seen["kept"] += bool(released) and outcomes == [False]
+            seen["biased"] += bool(commits)
+            seen["free"] += not span
+    assert engine.errors() == 0 and engine.faults() == 0
+    assert seen["released"] > 0 and seen["kept"] > 0 and seen["biased"] > 0 and seen["free"] == 8, seen
