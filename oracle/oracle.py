@@ -12,8 +12,10 @@ state projection and closed span to be equal.
 Scope: the span language of src/xgraph/oracle.py with the policies the engine serves:
 ordinary entity/fact spans, escapes, repeats, derivation, paths (union and committed),
 bound_escapes, unquoted_starts, start_rank "degree"/"sitelinks", KG versions,
-end_after_answer and opened states.  The reference's observation, menu, audit, STOP,
-expression and relation-support policies are not restated; asking for them raises.
+end_after_answer, opened states and residual-goal STOP (src/xgraph/oracle.py:1608-1635,
+with the question's relation table of xgraph_b200.stopping).  The reference's
+observation, menu, audit, expression and relation-support policies are not restated;
+asking for them raises.
 
 Like the reference it reads a KG index's arrays as plain data (edge tuples, token
 tuples) and recomputes everything per token from them.  One restructuring, for speed
@@ -92,6 +94,7 @@ class OracleState:
     ranks: tuple[tuple[str, int], ...] = ()
     version: str | None = None
     answer_complete: bool = False
+    stop: object = None  # the request's STOP table (xgraph_b200.stopping.StopRelations), kept across spans
 
 
 class _Graph:
@@ -127,10 +130,11 @@ class _SpanContext:
     closes: bool
     separates: bool
     escapes: bool
+    forced: bool = False  # residual-goal STOP: only the closer (or the label) goes on
 
 
 _UNSUPPORTED = {
-    "expressions": False, "stop": None, "relations": "frontier", "observe": 0,
+    "expressions": False, "relations": "frontier", "observe": 0,
     "observe_width": 0, "observe_defer": 0, "menu_close_next": False, "observe_select": False,
     "observe_answer": False, "observe_required": False, "observe_no_loop": False,
     "audit": False, "menu": 0, "observe_terminal": 0,
@@ -157,6 +161,7 @@ class Oracle:
         unquoted_starts: bool = False,
         end_after_answer: bool = False,
         eos_token_ids: Iterable[int] = (),
+        stop: str | None = None,
         **others,
     ) -> None:
         # Constructor checks in the reference's order (src/xgraph/oracle.py:439-455).
@@ -175,6 +180,15 @@ class Oracle:
                 raise TypeError(f"unexpected keyword argument {name!r}")
             if value != _UNSUPPORTED[name]:
                 raise ValueError(f"the {name} policy is not restated by this oracle")
+        if stop not in (None, "residual-goal"):
+            raise ValueError(f"unknown STOP rule {stop!r}; expected residual-goal")
+        if stop and not committed_paths:
+            raise ValueError("residual-goal STOP needs committed paths (committed_paths=True)")
+        self._stop_terms = None
+        if stop:
+            from xgraph_b200.stopping import RelationTerms
+
+            self._stop_terms = RelationTerms.from_index(index, tokenizer)
         self._eos = tokenizer.check_eos_token_ids(eos_token_ids) if end_after_answer else frozenset()
         self._end_after_answer = end_after_answer
         if start_rank not in ("degree", "sitelinks"):
@@ -189,6 +203,8 @@ class Oracle:
         self._relation_rows = [
             (relations.row_tokens(r), relations.owner_id(r)) for r in range(relations.num_rows)
         ]
+        self._relation_number = {owner: n for n, owner in enumerate(relations.owner_ids)}
+        self._label_prefix = syntax.label_prefix
         self._first_row: dict[str, int] = {}
         self._rows_of: dict[str, list[int]] = {}
         for row, (_, owner) in enumerate(self._entity_rows):
@@ -246,14 +262,18 @@ class Oracle:
 
     # -- states (src/xgraph/oracle.py:660-724) ------------------------------------
 
-    def initial_state(self, version: str | None = None) -> OracleState:
-        return OracleState(Phase.FREE, version=self._version(version))
+    def initial_state(self, version: str | None = None, *, question: str | None = None) -> OracleState:
+        stop = self._stop_terms.for_question(question) if self._stop_terms is not None else None
+        return OracleState(Phase.FREE, version=self._version(version), stop=stop)
 
-    def anchored_state(self, entities: list[str], version: str | None = None) -> OracleState:
+    def anchored_state(self, entities: list[str], version: str | None = None, *,
+                       question: str | None = None) -> OracleState:
         rows = self._rows_for(entities)
         if not rows:
             raise ValueError(f"anchor has no writable label rows: {entities!r}")
-        return OracleState(Phase.FREE, reached=frozenset(rows[:MAX_REACHED]), version=self._version(version))
+        stop = self.initial_state(question=question).stop
+        return OracleState(Phase.FREE, reached=frozenset(rows[:MAX_REACHED]), version=self._version(version),
+                           stop=stop)
 
     def opened_state(self, state: OracleState) -> OracleState:
         if state.answer_complete:
@@ -261,7 +281,7 @@ class Oracle:
         if state.phase is not Phase.FREE:
             raise ValueError(f"a span opens from free text, not from {state.phase.value}")
         return OracleState(Phase.SPAN, last_span=state.last_span, facts=state.facts,
-                           reached=state.reached, version=state.version)
+                           reached=state.reached, version=state.version, stop=state.stop)
 
     def _version(self, version: str | None) -> str | None:
         if version not in self._graphs:
@@ -322,7 +342,7 @@ class Oracle:
         if at + len(self._closer) != len(text):
             return None
         return OracleState(Phase.FREE, last_span=UNRESOLVED, facts=state.facts,
-                           reached=state.reached, version=state.version)
+                           reached=state.reached, version=state.version, stop=state.stop)
 
     # -- candidates (src/xgraph/oracle.py:830-894) --------------------------------
 
@@ -377,8 +397,13 @@ class Oracle:
                 len(state.written) - 1 < MAX_PATH_RELATIONS - 1
                 and any(graph.has_triples(e) for e in self._frontier(state, state.typed))
             )
-        escapes = self._escapes and state.typed is not None and self._may_escape(state)
-        return _SpanContext(complete, closes, separates, escapes)
+        # residual-goal STOP (src/xgraph/oracle.py:1081-1111): the separator and the escape
+        # marker neither start nor go on; the closer and the label do
+        forced = bool(complete) and self._residual_goal_stop(state)
+        if forced:
+            separates = False
+        escapes = self._escapes and state.typed is not None and self._may_escape(state) and not forced
+        return _SpanContext(complete, closes, separates, escapes, forced)
 
     @staticmethod
     def _branch(typed, label, data, delimiter, may_start, current):
@@ -398,8 +423,10 @@ class Oracle:
         closing, closing_label = self._branch(
             state.closing, state.closing_label, data, self._closer, ctx.closes, state.typed)
         separating, separating_label = self._branch(
-            state.separating, state.separating_label, data, self._separator, ctx.separates, state.typed)
-        escaping, _ = self._branch(state.escaping, (), data, self._escape, ctx.escapes, state.typed)
+            None if ctx.forced else state.separating, state.separating_label, data, self._separator, ctx.separates,
+            state.typed)
+        escaping, _ = self._branch(None if ctx.forced else state.escaping, (), data, self._escape, ctx.escapes,
+                                   state.typed)
 
         if closing == self._closer and state.segment is Segment.RELATION:  # a path ends
             frontier = self._frontier(state, closing_label)
@@ -412,7 +439,7 @@ class Oracle:
                 last_span=ClosedSpan((*state.written, closing_label), tuple(sorted(frontier)), (), True),
                 facts=state.facts,
                 reached=frozenset(rows[:MAX_REACHED]),
-                version=state.version,
+                version=state.version, stop=state.stop,
             )
         if closing == self._closer:
             facts, reached = state.facts, state.reached
@@ -427,13 +454,13 @@ class Oracle:
                 answer_complete=self._end_after_answer and self._answers_path(state),
                 facts=facts,
                 reached=reached,
-                version=state.version,
+                version=state.version, stop=state.stop,
             )
         if separating == self._separator:
             return self._next_segment(state, separating_label)
         if escaping == self._escape:
             return OracleState(Phase.ESCAPED, last_span=state.last_span, facts=state.facts,
-                               reached=state.reached, version=state.version)
+                               reached=state.reached, version=state.version, stop=state.stop)
         if label is None and closing is None and separating is None and escaping is None:
             return None
         return replace(
@@ -460,6 +487,26 @@ class Oracle:
             if r in state.relations and o in objects
         }
         return ClosedSpan((*state.written, label), (), tuple(sorted(triples)), True)
+
+    def _residual_goal_stop(self, state: OracleState) -> bool:
+        """src/xgraph/oracle.py:1608-1635: inside a path, the typed relation label is
+        complete, one of the relations it names is one the question's answer head names,
+        and no relation of the new, whole frontier covers a question word that neither the
+        written start nor the relations written so far (this one included) cover."""
+        goal = state.stop
+        if goal is None or not goal.head or state.segment is not Segment.RELATION:
+            return False
+        followed = {self._relation_number[r] for tokens, r in self._relation_rows if tokens == state.typed}
+        if not followed & goal.head:
+            return False
+        start = b"".join(self._bytes[t] for t in state.written[0]).decode("utf-8", "replace")
+        used = goal.used_by_start(start.removeprefix(self._label_prefix))
+        for label in (*state.written[1:], state.typed):
+            used |= goal.used_by_relations(
+                self._relation_number[r] for tokens, r in self._relation_rows if tokens == label)
+        frontier = self._frontier(state, state.typed)
+        return not any(goal.coverage.get(self._relation_number[r], 0) & ~used
+                       for _, r, _ in self._graph(state).from_subjects(frontier))
 
     def _may_escape(self, state: OracleState) -> bool:
         bound = state.segment is Segment.SUBJECT and self._derivation and bool(state.reached)
@@ -518,17 +565,17 @@ class Oracle:
             return OracleState(
                 Phase.SPAN, segment=Segment.RELATION, subjects=subjects, written=written,
                 last_span=state.last_span, facts=state.facts, reached=state.reached,
-                version=state.version, ranks=tuple(sorted(ranks.items())),
+                version=state.version, stop=state.stop, ranks=tuple(sorted(ranks.items())),
             )
         if self._paths:
             frontier = self._frontier(state, label)
             return OracleState(
                 Phase.SPAN, segment=Segment.RELATION, subjects=frozenset(frontier), written=written,
                 last_span=state.last_span, facts=state.facts, reached=state.reached,
-                version=state.version, ranks=tuple(sorted(frontier.items())),
+                version=state.version, stop=state.stop, ranks=tuple(sorted(frontier.items())),
             )
         return OracleState(
             Phase.SPAN, segment=Segment.OBJECT, subjects=state.subjects, relations=frozenset(items),
             written=written, last_span=state.last_span, facts=state.facts, reached=state.reached,
-            version=state.version,
+            version=state.version, stop=state.stop,
         )
