@@ -54,7 +54,8 @@ enum xg_dtype { XG_F32 = 0, XG_BF16 = 1, XG_F16 = 2 };
  * included), four expression fields (always 0: expressions are not served), the
  * end-after-answer flag and the last closed span (kind 0 none, 1 unresolved, 2 entity,
  * 3 fact, 4 path; its rows).  ex_hi and flags are this engine's own: the end of the
- * typed label's exact rows and which delimiter branches may start next. */
+ * typed label's exact rows and which delimiter branches may start next (or that STOP
+ * holds); stop_used_lo/hi are the reference's STOP mask (csrc/engine.cu:88). */
 typedef struct XgState {
   int32_t phase, pos, segment, depth, lo, hi;
   int32_t close_pos, close_lo, close_hi;
@@ -65,7 +66,8 @@ typedef struct XgState {
   int32_t answer_complete;
   int32_t last_kind, last_lo, last_hi, last_subj_lo, last_subj_hi, last_rel_lo, last_rel_hi;
   int32_t ex_hi, flags;
-  int32_t reserved[31];
+  int32_t stop_used_lo, stop_used_hi;  /* residual-goal STOP: question words the path has used (64-bit mask) */
+  int32_t reserved[29];
 } XgState;
 
 #define XG_STATE_INTS 64
@@ -197,6 +199,23 @@ XG_API int xg_drop_version(XgEngine* engine, int32_t version, void* stream);
 XG_API int xg_set_version(XgEngine* engine, int32_t slot, int32_t version, void* stream);
 /* Engine::open_span (csrc/engine.cu:2955-2962): the slot starts inside a span. */
 XG_API int xg_open_span(XgEngine* engine, int32_t slot, void* stream);
+/* Residual-goal STOP (the reference engine's stop="residual-goal", csrc/engine.cu:1001-1072,
+ * 1580-1583, 1872, 1902): enable it on an engine (path mode with committed paths) with the
+ * case-folded words of every entity label row, host CSR: label_offsets int64 [entity_rows
+ * + 1] into label_words, each row's words (its text after the label prefix, \w+ runs,
+ * case-folded) each followed by a 0 byte.  Allocates the per-slot STOP tables; slots start
+ * without one. */
+XG_API int xg_enable_stop(XgEngine* engine, const int64_t* label_offsets, const uint8_t* label_words,
+                          int64_t word_bytes);
+/* Engine::set_stop (csrc/engine.cu:2909-2940): one request's STOP table for the slot, host
+ * arrays: relations int32 [relation_count][3] (per relation number: 1 when the question's
+ * answer head names it, then the 64-bit mask of the relevant question words it covers, low
+ * and high halves), the relevant question words' UTF-8 bytes (at most 4096) and their
+ * offsets int32 [count + 1] (from 0 to word_bytes, count at most 64).  Call after begin; the
+ * slot's next begin (or admission) clears it.  XG_EINVAL without xg_enable_stop. */
+XG_API int xg_set_stop(XgEngine* engine, int32_t slot, const int32_t* relations, int32_t relation_count,
+                       const uint8_t* words, int32_t word_bytes, const int32_t* offsets, int32_t offset_count,
+                       void* stream);
 /* Engine::advance (csrc/engine.cu:3041-3054): advance slots 0..count-1 by tokens[i];
  * tokens_on_host != 0 means host memory (copied first). */
 XG_API int xg_advance(XgEngine* engine, const int32_t* tokens, int32_t count, int32_t tokens_on_host,

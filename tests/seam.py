@@ -42,6 +42,10 @@ def library():
     lib.xgs_relation_slice.restype = None
     lib.xgs_escape_policy.argtypes = [p, i32, p, p, p, p, i32]
     lib.xgs_escape_policy.restype = i32
+    lib.xgs_enable_stop.argtypes = [p, p, p, ctypes.c_int64]
+    lib.xgs_enable_stop.restype = None
+    lib.xgs_set_stop.argtypes = [p, i32, p, p, i32, p, i32]
+    lib.xgs_set_stop.restype = None
     return lib
 
 
@@ -79,6 +83,25 @@ class SeamEngine:
             released.ctypes.data_as(ctypes.c_void_p), counts[1:].ctypes.data_as(ctypes.c_void_p), cap)
         assert counts.max() <= cap
         return int(pos), set(commits[: counts[0]].tolist()), set(released[: counts[1]].tolist())
+
+    def enable_stop(self, tokenizer):
+        """Residual-goal STOP with the index's label words (as Engine(stop=...) does)."""
+        from xgraph_b200.stopping import RelationTerms, label_word_table
+
+        self._stop_offsets, self._stop_words = label_word_table(self.index, tokenizer)
+        self.lib.xgs_enable_stop(self.handle, self._stop_offsets.ctypes.data_as(ctypes.c_void_p),
+                                 self._stop_words.ctypes.data_as(ctypes.c_void_p), len(self._stop_words))
+        self._stop_terms = RelationTerms.from_index(self.index, tokenizer)
+
+    def set_stop(self, slot, question):
+        goal = self._stop_terms.for_question(question)
+        relations, offsets, words = goal.arrays(len(self.index.relations.owner_ids))
+        count = int(offsets[0])
+        word_offsets = np.ascontiguousarray(offsets[1: count + 2], dtype=np.int32)
+        buffer = np.frombuffer(words, dtype=np.uint8) if words else np.zeros(1, dtype=np.uint8)
+        self.lib.xgs_set_stop(self.handle, slot, relations.ctypes.data_as(ctypes.c_void_p),
+                              buffer.ctypes.data_as(ctypes.c_void_p), len(words),
+                              word_offsets.ctypes.data_as(ctypes.c_void_p), len(word_offsets))
 
     def relation_slice(self, entity, relation, version=0):
         out = np.zeros(3, dtype=np.int32)

@@ -33,6 +33,7 @@ def test_valid_arguments(extra):
                                    {"xgraph_prefill": "x"}, {"xgraph": 1, "xgraph_prefill": ""},
                                    {"xgraph": 1, "xgraph_prefill": "x", "xgraph_open": 1},
                                    {"xgraph": 1, "xgraph_replay_id": "k"}, {"xgraph": 1, "xgraph_stop": 1},
+                                   {"xgraph": 1, "xgraph_question": None, "xgraph_stop": 2},
                                    {"xgraph_stop": 0}, {"xgraph": 1, "xgraph_question": " "},
                                    {"xgraph": 1, "xgraph_relation_ranks": []}, {"xgraph": 1, "xgraph_path_options": "{}"},
                                    {"xgraph": 1, "xgraph_kg_version": 3}, {"xgraph": 1, "xgraph_kg_version": "v"}])
@@ -44,8 +45,9 @@ def test_invalid_arguments_raise(extra, monkeypatch):
 
 def test_unserved_settings_are_refused():
     adapter.check_served_settings({"XGRAPH_PATHS": "1", "XGRAPH_RELEASE_MASS": "0.2", "XGRAPH_RELATIONS": "frontier",
-                                   "XGRAPH_ESCAPE_BIAS": "-2.5", "XGRAPH_RELEASE_TOP": "1", "XGRAPH_OBSERVE": "0.0"})
-    for name, value in [("XGRAPH_MENU", "3"), ("XGRAPH_STOP", "residual-goal"), ("XGRAPH_AUDIT", "1"),
+                                   "XGRAPH_ESCAPE_BIAS": "-2.5", "XGRAPH_RELEASE_TOP": "1", "XGRAPH_OBSERVE": "0.0",
+                                   "XGRAPH_STOP": "residual-goal"})
+    for name, value in [("XGRAPH_MENU", "3"), ("XGRAPH_AUDIT", "1"),
                         ("XGRAPH_RELATIONS", "successor"), ("XGRAPH_EXPRESSIONS", "1"), ("XGRAPH_OBSERVE", "4")]:
         with pytest.raises(ValueError, match=name):
             adapter.check_served_settings({name: value})
@@ -111,7 +113,7 @@ def test_admissions_become_one_record_per_slot():
             admitted.append(records)
 
     proc = object.__new__(adapter.XGraphLogitsProcessor)
-    proc._engine, proc._stream = FakeEngine(), lambda: 0
+    proc._engine, proc._stream, proc._stop = FakeEngine(), lambda: 0, None
     proc._staged, proc._folded, proc._prefills = {}, None, {}
     assert proc.add_request(3, params(xgraph=1, xgraph_anchor=["Q1"], xgraph_kg_version="v1"))
     assert not proc.add_request(1, params())
@@ -131,6 +133,42 @@ def test_admissions_become_one_record_per_slot():
     proc.add_request(4, params())  # admitted and ended in one round: it ends
     proc.add_request(4, params(xgraph=1))
     assert proc._staged[4].ended
+
+
+def test_stop_questions_are_installed_after_their_admissions(monkeypatch):
+    """With XGRAPH_STOP=residual-goal a request's question becomes its slot's STOP table
+    (Engine.set_stop) right after an admit launch of the round's admissions (the table must
+    follow the slot's begin); a request with xgraph_stop=0 gets none."""
+    from xgraph_b200.engine import Admission
+
+    calls = []
+
+    class FakeEngine:
+        def admission_records(self, admissions):
+            return list(admissions)
+
+        def admit(self, records, stream):
+            calls.append(("admit", records))
+
+        def set_stop(self, slot, question, stream):
+            calls.append(("set_stop", slot, question))
+
+    monkeypatch.setenv("XGRAPH_STOP", "residual-goal")
+    proc = object.__new__(adapter.XGraphLogitsProcessor)
+    proc._engine, proc._stream, proc._stop = FakeEngine(), lambda: 0, "residual-goal"
+    proc._staged, proc._folded, proc._prefills = {}, None, {}
+    with pytest.raises(ValueError, match="xgraph_question"):
+        proc.add_request(0, params(xgraph=1))
+    assert proc.add_request(0, params(xgraph=1, xgraph_question="Which employer has Marie Curie?"))
+    assert proc.add_request(1, params(xgraph=1, xgraph_stop=0))
+    proc.apply_staged_writes()
+    assert calls == [("admit", [Admission(0, True), Admission(1, True)]),
+                     ("set_stop", 0, "Which employer has Marie Curie?")]
+    assert proc._folded is None
+    adapter.XGraphLogitsProcessor.validate_params(params(xgraph=1, xgraph_question="Which spouse has Ada?"))
+    with pytest.raises(ValueError, match="xgraph_question"):
+        adapter.XGraphLogitsProcessor.validate_params(params(xgraph=1))
+    adapter.XGraphLogitsProcessor.validate_params(params(xgraph=1, xgraph_stop=0))
 
 
 # -- GPU ---------------------------------------------------------------------------------

@@ -45,13 +45,15 @@ constexpr int32_t kTopCap = 256;      // per-warp candidate buffer of the top-64
 constexpr int32_t kItemBatch = 1;     // rounds of slice items whose loads are issued together
 constexpr int32_t kLoadBatch = 4;     // warp_for_loaded: rounds whose loads are issued together
 constexpr int32_t kScratchInts = 2 * kMaxSet + 2 + 2 * kMaxSet + kMaxSet;
+constexpr int32_t kMaxStopWords = 64;    // MAX_STOP_WORDS (src/xgraph/stopping.py:45)
+constexpr int32_t kMaxStopBytes = 4096;  // MAX_STOP_BYTES (src/xgraph/stopping.py:46)
 constexpr int8_t kReject = -1;
 constexpr int8_t kComplete = -2;
 
 enum Phase : int32_t { kFree = 0, kSpan = 1, kEscaped = 2, kError = 3 };
 enum Segment : int32_t { kSubject = 0, kRelation = 1, kObject = 2 };
 enum Closed : int32_t { kNone = 0, kUnresolved = 1, kEntitySpan = 2, kFactSpan = 3, kPathSpan = 4 };
-enum Flag : int32_t { kMayClose = 1, kMaySep = 2, kMayEsc = 4 };
+enum Flag : int32_t { kMayClose = 1, kMaySep = 2, kMayEsc = 4, kStop = 8 };
 
 // Slot memory (int32 words per slot): counts, then the fixed lists, then the bitmap of
 // the relations the current subjects / frontier have.
@@ -156,6 +158,16 @@ struct Tables {
   // when its own top token is disallowed; add escape_bias to the tokens that commit to it.
   float release_log_mass, escape_bias;
   int32_t release_top, release_on;
+  // residual-goal STOP (null stop_on: not enabled): every entity label row's case-folded
+  // words (CSR, each word followed by a 0 byte); per slot: whether a table is installed,
+  // per relation number (answer-head flag, covered question words low, high), and the
+  // relevant question words (count, then byte offsets; their bytes)
+  const int64_t* stop_label_off;
+  const uint8_t* stop_label_words;
+  int32_t* stop_on;           // [slots]
+  const int32_t* stop_rel;    // [slots][relations][3]
+  const int32_t* stop_woff;   // [slots][kMaxStopWords + 2]
+  const uint8_t* stop_words;  // [slots][kMaxStopBytes]
   // per-slot engine buffers
   XgState* states;
   int32_t* memory;
@@ -1027,6 +1039,104 @@ XG_COLD bool frontier_goes_on(const Ctx& c, int32_t rlo, int32_t rhi) {
   });
 }
 
+// ---------------------------------------------------------------------------------------
+// Residual-goal STOP (src/xgraph/oracle.py:1608-1635; csrc/engine.cu:1001-1072 of the
+// reference).
+
+XG_HD uint64_t stop_used(const XgState& s) {
+  return static_cast<uint32_t>(s.stop_used_lo) | (static_cast<uint64_t>(static_cast<uint32_t>(s.stop_used_hi)) << 32);
+}
+
+XG_HD void set_stop_used(XgState& s, uint64_t mask) {
+  s.stop_used_lo = static_cast<int32_t>(mask);
+  s.stop_used_hi = static_cast<int32_t>(mask >> 32);
+}
+
+XG_HD bool stop_installed(const Ctx& c) { return c.t.stop_on != nullptr && c.t.stop_on[c.slot] != 0; }
+
+// The slot's STOP entry of relation number r: (answer-head flag, coverage low, high).
+XG_HD const int32_t* stop_entry(const Ctx& c, int32_t r) {
+  return c.t.stop_rel + (static_cast<int64_t>(c.slot) * c.t.relations + r) * 3;
+}
+
+XG_HD uint64_t stop_coverage(const int32_t* e) {
+  return static_cast<uint32_t>(e[1]) | (static_cast<uint64_t>(static_cast<uint32_t>(e[2])) << 32);
+}
+
+// The question words the relations of relation-label rows [lo, hi) cover (every relation
+// the written label names, as the reference's consumed relations read them).
+XG_COLD uint64_t stop_consumed(const Ctx& c, int32_t lo, int32_t hi) {
+  uint64_t used = 0;
+  warp_for(c.w, lo, hi, [&](int32_t row) { used |= stop_coverage(stop_entry(c, c.t.rel.owner[row])); });
+#if XG_GPU
+  for (int32_t d = 16; d > 0; d >>= 1) used |= __shfl_xor_sync(0xffffffffu, used, d);
+#endif
+  return used;
+}
+
+// The question words among the words of entity label row `row` (the written start).
+XG_COLD uint64_t stop_start_words(const Ctx& c, int32_t row) {
+  const Tables& t = c.t;
+  const int32_t* offsets = t.stop_woff + static_cast<int64_t>(c.slot) * (kMaxStopWords + 2);
+  const uint8_t* words = t.stop_words + static_cast<int64_t>(c.slot) * kMaxStopBytes;
+  const int32_t count = offsets[0];
+  uint64_t used = 0;
+  // the row's words one after another; lanes take the question words
+  int64_t at = t.stop_label_off[row];
+  const int64_t end = t.stop_label_off[row + 1];
+#pragma unroll 1
+  while (at < end) {
+    int64_t stop = at;
+    while (stop < end && t.stop_label_words[stop] != 0) ++stop;
+    warp_for(c.w, 0, count, [&](int32_t k) {
+      const int32_t first = offsets[k + 1], last = offsets[k + 2];
+      if (stop - at != last - first) return;
+      int32_t j = 0;
+      while (j < last - first && words[first + j] == t.stop_label_words[at + j]) ++j;
+      if (j == last - first) used |= uint64_t{1} << k;
+    });
+    at = stop + 1;
+  }
+#if XG_GPU
+  for (int32_t d = 16; d > 0; d >>= 1) used |= __shfl_xor_sync(0xffffffffu, used, d);
+#endif
+  return used;
+}
+
+// Whether STOP holds after the complete relation label rows [s.lo, s.ex_hi) of a path: one
+// of their relations is named by the answer head, and no relation of the new, whole
+// capped frontier covers a question word that neither the start nor the relations written
+// so far (these included) cover.
+XG_COLD bool residual_goal_stop(const Ctx& c, const XgState& s) {
+  const Tables& t = c.t;
+  if (!t.paths || s.segment != kRelation || !stop_installed(c)) return false;
+  if (!warp_any(c.w, s.lo, s.ex_hi, [&](int32_t row) { return stop_entry(c, t.rel.owner[row])[0] != 0; }))
+    return false;
+  const uint64_t used = stop_used(s) | stop_consumed(c, s.lo, s.ex_hi);
+  const int32_t n = cached_frontier(c, s.lo, s.ex_hi);  // ENTITY keys in c.top[0, n)
+  const int32_t version = version_of(c);
+  bool open = false;  // some frontier relation covers an unused question word
+  for_each_slice_item(
+      c, n,
+      [&](int32_t k, const int32_t*& p, int32_t& len) {
+        const Edges g = edges_of(t, version, t.ent.owner[static_cast<int32_t>(c.top[k].a & 0xffffffffu)]);
+        if (g.runs >= 0) {  // one entry per relation run
+          p = t.run_rel + g.run0;
+          len = g.runs;
+        } else {
+          p = g.rel;
+          len = g.n;
+        }
+      },
+      [&](bool valid, int32_t, int32_t relation) {
+        if (valid && (stop_coverage(stop_entry(c, relation)) & ~used) != 0) open = true;
+      });
+#if XG_GPU
+  open = __any_sync(0xffffffffu, open);
+#endif
+  return !open;
+}
+
 // Which delimiter branches may start after the state's typed label
 // (src/xgraph/oracle.py:1039-1113: closes, separates, and the escape condition).
 XG_SHARED void set_flags(const Ctx& c, XgState& s) {
@@ -1057,11 +1167,17 @@ XG_SHARED void set_flags(const Ctx& c, XgState& s) {
                   });
     } else if (s.segment == kRelation) {
       separates = !t.paths || (s.hops < kMaxHops && frontier_goes_on(c, s.lo, s.ex_hi));
+      // residual-goal STOP (src/xgraph/oracle.py:1081-1111): only the closer or the label
+      // goes on (neither the separator nor the escape marker starts or goes on)
+      if (closes && t.stop_on != nullptr && residual_goal_stop(c, s)) {
+        s.flags |= kStop;
+        separates = false;
+      }
     }
     if (separates) s.flags |= kMaySep;
   }
   // escape (src/xgraph/oracle.py:1874-1883): a bound subject escapes only with bound_escapes
-  if (t.escapes && (t.bound_escapes || !bound)) s.flags |= kMayEsc;
+  if (t.escapes && (t.bound_escapes || !bound) && !(s.flags & kStop)) s.flags |= kMayEsc;
 }
 
 XG_HD void clear_span(XgState& s) {
@@ -1082,6 +1198,7 @@ XG_HD void open_span(const Ctx& c, XgState& s) {
   s.phase = kSpan;
   s.pos = 0;
   s.hi = c.t.ent.count;
+  s.stop_used_lo = s.stop_used_hi = 0;
   set_flags(c, s);
 }
 
@@ -1161,7 +1278,11 @@ XG_COLD void next_segment(const Ctx& c, XgState& s, int32_t llo, int32_t lhi) {
     s.subj_key = llo;
     s.segment = kRelation;
     s.hops = 1;
+    // STOP: the question words the written start covers (csrc/engine.cu:1872)
+    if (stop_installed(c)) set_stop_used(s, stop_start_words(c, llo));
   } else if (t.paths) {
+    // STOP: and those the relations just written cover (csrc/engine.cu:1902-1904)
+    if (stop_installed(c)) set_stop_used(s, stop_used(s) | stop_consumed(c, llo, lhi));
     const int32_t n = cached_frontier(c, llo, lhi);
     store_frontier(c, n);
     const int32_t* ents = c.mem + kMemFrontierEnt;
@@ -1293,14 +1414,14 @@ XG_HD void advance_span(const Ctx& c, XgState& s, int32_t token) {
     close_lo = s.lo;
     close_hi = s.ex_hi;
   }
-  if (s.sep_pos > 0) {
+  if (s.sep_pos > 0 && !(s.flags & kStop)) {
     sep = delim_next(t, packed, 1, s.sep_pos, token);
   } else if (s.flags & kMaySep) {
     sep = delim_next(t, packed, 1, 0, token);
     sep_lo = s.lo;
     sep_hi = s.ex_hi;
   }
-  if (s.esc_pos > 0) {
+  if (s.esc_pos > 0 && !(s.flags & kStop)) {
     esc = delim_next(t, packed, 2, s.esc_pos, token);
   } else if (s.flags & kMayEsc) {
     esc = delim_next(t, packed, 2, 0, token);
@@ -1561,8 +1682,9 @@ XG_HD MaskRef compose_mask(const Ctx& c, const XgState& s, uint32_t* own, bool z
     // each delimiter branch: its next tokens from where it stands, or from its start when
     // the flags let it begin here
     const int32_t close = s.close_pos > 0 ? s.close_pos : (s.flags & kMayClose) ? 0 : -1;
-    const int32_t sep = s.sep_pos > 0 ? s.sep_pos : (s.flags & kMaySep) ? 0 : -1;
-    const int32_t esc = s.esc_pos > 0 ? s.esc_pos : (s.flags & kMayEsc) ? 0 : -1;
+    const bool stop = s.flags & kStop;  // STOP: the separator and the escape marker neither go on nor start
+    const int32_t sep = s.sep_pos > 0 && !stop ? s.sep_pos : (s.flags & kMaySep) ? 0 : -1;
+    const int32_t esc = s.esc_pos > 0 && !stop ? s.esc_pos : (s.flags & kMayEsc) ? 0 : -1;
     add_delimiters(c, close, sep, esc, delta);
     warp_sync();
   }
@@ -1588,7 +1710,7 @@ XG_HD void build_mask(const Ctx& c, const XgState& s) {
 // further; -1 outside a span or with no way on.  A released row may write only the
 // marker's next tokens from there.
 XG_HD int32_t escape_position(const Tables& t, const XgState& s) {
-  if (s.phase != kSpan) return -1;
+  if (s.phase != kSpan || (s.flags & kStop)) return -1;
   const int32_t pos = s.esc_pos;
   if (delim_end(t.escape, pos) <= delim_begin(t.escape, pos)) return -1;
   return pos > 0 || (s.flags & kMayEsc) ? pos : -1;

@@ -175,6 +175,7 @@ __global__ void begin_kernel(const __grid_constant__ Tables t, const int32_t* sl
   t.active[slot] = on;
   t.base[slot] = t.free_mask;
   t.delta[slot] = nullptr;
+  if (t.stop_on) t.stop_on[slot] = 0;  // a new request has no STOP table until set_stop
 }
 
 // fill_mask: materialize each slot's current mask (base | delta) into its own buffer row;
@@ -772,6 +773,7 @@ __device__ bool admit_slot(const Ctx& c, XgState& s, const XgAdmission& a, int32
     t.active[c.slot] = on ? 1 : 0;
     t.base[c.slot] = t.free_mask;
     t.delta[c.slot] = nullptr;
+    if (t.stop_on) t.stop_on[c.slot] = 0;
   }
   __syncwarp();
   if (on && a.open_span) open_span(c, s);  // reads the anchors and version just written
@@ -1199,6 +1201,14 @@ struct XgEngine {
   int32_t* faults = nullptr;      // device-side faults (xg_faults)
   XgAdmission* admissions = nullptr;  // staging of host admissions: max_sequences entries
   size_t composed_bytes = 0;      // sync_apply's dynamic shared memory: one mask row
+  // residual-goal STOP (xg_enable_stop): label words, and per slot: installed flag, relation
+  // table, question word offsets and bytes
+  int64_t* stop_label_off = nullptr;
+  uint8_t* stop_label_words = nullptr;
+  int32_t* stop_on = nullptr;
+  int32_t* stop_rel = nullptr;
+  int32_t* stop_woff = nullptr;
+  uint8_t* stop_words = nullptr;
   VersionArena arena;
   Tables t{};
 };
@@ -1491,6 +1501,12 @@ void release(XgEngine* e) {
   cudaFree(e->tokens);
   cudaFree(e->draft_scratch);
   cudaFree(e->faults);
+  cudaFree(e->stop_label_off);
+  cudaFree(e->stop_label_words);
+  cudaFree(e->stop_on);
+  cudaFree(e->stop_rel);
+  cudaFree(e->stop_woff);
+  cudaFree(e->stop_words);
   cudaFree(e->admissions);
   for (void* p : {static_cast<void*>(e->arena.range), static_cast<void*>(e->arena.subjects),
                   static_cast<void*>(e->arena.adjacency), static_cast<void*>(e->arena.relations),
@@ -1827,6 +1843,85 @@ int xg_open_span(XgEngine* e, int32_t slot, void* stream) {
   a.slot = slot;
   a.op = 0;
   return slot_op(e, a, stream);
+}
+
+int xg_enable_stop(XgEngine* e, const int64_t* label_offsets, const uint8_t* label_words, int64_t word_bytes) {
+  if (!e || !label_offsets || (word_bytes > 0 && !label_words)) return fail(XG_EINVAL, "null argument");
+  if (!e->t.paths || !e->t.committed) return fail(XG_EINVAL, "residual-goal STOP needs committed paths (committed_paths=True)");
+  if (e->stop_on) return fail(XG_EINVAL, "STOP is already enabled on this engine");
+  const int64_t rows = e->layout.entity_rows;
+  if (label_offsets[0] != 0 || label_offsets[rows] != word_bytes)
+    return fail(XG_EINVAL, "STOP label words: offsets must run from 0 to the word bytes, one row per label row");
+  for (int64_t r = 0; r < rows; ++r)
+    if (label_offsets[r + 1] < label_offsets[r]) return fail(XG_EINVAL, "STOP label word offsets must not decrease");
+  const int64_t slots = e->max_sequences;
+  cudaError_t err = cudaSuccess;
+  auto alloc = [&](void** p, size_t bytes) {
+    if (err == cudaSuccess) err = cudaMalloc(p, bytes > 0 ? bytes : 16);
+  };
+  alloc(reinterpret_cast<void**>(&e->stop_label_off), (rows + 1) * sizeof(int64_t));
+  alloc(reinterpret_cast<void**>(&e->stop_label_words), static_cast<size_t>(word_bytes));
+  alloc(reinterpret_cast<void**>(&e->stop_on), slots * sizeof(int32_t));
+  alloc(reinterpret_cast<void**>(&e->stop_rel), slots * static_cast<size_t>(e->t.relations) * 3 * sizeof(int32_t));
+  alloc(reinterpret_cast<void**>(&e->stop_woff), slots * (kMaxStopWords + 2) * sizeof(int32_t));
+  alloc(reinterpret_cast<void**>(&e->stop_words), slots * static_cast<size_t>(kMaxStopBytes));
+  if (err == cudaSuccess)
+    err = cudaMemcpy(e->stop_label_off, label_offsets, (rows + 1) * sizeof(int64_t), cudaMemcpyHostToDevice);
+  if (err == cudaSuccess && word_bytes > 0)
+    err = cudaMemcpy(e->stop_label_words, label_words, static_cast<size_t>(word_bytes), cudaMemcpyHostToDevice);
+  if (err == cudaSuccess) err = cudaMemset(e->stop_on, 0, slots * sizeof(int32_t));
+  if (err != cudaSuccess) {
+    for (void* p : {static_cast<void*>(e->stop_label_off), static_cast<void*>(e->stop_label_words),
+                    static_cast<void*>(e->stop_on), static_cast<void*>(e->stop_rel), static_cast<void*>(e->stop_woff),
+                    static_cast<void*>(e->stop_words)})
+      cudaFree(p);
+    e->stop_label_off = nullptr;
+    e->stop_label_words = nullptr;
+    e->stop_on = e->stop_rel = e->stop_woff = nullptr;
+    e->stop_words = nullptr;
+    return cuda_fail(err, "STOP tables");
+  }
+  e->t.stop_label_off = e->stop_label_off;
+  e->t.stop_label_words = e->stop_label_words;
+  e->t.stop_on = e->stop_on;
+  e->t.stop_rel = e->stop_rel;
+  e->t.stop_woff = e->stop_woff;
+  e->t.stop_words = e->stop_words;
+  return XG_OK;
+}
+
+int xg_set_stop(XgEngine* e, int32_t slot, const int32_t* relations, int32_t relation_count, const uint8_t* words,
+                int32_t word_bytes, const int32_t* offsets, int32_t offset_count, void* stream) {
+  if (!e) return fail(XG_EINVAL, "null engine");
+  if (!e->stop_on) return fail(XG_EINVAL, "STOP is not enabled (stop='residual-goal')");
+  if (int rc = check_slot(e, slot)) return rc;
+  if (!relations || !offsets || (word_bytes > 0 && !words)) return fail(XG_EINVAL, "null argument");
+  const int32_t count = offset_count - 1;
+  if (relation_count != e->t.relations || count < 0 || count > kMaxStopWords || word_bytes < 0 ||
+      word_bytes > kMaxStopBytes)
+    return fail(XG_EINVAL, "STOP needs one entry per relation and at most 64 question words of 4096 bytes");
+  if (offsets[0] != 0 || offsets[count] != word_bytes)
+    return fail(XG_EINVAL, "STOP word offsets must cover the word bytes");
+  for (int32_t k = 0; k < count; ++k)
+    if (offsets[k + 1] < offsets[k]) return fail(XG_EINVAL, "STOP word offsets must not decrease");
+  std::vector<int32_t> woff(kMaxStopWords + 2, 0);
+  woff[0] = count;
+  for (int32_t k = 0; k <= count; ++k) woff[k + 1] = offsets[k];
+  cudaStream_t s = as_stream(stream);
+  static const int32_t on = 1;
+  XG_CUDA(cudaMemcpyAsync(e->stop_rel + static_cast<int64_t>(slot) * e->t.relations * 3, relations,
+                          static_cast<size_t>(relation_count) * 3 * sizeof(int32_t), cudaMemcpyHostToDevice, s),
+          "STOP upload");
+  XG_CUDA(cudaMemcpyAsync(e->stop_woff + static_cast<int64_t>(slot) * (kMaxStopWords + 2), woff.data(),
+                          woff.size() * sizeof(int32_t), cudaMemcpyHostToDevice, s),
+          "STOP upload");
+  if (word_bytes > 0)
+    XG_CUDA(cudaMemcpyAsync(e->stop_words + static_cast<int64_t>(slot) * kMaxStopBytes, words,
+                            static_cast<size_t>(word_bytes), cudaMemcpyHostToDevice, s),
+            "STOP upload");
+  XG_CUDA(cudaMemcpyAsync(e->stop_on + slot, &on, sizeof(int32_t), cudaMemcpyHostToDevice, s), "STOP upload");
+  // the staging vector is pageable: the copies above have read it when they return
+  return XG_OK;
 }
 
 int xg_advance(XgEngine* e, const int32_t* tokens, int32_t count, int32_t tokens_on_host, void* stream) {

@@ -24,6 +24,11 @@ struct SeamEngine {
   std::vector<Key> top;
   std::vector<int32_t> scratch;
   std::vector<int32_t> ver_range;  // the blob's cumulative version offsets as (begin, end) pairs
+  // residual-goal STOP (xgs_enable_stop)
+  std::vector<int64_t> stop_label_off;
+  std::vector<uint8_t> stop_label_words;
+  std::vector<int32_t> stop_on, stop_rel, stop_woff;
+  std::vector<uint8_t> stop_words;
   Tables t{};
 };
 
@@ -46,6 +51,7 @@ static void begin_slot(SeamEngine* e, int32_t slot, int32_t on) {
   e->active[slot] = on;
   e->base[slot] = e->t.free_mask;
   e->delta[slot] = nullptr;
+  if (!e->stop_on.empty()) e->stop_on[slot] = 0;
 }
 
 extern "C" {
@@ -206,6 +212,34 @@ void xgs_memory(SeamEngine* e, int32_t n, int32_t* out) {
 }
 
 int32_t xgs_memory_ints(SeamEngine* e) { return e->t.memory_ints; }
+
+// xg_enable_stop / xg_set_stop on the host (arguments checked by the library's entry points).
+void xgs_enable_stop(SeamEngine* e, const int64_t* offsets, const uint8_t* words, int64_t bytes) {
+  const int64_t rows = e->layout.entity_rows;
+  e->stop_label_off.assign(offsets, offsets + rows + 1);
+  e->stop_label_words.assign(words, words + bytes);
+  e->stop_on.assign(e->slots, 0);
+  e->stop_rel.assign(static_cast<size_t>(e->slots) * e->t.relations * 3, 0);
+  e->stop_woff.assign(static_cast<size_t>(e->slots) * (kMaxStopWords + 2), 0);
+  e->stop_words.assign(static_cast<size_t>(e->slots) * kMaxStopBytes, 0);
+  e->t.stop_label_off = e->stop_label_off.data();
+  e->t.stop_label_words = e->stop_label_words.data();
+  e->t.stop_on = e->stop_on.data();
+  e->t.stop_rel = e->stop_rel.data();
+  e->t.stop_woff = e->stop_woff.data();
+  e->t.stop_words = e->stop_words.data();
+}
+
+void xgs_set_stop(SeamEngine* e, int32_t slot, const int32_t* relations, const uint8_t* words, int32_t bytes,
+                  const int32_t* offsets, int32_t offset_count) {
+  std::memcpy(e->stop_rel.data() + static_cast<int64_t>(slot) * e->t.relations * 3, relations,
+              static_cast<size_t>(e->t.relations) * 3 * sizeof(int32_t));
+  int32_t* woff = e->stop_woff.data() + static_cast<int64_t>(slot) * (kMaxStopWords + 2);
+  woff[0] = offset_count - 1;
+  for (int32_t k = 0; k < offset_count; ++k) woff[k + 1] = offsets[k];
+  if (bytes > 0) std::memcpy(e->stop_words.data() + static_cast<int64_t>(slot) * kMaxStopBytes, words, bytes);
+  e->stop_on[slot] = 1;
+}
 
 // apply_mask's logit policies for a slot: returns its escape position (-1: release leaves
 // it alone); the tokens that commit it to the escape marker go to commits[0 .. *count) and

@@ -38,7 +38,7 @@ STATE_FIELDS = (
     "sep_pos", "sep_lo", "sep_hi", "esc_pos", "subj_lo", "subj_hi", "rel_lo", "rel_hi",
     "subj_key", "hops", "op_pos", "op_kind", "op", "operand", "answer_complete",
     "last_kind", "last_lo", "last_hi", "last_subj_lo", "last_subj_hi", "last_rel_lo",
-    "last_rel_hi", "ex_hi", "flags",
+    "last_rel_hi", "ex_hi", "flags", "stop_used_lo", "stop_used_hi",
 )
 """Names of the leading int32 words of a slot state (XgState in include/xgraph_b200.h)."""
 STATE_INTS = 64
@@ -55,7 +55,7 @@ DTYPES = {"float32": 0, "bfloat16": 1, "float16": 2}
 # Reference constructor options this engine does not serve, with their neutral values.
 _NOT_SERVED = {
     "expressions": False,
-    "stop": None, "relations": "frontier", "observe": 0, "observe_width": 0,
+    "relations": "frontier", "observe": 0, "observe_width": 0,
     "observe_defer": 0, "menu_close_next": False, "observe_select": False,
     "observe_answer": False, "observe_required": False, "observe_no_loop": False,
     "audit": False, "audit_entities": 20, "audit_relations": 8, "menu": 0,
@@ -112,6 +112,8 @@ def load_library(path: Path = LIBRARY):
         "xg_add_version": ([p, p, i32, p, p, p, p, ctypes.POINTER(i32)], ctypes.c_int),
         "xg_drop_version": ([p, i32, p], ctypes.c_int),
         "xg_build_adjacency": ([p, p, p, i64, p, p, i32, i32, p, i32, i64, p, p, p, p, p, p], ctypes.c_int),
+        "xg_enable_stop": ([p, p, p, i64], ctypes.c_int),
+        "xg_set_stop": ([p, i32, p, i32, p, i32, p, i32, p], ctypes.c_int),
         "xg_build_label_rows": ([i32, p, p, i64, p, p, i64, p, i32, i32, p, p, i64, p, p, p, p, p, p, p, p],
                                 ctypes.c_int),
     }
@@ -207,6 +209,7 @@ class Engine:
         unquoted_starts: bool = False,
         end_after_answer: bool = False,
         eos_token_ids: Iterable[int] = (),
+        stop: str | None = None,
         device_blob=None,
         **others,
     ) -> None:
@@ -230,6 +233,10 @@ class Engine:
                 raise TypeError(f"Engine() got an unexpected keyword argument {name!r}")
             if value != _NOT_SERVED[name]:
                 raise ValueError(f"the {name} policy is not served by this engine")
+        if stop not in (None, "residual-goal"):
+            raise ValueError(f"unknown STOP rule {stop!r}; expected residual-goal")
+        if stop and not committed_paths:
+            raise ValueError("residual-goal STOP needs committed paths (committed_paths=True)")
         sitelinks_rank = check_start_rank(start_rank, index) == "sitelinks"
         if not escapes and (release_mass > 0 or release_top):
             raise ValueError("release needs escapes: it releases to the escape marker")
@@ -273,6 +280,14 @@ class Engine:
                 ctypes.byref(self._options), int(max_sequences), ctypes.byref(handle))
         _check(rc)
         self._handle = handle
+        self._stop_terms = None
+        if stop:
+            from .stopping import RelationTerms, label_word_table
+
+            offsets, words = label_word_table(index, tokenizer)
+            _check(self._lib.xg_enable_stop(self._handle, offsets.ctypes.data_as(ctypes.c_void_p),
+                                            words.ctypes.data_as(ctypes.c_void_p), len(words)))
+            self._stop_terms = RelationTerms.from_index(index, tokenizer)
         info = _Info()
         _check(self._lib.xg_info(self._handle, ctypes.byref(info)))
         self._info = info
@@ -442,6 +457,22 @@ class Engine:
     def set_version(self, slot: int, version: str | None, stream: int = 0) -> None:
         number = self._version_number(version)
         _check(self._lib.xg_set_version(self._handle, int(slot), number, _stream(stream)))
+
+    def set_stop(self, slot: int, question: str, stream: int = 0) -> None:
+        """Residual-goal STOP (src/xgraph/engine.py:946-967): compile this request's STOP
+        relations from its question, after begin and before sync / open_span; the slot's
+        next begin clears them; draft rows read them in place."""
+        if self._stop_terms is None:
+            raise ValueError("set_stop needs stop='residual-goal'")
+        goal = self._stop_terms.for_question(question)
+        relations, offsets, words = goal.arrays(len(self._index.relations.owner_ids))
+        count = int(offsets[0])
+        word_offsets = np.ascontiguousarray(offsets[1: count + 2], dtype=np.int32)
+        buffer = np.frombuffer(words, dtype=np.uint8) if words else np.zeros(1, dtype=np.uint8)
+        _check(self._lib.xg_set_stop(
+            self._handle, int(slot), relations.ctypes.data_as(ctypes.c_void_p), relations.shape[0],
+            buffer.ctypes.data_as(ctypes.c_void_p), len(words), word_offsets.ctypes.data_as(ctypes.c_void_p),
+            len(word_offsets), _stream(stream)))
 
     def open_span(self, slot: int, stream: int = 0) -> None:
         _check(self._lib.xg_open_span(self._handle, int(slot), _stream(stream)))

@@ -192,3 +192,19 @@ class RelationTerms:
             for relation in self._by_stem[question_stems[word]]:
                 coverage[relation] = coverage.get(relation, 0) | (1 << i)
         return StopRelations(heads, frozenset(coverage), words, coverage)
+
+
+def label_word_table(index, tokenizer) -> tuple[np.ndarray, np.ndarray]:
+    """The engine's label words (xg_enable_stop): for every entity label row, the
+    case-folded \\w+ words of its text after the label prefix, each followed by a 0 byte, as
+    CSR (offsets int64 [rows + 1], bytes uint8); the reference's stop_label_offsets /
+    stop_label_words (src/xgraph/engine.py:537-551)."""
+    prefix = index.span_syntax.label_prefix
+    offsets = np.zeros(index.labels.num_rows + 1, dtype=np.int64)
+    written = bytearray()
+    for row in range(index.labels.num_rows):
+        raw = b"".join(tokenizer.token_bytes(t) or b"" for t in index.labels.row_tokens(row))
+        name = raw.decode("utf-8", "replace").removeprefix(prefix)
+        written.extend(b"\0".join(w.encode("utf-8") for w in start_words(name)) + b"\0")
+        offsets[row + 1] = len(written)
+    return offsets, np.frombuffer(written, dtype=np.uint8)

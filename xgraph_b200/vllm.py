@@ -27,9 +27,11 @@ which is then left unmasked), `xgraph_replay_id` (the key under which a replay's
 kept for `replay_statuses`).  Engine settings: XGRAPH_ESCAPES, XGRAPH_REPEATS,
 XGRAPH_RELEASE_MASS, XGRAPH_RELEASE_TOP, XGRAPH_DERIVATION, XGRAPH_ESCAPE_BIAS, XGRAPH_PATHS,
 XGRAPH_BOUND_ESCAPES, XGRAPH_COMMITTED_PATHS, XGRAPH_START_RANK, XGRAPH_UNQUOTED_STARTS,
-XGRAPH_END_AFTER_ANSWER.  The reference's research policies (STOP, expressions,
-observations, menus, audit, relation supports, per-request path options) are not served by
-this engine: a setting or argument that asks for one is refused with a ValueError naming it.
+XGRAPH_END_AFTER_ANSWER, XGRAPH_STOP (residual-goal: each opted-in request supplies its
+question as `xgraph_question`; `xgraph_stop` 0 turns STOP off for a request).  The
+reference's other research policies (expressions, observations, menus, audit, relation
+supports, per-request path options) are not served by this engine: a setting or argument
+that asks for one is refused with a ValueError naming it.
 
 This module imports only the standard library at import time: vLLM also calls
 validate_params in its frontend process.
@@ -60,15 +62,15 @@ PREFILL = "xgraph_prefill"
 REPLAY_ID = "xgraph_replay_id"
 """Per-request argument: the caller's key for the replay's outcome."""
 QUESTION = "xgraph_question"
-"""Per-request argument: the question text (accepted; no served policy reads it)."""
+"""Per-request argument: the question text, required with XGRAPH_STOP=residual-goal."""
 STOP = "xgraph_stop"
-"""Per-request argument: 0 turns STOP off for the request (STOP is never on here)."""
+"""Per-request argument: 0 turns STOP off for the request."""
 REPLAYS = ("replayed", "tail mismatch", "disallowed")
 """The outcomes of a replayed prefill, which XGraphLogitsProcessor.replays counts."""
 
 _UNSERVED_ARGS = ("xgraph_relation_ranks", "xgraph_path_options")
 _UNSERVED_SETTINGS = {  # setting: the value that keeps the policy off
-    "XGRAPH_EXPRESSIONS": "0", "XGRAPH_STOP": "", "XGRAPH_OBSERVE": "0", "XGRAPH_OBSERVE_SELECT": "0",
+    "XGRAPH_EXPRESSIONS": "0", "XGRAPH_OBSERVE": "0", "XGRAPH_OBSERVE_SELECT": "0",
     "XGRAPH_OBSERVE_ANSWER": "0", "XGRAPH_OBSERVE_WIDTH": "0", "XGRAPH_OBSERVE_DEFER": "0",
     "XGRAPH_OBSERVE_TERMINAL": "0", "XGRAPH_MENU": "0", "XGRAPH_MENU_CLOSE_NEXT": "0", "XGRAPH_AUDIT": "0",
     "XGRAPH_REQUEST_PATH_OPTIONS": "0", "XGRAPH_RELATIONS": "frontier",
@@ -220,6 +222,7 @@ class Staged:
     ended: bool = False
     prefill: bytes | None = None
     replay_id: str | None = None
+    question: str | None = None  # residual-goal STOP: the request's question
 
 
 class XGraphLogitsProcessor(_Base):
@@ -265,6 +268,7 @@ class XGraphLogitsProcessor(_Base):
             for ids in (getattr(served, "eos_token_id", None), generation.get("eos_token_id")):
                 if ids is not None:
                     eos_token_ids.extend([ids] if isinstance(ids, int) else ids)
+        self._stop = os.environ.get("XGRAPH_STOP") or None
         self._engine = Engine(
             index, tokenizer, index.span_syntax, req_states.max_num_reqs,
             escapes=os.environ.get("XGRAPH_ESCAPES", "1") != "0",
@@ -285,6 +289,7 @@ class XGraphLogitsProcessor(_Base):
             unquoted_starts=os.environ.get("XGRAPH_UNQUOTED_STARTS", "0") == "1",
             end_after_answer=end_after_answer,
             eos_token_ids=eos_token_ids,
+            stop=self._stop,
         )
         self._staged: dict[int, Staged] = {}   # slot -> admissions since the last apply_staged_writes
         self._folded = None                    # admission records the next step's launch applies
@@ -312,12 +317,13 @@ class XGraphLogitsProcessor(_Base):
         if unserved:
             raise ValueError(f"{unserved[0]!r} belongs to a policy the xgraph_b200 engine does not serve")
         question = extra.get(QUESTION)
-        if question is not None and not (isinstance(question, str) and question.strip()):
-            raise ValueError(f"{QUESTION!r} must be the question's text, not {question!r}")
         if STOP in extra:
             if type(extra[STOP]) is not int or extra[STOP] != 0:
-                raise ValueError(f"{STOP!r} can only be 0 (STOP is off in this engine), not {extra[STOP]!r}")
+                raise ValueError(f"the per-request argument {STOP!r} only accepts 0, got {extra[STOP]!r}")
             _needs_engine(engine, STOP)
+        if ((engine and extra.get(STOP) != 0 and os.environ.get("XGRAPH_STOP")) or question is not None) and not (
+                isinstance(question, str) and question.strip()):
+            raise ValueError(f"the per-request argument {QUESTION!r} must be the question text")
         opened = _flag(extra, OPEN)
         if opened:
             _needs_engine(engine, OPEN)
@@ -345,6 +351,11 @@ class XGraphLogitsProcessor(_Base):
             req_idx, True, tuple(str(e) for e in extra.get(ANCHOR) or ()),
             str(extra[KG_VERSION]) if extra.get(KG_VERSION) else None, bool(extra.get(OPEN))))
         entry.ended |= bool(earlier and earlier.ended)
+        if on and self._stop and extra.get(STOP) != 0:
+            question = extra.get(QUESTION)
+            if not isinstance(question, str) or not question.strip():
+                raise ValueError(f"residual-goal STOP needs the per-request argument {QUESTION!r}")
+            entry.question = question
         if on and extra.get(PREFILL):
             entry.prefill = str(extra[PREFILL]).encode("utf-8")
             entry.replay_id = extra.get(REPLAY_ID) or None
@@ -362,15 +373,23 @@ class XGraphLogitsProcessor(_Base):
         if self._folded is not None:  # a second round before any step: the first goes now
             self._engine.admit(self._folded, self._stream())
             self._folded = None
-        admissions = []
+        admissions, questions = [], []
         for slot, entry in sorted(self._staged.items()):
             admissions.append(Admission(slot, False) if entry.ended else entry.admission)
             if entry.prefill is not None and not entry.ended:
                 self._prefills[slot] = entry
             else:
                 self._prefills.pop(slot, None)
+            if entry.question is not None and not entry.ended:
+                questions.append((slot, entry.question))
         self._staged.clear()
-        self._folded = self._engine.admission_records(admissions)
+        records = self._engine.admission_records(admissions)
+        if questions:  # a STOP table goes in after its slot's begin: admit now, then install
+            self._engine.admit(records, self._stream())
+            for slot, question in questions:
+                self._engine.set_stop(slot, question, self._stream())
+        else:
+            self._folded = records
 
     def apply(self, logits: Any, ctx: Any) -> Any:
         """Advance every opted-in slot of the step over its newly committed tokens and set the
