@@ -8,8 +8,9 @@ csrc/engine.cu:2057-2074, 2562-2587).  At full size, on every row at every step:
 
 * the apply contract (csrc/engine.cu:2340-2346, 2562-2587): a column keeps its logit bit
   for bit or becomes -inf, nothing else;
-* the number of columns kept equals the allowed count the sampling engine's own mask had
-  at that step (its advance + fill_mask path): two device paths agree everywhere.
+* the whole -inf pattern equals the allowed set of the host seam (tests/seam.py: the same
+  per-row logic compiled by g++ as a sequential library, independent of the CUDA build,
+  itself pinned to the reference's golden walks) advanced over the same tokens.
 
 Against the oracle (oracle/oracle.py, the restatement of src/xgraph/oracle.py), advanced
 over the same tokens: the device state's public projection at every step of the checked
@@ -81,15 +82,17 @@ def oracle_allowed_sets(workload, syntax, options, prefixes: list, workers: int)
 @pytest.mark.parametrize("config, rows, steps, sampled_sets", CASES)
 def test_sync_apply_agrees_with_oracle_at_benchmark_config(config, rows, steps, sampled_sets):
     """GPU-sampled streams replayed through the fused step one token at a time.  Every row at
-    every step: each column keeps its logit bit for bit or becomes -inf, and the state
-    projection equals the oracle's after the same tokens (the oracle advanced over every
-    token of every row); whole allowed sets (the -inf pattern) equal the oracle's at seeded
-    (row, step) samples (every row and step at the toy size), computed on spawned workers."""
+    every step: each column keeps its logit bit for bit or becomes -inf, the -inf pattern is
+    exactly the complement of the host seam's mask after the same tokens, and the state
+    projection equals the oracle's (the oracle advanced over every token of every row);
+    whole allowed sets (the -inf pattern) equal the oracle's at seeded (row, step) samples
+    (every row and step at the toy size), computed on spawned workers."""
     import os
 
     import torch
 
     from oracle.oracle import Oracle
+    from tests.seam import SeamEngine
     from xgraph_b200.engine import Engine
     from xgraph_b200.syntax import SpanSyntax
     from xgraph_b200.synthetic import build_workload, sample_streams
@@ -118,6 +121,10 @@ def test_sync_apply_agrees_with_oracle_at_benchmark_config(config, rows, steps, 
     engine.reset()
     slots = torch.arange(rows, dtype=torch.int32, device="cuda")
     engine.begin(slots)
+    host_tokens = tokens.cpu().numpy()
+    seam = SeamEngine(w.index, w.served, syntax, rows, **options)
+    for r in range(rows):
+        seam.begin(r)
     prompt = torch.zeros(rows, dtype=torch.int32, device="cuda")
     states_at, kept_at = [], {}
     spans = 0
@@ -128,6 +135,13 @@ def test_sync_apply_agrees_with_oracle_at_benchmark_config(config, rows, steps, 
         blocked = torch.isneginf(logits)
         same = logits.view(bits) == source.view(bits)
         assert bool((blocked | same).all()), ("a column is neither its logit nor -inf", k)
+        if k > 0:
+            seam.advance(host_tokens[:, k - 1])
+        seam_allowed = np.unpackbits(seam.masks().view(np.uint8), axis=1, bitorder="little")[:, :vocab]
+        host_blocked = blocked.cpu().numpy()
+        mismatch = np.flatnonzero((host_blocked[:, :vocab] == seam_allowed.astype(bool)).any(axis=1))
+        assert mismatch.size == 0, ("-inf pattern differs from the host seam's mask", config, k, mismatch[:8].tolist())
+        assert host_blocked[:, vocab:].all()
         states = engine.states_host(rows)
         states_at.append(states)
         spans += int((states["phase"] == 1).sum())
@@ -137,7 +151,6 @@ def test_sync_apply_agrees_with_oracle_at_benchmark_config(config, rows, steps, 
     assert engine.errors() == 0 and engine.faults() == 0
     assert spans > rows * steps // 10  # the replay spends real time inside spans
 
-    host_tokens = tokens.cpu().numpy()
     order = sorted(kept_at)
     workers = max(1, min(os.cpu_count() or 1, 8 if config >= 4 else 16, len(order)))
     allowed = oracle_allowed_sets(w, syntax, options, [host_tokens[r, :k] for r, k in order], workers)

@@ -47,6 +47,7 @@ constexpr int32_t kLoadBatch = 4;     // warp_for_loaded: rounds whose loads are
 constexpr int32_t kScratchInts = 2 * kMaxSet + 2 + 2 * kMaxSet + kMaxSet;
 constexpr int32_t kMaxStopWords = 64;    // MAX_STOP_WORDS (src/xgraph/stopping.py:45)
 constexpr int32_t kMaxStopBytes = 4096;  // MAX_STOP_BYTES (src/xgraph/stopping.py:46)
+constexpr int32_t kSparseBlocked = 64;   // blocked tokens an automaton row may list (Tables::sparse)
 constexpr int8_t kReject = -1;
 constexpr int8_t kComplete = -2;
 
@@ -168,6 +169,18 @@ struct Tables {
   const int32_t* stop_rel;    // [slots][relations][3]
   const int32_t* stop_woff;   // [slots][kMaxStopWords + 2]
   const uint8_t* stop_words;  // [slots][kMaxStopBytes]
+  // Derived once per engine from the tables above (the device engine's write planning; the
+  // host seam leaves them empty): rel_any, a mask row holding every relation label token at
+  // any depth and every token of the delimiter lists -- a superset of every mask a state
+  // in a relation segment can have -- and its tokens; and, for the free-text (opener) and
+  // escaped (closer) automaton rows that block few tokens, those tokens: bit p of
+  // free_sparse / esc_sparse says that row p of free_mask / esc_mask has a list, at
+  // sparse[(p or 32 + p) * (1 + kSparseBlocked)]: its count, then its tokens.
+  const uint32_t* rel_any;     // [words_padded]
+  const int32_t* rel_any_tok;  // [rel_any_count]
+  int32_t rel_any_count;
+  const int32_t* sparse;       // [64][1 + kSparseBlocked]
+  uint32_t free_sparse, esc_sparse;
   // per-slot engine buffers
   XgState* states;
   int32_t* memory;
@@ -390,7 +403,51 @@ XG_COLD int32_t top_unique(const Warp& w, Key* buf, int32_t n, int32_t limit, bo
 #endif
 }
 
+// The buffer's keys reduced to what the mode keeps, ascending, at most kMaxSet of them.  On
+// the device the warp holds the (at most kTopCap) keys in registers, kTopCap / 32 per lane,
+// and extracts the least key kMaxSet times (a lane minimum, then a shuffle reduction),
+// dropping after each extraction every key equal to it (DISTINCT) or of the same entity
+// (ENTITY: the entity's least rank is the first of its keys to be extracted).  That is the
+// same function as sorting, keeping the first of each run and truncating, in ~64 short
+// rounds of register work instead of two shared-memory bitonic sorts of the whole buffer
+// (whose code, rarely run, also came from memory line by line: ~45 us per compaction).
 XG_COLD void top_compact(const Warp& w, TopSet& ts, int32_t mode) {
+#if XG_GPU
+  constexpr int32_t per = kTopCap / 32;
+  Key k[per];
+#pragma unroll
+  for (int32_t j = 0; j < per; ++j) {
+    const int32_t i = 32 * j + w.lane;
+    k[j] = i < ts.n ? ts.buf[i] : max_key();
+  }
+  __syncwarp();
+  int32_t out = 0;
+  #pragma unroll 1
+  for (; out < kMaxSet; ++out) {
+    Key m = k[0];
+#pragma unroll
+    for (int32_t j = 1; j < per; ++j)
+      if (key_less(k[j], m)) m = k[j];
+#pragma unroll
+    for (int32_t d = 16; d > 0; d >>= 1) {
+      Key o;
+      o.a = __shfl_xor_sync(0xffffffffu, m.a, d);
+      o.b = __shfl_xor_sync(0xffffffffu, m.b, d);
+      o.pad = __shfl_xor_sync(0xffffffffu, m.pad, d);
+      if (key_less(o, m)) m = o;
+    }
+    if (is_max(m)) break;  // (warp-uniform)
+    if (w.lane == 0) ts.buf[out] = m;
+#pragma unroll
+    for (int32_t j = 0; j < per; ++j) {
+      const bool same = mode == kEntity ? !is_max(k[j]) && static_cast<uint32_t>(k[j].a) == static_cast<uint32_t>(m.a)
+                                        : key_eq(k[j], m);
+      if (same) k[j] = max_key();
+    }
+  }
+  ts.n = out;
+  __syncwarp();
+#else
   if (mode == kEntity) {
     // (rank, row) -> (row, rank): the least rank of each entity comes first.
     warp_for(w, 0, ts.n, [&](int32_t i) {
@@ -410,6 +467,7 @@ XG_COLD void top_compact(const Warp& w, TopSet& ts, int32_t mode) {
     ts.n = top_unique(w, ts.buf, ts.n, kMaxSet, false);
   }
   warp_sync();
+#endif
 }
 
 // Offer one key per lane (valid lanes only); all lanes call it together.

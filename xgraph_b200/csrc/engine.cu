@@ -257,6 +257,46 @@ __device__ __forceinline__ void bulk_drain() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
+// Free-text and escaped rows of the automata that block few tokens (most allow every
+// token): the row's entry in Tables::sparse, or null (pointer arithmetic, no loads).
+__device__ __forceinline__ const int32_t* sparse_row(const Tables& t, const uint32_t* base) {
+  const int64_t stride = t.words_padded;  // (a bit is set only for a row the automaton has)
+  if (base >= t.free_mask && base < t.free_mask + 32 * stride) {
+    const int64_t at = base - t.free_mask;
+    if (at % stride == 0 && ((t.free_sparse >> (at / stride)) & 1u)) return t.sparse + (at / stride) * (1 + kSparseBlocked);
+  }
+  if (base >= t.esc_mask && base < t.esc_mask + 32 * stride) {
+    const int64_t at = base - t.esc_mask;
+    if (at % stride == 0 && ((t.esc_sparse >> (at / stride)) & 1u))
+      return t.sparse + (32 + at / stride) * (1 + kSparseBlocked);
+  }
+  return nullptr;
+}
+
+// Whole CTA: -inf into a sparse row's listed tokens below `cols` (when listed_here), then
+// into columns [c0, c1) past the vocabulary.
+template <int ELT>
+__device__ __forceinline__ void apply_sparse(const Tables& t, char* out, int32_t cols, const int32_t* list,
+                                             uint32_t neg, bool listed_here, int64_t c0, int64_t c1) {
+  if (listed_here) {
+    const int32_t n = list[0];
+    for (int32_t k = threadIdx.x; k < n; k += blockDim.x) {
+      const int32_t token = list[1 + k];
+      if (token >= cols) continue;
+      if (ELT == 2)
+        *reinterpret_cast<uint16_t*>(out + 2 * static_cast<int64_t>(token)) = static_cast<uint16_t>(neg);
+      else
+        *reinterpret_cast<uint32_t*>(out + 4 * static_cast<int64_t>(token)) = neg;
+    }
+  }
+  for (int64_t col = (c0 > t.vocab ? c0 : t.vocab) + threadIdx.x; col < c1; col += blockDim.x) {
+    if (ELT == 2)
+      *reinterpret_cast<uint16_t*>(out + 2 * col) = static_cast<uint16_t>(neg);
+    else
+      *reinterpret_cast<uint32_t*>(out + 4 * col) = neg;
+  }
+}
+
 // -inf into the disallowed columns of segments [s0, s1) (1024 columns each) of one
 // logits row whose first element is 16-byte aligned; the calling warps split them.
 //
@@ -269,6 +309,15 @@ __device__ __forceinline__ void bulk_drain() {
 // segment, leaving the SM's load/store pipe to the partial segments.  A warp issues the
 // loads of kApplyBatch segments before any of their stores (the stores may alias nothing
 // the compiler can prove, so it would not hoist the loads itself).
+//
+// A segment whose allowed and blocked columns interleave densely (a label-root mask: about
+// half the vocabulary allowed, scattered) is written column-contiguously instead: in round
+// r lane l takes column 32 r + l, so each predicated element store of the warp lands in
+// one 128-byte line (64 bytes of bf16) rather than spreading 2-byte pieces over four; the
+// L2 request count, which bounds such a row from one SM, falls fourfold, and no logit is
+// read.
+constexpr int32_t kDenseShare = 4;  // dense: at least 1/4 of its 8-column groups partly blocked
+
 template <int ELT>
 __device__ __forceinline__ void apply_segments(const Tables& t, char* out, int32_t cols, const uint32_t* base,
                                                const uint32_t* delta, uint32_t neg, int32_t s0, int32_t s1,
@@ -297,6 +346,28 @@ __device__ __forceinline__ void apply_segments(const Tables& t, char* out, int32
         continue;
       }
 #endif
+      if ((seg + 1) * 1024 <= cols) {
+        int32_t partial = 0;  // this lane's 8-column groups that are neither all allowed nor all blocked
+#pragma unroll
+        for (int32_t k = 0; k < 4; ++k) {
+          const uint32_t byte = (word[b] >> (8 * k)) & 0xffu;
+          partial += byte != 0u && byte != 0xffu;
+        }
+        if (__reduce_add_sync(0xffffffffu, partial) * kDenseShare >= 128) {
+          char* at = out + (static_cast<int64_t>(seg) * 1024 + lane) * ELT;
+#pragma unroll 4
+          for (int32_t r = 0; r < 32; ++r) {
+            const uint32_t w = __shfl_sync(0xffffffffu, word[b], r);
+            if (!((w >> lane) & 1u)) {
+              if (ELT == 2)
+                *reinterpret_cast<uint16_t*>(at + 64 * r) = static_cast<uint16_t>(neg);
+              else
+                *reinterpret_cast<uint32_t*>(at + 128 * r) = neg;
+            }
+          }
+          continue;
+        }
+      }
 #pragma unroll
       for (int32_t j = 0; j < 4; ++j) {
         const int32_t g = 32 * j + lane;
@@ -728,6 +799,10 @@ __global__ void __launch_bounds__(kApplyThreads, 4)
     apply_scalar<ELT>(t, out, c0, c0 + per < cols ? c0 + per : cols, base, delta, neg);
     return;
   }
+  if (const int32_t* list = delta == nullptr ? sparse_row(t, base) : nullptr) {  // few blocked tokens
+    apply_sparse<ELT>(t, out, cols, list, neg, chunk == 0, chunk == 0 ? 0 : cols, cols);
+    return;
+  }
   const int32_t segments = (cols + 1023) >> 10;
   const int32_t share = (segments + chunks - 1) / chunks;
   const int32_t s0 = chunk * share;
@@ -829,6 +904,7 @@ __global__ void __maxnreg__(kFusedRegisters)
   __shared__ int32_t edit_count;
   __shared__ int32_t delim0[kDelimCopy];                // tokens that start each delimiter
   __shared__ __align__(128) uint32_t blocked_run[kBlockedRunWords];
+  __shared__ int32_t prewritten;                        // the row's columns outside rel_any were written early
   extern __shared__ __align__(16) uint32_t composed[];  // [words_padded]: a delta built this step
   const int32_t i = blockIdx.x;
   const int32_t slot = f.a.slots[i];
@@ -876,6 +952,64 @@ __global__ void __maxnreg__(kFusedRegisters)
                            : k < c0 + c1 ? t.separator.tok[t.separator.at[0] + k - c0]
                                          : t.escape.tok[t.escape.at[0] + k - c0 - c1];
     }
+    // Early writes.  Some rows' next mask is known, before the state machine runs, to lie
+    // inside rel_any, every relation label token and delimiter token (~100 columns of a
+    // 128 K vocabulary): every column outside it is -inf whatever the state machine finds,
+    // and these warps write those columns now, while warp 0 runs the row's transitions (for
+    // a relation label the longest: the next path frontier) and while the memory system is
+    // still quiet; after the mask only rel_any's own columns remain.  With one new token and
+    // no admission, that is (a) a relation-segment row whose token continues no delimiter
+    // and is allowed by the slot's recorded mask: the token only narrows the relation label
+    // (advance_span neither closes, separates, escapes nor errs), so the row stays in its
+    // relation segment; (b) a subject (or path relation) row whose token completes the
+    // separator and not the closer: next_segment moves it into a relation segment.  (A row
+    // opening a span is not written early: its label-root mask leaves ~half the vocabulary
+    // scattered, whose partial-line stores took ~23 us however early they started.)
+    // Not with release, whose mass pass reads the row first.  The last warp decides, reading
+    // the slot's state, cursor and recorded mask before it arrives at barrier 1: warp 0
+    // writes none of them before that barrier (an admitted row, whose admission warp 0
+    // applies earlier, is never written early).
+    if (threadIdx.x >= blockDim.x - 32) {
+      bool early_write = false;
+      char* out_row = f.logits + static_cast<int64_t>(i) * f.stride * ELT;
+      if (was_on && !t.release_on && t.dstep != nullptr && t.rel_any_count > 0 &&
+          (reinterpret_cast<uintptr_t>(out_row) & 15u) == 0) {
+        const int32_t lane = threadIdx.x & 31;
+        const XgState* stored = t.states + slot;
+        const int32_t phase = stored->phase, segment = stored->segment, answered = stored->answer_complete;
+        const int32_t flags = stored->flags, close_pos = stored->close_pos, sep_pos = stored->sep_pos;
+        const int32_t recorded = t.cursors[slot], first = f.a.prompt_len[slot], last = f.a.total_len[slot];
+        const uint32_t* base0 = t.base[slot];
+        const uint32_t* delta0 = t.delta[slot];
+        bool admitted = false;
+#pragma unroll 1
+        for (int32_t at = 0; at < f.admit_count; at += 32)
+          admitted |= __any_sync(0xffffffffu, at + lane < f.admit_count && f.admit[at + lane].slot == slot);
+        const int32_t cursor0 = recorded < 0 ? first : recorded;
+        if (!admitted && !answered && cursor0 + 1 == last) {
+          const int32_t token = f.a.history[f.a.stride * slot + cursor0];
+          if (token >= 0 && token < t.vocab && phase == kSpan) {
+            const uint64_t packed = t.dstep[token];
+            // delim_next over the packed word: the next byte position of delimiter branch
+            // `offset + at`, or -1 (advance_span's reads, in its order)
+            auto next = [&](int32_t offset, int32_t at) {
+              const int32_t n = static_cast<int32_t>((packed >> (4 * (offset + at))) & 15u);
+              return n ? n : -1;
+            };
+            const int32_t close = close_pos > 0 ? next(0, close_pos) : (flags & kMayClose) ? next(0, 0) : -1;
+            const int32_t sep = sep_pos > 0 && !(flags & kStop) ? next(t.closer.len, sep_pos)
+                                : (flags & kMaySep) ? next(t.closer.len, 0) : -1;
+            if (segment == kRelation && packed == 0u &&
+                ((mask_word(base0, delta0, token >> 5) >> (token & 31)) & 1u))
+              early_write = true;
+            else if ((segment == kSubject || (segment == kRelation && t.paths)) && close != t.closer.len &&
+                     sep == t.separator.len)
+              early_write = true;
+          }
+        }
+      }
+      if (threadIdx.x == blockDim.x - 32) prewritten = early_write;
+    }
     __syncwarp();
     asm volatile("bar.arrive 1, %0;" ::"r"(blockDim.x) : "memory");
     // Release reads the whole logits row of a span row.  For a row that was in a span
@@ -916,6 +1050,12 @@ __global__ void __maxnreg__(kFusedRegisters)
         }
       }
     }
+    // warps 1..7 only: the -inf run is filled and the early-write decision made
+    asm volatile("bar.sync 2, %0;" ::"r"(blockDim.x - 32) : "memory");
+    if (prewritten) {
+      apply_segments<ELT>(t, f.logits + static_cast<int64_t>(i) * f.stride * ELT, f.cols, t.rel_any, nullptr, f.neg, 0,
+                          (f.cols + 1023) >> 10, (threadIdx.x >> 5) - 1, (blockDim.x >> 5) - 1, blocked_run);
+    }
     if (early) {
       uint8_t* ring = reinterpret_cast<uint8_t*>(composed + t.words_padded) + threadIdx.x * kRingBytes;
       const RowMass m = warp_mass(thread_mass<ELT, false>(t, row, served, nullptr, nullptr, f16, threadIdx.x - 32,
@@ -942,9 +1082,13 @@ __global__ void __maxnreg__(kFusedRegisters)
       }
       changed = true;
     }
-    if (changed) store_state(t, slot, s);
     __syncwarp();
     asm volatile("bar.sync 1, %0;" ::"r"(blockDim.x) : "memory");
+    // (the slot's state, cursor and mask pointers are written only after barrier 1: the
+    // early-write decision reads them before it)
+    if (changed) store_state(t, slot, s);
+    if (prewritten && !(s.phase == kSpan && s.segment == kRelation) && threadIdx.x == 0)
+      atomicOr(f.faults, 4);  // an early-written row left the relation segment (never expected)
     if (!on) {
       if (threadIdx.x == 0) use = MaskRef{nullptr, nullptr};  // inactive: untouched
     } else if (changed) {
@@ -1033,11 +1177,24 @@ __global__ void __maxnreg__(kFusedRegisters)
   }
   if (base != nullptr || delta != nullptr) {  // else inactive or error phase: untouched
     char* out = f.logits + static_cast<int64_t>(i) * f.stride * ELT;
-    if ((reinterpret_cast<uintptr_t>(out) & 15u) != 0)
+    if ((reinterpret_cast<uintptr_t>(out) & 15u) != 0) {
       apply_scalar<ELT>(t, out, 0, f.cols, base, delta, f.neg);
-    else
+    } else if (prewritten) {  // the columns outside rel_any are -inf already: its own tokens remain
+      for (int32_t k = threadIdx.x; k < t.rel_any_count; k += blockDim.x) {
+        const int32_t token = t.rel_any_tok[k];
+        if (token < f.cols && !((mask_word(base, delta, token >> 5) >> (token & 31)) & 1u)) {
+          if (ELT == 2)
+            *reinterpret_cast<uint16_t*>(out + 2 * static_cast<int64_t>(token)) = static_cast<uint16_t>(f.neg);
+          else
+            *reinterpret_cast<uint32_t*>(out + 4 * static_cast<int64_t>(token)) = f.neg;
+        }
+      }
+    } else if (const int32_t* list = delta == nullptr ? sparse_row(t, base) : nullptr) {  // few blocked tokens
+      apply_sparse<ELT>(t, out, f.cols, list, f.neg, true, 0, f.cols);
+    } else {
       apply_segments<ELT>(t, out, f.cols, base, delta, f.neg, 0, (f.cols + 1023) >> 10, threadIdx.x >> 5,
                           blockDim.x >> 5, blocked_run);
+    }
   }
   // admissions whose slot is not a row of this step (CTA i takes i, i + grid, ...)
   if (threadIdx.x < 32) {
@@ -1146,6 +1303,59 @@ __global__ void __launch_bounds__(kFusedThreads)
                       nullptr);
 }
 
+// Engine set-up, one CTA: the write planning tables derived from the packed ones
+// (Tables::rel_any, rel_any_tok, sparse, free_sparse, esc_sparse).  rel_any and out[0..2]
+// arrive zeroed; out[0] = how many tokens rel_any holds, out[1] / out[2] = the free /
+// escaped rows that have a sparse list.
+__global__ void __launch_bounds__(1024) derive_kernel(const __grid_constant__ Tables t, uint32_t* rel_any,
+                                                      int32_t* rel_any_tok, int32_t* sparse, int32_t* out,
+                                                      int32_t free_rows, int32_t esc_rows) {
+  __shared__ int32_t blocked;
+  auto mark = [&](uint32_t* row, int32_t token) {
+    if (token >= 0 && token < t.vocab) atomicOr(row + (token >> 5), 1u << (token & 31));
+  };
+  const int32_t relation_tokens = t.rel.off[t.rel.count];
+  for (int32_t k = threadIdx.x; k < relation_tokens; k += blockDim.x) mark(rel_any, t.rel.tok[k]);
+  for (const Delim* d : {&t.closer, &t.separator, &t.escape}) {
+    const int32_t n = d->off[d->len];
+    for (int32_t k = threadIdx.x; k < n; k += blockDim.x) mark(rel_any, d->tok[k]);
+  }
+  __syncthreads();
+  for (int32_t w = threadIdx.x; w < t.words; w += blockDim.x) {
+    for (uint32_t bits = rel_any[w]; bits; bits &= bits - 1u) rel_any_tok[atomicAdd(out, 1)] = 32 * w + __ffs(bits) - 1;
+  }
+  const uint32_t last = (t.vocab & 31) ? (1u << (t.vocab & 31)) - 1u : ~0u;  // the last word's vocabulary bits
+  for (int32_t which = 0; which < 2; ++which) {
+    const uint32_t* rows = which == 0 ? t.free_mask : t.esc_mask;
+    const int32_t count = min(which == 0 ? free_rows : esc_rows, 32);
+    for (int32_t p = 0; p < count; ++p) {
+      const uint32_t* row = rows + static_cast<int64_t>(p) * t.words_padded;
+      int32_t* list = sparse + (32 * which + p) * (1 + kSparseBlocked);
+      if (threadIdx.x == 0) blocked = 0;
+      __syncthreads();
+      int32_t mine = 0;
+      for (int32_t w = threadIdx.x; w < t.words; w += blockDim.x)
+        mine += __popc(~row[w] & (w + 1 < t.words ? ~0u : last));
+      atomicAdd(&blocked, mine);
+      __syncthreads();
+      const int32_t total = blocked;
+      __syncthreads();
+      if (total > kSparseBlocked) continue;  // (block-uniform)
+      if (threadIdx.x == 0) blocked = 0;
+      __syncthreads();
+      for (int32_t w = threadIdx.x; w < t.words; w += blockDim.x) {
+        for (uint32_t bits = ~row[w] & (w + 1 < t.words ? ~0u : last); bits; bits &= bits - 1u)
+          list[1 + atomicAdd(&blocked, 1)] = 32 * w + __ffs(bits) - 1;
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        list[0] = total;
+        out[1 + which] |= 1 << p;
+      }
+    }
+  }
+}
+
 }  // namespace xg
 
 // Scratch of xg_apply_mask_noalloc: one array in this library's device image per device,
@@ -1201,6 +1411,9 @@ struct XgEngine {
   int32_t* faults = nullptr;      // device-side faults (xg_faults)
   XgAdmission* admissions = nullptr;  // staging of host admissions: max_sequences entries
   size_t composed_bytes = 0;      // sync_apply's dynamic shared memory: one mask row
+  uint32_t* rel_any = nullptr;    // derived tables (derive_kernel): relation-segment superset mask,
+  int32_t* rel_any_tok = nullptr; //   its tokens,
+  int32_t* sparse = nullptr;      //   and the automaton rows' blocked-token lists
   // residual-goal STOP (xg_enable_stop): label words, and per slot: installed flag, relation
   // table, question word offsets and bytes
   int64_t* stop_label_off = nullptr;
@@ -1508,6 +1721,9 @@ void release(XgEngine* e) {
   cudaFree(e->stop_woff);
   cudaFree(e->stop_words);
   cudaFree(e->admissions);
+  cudaFree(e->rel_any);
+  cudaFree(e->rel_any_tok);
+  cudaFree(e->sparse);
   for (void* p : {static_cast<void*>(e->arena.range), static_cast<void*>(e->arena.subjects),
                   static_cast<void*>(e->arena.adjacency), static_cast<void*>(e->arena.relations),
                   static_cast<void*>(e->arena.objects)})
@@ -1551,6 +1767,8 @@ int load_blob_versions(XgEngine* e, const void* host_blob) {
   }
   return rebuild_versions(e, l.versions, subjects + 1, edges, nullptr);
 }
+
+int derive_tables(XgEngine* e);
 
 int create(const void* blob, bool on_device, const XgLayout* layout, const XgOptions* options,
            int32_t max_sequences, XgEngine** out) {
@@ -1629,6 +1847,10 @@ int create(const void* blob, bool on_device, const XgLayout* layout, const XgOpt
       return rc;
     }
   }
+  if (int rc = derive_tables(e)) {
+    release(e);
+    return rc;
+  }
   begin_kernel<<<static_cast<unsigned>((slots + 127) / 128), 128>>>(e->t, nullptr, max_sequences, 0, max_sequences);
   err = cudaGetLastError();
   if (err == cudaSuccess) err = cudaDeviceSynchronize();
@@ -1637,6 +1859,39 @@ int create(const void* blob, bool on_device, const XgLayout* layout, const XgOpt
     return cuda_fail(err, "engine initialization");
   }
   *out = e;
+  return XG_OK;
+}
+
+// The derived write-planning tables (derive_kernel), once per engine.
+int derive_tables(XgEngine* e) {
+  const int32_t wp = e->layout.words_padded, vocab = e->layout.vocab;
+  cudaError_t err = cudaMalloc(reinterpret_cast<void**>(&e->rel_any), static_cast<size_t>(wp) * sizeof(uint32_t));
+  if (err == cudaSuccess)
+    err = cudaMalloc(reinterpret_cast<void**>(&e->rel_any_tok), static_cast<size_t>(vocab > 0 ? vocab : 1) * sizeof(int32_t));
+  if (err == cudaSuccess) err = cudaMalloc(reinterpret_cast<void**>(&e->sparse), 64 * (1 + kSparseBlocked) * sizeof(int32_t));
+  if (err != cudaSuccess) {
+    cudaGetLastError();
+    return fail(XG_ENOMEM, std::string("device allocation failed: ") + cudaGetErrorString(err));
+  }
+  int32_t* scratch = nullptr;  // the kernel's three results
+  err = cudaMalloc(reinterpret_cast<void**>(&scratch), 3 * sizeof(int32_t));
+  if (err == cudaSuccess) err = cudaMemset(scratch, 0, 3 * sizeof(int32_t));
+  if (err == cudaSuccess) err = cudaMemset(e->rel_any, 0, static_cast<size_t>(wp) * sizeof(uint32_t));
+  if (err == cudaSuccess) {
+    derive_kernel<<<1, 1024>>>(e->t, e->rel_any, e->rel_any_tok, e->sparse, scratch, e->layout.opener_len,
+                               e->layout.closer_len);
+    err = cudaGetLastError();
+  }
+  int32_t host[3] = {0, 0, 0};
+  if (err == cudaSuccess) err = cudaMemcpy(host, scratch, sizeof(host), cudaMemcpyDeviceToHost);
+  cudaFree(scratch);
+  if (err != cudaSuccess) return cuda_fail(err, "engine set-up (derived tables)");
+  e->t.rel_any = e->rel_any;
+  e->t.rel_any_tok = e->rel_any_tok;
+  e->t.rel_any_count = host[0];
+  e->t.sparse = e->sparse;
+  e->t.free_sparse = static_cast<uint32_t>(host[1]);
+  e->t.esc_sparse = static_cast<uint32_t>(host[2]);
   return XG_OK;
 }
 
