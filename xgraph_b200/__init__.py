@@ -25,6 +25,8 @@ _EXPORTS = {
     "build_kg_versions": "kgversions",
     "ServedTokenizer": "tokenizer",
     "SpanSyntax": "syntax",
+    "MatchedExecutor": "programs",
+    "MatchedPath": "programs",
 }
 __all__ = list(_EXPORTS)
 

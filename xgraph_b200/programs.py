@@ -1,0 +1,265 @@
+"""Offline execution of written paths on the GPU: the reference's MatchedExecutor
+(src/xgraph/programs.py:328-1130), path mode with committed paths run after decoding.
+
+A path written without the engine, `start · r1 · ... · rk` (parsed from a model's output),
+executes as path mode would have executed it: labels read as the label index's rows, a
+relation label or alias following every relation it names, starts in best-connected order
+capped at 64, each frontier capped at 64 by start rank and first label row, the path
+resolving to the entities of the least start rank present, and the answer the best
+connected of the entities the answer span after the path may name (the first 64 label rows
+of those entities).
+
+Here the engine itself executes them: each path becomes the token stream of its span
+(`⟦ start · r1 · ... · rk⟧`, each piece encoded on its own as the reference's `_rows`
+reads a label: the label prefix and the text), one slot per path reading the path's KG
+version, and a whole batch runs as one sync launch up to the last relation label and one
+more for the closer.  The slot's memory then holds, from set_flags' separator test, the
+capped next frontier with its start ranks (the path's last frontier), and after the closer
+the reached label rows.  Only the final ordering (best-connected order: most sitelinks
+with the sitelink rank, then most adjacency entries in the path's version, then first
+label row) and the id lookups run on the host.  A path the engine would not have let be
+written (a start naming nothing with triples, a relation the frontier lacks, a label cut
+short) leaves its slot in the error phase and executes to nothing, as the reference's
+executor returns for it.
+
+Not served (refused by name): anchors, the offline repairs (`repair`, `strip_quotes`),
+and the observation / menu / audit settings.
+"""
+
+from __future__ import annotations
+
+from collections.abc import Iterable, Sequence
+from dataclasses import dataclass
+
+import numpy as np
+
+MAX_PATH_RELATIONS = 8  # src/xgraph/oracle.py:177
+MAX_REACHED = 64        # src/xgraph/oracle.py:172-175
+
+# slot memory (int32 words per slot; xgraph_b200/csrc/core.cuh, MemoryField)
+_MEM_REACHED, _MEM_FRONTIER = 1, 2
+_MEM_PENDING_LO, _MEM_PENDING_HI, _MEM_PENDING_COUNT = 4, 5, 6
+_MEM_REACHED_ROWS = 8 + 3 * MAX_REACHED
+_MEM_FRONTIER_ENT = _MEM_REACHED_ROWS + MAX_REACHED
+_MEM_FRONTIER_RANK = _MEM_FRONTIER_ENT + MAX_REACHED
+_MEM_PENDING_RANK = _MEM_FRONTIER_RANK + MAX_REACHED
+_MEM_PENDING_FIRST = _MEM_PENDING_RANK + MAX_REACHED
+
+_PHASE_ERROR = 3
+_ENTITY_SPAN, _PATH_SPAN = 2, 4
+
+_NOT_SERVED = {"strip_quotes": False, "observe_required": False, "observe_no_loop": False,
+               "observe_defer": 0, "menu_close_next": False}
+
+
+@dataclass(frozen=True)
+class MatchedPath:
+    """A written path as path mode's committed paths resolve it (the reference's
+    MatchedPath, src/xgraph/programs.py:328-366): the entities reached, best-connected
+    first (empty where the engine would not have let the path be written), the answer
+    delivered, and the plan (the start and relation labels path mode would write), None
+    where the path reaches nothing or names no relation."""
+
+    reached: tuple[str, ...]
+    answer: str | None
+    plan: tuple[str, ...] | None = None
+    stripped: bool = False
+
+    @property
+    def recorded_plan(self) -> dict | None:
+        if self.plan is None:
+            return None
+        return {"start": self.plan[0], "relations": list(self.plan[1:])}
+
+
+class MatchedExecutor:
+    """Parse-then-execute matched to path mode with committed paths (the reference's
+    MatchedExecutor, src/xgraph/programs.py:368-440: same constructor keywords, `execute`
+    signature and results), executed on the GPU by the engine; `execute_many` runs a whole
+    batch of paths in two kernel launches.  `max_paths` is the batch the engine is sized
+    for (larger batches run in pieces)."""
+
+    def __init__(self, index, tokenizer, *, versions=None, start_rank: str = "degree",
+                 unquoted_starts: bool = False, committed_paths: bool = True, max_paths: int = 256,
+                 **others) -> None:
+        from .engine import Engine
+        from .index import IndexMismatch
+
+        if index.tokenizer_fingerprint != tokenizer.fingerprint:
+            raise IndexMismatch("the KG index was built for another tokenizer")
+        for name, value in others.items():
+            if name not in _NOT_SERVED:
+                raise TypeError(f"MatchedExecutor() got an unexpected keyword argument {name!r}")
+            if value != _NOT_SERVED[name]:
+                raise ValueError(f"the {name} setting is not served by this executor")
+        if max_paths < 1:
+            raise ValueError(f"max_paths must be at least 1, got {max_paths}")
+        self._index, self._tokenizer, self._versions = index, tokenizer, versions
+        self._syntax = index.span_syntax
+        self._engine = Engine(index, tokenizer, self._syntax, max_paths, paths=True,
+                              committed_paths=committed_paths, versions=versions, start_rank=start_rank,
+                              unquoted_starts=unquoted_starts)
+        self._sitelinks = index.sitelinks if start_rank == "sitelinks" else None
+        self._pieces: dict[str, list[int]] = {}
+        self._first: np.ndarray | None = None
+
+    # -- host pieces ---------------------------------------------------------------------
+
+    def _encode(self, text: str) -> list[int]:
+        tokens = self._pieces.get(text)
+        if tokens is None:
+            tokens = self._pieces[text] = list(self._tokenizer.encode(text))
+        return tokens
+
+    def _label(self, text: str) -> list[int] | None:
+        """The tokens of a label as written (the label prefix, then the text), None for a
+        blank label (one the reference's executor reads as naming nothing)."""
+        if not text.strip():
+            return None
+        return self._encode(self._syntax.label_prefix + text) or None
+
+    def _stream(self, start: str, relations: Sequence[str]) -> tuple[list[int], int] | None:
+        """The span's tokens and how many come before the closer, or None where a label
+        is blank."""
+        tokens = list(self._encode(self._syntax.opener))
+        label = self._label(start)
+        if label is None:
+            return None
+        tokens += label
+        for written in relations:
+            label = self._label(written)
+            if label is None:
+                return None
+            tokens += self._encode(self._syntax.separator) + label
+        return tokens + self._encode(self._syntax.closer), len(tokens)
+
+    def _order(self, view, pairs: Iterable[tuple[int, int]]) -> list[int]:
+        """The entities of these (entity, label row) pairs in best-connected order."""
+        sitelinks = self._sitelinks
+
+        def key(pair: tuple[int, int]) -> tuple[int, int, int]:
+            entity, row = pair
+            linked = int(sitelinks[entity]) if sitelinks is not None else 0
+            return (-linked, -len(view.edges_at(entity)[0]), row)
+
+        return list(dict.fromkeys(entity for entity, _ in sorted(pairs, key=key)))
+
+    def _first_rows(self) -> np.ndarray:
+        """Each entity's first label row."""
+        if self._first is None:
+            owners = np.asarray(self._index.labels.owners, dtype=np.int64)
+            first = np.full(len(self._index.labels.owner_ids), np.iinfo(np.int64).max, dtype=np.int64)
+            np.minimum.at(first, owners, np.arange(len(owners), dtype=np.int64))
+            self._first = first
+        return self._first
+
+    def _last_hop(self, view, memory: np.ndarray, lo: int, hi: int) -> list[tuple[int, int]]:
+        """(entity, start rank) of the path's last frontier computed from the frontier before
+        it and the last relation's label rows [lo, hi) -- only for a path of the full eight
+        relations, where the engine's separator test (and so its cached next frontier) does
+        not run: the objects under every relation the label names, each with the least rank
+        it is reached from, kept to 64 by (rank, first label row)."""
+        index = self._index
+        follow = sorted({int(index.relations.owners[r]) for r in range(lo, hi)})
+        owners, first = index.labels.owners, self._first_rows()
+        reached: dict[int, int] = {}
+        count = int(memory[_MEM_FRONTIER])
+        for k in range(min(count, MAX_REACHED)):
+            entity, rank = int(memory[_MEM_FRONTIER_ENT + k]), int(memory[_MEM_FRONTIER_RANK + k])
+            relation_of, object_of = view.edges_at(entity)
+            for row in np.asarray(object_of)[np.isin(relation_of, follow)].tolist():
+                item = int(owners[row])
+                reached[item] = min(reached.get(item, rank), rank)
+        kept = sorted(reached, key=lambda e: (reached[e], int(first[e])))[:MAX_REACHED]
+        return [(e, reached[e]) for e in kept]
+
+    # -- execution -----------------------------------------------------------------------
+
+    def execute(self, start: str, relations: list[str], anchor: list[str] | None = None,
+                version: str | None = None, repair: bool = False) -> MatchedPath:
+        """The path from the start label along the relation labels (see the class)."""
+        return self.execute_many([(start, relations, version)], anchor=anchor, repair=repair)[0]
+
+    def execute_many(self, paths: Iterable[tuple[str, Sequence[str], str | None]], *,
+                     anchor=None, repair: bool = False) -> list[MatchedPath]:
+        """Each (start, relations, version) path executed, in order."""
+        if anchor is not None:
+            raise ValueError("anchored execution is not served by this executor")
+        if repair:
+            raise ValueError("the offline relation repair is not served by this executor")
+        paths = [(start, list(relations)[:MAX_PATH_RELATIONS], version) for start, relations, version in paths]
+        for _, _, version in paths:
+            self._engine.view(version)  # an unknown version name raises here, before any launch
+        out: list[MatchedPath] = []
+        size = self._engine.max_sequences
+        for at in range(0, len(paths), size):
+            out += self._batch(paths[at: at + size])
+        return out
+
+    def _batch(self, paths) -> list[MatchedPath]:
+        import torch
+
+        from .engine import Admission
+
+        engine, index = self._engine, self._index
+        n, size = len(paths), engine.max_sequences
+        streams = [self._stream(start, relations) for start, relations, _ in paths]
+        width = max([len(s[0]) for s in streams if s is not None] + [1])
+        history = np.zeros((size, width), dtype=np.int32)
+        before = np.zeros(size, dtype=np.int32)
+        total = np.zeros(size, dtype=np.int32)
+        for k, stream in enumerate(streams):
+            if stream is not None:
+                history[k, : len(stream[0])] = stream[0]
+                before[k], total[k] = stream[1], len(stream[0])
+        device = torch.device("cuda", torch.cuda.current_device())
+        engine.reset()
+        engine.admit([Admission(k, True, version=paths[k][2]) for k in range(n)])
+        slots = torch.arange(n, dtype=torch.int32, device=device)
+        history_d = torch.from_numpy(history).to(device)
+        prompt = torch.zeros(size, dtype=torch.int32, device=device)
+        engine.sync(slots, history_d, prompt, torch.from_numpy(before).to(device))
+        states_a, memory_a = engine.states_host(n), engine.memory_host(n)
+        engine.sync(slots, history_d, prompt, torch.from_numpy(total).to(device))
+        states_b, memory_b = engine.states_host(n), engine.memory_host(n)
+        owners, ids = index.labels.owners, index.labels.owner_ids
+
+        results = []
+        for k, (start, relations, version) in enumerate(paths):
+            empty = MatchedPath((), None, None)
+            if streams[k] is None or int(states_b["phase"][k]) == _PHASE_ERROR:
+                results.append(empty)
+                continue
+            view = engine.view(version)
+            kind = int(states_b["last_kind"][k])
+            if not relations:  # an entity span: every entity its label names
+                if kind != _ENTITY_SPAN:
+                    results.append(empty)
+                    continue
+                lo, hi = int(states_b["last_lo"][k]), int(states_b["last_hi"][k])
+                starts = self._order(view, [(int(owners[r]), r) for r in range(lo, hi)])
+                results.append(MatchedPath(tuple(ids[e] for e in starts), ids[starts[0]] if starts else None, None))
+                continue
+            if kind != _PATH_SPAN:
+                results.append(empty)
+                continue
+            memory = memory_a[k]
+            lo, hi = int(states_a["lo"][k]), int(states_a["ex_hi"][k])
+            if int(memory[_MEM_PENDING_LO]) == lo and int(memory[_MEM_PENDING_HI]) == hi:
+                count = int(memory[_MEM_PENDING_COUNT])
+                frontier = [(int(owners[int(memory[_MEM_PENDING_FIRST + i])]), int(memory[_MEM_PENDING_RANK + i]))
+                            for i in range(count)]
+            else:  # the eighth relation: no separator test ran
+                frontier = self._last_hop(view, memory, lo, hi)
+            if not frontier:
+                results.append(empty)
+                continue
+            best = min(rank for _, rank in frontier)
+            final = list(dict.fromkeys(e for e, rank in frontier if rank == best))
+            first = self._first_rows()
+            entities = self._order(view, [(e, int(first[e])) for e in final])
+            rows = memory_b[k][_MEM_REACHED_ROWS: _MEM_REACHED_ROWS + int(memory_b[k][_MEM_REACHED])].tolist()
+            answer = self._order(view, [(int(owners[r]), r) for r in rows])
+            results.append(MatchedPath(tuple(ids[e] for e in entities), ids[answer[0]] if answer else None,
+                                       (start, *relations)))
+        return results
