@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define XG_ABI_VERSION 2
+#define XG_ABI_VERSION 3
 
 #if defined(__GNUC__)
 #define XG_API __attribute__((visibility("default")))
@@ -131,6 +131,13 @@ typedef struct XgOptions {
   int32_t sitelinks_rank, end_after_answer;
   int32_t release_top;
   float release_log_mass, escape_bias;
+  /* relation support of path mode's relation segments, as the reference Engine's
+   * `relations` (src/xgraph/engine.py:666-668, csrc/engine.cu:354): 0 frontier (paths
+   * execute), 1 vocabulary (every relation), 2 successor (after the first relation, the
+   * successors of the preceding label's relations; tables from
+   * xg_set_relation_successors).  1 and 2 need path mode and no STOP; a closed plan is
+   * unresolved (last_kind 6) and binds nothing. */
+  int32_t relations;
 } XgOptions;
 
 typedef struct XgInfo {
@@ -216,6 +223,14 @@ XG_API int xg_enable_stop(XgEngine* engine, const int64_t* label_offsets, const 
 XG_API int xg_set_stop(XgEngine* engine, int32_t slot, const int32_t* relations, int32_t relation_count,
                        const uint8_t* words, int32_t word_bytes, const int32_t* offsets, int32_t offset_count,
                        void* stream);
+/* The successor tables of successor support (the reference engine's native table
+ * "relation_successors", src/xgraph/relations.py:31-60, csrc/engine.cu:355, 2734), host
+ * uint32 [tables][relations][relation_words]: table v (0 the base KG, then the versions
+ * built into the engine in order), bit r2 of row r1 set when some object of an r1 edge is
+ * the subject of an r2 edge in that KG.  Copied to the device (synchronously) before the
+ * first step; XG_EINVAL unless the engine was created with relations = 2, with more than
+ * 10,304 relations, or with fewer tables than 1 + the built-in versions. */
+XG_API int xg_set_relation_successors(XgEngine* engine, const uint32_t* tables, int32_t table_count);
 /* Engine::advance (csrc/engine.cu:3041-3054): advance slots 0..count-1 by tokens[i];
  * tokens_on_host != 0 means host memory (copied first). */
 XG_API int xg_advance(XgEngine* engine, const int32_t* tokens, int32_t count, int32_t tokens_on_host,

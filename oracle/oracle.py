@@ -12,10 +12,11 @@ state projection and closed span to be equal.
 Scope: the span language of src/xgraph/oracle.py with the policies the engine serves:
 ordinary entity/fact spans, escapes, repeats, derivation, paths (union and committed),
 bound_escapes, unquoted_starts, start_rank "degree"/"sitelinks", KG versions,
-end_after_answer, opened states and residual-goal STOP (src/xgraph/oracle.py:1608-1635,
-with the question's relation table of xgraph_b200.stopping).  The reference's
-observation, menu, audit, expression and relation-support policies are not restated;
-asking for them raises.
+end_after_answer, opened states, residual-goal STOP (src/xgraph/oracle.py:1608-1635,
+with the question's relation table of xgraph_b200.stopping) and the weaker relation
+supports relations="vocabulary" / "successor" (src/xgraph/oracle.py:67-79).  The
+reference's observation, menu, audit and expression policies are not restated; asking for
+them raises.
 
 Like the reference it reads a KG index's arrays as plain data (edge tuples, token
 tuples) and recomputes everything per token from them.  One restructuring, for speed
@@ -97,6 +98,9 @@ class OracleState:
     stop: object = None  # the request's STOP table (xgraph_b200.stopping.StopRelations), kept across spans
 
 
+RELATIONS = ("frontier", "vocabulary", "successor")  # src/xgraph/relations.py:18
+
+
 class _Graph:
     """One KG version's plain edges (src/xgraph/oracle.py:344-364), by subject.  A version
     holds only the subjects its edits touch and reads every other subject from the base
@@ -134,7 +138,7 @@ class _SpanContext:
 
 
 _UNSUPPORTED = {
-    "expressions": False, "relations": "frontier", "observe": 0,
+    "expressions": False, "observe": 0,
     "observe_width": 0, "observe_defer": 0, "menu_close_next": False, "observe_select": False,
     "observe_answer": False, "observe_required": False, "observe_no_loop": False,
     "audit": False, "menu": 0, "observe_terminal": 0,
@@ -162,6 +166,7 @@ class Oracle:
         end_after_answer: bool = False,
         eos_token_ids: Iterable[int] = (),
         stop: str | None = None,
+        relations: str = "frontier",
         **others,
     ) -> None:
         # Constructor checks in the reference's order (src/xgraph/oracle.py:439-455).
@@ -184,6 +189,12 @@ class Oracle:
             raise ValueError(f"unknown STOP rule {stop!r}; expected residual-goal")
         if stop and not committed_paths:
             raise ValueError("residual-goal STOP needs committed paths (committed_paths=True)")
+        # src/xgraph/relations.py:24-28 (check_relations)
+        if relations not in RELATIONS:
+            raise ValueError(f"unknown relations mode {relations!r}; expected one of {RELATIONS}")
+        if relations != "frontier" and (not paths or stop):
+            raise ValueError("weaker relations need path mode without expressions or STOP")
+        self._relations = relations
         self._stop_terms = None
         if stop:
             from xgraph_b200.stopping import RelationTerms
@@ -241,6 +252,19 @@ class Oracle:
             for edge in added:
                 touched[edge[0]].add(edge)
             self._graphs[name] = _Graph({s: list(v) for s, v in touched.items()}, base)
+        # successor support (src/xgraph/oracle.py:625-636): per KG version, relation r1 ->
+        # the relations some object of an r1 edge is the subject of
+        self._successors: dict[str | None, dict[str, set[str]]] = {}
+        if self._relations == "successor":
+            for name, graph in self._graphs.items():
+                all_edges = [e for subject in labels.owner_ids for e in graph.edges_of(subject)]
+                outgoing_of: dict[str, set[str]] = {}
+                for subject, relation, _ in all_edges:
+                    outgoing_of.setdefault(subject, set()).add(relation)
+                pairs: dict[str, set[str]] = {}
+                for _, relation, obj in all_edges:
+                    pairs.setdefault(relation, set()).update(outgoing_of.get(self._entity_rows[obj][1], ()))
+                self._successors[name] = pairs
         self._derivation = derivation or paths
         self._paths = paths
         self._bound_escapes = bound_escapes
@@ -371,7 +395,13 @@ class Oracle:
             return [(*self._entity_rows[r], r) for r in sorted(state.reached)]
         graph = self._graph(state)
         if state.segment is Segment.RELATION:
-            have = {r for _, r, _ in graph.from_subjects(state.subjects)}
+            if self._relations != "frontier":  # src/xgraph/oracle.py:865-878
+                if self._relations == "vocabulary" or not state.relations:
+                    have = {r for _, r in self._relation_rows}
+                else:
+                    have = set().union(*(self._successors[state.version].get(r, set()) for r in state.relations))
+            else:
+                have = {r for _, r, _ in graph.from_subjects(state.subjects)}
             return [(tokens, r, row) for row, (tokens, r) in enumerate(self._relation_rows) if r in have]
         objects = {
             o for s, r, o in graph.from_subjects(state.subjects)
@@ -393,9 +423,11 @@ class Oracle:
         if state.segment is Segment.SUBJECT:
             separates = not self._answers_path(state) and any(graph.has_triples(e) for e, _ in complete)
         elif state.segment is Segment.RELATION and complete:
-            separates = not self._paths or (
+            separates = not self._paths or (  # src/xgraph/oracle.py:1060-1078
                 len(state.written) - 1 < MAX_PATH_RELATIONS - 1
-                and any(graph.has_triples(e) for e in self._frontier(state, state.typed))
+                and (self._relations != "frontier"
+                     or any(graph.has_triples(e) for e in self._frontier(state, state.typed)))
+                and (self._relations != "successor" or bool(self._successors_after(state, state.typed)))
             )
         # residual-goal STOP (src/xgraph/oracle.py:1081-1111): the separator and the escape
         # marker neither start nor go on; the closer and the label do
@@ -429,6 +461,13 @@ class Oracle:
                                    state.typed)
 
         if closing == self._closer and state.segment is Segment.RELATION:  # a path ends
+            if self._relations != "frontier":  # an unexecuted plan (src/xgraph/oracle.py:1138-1147)
+                return OracleState(
+                    Phase.FREE,
+                    last_span=ClosedSpan((*state.written, closing_label), (), (), False),
+                    facts=state.facts,
+                    version=state.version, stop=state.stop,
+                )
             frontier = self._frontier(state, closing_label)
             if self._committed:
                 best = min(frontier.values())
@@ -547,11 +586,25 @@ class Oracle:
         reached = [row for row, (_, e) in enumerate(self._entity_rows) if e in entities]
         return frozenset(reached[:MAX_REACHED])
 
+    def _successors_after(self, state: OracleState, label) -> set[str]:
+        """src/xgraph/oracle.py:1599-1605."""
+        return set().union(*(
+            self._successors[state.version].get(r, set())
+            for tokens, r, _ in self._candidates(state, label, exact=True) if tokens == label
+        ))
+
     def _next_segment(self, state: OracleState, label) -> OracleState:
         candidates = [(item, row) for _, item, row in self._candidates(state, label, exact=True)]
         items = [item for item, _ in candidates]
         written = (*state.written, label)
         graph = self._graph(state)
+        if self._relations != "frontier":  # no frontier (src/xgraph/oracle.py:1809-1822)
+            return OracleState(
+                Phase.SPAN, segment=Segment.RELATION,
+                relations=frozenset(items) if state.segment is Segment.RELATION else frozenset(),
+                written=written, last_span=state.last_span, facts=state.facts, reached=state.reached,
+                version=state.version, stop=state.stop,
+            )
         if state.segment is Segment.SUBJECT:
             subjects = frozenset(e for e in items if graph.has_triples(e))
             ranks: dict[str, int] = {}

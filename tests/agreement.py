@@ -20,8 +20,8 @@ def last_span(record) -> tuple | None:
     closed = record["last_span"]
     if closed is None:
         return None
-    if not closed["resolved"]:
-        return ("unresolved", (), ())
+    if not closed["resolved"]:  # an escape (no labels) or a plan under a weaker relation support
+        return ("relation plan" if closed["labels"] else "unresolved", (), ())
     if not closed["triples"] and len(closed["labels"]) > 1:
         return ("path span", (), ())  # the engine records no path endpoints
     kind = "fact span" if closed["triples"] else "entity span"

@@ -12,6 +12,7 @@ from pathlib import Path
 import numpy as np
 
 from xgraph_b200.engine import STATE_FIELDS, STATE_INTS
+from xgraph_b200.relations import RELATIONS, relation_successors
 from xgraph_b200.tables import XgLayout, XgOptions, pack_tables
 
 ROOT = Path(__file__).resolve().parents[1]
@@ -33,6 +34,7 @@ def library():
         "xgs_destroy": [p], "xgs_begin": [p, i32, i32], "xgs_set_version": [p, i32, i32],
         "xgs_set_reached": [p, i32, p, i32], "xgs_open_span": [p, i32], "xgs_advance": [p, p, i32],
         "xgs_masks": [p, i32, p], "xgs_states": [p, i32, p], "xgs_memory": [p, i32, p],
+        "xgs_set_successors": [p, p, i32],
     }.items():
         getattr(lib, name).argtypes = args
         getattr(lib, name).restype = None
@@ -54,7 +56,8 @@ class SeamEngine:
 
     def __init__(self, index, tokenizer, syntax, slots, *, versions=None, escapes=True, repeats=True,
                  derivation=False, paths=False, bound_escapes=True, committed_paths=False,
-                 start_rank="degree", unquoted_starts=False, end_after_answer=False, eos_token_ids=()):
+                 start_rank="degree", unquoted_starts=False, end_after_answer=False, eos_token_ids=(),
+                 relations="frontier"):
         self.lib = library()
         self.index, self.versions = index, versions
         self.tables = pack_tables(index, tokenizer, syntax, escapes=escapes, versions=versions,
@@ -64,10 +67,15 @@ class SeamEngine:
                                  paths=int(paths), bound_escapes=int(bound_escapes),
                                  committed_paths=int(committed_paths),
                                  sitelinks_rank=int(start_rank == "sitelinks"),
-                                 end_after_answer=int(end_after_answer), release_log_mass=-np.inf)
+                                 end_after_answer=int(end_after_answer), release_log_mass=-np.inf,
+                                 relations=RELATIONS.index(relations))
         self.slots = slots
         self.handle = self.lib.xgs_create(self.tables.blob.ctypes.data_as(ctypes.c_void_p),
                                           ctypes.byref(self.tables.layout), ctypes.byref(self.options), slots)
+        if relations == "successor":
+            self._successors = np.ascontiguousarray(relation_successors(index, versions), dtype=np.uint32)
+            self.lib.xgs_set_successors(self.handle, self._successors.ctypes.data_as(ctypes.c_void_p),
+                                        self._successors.shape[0])
 
     def __del__(self):
         if getattr(self, "handle", None):

@@ -53,7 +53,13 @@ constexpr int8_t kComplete = -2;
 
 enum Phase : int32_t { kFree = 0, kSpan = 1, kEscaped = 2, kError = 3 };
 enum Segment : int32_t { kSubject = 0, kRelation = 1, kObject = 2 };
-enum Closed : int32_t { kNone = 0, kUnresolved = 1, kEntitySpan = 2, kFactSpan = 3, kPathSpan = 4 };
+// (kComparison is the reference's date comparison, not served; kRelationPlan a path closed
+// under a weaker relation support: its labels written, nothing executed)
+enum Closed : int32_t { kNone = 0, kUnresolved = 1, kEntitySpan = 2, kFactSpan = 3, kPathSpan = 4, kComparison = 5,
+                        kRelationPlan = 6 };
+// Relation support of a path's relation segments (src/xgraph/relations.py:18): the entity
+// frontier (paths executed), every relation, or the successors of the preceding label's.
+enum RelationMode : int32_t { kFrontierSupport = 0, kVocabularySupport = 1, kSuccessorSupport = 2 };
 enum Flag : int32_t { kMayClose = 1, kMaySep = 2, kMayEsc = 4, kStop = 8 };
 
 // Slot memory (int32 words per slot): counts, then the fixed lists, then the bitmap of
@@ -154,6 +160,13 @@ struct Tables {
   int32_t versions;
   int32_t vocab, words, words_padded, entities, relations, relation_words;
   int32_t escapes, repeats, derivation, paths, bound_escapes, committed, end_after_answer;
+  // weaker relation supports (RelationMode; kFrontierSupport: paths executed as usual).
+  // Successor support reads successors[v][r1] (relation_words words): bit r2 says that
+  // some object of an r1 edge is the subject of an r2 edge in KG version v; versions from
+  // successor_tables on read table 0 (the host registers no such version).
+  int32_t relation_mode;
+  const uint32_t* successors;
+  int32_t successor_tables;
   // apply_mask's logit policies (off: release_on 0, escape_bias 0): release a span row to
   // the escape marker when its log allowed mass is below release_log_mass, or (release_top)
   // when its own top token is disallowed; add escape_bias to the tokens that commit to it.
@@ -744,7 +757,9 @@ XG_HD bool kept_row(const Tables& t, int32_t row) {
 }
 
 // The last closed span was a path: the next span is its answer.
-XG_HD bool answers_path(const Tables& t, const XgState& s) { return t.paths && s.last_kind == kPathSpan; }
+XG_HD bool answers_path(const Tables& t, const XgState& s) {
+  return t.paths && (s.last_kind == kPathSpan || s.last_kind == kRelationPlan);
+}
 
 // Whether some candidate row of the state's segment lies in [lo, hi)
 // (src/xgraph/oracle.py:830-894: _candidates / _segment_candidates).
@@ -1195,6 +1210,60 @@ XG_COLD bool residual_goal_stop(const Ctx& c, const XgState& s) {
   return !open;
 }
 
+// ---------------------------------------------------------------------------------------
+// Weaker relation supports (src/xgraph/oracle.py:67-79, 865-878, 1060-1078, 1809-1822): a
+// relation segment's candidates are the relations in the slot memory's relation bitmap --
+// every relation (vocabulary support, and a path's first relation under successor
+// support), or the successors of the preceding label's supported relations.
+
+XG_HD const uint32_t* successor_row(const Ctx& c, int32_t relation) {
+  const int32_t version = version_of(c);
+  const int32_t table = version < c.t.successor_tables ? version : 0;
+  return c.t.successors + (static_cast<int64_t>(table) * c.t.relations + relation) * c.t.relation_words;
+}
+
+// Whether a separator may follow the exact relation label rows [lo, hi): vocabulary
+// support, some relation exists; successor support, some supported relation of the label
+// has a successor.
+XG_COLD bool relation_goes_on(const Ctx& c, int32_t lo, int32_t hi) {
+  const Tables& t = c.t;
+  if (t.relation_mode == kVocabularySupport) return t.rel.count > 0;
+  const int32_t rw = t.relation_words;
+  if (t.successors == nullptr) return false;  // (no tables set: no successor)
+  return warp_any(c.w, 0, (hi - lo) * rw, [&](int32_t i) {
+    const int32_t relation = t.rel.owner[lo + i / rw];
+    return has_relation(c, relation) && successor_row(c, relation)[i % rw] != 0u;
+  });
+}
+
+// The relation bitmap of the next relation segment: every relation (all), or the union of
+// the successors of the supported relations of the label rows [lo, hi), computed from the
+// old bitmap (a copy in the warp's scratch) before it is replaced.
+XG_COLD void next_support(const Ctx& c, int32_t lo, int32_t hi, bool all) {
+  const Tables& t = c.t;
+  const int32_t rw = t.relation_words;
+  int32_t* have = c.mem + kMemHave;
+  int32_t* old = c.scratch;  // rw <= kScratchInts (the host refuses more relations)
+  const uint32_t tail = (t.relations & 31) ? (1u << (t.relations & 31)) - 1u : ~0u;
+  if (all) {
+    warp_for(c.w, 0, rw, [&](int32_t w) { have[w] = static_cast<int32_t>(w + 1 < rw ? ~0u : tail); });
+    warp_sync();
+    return;
+  }
+  warp_for(c.w, 0, rw, [&](int32_t w) { old[w] = have[w]; });
+  warp_sync();
+  warp_for(c.w, 0, rw, [&](int32_t w) {
+    uint32_t word = 0u;
+    for (int32_t row = lo; row < hi; ++row) {
+      const int32_t relation = t.rel.owner[row];
+      if (t.successors && ((static_cast<uint32_t>(old[relation >> 5]) >> (relation & 31)) & 1u))
+        word |= successor_row(c, relation)[w];
+    }
+    have[w] = static_cast<int32_t>(word);
+  });
+  warp_sync();
+}
+
 // Which delimiter branches may start after the state's typed label
 // (src/xgraph/oracle.py:1039-1113: closes, separates, and the escape condition).
 XG_SHARED void set_flags(const Ctx& c, XgState& s) {
@@ -1224,7 +1293,9 @@ XG_SHARED void set_flags(const Ctx& c, XgState& s) {
                     return subject_candidate(c, bound, row) && row_degree(t, version, row) > 0;
                   });
     } else if (s.segment == kRelation) {
-      separates = !t.paths || (s.hops < kMaxHops && frontier_goes_on(c, s.lo, s.ex_hi));
+      separates = !t.paths || (s.hops < kMaxHops && (t.relation_mode != kFrontierSupport
+                                                         ? relation_goes_on(c, s.lo, s.ex_hi)
+                                                         : frontier_goes_on(c, s.lo, s.ex_hi)));
       // residual-goal STOP (src/xgraph/oracle.py:1081-1111): only the closer or the label
       // goes on (neither the separator nor the escape marker starts or goes on)
       if (closes && t.stop_on != nullptr && residual_goal_stop(c, s)) {
@@ -1272,7 +1343,16 @@ XG_COLD void next_segment(const Ctx& c, XgState& s, int32_t llo, int32_t lhi) {
   const int32_t version = version_of(c);
   if (s.segment == kSubject) {
     const bool bound = !unbound(t, c, s);
-    if (t.paths) {
+    if (t.paths && t.relation_mode != kFrontierSupport) {
+      // no execution frontier: the start keeps its admission, and the first relation may
+      // be any (src/xgraph/oracle.py:1809-1822)
+      mem_store(c, kMemFrontier, 0);
+      drop_cached_frontier(c);
+      warp_sync();
+      next_support(c, llo, lhi, true);
+      s.subj_lo = llo;
+      s.subj_hi = lhi;
+    } else if (t.paths) {
       // starts: every candidate with triples in best-connected order, kept to 64
       TopSet ts{c.top, 0};
       #pragma unroll 1
@@ -1338,6 +1418,9 @@ XG_COLD void next_segment(const Ctx& c, XgState& s, int32_t llo, int32_t lhi) {
     s.hops = 1;
     // STOP: the question words the written start covers (csrc/engine.cu:1872)
     if (stop_installed(c)) set_stop_used(s, stop_start_words(c, llo));
+  } else if (t.paths && t.relation_mode != kFrontierSupport) {
+    if (t.relation_mode == kSuccessorSupport) next_support(c, llo, lhi, false);
+    s.hops += 1;
   } else if (t.paths) {
     // STOP: and those the relations just written cover (csrc/engine.cu:1902-1904)
     if (stop_installed(c)) set_stop_used(s, stop_used(s) | stop_consumed(c, llo, lhi));
@@ -1365,7 +1448,15 @@ XG_COLD void next_segment(const Ctx& c, XgState& s, int32_t llo, int32_t lhi) {
 XG_COLD void close_span(const Ctx& c, XgState& s, int32_t llo, int32_t lhi) {
   const Tables& t = c.t;
   const int32_t version = version_of(c);
-  if (s.segment == kRelation) {  // a path ends
+  if (s.segment == kRelation && t.relation_mode != kFrontierSupport) {
+    // a plan under a weaker support: unresolved, nothing executed or bound
+    // (src/xgraph/oracle.py:1138-1147)
+    if (c.w.leader()) c.mem[kMemReached] = c.mem[kMemFrontier] = 0;
+    drop_cached_frontier(c);
+    warp_sync();
+    s.last_kind = kRelationPlan;
+    s.last_lo = s.last_hi = s.last_subj_lo = s.last_subj_hi = s.last_rel_lo = s.last_rel_hi = 0;
+  } else if (s.segment == kRelation) {  // a path ends
     int32_t n = cached_frontier(c, llo, lhi);
     if (t.committed && n > 0) n = keep_least_rank(c, n);
     reach_rows_of_top(c, n);

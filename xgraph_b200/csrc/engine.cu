@@ -1414,6 +1414,8 @@ struct XgEngine {
   uint32_t* rel_any = nullptr;    // derived tables (derive_kernel): relation-segment superset mask,
   int32_t* rel_any_tok = nullptr; //   its tokens,
   int32_t* sparse = nullptr;      //   and the automaton rows' blocked-token lists
+  uint32_t* successors = nullptr; // successor support's tables (xg_set_relation_successors)
+  int32_t successor_tables = 0;
   // residual-goal STOP (xg_enable_stop): label words, and per slot: installed flag, relation
   // table, question word offsets and bytes
   int64_t* stop_label_off = nullptr;
@@ -1692,6 +1694,9 @@ void bind_tables(XgEngine* e) {
   t.release_top = o.release_top != 0;
   t.release_on = o.release_top != 0 || o.release_log_mass > -INFINITY;
   t.escape_bias = o.escape_bias;
+  t.relation_mode = o.relations;
+  t.successors = e->successors;
+  t.successor_tables = e->successor_tables;
   t.states = e->states;
   t.memory = e->memory;
   t.memory_ints = kMemHave + ((l.relation_words + 3) & ~3);
@@ -1724,6 +1729,7 @@ void release(XgEngine* e) {
   cudaFree(e->rel_any);
   cudaFree(e->rel_any_tok);
   cudaFree(e->sparse);
+  cudaFree(e->successors);
   for (void* p : {static_cast<void*>(e->arena.range), static_cast<void*>(e->arena.subjects),
                   static_cast<void*>(e->arena.adjacency), static_cast<void*>(e->arena.relations),
                   static_cast<void*>(e->arena.objects)})
@@ -1782,6 +1788,12 @@ int create(const void* blob, bool on_device, const XgLayout* layout, const XgOpt
     return fail(XG_EINVAL, "release_log_mass must be the log of a mass in (0, 1), or -INFINITY when off");
   if ((options->release_top || options->release_log_mass > -INFINITY) && !options->escapes)
     return fail(XG_EINVAL, "release needs escapes: it releases to the escape marker");
+  if (options->relations < 0 || options->relations > 2)
+    return fail(XG_EINVAL, "relations must be 0 (frontier), 1 (vocabulary) or 2 (successor)");
+  if (options->relations != 0 && !options->paths)
+    return fail(XG_EINVAL, "weaker relations need path mode");
+  if (options->relations == 2 && layout->relation_words > kScratchInts)
+    return fail(XG_EINVAL, "successor support handles at most 10,304 relations");
   XgEngine* e = new XgEngine();
   e->layout = *layout;
   e->options = *options;
@@ -2104,6 +2116,7 @@ int xg_enable_stop(XgEngine* e, const int64_t* label_offsets, const uint8_t* lab
   if (!e || !label_offsets || (word_bytes > 0 && !label_words)) return fail(XG_EINVAL, "null argument");
   if (!e->t.paths || !e->t.committed) return fail(XG_EINVAL, "residual-goal STOP needs committed paths (committed_paths=True)");
   if (e->stop_on) return fail(XG_EINVAL, "STOP is already enabled on this engine");
+  if (e->t.relation_mode != 0) return fail(XG_EINVAL, "weaker relations need path mode without STOP");
   const int64_t rows = e->layout.entity_rows;
   if (label_offsets[0] != 0 || label_offsets[rows] != word_bytes)
     return fail(XG_EINVAL, "STOP label words: offsets must run from 0 to the word bytes, one row per label row");
@@ -2328,7 +2341,35 @@ int xg_admit(XgEngine* e, const XgAdmission* admissions, int32_t count, int32_t 
 int xg_add_version(XgEngine* e, const int32_t* subjects, int32_t count, const int64_t* adjacency,
                    const int32_t* edge_relations, const int32_t* edge_objects, void* stream, int32_t* version) {
   if (!e || !version) return fail(XG_EINVAL, "null argument");
+  if (e->t.relation_mode == 2)
+    return fail(XG_EINVAL, "successor support reads the successor tables of the versions built in; "
+                           "no version can be added while it runs");
   return add_version(e, subjects, count, adjacency, edge_relations, edge_objects, as_stream(stream), version);
+}
+
+int xg_set_relation_successors(XgEngine* e, const uint32_t* tables, int32_t table_count) {
+  if (!e || !tables) return fail(XG_EINVAL, "null argument");
+  if (e->t.relation_mode != 2) return fail(XG_EINVAL, "successor tables need relations = 2 (successor)");
+  if (table_count < 1 + e->layout.versions)
+    return fail(XG_EINVAL, "successor support needs one table for the base KG and one per built-in version");
+  const size_t bytes = static_cast<size_t>(table_count) * e->t.relations * e->t.relation_words * sizeof(uint32_t);
+  uint32_t* device = nullptr;
+  cudaError_t err = cudaMalloc(reinterpret_cast<void**>(&device), bytes > 0 ? bytes : 16);
+  if (err != cudaSuccess) {
+    cudaGetLastError();
+    return fail(XG_ENOMEM, std::string("device allocation failed: ") + cudaGetErrorString(err));
+  }
+  if (bytes > 0) err = cudaMemcpy(device, tables, bytes, cudaMemcpyHostToDevice);
+  if (err != cudaSuccess) {
+    cudaFree(device);
+    return cuda_fail(err, "successor tables upload");
+  }
+  cudaFree(e->successors);  // (the engine's stream is idle: the copy above synchronized)
+  e->successors = device;
+  e->successor_tables = table_count;
+  e->t.successors = device;
+  e->t.successor_tables = table_count;
+  return XG_OK;
 }
 
 int xg_drop_version(XgEngine* e, int32_t version, void* stream) {

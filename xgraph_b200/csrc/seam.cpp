@@ -29,6 +29,7 @@ struct SeamEngine {
   std::vector<uint8_t> stop_label_words;
   std::vector<int32_t> stop_on, stop_rel, stop_woff;
   std::vector<uint8_t> stop_words;
+  std::vector<uint32_t> successors;  // successor support's tables (xgs_set_successors)
   Tables t{};
 };
 
@@ -124,6 +125,7 @@ SeamEngine* xgs_create(const void* blob, const XgLayout* l, const XgOptions* o, 
   t.bound_escapes = o->bound_escapes;
   t.committed = o->committed_paths;
   t.end_after_answer = o->end_after_answer;
+  t.relation_mode = o->relations;
   t.memory_ints = kMemHave + ((l->relation_words + 3) & ~3);
   e->states.assign(slots, XgState{});
   e->memory.assign(static_cast<size_t>(slots) * t.memory_ints, 0);
@@ -214,6 +216,12 @@ void xgs_memory(SeamEngine* e, int32_t n, int32_t* out) {
 int32_t xgs_memory_ints(SeamEngine* e) { return e->t.memory_ints; }
 
 // xg_enable_stop / xg_set_stop on the host (arguments checked by the library's entry points).
+void xgs_set_successors(SeamEngine* e, const uint32_t* tables, int32_t count) {
+  e->successors.assign(tables, tables + static_cast<size_t>(count) * e->t.relations * e->t.relation_words);
+  e->t.successors = e->successors.data();
+  e->t.successor_tables = count;
+}
+
 void xgs_enable_stop(SeamEngine* e, const int64_t* offsets, const uint8_t* words, int64_t bytes) {
   const int64_t rows = e->layout.entity_rows;
   e->stop_label_off.assign(offsets, offsets + rows + 1);

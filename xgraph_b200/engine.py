@@ -45,7 +45,7 @@ STATE_INTS = 64
 LIBRARY = Path(__file__).resolve().parent / "libxgraph_b200.so"
 
 XG_OK, XG_EINVAL, XG_ECUDA, XG_ENOMEM = 0, 1, 2, 3
-ABI_VERSION = 2
+ABI_VERSION = 3
 """XG_ABI_VERSION of include/xgraph_b200.h that these bindings follow."""
 ADMISSION_INTS = 5 + MAX_REACHED
 """int32 words of one admission record (XgAdmission: slot, on, version, open_span,
@@ -55,7 +55,7 @@ DTYPES = {"float32": 0, "bfloat16": 1, "float16": 2}
 # Reference constructor options this engine does not serve, with their neutral values.
 _NOT_SERVED = {
     "expressions": False,
-    "relations": "frontier", "observe": 0, "observe_width": 0,
+    "observe": 0, "observe_width": 0,
     "observe_defer": 0, "menu_close_next": False, "observe_select": False,
     "observe_answer": False, "observe_required": False, "observe_no_loop": False,
     "audit": False, "audit_entities": 20, "audit_relations": 8, "menu": 0,
@@ -114,6 +114,7 @@ def load_library(path: Path = LIBRARY):
         "xg_build_adjacency": ([p, p, p, i64, p, p, i32, i32, p, i32, i64, p, p, p, p, p, p], ctypes.c_int),
         "xg_enable_stop": ([p, p, p, i64], ctypes.c_int),
         "xg_set_stop": ([p, i32, p, i32, p, i32, p, i32, p], ctypes.c_int),
+        "xg_set_relation_successors": ([p, p, i32], ctypes.c_int),
         "xg_build_label_rows": ([i32, p, p, i64, p, p, i64, p, i32, i32, p, p, i64, p, p, p, p, p, p, p, p],
                                 ctypes.c_int),
     }
@@ -210,6 +211,7 @@ class Engine:
         end_after_answer: bool = False,
         eos_token_ids: Iterable[int] = (),
         stop: str | None = None,
+        relations: str = "frontier",
         device_blob=None,
         **others,
     ) -> None:
@@ -237,6 +239,10 @@ class Engine:
             raise ValueError(f"unknown STOP rule {stop!r}; expected residual-goal")
         if stop and not committed_paths:
             raise ValueError("residual-goal STOP needs committed paths (committed_paths=True)")
+        from .relations import RELATIONS, check_relations
+
+        check_relations(relations, paths=paths, stop=stop)
+        self._relations = relations
         sitelinks_rank = check_start_rank(start_rank, index) == "sitelinks"
         if not escapes and (release_mass > 0 or release_top):
             raise ValueError("release needs escapes: it releases to the escape marker")
@@ -266,7 +272,7 @@ class Engine:
             sitelinks_rank=int(sitelinks_rank), end_after_answer=int(end_after_answer),
             release_top=int(bool(release_top)),
             release_log_mass=math.log(release_mass) if release_mass > 0 else -math.inf,
-            escape_bias=float(escape_bias),
+            escape_bias=float(escape_bias), relations=RELATIONS.index(relations),
         )
         handle = ctypes.c_void_p()
         if device_blob is None:
@@ -280,6 +286,12 @@ class Engine:
                 ctypes.byref(self._options), int(max_sequences), ctypes.byref(handle))
         _check(rc)
         self._handle = handle
+        if relations == "successor":
+            from .relations import relation_successors
+
+            tables = np.ascontiguousarray(relation_successors(index, versions), dtype=np.uint32)
+            _check(self._lib.xg_set_relation_successors(self._handle, tables.ctypes.data_as(ctypes.c_void_p),
+                                                        tables.shape[0]))
         self._stop_terms = None
         if stop:
             from .stopping import RelationTerms, label_word_table
@@ -377,6 +389,9 @@ class Engine:
 
         if not isinstance(name, str) or not name:
             raise ValueError(f"a KG version needs a non-empty name, got {name!r}")
+        if self._relations == "successor":
+            raise ValueError("successor support reads the successor tables of the versions built in; "
+                             "no version can be added while it runs")
         if name in self._added or (self._versions is not None and name in self._versions.names):
             raise ValueError(f"KG version {name!r} is registered already")
         if self._builder is None:

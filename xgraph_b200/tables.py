@@ -60,7 +60,7 @@ class XgOptions(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int32) for n in (
         "escapes", "repeats", "derivation", "paths", "bound_escapes", "committed_paths",
         "sitelinks_rank", "end_after_answer", "release_top")] + [
-        ("release_log_mass", ctypes.c_float), ("escape_bias", ctypes.c_float)]
+        ("release_log_mass", ctypes.c_float), ("escape_bias", ctypes.c_float), ("relations", ctypes.c_int32)]
 
 
 def mask_words(vocab_size: int) -> int:
