@@ -47,8 +47,9 @@ def test_unserved_settings_are_refused():
     adapter.check_served_settings({"XGRAPH_PATHS": "1", "XGRAPH_RELEASE_MASS": "0.2", "XGRAPH_RELATIONS": "frontier",
                                    "XGRAPH_ESCAPE_BIAS": "-2.5", "XGRAPH_RELEASE_TOP": "1", "XGRAPH_OBSERVE": "0.0",
                                    "XGRAPH_STOP": "residual-goal"})
+    adapter.check_served_settings({"XGRAPH_RELATIONS": "successor"})  # the relation supports are served
     for name, value in [("XGRAPH_MENU", "3"), ("XGRAPH_AUDIT", "1"),
-                        ("XGRAPH_RELATIONS", "successor"), ("XGRAPH_EXPRESSIONS", "1"), ("XGRAPH_OBSERVE", "4")]:
+                        ("XGRAPH_EXPRESSIONS", "1"), ("XGRAPH_OBSERVE", "4")]:
         with pytest.raises(ValueError, match=name):
             adapter.check_served_settings({name: value})
 

@@ -28,9 +28,10 @@ kept for `replay_statuses`).  Engine settings: XGRAPH_ESCAPES, XGRAPH_REPEATS,
 XGRAPH_RELEASE_MASS, XGRAPH_RELEASE_TOP, XGRAPH_DERIVATION, XGRAPH_ESCAPE_BIAS, XGRAPH_PATHS,
 XGRAPH_BOUND_ESCAPES, XGRAPH_COMMITTED_PATHS, XGRAPH_START_RANK, XGRAPH_UNQUOTED_STARTS,
 XGRAPH_END_AFTER_ANSWER, XGRAPH_STOP (residual-goal: each opted-in request supplies its
-question as `xgraph_question`; `xgraph_stop` 0 turns STOP off for a request).  The
-reference's other research policies (expressions, observations, menus, audit, relation
-supports, per-request path options) are not served by this engine: a setting or argument
+question as `xgraph_question`; `xgraph_stop` 0 turns STOP off for a request),
+XGRAPH_RELATIONS (frontier, vocabulary or successor relation support).  The reference's
+other research policies (expressions, observations, menus, audit, per-request path
+options) are not served by this engine: a setting or argument
 that asks for one is refused with a ValueError naming it.
 
 This module imports only the standard library at import time: vLLM also calls
@@ -73,7 +74,7 @@ _UNSERVED_SETTINGS = {  # setting: the value that keeps the policy off
     "XGRAPH_EXPRESSIONS": "0", "XGRAPH_OBSERVE": "0", "XGRAPH_OBSERVE_SELECT": "0",
     "XGRAPH_OBSERVE_ANSWER": "0", "XGRAPH_OBSERVE_WIDTH": "0", "XGRAPH_OBSERVE_DEFER": "0",
     "XGRAPH_OBSERVE_TERMINAL": "0", "XGRAPH_MENU": "0", "XGRAPH_MENU_CLOSE_NEXT": "0", "XGRAPH_AUDIT": "0",
-    "XGRAPH_REQUEST_PATH_OPTIONS": "0", "XGRAPH_RELATIONS": "frontier",
+    "XGRAPH_REQUEST_PATH_OPTIONS": "0",
 }
 
 _REGISTERED: dict[str, list[str]] = {}
@@ -290,6 +291,7 @@ class XGraphLogitsProcessor(_Base):
             end_after_answer=end_after_answer,
             eos_token_ids=eos_token_ids,
             stop=self._stop,
+            relations=os.environ.get("XGRAPH_RELATIONS") or "frontier",
         )
         self._staged: dict[int, Staged] = {}   # slot -> admissions since the last apply_staged_writes
         self._folded = None                    # admission records the next step's launch applies
