@@ -1192,6 +1192,17 @@ __global__ void __maxnreg__(kFusedRegisters)
     } else if (const int32_t* list = delta == nullptr ? sparse_row(t, base) : nullptr) {  // few blocked tokens
       apply_sparse<ELT>(t, out, f.cols, list, f.neg, true, 0, f.cols);
     } else {
+      // The whole mask row is staged in shared memory first (one round of loads for the
+      // row), so the store loop below reads no global memory: a load issued behind the
+      // CTA's own outstanding stores waits for them, and a label-root row's ~67 k partial
+      // stores held each of its later mask loads for microseconds.
+      if (base != nullptr || delta != composed) {
+        for (int32_t w = threadIdx.x; w < t.words_padded; w += blockDim.x)
+          composed[w] = (base ? __ldg(base + w) : 0u) | (delta ? delta[w] : 0u);  // (delta may be composed)
+        __syncthreads();
+        base = nullptr;
+        delta = composed;
+      }
       apply_segments<ELT>(t, out, f.cols, base, delta, f.neg, 0, (f.cols + 1023) >> 10, threadIdx.x >> 5,
                           blockDim.x >> 5, blocked_run);
     }
