@@ -283,8 +283,11 @@ XG_API int xg_sync_apply_admit(XgEngine* engine, const int32_t* slots, int32_t c
  * each admitted slot's mask. */
 XG_API int xg_admit(XgEngine* engine, const XgAdmission* admissions, int32_t count, int32_t on_host, void* stream);
 /* Device-side faults recorded since the last call, then cleared (waits for the device):
- * bit 0 a grid barrier of the fused step gave up waiting (bounded wait), bit 1 a device
- * admission with a field out of range was skipped.  0 in normal operation. */
+ * bit 1 (value 2) a device admission with a field out of range was skipped; bit 2 (value
+ * 4) a fused step wrote a row's columns outside the relation-segment superset early and
+ * the row then left its relation segment (its -inf would be wrong; never expected: the
+ * early-write rule follows the state machine's own branches).  Bit 0 is unused.  0 in
+ * normal operation. */
 XG_API int xg_faults(XgEngine* engine, int32_t* out);
 /* Engine::apply_mask (csrc/engine.cu:2990-3037): in place, logits[r, c] = -inf for every
  * column c its slot's mask disallows and every c >= vocab; rows of inactive slots and of

@@ -463,8 +463,9 @@ class Engine:
         del keep
 
     def faults(self) -> int:
-        """Device-side faults since the last call (waits; bit 0 a fused step's grid barrier
-        gave up waiting, bit 1 a device admission out of range was skipped); 0 normally."""
+        """Device-side faults since the last call (waits; value 2: a device admission out of
+        range was skipped; value 4: a row the fused step wrote early left its relation
+        segment, never expected); 0 normally."""
         out = ctypes.c_int32()
         _check(self._lib.xg_faults(self._handle, ctypes.byref(out)))
         return int(out.value)
