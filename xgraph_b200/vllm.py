@@ -52,22 +52,22 @@ except ImportError:  # no vLLM of that API: the class still works with stand-ins
 
 OPT_IN = "xgraph"
 ANCHOR = "xgraph_anchor"
-"""Per-request argument: the question's entity ids, where derivation mode starts."""
+"""Request extra arg: entity ids bound before the first span (derivation and path mode start there)."""
 KG_VERSION = "xgraph_kg_version"
-"""Per-request argument: the name of the KG version the request reads (XGRAPH_KG_VERSIONS)."""
+"""Request extra arg: which version of the XGRAPH_KG_VERSIONS file this request's KG reads."""
 VERSIONS = "XGRAPH_KG_VERSIONS"
 OPEN = "xgraph_open"
-"""Per-request argument: 1 starts the request inside a span (its prompt ends with the opener)."""
+"""Request extra arg: 1 when the prompt already ends in the span opener (decoding begins in a span)."""
 PREFILL = "xgraph_prefill"
-"""Per-request argument: the text the prompt ends with, which the engine replays."""
+"""Request extra arg: trailing prompt text to run through the engine before decoding."""
 REPLAY_ID = "xgraph_replay_id"
-"""Per-request argument: the caller's key for the replay's outcome."""
+"""Request extra arg: key under which the replay outcome is kept for replay_statuses."""
 QUESTION = "xgraph_question"
-"""Per-request argument: the question text, required with XGRAPH_STOP=residual-goal."""
+"""Request extra arg: the question, which STOP needs (XGRAPH_STOP=residual-goal)."""
 STOP = "xgraph_stop"
-"""Per-request argument: 0 turns STOP off for the request."""
+"""Request extra arg: 0 disables STOP for this one request."""
 REPLAYS = ("replayed", "tail mismatch", "disallowed")
-"""The outcomes of a replayed prefill, which XGraphLogitsProcessor.replays counts."""
+"""What a replayed prefill can end as (the keys of XGraphLogitsProcessor.replays)."""
 
 _UNSERVED_ARGS = ("xgraph_relation_ranks", "xgraph_path_options")
 _UNSERVED_SETTINGS = {  # setting: the value that keeps the policy off
@@ -137,7 +137,7 @@ def replay_statuses(llm, keys: list[str]) -> dict[str, dict]:
 
 
 def _version_names(path: str) -> list[str]:
-    """The version names of a version file, read once per process."""
+    """Version names of the file at `path`, cached for the life of the process."""
     if path not in _REGISTERED:
         from xgraph_b200.kgversions import version_names
 
