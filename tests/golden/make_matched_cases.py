@@ -15,7 +15,10 @@ degree or sitelink start rank, unquoted starts, KG versions with add / remove ed
 
 - paths walked along the KG's own edges, 1-4 relations, with random labels and aliases;
 - entity spans (no relation), starts that name nothing, relations the frontier lacks,
-  relation labels cut short, and walks longer than the 8-relation cap.
+  relation labels cut short, and walks longer than the 8-relation cap;
+- anchored paths and entity spans (see anchored_of), each recorded with whether the
+  executor fell back to every anchor entity, and an anchor naming no entity (recorded with
+  the reference's error).
 """
 
 from __future__ import annotations
@@ -75,6 +78,50 @@ def paths_of(world, rng: random.Random, count: int) -> list[tuple[str, list[str]
     return out
 
 
+def anchored_of(world, rng: random.Random, count: int) -> list[tuple[str, list[str], list[str]]]:
+    """Seeded anchored paths: walks as in paths_of (some of them entity spans) written from
+    one label of the start entity, with an anchor that is the start entity, the start and
+    another entity, another entity the same label names (a homonym, where there is one), or
+    an entity the label does not name (the executor then starts from every anchor entity);
+    and one anchor naming no entity with labels."""
+    ents = {e: labels for e, labels in world["entities"] if labels}
+    rels = {r: labels for r, labels in world["relations"] if labels}
+    named: dict[str, list[str]] = {}
+    for e, labels in ents.items():
+        for label in labels:
+            named.setdefault(label, []).append(e)
+    outgoing: dict[str, list[tuple[str, str]]] = {}
+    for s, r, o in world["triples"]:
+        if r in rels:
+            outgoing.setdefault(s, []).append((r, o))
+    subjects = sorted(s for s in outgoing if s in ents)
+    everyone = sorted(ents)
+    out = []
+    for k in range(count):
+        start = rng.choice(subjects)
+        name = rng.choice(ents[start])
+        hops, at = [], start
+        for _ in range(0 if k % 6 == 5 else rng.randint(1, 3)):
+            if at not in outgoing:
+                break
+            r, o = rng.choice(outgoing[at])
+            hops.append(rng.choice(rels[r]))
+            at = o
+        kind = k % 4
+        if kind == 0:
+            anchor = [start]
+        elif kind == 1:
+            anchor = [start, rng.choice(everyone)]
+        elif kind == 2:
+            others = [e for e in named[name] if e != start]
+            anchor = [rng.choice(others)] if others else [start]
+        else:
+            anchor = [rng.choice([e for e in everyone if e not in named[name]])]
+        out.append((name, hops, anchor))
+    out.append((rng.choice(ents[rng.choice(subjects)]), [], ["Q999999999"]))
+    return out
+
+
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__)
     parser.add_argument("--reference", type=Path, required=True, help="the reference checkout")
@@ -103,6 +150,7 @@ def main() -> None:
         versions = build_kg_versions(index, edits)
         rng = random.Random(sum(map(ord, world_name)) * 31 + 7)
         written = paths_of(world, rng, 64)
+        anchored = anchored_of(world, rng, 24)
         for setting in settings:
             executor = MatchedExecutor(index, served, versions=versions, **SETTINGS[setting])
             for n, (start, relations) in enumerate(written):
@@ -112,9 +160,22 @@ def main() -> None:
                               "relations": relations, "version": version,
                               "reached": list(path.reached), "answer": path.answer,
                               "plan": None if path.plan is None else list(path.plan)})
+            for n, (start, relations, anchor) in enumerate(anchored):
+                version = (None, "v0", "v1")[n % 3] if world_name != "crowd" else None
+                case = {"world": world_name, "setting": setting, "start": start, "relations": relations,
+                        "version": version, "anchor": anchor}
+                try:
+                    path = executor.execute(start, relations, anchor=anchor, version=version)
+                except ValueError as error:
+                    cases.append({**case, "error": str(error)})
+                    continue
+                # the executor's fallback: the start label names none of the anchor's entities
+                fallback = not executor._written_starts(start, anchor)
+                cases.append({**case, "fallback": fallback, "reached": list(path.reached),
+                              "answer": path.answer, "plan": None if path.plan is None else list(path.plan)})
     with gzip.open(HERE / "matched_cases.json.gz", "wt", encoding="utf-8") as f:
         json.dump({"settings": SETTINGS, "edits": all_edits, "cases": cases}, f)
-    empty = sum(1 for c in cases if not c["reached"])
+    empty = sum(1 for c in cases if not c.get("reached"))
     print(f"{len(cases)} cases ({empty} empty)")
 
 

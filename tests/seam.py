@@ -34,7 +34,7 @@ def library():
         "xgs_destroy": [p], "xgs_begin": [p, i32, i32], "xgs_set_version": [p, i32, i32],
         "xgs_set_reached": [p, i32, p, i32], "xgs_open_span": [p, i32], "xgs_advance": [p, p, i32],
         "xgs_masks": [p, i32, p], "xgs_states": [p, i32, p], "xgs_memory": [p, i32, p],
-        "xgs_set_successors": [p, p, i32],
+        "xgs_set_successors": [p, p, i32], "xgs_advance_slot": [p, i32, i32],
     }.items():
         getattr(lib, name).argtypes = args
         getattr(lib, name).restype = None
@@ -134,6 +134,14 @@ class SeamEngine:
     def advance(self, tokens):
         arr = np.ascontiguousarray(tokens, dtype=np.int32)
         self.lib.xgs_advance(self.handle, arr.ctypes.data_as(ctypes.c_void_p), len(arr))
+
+    def advance_slot(self, slot, token):
+        self.lib.xgs_advance_slot(self.handle, int(slot), int(token))
+
+    def memory(self):
+        out = np.zeros((self.slots, self.lib.xgs_memory_ints(self.handle)), dtype=np.int32)
+        self.lib.xgs_memory(self.handle, self.slots, out.ctypes.data_as(ctypes.c_void_p))
+        return out
 
     def masks(self):
         out = np.zeros((self.slots, self.tables.words), dtype=np.uint32)

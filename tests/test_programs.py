@@ -1,10 +1,12 @@
 """Offline path execution (xgraph_b200/programs.py) against the reference's MatchedExecutor.
 
-tests/golden/matched_cases.json.gz (tests/golden/make_matched_cases.py) holds 704 written
-paths over four golden worlds and four executor settings, with what the reference's
-MatchedExecutor (src/xgraph/programs.py:368-1130) made of each: entities reached in
-best-connected order, answer, plan.  The GPU executor runs each world's paths as batches
-of engine slots and must return the same three fields for every path.
+tests/golden/matched_cases.json.gz (tests/golden/make_matched_cases.py) holds 979 written
+paths over four golden worlds and four executor settings, 275 of them anchored, with what
+the reference's MatchedExecutor (src/xgraph/programs.py:368-1130) made of each: entities
+reached in best-connected order, answer, plan (or its error).  The executor runs each
+world's paths as batches of engine slots and must return the same three fields for every
+path it serves -- on the GPU, and on the CPU with the host seam of the kernels' row logic in
+place of the CUDA engine -- and refuse the anchored fallback it does not serve.
 """
 
 from __future__ import annotations
@@ -32,7 +34,13 @@ def test_matched_fixture_covers_the_cases():
     reaching nothing, entity spans, and walks cut at the 8-relation cap; and the reference's
     plan is the start and the (capped) relations exactly where a path reaches something."""
     cases = fixture()["cases"]
-    assert len(cases) == 704
+    assert len(cases) == 979
+    anchored = [c for c in cases if "anchor" in c]
+    assert len(anchored) == 275 and sum(1 for c in anchored if c.get("fallback")) == 66
+    assert sum(1 for c in anchored if "error" in c) == 11
+    assert sum(1 for c in served(anchored) if len(c["reached"]) > 1) > 50
+    assert any(not c["relations"] and c["reached"] for c in served(anchored))
+    cases = served(cases)
     assert sum(1 for c in cases if len(c["reached"]) > 1) > 100
     assert sum(1 for c in cases if not c["reached"]) > 100
     assert any(not c["relations"] and c["reached"] for c in cases)
@@ -45,7 +53,44 @@ def test_matched_fixture_covers_the_cases():
             assert c["plan"] is None
 
 
-def _executor(world_name: str, setting: str, max_paths: int = 256):
+class SeamRunner:
+    """The executor's runner over the host seam (core.cuh built with g++): the same
+    admissions and the same two syncs, one token at a time per slot, so the executor's host
+    logic and the kernels' row logic run on the CPU."""
+
+    def __init__(self, index, tokenizer, versions, settings, slots):
+        from tests.seam import SeamEngine
+
+        self.seam = SeamEngine(index, tokenizer, index.span_syntax, slots, versions=versions, paths=True,
+                               committed_paths=settings.get("committed_paths", True),
+                               start_rank=settings.get("start_rank", "degree"),
+                               unquoted_starts=settings.get("unquoted_starts", False))
+        self.versions, self.max_sequences = versions, slots
+
+    def view(self, version):
+        if version is not None and (self.versions is None or version not in self.versions.names):
+            raise ValueError(f"no KG version {version!r}")
+        return self.seam.view(version)
+
+    def run(self, history, before, total, admissions):
+        seam, n = self.seam, len(admissions)
+        for k, version, anchor in admissions:
+            seam.begin(k)
+            if anchor:
+                seam.anchor(k, anchor)
+            seam.set_version(k, version)
+        out = []
+        for upto in (before, total):
+            for k in range(n):
+                done = 0 if upto is before else int(before[k])
+                for token in history[k, done: int(upto[k])].tolist():
+                    seam.advance_slot(k, token)
+            states = seam.states()
+            out += [{name: v[:n] for name, v in states.items()}, seam.memory()[:n]]
+        return tuple(out)
+
+
+def _executor(world_name: str, setting: str, max_paths: int = 256, seam: bool = False):
     from xgraph_b200.kgversions import build_kg_versions
     from xgraph_b200.programs import MatchedExecutor
 
@@ -54,31 +99,72 @@ def _executor(world_name: str, setting: str, max_paths: int = 256):
     index = world_index(world_name, True)
     edits = {name: [tuple(e) for e in v] for name, v in data["edits"][world_name].items()}
     versions = build_kg_versions(index, edits)
-    return MatchedExecutor(index, served, versions=versions, max_paths=max_paths, **data["settings"][setting])
+    settings = data["settings"][setting]
+    runner = SeamRunner(index, served, versions, settings, max_paths) if seam else None
+    return MatchedExecutor(index, served, versions=versions, max_paths=max_paths, _runner=runner, **settings)
+
+
+def served(cases):
+    """The cases the executor serves: all but the anchored fallbacks and errors."""
+    return [c for c in cases if not c.get("fallback") and "error" not in c]
+
+
+def _groups():
+    groups = defaultdict(list)
+    for case in fixture()["cases"]:
+        groups[(case["world"], case["setting"])].append(case)
+    return groups
+
+
+def _refusals(executor, cases):
+    """The anchored fallbacks and anchors without label rows, one call each: ValueError."""
+    for case in cases:
+        if case.get("fallback"):
+            with pytest.raises(ValueError, match="names none of the anchor's entities"):
+                executor.execute(case["start"], case["relations"], anchor=case["anchor"], version=case["version"])
+        elif "error" in case:
+            with pytest.raises(ValueError, match="anchor has no writable label rows"):
+                executor.execute(case["start"], case["relations"], anchor=case["anchor"], version=case["version"])
+
+
+def _job(case) -> tuple:
+    return (case["start"], case["relations"], case["version"], case.get("anchor"))
+
+
+def _check(cases, got, where):
+    for case, path in zip(cases, got, strict=True):
+        at = (*where, case["start"], case["relations"], case["version"], case.get("anchor"))
+        assert list(path.reached) == case["reached"], at
+        assert path.answer == case["answer"], at
+        assert (None if path.plan is None else list(path.plan)) == case["plan"], at
+
+
+def test_matched_execution_on_the_host_seam_equals_the_reference():
+    """Every recorded path through the executor with the kernels' row logic on the CPU (the
+    host seam in place of the CUDA engine): the reference's entities in its order, its
+    answer and its plan."""
+    for (world_name, setting), cases in _groups().items():
+        executor = _executor(world_name, setting, max_paths=64, seam=True)
+        _check(served(cases), executor.execute_many([_job(c) for c in served(cases)]), (world_name, setting))
+        _refusals(executor, cases)
 
 
 @pytest.mark.gpu
 def test_matched_execution_equals_the_reference():
     """Every recorded path, executed on the GPU a world and setting at a time, reaches the
     reference's entities in its order, delivers its answer and reports its plan."""
-    groups = defaultdict(list)
-    for case in fixture()["cases"]:
-        groups[(case["world"], case["setting"])].append(case)
-    for (world_name, setting), cases in groups.items():
+    for (world_name, setting), cases in _groups().items():
         executor = _executor(world_name, setting)
-        got = executor.execute_many([(c["start"], c["relations"], c["version"]) for c in cases])
-        for case, path in zip(cases, got, strict=True):
-            where = (world_name, setting, case["start"], case["relations"], case["version"])
-            assert list(path.reached) == case["reached"], where
-            assert path.answer == case["answer"], where
-            assert (None if path.plan is None else list(path.plan)) == case["plan"], where
+        _check(served(cases), executor.execute_many([_job(c) for c in served(cases)]), (world_name, setting))
+        _refusals(executor, cases)
 
 
 @pytest.mark.gpu
 def test_matched_execution_in_small_batches_and_single_calls():
     """A batch larger than the executor's slots runs in pieces with the same results, and
     `execute` (one path) agrees with the batch."""
-    cases = [c for c in fixture()["cases"] if c["world"] == "rand_bpe" and c["setting"] == "committed"]
+    cases = [c for c in served(fixture()["cases"]) if c["world"] == "rand_bpe" and c["setting"] == "committed"
+             and "anchor" not in c]
     executor = _executor("rand_bpe", "committed", max_paths=7)
     got = executor.execute_many([(c["start"], c["relations"], c["version"]) for c in cases])
     assert [list(p.reached) for p in got] == [c["reached"] for c in cases]
@@ -87,11 +173,8 @@ def test_matched_execution_in_small_batches_and_single_calls():
         assert list(one.reached) == case["reached"] and one.answer == case["answer"]
 
 
-@pytest.mark.gpu
 def test_matched_executor_refuses_what_it_does_not_serve():
-    executor = _executor("toy", "committed", max_paths=2)
-    with pytest.raises(ValueError, match="anchored"):
-        executor.execute("Paris Hilton", ["place of birth"], anchor=["Q5"])
+    executor = _executor("toy", "committed", max_paths=2, seam=True)
     with pytest.raises(ValueError, match="repair"):
         executor.execute("Paris Hilton", ["place of birth"], repair=True)
     with pytest.raises(ValueError, match="no KG version"):

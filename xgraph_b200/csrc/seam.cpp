@@ -194,6 +194,15 @@ void xgs_advance(SeamEngine* e, const int32_t* tokens, int32_t count) {
   }
 }
 
+// One slot advanced by one token (the other slots untouched).
+void xgs_advance_slot(SeamEngine* e, int32_t slot, int32_t token) {
+  Ctx c = ctx(e, slot);
+  XgState s = e->states[slot];
+  advance_state(c, s, token);
+  e->states[slot] = s;
+  build_mask(c, s);
+}
+
 // Masks of slots 0..n-1 as [n, words] (zeros for the error phase).
 void xgs_masks(SeamEngine* e, int32_t n, uint32_t* out) {
   const int32_t words = e->layout.words;
@@ -215,12 +224,14 @@ void xgs_memory(SeamEngine* e, int32_t n, int32_t* out) {
 
 int32_t xgs_memory_ints(SeamEngine* e) { return e->t.memory_ints; }
 
-// xg_enable_stop / xg_set_stop on the host (arguments checked by the library's entry points).
+// xg_set_relation_successors on the host.
 void xgs_set_successors(SeamEngine* e, const uint32_t* tables, int32_t count) {
   e->successors.assign(tables, tables + static_cast<size_t>(count) * e->t.relations * e->t.relation_words);
   e->t.successors = e->successors.data();
   e->t.successor_tables = count;
 }
+
+// xg_enable_stop / xg_set_stop on the host (arguments checked by the library's entry points).
 
 void xgs_enable_stop(SeamEngine* e, const int64_t* offsets, const uint8_t* words, int64_t bytes) {
   const int64_t rows = e->layout.entity_rows;

@@ -22,8 +22,11 @@ written (a start naming nothing with triples, a relation the frontier lacks, a l
 short) leaves its slot in the error phase and executes to nothing, as the reference's
 executor returns for it.
 
-Not served (refused by name): anchors, the offline repairs (`repair`, `strip_quotes`),
-and the observation / menu / audit settings.
+Anchored paths start from the anchor's entities their start label names (each anchored
+slot admitted with the anchor's label rows).  Not served (refused by name): an anchored
+start naming none of the anchor's entities (the reference then starts from every anchor
+entity), the offline repairs (`repair`, `strip_quotes`) and the observation / menu / audit
+settings.
 """
 
 from __future__ import annotations
@@ -81,7 +84,7 @@ class MatchedExecutor:
 
     def __init__(self, index, tokenizer, *, versions=None, start_rank: str = "degree",
                  unquoted_starts: bool = False, committed_paths: bool = True, max_paths: int = 256,
-                 **others) -> None:
+                 _runner=None, **others) -> None:
         from .engine import Engine
         from .index import IndexMismatch
 
@@ -96,9 +99,11 @@ class MatchedExecutor:
             raise ValueError(f"max_paths must be at least 1, got {max_paths}")
         self._index, self._tokenizer, self._versions = index, tokenizer, versions
         self._syntax = index.span_syntax
-        self._engine = Engine(index, tokenizer, self._syntax, max_paths, paths=True,
-                              committed_paths=committed_paths, versions=versions, start_rank=start_rank,
-                              unquoted_starts=unquoted_starts)
+        # the engine-shaped runner that executes the batches (tests drive the host seam of the
+        # same row logic through it); by default the CUDA engine
+        self._runner = _runner if _runner is not None else _EngineRunner(Engine(
+            index, tokenizer, self._syntax, max_paths, paths=True, committed_paths=committed_paths,
+            versions=versions, start_rank=start_rank, unquoted_starts=unquoted_starts))
         self._sitelinks = index.sitelinks if start_rank == "sitelinks" else None
         self._pieces: dict[str, list[int]] = {}
         self._first: np.ndarray | None = None
@@ -175,35 +180,61 @@ class MatchedExecutor:
 
     # -- execution -----------------------------------------------------------------------
 
+    def _written_rows(self, start: str) -> list[int]:
+        """The label rows written exactly as `start` (the reference's `_rows`)."""
+        tokens = self._label(start)
+        if tokens is None:
+            return []
+        labels = self._index.labels
+        lo, hi = labels.prefix_range(tokens)
+        offsets = np.asarray(labels.offsets)
+        return [r for r in range(lo, hi) if int(offsets[r + 1] - offsets[r]) == len(tokens)]
+
+    def _bound_rows(self, anchor: Sequence[str]) -> list[int]:
+        """The first 64 label rows (row order) of the anchor's entities."""
+        owners = np.asarray(self._index.labels.owners)
+        at = {e: n for n, e in enumerate(self._index.labels.owner_ids)}
+        entities = [at[e] for e in anchor if e in at]
+        rows = np.flatnonzero(np.isin(owners, entities))[:MAX_REACHED].tolist()
+        if not rows:
+            raise ValueError(f"anchor has no writable label rows: {list(anchor)!r}")
+        return rows
+
     def execute(self, start: str, relations: list[str], anchor: list[str] | None = None,
                 version: str | None = None, repair: bool = False) -> MatchedPath:
         """The path from the start label along the relation labels (see the class)."""
-        return self.execute_many([(start, relations, version)], anchor=anchor, repair=repair)[0]
+        return self.execute_many([(start, relations, version, anchor)], repair=repair)[0]
 
-    def execute_many(self, paths: Iterable[tuple[str, Sequence[str], str | None]], *,
-                     anchor=None, repair: bool = False) -> list[MatchedPath]:
-        """Each (start, relations, version) path executed, in order."""
-        if anchor is not None:
-            raise ValueError("anchored execution is not served by this executor")
+    def execute_many(self, paths: Iterable[tuple], *, repair: bool = False) -> list[MatchedPath]:
+        """Each (start, relations, version) or (start, relations, version, anchor) path
+        executed, in order.  An anchored path starts from the anchor's entities its start
+        label names; one whose label names none of them (the reference then starts from every
+        anchor entity, which no written span can express) raises ValueError."""
         if repair:
             raise ValueError("the offline relation repair is not served by this executor")
-        paths = [(start, list(relations)[:MAX_PATH_RELATIONS], version) for start, relations, version in paths]
-        for _, _, version in paths:
-            self._engine.view(version)  # an unknown version name raises here, before any launch
+        jobs = []
+        for path in paths:
+            start, relations, version = path[0], list(path[1])[:MAX_PATH_RELATIONS], path[2]
+            anchor = path[3] if len(path) > 3 else None
+            self._runner.view(version)  # an unknown version name raises here, before any launch
+            if anchor is not None:
+                bound = self._bound_rows(anchor)
+                named = sorted(set(self._written_rows(start)) & set(bound))
+                if not named:
+                    raise ValueError(f"the anchored start {start!r} names none of the anchor's entities "
+                                     f"{list(anchor)!r}; that fallback is not served")
+                anchor = list(anchor)
+            jobs.append((start, relations, version, anchor))
         out: list[MatchedPath] = []
-        size = self._engine.max_sequences
-        for at in range(0, len(paths), size):
-            out += self._batch(paths[at: at + size])
+        size = self._runner.max_sequences
+        for at in range(0, len(jobs), size):
+            out += self._batch(jobs[at: at + size])
         return out
 
     def _batch(self, paths) -> list[MatchedPath]:
-        import torch
-
-        from .engine import Admission
-
-        engine, index = self._engine, self._index
-        n, size = len(paths), engine.max_sequences
-        streams = [self._stream(start, relations) for start, relations, _ in paths]
+        index = self._index
+        n, size = len(paths), self._runner.max_sequences
+        streams = [self._stream(start, relations) for start, relations, _, _ in paths]
         width = max([len(s[0]) for s in streams if s is not None] + [1])
         history = np.zeros((size, width), dtype=np.int32)
         before = np.zeros(size, dtype=np.int32)
@@ -212,32 +243,26 @@ class MatchedExecutor:
             if stream is not None:
                 history[k, : len(stream[0])] = stream[0]
                 before[k], total[k] = stream[1], len(stream[0])
-        device = torch.device("cuda", torch.cuda.current_device())
-        engine.reset()
-        engine.admit([Admission(k, True, version=paths[k][2]) for k in range(n)])
-        slots = torch.arange(n, dtype=torch.int32, device=device)
-        history_d = torch.from_numpy(history).to(device)
-        prompt = torch.zeros(size, dtype=torch.int32, device=device)
-        engine.sync(slots, history_d, prompt, torch.from_numpy(before).to(device))
-        states_a, memory_a = engine.states_host(n), engine.memory_host(n)
-        engine.sync(slots, history_d, prompt, torch.from_numpy(total).to(device))
-        states_b, memory_b = engine.states_host(n), engine.memory_host(n)
+        admissions = [(k, version, anchor) for k, (_, _, version, anchor) in enumerate(paths)]
+        states_a, memory_a, states_b, memory_b = self._runner.run(history, before, total, admissions)
         owners, ids = index.labels.owners, index.labels.owner_ids
 
         results = []
-        for k, (start, relations, version) in enumerate(paths):
+        for k, (start, relations, version, anchor) in enumerate(paths):
             empty = MatchedPath((), None, None)
             if streams[k] is None or int(states_b["phase"][k]) == _PHASE_ERROR:
                 results.append(empty)
                 continue
-            view = engine.view(version)
+            view = self._runner.view(version)
             kind = int(states_b["last_kind"][k])
-            if not relations:  # an entity span: every entity its label names
+            if not relations:  # an entity span: every entity its label names (the anchor's, anchored)
                 if kind != _ENTITY_SPAN:
                     results.append(empty)
                     continue
                 lo, hi = int(states_b["last_lo"][k]), int(states_b["last_hi"][k])
-                starts = self._order(view, [(int(owners[r]), r) for r in range(lo, hi)])
+                rows = (range(lo, hi) if anchor is None
+                        else sorted(set(self._written_rows(start)) & set(self._bound_rows(anchor))))
+                starts = self._order(view, [(int(owners[r]), r) for r in rows])
                 results.append(MatchedPath(tuple(ids[e] for e in starts), ids[starts[0]] if starts else None, None))
                 continue
             if kind != _PATH_SPAN:
@@ -263,3 +288,39 @@ class MatchedExecutor:
             results.append(MatchedPath(tuple(ids[e] for e in entities), ids[answer[0]] if answer else None,
                                        (start, *relations)))
         return results
+
+
+class _EngineRunner:
+    """The CUDA engine as the executor drives it: a batch of paths, one slot each (admitted
+    with its KG version and anchors in one launch), synced once up to each path's last
+    relation label and once through its closer; the slots' states and memory read back
+    after each."""
+
+    def __init__(self, engine) -> None:
+        self._engine = engine
+
+    @property
+    def max_sequences(self) -> int:
+        return self._engine.max_sequences
+
+    def view(self, version):
+        return self._engine.view(version)
+
+    def run(self, history: np.ndarray, before: np.ndarray, total: np.ndarray, admissions):
+        import torch
+
+        from .engine import Admission
+
+        engine = self._engine
+        n, size = len(admissions), engine.max_sequences
+        device = torch.device("cuda", torch.cuda.current_device())
+        engine.reset()
+        engine.admit([Admission(k, True, anchors=tuple(anchor or ()), version=version)
+                      for k, version, anchor in admissions])
+        slots = torch.arange(n, dtype=torch.int32, device=device)
+        history_d = torch.from_numpy(history).to(device)
+        prompt = torch.zeros(size, dtype=torch.int32, device=device)
+        engine.sync(slots, history_d, prompt, torch.from_numpy(before).to(device))
+        states_a, memory_a = engine.states_host(n), engine.memory_host(n)
+        engine.sync(slots, history_d, prompt, torch.from_numpy(total).to(device))
+        return states_a, memory_a, engine.states_host(n), engine.memory_host(n)
