@@ -13,10 +13,11 @@ Scope: the span language of src/xgraph/oracle.py with the policies the engine se
 ordinary entity/fact spans, escapes, repeats, derivation, paths (union and committed),
 bound_escapes, unquoted_starts, start_rank "degree"/"sitelinks", KG versions,
 end_after_answer, opened states, residual-goal STOP (src/xgraph/oracle.py:1608-1635,
-with the question's relation table of xgraph_b200.stopping) and the weaker relation
-supports relations="vocabulary" / "successor" (src/xgraph/oracle.py:67-79).  The
-reference's observation, menu, audit and expression policies are not restated; asking for
-them raises.
+with the question's relation table of xgraph_b200.stopping), the weaker relation
+supports relations="vocabulary" / "successor" (src/xgraph/oracle.py:67-79) and
+expressions, the date and value comparisons (src/xgraph/oracle.py:104-133).  The
+reference's observation, menu and audit policies are not restated; asking for them
+raises.
 
 Like the reference it reads a KG index's arrays as plain data (edge tuples, token
 tuples) and recomputes everything per token from them.  One restructuring, for speed
@@ -35,6 +36,7 @@ from enum import Enum
 MAX_FACTS = 64  # src/xgraph/oracle.py:172
 MAX_REACHED = 64  # src/xgraph/oracle.py:175
 MAX_PATH_RELATIONS = 8  # src/xgraph/oracle.py:177
+COMPARISONS = ("earlier", "later", "same")  # src/xgraph/oracle.py:196, by operator position
 
 
 class Phase(Enum):
@@ -96,6 +98,10 @@ class OracleState:
     version: str | None = None
     answer_complete: bool = False
     stop: object = None  # the request's STOP table (xgraph_b200.stopping.StopRelations), kept across spans
+    operating: bytes | None = None  # expressions: operator bytes typed so far (after the label prefix)
+    operator: int = 0  # expressions: the span's operator, its position + 1 (0: none)
+    starts: tuple[tuple[str, ...], ...] = ()  # expressions: each written operand's ranked starts
+    ranks_b: tuple[tuple[str, int], ...] = ()  # expressions: operand B's frontier with its ranks
 
 
 RELATIONS = ("frontier", "vocabulary", "successor")  # src/xgraph/relations.py:18
@@ -135,14 +141,27 @@ class _SpanContext:
     separates: bool
     escapes: bool
     forced: bool = False  # residual-goal STOP: only the closer (or the label) goes on
+    separator: bytes = b""  # the delimiter the separator branch matches (operand A: the operand separator)
+    operates: bool = False  # expressions: an operator may start with this token
 
 
 _UNSUPPORTED = {
-    "expressions": False, "observe": 0,
+    "observe": 0,
     "observe_width": 0, "observe_defer": 0, "menu_close_next": False, "observe_select": False,
     "observe_answer": False, "observe_required": False, "observe_no_loop": False,
     "audit": False, "menu": 0, "observe_terminal": 0,
 }
+
+
+def check_expressions(index) -> None:
+    """src/xgraph/index.py:686-704: the index a comparison can run on."""
+    if not index.span_syntax.writes_expressions:
+        raise ValueError("expressions need a KG index built for a span syntax with operators and an "
+                         f"operand separator, not {index.span_syntax}")
+    if not index.expressions:
+        raise ValueError("the KG index was saved before labels holding expression syntax were excluded")
+    if index.date_entities is None:
+        raise ValueError("expressions need a KG index with the date table")
 
 
 class Oracle:
@@ -167,6 +186,7 @@ class Oracle:
         eos_token_ids: Iterable[int] = (),
         stop: str | None = None,
         relations: str = "frontier",
+        expressions: bool = False,
         **others,
     ) -> None:
         # Constructor checks in the reference's order (src/xgraph/oracle.py:439-455).
@@ -185,6 +205,13 @@ class Oracle:
                 raise TypeError(f"unexpected keyword argument {name!r}")
             if value != _UNSUPPORTED[name]:
                 raise ValueError(f"the {name} policy is not restated by this oracle")
+        # src/xgraph/oracle.py:540-545
+        if expressions and not committed_paths:
+            raise ValueError("expressions need committed paths (committed_paths=True)")
+        if expressions and not escapes:
+            raise ValueError("expressions need escapes, the way out of an operand or relation")
+        if expressions and len(syntax.operators) > len(COMPARISONS):
+            raise ValueError(f"expressions know the operators of {COMPARISONS}, by position")
         if stop not in (None, "residual-goal"):
             raise ValueError(f"unknown STOP rule {stop!r}; expected residual-goal")
         if stop and not committed_paths:
@@ -192,7 +219,7 @@ class Oracle:
         # src/xgraph/relations.py:24-28 (check_relations)
         if relations not in RELATIONS:
             raise ValueError(f"unknown relations mode {relations!r}; expected one of {RELATIONS}")
-        if relations != "frontier" and (not paths or stop):
+        if relations != "frontier" and (not paths or expressions or stop):
             raise ValueError("weaker relations need path mode without expressions or STOP")
         self._relations = relations
         self._stop_terms = None
@@ -205,6 +232,20 @@ class Oracle:
         if start_rank not in ("degree", "sitelinks"):
             raise ValueError(f"start_rank must be one of ('degree', 'sitelinks'), got {start_rank!r}")
         labels, relations = index.labels, index.relations
+        # expressions (src/xgraph/oracle.py:557-569): each date entity's date; the operators
+        # offered (the value comparison only with the verdict entities), with the label prefix
+        self._expressions = expressions
+        self._dates = {}
+        if expressions:
+            from xgraph_b200.dates import unpack_date
+
+            check_expressions(index)
+            self._dates = {labels.owner_ids[int(e)]: unpack_date(int(k))
+                           for e, k in zip(index.date_entities, index.date_keys, strict=True)}
+        offered = syntax.operators if index.verdicts else syntax.operators[:2]
+        self._operators = [(syntax.label_prefix + op).encode("utf-8") for op in offered]
+        self._verdicts = dict(index.verdicts or {})
+        self._operand_separator = syntax.operand_separator.encode("utf-8")
         self._sitelinks: dict[str, int] = {}
         if start_rank == "sitelinks":
             if index.sitelinks is None:
@@ -278,10 +319,14 @@ class Oracle:
         self._separator = syntax.separator.encode("utf-8")
         self._escape = syntax.escape.encode("utf-8")
         self._entity_ids = labels.owner_ids
+        # rows no unbound subject names: quoted ones with unquoted starts, and always the
+        # verdict entities' (src/xgraph/oracle.py:650-659)
+        verdict_ids = set(self._verdicts.values())
         self._quoted_rows = frozenset(
             row
-            for row, (tokens, _) in enumerate(self._entity_rows)
-            if unquoted_starts and syntax.quoted(b"".join(self._bytes[t] for t in tokens))
+            for row, (tokens, owner) in enumerate(self._entity_rows)
+            if owner in verdict_ids
+            or (unquoted_starts and syntax.quoted(b"".join(self._bytes[t] for t in tokens)))
         )
 
     # -- states (src/xgraph/oracle.py:660-724) ------------------------------------
@@ -402,6 +447,8 @@ class Oracle:
                     have = set().union(*(self._successors[state.version].get(r, set()) for r in state.relations))
             else:
                 have = {r for _, r, _ in graph.from_subjects(state.subjects)}
+                if state.operator:  # a comparison: the relations both frontiers have
+                    have &= {r for _, r, _ in graph.from_subjects(dict(state.ranks_b))}
             return [(tokens, r, row) for row, (tokens, r) in enumerate(self._relation_rows) if r in have]
         objects = {
             o for s, r, o in graph.from_subjects(state.subjects)
@@ -418,15 +465,19 @@ class Oracle:
         closes = bool(complete) and (state.segment is not Segment.RELATION or self._paths)
         if closes and state.segment is Segment.OBJECT and not self._repeats:
             closes = (*state.written, state.typed) not in state.facts
+        if closes and state.operator:  # a comparison closes after a relation, where it has a result
+            closes = state.segment is Segment.RELATION and self._result(state, state.typed) is not None
         graph = self._graph(state)
+        operands = 2 if state.operator else 1  # the subject labels a path or comparison writes
         separates = False
         if state.segment is Segment.SUBJECT:
             separates = not self._answers_path(state) and any(graph.has_triples(e) for e, _ in complete)
         elif state.segment is Segment.RELATION and complete:
             separates = not self._paths or (  # src/xgraph/oracle.py:1060-1078
-                len(state.written) - 1 < MAX_PATH_RELATIONS - 1
+                len(state.written) - operands < MAX_PATH_RELATIONS - 1
                 and (self._relations != "frontier"
-                     or any(graph.has_triples(e) for e in self._frontier(state, state.typed)))
+                     or all(any(graph.has_triples(e) for e in self._frontier(state, state.typed, k))
+                            for k in range(operands)))
                 and (self._relations != "successor" or bool(self._successors_after(state, state.typed)))
             )
         # residual-goal STOP (src/xgraph/oracle.py:1081-1111): the separator and the escape
@@ -435,7 +486,12 @@ class Oracle:
         if forced:
             separates = False
         escapes = self._escapes and state.typed is not None and self._may_escape(state) and not forced
-        return _SpanContext(complete, closes, separates, escapes, forced)
+        # operand A of a comparison is followed by the operand separator instead
+        operand_a = state.operator and state.segment is Segment.SUBJECT and not state.written
+        operates = (self._expressions and state.segment is Segment.SUBJECT and not state.operator
+                    and state.typed == () and not state.reached)  # src/xgraph/oracle.py:1669-1678
+        return _SpanContext(complete, closes, separates, escapes, forced,
+                            self._operand_separator if operand_a else self._separator, operates)
 
     @staticmethod
     def _branch(typed, label, data, delimiter, may_start, current):
@@ -455,11 +511,25 @@ class Oracle:
         closing, closing_label = self._branch(
             state.closing, state.closing_label, data, self._closer, ctx.closes, state.typed)
         separating, separating_label = self._branch(
-            None if ctx.forced else state.separating, state.separating_label, data, self._separator, ctx.separates,
+            None if ctx.forced else state.separating, state.separating_label, data, ctx.separator, ctx.separates,
             state.typed)
+        operating = state.operating + data if state.operating is not None else data if ctx.operates else None
+        if operating is not None and not any(op.startswith(operating) for op in self._operators):
+            operating = None
         escaping, _ = self._branch(None if ctx.forced else state.escaping, (), data, self._escape, ctx.escapes,
                                    state.typed)
 
+        if closing == self._closer and state.operator:  # a comparison ends (src/xgraph/oracle.py:1115-1130)
+            committed, result = self._result(state, closing_label)
+            rows = self._rows_for(result)
+            return OracleState(
+                Phase.FREE,
+                last_span=ClosedSpan((*state.written, closing_label), tuple(sorted(result)), (), True,
+                                     COMPARISONS[state.operator - 1], committed),
+                facts=state.facts,
+                reached=frozenset(rows[:MAX_REACHED]),
+                version=state.version, stop=state.stop,
+            )
         if closing == self._closer and state.segment is Segment.RELATION:  # a path ends
             if self._relations != "frontier":  # an unexecuted plan (src/xgraph/oracle.py:1138-1147)
                 return OracleState(
@@ -495,12 +565,16 @@ class Oracle:
                 reached=reached,
                 version=state.version, stop=state.stop,
             )
-        if separating == self._separator:
+        if separating == ctx.separator:
             return self._next_segment(state, separating_label)
         if escaping == self._escape:
             return OracleState(Phase.ESCAPED, last_span=state.last_span, facts=state.facts,
                                reached=state.reached, version=state.version, stop=state.stop)
-        if label is None and closing is None and separating is None and escaping is None:
+        if operating in self._operators:  # operand A follows
+            return OracleState(Phase.SPAN, last_span=state.last_span, facts=state.facts, reached=state.reached,
+                               version=state.version, stop=state.stop,
+                               operator=self._operators.index(operating) + 1)
+        if label is None and closing is None and separating is None and escaping is None and operating is None:
             return None
         return replace(
             state,
@@ -510,6 +584,7 @@ class Oracle:
             separating=separating,
             separating_label=separating_label,
             escaping=escaping,
+            operating=operating,
         )
 
     # -- resolution and frontiers (src/xgraph/oracle.py:1655-1922) ---------------
@@ -533,7 +608,7 @@ class Oracle:
         and no relation of the new, whole frontier covers a question word that neither the
         written start nor the relations written so far (this one included) cover."""
         goal = state.stop
-        if goal is None or not goal.head or state.segment is not Segment.RELATION:
+        if goal is None or not goal.head or state.operator or state.segment is not Segment.RELATION:
             return False
         followed = {self._relation_number[r] for tokens, r in self._relation_rows if tokens == state.typed}
         if not followed & goal.head:
@@ -563,15 +638,62 @@ class Oracle:
             order = sorted(ranks, key=self._first_row.get)
         return {e: ranks[e] for e in order[:MAX_REACHED]}
 
-    def _frontier(self, state: OracleState, label) -> dict[str, int]:
+    def _frontier(self, state: OracleState, label, operand: int = 0) -> dict[str, int]:
+        """The objects of operand `operand`'s frontier (a comparison's B: ranks_b) under
+        every relation the label names, each with its least start rank, kept."""
         relations = {r for tokens, r in self._relation_rows if tokens == label}
-        start = dict(state.ranks)
+        start = dict(state.ranks_b if operand else state.ranks)
+        subjects = frozenset(start) if operand else state.subjects
         ranks: dict[str, int] = {}
-        for s, r, o in self._graph(state).from_subjects(state.subjects):
-            if s in state.subjects and r in relations:
+        for s, r, o in self._graph(state).from_subjects(subjects):
+            if s in subjects and r in relations:
                 entity = self._entity_rows[o][1]
                 ranks[entity] = min(ranks.get(entity, start[s]), start[s])
         return self._kept(ranks)
+
+    def _result(self, state: OracleState, label):
+        """A comparison closed after this relation label: the start entity each operand
+        commits to and the result, or None where it cannot close (src/xgraph/oracle.py:
+        1680-1737)."""
+        if COMPARISONS[state.operator - 1] == "same":
+            return self._same(state, label)
+        fronts = [self._frontier(state, label, k) for k in (0, 1)]
+        if not all(any(e in self._dates for e in front) for front in fronts):
+            return None
+        picked = []
+        for k, front in enumerate(fronts):  # each operand's best start that reaches a date
+            dated = {e: rank for e, rank in front.items() if e in self._dates}
+            best = min(dated.values())
+            earliest = min((self._dates[e] for e, rank in dated.items() if rank == best), key=lambda d: (d.lo, d.hi))
+            picked.append((state.starts[k][best], earliest))
+        (a, date_a), (b, date_b) = picked
+        if date_a.before(date_b):
+            earlier, later = {a}, {b}
+        elif date_b.before(date_a):
+            earlier, later = {b}, {a}
+        else:  # equal or overlapping: undetermined, both
+            earlier = later = {a, b}
+        return (a, b), frozenset(earlier if COMPARISONS[state.operator - 1] == "earlier" else later)
+
+    def _same(self, state: OracleState, label):
+        """A value comparison: each operand's best start with any value, and the verdict
+        entity (yes: a shared entity or an equal stored date)."""
+        reached = []
+        for k in (0, 1):
+            front = self._frontier(state, label, k)
+            if not front:
+                return None
+            best = min(front.values())
+            reached.append((state.starts[k][best], {e for e, rank in front.items() if rank == best}))
+        (a, values_a), (b, values_b) = reached
+        entities_a = {e for e in values_a if e not in self._dates}
+        entities_b = {e for e in values_b if e not in self._dates}
+        if bool(entities_a) != bool(entities_b):  # values of two kinds
+            return None
+        dates_a = {self._dates[e] for e in values_a if e in self._dates}
+        dates_b = {self._dates[e] for e in values_b if e in self._dates}
+        verdict = "yes" if entities_a & entities_b or dates_a & dates_b else "no"
+        return (a, b), frozenset({self._verdicts[verdict]})
 
     def _answers_path(self, state: OracleState) -> bool:
         last = state.last_span
@@ -612,6 +734,20 @@ class Oracle:
                 starts = self._best_connected(state, [(e, r) for e, r in candidates if e in subjects])
                 ranks = self._kept({e: rank for rank, e in enumerate(starts)})
                 subjects = frozenset(ranks)
+            if state.operator:  # a comparison: rank this operand's starts (src/xgraph/oracle.py:1834-1870)
+                ranked = tuple(sorted(ranks, key=ranks.get))
+                if not state.written:  # operand A: operand B follows
+                    return OracleState(
+                        Phase.SPAN, written=written, last_span=state.last_span, facts=state.facts,
+                        reached=state.reached, version=state.version, stop=state.stop,
+                        operator=state.operator, starts=(ranked,), ranks=tuple(sorted(ranks.items())),
+                    )
+                return OracleState(  # operand B: both frontiers go on in lock step
+                    Phase.SPAN, segment=Segment.RELATION, subjects=frozenset(dict(state.ranks)), written=written,
+                    last_span=state.last_span, facts=state.facts, reached=state.reached,
+                    version=state.version, stop=state.stop, ranks=state.ranks, operator=state.operator,
+                    starts=(*state.starts, ranked), ranks_b=tuple(sorted(ranks.items())),
+                )
             if not self._paths and self._derivation and subjects:
                 best = self._best_connected(state, [(e, r) for e, r in candidates if e in subjects])
                 subjects = frozenset(best[:1])
@@ -622,10 +758,12 @@ class Oracle:
             )
         if self._paths:
             frontier = self._frontier(state, label)
+            other = self._frontier(state, label, 1) if state.operator else {}
             return OracleState(
                 Phase.SPAN, segment=Segment.RELATION, subjects=frozenset(frontier), written=written,
                 last_span=state.last_span, facts=state.facts, reached=state.reached,
                 version=state.version, stop=state.stop, ranks=tuple(sorted(frontier.items())),
+                operator=state.operator, starts=state.starts, ranks_b=tuple(sorted(other.items())),
             )
         return OracleState(
             Phase.SPAN, segment=Segment.OBJECT, subjects=state.subjects, relations=frozenset(items),

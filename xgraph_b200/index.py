@@ -429,11 +429,16 @@ def build_kg_index_arrays(
     syntax: SpanSyntax,
     sitelinks: np.ndarray | Sequence[int] | None = None,
     device=None,
+    *,
+    dates: tuple[np.ndarray, np.ndarray] | None = None,
+    verdicts: dict[str, str] | None = None,
 ) -> KGIndex:
     """The KG index of entities and relations given as (id, labels) and triples given as
     an int (n, 3) array of (subject position, relation position, object position).
     `device` (a CUDA device): the edge arrays are built there by the library (the same
-    arrays as the host build's); None builds everything on the host."""
+    arrays as the host build's); None builds everything on the host.  `dates`: the date
+    table (xgraph_b200.dates.date_table); `verdicts`: the verdict entities by verdict,
+    which the entities must already hold."""
     triples = np.asarray(triples, dtype=np.int64).reshape(-1, 3)
     if len(triples) and (
         triples.min() < 0
@@ -464,6 +469,10 @@ def build_kg_index_arrays(
         "tokenizer": tokenizer.fingerprint, "syntax": repr(syntax),
         "sitelinks": counts if counts is not None else "none",
     }
+    if dates is not None:
+        parts["date_entities"], parts["date_keys"] = dates
+    if verdicts is not None:
+        parts["verdicts"] = verdicts
     return KGIndex(
         labels=labels,
         relations=relation_index,
@@ -473,6 +482,9 @@ def build_kg_index_arrays(
         unwritable_triples=unwritable,
         span_syntax=syntax,
         sitelinks=counts,
+        date_entities=None if dates is None else dates[0],
+        date_keys=None if dates is None else dates[1],
+        verdicts=verdicts,
         base_fingerprint=_fingerprint(parts),
     )
 
@@ -487,18 +499,22 @@ def build_kg_index(
     *,
     initial_case_aliases: bool = False,
 ) -> KGIndex:
-    """The KG index of an in-memory KG (src/xgraph/index.py:403-516).
+    """The KG index of an in-memory KG (src/xgraph/index.py:403-516).  With dates (Date
+    values by entity id) the index holds the date table of date comparisons; with verdicts
+    the verdict entities (xgraph_b200.dates.VERDICTS, each labelled with its verdict) are
+    appended to the KG's entities.  Initial-case aliases feed the reference's alias policy,
+    which this engine does not implement; asking for them raises ValueError."""
+    from .dates import VERDICTS, date_table
 
-    Date tables, verdict entities and initial-case aliases feed the reference's
-    expression and alias policies, which this engine does not implement; asking
-    for them raises ValueError rather than building a different index.
-    """
-    if dates is not None or verdicts or initial_case_aliases:
-        raise ValueError(
-            "dates, verdicts and initial_case_aliases belong to policies this engine "
-            "does not implement"
-        )
+    if initial_case_aliases:
+        raise ValueError("initial_case_aliases belongs to a policy this engine does not implement")
     validate(kg)
+    if verdicts:
+        taken = sorted(set(VERDICTS.values()) & {e.id for e in kg.entities})
+        if taken:
+            raise KGFormatError(f"the KG holds {taken}, the ids of the verdict entities")
+        kg = KnowledgeGraph((*kg.entities, *(Entity(i, (v,)) for v, i in VERDICTS.items())), kg.relations,
+                            kg.triples)
     entity_at = {e.id: n for n, e in enumerate(kg.entities)}
     relation_at = {r.id: n for n, r in enumerate(kg.relations)}
     triples = np.array(
@@ -507,6 +523,12 @@ def build_kg_index(
     counts = None
     if sitelinks is not None:
         counts = [sitelinks.get(e.id, 0) for e in kg.entities]
+    table = None
+    if dates is not None:
+        unknown = sorted(set(dates) - set(entity_at))
+        if unknown:
+            raise KGFormatError(f"dates name entities the KG lacks: {unknown[:5]}")
+        table = date_table({entity_at[e]: d for e, d in dates.items()})
     return build_kg_index_arrays(
         [(e.id, e.labels) for e in kg.entities],
         [(r.id, r.labels) for r in kg.relations],
@@ -514,6 +536,8 @@ def build_kg_index(
         tokenizer,
         syntax,
         sitelinks=counts,
+        dates=table,
+        verdicts=dict(VERDICTS) if verdicts else None,
     )
 
 
@@ -625,6 +649,8 @@ def save_kg_index(index: KGIndex, directory: str | Path) -> None:
     }
     if index.sitelinks is not None:
         arrays["sitelinks"] = index.sitelinks
+    if index.date_entities is not None:
+        arrays["date_entities"], arrays["date_keys"] = index.date_entities, index.date_keys
     np.savez(directory / "kg-index.npz", **arrays)
     header = {
         "format": "xgraph-b200-index-1",
@@ -636,6 +662,7 @@ def save_kg_index(index: KGIndex, directory: str | Path) -> None:
         "relations": {"owner_ids": list(index.relations.owner_ids),
                       "excluded": [[e.owner_id, e.label, e.reason] for e in index.relations.excluded]},
         "base_fingerprint": index.base_fingerprint,
+        "verdicts": index.verdicts,
     }
     (directory / "kg-index.json").write_text(json.dumps(header) + "\n", encoding="utf-8")
 
@@ -646,9 +673,9 @@ REFERENCE_INDEX_FORMAT = 1
 
 def load_kg_index(directory: str | Path) -> KGIndex:
     """Read a KG index saved by save_kg_index, or by the reference's save_kg_index (one .npy
-    file per array and kg-index.json, src/xgraph/index.py:731-903).  A reference index that
-    carries a date table, verdicts or initial-case aliases (policies this engine does not
-    serve) is refused."""
+    file per array and kg-index.json, src/xgraph/index.py:731-903), with its date table and
+    verdict entities.  A reference index that carries initial-case aliases (a policy this
+    engine does not serve) is refused."""
     directory = Path(directory)
     header = json.loads((directory / "kg-index.json").read_text(encoding="utf-8"))
     if header.get("format") == REFERENCE_INDEX_FORMAT:
@@ -671,16 +698,17 @@ def load_kg_index(directory: str | Path) -> KGIndex:
         adjacency_offsets=data["adjacency_offsets"], edge_relations=data["edge_relations"],
         edge_objects=data["edge_objects"], unwritable_triples=header["unwritable_triples"],
         span_syntax=syntax, sitelinks=data["sitelinks"] if "sitelinks" in data else None,
-        base_fingerprint=header["base_fingerprint"],
+        date_entities=data["date_entities"] if "date_entities" in data else None,
+        date_keys=data["date_keys"] if "date_keys" in data else None,
+        verdicts=header.get("verdicts"), base_fingerprint=header["base_fingerprint"],
     )
 
 
 def _load_reference_index(directory: Path, header: dict) -> KGIndex:
     """The reference's saved index (format 1) as this library's KGIndex; its recorded base
     fingerprint is kept when it has one, else this library's is computed."""
-    for key in ("dates", "verdicts", "initial_case_aliases"):
-        if header.get(key):
-            raise ValueError(f"{directory}: the index carries {key}, which this engine does not serve")
+    if header.get("initial_case_aliases"):
+        raise ValueError(f"{directory}: the index carries initial_case_aliases, which this engine does not serve")
 
     def array(name: str) -> np.ndarray:
         file = directory / f"{name}.npy"
@@ -703,17 +731,25 @@ def _load_reference_index(directory: Path, header: dict) -> KGIndex:
     labels, relations = part("labels"), part("relations")
     offsets, edge_rel, edge_obj = array("adjacency_offsets"), array("edge_relations"), array("edge_objects")
     sitelinks = array("sitelinks") if header.get("sitelinks") else None
-    fingerprint = header.get("base_fingerprint") or _fingerprint({
+    dates = (array("date_entities"), array("date_keys")) if header.get("dates") else None
+    parts = {
         "labels.tokens": labels.tokens, "labels.offsets": labels.offsets, "labels.owners": labels.owners,
         "labels.ids": list(labels.owner_ids), "relations.tokens": relations.tokens,
         "relations.offsets": relations.offsets, "relations.owners": relations.owners,
         "relations.ids": list(relations.owner_ids), "adjacency_offsets": offsets, "edge_relations": edge_rel,
         "edge_objects": edge_obj, "tokenizer": header["tokenizer_fingerprint"], "syntax": repr(syntax),
         "sitelinks": sitelinks if sitelinks is not None else "none",
-    })
+    }
+    if dates is not None:
+        parts["date_entities"], parts["date_keys"] = dates
+    if header.get("verdicts") is not None:
+        parts["verdicts"] = header["verdicts"]
+    fingerprint = header.get("base_fingerprint") or _fingerprint(parts)
     return KGIndex(labels=labels, relations=relations, adjacency_offsets=offsets, edge_relations=edge_rel,
                    edge_objects=edge_obj, unwritable_triples=header["unwritable_triples"], span_syntax=syntax,
-                   sitelinks=sitelinks, base_fingerprint=fingerprint)
+                   sitelinks=sitelinks, date_entities=None if dates is None else dates[0],
+                   date_keys=None if dates is None else dates[1], verdicts=header.get("verdicts"),
+                   expressions=bool(header.get("expressions", False)), base_fingerprint=fingerprint)
 
 
 def main(argv: list[str] | None = None) -> None:
