@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define XG_ABI_VERSION 3
+#define XG_ABI_VERSION 4
 
 #if defined(__GNUC__)
 #define XG_API __attribute__((visibility("default")))
@@ -109,8 +109,8 @@ typedef struct XgLayout {
 } XgLayout;
 
 /* Span-language policies, as the reference Engine's constructor flags
- * (src/xgraph/engine.py:582-623).  Expressions, STOP, observation, menu and audit policies
- * are not part of this engine.
+ * (src/xgraph/engine.py:582-623).  Observation, menu and audit policies are not part of
+ * this engine (residual-goal STOP: xg_enable_stop).
  *
  * The logit policies of apply_mask (and of the sync_apply steps, which include it), as the
  * native Engine's arguments (csrc/engine.cu:2601, 2668-2671):
@@ -138,6 +138,12 @@ typedef struct XgOptions {
    * xg_set_relation_successors).  1 and 2 need path mode and no STOP; a closed plan is
    * unresolved (last_kind 6) and binds nothing. */
   int32_t relations;
+  /* 1: expressions, the date and value comparisons, as the reference Engine's
+   * `expressions` (src/xgraph/engine.py:655-664, csrc/engine.cu:374-391): a span may be
+   * `⟦ earlier: A | B · r⟧` (or later:, same:); needs committed paths, escapes and frontier
+   * support, and its tables from xg_set_expressions before the first sync.  Each slot's
+   * memory then holds an operand region after its relation bitmap. */
+  int32_t expressions;
 } XgOptions;
 
 typedef struct XgInfo {
@@ -231,6 +237,26 @@ XG_API int xg_set_stop(XgEngine* engine, int32_t slot, const int32_t* relations,
  * first step; XG_EINVAL unless the engine was created with relations = 2, with more than
  * 10,304 relations, or with fewer tables than 1 + the built-in versions. */
 XG_API int xg_set_relation_successors(XgEngine* engine, const uint32_t* tables, int32_t table_count);
+/* The expression tables (the reference engine's native tables operand_*, operator<k>_*,
+ * operator_lcp, date_entities / date_lo / date_hi / date_keys and verdict_entities,
+ * src/xgraph/engine.py:345-360, 500-530, csrc/engine.cu:2745-2792), from host memory:
+ *   delimiters      int32 [delimiter_ints]: the operand separator's token lists, then each
+ *                   offered operator's (written after the label prefix, so with it in
+ *                   front), one after another, each as its length L (1..64), its L + 1 CSR
+ *                   offsets over byte positions, its tokens (ascending per position) and
+ *                   each token's next byte position (L: the delimiter complete);
+ *   operators       how many operators are offered (1..4; the value comparison, the third,
+ *                   only with the verdict entities);
+ *   operator_lcp    int32 [operators][operators]: the leading bytes two operators share;
+ *   date_entities   int32 [dates]: the date entities' positions, ascending;
+ *   date_keys       int32 [dates]: their dates, packed (year << 11 | month << 7 | day << 2 |
+ *                   precision; 0 for an unstated month or day);
+ *   verdicts        int32 [2]: the verdict entities' positions (yes, no), or null.
+ * Copied to the device (synchronously) before the first step; XG_EINVAL unless the engine
+ * was created with expressions = 1, or for malformed tables. */
+XG_API int xg_set_expressions(XgEngine* engine, const int32_t* delimiters, int64_t delimiter_ints, int32_t operators,
+                              const int32_t* operator_lcp, const int32_t* date_entities, const int32_t* date_keys,
+                              int32_t dates, const int32_t* verdicts);
 /* Engine::advance (csrc/engine.cu:3041-3054): advance slots 0..count-1 by tokens[i];
  * tokens_on_host != 0 means host memory (copied first). */
 XG_API int xg_advance(XgEngine* engine, const int32_t* tokens, int32_t count, int32_t tokens_on_host,

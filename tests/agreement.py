@@ -20,6 +20,8 @@ def last_span(record) -> tuple | None:
     closed = record["last_span"]
     if closed is None:
         return None
+    if closed.get("operator"):  # a comparison: its result (the operands are checked apart)
+        return ("comparison", tuple(closed["entity_ids"]), ())
     if not closed["resolved"]:  # an escape (no labels) or a plan under a weaker relation support
         return ("relation plan" if closed["labels"] else "unresolved", (), ())
     if not closed["triples"] and len(closed["labels"]) > 1:

@@ -48,6 +48,8 @@ def library():
     lib.xgs_enable_stop.restype = None
     lib.xgs_set_stop.argtypes = [p, i32, p, p, i32, p, i32]
     lib.xgs_set_stop.restype = None
+    lib.xgs_set_expressions.argtypes = [p, p, ctypes.c_int64, i32, p, p, p, i32, p]
+    lib.xgs_set_expressions.restype = i32
     return lib
 
 
@@ -57,7 +59,7 @@ class SeamEngine:
     def __init__(self, index, tokenizer, syntax, slots, *, versions=None, escapes=True, repeats=True,
                  derivation=False, paths=False, bound_escapes=True, committed_paths=False,
                  start_rank="degree", unquoted_starts=False, end_after_answer=False, eos_token_ids=(),
-                 relations="frontier"):
+                 relations="frontier", expressions=False):
         self.lib = library()
         self.index, self.versions = index, versions
         self.tables = pack_tables(index, tokenizer, syntax, escapes=escapes, versions=versions,
@@ -68,10 +70,18 @@ class SeamEngine:
                                  committed_paths=int(committed_paths),
                                  sitelinks_rank=int(start_rank == "sitelinks"),
                                  end_after_answer=int(end_after_answer), release_log_mass=-np.inf,
-                                 relations=RELATIONS.index(relations))
+                                 relations=RELATIONS.index(relations), expressions=int(expressions))
         self.slots = slots
         self.handle = self.lib.xgs_create(self.tables.blob.ctypes.data_as(ctypes.c_void_p),
                                           ctypes.byref(self.tables.layout), ctypes.byref(self.options), slots)
+        if expressions:
+            from xgraph_b200.tables import expression_tables
+
+            self._expr = expression_tables(index, tokenizer, syntax)
+            delims, operators, lcp, entities, keys, verdicts = self._expr
+            ptr = lambda a: None if a is None else a.ctypes.data_as(ctypes.c_void_p)  # noqa: E731
+            assert self.lib.xgs_set_expressions(self.handle, ptr(delims), len(delims), operators, ptr(lcp),
+                                                ptr(entities), ptr(keys), len(entities), ptr(verdicts)) == 0
         if relations == "successor":
             self._successors = np.ascontiguousarray(relation_successors(index, versions), dtype=np.uint32)
             self.lib.xgs_set_successors(self.handle, self._successors.ctypes.data_as(ctypes.c_void_p),

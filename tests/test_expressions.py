@@ -5,7 +5,8 @@ The fixture (tests/golden/make_expression_cases.py) holds walks of the reference
 path mode with committed paths and expressions on, with every state and allowed set, on
 four golden worlds with seeded date tables (three of them with the verdict entities, two
 with KG versions).  CPU: the index's date table and verdicts; the oracle reproduces every
-walk."""
+walk; the engine's per-row logic (core.cuh, host seam) reproduces every walk.  The same
+walks through the CUDA engine: tests/test_z_expressions_gpu.py."""
 
 from __future__ import annotations
 
@@ -147,3 +148,51 @@ def test_expressions_need_committed_paths_and_escapes():
 
     with pytest.raises(ValueError, match="date table"):
         Oracle(world_index("toy", False), served, SpanSyntax(), paths=True, committed_paths=True, expressions=True)
+
+
+def check_operator_fields(record: dict, states: dict, slot: int, view, where) -> None:
+    """The expression fields the agreement projection leaves out: the operator branch's
+    byte position, the span's operator, and a closed comparison's operands."""
+    from xgraph_b200.engine import closed_span
+
+    if record["phase"] == "span":
+        operating = bytes.fromhex(record["operating"]) if record["operating"] else b""
+        assert int(states["op_pos"][slot]) == len(operating), (where, "op_pos")
+        assert int(states["op"][slot]) == record["operator"], (where, "op")
+    span = record["last_span"]
+    if span and span.get("operator"):
+        closed = closed_span(view, states, slot)
+        assert (closed.operator, closed.operands) == (span["operator"], tuple(span["operands"])), where
+
+
+def test_seam_reproduces_the_expression_walks():
+    """The kernels' per-row logic (core.cuh on the host): every mask, state projection and
+    expression field of every walk."""
+    from tests.agreement import assert_agrees, engine_state, expected_state
+    from tests.conftest import unpack
+    from tests.seam import SeamEngine
+    from xgraph_b200.kgversions import build_kg_versions
+    from xgraph_b200.syntax import SpanSyntax
+
+    syntax = SpanSyntax()
+    for case in expression_cases():
+        _, served, _ = world(case["world"])
+        index = dated_index(case["world"])
+        edits = edits_of(case)
+        versions = build_kg_versions(index, edits) if edits else None
+        seam = SeamEngine(index, served, syntax, 1, paths=True, committed_paths=True, versions=versions,
+                          expressions=True)
+        for n, w in enumerate(case["walks"]):
+            seam.begin(0)
+            seam.set_version(0, w["version"])
+            view = seam.view(w["version"])
+            for k in range(len(w["tokens"]) + 1):
+                record = w["states"][k] if k < len(w["tokens"]) else w["final"]
+                allowed = w["allowed"][k] if k < len(w["tokens"]) else w["final_allowed"]
+                where = (case["world"], n, k)
+                assert sorted(unpack(seam.masks()[0], served.vocab_size)) == allowed, where
+                states = seam.states()
+                assert_agrees(expected_state(record, index, syntax), engine_state(states, 0, view), True, where)
+                check_operator_fields(record, states, 0, view, where)
+                if k < len(w["tokens"]):
+                    seam.advance([w["tokens"][k]])

@@ -103,3 +103,51 @@ def test_relation_segment_masks_lie_inside_rel_any_and_the_early_rule_holds():
                     assert oracle.allowed(nxt) <= superset, where
                 state = nxt
     assert relation_states > 500 and fired_a > 100 and fired_b > 50, (relation_states, fired_a, fired_b)
+
+
+def test_early_rule_holds_on_the_expression_walks():
+    """The same two facts on every state of the reference's expression walks (date and value
+    comparisons, tests/golden/make_expression_cases.py): a comparison's relation segment
+    allows only relation label and delimiter tokens, and the rule -- whose separator case
+    leaves out a comparison's operands, whose separator (the operand separator after operand
+    A) the packed delimiter steps do not describe -- leads only into relation segments."""
+    from tests.test_expressions import edits_of, expression_cases, make_oracle
+    from xgraph_b200.syntax import SpanSyntax
+
+    syntax = SpanSyntax()
+    closer, separator = syntax.closer.encode("utf-8"), syntax.separator.encode("utf-8")
+    relation_states = fired = 0
+    for case in expression_cases():
+        superset = rel_any(case["world"], True, False)
+        delims = delimiter_tokens(case["world"], True)
+        _, served, _ = world(case["world"])
+        oracle = make_oracle(case)
+        assert edits_of(case) is None or oracle is not None
+        for n, w in enumerate(case["walks"]):
+            state = oracle.initial_state(w["version"])
+            for step, token in enumerate(w["tokens"]):
+                where = (case["world"], n, step)
+                allowed = oracle.allowed(state)
+                in_span = state.phase.value == "span" and not state.answer_complete
+                if in_span and state.segment.value == "relation":
+                    relation_states += 1
+                    assert allowed <= superset, where
+                rule = False
+                if in_span and token in allowed:
+                    data = served.token_bytes(token)
+                    ctx = oracle._context(state)
+                    if state.segment.value == "relation" and token not in delims:
+                        rule = True
+                    elif (state.segment.value == "subject" and not state.operator) or state.segment.value == "relation":
+                        close = (state.closing + data if state.closing is not None
+                                 else data if ctx.closes else None)
+                        going = state.separating is not None and not ctx.forced
+                        sep = state.separating + data if going else data if ctx.separates else None
+                        rule = close != closer and sep == separator
+                nxt = oracle.advance(state, token)
+                if rule:
+                    fired += 1
+                    assert nxt.phase.value == "span" and nxt.segment.value == "relation", where
+                    assert oracle.allowed(nxt) <= superset, where
+                state = nxt
+    assert relation_states > 100 and fired > 50, (relation_states, fired)

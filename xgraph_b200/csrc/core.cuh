@@ -48,13 +48,14 @@ constexpr int32_t kScratchInts = 2 * kMaxSet + 2 + 2 * kMaxSet + kMaxSet;
 constexpr int32_t kMaxStopWords = 64;    // MAX_STOP_WORDS (src/xgraph/stopping.py:45)
 constexpr int32_t kMaxStopBytes = 4096;  // MAX_STOP_BYTES (src/xgraph/stopping.py:46)
 constexpr int32_t kSparseBlocked = 64;   // blocked tokens an automaton row may list (Tables::sparse)
+constexpr int32_t kMaxOperators = 4;     // expressions: the most operators a syntax may offer
 constexpr int8_t kReject = -1;
 constexpr int8_t kComplete = -2;
 
 enum Phase : int32_t { kFree = 0, kSpan = 1, kEscaped = 2, kError = 3 };
 enum Segment : int32_t { kSubject = 0, kRelation = 1, kObject = 2 };
-// (kComparison is the reference's date comparison, not served; kRelationPlan a path closed
-// under a weaker relation support: its labels written, nothing executed)
+// (kComparison a date or value comparison of expressions; kRelationPlan a path closed under
+// a weaker relation support: its labels written, nothing executed)
 enum Closed : int32_t { kNone = 0, kUnresolved = 1, kEntitySpan = 2, kFactSpan = 3, kPathSpan = 4, kComparison = 5,
                         kRelationPlan = 6 };
 // Relation support of a path's relation segments (src/xgraph/relations.py:18): the entity
@@ -80,6 +81,31 @@ enum MemoryField : int32_t {
   kMemPendingFirst = kMemPendingRank + kMaxSet,  //   and first label rows
   kMemHave = kMemPendingFirst + kMaxSet,         // relation bitmap
 };
+
+// Expressions: a comparison's operand region of slot memory, at Tables::mem_operand (after
+// the relation bitmap): operand B's frontier (entities, start ranks, count), each operand's
+// ranked starts (entity of rank k), operand A's best values of a value comparison (a
+// label row or a date key, and whether it is a date), and operand B's relation bitmap.
+enum OperandField : int32_t {
+  kOpFrontEnt = 0,
+  kOpFrontRank = kOpFrontEnt + kMaxSet,
+  kOpStartsA = kOpFrontRank + kMaxSet,
+  kOpStartsB = kOpStartsA + kMaxSet,
+  kOpFrontCount = kOpStartsB + kMaxSet,
+  kOpValues = kOpFrontCount + 4,
+  kOpDated = kOpValues + kMaxSet,
+  kOpHave = kOpDated + kMaxSet,  // + relation words (rounded up to 4)
+};
+
+// Slot memory ints: the fixed fields and the relation bitmap, and with expressions the
+// operand region after them (its offset: the ints without it).
+#if defined(__CUDACC__)
+__host__ __device__
+#endif
+inline int32_t memory_ints_for(int32_t relation_words, bool expressions) {
+  const int32_t words4 = (relation_words + 3) & ~3;
+  return kMemHave + words4 + (expressions ? kOpHave + words4 : 0);
+}
 
 struct Key {
   uint64_t a;
@@ -167,6 +193,23 @@ struct Tables {
   int32_t relation_mode;
   const uint32_t* successors;
   int32_t successor_tables;
+  // expressions (operator_count 0: off): the operators offered, each after the label prefix
+  // (the third, the value comparison, only with the verdict entities), operator_lcp[k * 4 +
+  // j] the leading bytes operators k and j share, and the operand separator; the date table
+  // (the date entities' positions, sorted, with their keys and interval bounds, packed as
+  // xgraph_b200.dates packs them); the verdict entities (yes, no); and the offset of each
+  // slot's operand region in its memory.
+  int32_t operator_count;
+  int32_t operator_lcp[kMaxOperators * kMaxOperators];
+  Delim operators[kMaxOperators];
+  Delim operand_sep;
+  const int32_t* date_entities;
+  const int32_t* date_keys;
+  const int32_t* date_lo;
+  const int32_t* date_hi;
+  int32_t date_count;
+  int32_t verdict_yes, verdict_no;
+  int32_t mem_operand;
   // apply_mask's logit policies (off: release_on 0, escape_bias 0): release a span row to
   // the escape marker when its log allowed mass is below release_log_mass, or (release_top)
   // when its own top token is disallowed; add escape_bias to the tokens that commit to it.
@@ -756,10 +799,14 @@ XG_HD bool kept_row(const Tables& t, int32_t row) {
   return !t.kept_prefix || t.kept_prefix[row + 1] > t.kept_prefix[row];
 }
 
-// The last closed span was a path: the next span is its answer.
+// The last closed span was a path (or a plan or comparison): the next span is its answer.
 XG_HD bool answers_path(const Tables& t, const XgState& s) {
-  return t.paths && (s.last_kind == kPathSpan || s.last_kind == kRelationPlan);
+  return t.paths && (s.last_kind == kPathSpan || s.last_kind == kRelationPlan || s.last_kind == kComparison);
 }
+
+// Expressions: the span writes a comparison's operand A (its separator is the operand
+// separator).
+XG_HD bool operand_a(const XgState& s) { return s.op != 0 && s.segment == kSubject && s.operand == 0; }
 
 // Whether some candidate row of the state's segment lies in [lo, hi)
 // (src/xgraph/oracle.py:830-894: _candidates / _segment_candidates).
@@ -872,9 +919,9 @@ XG_HD void for_each_slice_item(const Ctx& c, int32_t count, S slice, I item) {
 
 // Writes the bitmap of relations that the entities entity[0, n) have.  All (entity,
 // relation run) pairs are spread over the lanes (edges for a version's own list).
-XG_COLD void set_have(const Ctx& c, int32_t n, const int32_t* entity) {
+XG_COLD void set_have(const Ctx& c, int32_t n, const int32_t* entity, int32_t* have = nullptr) {
   const Tables& t = c.t;
-  int32_t* have = c.mem + kMemHave;
+  if (have == nullptr) have = c.mem + kMemHave;
   warp_for(c.w, 0, t.relation_words, [&](int32_t i) { have[i] = 0; });
   const int32_t version = version_of(c);
   for_each_slice_item(
@@ -902,12 +949,17 @@ XG_COLD void set_have(const Ctx& c, int32_t n, const int32_t* entity) {
 // most 64 edges were found no cap applies and no sort is needed: the keys stay as found,
 // an entity possibly more than once (once per rank it is reached with).  Every reader
 // treats the list as a set with least ranks, so the duplicates change nothing.
-XG_COLD int32_t next_frontier(const Ctx& c, int32_t rlo, int32_t rhi) {
+// (ents, ranks, count: another frontier than the slot's path frontier, a comparison's
+// operand B.)
+XG_COLD int32_t next_frontier(const Ctx& c, int32_t rlo, int32_t rhi, const int32_t* ents = nullptr,
+                              const int32_t* ranks = nullptr, int32_t count = 0) {
   const Tables& t = c.t;
   const int32_t version = version_of(c);
-  const int32_t* ents = c.mem + kMemFrontierEnt;
-  const int32_t* ranks = c.mem + kMemFrontierRank;
-  const int32_t count = c.mem[kMemFrontier];
+  if (ents == nullptr) {
+    ents = c.mem + kMemFrontierEnt;
+    ranks = c.mem + kMemFrontierRank;
+    count = c.mem[kMemFrontier];
+  }
   const bool folded = version == 0;  // every list is a base-KG slice with folded first rows
   TopSet ts{c.top, 0};
   #pragma unroll 1
@@ -1087,12 +1139,21 @@ XG_COLD int32_t cached_frontier(const Ctx& c, int32_t rlo, int32_t rhi) {
   return next_frontier(c, rlo, rhi);
 }
 
+// Whether some entity of the frontier in c.top[0, n) has triples.
+XG_COLD bool top_goes_on(const Ctx& c, int32_t n) {
+  const Tables& t = c.t;
+  const int32_t version = version_of(c);
+  return warp_any(c.w, 0, n, [&](int32_t i) {
+    const uint32_t known = c.top[i].pad;
+    if (known) return known == 1u;
+    return row_degree(t, version, static_cast<int32_t>(c.top[i].a & 0xffffffffu)) > 0;
+  });
+}
+
 // Whether the flags' "separator after a relation" holds in path mode: some entity of the
 // capped next frontier has triples.  The frontier is kept for the transition that follows.
 XG_COLD bool frontier_goes_on(const Ctx& c, int32_t rlo, int32_t rhi) {
   const int32_t n = next_frontier(c, rlo, rhi);
-  const int32_t version = version_of(c);
-  const Tables& t = c.t;
   int32_t* ranks = c.mem + kMemPendingRank;
   int32_t* firsts = c.mem + kMemPendingFirst;
   warp_for(c.w, 0, n, [&](int32_t i) {
@@ -1105,11 +1166,137 @@ XG_COLD bool frontier_goes_on(const Ctx& c, int32_t rlo, int32_t rhi) {
     c.mem[kMemPendingCount] = n;
   }
   warp_sync();
-  return warp_any(c.w, 0, n, [&](int32_t i) {
-    const uint32_t known = c.top[i].pad;
-    if (known) return known == 1u;
-    return row_degree(t, version, static_cast<int32_t>(c.top[i].a & 0xffffffffu)) > 0;
+  return top_goes_on(c, n);
+}
+
+// ---------------------------------------------------------------------------------------
+// Expressions: date and value comparisons (src/xgraph/oracle.py:104-133, 1680-1737;
+// csrc/engine.cu:547-611, 988-1125 of the reference).
+
+// The date table's index of an entity, or -1 for an entity that is no date.
+XG_HD int32_t date_index(const Tables& t, int32_t entity) {
+  const int32_t at = lower_index(t.date_entities, 0, t.date_count, entity);
+  return at < t.date_count && t.date_entities[at] == entity ? at : -1;
+}
+
+XG_HD int32_t delim_step(const Delim& d, int32_t pos, int32_t token);
+
+XG_HD uint32_t ordered(int32_t x) { return static_cast<uint32_t>(x) ^ 0x80000000u; }  // signed order as unsigned
+XG_HD int32_t unordered(uint32_t x) { return static_cast<int32_t>(x ^ 0x80000000u); }
+
+// The operator branch after `token` from byte position `pos` (bytes so far those of
+// operator `kind`): the new position, with `kind` the first operator the bytes still fit,
+// or -1 (src/xgraph/oracle.py:1097-1101; csrc/engine.cu:604-617).
+XG_HD int32_t operator_step(const Tables& t, int32_t pos, int32_t& kind, int32_t token) {
+  const int32_t from = kind;
+  #pragma unroll 1
+  for (int32_t j = 0; j < t.operator_count; ++j) {
+    if (pos > 0 && t.operator_lcp[from * kMaxOperators + j] < pos) continue;
+    const int32_t next = delim_step(t.operators[j], pos, token);
+    if (next >= 0) {
+      kind = j;
+      return next;
+    }
+  }
+  return -1;
+}
+
+// An operator may start here: the first token of an unbound span's subject, no operator yet
+// (src/xgraph/oracle.py:1669-1678).
+XG_HD bool may_operate(const Ctx& c, const XgState& s) {
+  return c.t.operator_count > 0 && s.segment == kSubject && s.op == 0 && s.lo >= 0 && s.depth == 0 &&
+         reached_count(c) == 0;
+}
+
+// The next frontier of a comparison's operand k through relation-label rows [rlo, rhi)
+// into c.top (operand A's from the separator test's cache when it holds it).
+XG_COLD int32_t operand_next(const Ctx& c, int32_t k, int32_t rlo, int32_t rhi) {
+  if (k == 0) return cached_frontier(c, rlo, rhi);
+  const int32_t* op = c.mem + c.t.mem_operand;
+  return next_frontier(c, rlo, rhi, op + kOpFrontEnt, op + kOpFrontRank, op[kOpFrontCount]);
+}
+
+// The least (start rank, first day, last day) over the dated entities of the frontier in
+// c.top[0, n) (Key.a: rank and first day, b: last day, both in signed order); max_key()
+// when none is a date.
+XG_COLD Key dated_pick(const Ctx& c, int32_t n) {
+  const Tables& t = c.t;
+  return warp_min(c.w, 0, n, [&](int32_t i) {
+    const int32_t at = date_index(t, t.ent.owner[static_cast<int32_t>(c.top[i].a & 0xffffffffu)]);
+    if (at < 0) return max_key();
+    return Key{((c.top[i].a >> 32) << 32) | ordered(t.date_lo[at]), ordered(t.date_hi[at]), 0u};
   });
+}
+
+// A value comparison's operand values: the entities of the least rank in the frontier in
+// c.top[0, n) (n > 0), each a label row (first row) or, for a date, its date key, into
+// values / dated; returns how many, with `rank` the least rank.
+XG_COLD int32_t best_values(const Ctx& c, int32_t n, int32_t* values, int32_t* dated, int32_t& rank) {
+  const Tables& t = c.t;
+  const int32_t m = keep_least_rank(c, n);
+  rank = static_cast<int32_t>(c.top[0].a >> 32);
+  warp_for(c.w, 0, m, [&](int32_t i) {
+    const int32_t row = static_cast<int32_t>(c.top[i].a & 0xffffffffu);
+    const int32_t at = date_index(t, t.ent.owner[row]);
+    values[i] = at >= 0 ? t.date_keys[at] : row;
+    dated[i] = at >= 0 ? 1 : 0;
+  });
+  warp_sync();
+  return m;
+}
+
+XG_COLD int32_t compare(const Ctx& c, int32_t op, int32_t lo, int32_t hi, int32_t& a, int32_t& b);
+
+// A comparison's relation label: both frontiers must go on for the separator, and it
+// closes where it has a result.
+XG_COLD void comparison_flags(const Ctx& c, const XgState& s, bool& separates, bool& closes) {
+  if (separates) separates = top_goes_on(c, operand_next(c, 1, s.lo, s.ex_hi));
+  int32_t a = 0, b = 0;
+  closes = compare(c, s.op, s.lo, s.ex_hi, a, b) >= 0;
+}
+
+// A comparison closed after the relation-label rows [lo, hi): -1 where it cannot close,
+// else its result -- 1 operand A's start, 2 operand B's, 3 both (undetermined), 4 the
+// verdict yes, 5 no -- with a and b the start entities the operands commit to
+// (src/xgraph/oracle.py:1680-1737).
+XG_COLD int32_t compare(const Ctx& c, int32_t op, int32_t lo, int32_t hi, int32_t& a, int32_t& b) {
+  const Tables& t = c.t;
+  int32_t* mem = c.mem + t.mem_operand;
+  if (op == 3) {  // a value comparison: each operand's best start with any value
+    int32_t rank_a = 0, rank_b = 0;
+    const int32_t na = operand_next(c, 0, lo, hi);
+    if (na == 0) return -1;
+    const int32_t ma = best_values(c, na, mem + kOpValues, mem + kOpDated, rank_a);
+    const int32_t nb = operand_next(c, 1, lo, hi);
+    if (nb == 0) return -1;
+    int32_t* values_b = c.scratch;
+    int32_t* dated_b = c.scratch + kMaxSet;
+    const int32_t mb = best_values(c, nb, values_b, dated_b, rank_b);
+    const int32_t* values_a = mem + kOpValues;
+    const int32_t* dated_a = mem + kOpDated;
+    const bool entities_a = warp_any(c.w, 0, ma, [&](int32_t i) { return dated_a[i] == 0; });
+    const bool entities_b = warp_any(c.w, 0, mb, [&](int32_t i) { return dated_b[i] == 0; });
+    if (entities_a != entities_b) return -1;  // values of two kinds
+    a = mem[kOpStartsA + rank_a];
+    b = mem[kOpStartsB + rank_b];
+    const bool shared = warp_any(c.w, 0, ma * mb, [&](int32_t p) {
+      const int32_t i = p / mb, j = p % mb;
+      return dated_a[i] == dated_b[j] && values_a[i] == values_b[j];
+    });
+    return shared ? 4 : 5;
+  }
+  // a date comparison: each operand's best start that reaches a date, its earliest date
+  const Key pa = dated_pick(c, operand_next(c, 0, lo, hi));
+  if (is_max(pa)) return -1;
+  const Key pb = dated_pick(c, operand_next(c, 1, lo, hi));
+  if (is_max(pb)) return -1;
+  a = mem[kOpStartsA + static_cast<int32_t>(pa.a >> 32)];
+  b = mem[kOpStartsB + static_cast<int32_t>(pb.a >> 32)];
+  const int32_t lo_a = unordered(static_cast<uint32_t>(pa.a & 0xffffffffu)), hi_a = unordered(pa.b);
+  const int32_t lo_b = unordered(static_cast<uint32_t>(pb.a & 0xffffffffu)), hi_b = unordered(pb.b);
+  const bool a_first = hi_a < lo_b, b_first = hi_b < lo_a;
+  if (op == 1) return a_first ? 1 : b_first ? 2 : 3;  // earlier
+  return a_first ? 2 : b_first ? 1 : 3;               // later
 }
 
 // ---------------------------------------------------------------------------------------
@@ -1277,7 +1464,8 @@ XG_SHARED void set_flags(const Ctx& c, XgState& s) {
   s.ex_hi = s.depth == 0 ? s.lo : bound_row(c.w, rows, s.lo, s.hi, s.depth, 0, false);
   const bool bound = s.segment == kSubject && !unbound(t, c, s);
   if (has_candidate(c, s, s.lo, s.ex_hi)) {
-    bool closes = s.segment != kRelation || t.paths;
+    // a comparison closes only after a relation label, where it has a result (below)
+    bool closes = (s.segment != kRelation || t.paths) && s.op == 0;
     if (closes && s.segment == kObject && !t.repeats) {
       const int32_t* facts = c.mem + kMemFactRows;
       const int32_t subj = s.subj_key, rel = s.rel_lo, obj = s.lo;
@@ -1285,7 +1473,6 @@ XG_SHARED void set_flags(const Ctx& c, XgState& s) {
         return facts[3 * i] == subj && facts[3 * i + 1] == rel && facts[3 * i + 2] == obj;
       });
     }
-    if (closes) s.flags |= kMayClose;
     bool separates = false;
     if (s.segment == kSubject) {
       const int32_t version = version_of(c);
@@ -1296,13 +1483,15 @@ XG_SHARED void set_flags(const Ctx& c, XgState& s) {
       separates = !t.paths || (s.hops < kMaxHops && (t.relation_mode != kFrontierSupport
                                                          ? relation_goes_on(c, s.lo, s.ex_hi)
                                                          : frontier_goes_on(c, s.lo, s.ex_hi)));
+      if (s.op != 0) comparison_flags(c, s, separates, closes);
       // residual-goal STOP (src/xgraph/oracle.py:1081-1111): only the closer or the label
       // goes on (neither the separator nor the escape marker starts or goes on)
-      if (closes && t.stop_on != nullptr && residual_goal_stop(c, s)) {
+      if (closes && s.op == 0 && t.stop_on != nullptr && residual_goal_stop(c, s)) {
         s.flags |= kStop;
         separates = false;
       }
     }
+    if (closes) s.flags |= kMayClose;
     if (separates) s.flags |= kMaySep;
   }
   // escape (src/xgraph/oracle.py:1874-1883): a bound subject escapes only with bound_escapes
@@ -1317,6 +1506,7 @@ XG_HD void clear_span(XgState& s) {
   s.sep_pos = s.sep_lo = s.sep_hi = 0;
   s.esc_pos = 0;
   s.subj_lo = s.subj_hi = s.rel_lo = s.rel_hi = s.subj_key = s.hops = 0;
+  s.op_pos = s.op_kind = s.op = s.operand = 0;
   s.ex_hi = 0;
   s.flags = 0;
 }
@@ -1380,8 +1570,13 @@ XG_COLD void next_segment(const Ctx& c, XgState& s, int32_t llo, int32_t lhi) {
 #endif
       }
       if (ts.pushed > 1) top_compact(c.w, ts, kDistinct);  // one key or none: nothing to order
-      int32_t* ents = c.mem + kMemFrontierEnt;
-      int32_t* ranks = c.mem + kMemFrontierRank;
+      // a comparison's operand B ranks its starts into the operand region (operand A's
+      // frontier stays the path frontier); each operand keeps its ranked starts
+      int32_t* op = c.mem + t.mem_operand;
+      const bool second = s.op != 0 && s.operand == 1;
+      int32_t* ents = second ? op + kOpFrontEnt : c.mem + kMemFrontierEnt;
+      int32_t* ranks = second ? op + kOpFrontRank : c.mem + kMemFrontierRank;
+      int32_t* starts = s.op == 0 ? nullptr : op + (second ? kOpStartsB : kOpStartsA);
       const int32_t n = ts.n;
       warp_for(c.w, 0, n, [&](int32_t i) {
         if (t.committed) {
@@ -1391,11 +1586,36 @@ XG_COLD void next_segment(const Ctx& c, XgState& s, int32_t llo, int32_t lhi) {
           ents[i] = t.ent.owner[static_cast<int32_t>(c.top[i].a & 0xffffffffu)];
           ranks[i] = 0;
         }
+        if (starts) starts[i] = ents[i];
       });
-      mem_store(c, kMemFrontier, n);
-      drop_cached_frontier(c);
+      if (second) {
+        mem_store(c, t.mem_operand + kOpFrontCount, n);
+      } else {
+        mem_store(c, kMemFrontier, n);
+        drop_cached_frontier(c);
+      }
       warp_sync();
-      set_have(c, n, ents);
+      if (s.op != 0 && s.operand == 0) {  // operand A written: operand B follows
+        s.operand = 1;
+        s.op_pos = s.op_kind = 0;
+        s.depth = 0;
+        s.lo = 0;
+        s.hi = t.ent.count;
+        s.close_pos = s.close_lo = s.close_hi = 0;
+        s.sep_pos = s.sep_lo = s.sep_hi = 0;
+        s.esc_pos = 0;
+        set_flags(c, s);
+        return;
+      }
+      if (second) {  // the relations both frontiers have
+        set_have(c, c.mem[kMemFrontier], c.mem + kMemFrontierEnt);
+        set_have(c, n, ents, op + kOpHave);
+        int32_t* have = c.mem + kMemHave;
+        warp_for(c.w, 0, t.relation_words, [&](int32_t w) { have[w] &= op[kOpHave + w]; });
+        warp_sync();
+      } else {
+        set_have(c, n, ents);
+      }
       s.subj_lo = llo;
       s.subj_hi = lhi;
     } else if (t.derivation) {
@@ -1417,7 +1637,7 @@ XG_COLD void next_segment(const Ctx& c, XgState& s, int32_t llo, int32_t lhi) {
     s.segment = kRelation;
     s.hops = 1;
     // STOP: the question words the written start covers (csrc/engine.cu:1872)
-    if (stop_installed(c)) set_stop_used(s, stop_start_words(c, llo));
+    if (stop_installed(c) && s.op == 0) set_stop_used(s, stop_start_words(c, llo));
   } else if (t.paths && t.relation_mode != kFrontierSupport) {
     if (t.relation_mode == kSuccessorSupport) next_support(c, llo, lhi, false);
     s.hops += 1;
@@ -1428,6 +1648,20 @@ XG_COLD void next_segment(const Ctx& c, XgState& s, int32_t llo, int32_t lhi) {
     store_frontier(c, n);
     const int32_t* ents = c.mem + kMemFrontierEnt;
     set_have(c, n, ents);
+    if (s.op != 0) {  // a comparison: operand B's frontier goes on in lock step
+      int32_t* op = c.mem + t.mem_operand;
+      const int32_t nb = operand_next(c, 1, llo, lhi);
+      warp_for(c.w, 0, nb, [&](int32_t i) {
+        op[kOpFrontEnt + i] = t.ent.owner[static_cast<int32_t>(c.top[i].a & 0xffffffffu)];
+        op[kOpFrontRank + i] = static_cast<int32_t>(c.top[i].a >> 32);
+      });
+      mem_store(c, t.mem_operand + kOpFrontCount, nb);
+      warp_sync();
+      set_have(c, nb, op + kOpFrontEnt, op + kOpHave);
+      int32_t* have = c.mem + kMemHave;
+      warp_for(c.w, 0, t.relation_words, [&](int32_t w) { have[w] &= op[kOpHave + w]; });
+      warp_sync();
+    }
     s.hops += 1;
   } else {
     s.rel_lo = llo;
@@ -1435,6 +1669,7 @@ XG_COLD void next_segment(const Ctx& c, XgState& s, int32_t llo, int32_t lhi) {
     s.segment = kObject;
   }
   warp_sync();
+  s.op_pos = s.op_kind = 0;
   s.depth = 0;
   s.lo = 0;
   s.hi = s.segment == kRelation ? t.rel.count : t.ent.count;
@@ -1448,7 +1683,32 @@ XG_COLD void next_segment(const Ctx& c, XgState& s, int32_t llo, int32_t lhi) {
 XG_COLD void close_span(const Ctx& c, XgState& s, int32_t llo, int32_t lhi) {
   const Tables& t = c.t;
   const int32_t version = version_of(c);
-  if (s.segment == kRelation && t.relation_mode != kFrontierSupport) {
+  if (s.segment == kRelation && s.op != 0) {  // a comparison ends (src/xgraph/oracle.py:1115-1130)
+    int32_t a = -1, b = -1;
+    const int32_t result = compare(c, s.op, llo, lhi, a, b);
+    // the result binds the answer: the rows of its entities (both starts, undetermined; the
+    // verdict's entity, a value comparison)
+    const int32_t first = result < 0 ? -1 : result == 2 ? b : result == 4 ? t.verdict_yes
+                                          : result == 5 ? t.verdict_no : a;
+    const int32_t second = result == 3 ? b : -1;
+    int32_t n = 0;
+    for (const int32_t e : {first, second}) {  // (an entity without label rows binds nothing)
+      const int32_t row = e >= 0 && e < t.entities ? t.ent_first_row[e] : -1;
+      if (row < 0) continue;
+      if (c.w.leader()) c.top[n] = Key{static_cast<uint32_t>(row), 0u, 0u};
+      ++n;
+    }
+    warp_sync();
+    reach_rows_of_top(c, n);
+    drop_cached_frontier(c);
+    warp_sync();
+    s.last_kind = kComparison;
+    s.last_lo = a;
+    s.last_hi = b;
+    s.last_subj_lo = result;
+    s.last_subj_hi = s.op;
+    s.last_rel_lo = s.last_rel_hi = 0;
+  } else if (s.segment == kRelation && t.relation_mode != kFrontierSupport) {
     // a plan under a weaker support: unresolved, nothing executed or bound
     // (src/xgraph/oracle.py:1138-1147)
     if (c.w.leader()) c.mem[kMemReached] = c.mem[kMemFrontier] = 0;
@@ -1550,12 +1810,40 @@ XG_HD int32_t delim_next(const Tables& t, uint64_t packed, int32_t which, int32_
   return delim_step(which == 0 ? t.closer : which == 1 ? t.separator : t.escape, pos, token);
 }
 
+// Expressions, out of the per-token path (most engines have none): the operand
+// separator's step, the operator branch after a token (alive, or starting at an unbound
+// span's first token; kind: the operator the bytes fit), and the span after a complete
+// operator (src/xgraph/oracle.py:1097-1101, 1235-1246).
+XG_COLD int32_t operand_sep_step(const Tables& t, int32_t pos, int32_t token) {
+  return delim_step(t.operand_sep, pos, token);
+}
+
+XG_COLD int32_t operator_branch(const Ctx& c, const XgState& s, int32_t token, int32_t& kind) {
+  if (s.op_pos > 0) return operator_step(c.t, s.op_pos, kind, token);
+  if (!may_operate(c, s)) return -1;
+  kind = 0;
+  return operator_step(c.t, 0, kind, token);
+}
+
+XG_COLD void start_operand_a(const Ctx& c, XgState& s, int32_t kind) {
+  clear_span(s);
+  s.pos = 0;
+  s.hi = c.t.ent.count;
+  s.op = kind + 1;
+  s.stop_used_lo = s.stop_used_hi = 0;
+  set_flags(c, s);
+}
+
 // One token inside a span (src/xgraph/oracle.py:896-1263, in-scope branches).
 XG_HD void advance_span(const Ctx& c, XgState& s, int32_t token) {
   const Tables& t = c.t;
-  int32_t close = -1, sep = -1, esc = -1;
+  int32_t close = -1, sep = -1, esc = -1, op = -1, op_kind = s.op_kind;
   int32_t close_lo = s.close_lo, close_hi = s.close_hi, sep_lo = s.sep_lo, sep_hi = s.sep_hi;
   const uint64_t packed = t.dstep ? t.dstep[token] : 0u;
+  // expressions: operand A of a comparison takes the operand separator in the separator's
+  // place
+  const bool first_operand = t.operator_count > 0 && operand_a(s);
+  const int32_t sep_len = first_operand ? t.operand_sep.len : t.separator.len;
   if (s.close_pos > 0) {
     close = delim_next(t, packed, 0, s.close_pos, token);
   } else if (s.flags & kMayClose) {
@@ -1564,12 +1852,13 @@ XG_HD void advance_span(const Ctx& c, XgState& s, int32_t token) {
     close_hi = s.ex_hi;
   }
   if (s.sep_pos > 0 && !(s.flags & kStop)) {
-    sep = delim_next(t, packed, 1, s.sep_pos, token);
+    sep = first_operand ? operand_sep_step(t, s.sep_pos, token) : delim_next(t, packed, 1, s.sep_pos, token);
   } else if (s.flags & kMaySep) {
-    sep = delim_next(t, packed, 1, 0, token);
+    sep = first_operand ? operand_sep_step(t, 0, token) : delim_next(t, packed, 1, 0, token);
     sep_lo = s.lo;
     sep_hi = s.ex_hi;
   }
+  if (t.operator_count > 0) op = operator_branch(c, s, token, op_kind);
   if (s.esc_pos > 0 && !(s.flags & kStop)) {
     esc = delim_next(t, packed, 2, s.esc_pos, token);
   } else if (s.flags & kMayEsc) {
@@ -1587,7 +1876,7 @@ XG_HD void advance_span(const Ctx& c, XgState& s, int32_t token) {
     close_span(c, s, close_lo, close_hi);
     return;
   }
-  if (sep == t.separator.len) {
+  if (sep == sep_len) {
     next_segment(c, s, sep_lo, sep_hi);
     return;
   }
@@ -1595,7 +1884,11 @@ XG_HD void advance_span(const Ctx& c, XgState& s, int32_t token) {
     end_span(s, kEscaped);
     return;
   }
-  if (lo < 0 && close < 0 && sep < 0 && esc < 0) {
+  if (op >= 0 && op == t.operators[op_kind].len) {
+    start_operand_a(c, s, op_kind);
+    return;
+  }
+  if (lo < 0 && close < 0 && sep < 0 && esc < 0 && op < 0) {
     s.phase = kError;
     return;
   }
@@ -1606,6 +1899,8 @@ XG_HD void advance_span(const Ctx& c, XgState& s, int32_t token) {
   s.sep_lo = sep > 0 ? sep_lo : 0;
   s.sep_hi = sep > 0 ? sep_hi : 0;
   s.esc_pos = esc > 0 ? esc : 0;
+  s.op_pos = op > 0 ? op : 0;
+  s.op_kind = op > 0 ? op_kind : 0;
   if (lo >= 0) {
     s.lo = lo;
     s.hi = hi;
@@ -1713,18 +2008,21 @@ XG_HD const uint32_t* wide_mask(const Tables& t, int32_t lo, int32_t depth) {
 // The tokens that continue the closer, separator and escape branches from byte positions
 // close, sep and esc (-1: that branch is not live), as one lane-parallel loop over the
 // three token lists (their loads issue together).
-XG_SHARED void add_delimiters(const Ctx& c, int32_t close, int32_t sep, int32_t esc, uint32_t* out) {
+// (operand: the separator branch matches the operand separator, a comparison's operand A.)
+XG_SHARED void add_delimiters(const Ctx& c, int32_t close, int32_t sep, int32_t esc, uint32_t* out,
+                              bool operand = false) {
   const Tables& t = c.t;
+  const Delim& sd = operand ? t.operand_sep : t.separator;
   const int32_t a0 = close >= 0 ? delim_begin(t.closer, close) : 0;
   const int32_t n0 = close >= 0 ? delim_end(t.closer, close) - a0 : 0;
-  const int32_t a1 = sep >= 0 ? delim_begin(t.separator, sep) : 0;
-  const int32_t n1 = sep >= 0 ? delim_end(t.separator, sep) - a1 : 0;
+  const int32_t a1 = sep >= 0 ? delim_begin(sd, sep) : 0;
+  const int32_t n1 = sep >= 0 ? delim_end(sd, sep) - a1 : 0;
   const int32_t a2 = esc >= 0 ? delim_begin(t.escape, esc) : 0;
   const int32_t n2 = esc >= 0 ? delim_end(t.escape, esc) - a2 : 0;
   // a branch at its start reads the copied start lists when there is a copy
   const int32_t c0 = t.closer.at[1] - t.closer.at[0], c1 = t.separator.at[1] - t.separator.at[0];
   const int32_t* p0 = c.delim0 && close == 0 ? c.delim0 : t.closer.tok + a0;
-  const int32_t* p1 = c.delim0 && sep == 0 ? c.delim0 + c0 : t.separator.tok + a1;
+  const int32_t* p1 = c.delim0 && sep == 0 && !operand ? c.delim0 + c0 : sd.tok + a1;
   const int32_t* p2 = c.delim0 && esc == 0 ? c.delim0 + c0 + c1 : t.escape.tok + a2;
   warp_for_loaded(
       c.w, 0, n0 + n1 + n2,
@@ -1785,6 +2083,18 @@ XG_COLD void add_label_tokens(const Ctx& c, const XgState& s, uint32_t* out) {
   }
 }
 
+// The tokens that continue the operator branch from its byte position (every operator the
+// bytes so far fit; at position 0 every operator).
+XG_COLD void add_operator_tokens(const Ctx& c, const XgState& s, uint32_t* out) {
+  const Tables& t = c.t;
+  #pragma unroll 1
+  for (int32_t j = 0; j < t.operator_count; ++j) {
+    if (s.op_pos > 0 && t.operator_lcp[s.op_kind * kMaxOperators + j] < s.op_pos) continue;
+    const Delim& d = t.operators[j];
+    warp_for(c.w, delim_begin(d, s.op_pos), delim_end(d, s.op_pos), [&](int32_t i) { set_bit(out, d.tok[i]); });
+  }
+}
+
 // A mask as base | delta (either may be null; both null: the error phase, nothing masked).
 struct MaskRef {
   const uint32_t* base;
@@ -1834,7 +2144,10 @@ XG_HD MaskRef compose_mask(const Ctx& c, const XgState& s, uint32_t* own, bool z
     const bool stop = s.flags & kStop;  // STOP: the separator and the escape marker neither go on nor start
     const int32_t sep = s.sep_pos > 0 && !stop ? s.sep_pos : (s.flags & kMaySep) ? 0 : -1;
     const int32_t esc = s.esc_pos > 0 && !stop ? s.esc_pos : (s.flags & kMayEsc) ? 0 : -1;
-    add_delimiters(c, close, sep, esc, delta);
+    add_delimiters(c, close, sep, esc, delta, t.operator_count > 0 && operand_a(s));
+    // expressions: the tokens that take the operator branch on (from where it stands, or
+    // from its start where an operator may start)
+    if (t.operator_count > 0 && (s.op_pos > 0 || may_operate(c, s))) add_operator_tokens(c, s, delta);
     warp_sync();
   }
   return MaskRef{base, delta};
@@ -1881,12 +2194,69 @@ XG_HD void for_each_escape_commit(const Ctx& c, const XgState& s, F f) {
   for (int32_t i = a; i < b; ++i) {
     const int32_t token = t.escape.tok[i];
     if (close >= 0 && delim_step(t.closer, close, token) >= 0) continue;
-    if (sep >= 0 && delim_step(t.separator, sep, token) >= 0) continue;
+    if (sep >= 0 && delim_step(operand_a(s) ? t.operand_sep : t.separator, sep, token) >= 0) continue;
+    int32_t kind = s.op_kind;
+    if ((s.op_pos > 0 || may_operate(c, s)) && operator_step(t, s.op_pos, kind, token) >= 0) continue;
     int32_t lo = s.lo, hi = s.hi;
     narrow(c.w, rows, lo, hi, s.depth, token);
     if (has_candidate(c, s, lo, hi)) continue;
     f(token);
   }
+}
+
+// ---------------------------------------------------------------------------------------
+// Host side of the expression tables (xg_set_expressions, and the host seam's copy).
+
+// One delimiter list of the packed buffer: where its offsets, tokens and next positions
+// start in the buffer, its length, and its first offsets (Delim::at).
+struct PackedDelim {
+  int64_t off, tok, next;
+  int32_t len;
+  int32_t at[17];
+};
+
+// Parses `count` delimiter lists packed one after another in p[0, ints): each its length
+// (1..64), its len + 1 CSR offsets (from 0, non-decreasing), then its tokens (in [0,
+// vocab), ascending within each byte position) and their next positions (1..len).  False
+// when the buffer is malformed or not used up exactly.
+inline bool parse_packed_delims(const int32_t* p, int64_t ints, int32_t count, int32_t vocab, PackedDelim* out) {
+  int64_t at = 0;
+  for (int32_t k = 0; k < count; ++k) {
+    if (at >= ints) return false;
+    const int32_t len = p[at];
+    if (len < 1 || len > 64 || at + 2 + len > ints) return false;
+    const int64_t off = at + 1;
+    if (p[off] != 0) return false;
+    for (int32_t i = 0; i < len; ++i)
+      if (p[off + i + 1] < p[off + i]) return false;
+    const int64_t n = p[off + len];
+    const int64_t tok = off + len + 1, next = tok + n;
+    if (next + n > ints) return false;
+    for (int32_t i = 0; i < len; ++i) {
+      for (int64_t j = p[off + i]; j < p[off + i + 1]; ++j) {
+        if (p[tok + j] < 0 || p[tok + j] >= vocab || p[next + j] <= i || p[next + j] > len) return false;
+        if (j > p[off + i] && p[tok + j] <= p[tok + j - 1]) return false;
+      }
+    }
+    out[k].off = off;
+    out[k].tok = tok;
+    out[k].next = next;
+    out[k].len = len;
+    for (int32_t i = 0; i < 17; ++i) out[k].at[i] = i <= len ? p[off + i] : 0;
+    at = next + n;
+  }
+  return at == ints;
+}
+
+// A date key's first (first) or last day, packed with precision bits 0 (xgraph_b200.dates
+// date_lo / date_hi).
+inline int32_t date_bound(int32_t key, bool first) {
+  const int64_t k = key;
+  const int64_t year = k >> 11, precision = k & 3;
+  int64_t month = (k >> 7) & 15, day = (k >> 2) & 31;
+  if (precision == 0 || month == 0) month = first ? 1 : 12;
+  if (precision != 2) day = first ? 1 : 31;
+  return static_cast<int32_t>(static_cast<uint32_t>(static_cast<uint64_t>((year << 11) | (month << 7) | (day << 2))));
 }
 
 }  // namespace xg

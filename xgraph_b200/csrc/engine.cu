@@ -1002,8 +1002,8 @@ __global__ void __maxnreg__(kFusedRegisters)
             if (segment == kRelation && packed == 0u &&
                 ((mask_word(base0, delta0, token >> 5) >> (token & 31)) & 1u))
               early_write = true;
-            else if ((segment == kSubject || (segment == kRelation && t.paths)) && close != t.closer.len &&
-                     sep == t.separator.len)
+            else if (((segment == kSubject && stored->op == 0) || (segment == kRelation && t.paths)) &&
+                     close != t.closer.len && sep == t.separator.len)
               early_write = true;
           }
         }
@@ -1427,6 +1427,16 @@ struct XgEngine {
   int32_t* sparse = nullptr;      //   and the automaton rows' blocked-token lists
   uint32_t* successors = nullptr; // successor support's tables (xg_set_relation_successors)
   int32_t successor_tables = 0;
+  // expressions (xg_set_expressions): one device buffer of the packed delimiter lists, then
+  // the date table (entities, keys, first days, last days); the Tables fields they give
+  int32_t* expr = nullptr;
+  int64_t expr_delim_ints = 0;
+  int32_t operator_count = 0;
+  int32_t operator_lcp[kMaxOperators * kMaxOperators] = {};
+  Delim operators[kMaxOperators] = {};
+  Delim operand_sep{};
+  int32_t date_count = 0;
+  int32_t verdict_yes = -1, verdict_no = -1;
   // residual-goal STOP (xg_enable_stop): label words, and per slot: installed flag, relation
   // table, question word offsets and bytes
   int64_t* stop_label_off = nullptr;
@@ -1649,6 +1659,24 @@ int add_version(XgEngine* e, const int32_t* subjects, int32_t count, const int64
   return XG_OK;
 }
 
+// The expression tables' fields of Tables (all zero until xg_set_expressions).  Only these:
+// the rest of Tables keeps what create bound (the delimiters' offsets among it).
+void bind_expressions(XgEngine* e) {
+  Tables& t = e->t;
+  t.operator_count = e->operator_count;
+  for (int32_t k = 0; k < kMaxOperators * kMaxOperators; ++k) t.operator_lcp[k] = e->operator_lcp[k];
+  for (int32_t k = 0; k < kMaxOperators; ++k) t.operators[k] = e->operators[k];
+  t.operand_sep = e->operand_sep;
+  const int32_t* dates = e->expr ? e->expr + e->expr_delim_ints : nullptr;
+  t.date_entities = dates;
+  t.date_keys = dates ? dates + e->date_count : nullptr;
+  t.date_lo = dates ? dates + 2 * e->date_count : nullptr;
+  t.date_hi = dates ? dates + 3 * e->date_count : nullptr;
+  t.date_count = e->date_count;
+  t.verdict_yes = e->verdict_yes;
+  t.verdict_no = e->verdict_no;
+}
+
 void bind_tables(XgEngine* e) {
   const XgLayout& l = e->layout;
   const char* b = e->blob;
@@ -1710,7 +1738,9 @@ void bind_tables(XgEngine* e) {
   t.successor_tables = e->successor_tables;
   t.states = e->states;
   t.memory = e->memory;
-  t.memory_ints = kMemHave + ((l.relation_words + 3) & ~3);
+  t.memory_ints = memory_ints_for(l.relation_words, o.expressions != 0);
+  t.mem_operand = o.expressions ? memory_ints_for(l.relation_words, false) : 0;
+  bind_expressions(e);
   t.masks = e->masks;
   t.base = e->base;
   t.delta = e->delta;
@@ -1741,6 +1771,7 @@ void release(XgEngine* e) {
   cudaFree(e->rel_any_tok);
   cudaFree(e->sparse);
   cudaFree(e->successors);
+  cudaFree(e->expr);
   for (void* p : {static_cast<void*>(e->arena.range), static_cast<void*>(e->arena.subjects),
                   static_cast<void*>(e->arena.adjacency), static_cast<void*>(e->arena.relations),
                   static_cast<void*>(e->arena.objects)})
@@ -1805,6 +1836,12 @@ int create(const void* blob, bool on_device, const XgLayout* layout, const XgOpt
     return fail(XG_EINVAL, "weaker relations need path mode");
   if (options->relations == 2 && layout->relation_words > kScratchInts)
     return fail(XG_EINVAL, "successor support handles at most 10,304 relations");
+  if (options->expressions && (!options->paths || !options->committed_paths))
+    return fail(XG_EINVAL, "expressions need committed paths (committed_paths=True)");
+  if (options->expressions && !options->escapes)
+    return fail(XG_EINVAL, "expressions need escapes, the way out of an operand or relation");
+  if (options->expressions && options->relations != 0)
+    return fail(XG_EINVAL, "weaker relations need path mode without expressions or STOP");
   XgEngine* e = new XgEngine();
   e->layout = *layout;
   e->options = *options;
@@ -1812,7 +1849,7 @@ int create(const void* blob, bool on_device, const XgLayout* layout, const XgOpt
   cudaGetDevice(&e->device);
   cudaDeviceGetAttribute(&e->sm_count, cudaDevAttrMultiProcessorCount, e->device);
   const int64_t slots = max_sequences;
-  const int32_t memory_ints = kMemHave + ((layout->relation_words + 3) & ~3);
+  const int32_t memory_ints = memory_ints_for(layout->relation_words, options->expressions != 0);
   cudaError_t err = cudaSuccess;
   auto alloc = [&](void** p, size_t bytes) {
     if (err == cudaSuccess) err = cudaMalloc(p, bytes > 0 ? bytes : 16);
@@ -2380,6 +2417,68 @@ int xg_set_relation_successors(XgEngine* e, const uint32_t* tables, int32_t tabl
   e->successor_tables = table_count;
   e->t.successors = device;
   e->t.successor_tables = table_count;
+  return XG_OK;
+}
+
+int xg_set_expressions(XgEngine* e, const int32_t* delimiters, int64_t delimiter_ints, int32_t operators,
+                       const int32_t* operator_lcp, const int32_t* date_entities, const int32_t* date_keys,
+                       int32_t dates, const int32_t* verdicts) {
+  if (!e || !delimiters || !operator_lcp || (dates > 0 && (!date_entities || !date_keys)))
+    return fail(XG_EINVAL, "null argument");
+  if (!e->options.expressions) return fail(XG_EINVAL, "expression tables need an engine created with expressions = 1");
+  if (operators < 1 || operators > kMaxOperators)
+    return fail(XG_EINVAL, "expressions offer 1 to 4 operators");
+  if (operators > 2 && !verdicts) return fail(XG_EINVAL, "a value comparison needs the verdict entities, yes and no");
+  if (dates < 0 || delimiter_ints < 1) return fail(XG_EINVAL, "negative table size");
+  PackedDelim parsed[1 + kMaxOperators];
+  if (!parse_packed_delims(delimiters, delimiter_ints, 1 + operators, e->layout.vocab, parsed))
+    return fail(XG_EINVAL, "malformed expression delimiter lists");
+  for (int32_t k = 0; k < operators * operators; ++k)
+    if (operator_lcp[k] < 0 || operator_lcp[k] > 64) return fail(XG_EINVAL, "operator_lcp out of range");
+  for (int32_t i = 0; i < dates; ++i) {
+    if (date_entities[i] < 0 || date_entities[i] >= e->layout.entities || (i > 0 && date_entities[i] <= date_entities[i - 1]))
+      return fail(XG_EINVAL, "date entities must be ascending entity positions");
+  }
+  if (verdicts) {
+    for (int32_t k = 0; k < 2; ++k)
+      if (verdicts[k] < 0 || verdicts[k] >= e->layout.entities) return fail(XG_EINVAL, "verdict entity out of range");
+  }
+  std::vector<int32_t> host(static_cast<size_t>(delimiter_ints) + 4 * static_cast<size_t>(dates));
+  std::memcpy(host.data(), delimiters, delimiter_ints * sizeof(int32_t));
+  int32_t* table = host.data() + delimiter_ints;
+  for (int32_t i = 0; i < dates; ++i) {
+    table[i] = date_entities[i];
+    table[dates + i] = date_keys[i];
+    table[2 * dates + i] = date_bound(date_keys[i], true);
+    table[3 * dates + i] = date_bound(date_keys[i], false);
+  }
+  int32_t* device = nullptr;
+  cudaError_t err = cudaMalloc(reinterpret_cast<void**>(&device), host.size() * sizeof(int32_t));
+  if (err != cudaSuccess) {
+    cudaGetLastError();
+    return fail(XG_ENOMEM, std::string("device allocation failed: ") + cudaGetErrorString(err));
+  }
+  err = cudaMemcpy(device, host.data(), host.size() * sizeof(int32_t), cudaMemcpyHostToDevice);
+  if (err != cudaSuccess) {
+    cudaFree(device);
+    return cuda_fail(err, "expression tables upload");
+  }
+  cudaFree(e->expr);  // (the engine's stream is idle: the copy above synchronized)
+  e->expr = device;
+  e->expr_delim_ints = delimiter_ints;
+  e->operator_count = operators;
+  for (int32_t k = 0; k < kMaxOperators * kMaxOperators; ++k) e->operator_lcp[k] = 0;
+  for (int32_t k = 0; k < operators; ++k)
+    for (int32_t j = 0; j < operators; ++j) e->operator_lcp[k * kMaxOperators + j] = operator_lcp[k * operators + j];
+  for (int32_t k = 0; k <= operators; ++k) {
+    Delim& d = k == 0 ? e->operand_sep : e->operators[k - 1];
+    d = Delim{device + parsed[k].off, device + parsed[k].tok, device + parsed[k].next, parsed[k].len, {}};
+    for (int32_t i = 0; i < 17; ++i) d.at[i] = parsed[k].at[i];
+  }
+  e->date_count = dates;
+  e->verdict_yes = verdicts ? verdicts[0] : -1;
+  e->verdict_no = verdicts ? verdicts[1] : -1;
+  bind_expressions(e);
   return XG_OK;
 }
 

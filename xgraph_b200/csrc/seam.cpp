@@ -30,6 +30,8 @@ struct SeamEngine {
   std::vector<int32_t> stop_on, stop_rel, stop_woff;
   std::vector<uint8_t> stop_words;
   std::vector<uint32_t> successors;  // successor support's tables (xgs_set_successors)
+  // expressions (xgs_set_expressions): the packed delimiter lists, the date table
+  std::vector<int32_t> expr_delims, date_entities, date_keys, date_lo, date_hi;
   Tables t{};
 };
 
@@ -126,7 +128,8 @@ SeamEngine* xgs_create(const void* blob, const XgLayout* l, const XgOptions* o, 
   t.committed = o->committed_paths;
   t.end_after_answer = o->end_after_answer;
   t.relation_mode = o->relations;
-  t.memory_ints = kMemHave + ((l->relation_words + 3) & ~3);
+  t.memory_ints = memory_ints_for(l->relation_words, o->expressions != 0);
+  t.mem_operand = o->expressions ? memory_ints_for(l->relation_words, false) : 0;
   e->states.assign(slots, XgState{});
   e->memory.assign(static_cast<size_t>(slots) * t.memory_ints, 0);
   e->masks.assign(static_cast<size_t>(slots) * l->words_padded, 0u);
@@ -223,6 +226,44 @@ void xgs_memory(SeamEngine* e, int32_t n, int32_t* out) {
 }
 
 int32_t xgs_memory_ints(SeamEngine* e) { return e->t.memory_ints; }
+
+// xg_set_expressions on the host (same arguments); 1 when the tables are malformed.
+int32_t xgs_set_expressions(SeamEngine* e, const int32_t* delimiters, int64_t ints, int32_t operators,
+                            const int32_t* lcp, const int32_t* date_entities, const int32_t* date_keys, int32_t dates,
+                            const int32_t* verdicts) {
+  Tables& t = e->t;
+  PackedDelim parsed[1 + kMaxOperators];
+  if (operators < 1 || operators > kMaxOperators || (operators > 2 && !verdicts) ||
+      !parse_packed_delims(delimiters, ints, 1 + operators, t.vocab, parsed))
+    return 1;
+  e->expr_delims.assign(delimiters, delimiters + ints);
+  const int32_t* base = e->expr_delims.data();
+  for (int32_t k = 0; k <= operators; ++k) {
+    Delim& d = k == 0 ? t.operand_sep : t.operators[k - 1];
+    d = Delim{base + parsed[k].off, base + parsed[k].tok, base + parsed[k].next, parsed[k].len, {}};
+    for (int32_t i = 0; i < 17; ++i) d.at[i] = parsed[k].at[i];
+  }
+  for (int32_t k = 0; k < kMaxOperators * kMaxOperators; ++k) t.operator_lcp[k] = 0;
+  for (int32_t k = 0; k < operators; ++k)
+    for (int32_t j = 0; j < operators; ++j) t.operator_lcp[k * kMaxOperators + j] = lcp[k * operators + j];
+  e->date_entities.assign(date_entities, date_entities + dates);
+  e->date_keys.assign(date_keys, date_keys + dates);
+  e->date_lo.resize(dates);
+  e->date_hi.resize(dates);
+  for (int32_t i = 0; i < dates; ++i) {
+    e->date_lo[i] = date_bound(date_keys[i], true);
+    e->date_hi[i] = date_bound(date_keys[i], false);
+  }
+  t.date_entities = e->date_entities.data();
+  t.date_keys = e->date_keys.data();
+  t.date_lo = e->date_lo.data();
+  t.date_hi = e->date_hi.data();
+  t.date_count = dates;
+  t.verdict_yes = verdicts ? verdicts[0] : -1;
+  t.verdict_no = verdicts ? verdicts[1] : -1;
+  t.operator_count = operators;
+  return 0;
+}
 
 // xg_set_relation_successors on the host.
 void xgs_set_successors(SeamEngine* e, const uint32_t* tables, int32_t count) {

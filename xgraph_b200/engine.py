@@ -23,13 +23,14 @@ from pathlib import Path
 
 import numpy as np
 
-from .index import IndexMismatch, check_start_rank
+from .index import IndexMismatch, check_expressions, check_start_rank
 from .tables import XgLayout, XgOptions, mask_words, pack_mask, pack_tables  # noqa: F401
 
 PHASES = ("free text", "span", "escaped", "error")
 PHASE_ERROR = PHASES.index("error")
 SEGMENTS = ("subject", "relation", "object")
 CLOSED = ("none", "unresolved", "entity span", "fact span", "path span", "comparison", "relation plan")
+COMPARISONS = ("earlier", "later", "same")  # the comparison each operator writes, by position
 MAX_FACTS = 64
 MAX_REACHED = 64
 MAX_DELIMITER_BYTES = 127
@@ -45,7 +46,7 @@ STATE_INTS = 64
 LIBRARY = Path(__file__).resolve().parent / "libxgraph_b200.so"
 
 XG_OK, XG_EINVAL, XG_ECUDA, XG_ENOMEM = 0, 1, 2, 3
-ABI_VERSION = 3
+ABI_VERSION = 4
 """XG_ABI_VERSION of include/xgraph_b200.h that these bindings follow."""
 ADMISSION_INTS = 5 + MAX_REACHED
 """int32 words of one admission record (XgAdmission: slot, on, version, open_span,
@@ -54,7 +55,6 @@ DTYPES = {"float32": 0, "bfloat16": 1, "float16": 2}
 
 # Reference constructor options this engine does not serve, with their neutral values.
 _NOT_SERVED = {
-    "expressions": False,
     "observe": 0, "observe_width": 0,
     "observe_defer": 0, "menu_close_next": False, "observe_select": False,
     "observe_answer": False, "observe_required": False, "observe_no_loop": False,
@@ -115,6 +115,7 @@ def load_library(path: Path = LIBRARY):
         "xg_enable_stop": ([p, p, p, i64], ctypes.c_int),
         "xg_set_stop": ([p, i32, p, i32, p, i32, p, i32, p], ctypes.c_int),
         "xg_set_relation_successors": ([p, p, i32], ctypes.c_int),
+        "xg_set_expressions": ([p, p, i64, i32, p, p, p, i32, p], ctypes.c_int),
         "xg_build_label_rows": ([i32, p, p, i64, p, p, i64, p, i32, i32, p, p, i64, p, p, p, p, p, p, p, p],
                                 ctypes.c_int),
     }
@@ -212,6 +213,7 @@ class Engine:
         eos_token_ids: Iterable[int] = (),
         stop: str | None = None,
         relations: str = "frontier",
+        expressions: bool = False,
         device_blob=None,
         **others,
     ) -> None:
@@ -239,9 +241,16 @@ class Engine:
             raise ValueError(f"unknown STOP rule {stop!r}; expected residual-goal")
         if stop and not committed_paths:
             raise ValueError("residual-goal STOP needs committed paths (committed_paths=True)")
+        # expressions (src/xgraph/engine.py:757-762)
+        if expressions and not committed_paths:
+            raise ValueError("expressions need committed paths (committed_paths=True)")
+        if expressions and not escapes:
+            raise ValueError("expressions need escapes, the way out of an operand or relation")
+        if expressions:
+            check_expressions(index)
         from .relations import RELATIONS, check_relations
 
-        check_relations(relations, paths=paths, stop=stop)
+        check_relations(relations, paths=paths, stop=stop, expressions=expressions)
         self._relations = relations
         sitelinks_rank = check_start_rank(start_rank, index) == "sitelinks"
         if not escapes and (release_mass > 0 or release_top):
@@ -273,6 +282,7 @@ class Engine:
             release_top=int(bool(release_top)),
             release_log_mass=math.log(release_mass) if release_mass > 0 else -math.inf,
             escape_bias=float(escape_bias), relations=RELATIONS.index(relations),
+            expressions=int(bool(expressions)),
         )
         handle = ctypes.c_void_p()
         if device_blob is None:
@@ -286,6 +296,13 @@ class Engine:
                 ctypes.byref(self._options), int(max_sequences), ctypes.byref(handle))
         _check(rc)
         self._handle = handle
+        if expressions:
+            from .tables import expression_tables
+
+            delims, operators, lcp, entities, keys, verdicts = expression_tables(index, tokenizer, syntax)
+            ptr = lambda a: None if a is None else a.ctypes.data_as(ctypes.c_void_p)  # noqa: E731
+            _check(self._lib.xg_set_expressions(self._handle, ptr(delims), len(delims), operators, ptr(lcp),
+                                                ptr(entities), ptr(keys), len(entities), ptr(verdicts)))
         if relations == "successor":
             from .relations import relation_successors
 
@@ -692,8 +709,21 @@ def closed_span(index, states: dict[str, np.ndarray], seq: int) -> ClosedSpanRec
     version's view (Engine.view)."""
     kind = CLOSED[int(states["last_kind"][seq])]
     lo, hi = int(states["last_lo"][seq]), int(states["last_hi"][seq])
+    if kind == "comparison":  # lo, hi: the operands' start entities; subj_lo the result, subj_hi the operator
+        from .dates import VERDICTS
+
+        ids = index.labels.owner_ids
+        result, operator = int(states["last_subj_lo"][seq]), int(states["last_subj_hi"][seq])
+        entities = {1: (ids[lo],), 2: (ids[hi],), 3: tuple(sorted({ids[lo], ids[hi]})),
+                    4: (VERDICTS["yes"],), 5: (VERDICTS["no"],)}[result]
+        return ClosedSpanRecord(kind, entities, (), COMPARISONS[operator - 1], (ids[lo], ids[hi]))
     if kind == "entity span":
-        return ClosedSpanRecord(kind, tuple(sorted(index.labels.owner_id(r) for r in range(lo, hi))))
+        owners = {index.labels.owner_id(r) for r in range(lo, hi)}
+        if int(states["last_subj_lo"][seq]) == -1:  # an unbound span names no verdict entity
+            from .dates import VERDICTS
+
+            owners -= set(VERDICTS.values())
+        return ClosedSpanRecord(kind, tuple(sorted(owners)))
     if kind != "fact span":
         return ClosedSpanRecord(kind)
     subjects = {index.labels.owner_id(r) for r in range(int(states["last_subj_lo"][seq]), int(states["last_subj_hi"][seq]))}

@@ -421,6 +421,19 @@ def _adjacency_device(
                 int(unwritable.value))
 
 
+def check_expressions(index: KGIndex) -> None:
+    """Refuse an index expressions cannot run on (src/xgraph/index.py:686-704): one built
+    for a span syntax without operators, one whose labels may hold expression syntax, one
+    without the date table."""
+    if not index.span_syntax.writes_expressions:
+        raise ValueError("expressions need a KG index built for a span syntax with operators and an "
+                         f"operand separator, not {index.span_syntax}")
+    if not index.expressions:
+        raise ValueError("the KG index was saved before labels holding expression syntax were excluded: rebuild it")
+    if index.date_entities is None:
+        raise ValueError("expressions need a KG index with the date table")
+
+
 def build_kg_index_arrays(
     entities: Sequence[tuple[str, Sequence[str]]],
     relations: Sequence[tuple[str, Sequence[str]]],

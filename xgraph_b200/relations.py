@@ -18,11 +18,11 @@ RELATIONS = ("frontier", "vocabulary", "successor")
 _CHUNK = 1 << 20  # edges joined per round, whatever the KG size
 
 
-def check_relations(mode: str, *, paths: bool, stop: str | None) -> None:
+def check_relations(mode: str, *, paths: bool, stop: str | None, expressions: bool = False) -> None:
     """The reference's checks (src/xgraph/relations.py:24-28), in its words."""
     if mode not in RELATIONS:
         raise ValueError(f"unknown relations mode {mode!r}; expected one of {RELATIONS}")
-    if mode != "frontier" and (not paths or stop):
+    if mode != "frontier" and (not paths or expressions or stop):
         raise ValueError("weaker relations need path mode without expressions or STOP")
 
 

@@ -60,7 +60,8 @@ class XgOptions(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int32) for n in (
         "escapes", "repeats", "derivation", "paths", "bound_escapes", "committed_paths",
         "sitelinks_rank", "end_after_answer", "release_top")] + [
-        ("release_log_mass", ctypes.c_float), ("escape_bias", ctypes.c_float), ("relations", ctypes.c_int32)]
+        ("release_log_mass", ctypes.c_float), ("escape_bias", ctypes.c_float), ("relations", ctypes.c_int32),
+        ("expressions", ctypes.c_int32)]
 
 
 def mask_words(vocab_size: int) -> int:
@@ -334,11 +335,17 @@ def pack_tables(index, tokenizer, syntax, *, escapes: bool, versions=None,
     first_row = np.full(entities, -1, dtype=np.int32)
     has_rows = np.diff(ent_rows_off) > 0
     first_row[has_rows] = ent_rows[ent_rows_off[:-1][has_rows]]
+    # rows no unbound subject names: quoted ones with unquoted starts, and always the
+    # verdict entities' (src/xgraph/oracle.py:650-659)
     kept = None
+    excluded = np.zeros(labels.num_rows, dtype=bool)
     if unquoted_starts:
-        q = quoted_rows(labels, token_bytes, syntax)
-        if q.any():
-            kept = ~q
+        excluded |= quoted_rows(labels, token_bytes, syntax)
+    if index.verdicts:
+        verdict_positions = [labels.owner_ids.index(v) for v in index.verdicts.values()]
+        excluded |= np.isin(np.asarray(labels.owners, dtype=np.int64), verdict_positions)
+    if excluded.any():
+        kept = ~excluded
     kept_prefix = None
     if kept is not None:
         kept_prefix = np.zeros(labels.num_rows + 1, dtype=np.int32)
@@ -435,3 +442,40 @@ def pack_tables(index, tokenizer, syntax, *, escapes: bool, versions=None,
     layout.wide_count = len(wide_keys)
     layout.ent_cols, layout.rel_cols = ent_col.shape[0], rel_col.shape[0]
     return PackedTables(blob=blob, layout=layout, words=words, words_padded=wp)
+
+
+def expression_tables(index, tokenizer, syntax):
+    """The tables of expressions, as xg_set_expressions takes them: the packed delimiter
+    lists (the operand separator's, then each offered operator's, written after the label
+    prefix; per list its length, CSR offsets, tokens and next positions), the number of
+    operators offered (the value comparison only with the verdict entities), their leading
+    shared bytes [operators * operators], the date table (entity positions, keys) and the
+    verdict entities' positions (yes, no) or None (src/xgraph/engine.py:345-360, 500-530)."""
+    token_bytes = [tokenizer.token_bytes(t) for t in range(tokenizer.vocab_size)]
+    offered = syntax.operators if index.verdicts else syntax.operators[:2]
+    if not offered or not syntax.operand_separator:
+        raise ValueError(f"expressions need a span syntax with operators and an operand separator, not {syntax}")
+    if len(offered) > 4:
+        raise ValueError("the engine holds at most 4 operators")
+    written = [(syntax.label_prefix + op).encode("utf-8") for op in offered]
+    parts = []
+    for delimiter in [syntax.operand_separator.encode("utf-8"), *written]:
+        if len(delimiter) > 64:
+            raise ValueError(f"an expression delimiter of {len(delimiter)} bytes is longer than 64")
+        off, tok, nxt = delimiter_lists(delimiter, token_bytes)
+        parts += [np.array([len(delimiter)], dtype=np.int32), off, tok, nxt]
+    delimiters = np.ascontiguousarray(np.concatenate(parts), dtype=np.int32)
+    lcp = np.zeros((len(written), len(written)), dtype=np.int32)
+    for k, a in enumerate(written):
+        for j, b in enumerate(written):
+            n = 0
+            while n < min(len(a), len(b)) and a[n] == b[n]:
+                n += 1
+            lcp[k, j] = n
+    entities = np.ascontiguousarray(index.date_entities, dtype=np.int32)
+    keys = np.ascontiguousarray(index.date_keys, dtype=np.int32)
+    verdicts = None
+    if index.verdicts:
+        ids = index.labels.owner_ids
+        verdicts = np.array([ids.index(index.verdicts["yes"]), ids.index(index.verdicts["no"])], dtype=np.int32)
+    return delimiters, len(written), np.ascontiguousarray(lcp.reshape(-1)), entities, keys, verdicts
