@@ -51,9 +51,12 @@ enum xg_dtype { XG_F32 = 0, XG_BF16 = 1, XG_F16 = 2 };
  * dead), the closer/separator branches' bytes matched and the label rows they started
  * after, the escape branch's bytes matched, the candidate subject and relation rows,
  * subj_key (first row of the subject label), hops (relations of the open path, this one
- * included), four expression fields (always 0: expressions are not served), the
+ * included), four expression fields (the operator branch's bytes matched and the operator
+ * they fit, the span's operator 1..3 or 0, the operand being written: 0 A, 1 B), the
  * end-after-answer flag and the last closed span (kind 0 none, 1 unresolved, 2 entity,
- * 3 fact, 4 path; its rows).  ex_hi and flags are this engine's own: the end of the
+ * 3 fact, 4 path, 5 comparison, 6 relation plan; its rows; a comparison: last_lo / last_hi
+ * the operands' committed start entities, last_subj_lo the result: 1 A, 2 B, 3 both, 4 the
+ * verdict yes, 5 no, last_subj_hi the operator).  ex_hi and flags are this engine's own: the end of the
  * typed label's exact rows and which delimiter branches may start next (or that STOP
  * holds); stop_used_lo/hi are the reference's STOP mask (csrc/engine.cu:88). */
 typedef struct XgState {

@@ -48,8 +48,8 @@ def test_unserved_settings_are_refused():
                                    "XGRAPH_ESCAPE_BIAS": "-2.5", "XGRAPH_RELEASE_TOP": "1", "XGRAPH_OBSERVE": "0.0",
                                    "XGRAPH_STOP": "residual-goal"})
     adapter.check_served_settings({"XGRAPH_RELATIONS": "successor"})  # the relation supports are served
-    for name, value in [("XGRAPH_MENU", "3"), ("XGRAPH_AUDIT", "1"),
-                        ("XGRAPH_EXPRESSIONS", "1"), ("XGRAPH_OBSERVE", "4")]:
+    adapter.check_served_settings({"XGRAPH_EXPRESSIONS": "1"})  # and expressions
+    for name, value in [("XGRAPH_MENU", "3"), ("XGRAPH_AUDIT", "1"), ("XGRAPH_OBSERVE", "4")]:
         with pytest.raises(ValueError, match=name):
             adapter.check_served_settings({name: value})
 

@@ -29,9 +29,10 @@ XGRAPH_RELEASE_MASS, XGRAPH_RELEASE_TOP, XGRAPH_DERIVATION, XGRAPH_ESCAPE_BIAS, 
 XGRAPH_BOUND_ESCAPES, XGRAPH_COMMITTED_PATHS, XGRAPH_START_RANK, XGRAPH_UNQUOTED_STARTS,
 XGRAPH_END_AFTER_ANSWER, XGRAPH_STOP (residual-goal: each opted-in request supplies its
 question as `xgraph_question`; `xgraph_stop` 0 turns STOP off for a request),
-XGRAPH_RELATIONS (frontier, vocabulary or successor relation support).  The reference's
-other research policies (expressions, observations, menus, audit, per-request path
-options) are not served by this engine: a setting or argument
+XGRAPH_RELATIONS (frontier, vocabulary or successor relation support), XGRAPH_EXPRESSIONS
+(1: date and value comparisons; needs XGRAPH_PATHS=1, XGRAPH_COMMITTED_PATHS=1 and an index
+with the date table).  The reference's other research policies (observations, menus, audit,
+per-request path options) are not served by this engine: a setting or argument
 that asks for one is refused with a ValueError naming it.
 
 This module imports only the standard library at import time: vLLM also calls
@@ -71,7 +72,7 @@ REPLAYS = ("replayed", "tail mismatch", "disallowed")
 
 _UNSERVED_ARGS = ("xgraph_relation_ranks", "xgraph_path_options")
 _UNSERVED_SETTINGS = {  # setting: the value that keeps the policy off
-    "XGRAPH_EXPRESSIONS": "0", "XGRAPH_OBSERVE": "0", "XGRAPH_OBSERVE_SELECT": "0",
+    "XGRAPH_OBSERVE": "0", "XGRAPH_OBSERVE_SELECT": "0",
     "XGRAPH_OBSERVE_ANSWER": "0", "XGRAPH_OBSERVE_WIDTH": "0", "XGRAPH_OBSERVE_DEFER": "0",
     "XGRAPH_OBSERVE_TERMINAL": "0", "XGRAPH_MENU": "0", "XGRAPH_MENU_CLOSE_NEXT": "0", "XGRAPH_AUDIT": "0",
     "XGRAPH_REQUEST_PATH_OPTIONS": "0",
@@ -270,6 +271,12 @@ class XGraphLogitsProcessor(_Base):
                 if ids is not None:
                     eos_token_ids.extend([ids] if isinstance(ids, int) else ids)
         self._stop = os.environ.get("XGRAPH_STOP") or None
+        # XGRAPH_EXPRESSIONS=1: a span may be a date or value comparison (src/xgraph/vllm.py:342-383)
+        expressions = os.environ.get("XGRAPH_EXPRESSIONS", "0") == "1"
+        if expressions and not (os.environ.get("XGRAPH_PATHS", "0") == "1"
+                                and os.environ.get("XGRAPH_COMMITTED_PATHS", "0") == "1"):
+            raise ValueError("XGRAPH_EXPRESSIONS=1 needs path mode with committed paths: "
+                             "XGRAPH_PATHS=1 and XGRAPH_COMMITTED_PATHS=1")
         self._engine = Engine(
             index, tokenizer, index.span_syntax, req_states.max_num_reqs,
             escapes=os.environ.get("XGRAPH_ESCAPES", "1") != "0",
@@ -292,6 +299,7 @@ class XGraphLogitsProcessor(_Base):
             eos_token_ids=eos_token_ids,
             stop=self._stop,
             relations=os.environ.get("XGRAPH_RELATIONS") or "frontier",
+            expressions=expressions,
         )
         self._staged: dict[int, Staged] = {}   # slot -> admissions since the last apply_staged_writes
         self._folded = None                    # admission records the next step's launch applies
