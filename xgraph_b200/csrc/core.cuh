@@ -1154,6 +1154,8 @@ XG_COLD bool top_goes_on(const Ctx& c, int32_t n) {
 // capped next frontier has triples.  The frontier is kept for the transition that follows.
 XG_COLD bool frontier_goes_on(const Ctx& c, int32_t rlo, int32_t rhi) {
   const int32_t n = next_frontier(c, rlo, rhi);
+  const int32_t version = version_of(c);
+  const Tables& t = c.t;
   int32_t* ranks = c.mem + kMemPendingRank;
   int32_t* firsts = c.mem + kMemPendingFirst;
   warp_for(c.w, 0, n, [&](int32_t i) {
@@ -1166,7 +1168,11 @@ XG_COLD bool frontier_goes_on(const Ctx& c, int32_t rlo, int32_t rhi) {
     c.mem[kMemPendingCount] = n;
   }
   warp_sync();
-  return top_goes_on(c, n);
+  return warp_any(c.w, 0, n, [&](int32_t i) {
+    const uint32_t known = c.top[i].pad;
+    if (known) return known == 1u;
+    return row_degree(t, version, static_cast<int32_t>(c.top[i].a & 0xffffffffu)) > 0;
+  });
 }
 
 // ---------------------------------------------------------------------------------------
