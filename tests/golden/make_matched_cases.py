@@ -19,6 +19,9 @@ degree or sitelink start rank, unquoted starts, KG versions with add / remove ed
 - anchored paths and entity spans (see anchored_of), each recorded with whether the
   executor fell back to every anchor entity, and an anchor naming no entity (recorded with
   the reference's error).
+
+Every path also records the executor's live frontier: `starts`, `frontier` (after its
+relations) and `frontier_relations` (src/xgraph/programs.py:596-736).
 """
 
 from __future__ import annotations
@@ -122,6 +125,14 @@ def anchored_of(world, rng: random.Random, count: int) -> list[tuple[str, list[s
     return out
 
 
+def live(executor, start, relations, anchor, version) -> dict:
+    """The executor's view of the path's live frontier: its starts, the capped frontier after
+    its relations, and the relations that frontier offers with their edge counts."""
+    return {"starts": list(executor.starts(start, anchor, version)),
+            "frontier": list(executor.frontier(start, relations, anchor, version)),
+            "frontier_relations": [list(x) for x in executor.frontier_relations(start, relations, anchor, version)]}
+
+
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__)
     parser.add_argument("--reference", type=Path, required=True, help="the reference checkout")
@@ -159,7 +170,8 @@ def main() -> None:
                 cases.append({"world": world_name, "setting": setting, "start": start,
                               "relations": relations, "version": version,
                               "reached": list(path.reached), "answer": path.answer,
-                              "plan": None if path.plan is None else list(path.plan)})
+                              "plan": None if path.plan is None else list(path.plan),
+                              **live(executor, start, relations, None, version)})
             for n, (start, relations, anchor) in enumerate(anchored):
                 version = (None, "v0", "v1")[n % 3] if world_name != "crowd" else None
                 case = {"world": world_name, "setting": setting, "start": start, "relations": relations,
@@ -172,7 +184,8 @@ def main() -> None:
                 # the executor's fallback: the start label names none of the anchor's entities
                 fallback = not executor._written_starts(start, anchor)
                 cases.append({**case, "fallback": fallback, "reached": list(path.reached),
-                              "answer": path.answer, "plan": None if path.plan is None else list(path.plan)})
+                              "answer": path.answer, "plan": None if path.plan is None else list(path.plan),
+                              **live(executor, start, relations, anchor, version)})
     with gzip.open(HERE / "matched_cases.json.gz", "wt", encoding="utf-8") as f:
         json.dump({"settings": SETTINGS, "edits": all_edits, "cases": cases}, f)
     empty = sum(1 for c in cases if not c.get("reached"))

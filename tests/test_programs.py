@@ -41,6 +41,8 @@ def test_matched_fixture_covers_the_cases():
     assert sum(1 for c in served(anchored) if len(c["reached"]) > 1) > 50
     assert any(not c["relations"] and c["reached"] for c in served(anchored))
     cases = served(cases)
+    assert sum(1 for c in cases if len(c["frontier"]) > 1) > 200 and sum(1 for c in cases if c["frontier_relations"]) > 400
+    assert sum(1 for c in cases if len(c["starts"]) > 1) > 100
     assert sum(1 for c in cases if len(c["reached"]) > 1) > 100
     assert sum(1 for c in cases if not c["reached"]) > 100
     assert any(not c["relations"] and c["reached"] for c in cases)
@@ -139,6 +141,23 @@ def _check(cases, got, where):
         assert (None if path.plan is None else list(path.plan)) == case["plan"], at
 
 
+def _check_live(executor, cases, where):
+    """The live frontier of every served case, a world's paths in one batch: starts,
+    frontier and frontier_relations equal the reference executor's."""
+    ids = executor._index.labels.owner_ids
+    jobs = [(c["start"], [], c["version"], c.get("anchor")) for c in cases]
+    jobs += [(c["start"], c["relations"], c["version"], c.get("anchor")) for c in cases]
+    got = executor.frontiers(jobs)
+    for case, starts, frontier in zip(cases, got[: len(cases)], got[len(cases):], strict=True):
+        at = (*where, case["start"], case["relations"], case["version"], case.get("anchor"))
+        assert [ids[e] for e, _ in starts] == case["starts"], at
+        assert [ids[e] for e, _ in frontier] == case["frontier"], at
+    for case in cases[:40]:
+        at = (*where, case["start"], case["relations"], case["version"], case.get("anchor"))
+        relations = executor.frontier_relations(case["start"], case["relations"], case.get("anchor"), case["version"])
+        assert [list(x) for x in relations] == case["frontier_relations"], at
+
+
 def test_matched_execution_on_the_host_seam_equals_the_reference():
     """Every recorded path through the executor with the kernels' row logic on the CPU (the
     host seam in place of the CUDA engine): the reference's entities in its order, its
@@ -147,16 +166,19 @@ def test_matched_execution_on_the_host_seam_equals_the_reference():
         executor = _executor(world_name, setting, max_paths=64, seam=True)
         _check(served(cases), executor.execute_many([_job(c) for c in served(cases)]), (world_name, setting))
         _refusals(executor, cases)
+        _check_live(executor, served(cases), (world_name, setting))
 
 
 @pytest.mark.gpu
 def test_matched_execution_equals_the_reference():
     """Every recorded path, executed on the GPU a world and setting at a time, reaches the
-    reference's entities in its order, delivers its answer and reports its plan."""
+    reference's entities in its order, delivers its answer and reports its plan; its
+    starts, live frontier and frontier relations are the reference executor's."""
     for (world_name, setting), cases in _groups().items():
         executor = _executor(world_name, setting)
         _check(served(cases), executor.execute_many([_job(c) for c in served(cases)]), (world_name, setting))
         _refusals(executor, cases)
+        _check_live(executor, served(cases), (world_name, setting))
 
 
 @pytest.mark.gpu
@@ -171,6 +193,23 @@ def test_matched_execution_in_small_batches_and_single_calls():
     for case in cases[:5]:
         one = executor.execute(case["start"], case["relations"], version=case["version"])
         assert list(one.reached) == case["reached"] and one.answer == case["answer"]
+
+
+def test_frontier_labels_name_the_frontier_relations():
+    """frontier_labels: the written labels (and aliases) of exactly the relations
+    frontier_relations lists, each naming one of them; named: the entities a label names."""
+    case = next(c for c in served(fixture()["cases"]) if c["world"] == "toy" and c["frontier_relations"])
+    executor = _executor("toy", case["setting"], max_paths=4, seam=True)
+    _, served_tokenizer, _ = world("toy")
+    args = (case["start"], case["relations"], case.get("anchor"), case["version"])
+    labels = executor.frontier_labels(*args)
+    want = {r for r, _ in case["frontier_relations"]}
+    relations = executor._index.relations
+    assert labels and labels == sorted(set(labels)) and set(labels) <= set(executor.relation_labels())
+    for label in labels:
+        lo, hi = relations.prefix_range(list(served_tokenizer.encode(" " + label)))
+        assert {relations.owner_id(r) for r in range(lo, hi)} & want, label
+    assert set(case["starts"]) <= executor.named(case["start"])
 
 
 def test_matched_executor_refuses_what_it_does_not_serve():

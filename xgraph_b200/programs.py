@@ -212,11 +212,22 @@ class MatchedExecutor:
         anchor entity, which no written span can express) raises ValueError."""
         if repair:
             raise ValueError("the offline relation repair is not served by this executor")
+        jobs = self._jobs(paths)
+        out: list[MatchedPath] = []
+        size = self._runner.max_sequences
+        for at in range(0, len(jobs), size):
+            out += self._batch(jobs[at: at + size])
+        return out
+
+    def _jobs(self, paths) -> list[tuple]:
+        """(start, relations capped at 8, version, anchor) of each path, checked before any
+        launch: an unknown version or an anchor without label rows raises, and so does an
+        anchored start naming none of the anchor's entities (the fallback not served)."""
         jobs = []
         for path in paths:
             start, relations, version = path[0], list(path[1])[:MAX_PATH_RELATIONS], path[2]
             anchor = path[3] if len(path) > 3 else None
-            self._runner.view(version)  # an unknown version name raises here, before any launch
+            self._runner.view(version)
             if anchor is not None:
                 bound = self._bound_rows(anchor)
                 named = sorted(set(self._written_rows(start)) & set(bound))
@@ -225,10 +236,118 @@ class MatchedExecutor:
                                      f"{list(anchor)!r}; that fallback is not served")
                 anchor = list(anchor)
             jobs.append((start, relations, version, anchor))
-        out: list[MatchedPath] = []
+        return jobs
+
+    # -- the live frontier (src/xgraph/programs.py:598-812) ------------------------------
+
+    def named(self, label: str) -> set[str]:
+        """The entities a label written exactly as this text names."""
+        ids, owners = self._index.labels.owner_ids, self._index.labels.owners
+        return {ids[int(owners[row])] for row in self._written_rows(label)}
+
+    def starts(self, start: str, anchor: list[str] | None = None, version: str | None = None) -> tuple[str, ...]:
+        """The entities a path from this start starts from, best-connected first: those the
+        label names (the anchor's, anchored) that have triples, the first 64."""
+        return self.frontier(start, [], anchor, version)
+
+    def frontier(self, start: str, relations: list[str], anchor: list[str] | None = None,
+                 version: str | None = None) -> tuple[str, ...]:
+        """The capped live frontier after the relations (every start sense that survives,
+        by start rank and first label row), or the starts for no relation."""
+        ids = self._index.labels.owner_ids
+        return tuple(ids[e] for e, _ in self.frontiers([(start, relations, version, anchor)])[0])
+
+    def frontier_relations(self, start: str, relations: list[str], anchor: list[str] | None = None,
+                           version: str | None = None) -> list[tuple[str, int]]:
+        """The relations path mode offers after the path so far: every relation of its whole
+        frontier, as (relation id, the frontier's edges with it), most edges first, then
+        index order; empty where the path has as many relations as a path may name."""
+        if len(relations) >= MAX_PATH_RELATIONS:
+            if anchor is not None:
+                self._bound_rows(anchor)
+            return []
+        view = self._runner.view(version)
+        counts: dict[int, int] = {}
+        for entity, _ in self.frontiers([(start, relations, version, anchor)])[0]:
+            found, times = np.unique(np.asarray(view.edges_at(entity)[0]), return_counts=True)
+            for relation, n in zip(found.tolist(), times.tolist(), strict=True):
+                counts[relation] = counts.get(relation, 0) + n
+        ids = self._index.relations.owner_ids
+        return [(ids[r], counts[r]) for r in sorted(counts, key=lambda r: (-counts[r], r))]
+
+    def frontier_labels(self, start: str, relations: list[str], anchor: list[str] | None = None,
+                        version: str | None = None) -> list[str]:
+        """The writable relation labels and aliases of the whole frontier, sorted."""
+        have = {relation for relation, _ in self.frontier_relations(start, relations, anchor, version)}
+        return self.relation_labels(have) if have else []
+
+    def relation_labels(self, relations: set[str] | None = None) -> list[str]:
+        """The writable relation vocabulary (the index's relation rows as written), or the
+        named relations' labels only, sorted."""
+        index, prefix = self._index.relations, self._syntax.label_prefix
+        ids = index.owner_ids
+        names = set()
+        for row in range(index.num_rows):
+            if relations is None or ids[int(index.owners[row])] in relations:
+                text = b"".join(self._tokenizer.token_bytes(t) for t in index.row_tokens(row))
+                names.add(text.decode("utf-8", errors="replace").removeprefix(prefix))
+        return sorted(names)
+
+    def frontiers(self, paths: Iterable[tuple]) -> list[list[tuple[int, int]]]:
+        """Each (start, relations, version[, anchor]) path's live frontier as (entity
+        position, start rank) pairs in order, from one engine slot each, a batch in one
+        launch: the ranked starts after `⟦ start ·` for no relation, else the frontier the
+        last relation reaches (read before the closer); empty where the engine would not
+        have let the path be written."""
+        jobs = self._jobs(paths)
+        out: list[list[tuple[int, int]]] = []
         size = self._runner.max_sequences
         for at in range(0, len(jobs), size):
-            out += self._batch(jobs[at: at + size])
+            out += self._frontier_batch(jobs[at: at + size])
+        return out
+
+    def _frontier_batch(self, paths) -> list[list[tuple[int, int]]]:
+        size = self._runner.max_sequences
+        streams = []
+        for start, relations, _, _ in paths:
+            if relations:
+                stream = self._stream(start, relations)
+                streams.append(None if stream is None else (stream[0][: stream[1]], stream[1]))
+            else:  # the starts: the span up to the separator after its start
+                label = self._label(start)
+                tokens = None if label is None else (self._encode(self._syntax.opener) + label
+                                                     + self._encode(self._syntax.separator))
+                streams.append(None if tokens is None else (tokens, len(tokens)))
+        width = max([len(s[0]) for s in streams if s is not None] + [1])
+        history = np.zeros((size, width), dtype=np.int32)
+        upto = np.zeros(size, dtype=np.int32)
+        for k, stream in enumerate(streams):
+            if stream is not None:
+                history[k, : len(stream[0])] = stream[0]
+                upto[k] = stream[1]
+        admissions = [(k, version, anchor) for k, (_, _, version, anchor) in enumerate(paths)]
+        states, memory, _, _ = self._runner.run(history, upto, upto, admissions)
+        owners, first = self._index.labels.owners, self._first_rows()
+        out = []
+        for k, (_, relations, version, _) in enumerate(paths):
+            if streams[k] is None or int(states["phase"][k]) == _PHASE_ERROR:
+                out.append([])
+                continue
+            row = memory[k]
+            if not relations:  # the ranked starts, as next_segment stored them
+                count = int(row[_MEM_FRONTIER])
+                out.append([(int(row[_MEM_FRONTIER_ENT + i]), int(row[_MEM_FRONTIER_RANK + i])) for i in range(count)])
+                continue
+            lo, hi = int(states["lo"][k]), int(states["ex_hi"][k])
+            if int(row[_MEM_PENDING_LO]) == lo and int(row[_MEM_PENDING_HI]) == hi:
+                pairs = [(int(owners[int(row[_MEM_PENDING_FIRST + i])]), int(row[_MEM_PENDING_RANK + i]))
+                         for i in range(int(row[_MEM_PENDING_COUNT]))]
+            else:  # the eighth relation: no separator test ran
+                pairs = self._last_hop(self._runner.view(version), row, lo, hi)
+            least: dict[int, int] = {}
+            for entity, rank in pairs:  # an entity may be listed once per rank it is reached with
+                least[entity] = min(least.get(entity, rank), rank)
+            out.append(sorted(least.items(), key=lambda p: (p[1], int(first[p[0]]))))
         return out
 
     def _batch(self, paths) -> list[MatchedPath]:
