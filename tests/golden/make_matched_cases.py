@@ -21,7 +21,8 @@ degree or sitelink start rank, unquoted starts, KG versions with add / remove ed
   the reference's error).
 
 Every path also records the executor's live frontier: `starts`, `frontier` (after its
-relations) and `frontier_relations` (src/xgraph/programs.py:596-736).
+relations) and `frontier_relations`, and the `derivations` of the entities it resolves to
+(src/xgraph/programs.py:596-736).
 """
 
 from __future__ import annotations
@@ -127,10 +128,12 @@ def anchored_of(world, rng: random.Random, count: int) -> list[tuple[str, list[s
 
 def live(executor, start, relations, anchor, version) -> dict:
     """The executor's view of the path's live frontier: its starts, the capped frontier after
-    its relations, and the relations that frontier offers with their edge counts."""
+    its relations, the relations that frontier offers with their edge counts, and the
+    derivations of the entities it resolves to."""
     return {"starts": list(executor.starts(start, anchor, version)),
             "frontier": list(executor.frontier(start, relations, anchor, version)),
-            "frontier_relations": [list(x) for x in executor.frontier_relations(start, relations, anchor, version)]}
+            "frontier_relations": [list(x) for x in executor.frontier_relations(start, relations, anchor, version)],
+            "derivations": [list(x) for x in executor.derivations(start, relations, anchor, version)]}
 
 
 def main() -> None:

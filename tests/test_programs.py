@@ -43,6 +43,7 @@ def test_matched_fixture_covers_the_cases():
     cases = served(cases)
     assert sum(1 for c in cases if len(c["frontier"]) > 1) > 200 and sum(1 for c in cases if c["frontier_relations"]) > 400
     assert sum(1 for c in cases if len(c["starts"]) > 1) > 100
+    assert sum(1 for c in cases if any(n > 1 for _, n in c["derivations"])) > 20
     assert sum(1 for c in cases if len(c["reached"]) > 1) > 100
     assert sum(1 for c in cases if not c["reached"]) > 100
     assert any(not c["relations"] and c["reached"] for c in cases)
@@ -142,8 +143,9 @@ def _check(cases, got, where):
 
 
 def _check_live(executor, cases, where):
-    """The live frontier of every served case, a world's paths in one batch: starts,
-    frontier and frontier_relations equal the reference executor's."""
+    """The live frontier of every served case (starts and frontiers of a world's paths in
+    one batch): starts, frontier, frontier_relations and derivations equal the reference
+    executor's."""
     ids = executor._index.labels.owner_ids
     jobs = [(c["start"], [], c["version"], c.get("anchor")) for c in cases]
     jobs += [(c["start"], c["relations"], c["version"], c.get("anchor")) for c in cases]
@@ -152,10 +154,12 @@ def _check_live(executor, cases, where):
         at = (*where, case["start"], case["relations"], case["version"], case.get("anchor"))
         assert [ids[e] for e, _ in starts] == case["starts"], at
         assert [ids[e] for e, _ in frontier] == case["frontier"], at
-    for case in cases[:40]:
+    for case in cases:
         at = (*where, case["start"], case["relations"], case["version"], case.get("anchor"))
         relations = executor.frontier_relations(case["start"], case["relations"], case.get("anchor"), case["version"])
         assert [list(x) for x in relations] == case["frontier_relations"], at
+        derivations = executor.derivations(case["start"], case["relations"], case.get("anchor"), case["version"])
+        assert [list(x) for x in derivations] == case["derivations"], at
 
 
 def test_matched_execution_on_the_host_seam_equals_the_reference():

@@ -138,9 +138,11 @@ class MatchedExecutor:
             tokens += self._encode(self._syntax.separator) + label
         return tokens + self._encode(self._syntax.closer), len(tokens)
 
-    def _order(self, view, pairs: Iterable[tuple[int, int]]) -> list[int]:
-        """The entities of these (entity, label row) pairs in best-connected order."""
-        sitelinks = self._sitelinks
+    def _order(self, view, pairs: Iterable[tuple[int, int]], sitelinks=False) -> list[int]:
+        """The entities of these (entity, label row) pairs in best-connected order (by the
+        executor's start rank, or by the given sitelink counts; None: by degree)."""
+        if sitelinks is False:
+            sitelinks = self._sitelinks
 
         def key(pair: tuple[int, int]) -> tuple[int, int, int]:
             entity, row = pair
@@ -180,12 +182,13 @@ class MatchedExecutor:
 
     # -- execution -----------------------------------------------------------------------
 
-    def _written_rows(self, start: str) -> list[int]:
-        """The label rows written exactly as `start` (the reference's `_rows`)."""
+    def _written_rows(self, start: str, labels=None) -> list[int]:
+        """The label rows (of the entity labels, or of `labels`) written exactly as `start`
+        (the reference's `_rows`)."""
         tokens = self._label(start)
         if tokens is None:
             return []
-        labels = self._index.labels
+        labels = self._index.labels if labels is None else labels
         lo, hi = labels.prefix_range(tokens)
         offsets = np.asarray(labels.offsets)
         return [r for r in range(lo, hi) if int(offsets[r + 1] - offsets[r]) == len(tokens)]
@@ -292,6 +295,52 @@ class MatchedExecutor:
                 text = b"".join(self._tokenizer.token_bytes(t) for t in index.row_tokens(row))
                 names.add(text.decode("utf-8", errors="replace").removeprefix(prefix))
         return sorted(names)
+
+    def derivations(self, start: str, relations: list[str], anchor: list[str] | None = None,
+                    version: str | None = None, rank: str | None = None) -> tuple[tuple[str, int], ...]:
+        """The entities the path resolves to (MatchedPath.reached), each with its number of
+        derivations: the distinct relation paths from the start it resolves from, one
+        relation and one entity of each hop's live frontier per hop (src/xgraph/programs.py:
+        606-662), best-connected first under `rank` (by default the executor's start rank).
+        The engine gives every hop's frontier (one slot per prefix of the path, one launch);
+        the paths are counted on the host.  Empty where the path is empty or names no
+        relation."""
+        from .index import check_start_rank
+
+        relations = list(relations)[:MAX_PATH_RELATIONS]
+        if not relations:
+            if anchor is not None:
+                self._bound_rows(anchor)
+            return ()
+        jobs = [(start, relations[:k], version, anchor) for k in range(len(relations) + 1)]
+        starts, *hops = self.frontiers(jobs)
+        if not hops[-1]:
+            return ()
+        index, view = self._index, self._runner.view(version)
+        owners = np.asarray(index.labels.owners)
+        best = min(r for _, r in hops[-1])
+        counts = {starts[best][0]: 1}
+        for written, kept in zip(relations, hops, strict=True):
+            follow = sorted({int(index.relations.owners[r]) for r in self._written_rows(written, index.relations)})
+            members = {e for e, _ in kept}
+            reached: dict[int, int] = {}
+            for entity, n in counts.items():
+                relation_of, object_of = view.edges_at(entity)
+                chosen = np.isin(relation_of, follow)
+                steps = {(int(r), int(owners[row])) for r, row in zip(np.asarray(relation_of)[chosen],
+                                                                       np.asarray(object_of)[chosen], strict=True)}
+                for _, item in steps:
+                    if item in members:
+                        reached[item] = reached.get(item, 0) + n
+            counts = reached
+        sitelinks = False
+        if rank is not None:
+            sitelinks = index.sitelinks if check_start_rank(rank, index) == "sitelinks" else None
+        first = self._first_rows()
+        final = [e for e, r in hops[-1] if r == best]
+        ordered = self._order(view, [(e, int(first[e])) for e in final], sitelinks)
+        ids = index.labels.owner_ids
+        return tuple((ids[e], counts.get(e, 0)) for e in ordered)
 
     def frontiers(self, paths: Iterable[tuple]) -> list[list[tuple[int, int]]]:
         """Each (start, relations, version[, anchor]) path's live frontier as (entity
