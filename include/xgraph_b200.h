@@ -54,9 +54,10 @@ enum xg_dtype { XG_F32 = 0, XG_BF16 = 1, XG_F16 = 2 };
  * included), four expression fields (the operator branch's bytes matched and the operator
  * they fit, the span's operator 1..3 or 0, the operand being written: 0 A, 1 B), the
  * end-after-answer flag and the last closed span (kind 0 none, 1 unresolved, 2 entity,
- * 3 fact, 4 path, 5 comparison, 6 relation plan; its rows; a comparison: last_lo / last_hi
- * the operands' committed start entities, last_subj_lo the result: 1 A, 2 B, 3 both, 4 the
- * verdict yes, 5 no, last_subj_hi the operator).  ex_hi and flags are this engine's own: the end of the
+ * 3 fact, 4 path, 5 comparison, 6 relation plan; its rows; a comparison, as the
+ * reference engine records it: last_lo / last_hi the label rows of the operands' committed
+ * starts, last_subj_lo the result: 0 A, 1 B, 2 both, 3 the verdict yes, 4 no, last_subj_hi
+ * the operator).  ex_hi and flags are this engine's own: the end of the
  * typed label's exact rows and which delimiter branches may start next (or that STOP
  * holds); stop_used_lo/hi are the reference's STOP mask (csrc/engine.cu:88). */
 typedef struct XgState {

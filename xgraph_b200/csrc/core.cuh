@@ -84,8 +84,9 @@ enum MemoryField : int32_t {
 
 // Expressions: a comparison's operand region of slot memory, at Tables::mem_operand (after
 // the relation bitmap): operand B's frontier (entities, start ranks, count), each operand's
-// ranked starts (entity of rank k), operand A's best values of a value comparison (a
-// label row or a date key, and whether it is a date), and operand B's relation bitmap.
+// ranked starts (the written label row of the start of rank k), operand A's best values of
+// a value comparison (a label row or a date key, and whether it is a date), and operand B's
+// relation bitmap.
 enum OperandField : int32_t {
   kOpFrontEnt = 0,
   kOpFrontRank = kOpFrontEnt + kMaxSet,
@@ -1262,9 +1263,9 @@ XG_COLD void comparison_flags(const Ctx& c, const XgState& s, bool& separates, b
 }
 
 // A comparison closed after the relation-label rows [lo, hi): -1 where it cannot close,
-// else its result -- 1 operand A's start, 2 operand B's, 3 both (undetermined), 4 the
-// verdict yes, 5 no -- with a and b the start entities the operands commit to
-// (src/xgraph/oracle.py:1680-1737).
+// else its result -- 0 operand A's start, 1 operand B's, 2 both (undetermined), 3 the
+// verdict yes, 4 no (the reference engine's codes, csrc/engine.cu:1782-1815) -- with a and
+// b the label rows of the starts the operands commit to (src/xgraph/oracle.py:1680-1737).
 XG_COLD int32_t compare(const Ctx& c, int32_t op, int32_t lo, int32_t hi, int32_t& a, int32_t& b) {
   const Tables& t = c.t;
   int32_t* mem = c.mem + t.mem_operand;
@@ -1289,7 +1290,7 @@ XG_COLD int32_t compare(const Ctx& c, int32_t op, int32_t lo, int32_t hi, int32_
       const int32_t i = p / mb, j = p % mb;
       return dated_a[i] == dated_b[j] && values_a[i] == values_b[j];
     });
-    return shared ? 4 : 5;
+    return shared ? 3 : 4;
   }
   // a date comparison: each operand's best start that reaches a date, its earliest date
   const Key pa = dated_pick(c, operand_next(c, 0, lo, hi));
@@ -1301,8 +1302,8 @@ XG_COLD int32_t compare(const Ctx& c, int32_t op, int32_t lo, int32_t hi, int32_
   const int32_t lo_a = unordered(static_cast<uint32_t>(pa.a & 0xffffffffu)), hi_a = unordered(pa.b);
   const int32_t lo_b = unordered(static_cast<uint32_t>(pb.a & 0xffffffffu)), hi_b = unordered(pb.b);
   const bool a_first = hi_a < lo_b, b_first = hi_b < lo_a;
-  if (op == 1) return a_first ? 1 : b_first ? 2 : 3;  // earlier
-  return a_first ? 2 : b_first ? 1 : 3;               // later
+  if (op == 1) return a_first ? 0 : b_first ? 1 : 2;  // earlier
+  return a_first ? 1 : b_first ? 0 : 2;               // later
 }
 
 // ---------------------------------------------------------------------------------------
@@ -1592,7 +1593,7 @@ XG_COLD void next_segment(const Ctx& c, XgState& s, int32_t llo, int32_t lhi) {
           ents[i] = t.ent.owner[static_cast<int32_t>(c.top[i].a & 0xffffffffu)];
           ranks[i] = 0;
         }
-        if (starts) starts[i] = ents[i];
+        if (starts) starts[i] = static_cast<int32_t>(c.top[i].b);  // the written label row
       });
       if (second) {
         mem_store(c, t.mem_operand + kOpFrontCount, n);
@@ -1694,9 +1695,10 @@ XG_COLD void close_span(const Ctx& c, XgState& s, int32_t llo, int32_t lhi) {
     const int32_t result = compare(c, s.op, llo, lhi, a, b);
     // the result binds the answer: the rows of its entities (both starts, undetermined; the
     // verdict's entity, a value comparison)
-    const int32_t first = result < 0 ? -1 : result == 2 ? b : result == 4 ? t.verdict_yes
-                                          : result == 5 ? t.verdict_no : a;
-    const int32_t second = result == 3 ? b : -1;
+    const int32_t ea = a >= 0 ? t.ent.owner[a] : -1, eb = b >= 0 ? t.ent.owner[b] : -1;
+    const int32_t first = result < 0 ? -1 : result == 1 ? eb : result == 3 ? t.verdict_yes
+                                          : result == 4 ? t.verdict_no : ea;
+    const int32_t second = result == 2 ? eb : -1;
     int32_t n = 0;
     for (const int32_t e : {first, second}) {  // (an entity without label rows binds nothing)
       const int32_t row = e >= 0 && e < t.entities ? t.ent_first_row[e] : -1;

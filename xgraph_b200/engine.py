@@ -709,14 +709,16 @@ def closed_span(index, states: dict[str, np.ndarray], seq: int) -> ClosedSpanRec
     version's view (Engine.view)."""
     kind = CLOSED[int(states["last_kind"][seq])]
     lo, hi = int(states["last_lo"][seq]), int(states["last_hi"][seq])
-    if kind == "comparison":  # lo, hi: the operands' start entities; subj_lo the result, subj_hi the operator
+    if kind == "comparison":  # lo, hi: the operands' start rows; subj_lo the result, subj_hi the operator
         from .dates import VERDICTS
 
-        ids = index.labels.owner_ids
+        operands = (index.labels.owner_id(lo), index.labels.owner_id(hi))
         result, operator = int(states["last_subj_lo"][seq]), int(states["last_subj_hi"][seq])
-        entities = {1: (ids[lo],), 2: (ids[hi],), 3: tuple(sorted({ids[lo], ids[hi]})),
-                    4: (VERDICTS["yes"],), 5: (VERDICTS["no"],)}[result]
-        return ClosedSpanRecord(kind, entities, (), COMPARISONS[operator - 1], (ids[lo], ids[hi]))
+        if result >= 3:  # a value comparison's verdict: 3 yes, 4 no
+            chosen = (VERDICTS["yes" if result == 3 else "no"],)
+        else:  # a date comparison's operand: 0 A's, 1 B's, 2 both
+            chosen = operands if result == 2 else operands[result: result + 1]
+        return ClosedSpanRecord(kind, tuple(sorted(set(chosen))), (), COMPARISONS[operator - 1], operands)
     if kind == "entity span":
         owners = {index.labels.owner_id(r) for r in range(lo, hi)}
         if int(states["last_subj_lo"][seq]) == -1:  # an unbound span names no verdict entity
