@@ -196,3 +196,63 @@ def test_seam_reproduces_the_expression_walks():
                 check_operator_fields(record, states, 0, view, where)
                 if k < len(w["tokens"]):
                     seam.advance([w["tokens"][k]])
+
+
+def test_engine_refuses_expressions_without_their_needs():
+    """The Engine's checks run before any device call (CPU): committed paths, escapes, the
+    date table, frontier support."""
+    from tests.conftest import world_index
+    from xgraph_b200.engine import Engine
+    from xgraph_b200.syntax import SpanSyntax
+
+    _, served, _ = world("toy")
+    index = dated_index("toy")
+    with pytest.raises(ValueError, match="committed paths"):
+        Engine(index, served, SpanSyntax(), 1, paths=True, expressions=True)
+    with pytest.raises(ValueError, match="escapes"):
+        Engine(index, served, SpanSyntax(), 1, paths=True, committed_paths=True, escapes=False, expressions=True)
+    with pytest.raises(ValueError, match="date table"):
+        Engine(world_index("toy", False), served, SpanSyntax(), 1, paths=True, committed_paths=True,
+               expressions=True)
+    with pytest.raises(ValueError, match="expressions"):
+        Engine(index, served, SpanSyntax(), 1, paths=True, committed_paths=True, expressions=True,
+               relations="vocabulary")
+
+
+def test_seam_refuses_malformed_expression_tables():
+    """xg_set_expressions' table checks (parse_packed_delims, shared with the host seam):
+    the packed lists must parse exactly, tokens lie in the vocabulary and ascend per byte
+    position, next positions stay inside the delimiter; the third operator needs the
+    verdict entities."""
+    import ctypes
+
+    import numpy as np
+
+    from tests.seam import SeamEngine
+    from xgraph_b200.syntax import SpanSyntax
+
+    _, served, _ = world("toy")
+    seam = SeamEngine(dated_index("toy"), served, SpanSyntax(), 1, paths=True, committed_paths=True,
+                      expressions=True)
+    delims, operators, lcp, entities, keys, verdicts = seam._expr
+
+    def call(d, ops=operators, v=verdicts):
+        d = np.ascontiguousarray(d, dtype=np.int32)
+        ptr = lambda a: None if a is None else a.ctypes.data_as(ctypes.c_void_p)  # noqa: E731
+        return seam.lib.xgs_set_expressions(seam.handle, ptr(d), len(d), ops, ptr(lcp), ptr(entities), ptr(keys),
+                                            len(entities), ptr(v))
+
+    assert call(delims) == 0
+    assert call(delims[:-1]) == 1                      # cut short
+    assert call(np.concatenate([delims, [0]])) == 1    # not used up
+    bad = delims.copy()
+    bad[0] = 0                                         # a delimiter of no bytes
+    assert call(bad) == 1
+    n = int(delims[1 + delims[0]])                     # the operand separator's token count
+    bad = delims.copy()
+    bad[2 + delims[0]] = served.vocab_size             # a token outside the vocabulary
+    assert call(bad) == 1
+    bad = delims.copy()
+    bad[2 + delims[0] + n] = int(delims[0]) + 1        # a next position past the delimiter
+    assert call(bad) == 1
+    assert call(delims, v=None) == 1                   # the value comparison without verdicts

@@ -1,8 +1,8 @@
 """Expressions on the GPU: the CUDA engine through the C ABI reproduces every reference
 walk of tests/golden/expression_cases.json.gz (date and value comparisons; see
 tests/test_expressions.py for the fixture and the CPU checks), by advance + fill_mask and by
-the fused step, and refuses what expressions need but lack.  Collected after the other GPU
-tests of the engine's established policies."""
+the fused step.  Collected after the other GPU tests of the engine's established
+policies."""
 
 from __future__ import annotations
 
@@ -68,23 +68,3 @@ def test_engine_reproduces_the_expression_walks():
             replay(engine, served, index, syntax, case, n, w, fused=False)
             replay(engine, served, index, syntax, case, n, w, fused=True)
         assert engine.faults() == 0
-
-
-@pytest.mark.gpu
-def test_engine_refuses_expressions_without_their_needs():
-    from tests.conftest import world_index
-    from xgraph_b200.engine import Engine
-    from xgraph_b200.syntax import SpanSyntax
-
-    _, served, _ = world("toy")
-    index = dated_index("toy")
-    with pytest.raises(ValueError, match="committed paths"):
-        Engine(index, served, SpanSyntax(), 1, paths=True, expressions=True)
-    with pytest.raises(ValueError, match="escapes"):
-        Engine(index, served, SpanSyntax(), 1, paths=True, committed_paths=True, escapes=False, expressions=True)
-    with pytest.raises(ValueError, match="date table"):
-        Engine(world_index("toy", False), served, SpanSyntax(), 1, paths=True, committed_paths=True,
-               expressions=True)
-    with pytest.raises(ValueError, match="expressions"):
-        Engine(index, served, SpanSyntax(), 1, paths=True, committed_paths=True, expressions=True,
-               relations="vocabulary")
