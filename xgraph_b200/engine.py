@@ -188,7 +188,13 @@ class Engine:
     token is disallowed, may write only the escape marker's next tokens; release is per
     call and leaves the slot's recorded mask alone.  escape_bias is added to the logits of
     the tokens that commit to the escape marker (16-bit logits hold the sum rounded to
-    nearest)."""
+    nearest).
+
+    With expressions=True (committed paths, escapes, frontier support and an index with the
+    date table, src/xgraph/engine.py:655-664) a span may be a date comparison
+    `⟦ earlier: A | B · r⟧` (or `later:`), or with the index's verdict entities a value
+    comparison `⟦ same: A | B · r⟧`; its result binds the answer span after it, and
+    closed_span reads it back as a "comparison" record."""
 
     def __init__(
         self,
