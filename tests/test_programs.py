@@ -48,11 +48,12 @@ def test_matched_fixture_covers_the_cases():
     assert sum(1 for c in cases if not c["reached"]) > 100
     assert any(not c["relations"] and c["reached"] for c in cases)
     assert any(len(c["relations"]) > MAX_PATH_RELATIONS and c["reached"] for c in cases)
+    assert sum(1 for c in cases if c.get("fallback") and c["reached"]) > 20
     for c in cases:
-        if c["reached"] and c["relations"]:
+        if c["reached"] and c["relations"] and not c.get("fallback"):
             assert c["plan"] == [c["start"], *c["relations"][:MAX_PATH_RELATIONS]]
             assert c["answer"] in c["reached"]
-        else:
+        else:  # (a fallback start plans nothing)
             assert c["plan"] is None
 
 
@@ -108,8 +109,9 @@ def _executor(world_name: str, setting: str, max_paths: int = 256, seam: bool = 
 
 
 def served(cases):
-    """The cases the executor serves: all but the anchored fallbacks and errors."""
-    return [c for c in cases if not c.get("fallback") and "error" not in c]
+    """The cases the executor serves: all but the anchors without label rows (errors);
+    the anchored fallbacks included (every fixture fallback anchors one entity)."""
+    return [c for c in cases if "error" not in c]
 
 
 def _groups():
@@ -120,12 +122,9 @@ def _groups():
 
 
 def _refusals(executor, cases):
-    """The anchored fallbacks and anchors without label rows, one call each: ValueError."""
+    """Anchors without label rows, one call each: ValueError."""
     for case in cases:
-        if case.get("fallback"):
-            with pytest.raises(ValueError, match="names none of the anchor's entities"):
-                executor.execute(case["start"], case["relations"], anchor=case["anchor"], version=case["version"])
-        elif "error" in case:
+        if "error" in case:
             with pytest.raises(ValueError, match="anchor has no writable label rows"):
                 executor.execute(case["start"], case["relations"], anchor=case["anchor"], version=case["version"])
 
@@ -218,6 +217,11 @@ def test_frontier_labels_name_the_frontier_relations():
 
 def test_matched_executor_refuses_what_it_does_not_serve():
     executor = _executor("toy", "committed", max_paths=2, seam=True)
+    kg, _, _ = world("toy")
+    a, b = [e for e in kg.entities if e.labels][:2]
+    assert not set(a.labels) & set(b.labels)
+    with pytest.raises(ValueError, match="no one label names them all"):  # a fallback no span can write
+        executor.execute("Nobody Here", ["place of birth"], anchor=[a.id, b.id])
     with pytest.raises(ValueError, match="repair"):
         executor.execute("Paris Hilton", ["place of birth"], repair=True)
     with pytest.raises(ValueError, match="no KG version"):

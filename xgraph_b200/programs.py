@@ -23,10 +23,10 @@ short) leaves its slot in the error phase and executes to nothing, as the refere
 executor returns for it.
 
 Anchored paths start from the anchor's entities their start label names (each anchored
-slot admitted with the anchor's label rows).  Not served (refused by name): an anchored
-start naming none of the anchor's entities (the reference then starts from every anchor
-entity), the offline repairs (`repair`, `strip_quotes`) and the observation / menu / audit
-settings.
+slot admitted with the anchor's label rows); a start naming none of them starts from every
+anchor entity, as the reference's does, written with a label that names them all (refused
+where no one label does).  Not served (refused by name): the offline repairs (`repair`,
+`strip_quotes`) and the observation / menu / audit settings.
 """
 
 from __future__ import annotations
@@ -123,11 +123,11 @@ class MatchedExecutor:
             return None
         return self._encode(self._syntax.label_prefix + text) or None
 
-    def _stream(self, start: str, relations: Sequence[str]) -> tuple[list[int], int] | None:
+    def _stream(self, start: str, relations: Sequence[str], label=None) -> tuple[list[int], int] | None:
         """The span's tokens and how many come before the closer, or None where a label
-        is blank."""
+        is blank (`label`: the start's tokens, in place of the start text's)."""
         tokens = list(self._encode(self._syntax.opener))
-        label = self._label(start)
+        label = self._label(start) if label is None else label
         if label is None:
             return None
         tokens += label
@@ -223,23 +223,44 @@ class MatchedExecutor:
         return out
 
     def _jobs(self, paths) -> list[tuple]:
-        """(start, relations capped at 8, version, anchor) of each path, checked before any
-        launch: an unknown version or an anchor without label rows raises, and so does an
-        anchored start naming none of the anchor's entities (the fallback not served)."""
+        """(start, relations capped at 8, version, anchor, start tokens, fallback) of each
+        path, checked before any launch: an unknown version or an anchor without label rows
+        raises.  An anchored start naming none of the anchor's entities falls back, as the
+        reference's executor does, to every anchor entity (src/xgraph/programs.py:832-836):
+        its span is written with a label that names exactly the anchor's entities among its
+        bound rows (the start tokens; the written start then plans nothing); where no label
+        does (anchor entities without a shared label), that fallback raises."""
         jobs = []
         for path in paths:
             start, relations, version = path[0], list(path[1])[:MAX_PATH_RELATIONS], path[2]
             anchor = path[3] if len(path) > 3 else None
             self._runner.view(version)
+            tokens, fallback = None, False
             if anchor is not None:
                 bound = self._bound_rows(anchor)
-                named = sorted(set(self._written_rows(start)) & set(bound))
-                if not named:
-                    raise ValueError(f"the anchored start {start!r} names none of the anchor's entities "
-                                     f"{list(anchor)!r}; that fallback is not served")
+                if not set(self._written_rows(start)) & set(bound):
+                    tokens, fallback = self._covering_label(bound), True
+                    if tokens is None:
+                        raise ValueError(f"the anchored start {start!r} names none of the anchor's entities "
+                                         f"{list(anchor)!r}, and no one label names them all; that fallback "
+                                         "is not served")
                 anchor = list(anchor)
-            jobs.append((start, relations, version, anchor))
+            jobs.append((start, relations, version, anchor, tokens, fallback))
         return jobs
+
+    def _covering_label(self, bound: list[int]) -> list[int] | None:
+        """The tokens of a label whose rows among the bound rows name every entity they name,
+        or None."""
+        labels = self._index.labels
+        owners = np.asarray(labels.owners)
+        every = {int(owners[r]) for r in bound}
+        named: dict[tuple[int, ...], set[int]] = {}
+        for row in bound:
+            named.setdefault(tuple(labels.row_tokens(row)), set()).add(int(owners[row]))
+        for tokens, entities in named.items():  # (bound rows are in row order: the first such label)
+            if entities == every:
+                return list(tokens)
+        return None
 
     # -- the live frontier (src/xgraph/programs.py:598-812) ------------------------------
 
@@ -358,12 +379,12 @@ class MatchedExecutor:
     def _frontier_batch(self, paths) -> list[list[tuple[int, int]]]:
         size = self._runner.max_sequences
         streams = []
-        for start, relations, _, _ in paths:
+        for start, relations, _, _, start_tokens, _ in paths:
             if relations:
-                stream = self._stream(start, relations)
+                stream = self._stream(start, relations, start_tokens)
                 streams.append(None if stream is None else (stream[0][: stream[1]], stream[1]))
             else:  # the starts: the span up to the separator after its start
-                label = self._label(start)
+                label = self._label(start) if start_tokens is None else start_tokens
                 tokens = None if label is None else (self._encode(self._syntax.opener) + label
                                                      + self._encode(self._syntax.separator))
                 streams.append(None if tokens is None else (tokens, len(tokens)))
@@ -374,11 +395,11 @@ class MatchedExecutor:
             if stream is not None:
                 history[k, : len(stream[0])] = stream[0]
                 upto[k] = stream[1]
-        admissions = [(k, version, anchor) for k, (_, _, version, anchor) in enumerate(paths)]
+        admissions = [(k, job[2], job[3]) for k, job in enumerate(paths)]
         states, memory, _, _ = self._runner.run(history, upto, upto, admissions)
         owners, first = self._index.labels.owners, self._first_rows()
         out = []
-        for k, (_, relations, version, _) in enumerate(paths):
+        for k, (_, relations, version, _, _, _) in enumerate(paths):
             if streams[k] is None or int(states["phase"][k]) == _PHASE_ERROR:
                 out.append([])
                 continue
@@ -402,7 +423,7 @@ class MatchedExecutor:
     def _batch(self, paths) -> list[MatchedPath]:
         index = self._index
         n, size = len(paths), self._runner.max_sequences
-        streams = [self._stream(start, relations) for start, relations, _, _ in paths]
+        streams = [self._stream(start, relations, tokens) for start, relations, _, _, tokens, _ in paths]
         width = max([len(s[0]) for s in streams if s is not None] + [1])
         history = np.zeros((size, width), dtype=np.int32)
         before = np.zeros(size, dtype=np.int32)
@@ -411,12 +432,12 @@ class MatchedExecutor:
             if stream is not None:
                 history[k, : len(stream[0])] = stream[0]
                 before[k], total[k] = stream[1], len(stream[0])
-        admissions = [(k, version, anchor) for k, (_, _, version, anchor) in enumerate(paths)]
+        admissions = [(k, job[2], job[3]) for k, job in enumerate(paths)]
         states_a, memory_a, states_b, memory_b = self._runner.run(history, before, total, admissions)
         owners, ids = index.labels.owners, index.labels.owner_ids
 
         results = []
-        for k, (start, relations, version, anchor) in enumerate(paths):
+        for k, (start, relations, version, anchor, _, fallback) in enumerate(paths):
             empty = MatchedPath((), None, None)
             if streams[k] is None or int(states_b["phase"][k]) == _PHASE_ERROR:
                 results.append(empty)
@@ -428,7 +449,7 @@ class MatchedExecutor:
                     results.append(empty)
                     continue
                 lo, hi = int(states_b["last_lo"][k]), int(states_b["last_hi"][k])
-                rows = (range(lo, hi) if anchor is None
+                rows = (range(lo, hi) if anchor is None else self._bound_rows(anchor) if fallback
                         else sorted(set(self._written_rows(start)) & set(self._bound_rows(anchor))))
                 starts = self._order(view, [(int(owners[r]), r) for r in rows])
                 results.append(MatchedPath(tuple(ids[e] for e in starts), ids[starts[0]] if starts else None, None))
@@ -453,8 +474,9 @@ class MatchedExecutor:
             entities = self._order(view, [(e, int(first[e])) for e in final])
             rows = memory_b[k][_MEM_REACHED_ROWS: _MEM_REACHED_ROWS + int(memory_b[k][_MEM_REACHED])].tolist()
             answer = self._order(view, [(int(owners[r]), r) for r in rows])
+            # a fallback start plans nothing: the written start names no entity it starts from
             results.append(MatchedPath(tuple(ids[e] for e in entities), ids[answer[0]] if answer else None,
-                                       (start, *relations)))
+                                       None if fallback else (start, *relations)))
         return results
 
 
