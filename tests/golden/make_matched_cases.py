@@ -21,8 +21,8 @@ degree or sitelink start rank, unquoted starts, KG versions with add / remove ed
   the reference's error).
 
 Every path also records the executor's live frontier: `starts`, `frontier` (after its
-relations) and `frontier_relations`, and the `derivations` of the entities it resolves to
-(src/xgraph/programs.py:596-736).
+relations) and `frontier_relations`, the `derivations` of the entities it resolves to, and
+`execute_set` (reached, uncapped reached, cap events; src/xgraph/programs.py:486-736).
 """
 
 from __future__ import annotations
@@ -133,7 +133,8 @@ def live(executor, start, relations, anchor, version) -> dict:
     return {"starts": list(executor.starts(start, anchor, version)),
             "frontier": list(executor.frontier(start, relations, anchor, version)),
             "frontier_relations": [list(x) for x in executor.frontier_relations(start, relations, anchor, version)],
-            "derivations": [list(x) for x in executor.derivations(start, relations, anchor, version)]}
+            "derivations": [list(x) for x in executor.derivations(start, relations, anchor, version)],
+            "execute_set": executor.execute_set(start, relations, anchor, version)}
 
 
 def main() -> None:

@@ -44,6 +44,9 @@ def test_matched_fixture_covers_the_cases():
     assert sum(1 for c in cases if len(c["frontier"]) > 1) > 200 and sum(1 for c in cases if c["frontier_relations"]) > 400
     assert sum(1 for c in cases if len(c["starts"]) > 1) > 100
     assert sum(1 for c in cases if any(n > 1 for _, n in c["derivations"])) > 20
+    stages = {e["stage"] for c in cases for e in c["execute_set"]["cap_events"]}
+    assert stages >= {"path_relations", "starts", "frontier", "answer_label_rows"}, stages
+    assert any(c["execute_set"]["uncapped_reached"] != c["execute_set"]["reached"] for c in cases)
     assert sum(1 for c in cases if len(c["reached"]) > 1) > 100
     assert sum(1 for c in cases if not c["reached"]) > 100
     assert any(not c["relations"] and c["reached"] for c in cases)
@@ -143,8 +146,8 @@ def _check(cases, got, where):
 
 def _check_live(executor, cases, where):
     """The live frontier of every served case (starts and frontiers of a world's paths in
-    one batch): starts, frontier, frontier_relations and derivations equal the reference
-    executor's."""
+    one batch): starts, frontier, frontier_relations, derivations and execute_set equal the
+    reference executor's."""
     ids = executor._index.labels.owner_ids
     jobs = [(c["start"], [], c["version"], c.get("anchor")) for c in cases]
     jobs += [(c["start"], c["relations"], c["version"], c.get("anchor")) for c in cases]
@@ -159,6 +162,8 @@ def _check_live(executor, cases, where):
         assert [list(x) for x in relations] == case["frontier_relations"], at
         derivations = executor.derivations(case["start"], case["relations"], case.get("anchor"), case["version"])
         assert [list(x) for x in derivations] == case["derivations"], at
+        complete = executor.execute_set(case["start"], case["relations"], case.get("anchor"), case["version"])
+        assert complete == case["execute_set"], at
 
 
 def test_matched_execution_on_the_host_seam_equals_the_reference():

@@ -105,6 +105,7 @@ class MatchedExecutor:
             index, tokenizer, self._syntax, max_paths, paths=True, committed_paths=committed_paths,
             versions=versions, start_rank=start_rank, unquoted_starts=unquoted_starts))
         self._sitelinks = index.sitelinks if start_rank == "sitelinks" else None
+        self._unquoted, self._committed = unquoted_starts, committed_paths
         self._pieces: dict[str, list[int]] = {}
         self._first: np.ndarray | None = None
 
@@ -362,6 +363,118 @@ class MatchedExecutor:
         ordered = self._order(view, [(e, int(first[e])) for e in final], sitelinks)
         ids = index.labels.owner_ids
         return tuple((ids[e], counts.get(e, 0)) for e in ordered)
+
+    def execute_set(self, start: str, relations: list[str], anchor: list[str] | None = None,
+                    version: str | None = None, *, witnesses: bool = False) -> dict:
+        """Complete answer support after commitment, with each cap the path met
+        (src/xgraph/programs.py:486-560): `reached`, the entities the capped walk's answer
+        binds (the best start's final entities' label rows, the first 64, best-connected);
+        `uncapped_reached`, the same walk with no start, frontier or label-row cap (a
+        sensitivity of the fixed plan, computed on the host as the reference does); and
+        `cap_events`, each cap met (path relations, anchor label rows, starts, a hop's
+        frontier, answer label rows) with the count before it.  The capped walk's frontiers
+        come from the engine (one slot per prefix of the path); the counts before each cap
+        are taken on the host.  Endpoint witnesses are not served."""
+        if witnesses:
+            raise ValueError("endpoint witnesses are not served by this executor")
+        view = self._runner.view(version)
+        index = self._index
+        owners = np.asarray(index.labels.owners)
+        ids = index.labels.owner_ids
+        events: list[dict] = []
+        if len(relations) > MAX_PATH_RELATIONS:
+            events.append({"stage": "path_relations", "before": len(relations), "kept": MAX_PATH_RELATIONS})
+        relations = list(relations)[:MAX_PATH_RELATIONS]
+        if anchor is not None:
+            at = {e: n for n, e in enumerate(ids)}
+            count = int(np.count_nonzero(np.isin(owners, sorted({at[e] for e in anchor if e in at}))))
+            if not count:
+                raise ValueError(f"anchor has no writable label rows: {anchor!r}")
+            if count > MAX_REACHED:
+                events.append({"stage": "anchor_label_rows", "before": count, "kept": MAX_REACHED})
+        result = {"reached": [], "uncapped_reached": [], "cap_events": events}
+        if not relations:
+            return result
+        # the capped walk: the engine's starts and hop frontiers; the host counts what each cap cut
+        starts, *hops = self.frontiers([(start, relations[:k], version, anchor) for k in range(len(relations) + 1)])
+        written = self._start_rows(start, anchor, uncapped=False)
+        with_triples = {int(owners[r]) for r in written if len(view.edges_at(int(owners[r]))[0])}
+        if len(with_triples) > MAX_REACHED:
+            events.append({"stage": "starts", "before": len(with_triples), "kept": MAX_REACHED})
+        previous = starts
+        for hop, (label, kept) in enumerate(zip(relations, hops, strict=True), start=1):
+            if not previous:
+                break
+            reached = self._step(view, {e for e, _ in previous}, label)
+            if len(reached) > MAX_REACHED:
+                events.append({"stage": "frontier", "hop": hop, "before": len(reached), "kept": MAX_REACHED})
+            previous = kept
+        if hops[-1]:
+            rows = self._final_rows(hops[-1])
+            if len(rows) > MAX_REACHED:
+                events.append({"stage": "answer_label_rows", "before": len(rows), "kept": MAX_REACHED})
+            result["reached"] = [ids[e] for e in self._order(view, [(int(owners[r]), r) for r in rows[:MAX_REACHED]])]
+        # the uncapped walk (host): every start, every entity each hop reaches
+        ranks = self._uncapped_starts(view, start, anchor)
+        for label in relations:
+            if not ranks:
+                break
+            reached: dict[int, int] = {}
+            for entity, rank in ranks.items():
+                for item in self._step(view, {entity}, label):
+                    reached[item] = min(reached.get(item, rank), rank)
+            ranks = reached
+        if ranks:
+            rows = self._final_rows(list(ranks.items()))
+            result["uncapped_reached"] = [ids[e] for e in self._order(view, [(int(owners[r]), r) for r in rows])]
+        return result
+
+    def _start_rows(self, start: str, anchor, *, uncapped: bool) -> list[int]:
+        """The label rows a path's start may name (src/xgraph/programs.py:832-860): the
+        anchor's (its first 64 rows, or all of them uncapped) among those written as the
+        start, or all of them when the start names none; unanchored, those written as the
+        start (none for a quoted start under unquoted starts)."""
+        written = self._written_rows(start)
+        if anchor is None:
+            if self._unquoted and self._syntax.quoted((self._syntax.label_prefix + start).encode("utf-8")):
+                return []
+            return written
+        at = {e: n for n, e in enumerate(self._index.labels.owner_ids)}
+        bound = np.flatnonzero(np.isin(np.asarray(self._index.labels.owners),
+                                       sorted({at[e] for e in anchor if e in at}))).tolist()
+        if not uncapped:
+            bound = bound[:MAX_REACHED]
+        named = [r for r in bound if r in set(written)]
+        return named or bound
+
+    def _uncapped_starts(self, view, start: str, anchor) -> dict[int, int]:
+        """Every start with triples and its rank (0 for union paths), uncapped."""
+        owners = np.asarray(self._index.labels.owners)
+        rows = self._start_rows(start, anchor, uncapped=True)
+        pairs = [(int(owners[r]), r) for r in rows if len(view.edges_at(int(owners[r]))[0])]
+        ordered = self._order(view, pairs)
+        if not self._committed:
+            first = self._first_rows()
+            ordered.sort(key=lambda e: int(first[e]))
+        return {e: (rank if self._committed else 0) for rank, e in enumerate(ordered)}
+
+    def _step(self, view, entities: set[int], label: str) -> set[int]:
+        """The entities reached from these under every relation the label names."""
+        index = self._index
+        owners = np.asarray(index.labels.owners)
+        follow = sorted({int(index.relations.owners[r]) for r in self._written_rows(label, index.relations)})
+        out: set[int] = set()
+        for entity in entities:
+            relation_of, object_of = view.edges_at(entity)
+            out.update(int(owners[row]) for row in np.asarray(object_of)[np.isin(relation_of, follow)].tolist())
+        return out
+
+    def _final_rows(self, frontier) -> list[int]:
+        """The label rows, sorted, of the frontier's entities of the least start rank."""
+        best = min(rank for _, rank in frontier)
+        rows = np.asarray(self._index.labels.owners)
+        final = sorted({e for e, rank in frontier if rank == best})
+        return np.flatnonzero(np.isin(rows, final)).tolist()
 
     def frontiers(self, paths: Iterable[tuple]) -> list[list[tuple[int, int]]]:
         """Each (start, relations, version[, anchor]) path's live frontier as (entity
