@@ -22,7 +22,8 @@ degree or sitelink start rank, unquoted starts, KG versions with add / remove ed
 
 Every path also records the executor's live frontier: `starts`, `frontier` (after its
 relations) and `frontier_relations`, the `derivations` of the entities it resolves to, and
-`execute_set` (reached, uncapped reached, cap events; src/xgraph/programs.py:486-736).
+`execute_set` (reached, uncapped reached, cap events; and with endpoint witnesses;
+src/xgraph/programs.py:486-736).
 """
 
 from __future__ import annotations
@@ -134,7 +135,17 @@ def live(executor, start, relations, anchor, version) -> dict:
             "frontier": list(executor.frontier(start, relations, anchor, version)),
             "frontier_relations": [list(x) for x in executor.frontier_relations(start, relations, anchor, version)],
             "derivations": [list(x) for x in executor.derivations(start, relations, anchor, version)],
-            "execute_set": executor.execute_set(start, relations, anchor, version)}
+            "execute_set": executor.execute_set(start, relations, anchor, version),
+            "witnesses": witnessed(executor, start, relations, anchor, version)}
+
+
+def witnessed(executor, start, relations, anchor, version):
+    """execute_set with witnesses, or the error it raises (an entity id whose tail is no
+    number cannot rank a chain)."""
+    try:
+        return executor.execute_set(start, relations, anchor, version, witnesses=True)
+    except ValueError as error:
+        return {"error": str(error)}
 
 
 def main() -> None:

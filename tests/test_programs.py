@@ -47,6 +47,7 @@ def test_matched_fixture_covers_the_cases():
     stages = {e["stage"] for c in cases for e in c["execute_set"]["cap_events"]}
     assert stages >= {"path_relations", "starts", "frontier", "answer_label_rows"}, stages
     assert any(c["execute_set"]["uncapped_reached"] != c["execute_set"]["reached"] for c in cases)
+    assert sum(1 for c in cases if len(c["witnesses"].get("witnesses", {})) > 1) > 50
     assert sum(1 for c in cases if len(c["reached"]) > 1) > 100
     assert sum(1 for c in cases if not c["reached"]) > 100
     assert any(not c["relations"] and c["reached"] for c in cases)
@@ -164,6 +165,13 @@ def _check_live(executor, cases, where):
         assert [list(x) for x in derivations] == case["derivations"], at
         complete = executor.execute_set(case["start"], case["relations"], case.get("anchor"), case["version"])
         assert complete == case["execute_set"], at
+        if "error" in case["witnesses"]:  # an id whose tail is no number ranks no chain
+            with pytest.raises(ValueError, match="invalid literal"):
+                executor.execute_set(case["start"], case["relations"], case.get("anchor"), case["version"],
+                                     witnesses=True)
+        else:
+            assert executor.execute_set(case["start"], case["relations"], case.get("anchor"), case["version"],
+                                        witnesses=True) == case["witnesses"], at
 
 
 def test_matched_execution_on_the_host_seam_equals_the_reference():

@@ -372,11 +372,14 @@ class MatchedExecutor:
         `uncapped_reached`, the same walk with no start, frontier or label-row cap (a
         sensitivity of the fixed plan, computed on the host as the reference does); and
         `cap_events`, each cap met (path relations, anchor label rows, starts, a hop's
-        frontier, answer label rows) with the count before it.  The capped walk's frontiers
-        come from the engine (one slot per prefix of the path); the counts before each cap
-        are taken on the host.  Endpoint witnesses are not served."""
-        if witnesses:
-            raise ValueError("endpoint witnesses are not served by this executor")
+        frontier, answer label rows) with the count before it; with witnesses (an index
+        with sitelink counts), `witnesses`: for each reached entity one start-to-endpoint
+        entity chain through the capped walk, chains ranked step by step by most sitelinks,
+        then numeric entity id.  The capped walk's frontiers come from the engine (one slot
+        per prefix of the path); the counts before each cap and the chains are taken on the
+        host."""
+        if witnesses and self._index.sitelinks is None:
+            raise ValueError("endpoint witnesses require an index with sitelink counts")
         view = self._runner.view(version)
         index = self._index
         owners = np.asarray(index.labels.owners)
@@ -393,6 +396,8 @@ class MatchedExecutor:
             if count > MAX_REACHED:
                 events.append({"stage": "anchor_label_rows", "before": count, "kept": MAX_REACHED})
         result = {"reached": [], "uncapped_reached": [], "cap_events": events}
+        if witnesses:
+            result["witnesses"] = {}
         if not relations:
             return result
         # the capped walk: the engine's starts and hop frontiers; the host counts what each cap cut
@@ -413,7 +418,11 @@ class MatchedExecutor:
             rows = self._final_rows(hops[-1])
             if len(rows) > MAX_REACHED:
                 events.append({"stage": "answer_label_rows", "before": len(rows), "kept": MAX_REACHED})
-            result["reached"] = [ids[e] for e in self._order(view, [(int(owners[r]), r) for r in rows[:MAX_REACHED]])]
+            ordered = self._order(view, [(int(owners[r]), r) for r in rows[:MAX_REACHED]])
+            result["reached"] = [ids[e] for e in ordered]
+            if witnesses:
+                chains = self._witnesses(view, starts, relations, hops)
+                result["witnesses"] = {ids[e]: [ids[p] for p in chains[e]] for e in ordered}
         # the uncapped walk (host): every start, every entity each hop reaches
         ranks = self._uncapped_starts(view, start, anchor)
         for label in relations:
@@ -428,6 +437,33 @@ class MatchedExecutor:
             rows = self._final_rows(list(ranks.items()))
             result["uncapped_reached"] = [ids[e] for e in self._order(view, [(int(owners[r]), r) for r in rows])]
         return result
+
+    def _witnesses(self, view, starts, relations, hops) -> dict[int, tuple[int, ...]]:
+        """One chain per entity of the capped walk's last frontier with the best rank,
+        restricted to the walk's own frontiers (src/xgraph/programs.py:562-595): from the
+        starts of the best rank (every start, union paths), each hop extends the chains in
+        order of (most sitelinks, numeric id) per step, and an entity keeps the first chain
+        that reaches it."""
+        index = self._index
+        ids, owners, sitelinks = index.labels.owner_ids, np.asarray(index.labels.owners), index.sitelinks
+        best = min(r for _, r in hops[-1])
+        paths = {e: (e,) for e, rank in starts if not self._committed or rank == best}
+
+        def key(entity):
+            return tuple((-int(sitelinks[e]), int(ids[e][1:])) for e in paths[entity])
+
+        for label, kept in zip(relations, hops, strict=True):
+            follow = sorted({int(index.relations.owners[r]) for r in self._written_rows(label, index.relations)})
+            ranks = dict(kept)
+            reached: dict[int, tuple[int, ...]] = {}
+            for entity in sorted(paths, key=key):
+                relation_of, object_of = view.edges_at(entity)
+                for row in np.asarray(object_of)[np.isin(relation_of, follow)].tolist():
+                    item = int(owners[row])
+                    if ranks.get(item) == best:
+                        reached.setdefault(item, (*paths[entity], item))
+            paths = reached
+        return paths
 
     def _start_rows(self, start: str, anchor, *, uncapped: bool) -> list[int]:
         """The label rows a path's start may name (src/xgraph/programs.py:832-860): the
