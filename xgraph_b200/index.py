@@ -591,7 +591,8 @@ def build_kg_directory_index(
     order; a triple naming an item or property without one is unwritable, like a triple
     whose subject, object or relation has no label row.  The arrays equal the reference
     builder's; `device` builds the edge arrays on that GPU.  The directory's date tables
-    and RDF ids feed policies this engine does not serve and are not read."""
+    and RDF ids are not read: an index for expressions takes its dates in memory
+    (build_kg_index's `dates`) or from a saved index that holds them."""
     kg = Path(kg)
     for name in KG_DIRECTORY_FILES:
         if not (kg / name).is_file():
