@@ -23,7 +23,7 @@ degree or sitelink start rank, unquoted starts, KG versions with add / remove ed
 Every path also records the executor's live frontier: `starts`, `frontier` (after its
 relations) and `frontier_relations`, the `derivations` of the entities it resolves to, and
 `execute_set` (reached, uncapped reached, cap events; and with endpoint witnesses;
-src/xgraph/programs.py:486-736).
+src/xgraph/programs.py:486-736), and its execution with relation repair.
 """
 
 from __future__ import annotations
@@ -136,7 +136,15 @@ def live(executor, start, relations, anchor, version) -> dict:
             "frontier_relations": [list(x) for x in executor.frontier_relations(start, relations, anchor, version)],
             "derivations": [list(x) for x in executor.derivations(start, relations, anchor, version)],
             "execute_set": executor.execute_set(start, relations, anchor, version),
-            "witnesses": witnessed(executor, start, relations, anchor, version)}
+            "witnesses": witnessed(executor, start, relations, anchor, version),
+            "repaired": repaired(executor, start, relations, anchor, version)}
+
+
+def repaired(executor, start, relations, anchor, version):
+    """execute with repair: reached, answer and plan."""
+    path = executor.execute(start, relations, anchor=anchor, version=version, repair=True)
+    return {"reached": list(path.reached), "answer": path.answer,
+            "plan": None if path.plan is None else list(path.plan)}
 
 
 def witnessed(executor, start, relations, anchor, version):

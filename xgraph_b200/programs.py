@@ -25,8 +25,10 @@ executor returns for it.
 Anchored paths start from the anchor's entities their start label names (each anchored
 slot admitted with the anchor's label rows); a start naming none of them starts from every
 anchor entity, as the reference's does, written with a label that names them all (refused
-where no one label does).  Not served (refused by name): the offline repairs (`repair`,
-`strip_quotes`) and the observation / menu / audit settings.
+where no one label does).  With repair, an unknown relation is replaced, hop by hop, by the
+frontier's most similar relation written with a label of its own (refused where it has
+none).  Not served (refused by name): `strip_quotes` and the observation / menu / audit
+settings.
 """
 
 from __future__ import annotations
@@ -206,7 +208,9 @@ class MatchedExecutor:
 
     def execute(self, start: str, relations: list[str], anchor: list[str] | None = None,
                 version: str | None = None, repair: bool = False) -> MatchedPath:
-        """The path from the start label along the relation labels (see the class)."""
+        """The path from the start label along the relation labels (see the class).  With
+        repair, a relation label that names no relation of its hop's frontier is replaced
+        by the label or alias of the frontier's relation most like it (see _repair)."""
         return self.execute_many([(start, relations, version, anchor)], repair=repair)[0]
 
     def execute_many(self, paths: Iterable[tuple], *, repair: bool = False) -> list[MatchedPath]:
@@ -214,14 +218,88 @@ class MatchedExecutor:
         executed, in order.  An anchored path starts from the anchor's entities its start
         label names; one whose label names none of them (the reference then starts from every
         anchor entity, which no written span can express) raises ValueError."""
+        paths = list(paths)
         if repair:
-            raise ValueError("the offline relation repair is not served by this executor")
+            paths = [(p[0], self._repaired(p[0], list(p[1])[:MAX_PATH_RELATIONS], p[2], p[3] if len(p) > 3 else None),
+                      *p[2:]) for p in paths]
         jobs = self._jobs(paths)
         out: list[MatchedPath] = []
         size = self._runner.max_sequences
         for at in range(0, len(jobs), size):
             out += self._batch(jobs[at: at + size])
         return out
+
+    def _repaired(self, start: str, relations: list[str], version, anchor) -> list[str]:
+        """The relation labels with each hop's unknown relation repaired (src/xgraph/
+        programs.py:1094-1128): where a label names no relation of its hop's frontier (the
+        engine's, one slot per prefix), the frontier's relation whose label or alias is
+        most like it (similarity at least 0.6) is followed instead, written as its most
+        similar label or alias that names no other relation of the frontier.  A relation
+        with no such label cannot be written as a span: that repair raises ValueError."""
+        index = self._index
+        view = self._runner.view(version)
+        labels = list(relations)
+        for hop in range(len(labels)):
+            frontier = self.frontiers([(start, labels[:hop], version, anchor)])[0]
+            if not frontier:
+                break
+            have: set[int] = set()
+            for entity, _ in frontier:
+                have.update(int(r) for r in np.asarray(view.edges_at(entity)[0]).tolist())
+            follow = {int(index.relations.owners[r]) for r in self._written_rows(labels[hop], index.relations)}
+            if follow & have:
+                continue
+            best, label = self._repair(have, labels[hop])
+            if best is None:
+                break  # the hop leads nowhere: the path reaches nothing, repaired or not
+            if label is None:
+                raise ValueError(f"the repaired relation of {labels[hop]!r} has no label of its own on its "
+                                 "frontier; such a path cannot be written as a span")
+            labels[hop] = label
+        return labels
+
+    def _repair(self, have: set[int], written: str) -> tuple[int | None, str | None]:
+        """The frontier relation (of `have`) with the label or alias most like the written
+        one, at least 0.6 alike (the larger of difflib's ratio and the word sets' Jaccard
+        overlap, on NFC-normalized casefolded text), the last of equal scores in relation
+        order; and its most similar label or alias that names no other relation of `have`."""
+        from difflib import SequenceMatcher
+        from unicodedata import normalize
+
+        def norm(text: str) -> str:
+            return normalize("NFC", text).casefold().strip()
+
+        def similarity(a: str, b: str) -> float:
+            words_a, words_b = set(a.split()), set(b.split())
+            overlap = len(words_a & words_b) / len(words_a | words_b) if words_a | words_b else 0.0
+            return max(SequenceMatcher(None, a, b).ratio(), overlap)
+
+        names = self._relation_names()
+        best, score = None, 0.6
+        for relation in sorted(have):
+            for name in names.get(relation, ()):
+                ratio = similarity(norm(name), norm(written))
+                if ratio >= score:
+                    best, score = relation, ratio
+        if best is None:
+            return None, None
+        index = self._index
+        for name in sorted(names[best], key=lambda n: -similarity(norm(n), norm(written))):
+            owners = {int(index.relations.owners[r]) for r in self._written_rows(name, index.relations)}
+            if owners & have == {best}:
+                return best, name
+        return best, None
+
+    def _relation_names(self) -> dict[int, list[str]]:
+        """Each relation's labels and aliases as its index rows write them, in row order."""
+        if getattr(self, "_names", None) is None:
+            index, prefix = self._index.relations, self._syntax.label_prefix
+            self._names: dict[int, list[str]] = {}
+            for row in range(index.num_rows):
+                text = b"".join(self._tokenizer.token_bytes(t) for t in index.row_tokens(row))
+                self._names.setdefault(int(index.owners[row]), []).append(
+                    text.decode("utf-8", errors="replace").removeprefix(prefix))
+        return self._names
 
     def _jobs(self, paths) -> list[tuple]:
         """(start, relations capped at 8, version, anchor, start tokens, fallback) of each
