@@ -16,6 +16,7 @@ degree or sitelink start rank, unquoted starts, KG versions with add / remove ed
 - paths walked along the KG's own edges, 1-4 relations, with random labels and aliases;
 - entity spans (no relation), starts that name nothing, relations the frontier lacks,
   relation labels cut short, and walks longer than the 8-relation cap;
+- with strip_quotes, every other start wrapped in quotation marks;
 - anchored paths and entity spans (see anchored_of), each recorded with whether the
   executor fell back to every anchor entity, and an anchor naming no entity (recorded with
   the reference's error).
@@ -42,9 +43,10 @@ SETTINGS = {
     "sitelinks": {"committed_paths": True, "start_rank": "sitelinks"},
     "union": {"committed_paths": False},
     "unquoted": {"committed_paths": True, "unquoted_starts": True},
+    "stripped": {"committed_paths": True, "strip_quotes": True},
 }
-PLAN = [("toy", ("committed", "sitelinks", "union")),
-        ("rand_bpe", ("committed", "sitelinks", "union", "unquoted")),
+PLAN = [("toy", ("committed", "sitelinks", "union", "stripped")),
+        ("rand_bpe", ("committed", "sitelinks", "union", "unquoted", "stripped")),
         ("rand_dense", ("committed", "union")),
         ("crowd", ("committed", "sitelinks"))]
 
@@ -189,11 +191,13 @@ def main() -> None:
             executor = MatchedExecutor(index, served, versions=versions, **SETTINGS[setting])
             for n, (start, relations) in enumerate(written):
                 version = (None, "v0", "v1")[n % 3] if world_name != "crowd" else None
+                if setting == "stripped" and n % 2 == 0:  # a start written in quotation marks
+                    start = ('"{}"', "\u201c{}\u201d", "'{}'", "\u00ab {} \u00bb")[n // 2 % 4].format(start)
                 path = executor.execute(start, relations, version=version)
                 cases.append({"world": world_name, "setting": setting, "start": start,
                               "relations": relations, "version": version,
                               "reached": list(path.reached), "answer": path.answer,
-                              "plan": None if path.plan is None else list(path.plan),
+                              "plan": None if path.plan is None else list(path.plan), "stripped": path.stripped,
                               **live(executor, start, relations, None, version)})
             for n, (start, relations, anchor) in enumerate(anchored):
                 version = (None, "v0", "v1")[n % 3] if world_name != "crowd" else None

@@ -1,12 +1,13 @@
 """Offline path execution (xgraph_b200/programs.py) against the reference's MatchedExecutor.
 
-tests/golden/matched_cases.json.gz (tests/golden/make_matched_cases.py) holds 979 written
-paths over four golden worlds and four executor settings, 275 of them anchored, with what
+tests/golden/matched_cases.json.gz (tests/golden/make_matched_cases.py) holds 1157 written
+paths over four golden worlds and five executor settings, 325 of them anchored, with what
 the reference's MatchedExecutor (src/xgraph/programs.py:368-1130) made of each: entities
 reached in best-connected order, answer, plan (or its error).  The executor runs each
 world's paths as batches of engine slots and must return the same three fields for every
-path it serves -- on the GPU, and on the CPU with the host seam of the kernels' row logic in
-place of the CUDA engine -- and refuse the anchored fallback it does not serve.
+path it serves (and the live frontier, derivations, execute_set, repairs and stripped
+starts) -- on the GPU, and on the CPU with the host seam of the kernels' row logic in place
+of the CUDA engine -- and refuse what it does not serve.
 """
 
 from __future__ import annotations
@@ -34,10 +35,11 @@ def test_matched_fixture_covers_the_cases():
     reaching nothing, entity spans, and walks cut at the 8-relation cap; and the reference's
     plan is the start and the (capped) relations exactly where a path reaches something."""
     cases = fixture()["cases"]
-    assert len(cases) == 979
+    assert len(cases) == 1157
+    assert sum(1 for c in cases if c.get("stripped")) > 40
     anchored = [c for c in cases if "anchor" in c]
-    assert len(anchored) == 275 and sum(1 for c in anchored if c.get("fallback")) == 66
-    assert sum(1 for c in anchored if "error" in c) == 11
+    assert len(anchored) == 325 and sum(1 for c in anchored if c.get("fallback")) == 78
+    assert sum(1 for c in anchored if "error" in c) == 13
     assert sum(1 for c in served(anchored) if len(c["reached"]) > 1) > 50
     assert any(not c["relations"] and c["reached"] for c in served(anchored))
     cases = served(cases)
@@ -56,7 +58,8 @@ def test_matched_fixture_covers_the_cases():
     assert sum(1 for c in cases if c.get("fallback") and c["reached"]) > 20
     for c in cases:
         if c["reached"] and c["relations"] and not c.get("fallback"):
-            assert c["plan"] == [c["start"], *c["relations"][:MAX_PATH_RELATIONS]]
+            start = c["plan"][0] if c.get("stripped") else c["start"]  # (a stripped start plans as read)
+            assert c["plan"] == [start, *c["relations"][:MAX_PATH_RELATIONS]]
             assert c["answer"] in c["reached"]
         else:  # (a fallback start plans nothing)
             assert c["plan"] is None
@@ -144,6 +147,7 @@ def _check(cases, got, where):
         assert list(path.reached) == case["reached"], at
         assert path.answer == case["answer"], at
         assert (None if path.plan is None else list(path.plan)) == case["plan"], at
+        assert path.stripped == case.get("stripped", False), at
 
 
 def _check_live(executor, cases, where):
@@ -152,7 +156,10 @@ def _check_live(executor, cases, where):
     without witnesses) and execution with repair equal the reference executor's."""
     ids = executor._index.labels.owner_ids
     jobs = [(c["start"], [], c["version"], c.get("anchor")) for c in cases]
-    jobs += [(c["start"], c["relations"], c["version"], c.get("anchor")) for c in cases]
+    # (frontier reads the start as written, stripped of quotation marks where that names
+    # something; starts takes it as written)
+    jobs += [(executor._read(c["start"], c.get("anchor"), c["version"]), c["relations"], c["version"], c.get("anchor"))
+             for c in cases]
     got = executor.frontiers(jobs)
     for case, starts, frontier in zip(cases, got[: len(cases)], got[len(cases):], strict=True):
         at = (*where, case["start"], case["relations"], case["version"], case.get("anchor"))
@@ -250,5 +257,5 @@ def test_matched_executor_refuses_what_it_does_not_serve():
     from xgraph_b200.programs import MatchedExecutor
 
     _, served, _ = world("toy")
-    with pytest.raises(ValueError, match="strip_quotes"):
-        MatchedExecutor(world_index("toy", True), served, strip_quotes=True)
+    with pytest.raises(ValueError, match="observe_required"):
+        MatchedExecutor(world_index("toy", True), served, observe_required=True)

@@ -27,14 +27,15 @@ slot admitted with the anchor's label rows); a start naming none of them starts 
 anchor entity, as the reference's does, written with a label that names them all (refused
 where no one label does).  With repair, an unknown relation is replaced, hop by hop, by the
 frontier's most similar relation written with a label of its own (refused where it has
-none).  Not served (refused by name): `strip_quotes` and the observation / menu / audit
-settings.
+none).  With strip_quotes, a start naming nothing to start from is read without the
+quotation marks wrapping it where that names something (MatchedPath.stripped).  Not
+served (refused by name): the observation / menu / audit settings.
 """
 
 from __future__ import annotations
 
 from collections.abc import Iterable, Sequence
-from dataclasses import dataclass
+from dataclasses import dataclass, replace
 
 import numpy as np
 
@@ -53,8 +54,21 @@ _MEM_PENDING_FIRST = _MEM_PENDING_RANK + MAX_REACHED
 _PHASE_ERROR = 3
 _ENTITY_SPAN, _PATH_SPAN = 2, 4
 
-_NOT_SERVED = {"strip_quotes": False, "observe_required": False, "observe_no_loop": False,
-               "observe_defer": 0, "menu_close_next": False}
+_NOT_SERVED = {"observe_required": False, "observe_no_loop": False, "observe_defer": 0,
+               "menu_close_next": False}
+
+# (opening, closing) quotation marks strip_quotes removes around a written start
+# (src/xgraph/programs.py:238-248)
+QUOTE_PAIRS = (('"', '"'), ("'", "'"), ("\u201c", "\u201d"), ("\u2018", "\u2019"), ("\u201e", "\u201c"),
+               ("\u00ab", "\u00bb"))
+
+
+def strip_quotes(text: str) -> str:
+    """The text without the paired quotation marks that wrap all of it, repeatedly, and the
+    spaces inside them; unchanged where nothing would be left."""
+    while len(text) > 2 and (text[0], text[-1]) in QUOTE_PAIRS and text[1:-1].strip():
+        text = text[1:-1].strip()
+    return text
 
 
 @dataclass(frozen=True)
@@ -86,7 +100,7 @@ class MatchedExecutor:
 
     def __init__(self, index, tokenizer, *, versions=None, start_rank: str = "degree",
                  unquoted_starts: bool = False, committed_paths: bool = True, max_paths: int = 256,
-                 _runner=None, **others) -> None:
+                 strip_quotes: bool = False, _runner=None, **others) -> None:
         from .engine import Engine
         from .index import IndexMismatch
 
@@ -107,7 +121,7 @@ class MatchedExecutor:
             index, tokenizer, self._syntax, max_paths, paths=True, committed_paths=committed_paths,
             versions=versions, start_rank=start_rank, unquoted_starts=unquoted_starts))
         self._sitelinks = index.sitelinks if start_rank == "sitelinks" else None
-        self._unquoted, self._committed = unquoted_starts, committed_paths
+        self._unquoted, self._committed, self._strip = unquoted_starts, committed_paths, strip_quotes
         self._pieces: dict[str, list[int]] = {}
         self._first: np.ndarray | None = None
 
@@ -218,7 +232,9 @@ class MatchedExecutor:
         executed, in order.  An anchored path starts from the anchor's entities its start
         label names; one whose label names none of them (the reference then starts from every
         anchor entity, which no written span can express) raises ValueError."""
-        paths = list(paths)
+        originals = list(paths)
+        paths = [(self._read(p[0], p[3] if len(p) > 3 else None, p[2]), *p[1:]) for p in originals]
+        stripped = [p[0] != q[0] for p, q in zip(paths, originals, strict=True)]
         if repair:
             paths = [(p[0], self._repaired(p[0], list(p[1])[:MAX_PATH_RELATIONS], p[2], p[3] if len(p) > 3 else None),
                       *p[2:]) for p in paths]
@@ -227,7 +243,32 @@ class MatchedExecutor:
         size = self._runner.max_sequences
         for at in range(0, len(jobs), size):
             out += self._batch(jobs[at: at + size])
-        return out
+        return [replace(path, stripped=True) if flag else path for path, flag in zip(out, stripped, strict=True)]
+
+    def _read(self, start: str, anchor, version) -> str:
+        """The start as read (src/xgraph/programs.py:887-895): with strip_quotes, a start
+        that names nothing to start from is read without the quotation marks wrapping it,
+        where that names something."""
+        if not self._strip:
+            return start
+        view = self._runner.view(version)
+        if self._names_start(view, start, anchor):
+            return start
+        unquoted = strip_quotes(start)
+        return unquoted if unquoted != start and self._names_start(view, unquoted, anchor) else start
+
+    def _names_start(self, view, start: str, anchor) -> bool:
+        """Whether the start label names an entity with triples the path may start from
+        (the anchor's among its rows, anchored; none for a quoted start under unquoted
+        starts)."""
+        owners = np.asarray(self._index.labels.owners)
+        written = self._written_rows(start)
+        if anchor is not None:
+            bound = set(self._bound_rows(anchor))
+            written = [r for r in written if r in bound]
+        elif self._unquoted and self._syntax.quoted((self._syntax.label_prefix + start).encode("utf-8")):
+            written = []
+        return any(len(view.edges_at(int(owners[r]))[0]) for r in written)
 
     def _repaired(self, start: str, relations: list[str], version, anchor) -> list[str]:
         """The relation labels with each hop's unknown relation repaired (src/xgraph/
@@ -350,14 +391,17 @@ class MatchedExecutor:
 
     def starts(self, start: str, anchor: list[str] | None = None, version: str | None = None) -> tuple[str, ...]:
         """The entities a path from this start starts from, best-connected first: those the
-        label names (the anchor's, anchored) that have triples, the first 64."""
-        return self.frontier(start, [], anchor, version)
+        label names (the anchor's, anchored) that have triples, the first 64 (the start as
+        written: no quotation marks are stripped here)."""
+        ids = self._index.labels.owner_ids
+        return tuple(ids[e] for e, _ in self.frontiers([(start, [], version, anchor)])[0])
 
     def frontier(self, start: str, relations: list[str], anchor: list[str] | None = None,
                  version: str | None = None) -> tuple[str, ...]:
         """The capped live frontier after the relations (every start sense that survives,
         by start rank and first label row), or the starts for no relation."""
         ids = self._index.labels.owner_ids
+        start = self._read(start, anchor, version)
         return tuple(ids[e] for e, _ in self.frontiers([(start, relations, version, anchor)])[0])
 
     def frontier_relations(self, start: str, relations: list[str], anchor: list[str] | None = None,
@@ -370,6 +414,7 @@ class MatchedExecutor:
                 self._bound_rows(anchor)
             return []
         view = self._runner.view(version)
+        start = self._read(start, anchor, version)
         counts: dict[int, int] = {}
         for entity, _ in self.frontiers([(start, relations, version, anchor)])[0]:
             found, times = np.unique(np.asarray(view.edges_at(entity)[0]), return_counts=True)
@@ -412,6 +457,7 @@ class MatchedExecutor:
             if anchor is not None:
                 self._bound_rows(anchor)
             return ()
+        start = self._read(start, anchor, version)
         jobs = [(start, relations[:k], version, anchor) for k in range(len(relations) + 1)]
         starts, *hops = self.frontiers(jobs)
         if not hops[-1]:
@@ -459,6 +505,7 @@ class MatchedExecutor:
         if witnesses and self._index.sitelinks is None:
             raise ValueError("endpoint witnesses require an index with sitelink counts")
         view = self._runner.view(version)
+        start = self._read(start, anchor, version)
         index = self._index
         owners = np.asarray(index.labels.owners)
         ids = index.labels.owner_ids
